@@ -1,0 +1,181 @@
+"""Packed decode cache for BDH: rotated keys KR and values V per layer.
+
+Same interface and layout as the reference ``bdh_cache.CacheManager`` (``bdh_cache.py:38-336``):
+
+* ``_kr_buf`` ``(n_layer, B, n_head, capacity, N)`` and ``_v_buf`` ``(n_layer, B, 1, capacity, D)``
+  in the storage dtype, layer-major, so a layer's past is a capacity-strided ``narrow`` view;
+* ``reserve(level, T)`` returns writable slot views at ``[seq_len, seq_len+T)``;
+  ``get_past(level)`` the committed prefix (cast to the compute dtype when storage differs);
+  ``append`` / ``stage`` write a block; ``commit()`` advances ``seq_len`` once per step;
+* optional paging (``page_size``) with geometric, page-aligned growth capped at ``max_seq``.
+
+Addition for the B200 decode kernel: ``get_past_raw(level)`` returns the storage-dtype views
+without any cast; the kernel reads bf16 or fp32 storage directly and widens in registers, so a
+bf16 cache never costs a full-past conversion per step.
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional, Tuple
+
+import torch
+
+
+class CacheManager:
+    """Per-layer packed KR/V in contiguous layer-major buffers (see module docstring)."""
+
+    def __init__(self, n_layer: int, max_seq: int, batch_size: int, n_head: int, n_latent: int,
+                 n_embd: int, device, *, compute_dtype: torch.dtype = torch.float32,
+                 storage_dtype: Optional[torch.dtype] = None, page_size: Optional[int] = None):
+        if max_seq < 1:
+            raise ValueError("max_seq must be >= 1")
+        if page_size is not None and page_size < 1:
+            raise ValueError("page_size must be >= 1 when set")
+        self.n_layer = n_layer
+        self.max_seq = max_seq
+        self.batch_size = batch_size
+        self.n_head = n_head
+        self.n_latent = n_latent
+        self.n_embd = n_embd
+        self.device = torch.device(device)
+        self.compute_dtype = compute_dtype
+        self.storage_dtype = storage_dtype or compute_dtype
+        self.storage_matches_compute = self.storage_dtype == self.compute_dtype
+        self.page_size = page_size
+        self.seq_len = 0
+        self._pending_t: Optional[int] = None
+        self.n_grows = 0
+        self.bytes_copied_on_grow = 0
+        self.capacity = max_seq if page_size is None else min(max_seq, page_size)
+        self._kr_buf = torch.zeros(n_layer, batch_size, n_head, self.capacity, n_latent,
+                                   dtype=self.storage_dtype, device=self.device)
+        self._v_buf = torch.zeros(n_layer, batch_size, 1, self.capacity, n_embd,
+                                  dtype=self.storage_dtype, device=self.device)
+
+    @property
+    def _kr(self) -> List[torch.Tensor]:
+        return [self._kr_buf[i] for i in range(self.n_layer)]
+
+    @property
+    def _v(self) -> List[torch.Tensor]:
+        return [self._v_buf[i] for i in range(self.n_layer)]
+
+    @classmethod
+    def from_config(cls, config, batch_size: int, max_seq: int, device, *,
+                    compute_dtype: torch.dtype = torch.float32,
+                    storage_dtype: Optional[torch.dtype] = None,
+                    page_size: Optional[int] = None) -> "CacheManager":
+        nh = config.n_head
+        D = config.n_embd
+        N = config.mlp_internal_dim_multiplier * D // nh
+        return cls(config.n_layer, max_seq, batch_size, nh, N, D, device,
+                   compute_dtype=compute_dtype, storage_dtype=storage_dtype, page_size=page_size)
+
+    # ------------------------------------------------------------------ capacity
+    def ensure_capacity(self, need: int) -> None:
+        self._ensure_capacity(need)
+
+    def _next_capacity(self, need: int) -> int:
+        ps = self.page_size
+        assert ps is not None
+        target = max(int(need), self.capacity * 2)
+        target = ((target + ps - 1) // ps) * ps
+        return min(self.max_seq, target)
+
+    def _ensure_capacity(self, need: int) -> None:
+        if need <= self.capacity:
+            return
+        if need > self.max_seq or self.page_size is None:
+            raise RuntimeError(f"cache overflow: need {need} slots but max_seq={self.max_seq}")
+        self._grow(self._next_capacity(need))
+
+    def _grow(self, new_cap: int) -> None:
+        if new_cap <= self.capacity:
+            return
+        kr = torch.empty(self.n_layer, self.batch_size, self.n_head, new_cap, self.n_latent,
+                         dtype=self.storage_dtype, device=self.device)
+        v = torch.empty(self.n_layer, self.batch_size, 1, new_cap, self.n_embd,
+                        dtype=self.storage_dtype, device=self.device)
+        used = self.seq_len + (self._pending_t or 0)
+        if used > 0:
+            kr[:, :, :, :used].copy_(self._kr_buf[:, :, :, :used])
+            v[:, :, :, :used].copy_(self._v_buf[:, :, :, :used])
+            self.bytes_copied_on_grow += used * self.n_layer * self.batch_size * (
+                self.n_head * self.n_latent + self.n_embd) * self._kr_buf.element_size()
+        self._kr_buf, self._v_buf = kr, v
+        self.capacity = new_cap
+        self.n_grows += 1
+
+    # --------------------------------------------------------------------- views
+    def get_past_raw(self, level: int) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor]]:
+        """Committed prefix of ``level`` as storage-dtype views (no cast, no copy)."""
+        if self.seq_len == 0:
+            return None, None
+        return (self._kr_buf[level].narrow(2, 0, self.seq_len),
+                self._v_buf[level].narrow(2, 0, self.seq_len))
+
+    def get_past(self, level: int) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor]]:
+        """Committed prefix of ``level``, cast to ``compute_dtype`` when storage differs."""
+        kr, v = self.get_past_raw(level)
+        if kr is not None and not self.storage_matches_compute:
+            kr = kr.to(self.compute_dtype)
+            v = v.to(self.compute_dtype)
+        return kr, v
+
+    def _track_pending(self, T: int) -> int:
+        end = self.seq_len + T
+        self._ensure_capacity(end)
+        if self._pending_t is None:
+            self._pending_t = T
+        elif self._pending_t != T:
+            raise RuntimeError(f"inconsistent append T: layer wrote {T}, pending={self._pending_t}")
+        return end
+
+    def reserve(self, level: int, T: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Writable views of the next block ``[seq_len, seq_len+T)`` of ``level`` (no copy).
+
+        A paging grow may happen first, which invalidates previously returned views.
+        """
+        if T < 1:
+            raise ValueError("reserve T must be >= 1")
+        self._track_pending(T)
+        return (self._kr_buf[level].narrow(2, self.seq_len, T),
+                self._v_buf[level].narrow(2, self.seq_len, T))
+
+    def _write_block(self, level: int, new_kr: torch.Tensor, new_v: torch.Tensor) -> int:
+        T = new_kr.size(2)
+        if T != new_v.size(2):
+            raise ValueError(f"kr T={T} != v T={new_v.size(2)}")
+        end = self._track_pending(T)
+        self._kr_buf[level].narrow(2, self.seq_len, T).copy_(new_kr)
+        self._v_buf[level].narrow(2, self.seq_len, T).copy_(new_v)
+        return end
+
+    def append(self, level: int, new_kr: torch.Tensor, new_v: torch.Tensor) -> None:
+        self._write_block(level, new_kr, new_v)
+
+    def stage(self, level: int, new_kr: torch.Tensor, new_v: torch.Tensor):
+        """Write the new block and return past+new views (cast when storage differs)."""
+        end = self._write_block(level, new_kr, new_v)
+        kr = self._kr_buf[level].narrow(2, 0, end)
+        v = self._v_buf[level].narrow(2, 0, end)
+        if not self.storage_matches_compute:
+            kr, v = kr.to(self.compute_dtype), v.to(self.compute_dtype)
+        return kr, v
+
+    def commit(self) -> None:
+        if self._pending_t is None:
+            return
+        self.seq_len += self._pending_t
+        self._pending_t = None
+
+    def reset(self) -> None:
+        self.seq_len = 0
+        self._pending_t = None
+        self.n_grows = 0
+        self.bytes_copied_on_grow = 0
+
+    @property
+    def bytes_allocated(self) -> int:
+        return (self._kr_buf.numel() * self._kr_buf.element_size()
+                + self._v_buf.numel() * self._v_buf.element_size())

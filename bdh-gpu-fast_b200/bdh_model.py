@@ -1,0 +1,240 @@
+"""BDH ("Dragon Hatchling") language model on the B200 attention path.
+
+A compact restatement of the reference model (``bdh_baseline.py:32-139`` architecture,
+``bdh.py:947-1072`` cached forward) that routes its attention through
+``kernels.attention_dispatch``. Parameter names, shapes and initialisation match the
+reference so ``state_dict``s load in either direction:
+
+    embed (V, D) · encoder (nh, D, N) · encoder_v (nh, D, N) · decoder (nh*N, D) ·
+    lm_head (D, V) · attn.freqs (1, 1, 1, N) buffer
+
+Per layer (all LayerNorms affine-free)::
+
+    x_sparse = relu(x @ encoder)                              (B, nh, T, N)
+    yKV      = LN( tril(R(x_sparse) R(x_sparse)^T, -1) @ x )  (B, nh, T, D)
+    y_sparse = relu(yKV @ encoder_v)
+    x        = LN( x + LN( (x_sparse * y_sparse) @ decoder ) )
+
+With ``BDH_ATTN_IMPL=cuda_sm100`` the RoPE is fused into the attention (in-register cos/sin,
+no tables), the cached decode step rotates the new query and writes it into the cache slot
+inside the decode kernel, and the cache is read in its storage dtype without copies. The
+encoder / decoder projections stay cuBLAS GEMMs (torch).
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import math
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from bdh_cache import CacheManager
+from kernels.attention import eager_decode_attn
+from kernels.attention_dispatch import (
+    bdh_attn,
+    bdh_rope_attn,
+    bdh_rope_attn_decode,
+    resolve_attn_impl,
+    rope_tables,
+)
+from kernels.rope import eager_rope_rotate
+
+
+@dataclasses.dataclass
+class BDHConfig:
+    n_layer: int = 6
+    n_embd: int = 256
+    dropout: float = 0.1
+    n_head: int = 4
+    mlp_internal_dim_multiplier: int = 128
+    vocab_size: int = 256
+
+
+def get_freqs(n: int, theta: float, dtype: torch.dtype) -> torch.Tensor:
+    """freq[i] = theta^(-2*floor(i/2)/n) / (2*pi) (reference bdh.py:41-49)."""
+    t = torch.arange(0, n, 1, dtype=dtype)
+    q = (t / 2).floor() * 2
+    return 1.0 / (theta ** (q / n)) / (2 * math.pi)
+
+
+def _try_extend_seq(past: torch.Tensor, new: torch.Tensor) -> Optional[torch.Tensor]:
+    """past||new as one view when ``new`` directly follows ``past`` in the same storage."""
+    if past.untyped_storage().data_ptr() != new.untyped_storage().data_ptr():
+        return None
+    if past.stride() != new.stride() or past.shape[:-2] != new.shape[:-2]:
+        return None
+    if new.storage_offset() != past.storage_offset() + past.size(-2) * past.stride(-2):
+        return None
+    return past.as_strided((*past.shape[:-2], past.size(-2) + new.size(-2), past.size(-1)),
+                           past.stride())
+
+
+class Attention(nn.Module):
+    """Strict-causal linear attention with BDH RoPE; K is Q (shared latent)."""
+
+    def __init__(self, config: BDHConfig):
+        super().__init__()
+        nh, D = config.n_head, config.n_embd
+        N = config.mlp_internal_dim_multiplier * D // nh
+        self.freqs = nn.Buffer(get_freqs(N, theta=2 ** 16, dtype=torch.float32).view(1, 1, 1, N))
+        self._attn_impl_override: Optional[str] = None
+
+    def rope_cos_sin(self, T: int, rope_start: int, device):
+        return rope_tables(self.freqs, T, rope_start, device)
+
+    def forward(self, Q, K, V, rope_start: int = 0, past_kr=None, past_v=None, out_kr=None,
+                past_is_raw: bool = False):
+        """Returns ``(out, QR, V)``; QR/V are this block's keys/values for the cache.
+
+        ``past_kr``/``past_v``: packed past (``past_is_raw``: in the cache storage dtype).
+        ``out_kr``: optional cache slot receiving QR.
+        """
+        assert K is Q
+        impl = self._attn_impl_override or resolve_attn_impl()
+        B, nh, T, _ = Q.shape
+        if past_kr is None:
+            out, QR = bdh_rope_attn(Q, V, self.freqs, rope_start, impl=impl, qr_out=out_kr)
+            return out, QR, V
+        S = past_kr.size(2)
+        if impl == "cuda_sm100" and T == 1:
+            if out_kr is not None:
+                out = bdh_rope_attn_decode(Q, past_kr, past_v, self.freqs, rope_start, impl=impl,
+                                           kr_slot=out_kr)
+                return out, out_kr, V
+            from kernels.sm100_attn import rope_rotate, tril_decode
+
+            QR = rope_rotate(Q, self.freqs, rope_start)
+            return tril_decode(QR, past_kr, past_v), QR, V
+        # eager T=1 decode, or a multi-token block continuing a past
+        cos, sin = rope_tables(self.freqs, T, rope_start, Q.device)
+        QR = eager_rope_rotate(Q, cos, sin, out=out_kr) if impl == "eager" else None
+        if QR is None:
+            from kernels.sm100_attn import rope_rotate
+
+            QR = rope_rotate(Q, self.freqs, rope_start, out=out_kr)
+        if past_is_raw and past_kr.dtype != QR.dtype:
+            past_kr, past_v = past_kr.to(QR.dtype), past_v.to(QR.dtype)
+        if T == 1:
+            return eager_decode_attn(QR, past_kr, past_v.to(QR.dtype)), QR, V
+        KR_all = _try_extend_seq(past_kr, QR)
+        V_all = _try_extend_seq(past_v, V) if KR_all is not None else None
+        if KR_all is None or V_all is None:
+            KR_all = torch.cat([past_kr, QR.to(past_kr.dtype)], dim=2)
+            V_all = torch.cat([past_v, V.to(past_v.dtype)], dim=2)
+        Vq = V_all.to(QR.dtype) if impl == "cuda_sm100" else V_all
+        out = bdh_attn(KR_all.to(QR.dtype), KR_all.to(QR.dtype), Vq, impl=impl)[:, :, S:, :]
+        return out, QR, V
+
+
+class BDH(nn.Module):
+    def __init__(self, config: BDHConfig):
+        super().__init__()
+        self.config = config
+        nh, D = config.n_head, config.n_embd
+        N = config.mlp_internal_dim_multiplier * D // nh
+        self.decoder = nn.Parameter(torch.zeros((nh * N, D)).normal_(std=0.02))
+        self.encoder = nn.Parameter(torch.zeros((nh, D, N)).normal_(std=0.02))
+        self.attn = Attention(config)
+        self.ln = nn.LayerNorm(D, elementwise_affine=False, bias=False)
+        self.embed = nn.Embedding(config.vocab_size, D)
+        self.drop = nn.Dropout(config.dropout)
+        self.encoder_v = nn.Parameter(torch.zeros((nh, D, N)).normal_(std=0.02))
+        self.lm_head = nn.Parameter(torch.zeros((D, config.vocab_size)).normal_(std=0.02))
+        nn.init.normal_(self.embed.weight, mean=0.0, std=0.02)
+
+    def _ln(self, x: torch.Tensor) -> torch.Tensor:
+        return F.layer_norm(x, (x.size(-1),), eps=self.ln.eps)
+
+    def forward(self, idx: torch.Tensor, targets: Optional[torch.Tensor] = None,
+                cache: Optional[CacheManager] = None, *, logits_out: Optional[torch.Tensor] = None):
+        """Logits ``(B, T, V)`` (and the CE loss with ``targets``).
+
+        ``cache``: a ``CacheManager``; ``idx`` is then the next block and RoPE continues at
+        ``cache.seq_len``. ``logits_out``: (B, V) fp32 buffer for the last-token logits (T == 1).
+        """
+        C = self.config
+        B, T = idx.shape
+        nh, D = C.n_head, C.n_embd
+        N = D * C.mlp_internal_dim_multiplier // nh
+        x = self._ln(self.embed(idx))  # (B, T, D)
+        rope_start = cache.seq_len if cache is not None else 0
+        impl = self.attn._attn_impl_override or resolve_attn_impl()
+        grad = torch.is_grad_enabled()
+        for level in range(C.n_layer):
+            x_bthn = F.relu(torch.einsum("btd,hdn->bthn", x, self.encoder))
+            x_sparse = x_bthn.permute(0, 2, 1, 3)  # (B, nh, T, N) view
+            v_tok = x.unsqueeze(1)
+            past_kr = past_v = out_kr = None
+            raw = False
+            if cache is not None:
+                native = impl == "cuda_sm100" and not grad
+                eager_inplace = (not grad and cache.storage_matches_compute
+                                 and v_tok.dtype == cache.storage_dtype)
+                if native or eager_inplace:
+                    dst_kr, dst_v = cache.reserve(level, T)
+                    if native:
+                        past_kr, past_v = cache.get_past_raw(level)
+                        raw = True
+                    else:
+                        past_kr, past_v = cache.get_past(level)
+                    dst_v.copy_(v_tok)
+                    out_kr = dst_kr
+                    v_tok = dst_v
+                else:
+                    past_kr, past_v = cache.get_past(level)
+            y_kv, new_kr, new_v = self.attn(x_sparse, x_sparse, v_tok, rope_start=rope_start,
+                                            past_kr=past_kr, past_v=past_v, out_kr=out_kr,
+                                            past_is_raw=raw)
+            if cache is not None and out_kr is None:
+                cache.append(level, new_kr, new_v)
+            y_kv = self._ln(y_kv)
+            y_bthn = F.relu(torch.einsum("bhtd,hdn->bthn", y_kv, self.encoder_v))
+            xy = self.drop(x_bthn * y_bthn)
+            y_mlp = F.linear(xy.reshape(B, T, nh * N), self.decoder.t())
+            x = self._ln(x + self._ln(y_mlp))
+        if cache is not None:
+            cache.commit()
+        if logits_out is not None:
+            if T != 1:
+                raise ValueError("logits_out requires T==1 decode")
+            torch.mm(x[:, -1, :].to(logits_out.dtype), self.lm_head.to(logits_out.dtype), out=logits_out)
+            return logits_out, None
+        logits = F.linear(x, self.lm_head.t())
+        loss = None
+        if targets is not None:
+            loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1))
+        return logits, loss
+
+    @torch.inference_mode()
+    def generate(self, idx: torch.Tensor, max_new_tokens: int, temperature: float = 1.0,
+                 top_k: Optional[int] = None, *, cache_dtype: Optional[torch.dtype] = None,
+                 amp_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        """Autoregressive sampling with the packed cache (prefill, then T=1 steps)."""
+        was_training = self.training
+        self.eval()
+        B, T0 = idx.shape
+        cache = CacheManager.from_config(self.config, B, T0 + max_new_tokens, idx.device,
+                                         storage_dtype=cache_dtype)
+        out = torch.empty(B, T0 + max_new_tokens, dtype=idx.dtype, device=idx.device)
+        out[:, :T0] = idx
+        ctx = (torch.autocast(idx.device.type, dtype=amp_dtype) if amp_dtype is not None
+               else torch.autocast(idx.device.type, enabled=False))
+        with ctx:
+            logits, _ = self(idx, cache=cache)
+            step = logits[:, -1, :].float()
+            for t in range(max_new_tokens):
+                step = step / temperature
+                if top_k is not None:
+                    vals, _ = torch.topk(step, min(top_k, step.size(-1)))
+                    step = step.masked_fill(step < vals[:, [-1]], float("-inf"))
+                nxt = torch.multinomial(F.softmax(step, dim=-1), 1)
+                out[:, T0 + t] = nxt[:, 0]
+                if t + 1 < max_new_tokens:
+                    logits, _ = self(nxt, cache=cache)
+                    step = logits[:, -1, :].float()
+        if was_training:
+            self.train()
+        return out

@@ -1,0 +1,247 @@
+// extern "C" boundary of libbdh_sm100.so: argument validation, workspace carving and kernel
+// sequencing. No torch types cross this boundary and nothing here allocates device memory.
+#include <cstring>
+#include <sstream>
+#include <string>
+
+#include "bdh_sm100.h"
+#include "internal.h"
+#include "tma_host.h"
+
+namespace bdh {
+__device__ int g_device_error = 0;  // first pipeline failure code of any kernel on this device
+
+namespace {
+
+int* device_error_ptr() {
+  static int* cache[64] = {nullptr};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<int*>(p);
+  }
+  return cache[dev];
+}
+
+int fail(int code, const std::string& msg) {
+  set_error(msg);
+  return code;
+}
+
+bool dtype_ok(int d) { return d == BDH_DTYPE_F32 || d == BDH_DTYPE_BF16; }
+int esize(int d) { return d == BDH_DTYPE_F32 ? 4 : 2; }
+
+size_t align_up(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Workspace layout of the forward (byte offsets), shared by the size query and the call.
+struct FwdLayout {
+  size_t q_hi = 0, q_lo = 0, k_hi = 0, k_lo = 0, v_hi = 0, v_lo = 0, p_hi = 0, p_lo = 0;
+  size_t total = 0;
+};
+
+FwdLayout fwd_layout(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T, int64_t N, int64_t D,
+                     bool k_is_q) {
+  FwdLayout L;
+  size_t off = 0;
+  const int e = esize(dtype);
+  if (dtype == BDH_DTYPE_F32) {
+    const size_t qbytes = align_up(static_cast<size_t>(B * H * T * N) * 4);
+    const size_t vbytes = align_up(static_cast<size_t>(B * Hv * D * vt_ld(T)) * 4);
+    L.q_hi = off; off += qbytes;
+    L.q_lo = off; off += qbytes;
+    if (!k_is_q) {
+      L.k_hi = off; off += qbytes;
+      L.k_lo = off; off += qbytes;
+    }
+    L.v_hi = off; off += vbytes;
+    L.v_lo = off; off += vbytes;
+  }
+  const size_t pbytes = align_up(static_cast<size_t>(B * H * T * score_ld(T)) * e);
+  L.p_hi = off; off += pbytes;
+  L.p_lo = off; off += pbytes;
+  L.total = off;
+  return L;
+}
+
+bool check_rows(const char* what, const int64_t s[4], int elem, std::string* msg) {
+  if (s[3] != 1) {
+    *msg = std::string(what) + ": the last dimension must be contiguous (stride 1)";
+    return false;
+  }
+  return true;
+}
+
+}  // namespace
+}  // namespace bdh
+
+using namespace bdh;
+
+extern "C" {
+
+int bdh_abi_version(void) { return BDH_ABI_VERSION; }
+
+const char* bdh_last_error(void) { return last_error(); }
+
+int bdh_device_error(int device, int* code, int reset) {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (cudaSetDevice(device) != cudaSuccess) return fail(BDH_ERR_CUDA, "bdh_device_error: bad device");
+  int* p = device_error_ptr();
+  int v = 0;
+  cudaError_t e = p ? cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) : cudaErrorInvalidSymbol;
+  if (e == cudaSuccess && reset) {
+    const int zero = 0;
+    e = cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice);
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(BDH_ERR_CUDA, std::string("bdh_device_error: ") + cudaGetErrorString(e));
+  if (code) *code = v;
+  return BDH_OK;
+}
+
+int bdh_rope_rotate(const void* x, int x_dtype, const int64_t x_strides[4], void* y, int y_dtype,
+                    const int64_t y_strides[4], void* y_lo, const float* freqs, int64_t B,
+                    int64_t H, int64_t T, int64_t N, int64_t pos0, void* stream) {
+  if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(BDH_ERR_INVALID, "rope: dtype must be f32 or bf16");
+  if (B < 0 || H < 0 || T < 0 || N < 0) return fail(BDH_ERR_INVALID, "rope: negative size");
+  if (N % 2 != 0) return fail(BDH_ERR_INVALID, "rope: RoPE last dim must be even");
+  if (x_strides[3] != 1 || y_strides[3] != 1) return fail(BDH_ERR_INVALID, "rope: last dim must be contiguous");
+  if (y_lo != nullptr && y_dtype != BDH_DTYPE_F32) return fail(BDH_ERR_INVALID, "rope: y_lo requires f32 output");
+  if (B * H * T * N > 0 && (x == nullptr || y == nullptr || freqs == nullptr))
+    return fail(BDH_ERR_INVALID, "rope: null pointer");
+  return launch_rope(x, x_dtype, x_strides, y, y_dtype, y_strides, static_cast<float*>(y_lo), freqs,
+                     B, H, T, N, pos0, static_cast<cudaStream_t>(stream));
+}
+
+size_t bdh_tril_score_v_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,
+                                       int64_t N, int64_t D, int k_is_q) {
+  if (!dtype_ok(dtype)) return 0;
+  return fwd_layout(dtype, B, H, Hv, T, N, D, k_is_q != 0).total;
+}
+
+int bdh_tril_score_v(const void* q, const int64_t q_strides[4], const void* k,
+                     const int64_t k_strides[4], const void* v, const int64_t v_strides[4],
+                     int dtype, void* out, const int64_t out_strides[4], int out_dtype,
+                     int64_t B, int64_t H, int64_t Hv, int64_t T, int64_t N, int64_t D,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (!dtype_ok(dtype) || !dtype_ok(out_dtype))
+    return fail(BDH_ERR_INVALID, "tril_score_v: dtype must be f32 or bf16");
+  if (B < 0 || H < 0 || T < 0 || N < 0 || D < 0)
+    return fail(BDH_ERR_INVALID, "tril_score_v: negative size");
+  if (Hv != 1 && Hv != H) return fail(BDH_ERR_INVALID, "tril_score_v: v heads must equal q heads or 1");
+  if (B * H * T * D == 0) return BDH_OK;
+  if (N == 0) return fail(BDH_ERR_INVALID, "tril_score_v: latent width N must be positive");
+  std::string msg;
+  if (!check_rows("q", q_strides, esize(dtype), &msg) || !check_rows("k", k_strides, esize(dtype), &msg) ||
+      !check_rows("v", v_strides, esize(dtype), &msg) ||
+      !check_rows("out", out_strides, esize(out_dtype), &msg))
+    return fail(BDH_ERR_INVALID, "tril_score_v: " + msg);
+  if (T > (int64_t(1) << 24) || B * H > (int64_t(1) << 30))
+    return fail(BDH_ERR_INVALID, "tril_score_v: sizes beyond the supported range");
+  const bool k_is_q = (k == q) && std::memcmp(q_strides, k_strides, 4 * sizeof(int64_t)) == 0;
+  const FwdLayout L = fwd_layout(dtype, B, H, Hv, T, N, D, k_is_q);
+  if (workspace == nullptr || workspace_bytes < L.total) {
+    std::ostringstream os;
+    os << "tril_score_v: workspace of " << L.total << " bytes required, got " << workspace_bytes;
+    return fail(BDH_ERR_WORKSPACE, os.str());
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* err = device_error_ptr();
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  FwdArgs a;
+  a.dtype = dtype;
+  a.out = out;
+  a.out_dtype = out_dtype;
+  std::memcpy(a.out_strides, out_strides, sizeof(a.out_strides));
+  a.B = B; a.H = H; a.Hv = Hv; a.T = T; a.N = N; a.D = D;
+  if (dtype == BDH_DTYPE_F32) {
+    // fp32 operands become exact tf32 hi/lo pairs (contiguous) for the 3-product path.
+    const int64_t qcs[4] = {H * T * N, T * N, N, 1};
+    float* qh = reinterpret_cast<float*>(ws + L.q_hi);
+    float* ql = reinterpret_cast<float*>(ws + L.q_lo);
+    int rc = launch_split_tf32(static_cast<const float*>(q), q_strides, qh, ql, B, H, T, N, st);
+    if (rc) return rc;
+    a.q = qh; a.q_lo = ql;
+    std::memcpy(a.q_strides, qcs, sizeof(qcs));
+    if (k_is_q) {
+      a.k = qh; a.k_lo = ql;
+    } else {
+      float* kh = reinterpret_cast<float*>(ws + L.k_hi);
+      float* kl = reinterpret_cast<float*>(ws + L.k_lo);
+      rc = launch_split_tf32(static_cast<const float*>(k), k_strides, kh, kl, B, H, T, N, st);
+      if (rc) return rc;
+      a.k = kh; a.k_lo = kl;
+    }
+    std::memcpy(a.k_strides, qcs, sizeof(qcs));
+    float* vh = reinterpret_cast<float*>(ws + L.v_hi);
+    float* vl = reinterpret_cast<float*>(ws + L.v_lo);
+    // V is consumed transposed ([B*Hv][D][keys]) so that both tf32 operands are K-major.
+    rc = launch_split_tf32_t(static_cast<const float*>(v), v_strides, vh, vl, B, Hv, T, D,
+                             vt_ld(T), st);
+    if (rc) return rc;
+    a.v = vh; a.v_lo = vl;
+  } else {
+    a.q = q; a.k = k; a.v = v;
+    std::memcpy(a.q_strides, q_strides, sizeof(a.q_strides));
+    std::memcpy(a.k_strides, k_strides, sizeof(a.k_strides));
+    std::memcpy(a.v_strides, v_strides, sizeof(a.v_strides));
+  }
+  int rc = launch_score(a, ws + L.p_hi, ws + L.p_lo, st, err);
+  if (rc) return rc;
+  return launch_value(a, ws + L.p_hi, ws + L.p_lo, st, err);
+}
+
+size_t bdh_tril_decode_workspace_size(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t D) {
+  return decode_workspace_bytes(B, H, Tq, S, D);
+}
+
+int bdh_tril_decode(const void* q, const int64_t q_strides[4], int q_dtype, const void* k_past,
+                    const int64_t k_strides[4], const void* v_past, const int64_t v_strides[4],
+                    int kv_dtype, void* out, const int64_t out_strides[4], int64_t B, int64_t H,
+                    int64_t Hv, int64_t Tq, int64_t S, int64_t N, int64_t D, const float* freqs,
+                    int64_t pos, void* kr_slot, const int64_t slot_strides[4], void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (!dtype_ok(q_dtype) || !dtype_ok(kv_dtype)) return fail(BDH_ERR_INVALID, "tril_decode: dtype must be f32 or bf16");
+  if (B < 0 || H < 0 || Tq < 0 || S < 0 || N < 0 || D < 0) return fail(BDH_ERR_INVALID, "tril_decode: negative size");
+  if (Hv != 1 && Hv != H) return fail(BDH_ERR_INVALID, "tril_decode: v_past heads must equal q heads or 1");
+  if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || out_strides[3] != 1)
+    return fail(BDH_ERR_INVALID, "tril_decode: last dimension must be contiguous");
+  if (kr_slot != nullptr && (freqs == nullptr || slot_strides == nullptr || slot_strides[3] != 1))
+    return fail(BDH_ERR_INVALID, "tril_decode: kr_slot needs freqs and contiguous slot rows");
+  if (B * H * Tq == 0) return BDH_OK;
+  if (S > (int64_t(1) << 30) || N > 48 * 1024) return fail(BDH_ERR_INVALID, "tril_decode: sizes beyond the supported range");
+  const size_t need = decode_workspace_bytes(B, H, Tq, S, D);
+  if (workspace == nullptr || workspace_bytes < need) {
+    std::ostringstream os;
+    os << "tril_decode: workspace of " << need << " bytes required, got " << workspace_bytes;
+    return fail(BDH_ERR_WORKSPACE, os.str());
+  }
+  DecodeArgs a;
+  a.q = q; a.q_dtype = q_dtype; a.k = k_past; a.v = v_past; a.kv_dtype = kv_dtype; a.out = out;
+  std::memcpy(a.q_strides, q_strides, sizeof(a.q_strides));
+  std::memcpy(a.k_strides, k_strides, sizeof(a.k_strides));
+  std::memcpy(a.v_strides, v_strides, sizeof(a.v_strides));
+  std::memcpy(a.out_strides, out_strides, sizeof(a.out_strides));
+  a.B = B; a.H = H; a.Hv = Hv; a.Tq = Tq; a.S = S; a.N = N; a.D = D;
+  a.freqs = freqs; a.pos = pos; a.slot = kr_slot;
+  if (slot_strides != nullptr) std::memcpy(a.slot_strides, slot_strides, sizeof(a.slot_strides));
+  return launch_decode(a, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream));
+}
+
+size_t bdh_tril_score_v_bwd_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,
+                                           int64_t N, int64_t D, int k_is_q) {
+  (void)dtype; (void)B; (void)H; (void)Hv; (void)T; (void)N; (void)D; (void)k_is_q;
+  return 0;
+}
+
+int bdh_tril_score_v_bwd(const void*, const int64_t*, const void*, const int64_t*, const void*,
+                         const int64_t*, const void*, const int64_t*, int, void*, const int64_t*,
+                         void*, const int64_t*, void*, const int64_t*, int64_t, int64_t, int64_t,
+                         int64_t, int64_t, int64_t, const float*, int64_t, void*, size_t, void*) {
+  return fail(BDH_ERR_INVALID, "tril_score_v_bwd: not available in this build");
+}
+
+}  // extern "C"

@@ -1,0 +1,284 @@
+// Cached decode step: out[b,h,tq] = sum_j (q[b,h,tq] . K_past[b,h,j]) V_past[b,hv,j]
+// (reference: csrc/tril_attn_cuda.cu:431-542 tril_decode_*_kernel, kernels/attention.py:193-219
+// _two_gemm_decode; every cached key precedes the query, so there is no mask).
+//
+// HBM-bound: the whole key history is streamed once per step. Grid = (split, b*h, tq); each
+// CTA owns DEC_ROWS consecutive cached rows of one (b, h):
+//   1. q (optionally RoPE-rotated in registers, and then also written to this step's cache
+//      slot by split 0) is staged in shared memory as fp32;
+//   2. each warp streams two key rows at a time with 16-byte coalesced loads straight from
+//      the capacity-strided cache view (no contiguous copy), widening bf16 in registers, and
+//      reduces the dot products with warp shuffles;
+//   3. the CTA forms its partial out = sum_j s_j V_j (one thread per output column);
+//   4. a second small kernel sums the per-split partials in a fixed order (deterministic).
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+#include "internal.h"
+#include "tma_host.h"
+
+namespace bdh {
+
+namespace {
+
+constexpr int kDecThreads = 256;
+constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kDecRows = 64;  // cached rows per CTA
+
+__device__ __forceinline__ float bf16_round_d(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__device__ __forceinline__ void rope_cis_d(float pos, float f, float& c, float& s) {
+  float ph = __fmul_rn(pos, f);
+  ph = __fsub_rn(ph, floorf(ph));
+  ph = __fmul_rn(ph, __int_as_float(0x40C90FDB));
+  sincosf(ph, &s, &c);
+}
+
+template <typename T>
+__device__ __forceinline__ float ld_elem(const T* p, int64_t i);
+template <>
+__device__ __forceinline__ float ld_elem<float>(const float* p, int64_t i) {
+  return p[i];
+}
+template <>
+__device__ __forceinline__ float ld_elem<uint16_t>(const uint16_t* p, int64_t i) {
+  return bf16_bits_to_f32(p[i]);
+}
+template <typename T>
+__device__ __forceinline__ void st_elem(T* p, int64_t i, float v);
+template <>
+__device__ __forceinline__ void st_elem<float>(float* p, int64_t i, float v) {
+  p[i] = v;
+}
+template <>
+__device__ __forceinline__ void st_elem<uint16_t>(uint16_t* p, int64_t i, float v) {
+  p[i] = static_cast<uint16_t>(f32_to_bf16_bits(v));
+}
+
+// Dot products of q (shared, fp32) with two key rows; VEC = 16-byte loads along N.
+template <typename TK, bool VEC>
+__device__ __forceinline__ void dot2(const float* __restrict__ qs, const TK* __restrict__ k0,
+                                     const TK* __restrict__ k1, int N, bool has1, float& d0,
+                                     float& d1) {
+  const int lane = threadIdx.x & 31;
+  float a0 = 0.f, a1 = 0.f;
+  if (VEC) {
+    constexpr int E = 16 / sizeof(TK);  // elements per 16-byte load
+#pragma unroll 4
+    for (int n = lane * E; n < N; n += 32 * E) {
+      float qv[E];
+#pragma unroll
+      for (int i = 0; i < E; i += 4) {
+        const float4 t = *reinterpret_cast<const float4*>(qs + n + i);
+        qv[i] = t.x; qv[i + 1] = t.y; qv[i + 2] = t.z; qv[i + 3] = t.w;
+      }
+      const uint4 u0 = __ldcs(reinterpret_cast<const uint4*>(k0 + n));
+      uint4 u1 = make_uint4(0, 0, 0, 0);
+      if (has1) u1 = __ldcs(reinterpret_cast<const uint4*>(k1 + n));
+      const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w};
+      const uint32_t w1[4] = {u1.x, u1.y, u1.z, u1.w};
+      if (sizeof(TK) == 4) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          a0 = fmaf(qv[i], __uint_as_float(w0[i]), a0);
+          a1 = fmaf(qv[i], __uint_as_float(w1[i]), a1);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          a0 = fmaf(qv[2 * i], bf16_bits_to_f32(w0[i] & 0xFFFFu), a0);
+          a0 = fmaf(qv[2 * i + 1], bf16_bits_to_f32(w0[i] >> 16), a0);
+          a1 = fmaf(qv[2 * i], bf16_bits_to_f32(w1[i] & 0xFFFFu), a1);
+          a1 = fmaf(qv[2 * i + 1], bf16_bits_to_f32(w1[i] >> 16), a1);
+        }
+      }
+    }
+  } else {
+    for (int n = lane; n < N; n += 32) {
+      a0 = fmaf(qs[n], ld_elem(k0, n), a0);
+      if (has1) a1 = fmaf(qs[n], ld_elem(k1, n), a1);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+    a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+  }
+  d0 = a0;
+  d1 = a1;
+}
+
+template <typename TQ, typename TK, bool VEC>
+__global__ void __launch_bounds__(kDecThreads) decode_partial_kernel(
+    const TQ* __restrict__ q, const TK* __restrict__ kp, const TK* __restrict__ vp,
+    float* __restrict__ partial, TK* __restrict__ slot, const float* __restrict__ freqs,
+    int H, int Hv, int Tq, int S, int N, int D, int64_t qsb, int64_t qsh, int64_t qst,
+    int64_t ksb, int64_t ksh, int64_t kst, int64_t vsb, int64_t vsh, int64_t vst, int64_t ssb,
+    int64_t ssh, int64_t sst, int64_t pos) {
+  extern __shared__ float dsm[];
+  float* qs = dsm;              // N floats
+  float* sc = dsm + N;          // kDecRows scores
+  const int split = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int tq = blockIdx.z;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int hv = Hv == 1 ? 0 : h;
+  const int nsplit = gridDim.x;
+
+  // 1. stage q (rotated when freqs is given).
+  const TQ* qr = q + b * qsb + h * qsh + tq * qst;
+  if (freqs != nullptr) {
+    constexpr bool BF16 = sizeof(TQ) == 2;
+    const float p = static_cast<float>(pos + tq);
+    for (int n = threadIdx.x * 2; n < N; n += blockDim.x * 2) {
+      float c0, s0, c1, s1;
+      rope_cis_d(p, freqs[n], c0, s0);
+      rope_cis_d(p, freqs[n + 1], c1, s1);
+      const float x0 = ld_elem(qr, n), x1 = ld_elem(qr, n + 1);
+      float y0, y1;
+      if (BF16) {
+        y0 = bf16_round_d(__fadd_rn(bf16_round_d(__fmul_rn(x0, c0)), bf16_round_d(__fmul_rn(-x1, s0))));
+        y1 = bf16_round_d(__fadd_rn(bf16_round_d(__fmul_rn(x1, c1)), bf16_round_d(__fmul_rn(x0, s1))));
+      } else {
+        y0 = __fsub_rn(__fmul_rn(x0, c0), __fmul_rn(x1, s0));
+        y1 = __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(x0, s1));
+      }
+      qs[n] = y0;
+      qs[n + 1] = y1;
+      if (slot != nullptr && split == 0) {
+        TK* sr = slot + b * ssb + h * ssh + tq * sst;
+        st_elem(sr, n, y0);
+        st_elem(sr, n + 1, y1);
+      }
+    }
+  } else {
+    for (int n = threadIdx.x; n < N; n += blockDim.x) qs[n] = ld_elem(qr, n);
+  }
+  __syncthreads();
+
+  // 2. scores for this split's rows.
+  const int j0 = split * kDecRows;
+  const int rows = max(0, min(kDecRows, S - j0));
+  const int warp = threadIdx.x >> 5;
+  const TK* kbase = kp + b * ksb + h * ksh;
+  for (int r = warp * 2; r < rows; r += kDecWarps * 2) {
+    const bool has1 = r + 1 < rows;
+    float d0, d1;
+    dot2<TK, VEC>(qs, kbase + (j0 + r) * kst, kbase + (j0 + r + (has1 ? 1 : 0)) * kst, N, has1,
+                  d0, d1);
+    if ((threadIdx.x & 31) == 0) {
+      sc[r] = d0;
+      if (has1) sc[r + 1] = d1;
+    }
+  }
+  __syncthreads();
+
+  // 3. partial out = sum_j s_j V_j.
+  const TK* vbase = vp + b * vsb + hv * vsh;
+  float* dst = partial + ((static_cast<int64_t>(split) * gridDim.y + bh) * Tq + tq) * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int r = 0; r < rows; ++r) acc = fmaf(sc[r], ld_elem(vbase + (j0 + r) * vst, d), acc);
+    dst[d] = acc;
+  }
+  (void)nsplit;
+}
+
+template <typename TO>
+__global__ void decode_reduce_kernel(const float* __restrict__ partial, TO* __restrict__ out,
+                                     int nsplit, int H, int Tq, int D, int64_t BHT, int64_t osb,
+                                     int64_t osh, int64_t ost) {
+  const int64_t row = blockIdx.x;  // (b*H + h)*Tq + tq
+  const int tq = static_cast<int>(row % Tq);
+  const int64_t bh = row / Tq;
+  const int h = static_cast<int>(bh % H);
+  const int64_t b = bh / H;
+  TO* o = out + b * osb + h * osh + tq * ost;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < nsplit; ++s) acc += partial[(s * BHT + row) * D + d];
+    st_elem(o, d, acc);
+  }
+}
+
+}  // namespace
+
+int decode_splits(int64_t S) { return static_cast<int>(std::max<int64_t>(1, (S + kDecRows - 1) / kDecRows)); }
+
+size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t D) {
+  return static_cast<size_t>(decode_splits(S)) * static_cast<size_t>(B * H * Tq * D) * sizeof(float);
+}
+
+int launch_decode(const DecodeArgs& a, float* partial, cudaStream_t stream) {
+  if (a.B * a.H * a.Tq == 0 || a.D == 0) {
+    return BDH_OK;
+  }
+  const int nsplit = decode_splits(a.S);
+  const int ke = a.kv_dtype == BDH_DTYPE_F32 ? 4 : 2;
+  bool vec = (a.N % (16 / ke) == 0) && ((reinterpret_cast<uintptr_t>(a.k) & 15u) == 0) &&
+             (a.k_strides[0] * ke) % 16 == 0 && (a.k_strides[1] * ke) % 16 == 0 &&
+             (a.k_strides[2] * ke) % 16 == 0;
+  if (a.freqs != nullptr && (a.N % 2) != 0) {
+    set_error("decode: fused RoPE needs an even latent width");
+    return BDH_ERR_INVALID;
+  }
+  const dim3 grid(static_cast<unsigned>(nsplit), static_cast<unsigned>(a.B * a.H),
+                  static_cast<unsigned>(a.Tq));
+  const size_t smem = (static_cast<size_t>(a.N) + kDecRows) * sizeof(float);
+  if (smem > 200 * 1024) {
+    set_error("decode: latent width too large for the shared-memory q stage");
+    return BDH_ERR_INVALID;
+  }
+  const int Hi = static_cast<int>(a.H), Hvi = static_cast<int>(a.Hv), Tqi = static_cast<int>(a.Tq);
+  const int Si = static_cast<int>(a.S), Ni = static_cast<int>(a.N), Di = static_cast<int>(a.D);
+#define BDH_DEC_LAUNCH(TQ, TK, V)                                                                 \
+  do {                                                                                            \
+    auto kern = decode_partial_kernel<TQ, TK, V>;                                                 \
+    if (smem > 48 * 1024)                                                                         \
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,                     \
+                           static_cast<int>(smem));                                               \
+    kern<<<grid, kDecThreads, smem, stream>>>(                                                    \
+        static_cast<const TQ*>(a.q), static_cast<const TK*>(a.k), static_cast<const TK*>(a.v),    \
+        partial, static_cast<TK*>(a.slot), a.freqs, Hi, Hvi, Tqi, Si, Ni, Di, a.q_strides[0],     \
+        a.q_strides[1], a.q_strides[2], a.k_strides[0], a.k_strides[1], a.k_strides[2],           \
+        a.v_strides[0], a.v_strides[1], a.v_strides[2], a.slot_strides[0], a.slot_strides[1],     \
+        a.slot_strides[2], a.pos);                                                                \
+  } while (0)
+  const bool qf = a.q_dtype == BDH_DTYPE_F32, kf = a.kv_dtype == BDH_DTYPE_F32;
+  if (qf && kf) {
+    if (vec) BDH_DEC_LAUNCH(float, float, true); else BDH_DEC_LAUNCH(float, float, false);
+  } else if (qf) {
+    if (vec) BDH_DEC_LAUNCH(float, uint16_t, true); else BDH_DEC_LAUNCH(float, uint16_t, false);
+  } else if (kf) {
+    if (vec) BDH_DEC_LAUNCH(uint16_t, float, true); else BDH_DEC_LAUNCH(uint16_t, float, false);
+  } else {
+    if (vec) BDH_DEC_LAUNCH(uint16_t, uint16_t, true); else BDH_DEC_LAUNCH(uint16_t, uint16_t, false);
+  }
+#undef BDH_DEC_LAUNCH
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("decode_partial_kernel launch: ") + cudaGetErrorString(e));
+    return BDH_ERR_CUDA;
+  }
+  const int64_t bht = a.B * a.H * a.Tq;
+  const int threads = static_cast<int>(std::min<int64_t>(256, std::max<int64_t>(32, a.D)));
+  if (qf)
+    decode_reduce_kernel<float><<<static_cast<unsigned>(bht), threads, 0, stream>>>(
+        partial, static_cast<float*>(a.out), nsplit, Hi, Tqi, Di, bht, a.out_strides[0],
+        a.out_strides[1], a.out_strides[2]);
+  else
+    decode_reduce_kernel<uint16_t><<<static_cast<unsigned>(bht), threads, 0, stream>>>(
+        partial, static_cast<uint16_t*>(a.out), nsplit, Hi, Tqi, Di, bht, a.out_strides[0],
+        a.out_strides[1], a.out_strides[2]);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("decode_reduce_kernel launch: ") + cudaGetErrorString(e));
+    return BDH_ERR_CUDA;
+  }
+  return BDH_OK;
+}
+
+}  // namespace bdh

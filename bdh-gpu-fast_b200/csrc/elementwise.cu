@@ -1,0 +1,339 @@
+// HBM-bound elementwise kernels of the path:
+//   * RoPE apply with in-register phase and sincos (no cos/sin tables in HBM), reproducing
+//     the reference arithmetic step by step:
+//       bdh.py:142-150   positions (fp32 arange) * freqs            -> fp32 product
+//       bdh.py:119-122   (phase mod 1) * 2pi, then cos / sin         -> fp32
+//       kernels/rope.py:108-126 pair rotation; for bf16 inputs every product is rounded to
+//       bf16 before the bf16 add (the `.to(v.dtype)` casts).
+//   * tf32 split of fp32 operands (hi = tf32 round-to-nearest, lo = x - hi) feeding the
+//     3-product tf32 tensor-core path.
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+#include "internal.h"
+#include "tma_host.h"
+
+namespace bdh {
+
+namespace {
+
+// fp32 2*pi exactly as torch rounds the Python scalar (0x40C90FDB).
+__device__ __forceinline__ float two_pi_f32() { return __int_as_float(0x40C90FDB); }
+
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// cos / sin of the reference phase for position `pos` and frequency `f`.
+__device__ __forceinline__ void rope_cis(float pos, float f, float& c, float& s) {
+  float ph = __fmul_rn(pos, f);
+  ph = __fsub_rn(ph, floorf(ph));  // exact fractional part (ph >= 0)
+  ph = __fmul_rn(ph, two_pi_f32());
+  sincosf(ph, &s, &c);
+}
+
+// Rotate one (x0, x1) pair. BF16 = the input dtype is bf16 (products rounded before the add).
+template <bool BF16>
+__device__ __forceinline__ void rotate_pair(float x0, float x1, float c0, float s0, float c1,
+                                            float s1, float& y0, float& y1) {
+  if (BF16) {
+    y0 = bf16_round(__fadd_rn(bf16_round(__fmul_rn(x0, c0)), bf16_round(__fmul_rn(-x1, s0))));
+    y1 = bf16_round(__fadd_rn(bf16_round(__fmul_rn(x1, c1)), bf16_round(__fmul_rn(x0, s1))));
+  } else {
+    y0 = __fsub_rn(__fmul_rn(x0, c0), __fmul_rn(x1, s0));
+    y1 = __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(x0, s1));
+  }
+}
+
+__device__ __forceinline__ void load8(const uint16_t* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = bf16_bits_to_f32(w[i] & 0xFFFFu);
+    v[2 * i + 1] = bf16_bits_to_f32(w[i] >> 16);
+  }
+}
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void store8(uint16_t* p, const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ float load1(const uint16_t* p) { return bf16_bits_to_f32(*p); }
+__device__ __forceinline__ float load1(const float* p) { return *p; }
+__device__ __forceinline__ void store1(uint16_t* p, float v) {
+  *p = static_cast<uint16_t>(f32_to_bf16_bits(v));
+}
+__device__ __forceinline__ void store1(float* p, float v) { *p = v; }
+
+// Grid: x = (position t, 2048-element chunk of N), y = group of (b, h) rows. The (cos, sin)
+// of a (t, n) pair is computed once per thread and reused for every (b, h) row of the
+// group, so the trigonometry is amortised over B*H rows and the kernel runs at HBM speed.
+template <typename TX, typename TY, bool VEC>
+__global__ void __launch_bounds__(256) rope_kernel(const TX* __restrict__ x, TY* __restrict__ y,
+                                                   float* __restrict__ y_lo,
+                                                   const float* __restrict__ freqs, int H, int T,
+                                                   int N, int BH, int rows_per_group,
+                                                   int64_t xsb, int64_t xsh, int64_t xst,
+                                                   int64_t ysb, int64_t ysh, int64_t yst,
+                                                   int64_t pos0) {
+  constexpr bool BF16_IN = sizeof(TX) == 2;
+  constexpr int E = VEC ? 8 : 2;  // elements per thread
+  const int chunks = (N + 256 * E - 1) / (256 * E);
+  const int t = static_cast<int>(blockIdx.x / chunks);
+  const int n0 = static_cast<int>(blockIdx.x % chunks) * 256 * E + threadIdx.x * E;
+  if (n0 >= N) return;
+  const float pos = static_cast<float>(pos0 + t);
+  float c[E], s[E];
+  {
+    float f[E];
+    if (VEC) {
+      const float4 fa = __ldg(reinterpret_cast<const float4*>(freqs + n0));
+      const float4 fb = __ldg(reinterpret_cast<const float4*>(freqs + n0 + 4));
+      f[0] = fa.x; f[1] = fa.y; f[2] = fa.z; f[3] = fa.w;
+      f[4 % E] = fb.x; f[5 % E] = fb.y; f[6 % E] = fb.z; f[7 % E] = fb.w;
+    } else {
+      f[0] = __ldg(freqs + n0);
+      f[1] = __ldg(freqs + n0 + 1);
+    }
+#pragma unroll
+    for (int p = 0; p < E / 2; ++p) {
+      rope_cis(pos, f[2 * p], c[2 * p], s[2 * p]);
+      if (f[2 * p + 1] == f[2 * p]) {
+        c[2 * p + 1] = c[2 * p];
+        s[2 * p + 1] = s[2 * p];
+      } else {
+        rope_cis(pos, f[2 * p + 1], c[2 * p + 1], s[2 * p + 1]);
+      }
+    }
+  }
+  const int bh0 = blockIdx.y * rows_per_group;
+  const int bh1 = min(BH, bh0 + rows_per_group);
+  constexpr int U = 4;  // rows in flight per thread
+  for (int bh = bh0; bh < bh1; bh += U) {
+    float v[U][8];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (bh + u < bh1) {
+        const int r = bh + u;
+        const int b = r / H, h = r - (r / H) * H;
+        const TX* xr = x + b * xsb + h * xsh + t * xst + n0;
+        if (VEC) {
+          load8(xr, v[u]);
+        } else {
+          v[u][0] = load1(xr);
+          v[u][1] = load1(xr + 1);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (bh + u >= bh1) break;
+      const int r = bh + u;
+      const int b = r / H, h = r - (r / H) * H;
+      TY* yr = y + b * ysb + h * ysh + t * yst + n0;
+      float o[8];
+#pragma unroll
+      for (int p = 0; p < E / 2; ++p)
+        rotate_pair<BF16_IN>(v[u][2 * p], v[u][2 * p + 1], c[2 * p], s[2 * p], c[2 * p + 1],
+                             s[2 * p + 1], o[2 * p], o[2 * p + 1]);
+      if (y_lo != nullptr) {
+        float* lr = y_lo + b * ysb + h * ysh + t * yst + n0;
+        float lo[8];
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+          const float hi = tf32_round(o[i]);
+          lo[i] = o[i] - hi;
+          o[i] = hi;
+        }
+        if (VEC) {
+          store8(lr, lo);
+        } else {
+          lr[0] = lo[0];
+          lr[1] = lo[1];
+        }
+      }
+      if (VEC) {
+        store8(yr, o);
+      } else {
+        store1(yr, o[0]);
+        store1(yr + 1, o[1]);
+      }
+    }
+  }
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(256) split_tf32_kernel(const float* __restrict__ x,
+                                                         float* __restrict__ hi,
+                                                         float* __restrict__ lo, int H, int T,
+                                                         int N, int64_t xsb, int64_t xsh,
+                                                         int64_t xst) {
+  const int64_t row = blockIdx.x;
+  const int t = static_cast<int>(row % T);
+  const int64_t bh = row / T;
+  const int h = static_cast<int>(bh % H);
+  const int64_t b = bh / H;
+  const float* xr = x + b * xsb + h * xsh + t * xst;
+  float* hr = hi + row * N;
+  float* lr = lo + row * N;
+  if (VEC) {
+    for (int n0 = threadIdx.x * 4; n0 < N; n0 += blockDim.x * 4) {
+      const float4 a = *reinterpret_cast<const float4*>(xr + n0);
+      const float4 ha = make_float4(tf32_round(a.x), tf32_round(a.y), tf32_round(a.z), tf32_round(a.w));
+      *reinterpret_cast<float4*>(hr + n0) = ha;
+      *reinterpret_cast<float4*>(lr + n0) = make_float4(a.x - ha.x, a.y - ha.y, a.z - ha.z, a.w - ha.w);
+    }
+  } else {
+    for (int n = threadIdx.x; n < N; n += blockDim.x) {
+      const float a = xr[n];
+      const float ha = tf32_round(a);
+      hr[n] = ha;
+      lr[n] = a - ha;
+    }
+  }
+}
+
+// Transposing split: x (B, H, T, N) -> hi/lo [B*H][N][ldt] through a 32 x 32 shared tile.
+__global__ void __launch_bounds__(256) split_tf32_t_kernel(const float* __restrict__ x,
+                                                           float* __restrict__ hi,
+                                                           float* __restrict__ lo, int H, int T,
+                                                           int N, int64_t ldt, int64_t xsb,
+                                                           int64_t xsh, int64_t xst) {
+  __shared__ float tile[32][33];
+  const int bh = blockIdx.z;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int n0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
+  const float* xb = x + b * xsb + h * xsh;
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int t = t0 + r, n = n0 + threadIdx.x;
+    tile[r][threadIdx.x] = (t < T && n < N) ? xb[t * xst + n] : 0.0f;
+  }
+  __syncthreads();
+  float* hb = hi + static_cast<int64_t>(bh) * N * ldt;
+  float* lb = lo + static_cast<int64_t>(bh) * N * ldt;
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int n = n0 + r, t = t0 + threadIdx.x;
+    if (n < N && t < T) {
+      const float v = tile[threadIdx.x][r];
+      const float hv = tf32_round(v);
+      hb[n * ldt + t] = hv;
+      lb[n * ldt + t] = v - hv;
+    }
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int launch_rope(const void* x, int x_dtype, const int64_t xs[4], void* y, int y_dtype,
+                const int64_t ys[4], float* y_lo, const float* freqs, int64_t B, int64_t H,
+                int64_t T, int64_t N, int64_t pos0, cudaStream_t stream) {
+  const int64_t rows = B * H * T;
+  if (rows == 0 || N == 0) return BDH_OK;
+  const int xe = x_dtype == BDH_DTYPE_F32 ? 4 : 2;
+  const int ye = y_dtype == BDH_DTYPE_F32 ? 4 : 2;
+  bool vec = (N % 8 == 0) && aligned16(x) && aligned16(y) && aligned16(freqs) &&
+             (y_lo == nullptr || aligned16(y_lo));
+  for (int i = 0; i < 3; ++i) vec = vec && (xs[i] * xe) % 16 == 0 && (ys[i] * ye) % 16 == 0;
+  const int E = vec ? 8 : 2;
+  const int64_t chunks = (N + 256 * E - 1) / (256 * E);
+  const int64_t gx = T * chunks;
+  const int64_t BH = B * H;
+  // Enough (b, h) groups to give every SM several CTAs, fewer when T already does.
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int64_t want = 16LL * sm_count(dev);
+  int64_t groups = std::min<int64_t>(BH, std::max<int64_t>(1, (want + gx - 1) / gx));
+  const int64_t rpg = (BH + groups - 1) / groups;
+  groups = (BH + rpg - 1) / rpg;
+  if (gx > 0x7FFFFFFFLL || groups > 65535) {
+    set_error("rope: grid too large");
+    return BDH_ERR_INVALID;
+  }
+  const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(groups));
+  const int Hi = static_cast<int>(H), Ti = static_cast<int>(T), Ni = static_cast<int>(N);
+  const int BHi = static_cast<int>(BH), R = static_cast<int>(rpg);
+#define BDH_ROPE_LAUNCH(TX, TY)                                                                   \
+  do {                                                                                            \
+    if (vec)                                                                                      \
+      rope_kernel<TX, TY, true><<<grid, 256, 0, stream>>>(                                        \
+          static_cast<const TX*>(x), static_cast<TY*>(y), y_lo, freqs, Hi, Ti, Ni, BHi, R, xs[0], \
+          xs[1], xs[2], ys[0], ys[1], ys[2], pos0);                                               \
+    else                                                                                          \
+      rope_kernel<TX, TY, false><<<grid, 256, 0, stream>>>(                                       \
+          static_cast<const TX*>(x), static_cast<TY*>(y), y_lo, freqs, Hi, Ti, Ni, BHi, R, xs[0], \
+          xs[1], xs[2], ys[0], ys[1], ys[2], pos0);                                               \
+  } while (0)
+  if (x_dtype == BDH_DTYPE_BF16 && y_dtype == BDH_DTYPE_BF16) BDH_ROPE_LAUNCH(uint16_t, uint16_t);
+  else if (x_dtype == BDH_DTYPE_BF16) BDH_ROPE_LAUNCH(uint16_t, float);
+  else if (y_dtype == BDH_DTYPE_BF16) BDH_ROPE_LAUNCH(float, uint16_t);
+  else BDH_ROPE_LAUNCH(float, float);
+#undef BDH_ROPE_LAUNCH
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("rope_kernel launch: ") + cudaGetErrorString(e));
+    return BDH_ERR_CUDA;
+  }
+  return BDH_OK;
+}
+
+int launch_split_tf32(const float* x, const int64_t xs[4], float* hi, float* lo, int64_t B,
+                      int64_t H, int64_t T, int64_t N, cudaStream_t stream) {
+  const int64_t rows = B * H * T;
+  if (rows == 0 || N == 0) return BDH_OK;
+  bool vec = (N % 4 == 0) && aligned16(x) && aligned16(hi) && aligned16(lo);
+  for (int i = 0; i < 3; ++i) vec = vec && (xs[i] * 4) % 16 == 0;
+  const int threads = static_cast<int>(std::min<int64_t>(256, std::max<int64_t>(32, N / 4)));
+  if (vec)
+    split_tf32_kernel<true><<<static_cast<unsigned>(rows), threads, 0, stream>>>(
+        x, hi, lo, static_cast<int>(H), static_cast<int>(T), static_cast<int>(N), xs[0], xs[1], xs[2]);
+  else
+    split_tf32_kernel<false><<<static_cast<unsigned>(rows), threads, 0, stream>>>(
+        x, hi, lo, static_cast<int>(H), static_cast<int>(T), static_cast<int>(N), xs[0], xs[1], xs[2]);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("split_tf32_kernel launch: ") + cudaGetErrorString(e));
+    return BDH_ERR_CUDA;
+  }
+  return BDH_OK;
+}
+
+int launch_split_tf32_t(const float* x, const int64_t xs[4], float* hi, float* lo, int64_t B,
+                        int64_t H, int64_t T, int64_t N, int64_t ldt, cudaStream_t stream) {
+  if (B * H * T * N == 0) return BDH_OK;
+  const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((T + 31) / 32),
+                  static_cast<unsigned>(B * H));
+  split_tf32_t_kernel<<<grid, dim3(32, 8), 0, stream>>>(x, hi, lo, static_cast<int>(H),
+                                                        static_cast<int>(T), static_cast<int>(N),
+                                                        ldt, xs[0], xs[1], xs[2]);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("split_tf32_t_kernel launch: ") + cudaGetErrorString(e));
+    return BDH_ERR_CUDA;
+  }
+  return BDH_OK;
+}
+
+}  // namespace bdh

@@ -1,0 +1,242 @@
+// Persistent, warp-specialised tcgen05 GEMM engine for the tril-attention contractions.
+//
+// One CTA per SM (192 threads) walks a strided list of output tiles:
+//   warp 0      : TMA producer (one elected lane) filling a ring of STAGES shared-memory
+//                 stages; each stage holds one 128-byte-wide K slice of every operand term.
+//   warp 1      : TMEM allocator + MMA issuer (one elected lane); accumulates a 128 x BN
+//                 fp32 tile into one of two TMEM buffers (double buffered across tiles).
+//   warps 2..5  : epilogue (128 threads = 128 TMEM lanes = 128 tile rows); drains the
+//                 accumulator with tcgen05.ld and hands 32-column chunks to the problem's
+//                 epilogue (masking, hi/lo splitting, RoPE adjoint, stores).
+//
+// The problem policy `P` supplies the tile list, the K-block count of each tile, the TMA
+// loads of one stage and the epilogue. Operands are 128B-swizzled, either K-major (rows of
+// 128 bytes along K) or MN-major (128-byte chunks along M/N, K rows of 128 bytes).
+// "Terms" implement split precision: A = sum of A_TERMS tiles, B = sum of B_TERMS tiles, and
+// the MMA issues hi*hi (+ hi*lo + lo*hi) products; the lo*lo product is dropped.
+#pragma once
+
+#include "common.cuh"
+
+namespace bdh {
+
+constexpr int kTcThreads = 192;
+constexpr int kEpiThreads = 128;
+
+template <int ELEM_, int BN_, bool A_MN_, bool B_MN_, int A_TERMS_, int B_TERMS_, int STAGES_>
+struct TcShape {
+  static constexpr int ELEM = ELEM_;               // operand element bytes: 2 (bf16) or 4 (tf32)
+  static constexpr int BM = 128;
+  static constexpr int BN = BN_;
+  static constexpr int BK = 128 / ELEM;            // K elements per stage
+  static constexpr int UK = 32 / ELEM;             // K elements per tcgen05.mma
+  static constexpr bool A_MN = A_MN_;
+  static constexpr bool B_MN = B_MN_;
+  static constexpr int A_TERMS = A_TERMS_;
+  static constexpr int B_TERMS = B_TERMS_;
+  static constexpr int STAGES = STAGES_;
+  static constexpr int A_TILE = BM * 128;          // bytes of one A term in one stage
+  static constexpr int B_TILE = BN * 128;
+  static constexpr int STAGE_BYTES = A_TILE * A_TERMS + B_TILE * B_TERMS;
+  static constexpr int TMEM_COLS = 2 * BN;         // two fp32 accumulators
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static constexpr uint32_t IDESC =
+      make_idesc(ELEM == 2 ? 1u : 2u, A_MN ? 1u : 0u, B_MN ? 1u : 0u, BM, BN);
+  static constexpr int NPAIRS = (A_TERMS == 1 && B_TERMS == 1) ? 1 : (A_TERMS == 2 && B_TERMS == 2 ? 3 : 2);
+
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
+  static_assert(STAGES * STAGE_BYTES + BAR_BYTES + 1024 <= 232448, "shared memory budget");
+
+  // Byte offset of the kk-th MMA's K slice inside one term tile.
+  __device__ static __forceinline__ uint32_t a_koff(int kk) {
+    return A_MN ? static_cast<uint32_t>(kk * UK * 128) : static_cast<uint32_t>(kk * 32);
+  }
+  __device__ static __forceinline__ uint32_t b_koff(int kk) {
+    return B_MN ? static_cast<uint32_t>(kk * UK * 128) : static_cast<uint32_t>(kk * 32);
+  }
+  __device__ static __forceinline__ uint64_t a_desc(uint32_t addr) {
+    return smem_desc_sw128(addr, A_MN ? BK * 128 : 16, 1024);
+  }
+  __device__ static __forceinline__ uint64_t b_desc(uint32_t addr) {
+    return smem_desc_sw128(addr, B_MN ? BK * 128 : 16, 1024);
+  }
+};
+
+// Spin on `bar` ignoring the abort flag (used to drain in-flight async work before exit).
+__device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0u && globaltimer_ns() - t0 > BDH_WAIT_TIMEOUT_NS) {
+      if (err != nullptr) atomicCAS(err, 0, kErrTimeoutDrain);
+      return false;
+    }
+  }
+}
+
+template <class S, class P>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ typename P::Params prm) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::STAGES * S::STAGE_BYTES);
+  uint64_t* empty = full + S::STAGES;
+  uint64_t* tfull = empty + S::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int ntiles = P::num_tiles(prm);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull + a, 1);
+      mbar_init(tempty + a, kEpiThreads);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, S::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      P::prefetch(prm);
+      int stage = 0;
+      uint32_t ph = 0;
+      uint32_t n_issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        typename P::Tile tile = P::tile(prm, t);
+        const int nkb = P::k_blocks(prm, tile);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (*abort_flag ||
+              !wait_bounded(empty + stage, ph ^ 1u, abort_flag, prm.err, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full + stage, S::STAGE_BYTES);
+          uint8_t* a_dst = smem + stage * S::STAGE_BYTES;
+          uint8_t* b_dst = a_dst + S::A_TERMS * S::A_TILE;
+          P::load_stage(prm, tile, kb, full + stage, a_dst, b_dst);
+          ++n_issued;
+          if (++stage == S::STAGES) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Every issued TMA load must land before this CTA may retire its shared memory.
+      for (int s = 0; s < S::STAGES; ++s) {
+        if (n_issued > static_cast<uint32_t>(s)) {
+          const uint32_t k_last = (n_issued - 1u - static_cast<uint32_t>(s)) / S::STAGES;
+          wait_drain(full + s, k_last & 1u, prm.err);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t ph = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++lt) {
+        typename P::Tile tile = P::tile(prm, t);
+        const int nkb = P::k_blocks(prm, tile);
+        const int acc = lt & 1;
+        const uint32_t aph = static_cast<uint32_t>(lt >> 1) & 1u;
+        if (!wait_bounded(tempty + acc, aph ^ 1u, abort_flag, prm.err, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * S::BN);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!wait_bounded(full + stage, ph, abort_flag, prm.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + stage * S::STAGE_BYTES);
+          const uint32_t b_base = a_base + S::A_TERMS * S::A_TILE;
+          const uint32_t pair_mask = P::pair_mask(prm, tile, kb);
+#pragma unroll
+          for (int kk = 0; kk < S::BK / S::UK; ++kk) {
+#pragma unroll
+            for (int pr = 0; pr < S::NPAIRS; ++pr) {
+              if (!((pair_mask >> pr) & 1u)) continue;
+              // pair 0: A0*B0; pair 1: A1*B0 (or A0*B1 when only B is split); pair 2: A0*B1
+              const int ta = (pr == 1 && S::A_TERMS == 2) ? 1 : 0;
+              const int tb = (pr == 2 || (pr == 1 && S::A_TERMS == 1)) ? 1 : 0;
+              const uint64_t ad = S::a_desc(a_base + ta * S::A_TILE + S::a_koff(kk));
+              const uint64_t bd = S::b_desc(b_base + tb * S::B_TILE + S::b_koff(kk));
+              const uint32_t accumulate = (kb > 0 || kk > 0 || pr > 0) ? 1u : 0u;
+              if (S::ELEM == 2)
+                umma_f16(d_tmem, ad, bd, S::IDESC, accumulate);
+              else
+                umma_tf32(d_tmem, ad, bd, S::IDESC, accumulate);
+            }
+          }
+          umma_commit(empty + stage);
+          if (++stage == S::STAGES) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull + acc);
+      }
+      // All MMAs issued by this thread must finish before TMEM is released.
+      umma_commit(drain);
+      wait_drain(drain, 0u, prm.err);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + static_cast<int>(lane_id());
+    int lt = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++lt) {
+      typename P::Tile tile = P::tile(prm, t);
+      const int acc = lt & 1;
+      const uint32_t aph = static_cast<uint32_t>(lt >> 1) & 1u;
+      bool ok = wait_bounded(tfull + acc, aph, abort_flag, prm.err, kErrTimeoutEpilogue);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const uint32_t tbase =
+          tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * S::BN);
+#pragma unroll 1
+      for (int c0 = 0; c0 < S::BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tbase + static_cast<uint32_t>(c0), r);
+        tmem_ld_wait();
+        P::epilogue(prm, tile, row, c0, r);
+      }
+      tc_fence_before();
+      mbar_arrive(tempty + acc);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::TMEM_COLS);
+  }
+}
+
+}  // namespace bdh

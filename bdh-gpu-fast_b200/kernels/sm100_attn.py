@@ -1,0 +1,418 @@
+"""ctypes binding of libbdh_sm100.so — the sm_100a tril attention behind ``BDH_ATTN_IMPL=cuda_sm100``.
+
+Mirrors the reference's native wrapper ``kernels/cuda_attn.py`` (``tril_score_v`` :391-414,
+``tril_decode`` :490-502, shape checks :103-131, ``has_cuda_ext`` / ``ext_status`` :81-100,
+:505-513) with two deliberate differences:
+
+* no silent fallback: a missing library, a CPU tensor or a failing launch raises
+  (the reference returned its pure-PyTorch result on any exception, ``cuda_attn.py:401-409``);
+* no ``.contiguous()`` of inputs: strided views (permuted Q, capacity-strided cache views) are
+  passed to the kernels as they are (the reference copied them, ``csrc/tril_attn_cuda.cu:264-266,
+  563-565``).
+
+Semantics (identical to the reference)::
+
+    tril_score_v(q, k, v)        = (q @ k.mT).tril(-1) @ v      # v heads 1 or H (broadcast)
+    tril_decode(q, k_past, v_past) = (q @ k_past.mT) @ v_past    # S == 0 -> zeros
+
+Tensors: q, k ``(B, H, T, N)``; v ``(B, Hv, T, D)``; fp32 or bf16 (fp32 accumulation always);
+the output is a fresh ``(B, H, T, D)`` tensor in q's dtype. Device memory (outputs and the
+library's scratch workspace) comes from the PyTorch caching allocator on the current stream.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Optional
+
+import torch
+
+_PKG = Path(__file__).resolve().parent.parent
+_LIB_PATH = Path(os.environ.get("BDH_SM100_LIB", str(_PKG / "libbdh_sm100.so")))
+
+_lib: Optional[ctypes.CDLL] = None
+_lib_error: Optional[BaseException] = None
+
+_F32 = 0
+_BF16 = 1
+
+_c_i64_4 = ctypes.c_int64 * 4
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+
+
+def _declare(lib: ctypes.CDLL) -> None:
+    P = ctypes.POINTER(ctypes.c_int64)
+    lib.bdh_abi_version.restype = ctypes.c_int
+    lib.bdh_last_error.restype = ctypes.c_char_p
+    lib.bdh_device_error.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int]
+    lib.bdh_rope_rotate.argtypes = [_vp, ctypes.c_int, P, _vp, ctypes.c_int, P, _vp, _vp,
+                                    _i64, _i64, _i64, _i64, _i64, _vp]
+    lib.bdh_tril_score_v_workspace_size.restype = ctypes.c_size_t
+    lib.bdh_tril_score_v_workspace_size.argtypes = [ctypes.c_int, _i64, _i64, _i64, _i64, _i64,
+                                                    _i64, ctypes.c_int]
+    lib.bdh_tril_score_v.argtypes = [_vp, P, _vp, P, _vp, P, ctypes.c_int, _vp, P, ctypes.c_int,
+                                     _i64, _i64, _i64, _i64, _i64, _i64, _vp, ctypes.c_size_t, _vp]
+    lib.bdh_tril_decode_workspace_size.restype = ctypes.c_size_t
+    lib.bdh_tril_decode_workspace_size.argtypes = [_i64, _i64, _i64, _i64, _i64]
+    lib.bdh_tril_decode.argtypes = [_vp, P, ctypes.c_int, _vp, P, _vp, P, ctypes.c_int, _vp, P,
+                                    _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, P,
+                                    _vp, ctypes.c_size_t, _vp]
+    lib.bdh_tril_score_v_bwd_workspace_size.restype = ctypes.c_size_t
+    lib.bdh_tril_score_v_bwd_workspace_size.argtypes = [ctypes.c_int, _i64, _i64, _i64, _i64,
+                                                        _i64, _i64, ctypes.c_int]
+    lib.bdh_tril_score_v_bwd.argtypes = [_vp, P, _vp, P, _vp, P, _vp, P, ctypes.c_int, _vp, P,
+                                         _vp, P, _vp, P, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
+                                         _i64, _vp, ctypes.c_size_t, _vp]
+    for name in ("bdh_rope_rotate", "bdh_tril_score_v", "bdh_tril_decode", "bdh_tril_score_v_bwd"):
+        getattr(lib, name).restype = ctypes.c_int
+
+
+def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
+    """Load (once) and return the C-ABI library; raises if it cannot be loaded."""
+    global _lib, _lib_error
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path is not None else _LIB_PATH
+    try:
+        lib = ctypes.CDLL(str(p))
+        _declare(lib)
+        ver = lib.bdh_abi_version()
+        if ver != 1:
+            raise RuntimeError(f"{p}: unexpected ABI version {ver}")
+    except BaseException as exc:  # noqa: BLE001 - remembered for ext_status()
+        _lib_error = exc
+        raise
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def _try_load() -> Optional[ctypes.CDLL]:
+    try:
+        return load_library()
+    except BaseException:  # noqa: BLE001
+        return None
+
+
+def has_cuda_ext() -> bool:
+    """True if libbdh_sm100.so loads (it always carries the sm_100a kernels)."""
+    return _try_load() is not None
+
+
+def has_cuda_kernel() -> bool:
+    """True if the library loads and a CUDA device is present to run it."""
+    return has_cuda_ext() and torch.cuda.is_available()
+
+
+def ext_status() -> str:
+    """Human-readable status (same role as the reference's ``cuda_attn.ext_status``)."""
+    if _try_load() is None:
+        err = _lib_error
+        detail = f"{type(err).__name__}: {err}" if err is not None else "not attempted"
+        return f"native=unavailable ({detail})"
+    cuda = "yes" if torch.cuda.is_available() else "no"
+    return f"native=loaded lib={_LIB_PATH.name} has_cuda_kernel={cuda} has_decode=yes has_bwd=yes"
+
+
+def _require_lib() -> ctypes.CDLL:
+    lib = _try_load()
+    if lib is None:
+        raise RuntimeError(
+            f"cuda_sm100: {_LIB_PATH} is not loadable ({_lib_error!r}); build it with "
+            "`python bdh-gpu-fast_b200/build_lib.py`"
+        )
+    return lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = _require_lib().bdh_last_error().decode(errors="replace")
+        raise RuntimeError(f"cuda_sm100 {what} failed (code {rc}): {msg}")
+
+
+def device_error(device: Optional[torch.device] = None, reset: bool = True) -> int:
+    """Synchronise and return the device error word (0 = no kernel reported a failure)."""
+    lib = _require_lib()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    code = ctypes.c_int(0)
+    _check(lib.bdh_device_error(dev.index or 0, ctypes.byref(code), 1 if reset else 0), "device_error")
+    return int(code.value)
+
+
+# --------------------------------------------------------------------------- checks
+def _check_cold_shapes(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError("q, k, v must be 4D (B, H, T, D)")
+    if q.shape != k.shape:
+        raise ValueError(f"q and k shapes must match, got {tuple(q.shape)} vs {tuple(k.shape)}")
+    if v.size(0) != q.size(0) or v.size(2) != q.size(2):
+        raise ValueError("v batch/seq must match q")
+    if v.size(1) not in (1, q.size(1)):
+        raise ValueError("v heads must equal q heads or 1")
+
+
+def _check_decode_shapes(q: torch.Tensor, k_past: torch.Tensor, v_past: torch.Tensor):
+    if q.dim() != 4 or k_past.dim() != 4 or v_past.dim() != 4:
+        raise ValueError("q, k_past, v_past must be 4D")
+    B, H, Tq, Dk = q.shape
+    S = k_past.size(2)
+    if k_past.shape[:2] != (B, H) or k_past.size(-1) != Dk:
+        raise ValueError(f"k_past shape {tuple(k_past.shape)} incompatible with q {tuple(q.shape)}")
+    if v_past.size(0) != B or v_past.size(2) != S:
+        raise ValueError(f"v_past shape {tuple(v_past.shape)} incompatible with k_past S={S}")
+    if v_past.size(1) not in (1, H):
+        raise ValueError("v_past heads must equal q heads or 1")
+    return B, H, Tq, S, v_past.size(-1)
+
+
+def _code(dtype: torch.dtype) -> int:
+    if dtype == torch.float32:
+        return _F32
+    if dtype == torch.bfloat16:
+        return _BF16
+    raise TypeError(f"cuda_sm100 supports float32 and bfloat16 tensors, got {dtype}")
+
+
+def _require_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError("cuda_sm100 requires CUDA tensors (no CPU fallback)")
+        if t.device != dev:
+            raise RuntimeError("cuda_sm100: all tensors must be on the same device")
+    return dev
+
+
+def _strides(t: torch.Tensor):
+    return _c_i64_4(*t.stride())
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _tma_ready(x: torch.Tensor) -> torch.Tensor:
+    """Return x if TMA can read it in place, else a zero-padded contiguous copy.
+
+    TMA needs a 16-byte aligned base and 16-byte multiple strides; the padding (zeros on the
+    last dimension) does not change any dot product over that dimension.
+    """
+    esz = x.element_size()
+    ok = x.stride(-1) == 1 and x.data_ptr() % 16 == 0
+    if ok:
+        for d in range(x.dim() - 1):
+            if x.size(d) > 1 and (x.stride(d) * esz) % 16 != 0:
+                ok = False
+                break
+    if ok:
+        return x
+    mult = 16 // esz
+    n = x.size(-1)
+    npad = (n + mult - 1) // mult * mult
+    y = torch.zeros(*x.shape[:-1], npad, dtype=x.dtype, device=x.device)
+    y[..., :n].copy_(x)
+    return y
+
+
+# -------------------------------------------------------------------------- forward
+def tril_score_v(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """``(q @ k.mT).tril(-1) @ v`` on the sm_100a tensor cores (fp32 accumulation)."""
+    _check_cold_shapes(q, k, v)
+    dev = _require_cuda(q, k, v)
+    lib = _require_lib()
+    B, H, T, N = q.shape
+    Hv, D = v.size(1), v.size(-1)
+    dt = _code(q.dtype)
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError(f"cuda_sm100: q, k, v dtypes must match, got {q.dtype}, {k.dtype}, {v.dtype}")
+    out = torch.empty(B, H, T, D, dtype=q.dtype, device=dev)
+    if out.numel() == 0:
+        return out
+    same = k is q
+    qq = _tma_ready(q)
+    kk = qq if same else _tma_ready(k)
+    vv = _tma_ready(v)
+    Np = qq.size(-1)
+    Dp = vv.size(-1)
+    if Dp != D:
+        out_full = torch.empty(B, H, T, Dp, dtype=q.dtype, device=dev)
+    else:
+        out_full = out
+    k_is_q = 1 if kk is qq else 0
+    wsz = lib.bdh_tril_score_v_workspace_size(dt, B, H, Hv, T, Np, Dp, k_is_q)
+    ws = torch.empty(max(int(wsz), 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.bdh_tril_score_v(
+            qq.data_ptr(), _strides(qq), kk.data_ptr(), _strides(kk), vv.data_ptr(), _strides(vv),
+            dt, out_full.data_ptr(), _strides(out_full), dt, B, H, Hv, T, Np, Dp,
+            ws.data_ptr(), int(wsz), _stream(dev))
+    _check(rc, "tril_score_v")
+    if out_full is not out:
+        out.copy_(out_full[..., :D])
+    return out
+
+
+def rope_rotate(x: torch.Tensor, freqs: torch.Tensor, pos0: int = 0,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """BDH RoPE of ``x`` (B,H,T,N) at positions ``pos0 .. pos0+T-1`` computed in registers.
+
+    Same arithmetic as ``Attention.rope`` with the ``rope_cos_sin`` tables (bdh.py:119-150,
+    kernels/rope.py:108-126) but without materialising the tables. ``out`` may be a strided
+    view (e.g. a cache slot) of another dtype; it must not overlap ``x``.
+    """
+    if x.dim() != 4:
+        raise ValueError("rope_rotate expects a 4-D (B, H, T, N) tensor")
+    if x.size(-1) % 2 != 0:
+        raise ValueError(f"RoPE last dim must be even, got {x.size(-1)}")
+    dev = _require_cuda(x, freqs)
+    lib = _require_lib()
+    f = freqs.reshape(-1)
+    if f.dtype != torch.float32 or f.numel() != x.size(-1):
+        raise ValueError("freqs must be float32 with one entry per latent dimension")
+    f = f.contiguous()
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, device=dev)
+    elif out.shape != x.shape or out.device != x.device:
+        raise ValueError("rope out= must match x shape/device")
+    elif torch._C._overlaps(out, x):
+        raise ValueError("rope out= must not alias x")
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if out.stride(-1) != 1:
+        raise ValueError("rope out= must have a contiguous last dimension")
+    B, H, T, N = x.shape
+    with torch.cuda.device(dev):
+        rc = lib.bdh_rope_rotate(x.data_ptr(), _code(x.dtype), _strides(x), out.data_ptr(),
+                                 _code(out.dtype), _strides(out), None, f.data_ptr(),
+                                 B, H, T, N, int(pos0), _stream(dev))
+    _check(rc, "rope_rotate")
+    return out
+
+
+# --------------------------------------------------------------------------- decode
+def tril_decode(q: torch.Tensor, k_past: torch.Tensor, v_past: torch.Tensor, *,
+                freqs: Optional[torch.Tensor] = None, pos: int = 0,
+                kr_slot: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``(q @ k_past.mT) @ v_past`` streaming the (possibly capacity-strided) cache in place.
+
+    ``k_past``/``v_past`` may be stored in another dtype than ``q`` (e.g. bf16 cache storage
+    with fp32 compute): they are widened in registers, never copied. With ``freqs`` the query
+    is RoPE-rotated to positions ``pos..`` first, and with ``kr_slot`` the rotated rows are
+    also written there (the cache write of this step).
+    """
+    B, H, Tq, S, D = _check_decode_shapes(q, k_past, v_past)
+    dev = _require_cuda(q, k_past, v_past)
+    lib = _require_lib()
+    if k_past.dtype != v_past.dtype:
+        raise TypeError("k_past and v_past must share the cache storage dtype")
+    qd = _code(q.dtype)
+    kd = _code(k_past.dtype)
+    out = torch.empty(B, H, Tq, D, dtype=q.dtype, device=dev)
+    if out.numel() == 0:
+        if kr_slot is not None and freqs is not None and Tq > 0:
+            rope_rotate(q, freqs, pos, out=kr_slot)
+        return out
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if k_past.stride(-1) != 1 or v_past.stride(-1) != 1:
+        raise ValueError("cache views must have a contiguous last dimension")
+    N = q.size(-1)
+    fptr = None
+    if freqs is not None:
+        f = freqs.reshape(-1)
+        if f.dtype != torch.float32 or f.numel() != N:
+            raise ValueError("freqs must be float32 with one entry per latent dimension")
+        f = f.contiguous()
+        fptr = f.data_ptr()
+    slot_ptr = None
+    slot_strides = None
+    if kr_slot is not None:
+        if freqs is None:
+            raise ValueError("kr_slot requires freqs (the slot receives the rotated query)")
+        if kr_slot.shape != q.shape or kr_slot.dtype != k_past.dtype or kr_slot.stride(-1) != 1:
+            raise ValueError("kr_slot must match q's shape, the cache dtype and have unit last stride")
+        slot_ptr = kr_slot.data_ptr()
+        slot_strides = _strides(kr_slot)
+    wsz = lib.bdh_tril_decode_workspace_size(B, H, Tq, S, D)
+    ws = torch.empty(max(int(wsz), 4), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.bdh_tril_decode(
+            q.data_ptr(), _strides(q), qd, k_past.data_ptr(), _strides(k_past), v_past.data_ptr(),
+            _strides(v_past), kd, out.data_ptr(), _strides(out), B, H, v_past.size(1), Tq, S, N, D,
+            fptr, int(pos), slot_ptr, slot_strides, ws.data_ptr(), int(wsz), _stream(dev))
+    _check(rc, "tril_decode")
+    return out
+
+
+# ------------------------------------------------------------------------- backward
+def tril_score_v_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch.Tensor,
+                     *, freqs: Optional[torch.Tensor] = None, pos0: int = 0):
+    """Analytic gradients of ``tril(q k^T, -1) v``: returns ``(dq, dk, dv)``.
+
+    When ``k is q`` the returned ``dq`` already holds ``dq + dk`` and ``dk`` is None (the
+    self-attention form of ``StrictTrilSelfAttnFn``). With ``freqs`` (self form only) ``q`` is
+    the rotated QR and ``dq`` is the gradient with respect to the unrotated latent.
+    """
+    _check_cold_shapes(q, k, v)
+    dev = _require_cuda(q, k, v, dout)
+    lib = _require_lib()
+    B, H, T, N = q.shape
+    Hv, D = v.size(1), v.size(-1)
+    if dout.shape != (B, H, T, D):
+        raise ValueError(f"dout shape {tuple(dout.shape)} must be {(B, H, T, D)}")
+    dt = _code(q.dtype)
+    same = k is q
+    if freqs is not None and not same:
+        raise ValueError("the fused RoPE adjoint needs the self-attention form (k is q)")
+    qq = _tma_ready(q)
+    kk = qq if same else _tma_ready(k)
+    vv = _tma_ready(v)
+    dd = _tma_ready(dout.to(q.dtype))
+    Np, Dp = qq.size(-1), vv.size(-1)
+    if dd.size(-1) != Dp:
+        dd = torch.nn.functional.pad(dd, (0, Dp - dd.size(-1)))
+    dq = torch.empty(B, H, T, Np, dtype=q.dtype, device=dev)
+    dk = None if same else torch.empty(B, H, T, Np, dtype=q.dtype, device=dev)
+    dv = torch.empty(B, Hv, T, Dp, dtype=q.dtype, device=dev)
+    fptr = None
+    if freqs is not None:
+        f = freqs.reshape(-1).contiguous()
+        if f.dtype != torch.float32 or f.numel() != N:
+            raise ValueError("freqs must be float32 with one entry per latent dimension")
+        if Np != N:
+            raise ValueError("the fused RoPE adjoint needs an aligned latent width")
+        fptr = f.data_ptr()
+    k_is_q = 1 if same else 0
+    wsz = lib.bdh_tril_score_v_bwd_workspace_size(dt, B, H, Hv, T, Np, Dp, k_is_q)
+    ws = torch.empty(max(int(wsz), 1), dtype=torch.uint8, device=dev)
+    dk_ptr = dk.data_ptr() if dk is not None else None
+    dk_str = _strides(dk) if dk is not None else _strides(dq)
+    with torch.cuda.device(dev):
+        rc = lib.bdh_tril_score_v_bwd(
+            qq.data_ptr(), _strides(qq), kk.data_ptr(), _strides(kk), vv.data_ptr(), _strides(vv),
+            dd.data_ptr(), _strides(dd), dt, dq.data_ptr(), _strides(dq), dk_ptr, dk_str,
+            dv.data_ptr(), _strides(dv), B, H, Hv, T, Np, Dp, fptr, int(pos0),
+            ws.data_ptr(), int(wsz), _stream(dev))
+    _check(rc, "tril_score_v_bwd")
+    if Np != N:
+        dq = dq[..., :N].contiguous()
+        dk = dk[..., :N].contiguous() if dk is not None else None
+    if Dp != D:
+        dv = dv[..., :D].contiguous()
+    return dq, dk, dv
+
+
+__all__ = [
+    "load_library",
+    "has_cuda_ext",
+    "has_cuda_kernel",
+    "ext_status",
+    "device_error",
+    "tril_score_v",
+    "tril_decode",
+    "tril_score_v_bwd",
+    "rope_rotate",
+]

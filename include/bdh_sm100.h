@@ -1,0 +1,135 @@
+/*
+ * bdh_sm100.h — C ABI of the B200 (sm_100a) strict-causal linear "tril" attention of BDH.
+ *
+ *   forward : out = tril((R.Q)(R.Q)^T, -1) . V        (no softmax, no scale, diagonal excluded)
+ *   decode  : out = (q . K_past^T) . V_past             (every cached key precedes the query)
+ *   backward: dQ_total = (dS + dS^T) . QR,  dV = sum_h M^T . dO,
+ *             with M = tril(QR QR^T, -1) and dS = tril(dO V^T, -1)
+ *
+ * Every entry point takes plain device pointers, element strides and sizes, and a CUDA
+ * stream (cudaStream_t passed as void*). Tensors are 4-D (B, H, T, X) with the last
+ * dimension contiguous (stride 1); any other strides are accepted as long as each
+ * row/head/batch stride is a multiple of 16 bytes (TMA rule) — so permuted views and
+ * capacity-strided cache views are read in place, never copied. V may have one head
+ * (shared by all query heads) or H heads. Outputs are written, never accumulated into.
+ *
+ * Scratch memory is always provided by the caller (`workspace`, sized by the matching
+ * *_workspace_size function); the library itself never allocates device memory.
+ *
+ * Return value: BDH_OK (0) or an error code; bdh_last_error() gives the message of the
+ * calling thread's last failure. Kernels never trap: a pipeline wait that exceeds its
+ * time limit records a code in the device error word (bdh_device_error) and returns.
+ */
+#ifndef BDH_SM100_H_
+#define BDH_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BDH_ABI_VERSION 1
+
+#define BDH_DTYPE_F32 0
+#define BDH_DTYPE_BF16 1
+
+#define BDH_OK 0
+#define BDH_ERR_INVALID 1   /* bad shape / dtype / stride / alignment (nothing launched) */
+#define BDH_ERR_CUDA 2      /* CUDA runtime error at launch */
+#define BDH_ERR_WORKSPACE 3 /* workspace missing or too small */
+
+/* ABI version of the loaded library (BDH_ABI_VERSION). */
+int bdh_abi_version(void);
+
+/* Message of the calling thread's last failing call ("" if none). */
+const char* bdh_last_error(void);
+
+/* Read (and optionally clear) the device error word of `device`: 0 = no kernel has
+ * reported a failure; otherwise one of the codes of csrc/common.cuh (pipeline timeouts).
+ * Synchronises the device. */
+int bdh_device_error(int device, int* code, int reset);
+
+/*
+ * RoPE apply: y = R(pos0 + t) x, pairwise on (x[2p], x[2p+1]) with
+ *   phase[t,n] = ((pos0 + t) * freqs[n] mod 1) * 2pi   (fp32, as the reference computes it)
+ *   y0 = x0*cos - x1*sin,  y1 = x1*cos + x0*sin
+ * For bf16 x each product is rounded to bf16 before the add, as the reference does.
+ * x: (B,H,T,N) in x_dtype; y: (B,H,T,N) in y_dtype (may differ: a cache slot in another
+ * dtype). `y_lo` (optional, only with y_dtype F32) receives y - tf32(y) and y then holds
+ * tf32(y): the split operand of the fp32 tensor-core path.
+ * Replaces: kernels/rope.py:220-240 (eager_rope_rotate) behind kernels/rope_dispatch.py:64-99
+ * (bdh_rope_rotate / bdh_rope_rotate_paired) and bdh.py:119-150 (phase / cos / sin tables).
+ */
+int bdh_rope_rotate(const void* x, int x_dtype, const int64_t x_strides[4], void* y, int y_dtype,
+                    const int64_t y_strides[4], void* y_lo, const float* freqs, int64_t B,
+                    int64_t H, int64_t T, int64_t N, int64_t pos0, void* stream);
+
+/* Scratch bytes bdh_tril_score_v needs for these sizes (dtype of q/k/v). */
+size_t bdh_tril_score_v_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,
+                                       int64_t N, int64_t D, int k_is_q);
+
+/*
+ * Forward: out[b,h] = tril(q[b,h] k[b,h]^T, -1) v[b,hv], fp32 accumulation.
+ * q, k: (B,H,T,N); v: (B,Hv,T,D) with Hv in {1,H}; out: (B,H,T,D) in out_dtype.
+ * dtype is the element type of q, k and v (all the same). k may equal q (BDH: K is Q).
+ * Replaces: csrc/tril_attn.h:20 tril_score_v(q,k,v) as bound at csrc/tril_attn_bind.cpp:3-12
+ * and :27 (pybind "tril_score_v"), called from kernels/cuda_attn.py:391-414.
+ */
+int bdh_tril_score_v(const void* q, const int64_t q_strides[4], const void* k,
+                     const int64_t k_strides[4], const void* v, const int64_t v_strides[4],
+                     int dtype, void* out, const int64_t out_strides[4], int out_dtype,
+                     int64_t B, int64_t H, int64_t Hv, int64_t T, int64_t N, int64_t D,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scratch bytes bdh_tril_decode needs. */
+size_t bdh_tril_decode_workspace_size(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t D);
+
+/*
+ * Decode against a packed past: out[b,h] = (q[b,h] k_past[b,h]^T) v_past[b,hv].
+ * q: (B,H,Tq,N) in q_dtype; k_past: (B,H,S,N) and v_past: (B,Hv,S,D) in kv_dtype (the cache
+ * storage type; read as stored, widened in registers); out: (B,H,Tq,D) in q_dtype.
+ * S == 0 gives zeros. Optional fused RoPE: when freqs != NULL, q is first rotated to
+ * position `pos` (all Tq rows at pos .. pos+Tq-1) and, when kr_slot != NULL, the rotated
+ * rows are also written to kr_slot (B,H,Tq,N) in kv_dtype (the cache write of this step).
+ * Replaces: csrc/tril_attn.h:21 tril_decode(q,k_past,v_past) bound at
+ * csrc/tril_attn_bind.cpp:14-23 and :31, called from kernels/cuda_attn.py:490-502; the fused
+ * form replaces bdh.py:396-401 (RoPE into the cache slot) + bdh.py:431-437 (decode call).
+ */
+int bdh_tril_decode(const void* q, const int64_t q_strides[4], int q_dtype, const void* k_past,
+                    const int64_t k_strides[4], const void* v_past, const int64_t v_strides[4],
+                    int kv_dtype, void* out, const int64_t out_strides[4], int64_t B, int64_t H,
+                    int64_t Hv, int64_t Tq, int64_t S, int64_t N, int64_t D, const float* freqs,
+                    int64_t pos, void* kr_slot, const int64_t slot_strides[4], void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* Scratch bytes bdh_tril_score_v_bwd needs. */
+size_t bdh_tril_score_v_bwd_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,
+                                           int64_t N, int64_t D, int k_is_q);
+
+/*
+ * Backward of the forward above for upstream gradient dout (B,H,T,D):
+ *   dS = tril(dout v^T, -1), M = tril(q k^T, -1)
+ *   dq = dS k,  dk = dS^T q,  dv = sum over heads sharing v of M^T dout.
+ * When k == q (k_is_q = 1) dq receives dq + dk (the self-attention gradient) and dk is unused.
+ * When freqs != NULL (requires k_is_q) q is the ROTATED input QR and dq receives the gradient
+ * with respect to the UNROTATED latent: R(pos0+t)^T (dS + dS^T) QR (RoPE adjoint fused).
+ * Outputs dq (B,H,T,N), dk (B,H,T,N), dv (B,Hv,T,D) are written in `dtype`.
+ * Replaces: kernels/attention_bwd.py:45-83 / :86-181 (analytic_tril_attn_backward[_blocked])
+ * as used by StrictTrilAttnFn / StrictTrilSelfAttnFn (kernels/attention_bwd.py:218-291) and,
+ * with freqs, the RoPE backward of kernels/rope.py:540-557.
+ */
+int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* k,
+                         const int64_t k_strides[4], const void* v, const int64_t v_strides[4],
+                         const void* dout, const int64_t dout_strides[4], int dtype, void* dq,
+                         const int64_t dq_strides[4], void* dk, const int64_t dk_strides[4],
+                         void* dv, const int64_t dv_strides[4], int64_t B, int64_t H, int64_t Hv,
+                         int64_t T, int64_t N, int64_t D, const float* freqs, int64_t pos0,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BDH_SM100_H_ */

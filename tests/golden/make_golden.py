@@ -1,0 +1,164 @@
+"""Generate the golden fixtures under tests/golden/ by running the REFERENCE implementation.
+
+Run in the build container (the reference checkout is not available on GPU hosts):
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /root/reference
+
+It imports the reference's own Python modules (``bdh``, ``bdh_baseline``, ``bdh_cache``,
+``kernels``) and its CPU extension built by ``oracle/build_ref.py`` (``csrc/tril_attn_cpu.cpp``),
+runs them on small seeded inputs and stores inputs + outputs as .npz files. The tests pin the
+numpy oracle (oracle/tril_oracle.py) and the GPU kernels against these files.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+
+
+def _f32(t):
+    return t.detach().to("cpu").float().numpy()
+
+
+def main(reference: Path) -> None:
+    sys.path.insert(0, str(reference))
+    sys.path.insert(0, str(REPO / "oracle"))
+    import torch
+
+    import bdh  # reference optimized model
+    import bdh_baseline  # reference frozen upstream model
+    from bdh_cache import CacheManager
+    from kernels.attention_bwd import StrictTrilSelfAttnFn, analytic_tril_attn_backward
+    from kernels.cuda_attn import tril_decode_ref, tril_score_v_ref
+
+    import build_ref
+
+    ext = build_ref.load_module()
+    torch.manual_seed(0)
+
+    # ------------------------------------------------------------------ RoPE
+    rope = {}
+    for n in (64, 256, 8192):
+        rope[f"freqs_{n}"] = bdh.get_freqs(n, theta=2 ** 16, dtype=torch.float32).numpy()
+    cfg = bdh.BDHConfig(n_layer=1, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4, dropout=0.0)
+    att = bdh.Attention(cfg)  # N = 64
+    g = torch.Generator().manual_seed(1)
+    x = torch.relu(torch.randn(2, 3, 17, 64, generator=g))
+    rope["x"] = x.numpy()
+    for pos0 in (0, 37, 4000):
+        cs = att.rope_cos_sin(17, pos0, torch.device("cpu"))
+        rope[f"y_f32_pos{pos0}"] = _f32(att.rope(None, x, cos_sin=cs))
+        xb = x.to(torch.bfloat16)
+        rope[f"y_bf16_pos{pos0}"] = _f32(att.rope(None, xb, cos_sin=cs))
+    np.savez_compressed(HERE / "golden_rope.npz", **rope)
+
+    # --------------------------------------------------------------- forward
+    fwd = {}
+    g = torch.Generator().manual_seed(2)
+
+    def case(name, B, H, Hv, T, N, D, dtype=torch.float32, distinct_k=False):
+        q = torch.relu(torch.randn(B, H, T, N, generator=g)).to(dtype)
+        k = torch.relu(torch.randn(B, H, T, N, generator=g)).to(dtype) if distinct_k else q
+        v = torch.randn(B, Hv, T, D, generator=g).to(dtype)
+        fwd[f"{name}_q"] = _f32(q)
+        if distinct_k:
+            fwd[f"{name}_k"] = _f32(k)
+        fwd[f"{name}_v"] = _f32(v)
+        fwd[f"{name}_out_ext"] = _f32(ext.tril_score_v_cpu(q, k, v))  # csrc/tril_attn_cpu.cpp
+        fwd[f"{name}_out_ref"] = _f32(tril_score_v_ref(q.float(), k.float(), v.float()))
+
+    case("shared_v", 2, 3, 1, 130, 64, 32)
+    case("per_head_v", 2, 3, 3, 130, 64, 32)
+    case("t1", 1, 2, 1, 1, 16, 8)
+    case("t2", 1, 2, 1, 2, 16, 8)
+    case("distinct_k", 1, 2, 1, 40, 16, 8, distinct_k=True)
+    case("bf16", 1, 2, 1, 70, 64, 32, dtype=torch.bfloat16)
+    case("tiled", 1, 2, 1, 300, 32, 16)  # T*T > 65536: the extension's tiled path
+    # baseline Attention.forward (RoPE + tril) on raw latents
+    bcfg = bdh_baseline.BDHConfig(n_layer=1, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4)
+    batt = bdh_baseline.Attention(bcfg)
+    q = torch.relu(torch.randn(1, 2, 50, 64, generator=g))
+    v = torch.randn(1, 1, 50, 32, generator=g)
+    fwd["baseline_attn_q"] = q.numpy()
+    fwd["baseline_attn_v"] = v.numpy()
+    fwd["baseline_attn_out"] = _f32(batt(q, q, v))
+    fwd["baseline_attn_freqs"] = batt.freqs.reshape(-1).numpy()
+    np.savez_compressed(HERE / "golden_fwd.npz", **fwd)
+
+    # ---------------------------------------------------------------- decode
+    dec = {}
+    g = torch.Generator().manual_seed(3)
+    kbuf = torch.randn(2, 2, 40, 64, generator=g)
+    vbuf = torch.randn(2, 1, 40, 32, generator=g)
+    q = torch.randn(2, 2, 1, 64, generator=g)
+    dec["kbuf"], dec["vbuf"], dec["q"] = kbuf.numpy(), vbuf.numpy(), q.numpy()
+    for S in (0, 1, 25):
+        kp, vp = kbuf.narrow(2, 0, S), vbuf.narrow(2, 0, S)
+        dec[f"out_ext_S{S}"] = _f32(ext.tril_decode_cpu(q, kp, vp))
+        dec[f"out_ref_S{S}"] = _f32(tril_decode_ref(q, kp, vp))
+    q2 = torch.randn(1, 2, 3, 64, generator=g)  # Tq > 1
+    dec["q_tq3"] = q2.numpy()
+    dec["out_ext_tq3"] = _f32(ext.tril_decode_cpu(q2, kbuf[:1].narrow(2, 0, 25), vbuf[:1].narrow(2, 0, 25)))
+    np.savez_compressed(HERE / "golden_decode.npz", **dec)
+
+    # -------------------------------------------------------------- backward
+    bwd = {}
+    g = torch.Generator().manual_seed(4)
+    Q = torch.randn(1, 2, 24, 16, generator=g, dtype=torch.float64)
+    K = torch.randn(1, 2, 24, 16, generator=g, dtype=torch.float64)
+    V = torch.randn(1, 1, 24, 8, generator=g, dtype=torch.float64)
+    dO = torch.randn(1, 2, 24, 8, generator=g, dtype=torch.float64)
+    dQ, dK, dV = analytic_tril_attn_backward(Q, K, V, dO)
+    bwd.update(Q=Q.numpy(), K=K.numpy(), V=V.numpy(), dO=dO.numpy(), dQ=dQ.numpy(), dK=dK.numpy(),
+               dV=dV.numpy())
+    Qs = Q.clone().requires_grad_(True)
+    Vs = V.clone().requires_grad_(True)
+    out = StrictTrilSelfAttnFn.apply(Qs, Vs, "eager")
+    out.backward(dO)
+    bwd["self_out"] = out.detach().numpy()
+    bwd["self_dQ"] = Qs.grad.numpy()
+    bwd["self_dV"] = Vs.grad.numpy()
+    np.savez_compressed(HERE / "golden_bwd.npz", **bwd)
+
+    # ----------------------------------------------------------------- model
+    mod = {}
+    torch.manual_seed(5)
+    mcfg = bdh_baseline.BDHConfig(n_layer=2, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4,
+                                  dropout=0.0, vocab_size=256)
+    base = bdh_baseline.BDH(mcfg).eval()
+    for k, v in base.state_dict().items():
+        mod[f"w_{k}"] = v.numpy()
+    g = torch.Generator().manual_seed(6)
+    idx = torch.randint(0, 256, (2, 24), generator=g)
+    mod["idx"] = idx.numpy()
+    with torch.no_grad():
+        mod["logits_baseline"] = _f32(base(idx)[0])
+        opt = bdh.BDH(bdh.BDHConfig(**dataclasses_asdict(mcfg))).eval()
+        opt.load_state_dict(base.state_dict(), strict=False)
+        mod["logits_opt"] = _f32(opt(idx)[0])
+        # cached prefill of 16 tokens, then 8 teacher-forced T=1 steps
+        cache = CacheManager.from_config(opt.config, batch_size=2, max_seq=24, device="cpu")
+        lg, _ = opt(idx[:, :16], cache=cache)
+        steps = [_f32(lg[:, -1])]
+        for t in range(16, 24):
+            lg, _ = opt(idx[:, t:t + 1], cache=cache)
+            steps.append(_f32(lg[:, -1]))
+        mod["logits_cached_steps"] = np.stack(steps)
+    np.savez_compressed(HERE / "golden_model.npz", **mod)
+    print("wrote", sorted(p.name for p in HERE.glob("golden_*.npz")))
+
+
+def dataclasses_asdict(c):
+    import dataclasses
+
+    return dataclasses.asdict(c)
+
+
+if __name__ == "__main__":
+    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))

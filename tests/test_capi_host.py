@@ -1,0 +1,83 @@
+"""The C-ABI library loads on a CPU-only host, exports every symbol include/bdh_sm100.h
+declares, and rejects bad arguments on the host side (no kernel is launched)."""
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import REPO
+
+HEADER = REPO / "include" / "bdh_sm100.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:size_t|int|const char\*)\s+(bdh_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_boundary():
+    names = _declared()
+    for n in ("bdh_tril_score_v", "bdh_tril_decode", "bdh_tril_score_v_bwd", "bdh_rope_rotate",
+              "bdh_last_error", "bdh_abi_version"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    from kernels import sm100_attn as sa
+
+    lib = sa.load_library()
+    for name in _declared():
+        assert hasattr(lib, name), f"{name} missing from {sa._LIB_PATH}"
+    assert lib.bdh_abi_version() == 1
+
+
+def test_workspace_queries_are_host_only():
+    from kernels import sm100_attn as sa
+
+    lib = sa.load_library()
+    B, H, T, N, D = 2, 4, 300, 512, 256
+    bf = lib.bdh_tril_score_v_workspace_size(1, B, H, 1, T, N, D, 1)
+    ldp = (T + 7) // 8 * 8
+    assert bf >= 2 * B * H * T * ldp * 2
+    f32 = lib.bdh_tril_score_v_workspace_size(0, B, H, 1, T, N, D, 1)
+    assert f32 > 2 * B * H * T * N * 4  # tf32 hi/lo operand copies + score pair
+    assert lib.bdh_tril_decode_workspace_size(64, 4, 1, 1000, 256) == 16 * 64 * 4 * 256 * 4
+    assert lib.bdh_tril_score_v_bwd_workspace_size(1, B, H, 1, T, N, D, 1) > 0
+
+
+def _i64x4(*v):
+    return (ctypes.c_int64 * 4)(*v)
+
+
+def test_invalid_arguments_rejected_before_launch():
+    from kernels import sm100_attn as sa
+
+    lib = sa.load_library()
+    s = _i64x4(4096, 1024, 64, 1)
+    # bad dtype
+    rc = lib.bdh_tril_score_v(None, s, None, s, None, s, 7, None, s, 1, 1, 1, 1, 16, 64, 64, None, 0, None)
+    assert rc == 1 and b"dtype" in lib.bdh_last_error()
+    # v heads neither 1 nor H
+    rc = lib.bdh_tril_score_v(None, s, None, s, None, s, 1, None, s, 1, 1, 4, 2, 16, 64, 64, None, 0, None)
+    assert rc == 1 and b"heads" in lib.bdh_last_error()
+    # non-unit last stride
+    bad = _i64x4(4096, 1024, 64, 2)
+    rc = lib.bdh_tril_score_v(None, bad, None, bad, None, s, 1, None, s, 1, 1, 1, 1, 16, 64, 64, None, 0, None)
+    assert rc == 1 and b"contiguous" in lib.bdh_last_error()
+    # missing workspace
+    rc = lib.bdh_tril_score_v(None, s, None, s, None, s, 1, None, s, 1, 1, 1, 1, 16, 64, 64, None, 0, None)
+    assert rc == 3 and b"workspace" in lib.bdh_last_error()
+    # odd RoPE width
+    rc = lib.bdh_rope_rotate(None, 1, s, None, 1, s, None, None, 1, 1, 4, 63, 0, None)
+    assert rc == 1 and b"even" in lib.bdh_last_error()
+    # empty problems are a no-op success
+    rc = lib.bdh_tril_score_v(None, s, None, s, None, s, 1, None, s, 1, 0, 1, 1, 16, 64, 64, None, 0, None)
+    assert rc == 0
+
+
+def test_build_recipe_targets_sm100a():
+    import build_lib
+
+    assert "arch=compute_100a,code=sm_100a" in " ".join(build_lib.ARCH)
+    assert "-lineinfo" in build_lib.NVCC_FLAGS
