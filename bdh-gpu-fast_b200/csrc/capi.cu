@@ -66,6 +66,52 @@ FwdLayout fwd_layout(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T, int
   return L;
 }
 
+// Workspace layout of the backward (byte offsets).
+struct BwdLayout {
+  size_t s1_hi = 0, s1_lo = 0, s2_hi = 0, s2_lo = 0;
+  size_t do_hi = 0, do_lo = 0, v_hi = 0, v_lo = 0, q_hi = 0, q_lo = 0, k_hi = 0, k_lo = 0;
+  size_t qt_hi = 0, qt_lo = 0, kt_hi = 0, kt_lo = 0, dot_hi = 0, dot_lo = 0;
+  size_t total = 0;
+};
+
+BwdLayout bwd_layout(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T, int64_t N, int64_t D,
+                     bool k_is_q) {
+  BwdLayout L;
+  size_t off = 0;
+  const int e = esize(dtype);
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += align_up(bytes);
+    return o;
+  };
+  const size_t pbytes = static_cast<size_t>(B * H * T * score_ld(T)) * e;
+  L.s1_hi = take(pbytes);
+  L.s1_lo = take(pbytes);
+  if (!k_is_q) {
+    L.s2_hi = take(pbytes);
+    L.s2_lo = take(pbytes);
+  }
+  if (dtype == BDH_DTYPE_F32) {
+    const int64_t ldt = vt_ld(T);
+    const size_t dob = static_cast<size_t>(B * H * T * D) * 4;
+    const size_t vb = static_cast<size_t>(B * Hv * T * D) * 4;
+    const size_t qb = static_cast<size_t>(B * H * T * N) * 4;
+    const size_t qtb = static_cast<size_t>(B * H * N * ldt) * 4;
+    const size_t dotb = static_cast<size_t>(B * H * D * ldt) * 4;
+    L.do_hi = take(dob); L.do_lo = take(dob);
+    L.v_hi = take(vb); L.v_lo = take(vb);
+    L.q_hi = take(qb); L.q_lo = take(qb);
+    L.qt_hi = take(qtb); L.qt_lo = take(qtb);
+    L.dot_hi = take(dotb); L.dot_lo = take(dotb);
+    if (!k_is_q) {
+      L.k_hi = take(qb); L.k_lo = take(qb);
+      L.kt_hi = take(qtb); L.kt_lo = take(qtb);
+    }
+  }
+  L.total = off;
+  return L;
+}
+
 bool check_rows(const char* what, const int64_t s[4], int elem, std::string* msg) {
   if (s[3] != 1) {
     *msg = std::string(what) + ": the last dimension must be contiguous (stride 1)";
@@ -233,15 +279,158 @@ int bdh_tril_decode(const void* q, const int64_t q_strides[4], int q_dtype, cons
 
 size_t bdh_tril_score_v_bwd_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,
                                            int64_t N, int64_t D, int k_is_q) {
-  (void)dtype; (void)B; (void)H; (void)Hv; (void)T; (void)N; (void)D; (void)k_is_q;
-  return 0;
+  if (!dtype_ok(dtype)) return 0;
+  return bwd_layout(dtype, B, H, Hv, T, N, D, k_is_q != 0).total;
 }
 
-int bdh_tril_score_v_bwd(const void*, const int64_t*, const void*, const int64_t*, const void*,
-                         const int64_t*, const void*, const int64_t*, int, void*, const int64_t*,
-                         void*, const int64_t*, void*, const int64_t*, int64_t, int64_t, int64_t,
-                         int64_t, int64_t, int64_t, const float*, int64_t, void*, size_t, void*) {
-  return fail(BDH_ERR_INVALID, "tril_score_v_bwd: not available in this build");
+int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* k,
+                         const int64_t k_strides[4], const void* v, const int64_t v_strides[4],
+                         const void* dout, const int64_t dout_strides[4], int dtype, void* dq,
+                         const int64_t dq_strides[4], void* dk, const int64_t dk_strides[4],
+                         void* dv, const int64_t dv_strides[4], int64_t B, int64_t H, int64_t Hv,
+                         int64_t T, int64_t N, int64_t D, const float* freqs, int64_t pos0,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (!dtype_ok(dtype)) return fail(BDH_ERR_INVALID, "tril_score_v_bwd: dtype must be f32 or bf16");
+  if (B < 0 || H < 0 || T < 0 || N < 0 || D < 0)
+    return fail(BDH_ERR_INVALID, "tril_score_v_bwd: negative size");
+  if (Hv != 1 && Hv != H) return fail(BDH_ERR_INVALID, "tril_score_v_bwd: v heads must equal q heads or 1");
+  const bool k_is_q = (k == q) && std::memcmp(q_strides, k_strides, 4 * sizeof(int64_t)) == 0;
+  if (!k_is_q && (dk == nullptr || dk_strides == nullptr))
+    return fail(BDH_ERR_INVALID, "tril_score_v_bwd: dk is required when k is not q");
+  if (freqs != nullptr && !k_is_q)
+    return fail(BDH_ERR_INVALID, "tril_score_v_bwd: the fused RoPE adjoint needs k == q");
+  if (freqs != nullptr && (N % 2) != 0)
+    return fail(BDH_ERR_INVALID, "tril_score_v_bwd: RoPE last dim must be even");
+  for (const int64_t* st : {q_strides, k_strides, v_strides, dout_strides, dq_strides, dv_strides})
+    if (st[3] != 1) return fail(BDH_ERR_INVALID, "tril_score_v_bwd: last dimension must be contiguous");
+  if (!k_is_q && dk_strides[3] != 1)
+    return fail(BDH_ERR_INVALID, "tril_score_v_bwd: last dimension must be contiguous");
+  if (T > (int64_t(1) << 24) || B * H > (int64_t(1) << 30))
+    return fail(BDH_ERR_INVALID, "tril_score_v_bwd: sizes beyond the supported range");
+  if (B * H * T == 0) return BDH_OK;
+  const BwdLayout L = bwd_layout(dtype, B, H, Hv, T, N, D, k_is_q);
+  if (workspace == nullptr || workspace_bytes < L.total) {
+    std::ostringstream os;
+    os << "tril_score_v_bwd: workspace of " << L.total << " bytes required, got " << workspace_bytes;
+    return fail(BDH_ERR_WORKSPACE, os.str());
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* err = device_error_ptr();
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int elem = esize(dtype);
+  const bool f32 = dtype == BDH_DTYPE_F32;
+  int rc = 0;
+  // Operands as the tensor-core passes consume them.
+  const void* q_op[2] = {q, nullptr};
+  const void* k_op[2] = {k, nullptr};
+  const void* v_op[2] = {v, nullptr};
+  const void* do_op[2] = {dout, nullptr};
+  int64_t qs[4], ks[4], vs[4], dos[4];
+  std::memcpy(qs, q_strides, sizeof(qs));
+  std::memcpy(ks, k_strides, sizeof(ks));
+  std::memcpy(vs, v_strides, sizeof(vs));
+  std::memcpy(dos, dout_strides, sizeof(dos));
+  const void* qT[2] = {q, nullptr};   // grad-q B operand for dS^T Q / G Q
+  const void* kT[2] = {k, nullptr};   // grad-q B operand for dS K
+  const void* doT[2] = {dout, nullptr};
+  if (f32) {
+    const int64_t ldt = vt_ld(T);
+    auto split = [&](const void* x, const int64_t* xs, int64_t h, int64_t w, size_t hi_off,
+                     size_t lo_off, const void** dst, int64_t* dst_strides) -> int {
+      float* hi = reinterpret_cast<float*>(ws + hi_off);
+      float* lo = reinterpret_cast<float*>(ws + lo_off);
+      int r = launch_split_tf32(static_cast<const float*>(x), xs, hi, lo, B, h, T, w, st);
+      dst[0] = hi;
+      dst[1] = lo;
+      const int64_t cs[4] = {h * T * w, T * w, w, 1};
+      std::memcpy(dst_strides, cs, sizeof(cs));
+      return r;
+    };
+    auto split_t = [&](const void* x, const int64_t* xs, int64_t h, int64_t w, size_t hi_off,
+                       size_t lo_off, const void** dst) -> int {
+      float* hi = reinterpret_cast<float*>(ws + hi_off);
+      float* lo = reinterpret_cast<float*>(ws + lo_off);
+      dst[0] = hi;
+      dst[1] = lo;
+      return launch_split_tf32_t(static_cast<const float*>(x), xs, hi, lo, B, h, T, w, ldt, st);
+    };
+    if ((rc = split(dout, dout_strides, H, D, L.do_hi, L.do_lo, do_op, dos))) return rc;
+    if ((rc = split(v, v_strides, Hv, D, L.v_hi, L.v_lo, v_op, vs))) return rc;
+    if ((rc = split(q, q_strides, H, N, L.q_hi, L.q_lo, q_op, qs))) return rc;
+    if ((rc = split_t(q, q_strides, H, N, L.qt_hi, L.qt_lo, qT))) return rc;
+    if ((rc = split_t(dout, dout_strides, H, D, L.dot_hi, L.dot_lo, doT))) return rc;
+    if (k_is_q) {
+      k_op[0] = q_op[0]; k_op[1] = q_op[1];
+      std::memcpy(ks, qs, sizeof(ks));
+    } else {
+      if ((rc = split(k, k_strides, H, N, L.k_hi, L.k_lo, k_op, ks))) return rc;
+      if ((rc = split_t(k, k_strides, H, N, L.kt_hi, L.kt_lo, kT))) return rc;
+    }
+  }
+  void* g_hi = ws + L.s1_hi;
+  void* g_lo = ws + L.s1_lo;
+  // 1. dS = tril(dO V^T, -1) -> G (K is Q) or L / U.
+  ScoreArgs sa;
+  sa.elem = elem;
+  sa.a[0] = do_op[0]; sa.a[1] = do_op[1];
+  sa.b[0] = v_op[0]; sa.b[1] = v_op[1];
+  std::memcpy(sa.a_strides, dos, sizeof(dos));
+  std::memcpy(sa.b_strides, vs, sizeof(vs));
+  sa.B = B; sa.H = H; sa.Hb = Hv; sa.T = T; sa.K = D;
+  sa.mode = k_is_q ? kStoreSym : kStoreLU;
+  sa.p_hi = g_hi; sa.p_lo = g_lo;
+  sa.p2_hi = ws + L.s2_hi; sa.p2_lo = ws + L.s2_lo;
+  if ((rc = launch_score_pass(sa, st, err))) return rc;
+  // 2. dQ (and dK).
+  GradQArgs ga;
+  ga.elem = elem;
+  ga.B = B; ga.H = H; ga.T = T; ga.N = N;
+  ga.out_dtype = dtype;
+  ga.g_hi = g_hi; ga.g_lo = g_lo;
+  ga.out = dq;
+  std::memcpy(ga.out_strides, dq_strides, sizeof(ga.out_strides));
+  if (k_is_q) {
+    ga.krange = 0;
+    ga.x[0] = qT[0]; ga.x[1] = qT[1];
+    std::memcpy(ga.x_strides, q_strides, sizeof(ga.x_strides));
+    ga.freqs = freqs;
+    ga.pos0 = pos0;
+    if ((rc = launch_grad_q(ga, st, err))) return rc;
+  } else {
+    ga.krange = 1;
+    ga.x[0] = kT[0]; ga.x[1] = kT[1];
+    std::memcpy(ga.x_strides, k_strides, sizeof(ga.x_strides));
+    if ((rc = launch_grad_q(ga, st, err))) return rc;
+    ga.krange = 2;
+    ga.g_hi = ws + L.s2_hi; ga.g_lo = ws + L.s2_lo;
+    ga.x[0] = qT[0]; ga.x[1] = qT[1];
+    std::memcpy(ga.x_strides, q_strides, sizeof(ga.x_strides));
+    ga.out = dk;
+    std::memcpy(ga.out_strides, dk_strides, sizeof(ga.out_strides));
+    if ((rc = launch_grad_q(ga, st, err))) return rc;
+  }
+  // 3. M^T = tril(Q K^T, -1)^T into the first score pair (its G / L contents are consumed).
+  ScoreArgs sm;
+  sm.elem = elem;
+  sm.a[0] = q_op[0]; sm.a[1] = q_op[1];
+  sm.b[0] = k_op[0]; sm.b[1] = k_op[1];
+  std::memcpy(sm.a_strides, qs, sizeof(qs));
+  std::memcpy(sm.b_strides, ks, sizeof(ks));
+  sm.B = B; sm.H = H; sm.Hb = H; sm.T = T; sm.K = N;
+  sm.mode = kStoreTrans;
+  sm.p_hi = g_hi; sm.p_lo = g_lo;
+  if ((rc = launch_score_pass(sm, st, err))) return rc;
+  // 4. dV = sum_h M^T dO.
+  GradVArgs va;
+  va.elem = elem;
+  va.mt_hi = g_hi; va.mt_lo = g_lo;
+  va.dout[0] = doT[0]; va.dout[1] = doT[1];
+  std::memcpy(va.do_strides, dout_strides, sizeof(va.do_strides));
+  va.B = B; va.H = H; va.Hv = Hv; va.T = T; va.D = D;
+  va.out = dv;
+  std::memcpy(va.out_strides, dv_strides, sizeof(va.out_strides));
+  va.out_dtype = dtype;
+  return launch_grad_v(va, st, err);
 }
 
 }  // extern "C"

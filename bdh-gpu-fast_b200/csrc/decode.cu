@@ -248,6 +248,7 @@ int launch_decode(const DecodeArgs& a, float* partial, cudaStream_t stream) {
         a.slot_strides[2], a.pos);                                                                \
   } while (0)
   const bool qf = a.q_dtype == BDH_DTYPE_F32, kf = a.kv_dtype == BDH_DTYPE_F32;
+  prof_start(kProfDecode, stream);
   if (qf && kf) {
     if (vec) BDH_DEC_LAUNCH(float, float, true); else BDH_DEC_LAUNCH(float, float, false);
   } else if (qf) {
@@ -273,6 +274,7 @@ int launch_decode(const DecodeArgs& a, float* partial, cudaStream_t stream) {
     decode_reduce_kernel<uint16_t><<<static_cast<unsigned>(bht), threads, 0, stream>>>(
         partial, static_cast<uint16_t*>(a.out), nsplit, Hi, Tqi, Di, bht, a.out_strides[0],
         a.out_strides[1], a.out_strides[2]);
+  prof_stop(kProfDecode, stream);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("decode_reduce_kernel launch: ") + cudaGetErrorString(e));

@@ -286,11 +286,13 @@ int launch_rope(const void* x, int x_dtype, const int64_t xs[4], void* y, int y_
           static_cast<const TX*>(x), static_cast<TY*>(y), y_lo, freqs, Hi, Ti, Ni, BHi, R, xs[0], \
           xs[1], xs[2], ys[0], ys[1], ys[2], pos0);                                               \
   } while (0)
+  prof_start(kProfRope, stream);
   if (x_dtype == BDH_DTYPE_BF16 && y_dtype == BDH_DTYPE_BF16) BDH_ROPE_LAUNCH(uint16_t, uint16_t);
   else if (x_dtype == BDH_DTYPE_BF16) BDH_ROPE_LAUNCH(uint16_t, float);
   else if (y_dtype == BDH_DTYPE_BF16) BDH_ROPE_LAUNCH(float, uint16_t);
   else BDH_ROPE_LAUNCH(float, float);
 #undef BDH_ROPE_LAUNCH
+  prof_stop(kProfRope, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("rope_kernel launch: ") + cudaGetErrorString(e));
@@ -306,12 +308,14 @@ int launch_split_tf32(const float* x, const int64_t xs[4], float* hi, float* lo,
   bool vec = (N % 4 == 0) && aligned16(x) && aligned16(hi) && aligned16(lo);
   for (int i = 0; i < 3; ++i) vec = vec && (xs[i] * 4) % 16 == 0;
   const int threads = static_cast<int>(std::min<int64_t>(256, std::max<int64_t>(32, N / 4)));
+  prof_start(kProfSplit, stream);
   if (vec)
     split_tf32_kernel<true><<<static_cast<unsigned>(rows), threads, 0, stream>>>(
         x, hi, lo, static_cast<int>(H), static_cast<int>(T), static_cast<int>(N), xs[0], xs[1], xs[2]);
   else
     split_tf32_kernel<false><<<static_cast<unsigned>(rows), threads, 0, stream>>>(
         x, hi, lo, static_cast<int>(H), static_cast<int>(T), static_cast<int>(N), xs[0], xs[1], xs[2]);
+  prof_stop(kProfSplit, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("split_tf32_kernel launch: ") + cudaGetErrorString(e));
@@ -325,9 +329,11 @@ int launch_split_tf32_t(const float* x, const int64_t xs[4], float* hi, float* l
   if (B * H * T * N == 0) return BDH_OK;
   const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((T + 31) / 32),
                   static_cast<unsigned>(B * H));
+  prof_start(kProfSplit, stream);
   split_tf32_t_kernel<<<grid, dim3(32, 8), 0, stream>>>(x, hi, lo, static_cast<int>(H),
                                                         static_cast<int>(T), static_cast<int>(N),
                                                         ldt, xs[0], xs[1], xs[2]);
+  prof_stop(kProfSplit, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("split_tf32_t_kernel launch: ") + cudaGetErrorString(e));

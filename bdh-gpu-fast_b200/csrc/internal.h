@@ -9,6 +9,12 @@
 
 namespace bdh {
 
+// Launch timing hooks (prof.cpp); kinds as documented at bdh_profile_end.
+enum ProfKind : int { kProfScore = 0, kProfValue = 1, kProfRope = 2, kProfDecode = 3,
+                      kProfGradQ = 4, kProfGradV = 5, kProfSplit = 6 };
+void prof_start(int kind, cudaStream_t s);
+void prof_stop(int kind, cudaStream_t s);
+
 // One forward problem. For fp32 inputs q/k/v point at tf32 "hi" operands and *_lo at the
 // matching residuals (x - hi); for bf16 the *_lo pointers are unused.
 struct FwdArgs {
@@ -28,12 +34,67 @@ struct FwdArgs {
   int64_t B = 0, H = 0, Hv = 0, T = 0, N = 0, D = 0;
 };
 
+// Layouts of the masked score pass output (see score_pass.cuh).
+enum ScoreStore : int { kStoreDirect = 0, kStoreTrans = 1, kStoreSym = 2, kStoreLU = 3 };
+
+// One masked score pass S = tril(A B^T, -1) per unit; A: (B,H,T,K), B: (B,Hb,T,K) with
+// Hb in {1,H}. elem 2: bf16 operands (a[0], b[0]); elem 4: tf32 hi/lo pairs (a[0..1], b[0..1]).
+struct ScoreArgs {
+  int elem = 2;
+  const void* a[2] = {nullptr, nullptr};
+  int64_t a_strides[4] = {0, 0, 0, 1};
+  const void* b[2] = {nullptr, nullptr};
+  int64_t b_strides[4] = {0, 0, 0, 1};
+  int64_t B = 0, H = 0, Hb = 0, T = 0, K = 0;
+  int mode = kStoreDirect;
+  void* p_hi = nullptr;
+  void* p_lo = nullptr;
+  void* p2_hi = nullptr;
+  void* p2_lo = nullptr;
+};
+int launch_score_pass(const ScoreArgs& a, cudaStream_t stream, int* err);
+
 int64_t score_ld(int64_t T);
 // Row length (keys) of the transposed tf32 V operand: [B*Hv][D][vt_ld(T)].
 int64_t vt_ld(int64_t T);
 int launch_score(const FwdArgs& a, void* p_hi, void* p_lo, cudaStream_t stream, int* err);
 int launch_value(const FwdArgs& a, const void* p_hi, const void* p_lo, cudaStream_t stream,
                  int* err);
+
+// Backward passes (attn_bwd.cu).
+// out[u] = Gs[u] X[u] with Gs a hi/lo score pair ([B*H][T][score_ld(T)]); krange 0: all keys,
+// 1: keys below the end of each 128-row block, 2: keys from the start of each block.
+// elem 2: X is (B,H,T,N) bf16 (x[0], x_strides); elem 4: X^T tf32 hi/lo [B*H][N][vt_ld(T)].
+struct GradQArgs {
+  int elem = 2;
+  const void* g_hi = nullptr;
+  const void* g_lo = nullptr;
+  const void* x[2] = {nullptr, nullptr};
+  int64_t x_strides[4] = {0, 0, 0, 1};
+  int64_t B = 0, H = 0, T = 0, N = 0;
+  int krange = 0;
+  void* out = nullptr;
+  int64_t out_strides[4] = {0, 0, 0, 1};
+  int out_dtype = BDH_DTYPE_BF16;
+  const float* freqs = nullptr;
+  int64_t pos0 = 0;
+};
+int launch_grad_q(const GradQArgs& a, cudaStream_t stream, int* err);
+
+// dV[b,hv] = sum over heads sharing hv of Mt_h dO_h with Mt = M^T as a hi/lo score pair.
+// elem 2: dO is (B,H,T,D) bf16; elem 4: dO^T tf32 hi/lo [B*H][D][vt_ld(T)].
+struct GradVArgs {
+  int elem = 2;
+  const void* mt_hi = nullptr;
+  const void* mt_lo = nullptr;
+  const void* dout[2] = {nullptr, nullptr};
+  int64_t do_strides[4] = {0, 0, 0, 1};
+  int64_t B = 0, H = 0, Hv = 0, T = 0, D = 0;
+  void* out = nullptr;
+  int64_t out_strides[4] = {0, 0, 0, 1};
+  int out_dtype = BDH_DTYPE_BF16;
+};
+int launch_grad_v(const GradVArgs& a, cudaStream_t stream, int* err);
 
 // Elementwise kernels (elementwise.cu).
 int launch_rope(const void* x, int x_dtype, const int64_t xs[4], void* y, int y_dtype,

@@ -1,0 +1,210 @@
+// The masked score pass shared by forward and backward, and the persistent launcher.
+//
+//   S[u] = tril(A[u] B[u]^T, -1)   over the lower-triangular 128 x BN tiles of each unit u=(b,h)
+//
+// with the K-loop over the contraction width (N for Q K^T, D for dO V^T). S is written as an
+// exact split pair (bf16 hi + bf16 lo, or tf32 hi + fp32 lo) in one of four layouts:
+//   kStoreDirect : S at [u][i][j]                       (forward P)
+//   kStoreTrans  : S^T at [u][j][i]                     (backward M^T, the K-major A of dV)
+//   kStoreSym    : S + S^T at [u][i][j]                 (backward G = dS + dS^T, K is Q)
+//   kStoreLU     : S at out1[u][i][j], S^T at out2      (backward dS / dS^T, K distinct)
+// Transposed stores are coalesced across the warp: lanes own consecutive rows i, so for a
+// fixed column j the 32 lanes write 32 consecutive elements of row j of the transpose.
+#pragma once
+
+#include <algorithm>
+#include <string>
+
+#include "bdh_sm100.h"
+#include "internal.h"
+#include "tc_engine.cuh"
+#include "tma_host.h"
+
+namespace bdh {
+
+__device__ __forceinline__ int ceil_div_d(int a, int b) { return (a + b - 1) / b; }
+
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// fp32 inputs (ELEM 4) accumulate in 256-wide K chunks (see TcShape::KCHUNK).
+template <int ELEM, int BN, int STAGES>
+struct ScoreProb {
+  static constexpr int TERMS = ELEM == 2 ? 1 : 2;
+  using S = TcShape<ELEM, BN, false, false, TERMS, TERMS, STAGES, ELEM == 4 ? 8 : 0>;
+  struct Params {
+    CUtensorMap a_map[2];  // rows i of A (hi, lo), box BK x 128
+    CUtensorMap b_map[2];  // rows j of B (hi, lo), box BK x BN
+    int H, T, K;           // heads, sequence length, contraction width
+    int b_shared;          // B has a single head shared by all H heads of A
+    int mode;              // ScoreStore
+    int mt;                // 128-row blocks per unit
+    int tiles_per_unit;
+    int units;
+    void* p_hi;            // [units][T][ldp]
+    void* p_lo;
+    void* p2_hi;           // kStoreLU: transposed destination
+    void* p2_lo;
+    int64_t ldp;
+    int* err;
+  };
+  struct Tile {
+    int unit, mi, ni;
+  };
+
+  __device__ static int nt_for(const Params& p, int mi) {
+    return ceil_div_d(min(p.T, (mi + 1) * S::BM), BN);
+  }
+  __device__ static int num_tiles(const Params& p) { return p.units * p.tiles_per_unit; }
+  __device__ static Tile tile(const Params& p, int t) {
+    Tile tl;
+    tl.unit = t / p.tiles_per_unit;
+    int r = t - tl.unit * p.tiles_per_unit;
+    int mi = 0;
+    for (;; ++mi) {
+      const int c = nt_for(p, mi);
+      if (r < c) break;
+      r -= c;
+    }
+    tl.mi = mi;
+    tl.ni = r;
+    return tl;
+  }
+  __device__ static int k_blocks(const Params& p, const Tile&) { return ceil_div_d(p.K, S::BK); }
+  __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x7u; }
+  __device__ static void prefetch(const Params& p) {
+    for (int i = 0; i < TERMS; ++i) {
+      tma_prefetch_desc(&p.a_map[i]);
+      tma_prefetch_desc(&p.b_map[i]);
+    }
+  }
+  __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint64_t* bar,
+                                    uint8_t* a_dst, uint8_t* b_dst) {
+    const int b = tl.unit / p.H, h = tl.unit - (tl.unit / p.H) * p.H;
+    const int hb = p.b_shared ? 0 : h;
+    for (int i = 0; i < TERMS; ++i) {
+      tma_load_4d(&p.a_map[i], bar, a_dst + i * S::A_TILE, kb * S::BK, tl.mi * S::BM, h, b);
+      tma_load_4d(&p.b_map[i], bar, b_dst + i * S::B_TILE, kb * S::BK, tl.ni * BN, hb, b);
+    }
+  }
+
+  // Split x into the stored pair (hi, lo): bf16 bits or tf32/fp32 values.
+  __device__ static __forceinline__ void split(float x, uint32_t& hi, uint32_t& lo) {
+    if (ELEM == 2) {
+      hi = f32_to_bf16_bits(x);
+      lo = f32_to_bf16_bits(x - bf16_bits_to_f32(hi));
+    } else {
+      const float h = tf32_rna(x);
+      hi = __float_as_uint(h);
+      lo = __float_as_uint(x - h);
+    }
+  }
+  __device__ static __forceinline__ void store1(void* base, size_t idx, uint32_t bits) {
+    if (ELEM == 2)
+      static_cast<uint16_t*>(base)[idx] = static_cast<uint16_t>(bits);
+    else
+      static_cast<uint32_t*>(base)[idx] = bits;
+  }
+
+  __device__ static void epilogue(const Params& p, const Tile& tl, int row, int c0,
+                                  const uint32_t (&r)[32]) {
+    const int gi = tl.mi * S::BM + row;
+    if (gi >= p.T) return;
+    const int gj_base = tl.ni * BN + c0;
+    const bool diag = tl.ni * BN < (tl.mi + 1) * S::BM && (tl.ni + 1) * BN > tl.mi * S::BM;
+    uint32_t hi[32], lo[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const float x = gj_base + e < gi ? __uint_as_float(r[e]) : 0.0f;
+      split(x, hi[e], lo[e]);
+    }
+    const size_t unit_off = static_cast<size_t>(tl.unit) * p.T;
+    // ---- direct store S[i][j] (vectorised unless it must skip the upper part of a diagonal tile)
+    if (p.mode == kStoreDirect || p.mode == kStoreLU || (p.mode == kStoreSym && !diag)) {
+      const size_t row_off = (unit_off + gi) * static_cast<size_t>(p.ldp);
+      if (ELEM == 2) {
+        uint16_t* dh = static_cast<uint16_t*>(p.p_hi) + row_off;
+        uint16_t* dl = static_cast<uint16_t*>(p.p_lo) + row_off;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const int gj0 = gj_base + 8 * v;
+          if (gj0 + 8 > p.ldp) continue;
+          *reinterpret_cast<uint4*>(dh + gj0) =
+              make_uint4(hi[8 * v] | (hi[8 * v + 1] << 16), hi[8 * v + 2] | (hi[8 * v + 3] << 16),
+                         hi[8 * v + 4] | (hi[8 * v + 5] << 16), hi[8 * v + 6] | (hi[8 * v + 7] << 16));
+          *reinterpret_cast<uint4*>(dl + gj0) =
+              make_uint4(lo[8 * v] | (lo[8 * v + 1] << 16), lo[8 * v + 2] | (lo[8 * v + 3] << 16),
+                         lo[8 * v + 4] | (lo[8 * v + 5] << 16), lo[8 * v + 6] | (lo[8 * v + 7] << 16));
+        }
+      } else {
+        uint32_t* dh = static_cast<uint32_t*>(p.p_hi) + row_off;
+        uint32_t* dl = static_cast<uint32_t*>(p.p_lo) + row_off;
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const int gj0 = gj_base + 4 * v;
+          if (gj0 + 4 > p.ldp) continue;
+          *reinterpret_cast<uint4*>(dh + gj0) = make_uint4(hi[4 * v], hi[4 * v + 1], hi[4 * v + 2], hi[4 * v + 3]);
+          *reinterpret_cast<uint4*>(dl + gj0) = make_uint4(lo[4 * v], lo[4 * v + 1], lo[4 * v + 2], lo[4 * v + 3]);
+        }
+      }
+    } else if (p.mode == kStoreSym) {
+      // diagonal tile: this orientation owns j <= i (the diagonal itself is zero)
+      const size_t row_off = (unit_off + gi) * static_cast<size_t>(p.ldp);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int gj = gj_base + e;
+        if (gj <= gi) {
+          store1(p.p_hi, row_off + gj, hi[e]);
+          store1(p.p_lo, row_off + gj, lo[e]);
+        }
+      }
+    }
+    // ---- transposed store S^T[j][i]
+    if (p.mode == kStoreTrans || p.mode == kStoreLU || p.mode == kStoreSym) {
+      void* th = p.mode == kStoreLU ? p.p2_hi : p.p_hi;
+      void* tlo = p.mode == kStoreLU ? p.p2_lo : p.p_lo;
+      const bool strict = p.mode == kStoreSym && diag;  // Sym diagonal: only j < i here
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int gj = gj_base + e;
+        if (gj >= p.T || (strict && gj >= gi)) continue;
+        const size_t idx = (unit_off + gj) * static_cast<size_t>(p.ldp) + gi;
+        store1(th, idx, hi[e]);
+        store1(tlo, idx, lo[e]);
+      }
+    }
+  }
+};
+
+template <class S, class P>
+static int launch_tc(const typename P::Params& prm, int ntiles, cudaStream_t stream, int kind) {
+  if (ntiles <= 0) return 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr_set[64] = {false};
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<S, P>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         S::SMEM_BYTES);
+    if (e != cudaSuccess) {
+      set_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+      return BDH_ERR_CUDA;
+    }
+    attr_set[dev] = true;
+  }
+  const int grid = std::min(ntiles, sm_count(dev));
+  prof_start(kind, stream);
+  tc_gemm_kernel<S, P><<<grid, kTcThreads, S::SMEM_BYTES, stream>>>(prm);
+  prof_stop(kind, stream);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("tc_gemm_kernel launch: ") + cudaGetErrorString(e));
+    return BDH_ERR_CUDA;
+  }
+  return 0;
+}
+
+}  // namespace bdh

@@ -23,7 +23,13 @@ namespace bdh {
 constexpr int kTcThreads = 192;
 constexpr int kEpiThreads = 128;
 
-template <int ELEM_, int BN_, bool A_MN_, bool B_MN_, int A_TERMS_, int B_TERMS_, int STAGES_>
+// KCHUNK_ > 0: the K-loop of a tile is cut into chunks of KCHUNK_ k-blocks, each accumulated in
+// its own TMEM buffer and summed by the epilogue in fp32 registers (round-to-nearest). This
+// bounds the length of every tensor-core accumulation chain, which matters for the fp32 path:
+// one accumulator fed by thousands of MMAs drifted to ~5e-5 relative error at K = 8192 with
+// the 3-product tf32 split, above the 1e-5 fp32 tolerance).
+template <int ELEM_, int BN_, bool A_MN_, bool B_MN_, int A_TERMS_, int B_TERMS_, int STAGES_,
+          int KCHUNK_ = 0>
 struct TcShape {
   static constexpr int ELEM = ELEM_;               // operand element bytes: 2 (bf16) or 4 (tf32)
   static constexpr int BM = 128;
@@ -35,6 +41,7 @@ struct TcShape {
   static constexpr int A_TERMS = A_TERMS_;
   static constexpr int B_TERMS = B_TERMS_;
   static constexpr int STAGES = STAGES_;
+  static constexpr int KCHUNK = KCHUNK_;
   static constexpr int A_TILE = BM * 128;          // bytes of one A term in one stage
   static constexpr int B_TILE = BN * 128;
   static constexpr int STAGE_BYTES = A_TILE * A_TERMS + B_TILE * B_TERMS;
@@ -46,6 +53,11 @@ struct TcShape {
   static constexpr int NPAIRS = (A_TERMS == 1 && B_TERMS == 1) ? 1 : (A_TERMS == 2 && B_TERMS == 2 ? 3 : 2);
 
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
+  static_assert(KCHUNK == 0 || BN <= 128, "chunked accumulation keeps BN fp32 sums per thread");
+
+  __host__ __device__ static int chunks(int nkb) {
+    return KCHUNK == 0 ? 1 : (nkb + KCHUNK - 1) / KCHUNK;
+  }
   static_assert(STAGES * STAGE_BYTES + BAR_BYTES + 1024 <= 232448, "shared memory budget");
 
   // Byte offset of the kk-th MMA's K slice inside one term tile.
@@ -153,53 +165,58 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (elect_one()) {
       int stage = 0;
       uint32_t ph = 0;
-      int lt = 0;
+      int lc = 0;  // accumulation chunks issued by this CTA (selects the TMEM buffer)
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++lt) {
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
         typename P::Tile tile = P::tile(prm, t);
         const int nkb = P::k_blocks(prm, tile);
-        const int acc = lt & 1;
-        const uint32_t aph = static_cast<uint32_t>(lt >> 1) & 1u;
-        if (!wait_bounded(tempty + acc, aph ^ 1u, abort_flag, prm.err, kErrTimeoutMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * S::BN);
-        for (int kb = 0; kb < nkb; ++kb) {
-          if (!wait_bounded(full + stage, ph, abort_flag, prm.err, kErrTimeoutMma)) {
+        const int nch = S::chunks(nkb);
+        for (int ch = 0; ch < nch && ok; ++ch, ++lc) {
+          const int acc = lc & 1;
+          const uint32_t aph = static_cast<uint32_t>(lc >> 1) & 1u;
+          if (!wait_bounded(tempty + acc, aph ^ 1u, abort_flag, prm.err, kErrTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(smem + stage * S::STAGE_BYTES);
-          const uint32_t b_base = a_base + S::A_TERMS * S::A_TILE;
-          const uint32_t pair_mask = P::pair_mask(prm, tile, kb);
+          const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * S::BN);
+          const int kb0 = S::KCHUNK == 0 ? 0 : ch * S::KCHUNK;
+          const int kb1 = S::KCHUNK == 0 ? nkb : min(nkb, kb0 + S::KCHUNK);
+          for (int kb = kb0; kb < kb1; ++kb) {
+            if (!wait_bounded(full + stage, ph, abort_flag, prm.err, kErrTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(smem + stage * S::STAGE_BYTES);
+            const uint32_t b_base = a_base + S::A_TERMS * S::A_TILE;
+            const uint32_t pair_mask = P::pair_mask(prm, tile, kb);
 #pragma unroll
-          for (int kk = 0; kk < S::BK / S::UK; ++kk) {
+            for (int kk = 0; kk < S::BK / S::UK; ++kk) {
 #pragma unroll
-            for (int pr = 0; pr < S::NPAIRS; ++pr) {
-              if (!((pair_mask >> pr) & 1u)) continue;
-              // pair 0: A0*B0; pair 1: A1*B0 (or A0*B1 when only B is split); pair 2: A0*B1
-              const int ta = (pr == 1 && S::A_TERMS == 2) ? 1 : 0;
-              const int tb = (pr == 2 || (pr == 1 && S::A_TERMS == 1)) ? 1 : 0;
-              const uint64_t ad = S::a_desc(a_base + ta * S::A_TILE + S::a_koff(kk));
-              const uint64_t bd = S::b_desc(b_base + tb * S::B_TILE + S::b_koff(kk));
-              const uint32_t accumulate = (kb > 0 || kk > 0 || pr > 0) ? 1u : 0u;
-              if (S::ELEM == 2)
-                umma_f16(d_tmem, ad, bd, S::IDESC, accumulate);
-              else
-                umma_tf32(d_tmem, ad, bd, S::IDESC, accumulate);
+              for (int pr = 0; pr < S::NPAIRS; ++pr) {
+                if (!((pair_mask >> pr) & 1u)) continue;
+                // pair 0: A0*B0; pair 1: A1*B0 (or A0*B1 when only B is split); pair 2: A0*B1
+                const int ta = (pr == 1 && S::A_TERMS == 2) ? 1 : 0;
+                const int tb = (pr == 2 || (pr == 1 && S::A_TERMS == 1)) ? 1 : 0;
+                const uint64_t ad = S::a_desc(a_base + ta * S::A_TILE + S::a_koff(kk));
+                const uint64_t bd = S::b_desc(b_base + tb * S::B_TILE + S::b_koff(kk));
+                const uint32_t accumulate = (kb > kb0 || kk > 0 || pr > 0) ? 1u : 0u;
+                if (S::ELEM == 2)
+                  umma_f16(d_tmem, ad, bd, S::IDESC, accumulate);
+                else
+                  umma_tf32(d_tmem, ad, bd, S::IDESC, accumulate);
+              }
+            }
+            umma_commit(empty + stage);
+            if (++stage == S::STAGES) {
+              stage = 0;
+              ph ^= 1u;
             }
           }
-          umma_commit(empty + stage);
-          if (++stage == S::STAGES) {
-            stage = 0;
-            ph ^= 1u;
-          }
+          if (!ok) break;
+          umma_commit(tfull + acc);
         }
-        if (!ok) break;
-        umma_commit(tfull + acc);
       }
       // All MMAs issued by this thread must finish before TMEM is released.
       umma_commit(drain);
@@ -209,25 +226,68 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---------------------------------------------------------------- epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + static_cast<int>(lane_id());
-    int lt = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++lt) {
+    int lc = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
       typename P::Tile tile = P::tile(prm, t);
-      const int acc = lt & 1;
-      const uint32_t aph = static_cast<uint32_t>(lt >> 1) & 1u;
-      bool ok = wait_bounded(tfull + acc, aph, abort_flag, prm.err, kErrTimeoutEpilogue);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
-      const uint32_t tbase =
-          tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * S::BN);
+      if (S::KCHUNK == 0) {
+        const int acc = lc & 1;
+        const uint32_t aph = static_cast<uint32_t>(lc >> 1) & 1u;
+        ok = wait_bounded(tfull + acc, aph, abort_flag, prm.err, kErrTimeoutEpilogue);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tbase =
+            tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * S::BN);
 #pragma unroll 1
-      for (int c0 = 0; c0 < S::BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tbase + static_cast<uint32_t>(c0), r);
-        tmem_ld_wait();
-        P::epilogue(prm, tile, row, c0, r);
+        for (int c0 = 0; c0 < S::BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + static_cast<uint32_t>(c0), r);
+          tmem_ld_wait();
+          P::epilogue(prm, tile, row, c0, r);
+        }
+        tc_fence_before();
+        mbar_arrive(tempty + acc);
+        ++lc;
+      } else {
+        constexpr int BNC = S::KCHUNK == 0 ? 32 : S::BN;
+        float sum[BNC];
+#pragma unroll
+        for (int i = 0; i < BNC; ++i) sum[i] = 0.0f;
+        const int nch = S::chunks(P::k_blocks(prm, tile));
+        for (int ch = 0; ch < nch; ++ch, ++lc) {
+          const int acc = lc & 1;
+          const uint32_t aph = static_cast<uint32_t>(lc >> 1) & 1u;
+          ok = wait_bounded(tfull + acc, aph, abort_flag, prm.err, kErrTimeoutEpilogue);
+          if (!__all_sync(0xffffffffu, ok)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tbase =
+              tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * S::BN);
+#pragma unroll
+          for (int c0 = 0; c0 < BNC; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld32(tbase + static_cast<uint32_t>(c0), r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) sum[c0 + e] = __fadd_rn(sum[c0 + e], __uint_as_float(r[e]));
+          }
+          tc_fence_before();
+          mbar_arrive(tempty + acc);
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int c0 = 0; c0 < BNC; c0 += 32) {
+          uint32_t r[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(sum[c0 + e]);
+          P::epilogue(prm, tile, row, c0, r);
+        }
       }
-      tc_fence_before();
-      mbar_arrive(tempty + acc);
     }
   }
 

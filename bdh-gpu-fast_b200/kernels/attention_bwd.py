@@ -117,7 +117,12 @@ class RopeTrilSelfAttnFn(torch.autograd.Function):
         from .sm100_attn import rope_rotate, tril_score_v
 
         with torch.no_grad():
-            QR = rope_rotate(Q, freqs, pos0, out=qr_out)
+            if qr_out is not None and qr_out.dtype != Q.dtype:
+                # a cache slot in another storage dtype: attend in Q's dtype, store the cast
+                QR = rope_rotate(Q, freqs, pos0)
+                qr_out.copy_(QR)
+            else:
+                QR = rope_rotate(Q, freqs, pos0, out=qr_out)
             out = tril_score_v(QR, QR, V)
         ctx.pos0 = int(pos0)
         ctx.save_for_backward(QR, V, freqs)

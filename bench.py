@@ -1,0 +1,522 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 BDH tril-attention path (one JSON line on rank 0).
+
+Default workload: full BDH prefill forward under bf16 autocast with
+``BDH_ATTN_IMPL=cuda_sm100`` — n_layer=6, n_embd=256, n_head=4, N=8192/head, vocab 256,
+random N(0, 0.02) weights, synthetic token ids uniform in [0, 256), B=32 x T=512 per GPU
+(weak scaling: every rank runs its own batch; no collective on the data path).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--config 1|2|3|4|5]
+
+* ``value``      tokens/s over all ranks, inputs resident in HBM (device-timed, max over ranks)
+* ``e2e``        the same through the public model API with host buffers: pinned token ids
+                 copied in and logits copied out inside every timed step
+* ``roofline``   the dominant kernel of this path (the tcgen05 score pass), timed live inside
+                 the timed region with CUDA events recorded by the library around each launch
+* ``cpu_baseline`` the reference's own CPU extension (``csrc/tril_attn_cpu.cpp``, built into
+                 oracle/_ref) inside the same model on the host cores, on a bounded sample
+* ``--impl reference`` runs only that CPU reference arm (rank 0) on this config's metric.
+
+Other ``--config`` values run the standalone-op workloads (1: fp32 op, 3: long-T bf16 op,
+4: cached decode, 5: forward+backward) with the same JSON schema; they are measurement aids,
+the driver's headline is config 2.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "bdh-gpu-fast_b200"))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+N_LAT, D_MODEL, N_HEAD, N_LAYER, VOCAB = 8192, 256, 4, 6, 256
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clock / throttle reasons during the timed region."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.uuid = None
+        try:
+            self.uuid = str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:  # noqa: BLE001
+            pass
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            if self.uuid and self.uuid.replace("GPU-", "") not in parts[0]:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ native timing
+def _prof_lib():
+    import ctypes
+
+    from kernels import sm100_attn
+
+    lib = sm100_attn.load_library()
+    lib.bdh_profile_begin.restype = ctypes.c_int
+    lib.bdh_profile_end.restype = ctypes.c_int
+    return lib
+
+
+def profile_begin():
+    _prof_lib().bdh_profile_begin()
+
+
+def profile_end():
+    import ctypes
+
+    lib = _prof_lib()
+    ms = (ctypes.c_double * 8)()
+    cnt = (ctypes.c_int * 8)()
+    rc = lib.bdh_profile_end(ms, cnt)
+    if rc != 0:
+        raise RuntimeError(lib.bdh_last_error().decode())
+    kinds = ["score", "value", "rope", "decode", "grad_q", "grad_v", "split", "other"]
+    return {k: {"ms": ms[i], "launches": cnt[i]} for i, k in enumerate(kinds)}
+
+
+# ---------------------------------------------------------------------- helpers
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    return world, rank, dev
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed(fn, steps: int, world: int, dev) -> float:
+    """Device time (ms) of `steps` calls, bracketed by barrier + synchronize; max over ranks."""
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    return max_over_ranks(s.elapsed_time(e), world, dev)
+
+
+def load_traffic(name: str):
+    p = REPO / "profiles" / f"{name}.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("traffic_bytes_per_launch")
+        except Exception:  # noqa: BLE001
+            return None
+    return None
+
+
+# ------------------------------------------------------------------ CPU reference
+def cpu_reference_model(B_cpu: int, T: int, steps: int):
+    """BDH prefill on the host: the reference CPU extension computes the attention inside the
+    model (everything else is PyTorch CPU ops in fp32). Returns (tokens/s, kind, cores, sample)."""
+    import bdh_model
+    from kernels import attention_dispatch as ad
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    kind = "reference"
+    try:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import build_ref
+
+        ext = build_ref.load_module()
+        attn = lambda q, k, v: ext.tril_score_v_cpu(q, k, v)  # noqa: E731
+    except Exception:  # noqa: BLE001 - reference not built here: time the numpy port instead
+        import numpy as np
+
+        import tril_oracle
+
+        kind = "port"
+        attn = lambda q, k, v: torch.from_numpy(  # noqa: E731
+            tril_oracle.tril_score_v(q.numpy(), k.numpy(), v.numpy(), acc=np.float32))
+    cfg = bdh_model.BDHConfig(n_layer=N_LAYER, n_embd=D_MODEL, n_head=N_HEAD,
+                              mlp_internal_dim_multiplier=128, vocab_size=VOCAB, dropout=0.0)
+    torch.manual_seed(1002)
+    model = bdh_model.BDH(cfg).eval()
+    model.attn._attn_impl_override = "eager"
+    g = torch.Generator().manual_seed(2002)
+    idx = torch.randint(0, VOCAB, (B_cpu, T), generator=g)
+    orig = ad.eager_tril_attn
+    ad.eager_tril_attn = attn
+    try:
+        with torch.inference_mode():
+            model(idx)  # warm-up
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                model(idx)
+            dt = time.perf_counter() - t0
+    finally:
+        ad.eager_tril_attn = orig
+    cpu = ""
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                cpu = ln.split(":", 1)[1].strip()
+                break
+    except Exception:  # noqa: BLE001
+        pass
+    sample = (f"BDH prefill B={B_cpu} x T={T}, {N_LAYER} layers, fp32, {steps} timed forward(s) "
+              f"after 1 warm-up; attention by the reference CPU extension; {cores} threads; {cpu}")
+    return B_cpu * T * steps / dt, kind, cores, sample
+
+
+# --------------------------------------------------------------------- config 2
+def bench_config2(args, world, rank, dev):
+    import bdh_model
+    from kernels import sm100_attn
+
+    B, T = 32, 512
+    cfg = bdh_model.BDHConfig(n_layer=N_LAYER, n_embd=D_MODEL, n_head=N_HEAD,
+                              mlp_internal_dim_multiplier=128, vocab_size=VOCAB, dropout=0.0)
+    torch.manual_seed(1002)  # identical weights on every rank
+    model = bdh_model.BDH(cfg).to(dev).eval()
+    model.attn._attn_impl_override = "cuda_sm100"
+    g = torch.Generator().manual_seed(2002 + 7919 * rank)
+    idx_host = torch.randint(0, VOCAB, (B, T), generator=g).pin_memory()
+    idx = idx_host.to(dev)
+
+    def step():
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+            return model(idx)[0]
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    assert sm100_attn.device_error(dev) == 0
+    clocks = ClockSampler(dev)
+    clocks.start()
+    profile_begin()
+    ms = timed(step, args.steps, world, dev)
+    prof = profile_end()
+    clk = clocks.stop()
+    value = world * B * T * args.steps / (ms / 1e3)
+
+    # end to end through the public API with host buffers
+    idx_dev = torch.empty_like(idx)
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        out_shape = model(idx)[0].shape
+    logits_host = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        idx_dev.copy_(idx_host, non_blocking=True)
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+            logits = model(idx_dev)[0]
+        logits_host.copy_(logits, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    ms_e2e = timed(e2e_step, args.steps, world, dev)
+    torch.cuda.synchronize(dev)
+    e2e = world * B * T * args.steps / (ms_e2e / 1e3)
+
+    # roofline of the score pass (dominant kernel of the path): algorithmic flops of the
+    # causal Q K^T per launch = B * H * T * (T - 1) * N  (T(T-1)/2 pairs x 2N flops)
+    peaks, src = load_peaks()
+    sc = prof["score"]
+    flops_launch = B * N_HEAD * T * (T - 1) * N_LAT
+    achieved = flops_launch / (sc["ms"] / sc["launches"] / 1e3) / 1e12 if sc["launches"] else None
+    peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    attn_ms = sum(prof[k]["ms"] for k in ("score", "value", "rope"))
+    attn_flops = N_LAYER * args.steps * B * N_HEAD * T * (T - 1) * (N_LAT + D_MODEL)
+    launches = sum(v["launches"] for v in prof.values())
+    line = {
+        "metric": "BDH prefill tokens/s (config 2: 6L, D=256, nh=4, N=8192, B=32, T=512)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "BDH prefill forward, bf16 autocast, random-init weights, "
+                               "token ids uniform [0,256)",
+                   "global_batch": B * world, "per_gpu_batch": B, "seq_len": T,
+                   "n_layer": N_LAYER, "n_head": N_HEAD, "n_latent_per_head": N_LAT, "n_embd": D_MODEL,
+                   "parallelism": f"batch-sharded x{world} (weak), no collective on the data path",
+                   "cache": "inputs larger than L2 (1 GB latent per layer per GPU); no flush"},
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": idx_host.numel() * 8,
+                "d2h_bytes_per_step": logits_host.numel() * 2},
+        "roofline": {"kernel": "score pass tril(QR QR^T,-1) (tc_gemm_kernel<ScoreProb<bf16>>)",
+                     "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": (achieved / peak) if achieved else None,
+                     "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
+                     "traffic": load_traffic("score_pass_config2"),
+                     "avg_launch_ms": sc["ms"] / sc["launches"] if sc["launches"] else None,
+                     "flops_per_launch": flops_launch},
+        "attn_tflops": attn_flops / (attn_ms / 1e3) / 1e12 if attn_ms else None,
+        "attn_share_of_step": attn_ms / ms if ms else None,
+        "kernel_ms": {k: v["ms"] / args.steps for k, v in prof.items() if v["launches"]},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, kind, cores, sample = cpu_reference_model(1, T, 1)
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
+    return line
+
+
+# ----------------------------------------------------------- standalone op configs
+def _op_inputs(cfg_id, dev, rank):
+    g = torch.Generator(device=dev).manual_seed(1000 + cfg_id + 7919 * rank)
+    if cfg_id == 1:
+        B, H, T, N, D, dt = 4, 4, 512, N_LAT, D_MODEL, torch.float32
+        q = torch.relu(torch.randn(B, H, T, N, device=dev, generator=g))
+        v = torch.randn(B, 1, T, D, device=dev, generator=g)
+    elif cfg_id == 3:
+        B, H, T, N, D, dt = 8, 4, 8192, N_LAT, D_MODEL, torch.bfloat16
+        q = torch.relu(torch.randn(B, H, T, N, device=dev, generator=g) - 1.645).to(dt)
+        v = torch.nn.functional.layer_norm(torch.randn(B, 1, T, D, device=dev, generator=g), (D,)).to(dt)
+    else:  # 5
+        B, H, T, N, D, dt = 16, 4, 2048, N_LAT, D_MODEL, torch.bfloat16
+        q = torch.relu(torch.randn(B, H, T, N, device=dev, generator=g)).to(dt)
+        v = torch.randn(B, 1, T, D, device=dev, generator=g).to(dt)
+    return q, v, (B, H, T, N, D, dt)
+
+
+def bench_op(args, world, rank, dev):
+    import bdh_model
+    from kernels.attention_dispatch import bdh_rope_attn
+
+    cfg_id = args.config
+    q, v, (B, H, T, N, D, dt) = _op_inputs(cfg_id, dev, rank)
+    freqs = bdh_model.get_freqs(N, 2 ** 16, torch.float32).to(dev)
+    if cfg_id == 5:
+        dO = torch.randn(B, H, T, D, device=dev).to(dt)
+        qg = q.clone().requires_grad_(True)
+        vg = v.clone().requires_grad_(True)
+
+        def step():
+            out, _ = bdh_rope_attn(qg, vg, freqs, 0, impl="cuda_sm100")
+            out.backward(dO)
+    else:
+        def step():
+            return bdh_rope_attn(q, v, freqs, 0, impl="cuda_sm100")[0]
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(dev)
+    clocks.start()
+    profile_begin()
+    ms = timed(step, args.steps, world, dev)
+    prof = profile_end()
+    clk = clocks.stop()
+    fwd = B * H * T * (T - 1) * (N + D)
+    bwd = B * H * T * (T - 1) * (3 * N + 2 * D) if cfg_id == 5 else 0
+    flops = (fwd + bwd) * args.steps * world
+    peaks, src = load_peaks()
+    sc = prof["score"]
+    per_launch = None
+    if sc["launches"]:
+        per_launch = sc["ms"] / sc["launches"]
+    line = {
+        "metric": f"tril-attn TFLOP/s (config {cfg_id}, causal flops)", "value": flops / (ms / 1e3) / 1e12,
+        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32" if dt == torch.float32 else "bf16", "data": "synthetic",
+        "config": {"workload": f"config {cfg_id} op", "B": B, "H": H, "T": T, "N": N, "D": D,
+                   "tokens_per_s": world * B * T * args.steps / (ms / 1e3),
+                   "cache": "inputs larger than L2"},
+        "kernel_ms": {k: v_["ms"] / args.steps for k, v_ in prof.items() if v_["launches"]},
+        "score_ms_per_launch": per_launch,
+        "gpu_launches": sum(v_["launches"] for v_ in prof.values()),
+        "clocks": clk, "peak_source": src,
+    }
+    return line
+
+
+# ------------------------------------------------------------------ config 4 decode
+def bench_decode(args, world, rank, dev):
+    import bdh_model
+    from bdh_cache import CacheManager
+
+    B, P = 64, 512
+    cfg = bdh_model.BDHConfig(n_layer=N_LAYER, n_embd=D_MODEL, n_head=N_HEAD,
+                              mlp_internal_dim_multiplier=128, vocab_size=VOCAB, dropout=0.0)
+    torch.manual_seed(1004)
+    model = bdh_model.BDH(cfg).to(dev).eval()
+    model.attn._attn_impl_override = "cuda_sm100"
+    steps_total = args.warmup + args.steps
+    g = torch.Generator().manual_seed(2004 + 7919 * rank)
+    toks = torch.randint(0, VOCAB, (B, P + steps_total), generator=g).to(dev)
+    storage = torch.bfloat16 if args.decode_bf16 else None
+    cache = CacheManager.from_config(cfg, B, P + steps_total, dev, storage_dtype=storage)
+    buf = torch.empty(B, VOCAB, dtype=torch.float32, device=dev)
+    with torch.inference_mode():
+        model(toks[:, :P], cache=cache)
+        pos = [P]
+
+        def step():
+            p = pos[0]
+            model(toks[:, p:p + 1], cache=cache, logits_out=buf)
+            pos[0] = p + 1
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        S0 = pos[0]
+        profile_begin()
+        ms = timed(step, args.steps, world, dev)
+        prof = profile_end()
+    esz = 2 if storage is not None else 4
+    S_mean = S0 + (args.steps - 1) / 2
+    bytes_step = N_LAYER * (B * N_HEAD * S_mean * N_LAT * esz + B * S_mean * D_MODEL * esz)
+    dec = prof["decode"]
+    peaks, src = load_peaks()
+    gbs = bytes_step * args.steps / (dec["ms"] / 1e3) / 1e9 if dec["ms"] else None
+    return {
+        "metric": "BDH decode tokens/s (config 4)", "value": world * B * args.steps / (ms / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 cache" if storage is not None else "f32",
+        "data": "synthetic", "config": {"workload": "config 4 decode", "B": B, "prompt": P,
+                                        "S_mean": S_mean},
+        "roofline": {"kernel": "decode", "bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"] if gbs else None},
+        "kernel_ms": {k: v_["ms"] / args.steps for k, v_ in prof.items() if v_["launches"]},
+        "gpu_launches": sum(v_["launches"] for v_ in prof.values()),
+    }
+
+
+# ------------------------------------------------------------------- reference arm
+def reference_arm(args, world, rank):
+    if rank != 0:
+        return None
+    T = 512
+    tok_s, kind, cores, sample = cpu_reference_model(1, T, max(1, args.steps))
+    line = {
+        "metric": "BDH prefill tokens/s (config 2: 6L, D=256, nh=4, N=8192, B=32, T=512)",
+        "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * T / tok_s, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "BDH prefill forward on the host CPU (bounded sample of config 2)",
+                   "seq_len": T},
+        "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample},
+        "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="sm100", choices=["sm100", "reference"])
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-bf16", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl != "reference":
+        args.warmup = 3
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        line = reference_arm(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    world, rank, dev = init_dist()
+    try:
+        if args.config == 2:
+            line = bench_config2(args, world, rank, dev)
+        elif args.config == 4:
+            line = bench_decode(args, world, rank, dev)
+        else:
+            line = bench_op(args, world, rank, dev)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -128,6 +128,17 @@ int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* 
                          int64_t T, int64_t N, int64_t D, const float* freqs, int64_t pos0,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Launch timing for benchmarks (no counterpart in the reference, which timed whole calls with
+ * perf_counter, benchmarks/bench_gpu_attn.py:263-280). Between begin and end, every kernel of
+ * this library is bracketed by CUDA events on its own stream; end synchronises them and
+ * returns the summed device milliseconds and launch counts per kernel kind:
+ *   0 score pass, 1 value pass, 2 RoPE, 3 decode, 4 grad-Q pass, 5 grad-V pass, 6 split/transpose.
+ */
+#define BDH_PROF_KINDS 8
+int bdh_profile_begin(void);
+int bdh_profile_end(double ms[BDH_PROF_KINDS], int launches[BDH_PROF_KINDS]);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,379 @@
+"""GPU parity of the sm_100a kernels (called through the C-ABI library via kernels.sm100_attn)
+against the reference's own outputs (tests/golden) and the pinned numpy oracle.
+
+Tolerances (relative Frobenius, from the task's north star): fp32 path <= 1e-5; bf16 inputs
+with fp32 accumulation <= 3e-3. RoPE is checked element-wise (it is bit-exact arithmetic up to
+the cos/sin implementations).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import tril_oracle as O
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+TOL = {torch.float32: 1e-5, torch.bfloat16: 3e-3}
+
+
+def sa():
+    from kernels import sm100_attn
+
+    return sm100_attn
+
+
+def rel(a, b):
+    return O.rel_fro(np.asarray(a, dtype=np.float64), np.asarray(b, dtype=np.float64))
+
+
+def t(x, dtype=torch.float32):
+    return torch.as_tensor(np.asarray(x)).to(device=DEV, dtype=dtype)
+
+
+def np64(x):
+    return x.detach().double().cpu().numpy()
+
+
+@pytest.fixture(autouse=True)
+def _device_error_clean():
+    yield
+    assert sa().device_error() == 0, "a kernel reported a pipeline timeout"
+
+
+# --------------------------------------------------------------------------- RoPE
+@pytest.mark.parametrize("pos0", [0, 37, 4000])
+def test_rope_fp32_golden(pos0):
+    g = golden("rope")
+    y = sa().rope_rotate(t(g["x"]), t(g["freqs_64"]), pos0)
+    np.testing.assert_allclose(y.cpu().numpy(), g[f"y_f32_pos{pos0}"], rtol=0, atol=2e-6)
+
+
+@pytest.mark.parametrize("pos0", [0, 37, 4000])
+def test_rope_bf16_golden(pos0):
+    g = golden("rope")
+    y = sa().rope_rotate(t(g["x"], torch.bfloat16), t(g["freqs_64"]), pos0).float().cpu().numpy()
+    ref = g[f"y_bf16_pos{pos0}"]
+    assert np.mean(y != ref) < 2e-3
+    np.testing.assert_allclose(y, ref, rtol=0, atol=2 ** -7 * np.abs(ref).max())
+
+
+def test_rope_permuted_view_into_strided_slot_of_other_dtype():
+    N = 256
+    f = torch.tensor(O.get_freqs(N), device=DEV)
+    x = torch.relu(torch.randn(2, 9, 3, N, device=DEV)).permute(0, 2, 1, 3)  # (B,H,T,N) view
+    buf = torch.zeros(2, 3, 20, N, device=DEV, dtype=torch.bfloat16)        # capacity 20
+    slot = buf.narrow(2, 5, 9)
+    sa().rope_rotate(x, f, 5, out=slot)
+    ref = O.rope(x.cpu().numpy(), O.get_freqs(N), 5)
+    np.testing.assert_allclose(slot.float().cpu().numpy(), O.bf16_round(ref), rtol=0, atol=2e-2)
+    assert torch.all(buf[:, :, :5] == 0) and torch.all(buf[:, :, 14:] == 0)
+
+
+def test_rope_bf16_bit_pattern_large_batch():
+    N, T = 8192, 64
+    f = O.get_freqs(N)
+    x = torch.relu(torch.randn(4, 4, T, N, device=DEV)).to(torch.bfloat16)
+    y = sa().rope_rotate(x, torch.tensor(f, device=DEV), 100).float().cpu().numpy()
+    ref = O.rope(x.float().cpu().numpy(), f, 100, bf16=True)
+    assert np.mean(y != ref) < 1e-3  # rare one-ulp cos/sin differences flip a bf16 rounding
+    assert rel(y, ref) < 1e-3
+
+
+# ------------------------------------------------------------------------ forward
+@pytest.mark.parametrize("name", ["shared_v", "per_head_v", "t1", "t2", "distinct_k", "bf16", "tiled"])
+def test_forward_golden(name):
+    g = golden("fwd")
+    dt = torch.bfloat16 if name == "bf16" else torch.float32
+    q = t(g[f"{name}_q"], dt)
+    k = t(g[f"{name}_k"], dt) if f"{name}_k" in g else q
+    v = t(g[f"{name}_v"], dt)
+    out = sa().tril_score_v(q, k, v)
+    assert out.dtype == dt and out.shape == (q.size(0), q.size(1), q.size(2), v.size(-1))
+    ext = g[f"{name}_out_ext"]
+    exact = O.tril_score_v(np64(q), np64(k), np64(v))
+    o = out.float().cpu().numpy()
+    assert np.all(o[:, :, 0] == 0)
+    if np.abs(exact).max() == 0:
+        assert np.all(o == 0)
+        return
+    assert rel(o, exact) <= TOL[dt]
+    assert rel(o, ext) <= TOL[dt] * (2 if dt == torch.bfloat16 else 1.5)
+
+
+def test_baseline_attention_with_fused_rope():
+    from kernels.attention_dispatch import bdh_rope_attn
+
+    g = golden("fwd")
+    out, qr = bdh_rope_attn(t(g["baseline_attn_q"]), t(g["baseline_attn_v"]),
+                            t(g["baseline_attn_freqs"]), 0, impl="cuda_sm100")
+    assert rel(out.cpu().numpy(), g["baseline_attn_out"]) < 1e-5
+
+
+SHAPES = [  # B, H, Hv, T, N, D
+    (1, 1, 1, 1, 16, 8),
+    (1, 2, 1, 2, 16, 8),
+    (2, 3, 1, 3, 64, 32),
+    (1, 2, 2, 17, 72, 40),
+    (1, 2, 1, 127, 64, 256),
+    (1, 1, 1, 128, 128, 256),
+    (2, 2, 1, 129, 200, 256),
+    (1, 4, 4, 300, 512, 300),
+    (1, 2, 1, 257, 8192, 256),
+]
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_forward_shapes_vs_oracle(shape, dt):
+    B, H, Hv, T, N, D = shape
+    gen = torch.Generator(device=DEV).manual_seed(hash(shape) % 1000)
+    q = torch.relu(torch.randn(B, H, T, N, device=DEV, generator=gen)).to(dt)
+    v = torch.randn(B, Hv, T, D, device=DEV, generator=gen).to(dt)
+    out = sa().tril_score_v(q, q, v)
+    ref = O.tril_score_v(np64(q), np64(q), np64(v))
+    assert rel(out.float().cpu().numpy(), ref) <= TOL[dt]
+    assert torch.all(out[:, :, 0] == 0)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_forward_distinct_k_and_permuted_views(dt):
+    B, H, T, N, D = 2, 3, 200, 256, 64
+    q = torch.relu(torch.randn(B, T, H, N, device=DEV)).to(dt).permute(0, 2, 1, 3)
+    k = torch.relu(torch.randn(B, T, H, N, device=DEV)).to(dt).permute(0, 2, 1, 3)
+    v = torch.randn(B, T, D, device=DEV).to(dt).unsqueeze(1)
+    out = sa().tril_score_v(q, k, v)
+    ref = O.tril_score_v(np64(q), np64(k), np64(v))
+    assert rel(out.float().cpu().numpy(), ref) <= TOL[dt]
+
+
+def test_forward_empty_and_zero_cases():
+    q = torch.zeros(2, 3, 0, 64, device=DEV)
+    v = torch.zeros(2, 1, 0, 32, device=DEV)
+    assert sa().tril_score_v(q, q, v).shape == (2, 3, 0, 32)
+    q = torch.randn(1, 2, 1, 64, device=DEV)
+    v = torch.randn(1, 1, 1, 32, device=DEV)
+    assert torch.all(sa().tril_score_v(q, q, v) == 0)
+
+
+def test_forward_linear_in_v_full_size_bf16():
+    """Config-1 shapes (B=4, nh=4, T=512, N=8192, D=256): linearity in V and row 0 == 0,
+    plus agreement with a float64 torch reference on the device."""
+    B, H, T, N, D = 4, 4, 512, 8192, 256
+    q = torch.relu(torch.randn(B, H, T, N, device=DEV)).to(torch.bfloat16)
+    v1 = torch.randn(B, 1, T, D, device=DEV).to(torch.bfloat16)
+    v2 = torch.randn(B, 1, T, D, device=DEV).to(torch.bfloat16)
+    o1 = sa().tril_score_v(q, q, v1).double()
+    o2 = sa().tril_score_v(q, q, v2).double()
+    o12 = sa().tril_score_v(q, q, (v1.float() + v2.float()).to(torch.bfloat16)).double()
+    assert ((o12 - o1 - o2).norm() / o12.norm()).item() < 6e-3  # v1+v2 rounded to bf16
+    assert torch.all(o1[:, :, 0] == 0)
+    qd = q.double()
+    ref = ((qd @ qd.mT).tril(-1)) @ v1.double()
+    assert ((o1 - ref).norm() / ref.norm()).item() <= 3e-3
+
+
+def test_forward_full_size_fp32_config1():
+    B, H, T, N, D = 4, 4, 512, 8192, 256
+    q = torch.relu(torch.randn(B, H, T, N, device=DEV))
+    v = torch.randn(B, 1, T, D, device=DEV)
+    out = sa().tril_score_v(q, q, v).double()
+    qd = q.double()
+    ref = ((qd @ qd.mT).tril(-1)) @ v.double()
+    assert ((out - ref).norm() / ref.norm()).item() <= 1e-5
+
+
+# ------------------------------------------------------------------------- decode
+@pytest.mark.parametrize("S", [0, 1, 25])
+def test_decode_golden_capacity_views(S):
+    g = golden("decode")
+    kbuf, vbuf = t(g["kbuf"]), t(g["vbuf"])
+    out = sa().tril_decode(t(g["q"]), kbuf.narrow(2, 0, S), vbuf.narrow(2, 0, S))
+    ref = g[f"out_ext_S{S}"]
+    if S == 0:
+        assert torch.all(out == 0) and out.shape == ref.shape
+    else:
+        assert rel(out.cpu().numpy(), ref) < 1e-6
+
+
+def test_decode_multi_query_rows():
+    g = golden("decode")
+    out = sa().tril_decode(t(g["q_tq3"]), t(g["kbuf"])[:1].narrow(2, 0, 25), t(g["vbuf"])[:1].narrow(2, 0, 25))
+    assert rel(out.cpu().numpy(), g["out_ext_tq3"]) < 1e-6
+
+
+@pytest.mark.parametrize("qdt,kvdt", [(torch.float32, torch.float32), (torch.float32, torch.bfloat16),
+                                      (torch.bfloat16, torch.bfloat16), (torch.bfloat16, torch.float32)])
+def test_decode_storage_dtypes(qdt, kvdt):
+    B, H, S, cap, N, D = 3, 4, 700, 1024, 8192, 256
+    kbuf = torch.randn(B, H, cap, N, device=DEV).to(kvdt)
+    vbuf = torch.randn(B, 1, cap, D, device=DEV).to(kvdt)
+    q = torch.randn(B, H, 1, N, device=DEV).to(qdt)
+    kp, vp = kbuf.narrow(2, 0, S), vbuf.narrow(2, 0, S)
+    out = sa().tril_decode(q, kp, vp)
+    assert out.dtype == qdt
+    ref = (q.double() @ kp.double().mT) @ vp.double()
+    assert ((out.double() - ref).norm() / ref.norm()).item() <= TOL[qdt] * (1 if qdt == torch.float32 else 1)
+
+
+def test_decode_equals_last_row_of_forward():
+    B, H, T, N, D = 2, 4, 300, 1024, 256
+    q = torch.relu(torch.randn(B, H, T, N, device=DEV))
+    v = torch.randn(B, 1, T, D, device=DEV)
+    full = sa().tril_score_v(q, q, v)
+    last = sa().tril_decode(q[:, :, -1:], q[:, :, :-1], v[:, :, :-1])
+    assert ((last - full[:, :, -1:]).norm() / full[:, :, -1:].norm()).item() < 1e-5
+
+
+@pytest.mark.parametrize("kvdt", [torch.float32, torch.bfloat16])
+def test_decode_fused_rope_writes_slot(kvdt):
+    B, H, S, cap, N, D = 2, 4, 33, 40, 512, 64
+    f = O.get_freqs(N)
+    kbuf = torch.randn(B, H, cap, N, device=DEV).to(kvdt)
+    vbuf = torch.randn(B, 1, cap, D, device=DEV).to(kvdt)
+    q = torch.relu(torch.randn(B, H, 1, N, device=DEV))
+    slot = kbuf.narrow(2, S, 1)
+    out = sa().tril_decode(q, kbuf.narrow(2, 0, S), vbuf.narrow(2, 0, S),
+                           freqs=torch.tensor(f, device=DEV), pos=S, kr_slot=slot)
+    qr = O.rope(q.cpu().numpy(), f, S)
+    np.testing.assert_allclose(slot.float().cpu().numpy(), qr if kvdt == torch.float32 else O.bf16_round(qr),
+                               rtol=0, atol=2e-6 if kvdt == torch.float32 else 3e-2)
+    ref = O.tril_decode(qr, np64(kbuf[:, :, :S]), np64(vbuf[:, :, :S]))
+    assert rel(out.cpu().numpy(), ref) < 1e-5
+
+
+# ----------------------------------------------------------------------- backward
+def test_backward_golden_fp32():
+    g = golden("bwd")
+    q, k, v, do = (t(g[n]) for n in ("Q", "K", "V", "dO"))
+    dq, dk, dv = sa().tril_score_v_bwd(q, k, v, do)
+    assert rel(dq.cpu().numpy(), g["dQ"]) < 1e-5
+    assert rel(dk.cpu().numpy(), g["dK"]) < 1e-5
+    assert rel(dv.cpu().numpy(), g["dV"]) < 1e-5
+    dqt, none, dvs = sa().tril_score_v_bwd(q, q, v, do)
+    assert none is None
+    assert rel(dqt.cpu().numpy(), g["self_dQ"]) < 1e-5
+    assert rel(dvs.cpu().numpy(), g["self_dV"]) < 1e-5
+
+
+BWD_SHAPES = [  # B, H, Hv, T, N, D
+    (1, 2, 1, 5, 16, 8),
+    (1, 2, 2, 130, 64, 32),
+    (2, 3, 1, 257, 256, 256),
+    (1, 4, 1, 512, 1024, 256),
+]
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", BWD_SHAPES)
+@pytest.mark.parametrize("self_form", [True, False])
+def test_backward_vs_oracle(shape, dt, self_form):
+    B, H, Hv, T, N, D = shape
+    q = torch.relu(torch.randn(B, H, T, N, device=DEV)).to(dt)
+    k = q if self_form else torch.relu(torch.randn(B, H, T, N, device=DEV)).to(dt)
+    v = torch.randn(B, Hv, T, D, device=DEV).to(dt)
+    do = torch.randn(B, H, T, D, device=DEV).to(dt)
+    dq, dk, dv = sa().tril_score_v_bwd(q, k, v, do)
+    rq, rk, rv = O.tril_backward(np64(q), np64(k), np64(v), np64(do), k_is_q=self_form)
+    assert rel(dq.float().cpu().numpy(), rq) <= TOL[dt]
+    assert rel(dv.float().cpu().numpy(), rv) <= TOL[dt]
+    if not self_form:
+        assert rel(dk.float().cpu().numpy(), rk) <= TOL[dt]
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_backward_fused_rope_adjoint(dt):
+    B, H, T, N, D, pos0 = 1, 2, 200, 512, 64, 7
+    f = O.get_freqs(N)
+    x = torch.relu(torch.randn(B, H, T, N, device=DEV)).to(dt)
+    qr = sa().rope_rotate(x, torch.tensor(f, device=DEV), pos0)
+    v = torch.randn(B, 1, T, D, device=DEV).to(dt)
+    do = torch.randn(B, H, T, D, device=DEV).to(dt)
+    dx, _, dv = sa().tril_score_v_bwd(qr, qr, v, do, freqs=torch.tensor(f, device=DEV), pos0=pos0)
+    gq, _, gv = O.tril_backward(np64(qr), np64(qr), np64(v), np64(do), k_is_q=True)
+    ref = O.rope_backward(gq, f, pos0)
+    assert rel(dx.float().cpu().numpy(), ref) <= TOL[dt]
+    assert rel(dv.float().cpu().numpy(), gv) <= TOL[dt]
+
+
+def test_autograd_functions_native_match_eager(monkeypatch):
+    import kernels
+
+    monkeypatch.setenv("BDH_ATTN_AUTOGRAD", "1")
+    B, H, T, N, D = 2, 4, 150, 256, 64
+    q0 = torch.relu(torch.randn(B, H, T, N, device=DEV))
+    v0 = torch.randn(B, 1, T, D, device=DEV)
+    g = torch.randn(B, H, T, D, device=DEV)
+    grads = {}
+    for impl in ("eager", "cuda_sm100"):
+        q = q0.clone().requires_grad_(True)
+        v = v0.clone().requires_grad_(True)
+        out = kernels.bdh_attn(q, q, v, impl=impl)
+        out.backward(g)
+        grads[impl] = (out.detach(), q.grad, v.grad)
+    for a, b in zip(grads["eager"], grads["cuda_sm100"]):
+        assert ((a.double() - b.double()).norm() / a.double().norm()).item() < 1e-5
+
+
+def test_rope_attn_autograd_matches_eager():
+    from kernels.attention_dispatch import bdh_rope_attn
+
+    B, H, T, N, D = 1, 2, 96, 128, 32
+    f = torch.tensor(O.get_freqs(N), device=DEV)
+    x0 = torch.relu(torch.randn(B, H, T, N, device=DEV))
+    v0 = torch.randn(B, 1, T, D, device=DEV)
+    g = torch.randn(B, H, T, D, device=DEV)
+    res = {}
+    for impl in ("eager", "cuda_sm100"):
+        x = x0.clone().requires_grad_(True)
+        v = v0.clone().requires_grad_(True)
+        out, _ = bdh_rope_attn(x, v, f, 3, impl=impl, use_autograd_fn=False)
+        out.backward(g)
+        res[impl] = (out.detach(), x.grad, v.grad)
+    for a, b in zip(res["eager"], res["cuda_sm100"]):
+        assert ((a.double() - b.double()).norm() / a.double().norm()).item() < 1e-5
+
+
+# -------------------------------------------------------------------------- model
+def _golden_model(impl, monkeypatch):
+    import bdh_model
+
+    monkeypatch.setenv("BDH_ATTN_IMPL", impl)
+    g = golden("model")
+    cfg = bdh_model.BDHConfig(n_layer=2, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4,
+                              dropout=0.0, vocab_size=256)
+    m = bdh_model.BDH(cfg)
+    sd = {k[2:]: torch.tensor(g[k]) for k in g.files if k.startswith("w_")}
+    m.load_state_dict(sd)
+    return m.to(DEV).eval(), g
+
+
+@pytest.mark.parametrize("impl", ["eager", "cuda_sm100"])
+def test_model_logits_match_reference(impl, monkeypatch):
+    m, g = _golden_model(impl, monkeypatch)
+    idx = torch.tensor(g["idx"], device=DEV)
+    with torch.no_grad():
+        logits, _ = m(idx)
+    assert rel(logits.cpu().numpy(), g["logits_baseline"]) < 1e-5
+
+
+@pytest.mark.parametrize("impl", ["eager", "cuda_sm100"])
+@pytest.mark.parametrize("storage", [None, torch.bfloat16])
+def test_model_cached_decode_matches_reference(impl, storage, monkeypatch):
+    from bdh_cache import CacheManager
+
+    m, g = _golden_model(impl, monkeypatch)
+    idx = torch.tensor(g["idx"], device=DEV)
+    cache = CacheManager.from_config(m.config, batch_size=2, max_seq=24, device=DEV, storage_dtype=storage)
+    ref = g["logits_cached_steps"]
+    with torch.inference_mode():
+        lg, _ = m(idx[:, :16], cache=cache)
+        steps = [lg[:, -1].float().cpu().numpy()]
+        for s in range(16, 24):
+            lg, _ = m(idx[:, s:s + 1], cache=cache)
+            steps.append(lg[:, -1].float().cpu().numpy())
+    tol = 1e-5 if storage is None else 3e-3
+    for a, b in zip(steps, ref):
+        assert rel(a, b) < tol
