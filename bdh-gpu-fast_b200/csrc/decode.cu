@@ -12,6 +12,8 @@
 //   3. the CTA forms its partial out = sum_j s_j V_j (one thread per output column);
 //   4. a second small kernel sums the per-split partials in a fixed order (deterministic).
 #include <algorithm>
+#include <mutex>
+#include <sstream>
 #include <string>
 
 #include "common.cuh"
@@ -284,3 +286,77 @@ int launch_decode(const DecodeArgs& a, float* partial, cudaStream_t stream) {
 }
 
 }  // namespace bdh
+
+// ------------------------------------------------------------- allocation-free decode
+// Some callers cannot obtain device memory when they call in. Examples: a serving process that
+// reserves its whole device-memory budget up front and forbids allocations afterwards; a
+// foreign-language host binding that has no device allocator to hand; a latency-critical loop
+// where an allocation's possible implicit device synchronisation is not acceptable. For them
+// bdh_tril_decode_noalloc runs the same decode with its per-split partial sums placed in one
+// fixed array compiled into this library, instead of a caller-provided workspace.
+namespace bdh {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB, held by every device that loads the library
+
+static __device__ __align__(256) float g_decode_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+// Device address of the array on the current device. In host code the array's name only
+// stands for it; the real address must be looked up once per device, with that device current.
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {nullptr};
+
+float* noalloc_scratch(int* rc) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("tril_decode_noalloc: no usable current CUDA device");
+    *rc = BDH_ERR_CUDA;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error(std::string("tril_decode_noalloc: cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+      *rc = BDH_ERR_CUDA;
+      return nullptr;
+    }
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *rc = BDH_OK;
+  return g_noalloc_ptr[dev];
+}
+
+}  // namespace
+}  // namespace bdh
+
+extern "C" int bdh_tril_decode_noalloc(const void* q, const int64_t q_strides[4], int q_dtype,
+                                       const void* k_past, const int64_t k_strides[4],
+                                       const void* v_past, const int64_t v_strides[4],
+                                       int kv_dtype, void* out, const int64_t out_strides[4],
+                                       int64_t B, int64_t H, int64_t Hv, int64_t Tq, int64_t S,
+                                       int64_t N, int64_t D, const float* freqs, int64_t pos,
+                                       void* kr_slot, const int64_t slot_strides[4],
+                                       void* stream) {
+  if (B < 0 || H < 0 || Tq < 0 || S < 0 || D < 0) {
+    bdh::set_error("tril_decode_noalloc: negative size");
+    return BDH_ERR_INVALID;
+  }
+  const size_t need = bdh::decode_workspace_bytes(B, H, Tq, S, D);
+  if (need > bdh::kNoAllocScratchBytes) {
+    std::ostringstream os;
+    os << "tril_decode_noalloc: this problem needs " << need << " bytes of scratch "
+       << "(ceil(S/64) * B * H * Tq * D * 4) but the built-in array holds "
+       << bdh::kNoAllocScratchBytes << " bytes; use bdh_tril_decode with a workspace";
+    bdh::set_error(os.str());
+    return BDH_ERR_INVALID;
+  }
+  int rc = BDH_OK;
+  float* scratch = bdh::noalloc_scratch(&rc);
+  if (scratch == nullptr) return rc;
+  return bdh_tril_decode(q, q_strides, q_dtype, k_past, k_strides, v_past, v_strides, kv_dtype, out,
+                         out_strides, B, H, Hv, Tq, S, N, D, freqs, pos, kr_slot, slot_strides,
+                         scratch, bdh::kNoAllocScratchBytes, stream);
+}
+

@@ -104,6 +104,29 @@ int bdh_tril_decode(const void* q, const int64_t q_strides[4], int q_dtype, cons
                     int64_t pos, void* kr_slot, const int64_t slot_strides[4], void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/*
+ * Decode without any device allocation: the same computation as bdh_tril_decode, for callers
+ * that cannot provide a workspace (a process with a fixed device-memory budget reserved up
+ * front, a host binding without a device allocator, a loop that must not risk the implicit
+ * synchronisation of an allocation). The per-split partial sums live in one 8 MiB array
+ * compiled into the library, which every device that loads the library keeps until exit.
+ * Limit: ceil(S / 64) * B * H * Tq * D * 4 bytes must not exceed 8 MiB (e.g. B*H = 256,
+ * Tq = 1, D = 256 allows S <= 2048); larger problems return BDH_ERR_INVALID with a message.
+ * The first call on each device looks the array's device address up (cudaGetSymbolAddress)
+ * with that device current: make that first call before any stream capture begins.
+ * All calls on a device share the array and it keeps the last call's contents; every
+ * element a call reads is written by the same call first, so nothing needs clearing, but
+ * calls whose work overlaps on the GPU (different streams, no ordering) race on it.
+ * No counterpart in the reference: it has no allocation-free entry point.
+ */
+int bdh_tril_decode_noalloc(const void* q, const int64_t q_strides[4], int q_dtype,
+                            const void* k_past, const int64_t k_strides[4], const void* v_past,
+                            const int64_t v_strides[4], int kv_dtype, void* out,
+                            const int64_t out_strides[4], int64_t B, int64_t H, int64_t Hv,
+                            int64_t Tq, int64_t S, int64_t N, int64_t D, const float* freqs,
+                            int64_t pos, void* kr_slot, const int64_t slot_strides[4],
+                            void* stream);
+
 /* Scratch bytes bdh_tril_score_v_bwd needs. */
 size_t bdh_tril_score_v_bwd_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,
                                            int64_t N, int64_t D, int k_is_q);
