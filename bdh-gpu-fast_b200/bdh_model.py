@@ -86,18 +86,22 @@ class Attention(nn.Module):
         return rope_tables(self.freqs, T, rope_start, device)
 
     def forward(self, Q, K, V, rope_start: int = 0, past_kr=None, past_v=None, out_kr=None,
-                past_is_raw: bool = False):
+                past_is_raw: bool = False, relu_input: bool = False):
         """Returns ``(out, QR, V)``; QR/V are this block's keys/values for the cache.
 
         ``past_kr``/``past_v``: packed past (``past_is_raw``: in the cache storage dtype).
-        ``out_kr``: optional cache slot receiving QR.
+        ``out_kr``: optional cache slot receiving QR. ``relu_input``: Q is the encoder
+        pre-activation; the latent is ``relu(Q)`` (folded into the RoPE read when possible).
         """
         assert K is Q
         impl = self._attn_impl_override or resolve_attn_impl()
         B, nh, T, _ = Q.shape
         if past_kr is None:
-            out, QR = bdh_rope_attn(Q, V, self.freqs, rope_start, impl=impl, qr_out=out_kr)
+            out, QR = bdh_rope_attn(Q, V, self.freqs, rope_start, impl=impl, qr_out=out_kr,
+                                    relu_input=relu_input)
             return out, QR, V
+        if relu_input:
+            Q = F.relu(Q)
         S = past_kr.size(2)
         if impl == "cuda_sm100" and T == 1:
             if out_kr is not None:
@@ -163,8 +167,12 @@ class BDH(nn.Module):
         rope_start = cache.seq_len if cache is not None else 0
         impl = self.attn._attn_impl_override or resolve_attn_impl()
         grad = torch.is_grad_enabled()
+        # Inference on B200: both ReLUs are folded into native kernels (the RoPE read and the
+        # gated product), so the latents are never rewritten just to clamp them.
+        fused = impl == "cuda_sm100" and not grad and (not self.training or self.drop.p == 0.0)
         for level in range(C.n_layer):
-            x_bthn = F.relu(torch.einsum("btd,hdn->bthn", x, self.encoder))
+            x_lat = torch.einsum("btd,hdn->bthn", x, self.encoder)  # (B, T, nh, N)
+            x_bthn = x_lat if fused else F.relu(x_lat)
             x_sparse = x_bthn.permute(0, 2, 1, 3)  # (B, nh, T, N) view
             v_tok = x.unsqueeze(1)
             past_kr = past_v = out_kr = None
@@ -187,12 +195,17 @@ class BDH(nn.Module):
                     past_kr, past_v = cache.get_past(level)
             y_kv, new_kr, new_v = self.attn(x_sparse, x_sparse, v_tok, rope_start=rope_start,
                                             past_kr=past_kr, past_v=past_v, out_kr=out_kr,
-                                            past_is_raw=raw)
+                                            past_is_raw=raw, relu_input=fused)
             if cache is not None and out_kr is None:
                 cache.append(level, new_kr, new_v)
             y_kv = self._ln(y_kv)
-            y_bthn = F.relu(torch.einsum("bhtd,hdn->bthn", y_kv, self.encoder_v))
-            xy = self.drop(x_bthn * y_bthn)
+            y_lat = torch.einsum("bhtd,hdn->bthn", y_kv, self.encoder_v)
+            if fused:
+                from kernels.sm100_attn import relu_mul
+
+                xy = relu_mul(x_lat, y_lat)
+            else:
+                xy = self.drop(x_bthn * F.relu(y_lat))
             y_mlp = F.linear(xy.reshape(B, T, nh * N), self.decoder.t())
             x = self._ln(x + self._ln(y_mlp))
         if cache is not None:

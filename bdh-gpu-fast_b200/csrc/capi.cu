@@ -150,7 +150,7 @@ int bdh_device_error(int device, int* code, int reset) {
 
 int bdh_rope_rotate(const void* x, int x_dtype, const int64_t x_strides[4], void* y, int y_dtype,
                     const int64_t y_strides[4], void* y_lo, const float* freqs, int64_t B,
-                    int64_t H, int64_t T, int64_t N, int64_t pos0, void* stream) {
+                    int64_t H, int64_t T, int64_t N, int64_t pos0, int flags, void* stream) {
   if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(BDH_ERR_INVALID, "rope: dtype must be f32 or bf16");
   if (B < 0 || H < 0 || T < 0 || N < 0) return fail(BDH_ERR_INVALID, "rope: negative size");
   if (N % 2 != 0) return fail(BDH_ERR_INVALID, "rope: RoPE last dim must be even");
@@ -158,8 +158,21 @@ int bdh_rope_rotate(const void* x, int x_dtype, const int64_t x_strides[4], void
   if (y_lo != nullptr && y_dtype != BDH_DTYPE_F32) return fail(BDH_ERR_INVALID, "rope: y_lo requires f32 output");
   if (B * H * T * N > 0 && (x == nullptr || y == nullptr || freqs == nullptr))
     return fail(BDH_ERR_INVALID, "rope: null pointer");
+  if ((flags & ~BDH_ROPE_RELU_INPUT) != 0) return fail(BDH_ERR_INVALID, "rope: unknown flags");
   return launch_rope(x, x_dtype, x_strides, y, y_dtype, y_strides, static_cast<float*>(y_lo), freqs,
-                     B, H, T, N, pos0, static_cast<cudaStream_t>(stream));
+                     B, H, T, N, pos0, (flags & BDH_ROPE_RELU_INPUT) ? 1 : 0,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int bdh_relu_mul(const void* x, const int64_t x_strides[4], const void* y,
+                 const int64_t y_strides[4], void* out, const int64_t out_strides[4], int dtype,
+                 int64_t B, int64_t H, int64_t T, int64_t N, void* stream) {
+  if (!dtype_ok(dtype)) return fail(BDH_ERR_INVALID, "relu_mul: dtype must be f32 or bf16");
+  if (B < 0 || H < 0 || T < 0 || N < 0) return fail(BDH_ERR_INVALID, "relu_mul: negative size");
+  if (x_strides[3] != 1 || y_strides[3] != 1 || out_strides[3] != 1)
+    return fail(BDH_ERR_INVALID, "relu_mul: last dimension must be contiguous");
+  return launch_relu_mul(x, x_strides, y, y_strides, out, out_strides, dtype, B, H, T, N,
+                         static_cast<cudaStream_t>(stream));
 }
 
 size_t bdh_tril_score_v_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,

@@ -220,9 +220,18 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) {
   return __uint_as_float(bits16 << 16);
 }
 
-// Round-to-nearest-even bf16 of x, returned as the 16 raw bits.
+// Round-to-nearest-even bf16 of x, returned as the 16 raw bits. Integer arithmetic on the ALU
+// pipes (the F2F conversion instruction issues on the 16-lane/clk XU pipe, which became the
+// bottleneck of the RoPE pass); NaN inputs stay (quiet) NaN.
 __device__ __forceinline__ uint32_t f32_to_bf16_bits(float x) {
-  return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(x)));
+  const uint32_t u = __float_as_uint(x);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (u >> 16) | 0x40u;
+  return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
+}
+
+// x rounded to the nearest bf16 value (ties to even), kept as fp32.
+__device__ __forceinline__ float bf16_round_f32(float x) {
+  return __uint_as_float(f32_to_bf16_bits(x) << 16);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

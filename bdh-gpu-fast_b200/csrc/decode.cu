@@ -28,9 +28,7 @@ constexpr int kDecThreads = 256;
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kDecRows = 64;  // cached rows per CTA
 
-__device__ __forceinline__ float bf16_round_d(float x) {
-  return __bfloat162float(__float2bfloat16_rn(x));
-}
+__device__ __forceinline__ float bf16_round_d(float x) { return bf16_round_f32(x); }
 
 __device__ __forceinline__ void rope_cis_d(float pos, float f, float& c, float& s) {
   float ph = __fmul_rn(pos, f);

@@ -21,9 +21,7 @@ namespace {
 // fp32 2*pi exactly as torch rounds the Python scalar (0x40C90FDB).
 __device__ __forceinline__ float two_pi_f32() { return __int_as_float(0x40C90FDB); }
 
-__device__ __forceinline__ float bf16_round(float x) {
-  return __bfloat162float(__float2bfloat16_rn(x));
-}
+__device__ __forceinline__ float bf16_round(float x) { return bf16_round_f32(x); }
 
 __device__ __forceinline__ float tf32_round(float x) {
   uint32_t r;
@@ -89,6 +87,48 @@ __device__ __forceinline__ void store1(float* p, float v) { *p = v; }
 // Grid: x = (position t, 2048-element chunk of N), y = group of (b, h) rows. The (cos, sin)
 // of a (t, n) pair is computed once per thread and reused for every (b, h) row of the
 // group, so the trigonometry is amortised over B*H rows and the kernel runs at HBM speed.
+// Each thread keeps U rows of raw 16-byte vectors in flight (streaming loads/stores: the
+// latent is read once and the rotated copy is not re-read by this kernel).
+template <typename TX>
+struct RawVec {  // 8 elements of TX as raw 16-byte words
+  static constexpr int W = sizeof(TX) * 8 / 16;
+  uint4 w[W];
+};
+
+__device__ __forceinline__ void raw_load(const uint16_t* p, RawVec<uint16_t>& r) {
+  r.w[0] = __ldcs(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ void raw_load(const float* p, RawVec<float>& r) {
+  r.w[0] = __ldcs(reinterpret_cast<const uint4*>(p));
+  r.w[1] = __ldcs(reinterpret_cast<const uint4*>(p) + 1);
+}
+__device__ __forceinline__ void raw_unpack(const RawVec<uint16_t>& r, float (&v)[8]) {
+  const uint32_t w[4] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = bf16_bits_to_f32(w[i] & 0xFFFFu);
+    v[2 * i + 1] = bf16_bits_to_f32(w[i] >> 16);
+  }
+}
+__device__ __forceinline__ void raw_unpack(const RawVec<float>& r, float (&v)[8]) {
+  v[0] = __uint_as_float(r.w[0].x); v[1] = __uint_as_float(r.w[0].y);
+  v[2] = __uint_as_float(r.w[0].z); v[3] = __uint_as_float(r.w[0].w);
+  v[4] = __uint_as_float(r.w[1].x); v[5] = __uint_as_float(r.w[1].y);
+  v[6] = __uint_as_float(r.w[1].z); v[7] = __uint_as_float(r.w[1].w);
+}
+__device__ __forceinline__ void store8_cs(uint16_t* p, const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  __stcs(reinterpret_cast<uint4*>(p), u);
+}
+__device__ __forceinline__ void store8_cs(float* p, const float (&v)[8]) {
+  __stcs(reinterpret_cast<float4*>(p), make_float4(v[0], v[1], v[2], v[3]));
+  __stcs(reinterpret_cast<float4*>(p) + 1, make_float4(v[4], v[5], v[6], v[7]));
+}
+
 template <typename TX, typename TY, bool VEC>
 __global__ void __launch_bounds__(256) rope_kernel(const TX* __restrict__ x, TY* __restrict__ y,
                                                    float* __restrict__ y_lo,
@@ -96,7 +136,7 @@ __global__ void __launch_bounds__(256) rope_kernel(const TX* __restrict__ x, TY*
                                                    int N, int BH, int rows_per_group,
                                                    int64_t xsb, int64_t xsh, int64_t xst,
                                                    int64_t ysb, int64_t ysh, int64_t yst,
-                                                   int64_t pos0) {
+                                                   int64_t pos0, int relu_in) {
   constexpr bool BF16_IN = sizeof(TX) == 2;
   constexpr int E = VEC ? 8 : 2;  // elements per thread
   const int chunks = (N + 256 * E - 1) / (256 * E);
@@ -129,56 +169,68 @@ __global__ void __launch_bounds__(256) rope_kernel(const TX* __restrict__ x, TY*
   }
   const int bh0 = blockIdx.y * rows_per_group;
   const int bh1 = min(BH, bh0 + rows_per_group);
-  constexpr int U = 4;  // rows in flight per thread
-  for (int bh = bh0; bh < bh1; bh += U) {
-    float v[U][8];
+  if (VEC) {
+    constexpr int U = 8;  // rows in flight per thread
+    for (int bh = bh0; bh < bh1; bh += U) {
+      RawVec<TX> raw[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (bh + u < bh1) {
+      for (int u = 0; u < U; ++u) {
+        if (bh + u < bh1) {
+          const int r = bh + u;
+          const int b = r / H, h = r - (r / H) * H;
+          raw_load(x + b * xsb + h * xsh + t * xst + n0, raw[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (bh + u >= bh1) break;
         const int r = bh + u;
         const int b = r / H, h = r - (r / H) * H;
-        const TX* xr = x + b * xsb + h * xsh + t * xst + n0;
-        if (VEC) {
-          load8(xr, v[u]);
-        } else {
-          v[u][0] = load1(xr);
-          v[u][1] = load1(xr + 1);
+        float v[8], o[8];
+        raw_unpack(raw[u], v);
+        if (relu_in) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = fmaxf(v[i], 0.0f);
         }
+#pragma unroll
+        for (int p = 0; p < 4; ++p)
+          rotate_pair<BF16_IN>(v[2 * p], v[2 * p + 1], c[2 * p], s[2 * p], c[2 * p + 1],
+                               s[2 * p + 1], o[2 * p], o[2 * p + 1]);
+        const int64_t yo = b * ysb + h * ysh + t * yst + n0;
+        if (y_lo != nullptr) {
+          float lo[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float hi = tf32_round(o[i]);
+            lo[i] = o[i] - hi;
+            o[i] = hi;
+          }
+          store8_cs(y_lo + yo, lo);
+        }
+        store8_cs(y + yo, o);
       }
     }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (bh + u >= bh1) break;
-      const int r = bh + u;
+  } else {
+    for (int r = bh0; r < bh1; ++r) {
       const int b = r / H, h = r - (r / H) * H;
-      TY* yr = y + b * ysb + h * ysh + t * yst + n0;
-      float o[8];
-#pragma unroll
-      for (int p = 0; p < E / 2; ++p)
-        rotate_pair<BF16_IN>(v[u][2 * p], v[u][2 * p + 1], c[2 * p], s[2 * p], c[2 * p + 1],
-                             s[2 * p + 1], o[2 * p], o[2 * p + 1]);
+      const TX* xr = x + b * xsb + h * xsh + t * xst + n0;
+      float o0, o1;
+      float x0 = load1(xr), x1 = load1(xr + 1);
+      if (relu_in) {
+        x0 = fmaxf(x0, 0.0f);
+        x1 = fmaxf(x1, 0.0f);
+      }
+      rotate_pair<BF16_IN>(x0, x1, c[0], s[0], c[1], s[1], o0, o1);
+      const int64_t yo = b * ysb + h * ysh + t * yst + n0;
       if (y_lo != nullptr) {
-        float* lr = y_lo + b * ysb + h * ysh + t * yst + n0;
-        float lo[8];
-#pragma unroll
-        for (int i = 0; i < E; ++i) {
-          const float hi = tf32_round(o[i]);
-          lo[i] = o[i] - hi;
-          o[i] = hi;
-        }
-        if (VEC) {
-          store8(lr, lo);
-        } else {
-          lr[0] = lo[0];
-          lr[1] = lo[1];
-        }
+        const float h0 = tf32_round(o0), h1 = tf32_round(o1);
+        y_lo[yo] = o0 - h0;
+        y_lo[yo + 1] = o1 - h1;
+        o0 = h0;
+        o1 = h1;
       }
-      if (VEC) {
-        store8(yr, o);
-      } else {
-        store1(yr, o[0]);
-        store1(yr + 1, o[1]);
-      }
+      store1(y + yo, o0);
+      store1(y + yo + 1, o1);
     }
   }
 }
@@ -249,7 +301,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int launch_rope(const void* x, int x_dtype, const int64_t xs[4], void* y, int y_dtype,
                 const int64_t ys[4], float* y_lo, const float* freqs, int64_t B, int64_t H,
-                int64_t T, int64_t N, int64_t pos0, cudaStream_t stream) {
+                int64_t T, int64_t N, int64_t pos0, int relu_in, cudaStream_t stream) {
   const int64_t rows = B * H * T;
   if (rows == 0 || N == 0) return BDH_OK;
   const int xe = x_dtype == BDH_DTYPE_F32 ? 4 : 2;
@@ -280,11 +332,11 @@ int launch_rope(const void* x, int x_dtype, const int64_t xs[4], void* y, int y_
     if (vec)                                                                                      \
       rope_kernel<TX, TY, true><<<grid, 256, 0, stream>>>(                                        \
           static_cast<const TX*>(x), static_cast<TY*>(y), y_lo, freqs, Hi, Ti, Ni, BHi, R, xs[0], \
-          xs[1], xs[2], ys[0], ys[1], ys[2], pos0);                                               \
+          xs[1], xs[2], ys[0], ys[1], ys[2], pos0, relu_in);                                      \
     else                                                                                          \
       rope_kernel<TX, TY, false><<<grid, 256, 0, stream>>>(                                       \
           static_cast<const TX*>(x), static_cast<TY*>(y), y_lo, freqs, Hi, Ti, Ni, BHi, R, xs[0], \
-          xs[1], xs[2], ys[0], ys[1], ys[2], pos0);                                               \
+          xs[1], xs[2], ys[0], ys[1], ys[2], pos0, relu_in);                                      \
   } while (0)
   prof_start(kProfRope, stream);
   if (x_dtype == BDH_DTYPE_BF16 && y_dtype == BDH_DTYPE_BF16) BDH_ROPE_LAUNCH(uint16_t, uint16_t);
@@ -337,6 +389,77 @@ int launch_split_tf32_t(const float* x, const int64_t xs[4], float* hi, float* l
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("split_tf32_t_kernel launch: ") + cudaGetErrorString(e));
+    return BDH_ERR_CUDA;
+  }
+  return BDH_OK;
+}
+
+// out = relu(x) * relu(y) over (B, H, T, N) tensors with a contiguous last dimension and
+// arbitrary other strides (the model's gated product x_sparse * y_sparse, reference
+// bdh_baseline.py:124-126 / bdh.py:927-945, with both ReLUs folded in). Products are rounded
+// once to the output dtype, as the eager op does.
+template <typename TE, bool VEC>
+__global__ void __launch_bounds__(256) relu_mul_kernel(const TE* __restrict__ x,
+                                                       const TE* __restrict__ y, TE* __restrict__ o,
+                                                       int H, int T, int N, int64_t xsb,
+                                                       int64_t xsh, int64_t xst, int64_t ysb,
+                                                       int64_t ysh, int64_t yst, int64_t osb,
+                                                       int64_t osh, int64_t ost) {
+  const int64_t row = blockIdx.x;
+  const int t = static_cast<int>(row % T);
+  const int64_t bh = row / T;
+  const int h = static_cast<int>(bh % H);
+  const int64_t b = bh / H;
+  const TE* xr = x + b * xsb + h * xsh + t * xst;
+  const TE* yr = y + b * ysb + h * ysh + t * yst;
+  TE* orow = o + b * osb + h * osh + t * ost;
+  if (VEC) {
+    for (int n0 = threadIdx.x * 8; n0 < N; n0 += blockDim.x * 8) {
+      RawVec<TE> rx, ry;
+      raw_load(xr + n0, rx);
+      raw_load(yr + n0, ry);
+      float vx[8], vy[8], vo[8];
+      raw_unpack(rx, vx);
+      raw_unpack(ry, vy);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) vo[i] = __fmul_rn(fmaxf(vx[i], 0.0f), fmaxf(vy[i], 0.0f));
+      store8_cs(orow + n0, vo);
+    }
+  } else {
+    for (int n = threadIdx.x; n < N; n += blockDim.x)
+      store1(orow + n, __fmul_rn(fmaxf(load1(xr + n), 0.0f), fmaxf(load1(yr + n), 0.0f)));
+  }
+}
+
+int launch_relu_mul(const void* x, const int64_t xs[4], const void* y, const int64_t ys[4],
+                    void* out, const int64_t os[4], int dtype, int64_t B, int64_t H, int64_t T,
+                    int64_t N, cudaStream_t stream) {
+  const int64_t rows = B * H * T;
+  if (rows == 0 || N == 0) return BDH_OK;
+  const int es = dtype == BDH_DTYPE_F32 ? 4 : 2;
+  bool vec = (N % 8 == 0) && aligned16(x) && aligned16(y) && aligned16(out);
+  for (int i = 0; i < 3; ++i)
+    vec = vec && (xs[i] * es) % 16 == 0 && (ys[i] * es) % 16 == 0 && (os[i] * es) % 16 == 0;
+  const int threads = static_cast<int>(std::min<int64_t>(256, std::max<int64_t>(32, N / 8)));
+  const int Hi = static_cast<int>(H), Ti = static_cast<int>(T), Ni = static_cast<int>(N);
+#define BDH_RM_LAUNCH(TE)                                                                         \
+  do {                                                                                            \
+    if (vec)                                                                                      \
+      relu_mul_kernel<TE, true><<<static_cast<unsigned>(rows), threads, 0, stream>>>(             \
+          static_cast<const TE*>(x), static_cast<const TE*>(y), static_cast<TE*>(out), Hi, Ti,   \
+          Ni, xs[0], xs[1], xs[2], ys[0], ys[1], ys[2], os[0], os[1], os[2]);                    \
+    else                                                                                          \
+      relu_mul_kernel<TE, false><<<static_cast<unsigned>(rows), threads, 0, stream>>>(            \
+          static_cast<const TE*>(x), static_cast<const TE*>(y), static_cast<TE*>(out), Hi, Ti,   \
+          Ni, xs[0], xs[1], xs[2], ys[0], ys[1], ys[2], os[0], os[1], os[2]);                    \
+  } while (0)
+  prof_start(kProfOther, stream);
+  if (dtype == BDH_DTYPE_F32) BDH_RM_LAUNCH(float); else BDH_RM_LAUNCH(uint16_t);
+#undef BDH_RM_LAUNCH
+  prof_stop(kProfOther, stream);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("relu_mul_kernel launch: ") + cudaGetErrorString(e));
     return BDH_ERR_CUDA;
   }
   return BDH_OK;

@@ -11,7 +11,7 @@ namespace bdh {
 
 // Launch timing hooks (prof.cpp); kinds as documented at bdh_profile_end.
 enum ProfKind : int { kProfScore = 0, kProfValue = 1, kProfRope = 2, kProfDecode = 3,
-                      kProfGradQ = 4, kProfGradV = 5, kProfSplit = 6 };
+                      kProfGradQ = 4, kProfGradV = 5, kProfSplit = 6, kProfOther = 7 };
 void prof_start(int kind, cudaStream_t s);
 void prof_stop(int kind, cudaStream_t s);
 
@@ -99,7 +99,11 @@ int launch_grad_v(const GradVArgs& a, cudaStream_t stream, int* err);
 // Elementwise kernels (elementwise.cu).
 int launch_rope(const void* x, int x_dtype, const int64_t xs[4], void* y, int y_dtype,
                 const int64_t ys[4], float* y_lo, const float* freqs, int64_t B, int64_t H,
-                int64_t T, int64_t N, int64_t pos0, cudaStream_t stream);
+                int64_t T, int64_t N, int64_t pos0, int relu_in, cudaStream_t stream);
+// out = relu(x) * relu(y), all (B,H,T,N) with a contiguous last dimension.
+int launch_relu_mul(const void* x, const int64_t xs[4], const void* y, const int64_t ys[4],
+                    void* out, const int64_t os[4], int dtype, int64_t B, int64_t H, int64_t T,
+                    int64_t N, cudaStream_t stream);
 // x (strided, fp32) -> contiguous hi = tf32(x), lo = x - hi.
 int launch_split_tf32(const float* x, const int64_t xs[4], float* hi, float* lo, int64_t B,
                       int64_t H, int64_t T, int64_t N, cudaStream_t stream);

@@ -113,19 +113,23 @@ class RopeTrilSelfAttnFn(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, Q, V, freqs, pos0: int, qr_out: Optional[torch.Tensor]):
+    def forward(ctx, Q, V, freqs, pos0: int, qr_out: Optional[torch.Tensor], relu_input: bool = False):
         from .sm100_attn import rope_rotate, tril_score_v
 
         with torch.no_grad():
             if qr_out is not None and qr_out.dtype != Q.dtype:
                 # a cache slot in another storage dtype: attend in Q's dtype, store the cast
-                QR = rope_rotate(Q, freqs, pos0)
+                QR = rope_rotate(Q, freqs, pos0, relu_input=relu_input)
                 qr_out.copy_(QR)
             else:
-                QR = rope_rotate(Q, freqs, pos0, out=qr_out)
+                QR = rope_rotate(Q, freqs, pos0, out=qr_out, relu_input=relu_input)
             out = tril_score_v(QR, QR, V)
         ctx.pos0 = int(pos0)
-        ctx.save_for_backward(QR, V, freqs)
+        ctx.relu_input = bool(relu_input)
+        if relu_input:
+            ctx.save_for_backward(QR, V, freqs, Q)
+        else:
+            ctx.save_for_backward(QR, V, freqs)
         ctx.mark_non_differentiable(QR)
         return out, QR
 
@@ -133,9 +137,11 @@ class RopeTrilSelfAttnFn(torch.autograd.Function):
     def backward(ctx, dO, _dQR):
         from .sm100_attn import tril_score_v_bwd
 
-        QR, V, freqs = ctx.saved_tensors
+        QR, V, freqs = ctx.saved_tensors[:3]
         dQ, _, dV = tril_score_v_bwd(QR, QR, V, dO.contiguous(), freqs=freqs, pos0=ctx.pos0)
-        return dQ, dV, None, None, None
+        if ctx.relu_input:
+            dQ = dQ * (ctx.saved_tensors[3] > 0).to(dQ.dtype)
+        return dQ, dV, None, None, None, None
 
 
 def strict_tril_attn(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, *,

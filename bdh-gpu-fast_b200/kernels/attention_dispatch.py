@@ -162,7 +162,8 @@ def bdh_attn_decode(Q: torch.Tensor, K_past: torch.Tensor, V_past: torch.Tensor,
 
 def bdh_rope_attn(Q: torch.Tensor, V: torch.Tensor, freqs: torch.Tensor, rope_start: int = 0, *,
                   impl: str | None = None, qr_out: Optional[torch.Tensor] = None,
-                  use_autograd_fn: Optional[bool] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+                  use_autograd_fn: Optional[bool] = None,
+                  relu_input: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
     """Fused RoPE + strict-tril self attention: returns ``(out, QR)``.
 
     ``Q`` is the unrotated latent (B,H,T,N) (any strides with a contiguous last dim, e.g. the
@@ -170,15 +171,19 @@ def bdh_rope_attn(Q: torch.Tensor, V: torch.Tensor, freqs: torch.Tensor, rope_st
     destination for QR (a cache slot). On ``cuda_sm100`` RoPE runs in-register (no cos/sin
     tables) and autograd (when enabled or when Q requires grad) differentiates through the
     fused native backward. On ``eager`` the tables are built and applied with PyTorch ops.
+    ``relu_input``: Q is the encoder pre-activation and ``relu(Q)`` is rotated (the ReLU is
+    folded into the RoPE read on ``cuda_sm100``).
     """
     name = resolve_cold_impl(int(Q.size(2)), requested=impl, probe=Q)
     if name == "cuda_sm100":
         if V.dtype != Q.dtype:
             V = V.to(Q.dtype)
-        out, QR = RopeTrilSelfAttnFn.apply(Q, V, freqs, int(rope_start), qr_out)
+        out, QR = RopeTrilSelfAttnFn.apply(Q, V, freqs, int(rope_start), qr_out, bool(relu_input))
         return out, QR
     from .rope import eager_rope_rotate
 
+    if relu_input:
+        Q = torch.relu(Q)
     cos, sin = rope_tables(freqs, Q.size(2), rope_start, Q.device)
     QR = eager_rope_rotate(Q, cos, sin, out=qr_out)
     return bdh_attn(QR, QR, V, impl="eager", use_autograd_fn=use_autograd_fn), QR

@@ -49,7 +49,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.bdh_last_error.restype = ctypes.c_char_p
     lib.bdh_device_error.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int]
     lib.bdh_rope_rotate.argtypes = [_vp, ctypes.c_int, P, _vp, ctypes.c_int, P, _vp, _vp,
-                                    _i64, _i64, _i64, _i64, _i64, _vp]
+                                    _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _vp]
+    lib.bdh_relu_mul.argtypes = [_vp, P, _vp, P, _vp, P, ctypes.c_int, _i64, _i64, _i64, _i64, _vp]
     lib.bdh_tril_score_v_workspace_size.restype = ctypes.c_size_t
     lib.bdh_tril_score_v_workspace_size.argtypes = [ctypes.c_int, _i64, _i64, _i64, _i64, _i64,
                                                     _i64, ctypes.c_int]
@@ -66,7 +67,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.bdh_tril_score_v_bwd.argtypes = [_vp, P, _vp, P, _vp, P, _vp, P, ctypes.c_int, _vp, P,
                                          _vp, P, _vp, P, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
                                          _i64, _vp, ctypes.c_size_t, _vp]
-    for name in ("bdh_rope_rotate", "bdh_tril_score_v", "bdh_tril_decode", "bdh_tril_score_v_bwd"):
+    for name in ("bdh_rope_rotate", "bdh_tril_score_v", "bdh_tril_decode", "bdh_tril_score_v_bwd",
+                 "bdh_relu_mul"):
         getattr(lib, name).restype = ctypes.c_int
 
 
@@ -256,12 +258,13 @@ def tril_score_v(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Ten
 
 
 def rope_rotate(x: torch.Tensor, freqs: torch.Tensor, pos0: int = 0,
-                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                out: Optional[torch.Tensor] = None, relu_input: bool = False) -> torch.Tensor:
     """BDH RoPE of ``x`` (B,H,T,N) at positions ``pos0 .. pos0+T-1`` computed in registers.
 
     Same arithmetic as ``Attention.rope`` with the ``rope_cos_sin`` tables (bdh.py:119-150,
     kernels/rope.py:108-126) but without materialising the tables. ``out`` may be a strided
-    view (e.g. a cache slot) of another dtype; it must not overlap ``x``.
+    view (e.g. a cache slot) of another dtype; it must not overlap ``x``. ``relu_input``
+    rotates ``relu(x)`` (the encoder's ReLU folded into the read).
     """
     if x.dim() != 4:
         raise ValueError("rope_rotate expects a 4-D (B, H, T, N) tensor")
@@ -287,8 +290,28 @@ def rope_rotate(x: torch.Tensor, freqs: torch.Tensor, pos0: int = 0,
     with torch.cuda.device(dev):
         rc = lib.bdh_rope_rotate(x.data_ptr(), _code(x.dtype), _strides(x), out.data_ptr(),
                                  _code(out.dtype), _strides(out), None, f.data_ptr(),
-                                 B, H, T, N, int(pos0), _stream(dev))
+                                 B, H, T, N, int(pos0), 1 if relu_input else 0, _stream(dev))
     _check(rc, "rope_rotate")
+    return out
+
+
+def relu_mul(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """``relu(x) * relu(y)`` for 4-D tensors of one dtype (contiguous last dim, any strides),
+    returned contiguous in ``x``'s shape — the gated product of a BDH layer."""
+    if x.dim() != 4 or x.shape != y.shape or x.dtype != y.dtype:
+        raise ValueError("relu_mul expects two 4-D tensors of the same shape and dtype")
+    dev = _require_cuda(x, y)
+    lib = _require_lib()
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if y.stride(-1) != 1:
+        y = y.contiguous()
+    out = torch.empty(x.shape, dtype=x.dtype, device=dev)
+    B, H, T, N = x.shape
+    with torch.cuda.device(dev):
+        rc = lib.bdh_relu_mul(x.data_ptr(), _strides(x), y.data_ptr(), _strides(y), out.data_ptr(),
+                              _strides(out), _code(x.dtype), B, H, T, N, _stream(dev))
+    _check(rc, "relu_mul")
     return out
 
 
@@ -415,4 +438,5 @@ __all__ = [
     "tril_decode",
     "tril_score_v_bwd",
     "rope_rotate",
+    "relu_mul",
 ]

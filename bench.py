@@ -163,6 +163,11 @@ def barrier(world):
         dist.barrier()
 
 
+def rank_seed(base: int, rank: int) -> int:
+    """Seed of rank `rank`'s synthetic batch (weights use a rank-independent seed)."""
+    return base + 7919 * rank
+
+
 def max_over_ranks(x: float, world: int, dev) -> float:
     if world == 1:
         return x
@@ -255,13 +260,13 @@ def bench_config2(args, world, rank, dev):
     import bdh_model
     from kernels import sm100_attn
 
-    B, T = 32, 512
+    B, T = args.batch or 32, 512
     cfg = bdh_model.BDHConfig(n_layer=N_LAYER, n_embd=D_MODEL, n_head=N_HEAD,
                               mlp_internal_dim_multiplier=128, vocab_size=VOCAB, dropout=0.0)
     torch.manual_seed(1002)  # identical weights on every rank
     model = bdh_model.BDH(cfg).to(dev).eval()
     model.attn._attn_impl_override = "cuda_sm100"
-    g = torch.Generator().manual_seed(2002 + 7919 * rank)
+    g = torch.Generator().manual_seed(rank_seed(2002, rank))
     idx_host = torch.randint(0, VOCAB, (B, T), generator=g).pin_memory()
     idx = idx_host.to(dev)
 
@@ -343,7 +348,7 @@ def bench_config2(args, world, rank, dev):
 
 # ----------------------------------------------------------- standalone op configs
 def _op_inputs(cfg_id, dev, rank):
-    g = torch.Generator(device=dev).manual_seed(1000 + cfg_id + 7919 * rank)
+    g = torch.Generator(device=dev).manual_seed(rank_seed(1000 + cfg_id, rank))
     if cfg_id == 1:
         B, H, T, N, D, dt = 4, 4, 512, N_LAT, D_MODEL, torch.float32
         q = torch.relu(torch.randn(B, H, T, N, device=dev, generator=g))
@@ -423,7 +428,7 @@ def bench_decode(args, world, rank, dev):
     model = bdh_model.BDH(cfg).to(dev).eval()
     model.attn._attn_impl_override = "cuda_sm100"
     steps_total = args.warmup + args.steps
-    g = torch.Generator().manual_seed(2004 + 7919 * rank)
+    g = torch.Generator().manual_seed(rank_seed(2004, rank))
     toks = torch.randint(0, VOCAB, (B, P + steps_total), generator=g).to(dev)
     storage = torch.bfloat16 if args.decode_bf16 else None
     cache = CacheManager.from_config(cfg, B, P + steps_total, dev, storage_dtype=storage)
@@ -493,6 +498,8 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode-bf16", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="config 2 per-GPU batch override (profiling aid; default 32)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl != "reference":
         args.warmup = 3

@@ -62,9 +62,20 @@ int bdh_device_error(int device, int* code, int reset);
  * Replaces: kernels/rope.py:220-240 (eager_rope_rotate) behind kernels/rope_dispatch.py:64-99
  * (bdh_rope_rotate / bdh_rope_rotate_paired) and bdh.py:119-150 (phase / cos / sin tables).
  */
+#define BDH_ROPE_RELU_INPUT 1 /* flags bit: rotate relu(x) (the ReLU of the BDH encoder, bdh.py:994) */
 int bdh_rope_rotate(const void* x, int x_dtype, const int64_t x_strides[4], void* y, int y_dtype,
                     const int64_t y_strides[4], void* y_lo, const float* freqs, int64_t B,
-                    int64_t H, int64_t T, int64_t N, int64_t pos0, void* stream);
+                    int64_t H, int64_t T, int64_t N, int64_t pos0, int flags, void* stream);
+
+/*
+ * Gated product of the BDH layer: out = relu(x) * relu(y), all (B,H,T,N) with a contiguous last
+ * dimension and any other strides (the einsum outputs are read in place), rounded once to dtype.
+ * Replaces the eager `x_sparse * y_sparse` of bdh.py:927-945 / bdh_baseline.py:124-126 together
+ * with the two F.relu passes before it (bdh.py:861-925).
+ */
+int bdh_relu_mul(const void* x, const int64_t x_strides[4], const void* y,
+                 const int64_t y_strides[4], void* out, const int64_t out_strides[4], int dtype,
+                 int64_t B, int64_t H, int64_t T, int64_t N, void* stream);
 
 /* Scratch bytes bdh_tril_score_v needs for these sizes (dtype of q/k/v). */
 size_t bdh_tril_score_v_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,
@@ -156,7 +167,8 @@ int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* 
  * perf_counter, benchmarks/bench_gpu_attn.py:263-280). Between begin and end, every kernel of
  * this library is bracketed by CUDA events on its own stream; end synchronises them and
  * returns the summed device milliseconds and launch counts per kernel kind:
- *   0 score pass, 1 value pass, 2 RoPE, 3 decode, 4 grad-Q pass, 5 grad-V pass, 6 split/transpose.
+ *   0 score pass, 1 value pass, 2 RoPE, 3 decode, 4 grad-Q pass, 5 grad-V pass, 6 split/transpose,
+ *   7 gated product (bdh_relu_mul).
  */
 #define BDH_PROF_KINDS 8
 int bdh_profile_begin(void);

@@ -69,7 +69,7 @@ def test_invalid_arguments_rejected_before_launch():
     rc = lib.bdh_tril_score_v(None, s, None, s, None, s, 1, None, s, 1, 1, 1, 1, 16, 64, 64, None, 0, None)
     assert rc == 3 and b"workspace" in lib.bdh_last_error()
     # odd RoPE width
-    rc = lib.bdh_rope_rotate(None, 1, s, None, 1, s, None, None, 1, 1, 4, 63, 0, None)
+    rc = lib.bdh_rope_rotate(None, 1, s, None, 1, s, None, None, 1, 1, 4, 63, 0, 0, None)
     assert rc == 1 and b"even" in lib.bdh_last_error()
     # empty problems are a no-op success
     rc = lib.bdh_tril_score_v(None, s, None, s, None, s, 1, None, s, 1, 0, 1, 1, 16, 64, 64, None, 0, None)

@@ -377,3 +377,26 @@ def test_model_cached_decode_matches_reference(impl, storage, monkeypatch):
     tol = 1e-5 if storage is None else 3e-3
     for a, b in zip(steps, ref):
         assert rel(a, b) < tol
+
+
+# ------------------------------------------------------- fused ReLU / gated product
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_rope_relu_input_equals_rope_of_relu(dt):
+    N = 1024
+    f = torch.tensor(O.get_freqs(N), device=DEV)
+    x = torch.randn(2, 33, 4, N, device=DEV).to(dt).permute(0, 2, 1, 3)  # pre-activation view
+    a = sa().rope_rotate(x, f, 11, relu_input=True)
+    b = sa().rope_rotate(torch.relu(x), f, 11)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_relu_mul_matches_torch_on_einsum_layouts(dt):
+    B, T, H, N, D = 2, 40, 4, 512, 32
+    x = torch.randn(B, T, H, N, device=DEV).to(dt)                       # contiguous (b,t,h,n)
+    yk = torch.randn(B, H, T, D, device=DEV).to(dt)
+    w = torch.randn(H, D, N, device=DEV).to(dt)
+    y = torch.einsum("bhtd,hdn->bthn", yk, w)                            # strided view
+    out = sa().relu_mul(x, y)
+    ref = torch.relu(x) * torch.relu(y)
+    assert out.is_contiguous() and torch.equal(out, ref)
