@@ -229,13 +229,21 @@ __device__ __forceinline__ uint32_t f32_to_bf16_bits(float x) {
   return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
 }
 
+// Two fp32 values to a packed bf16x2 word (lo in bits 0-15), round-to-nearest-even, with one
+// conversion instruction for the pair.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float bf16x2_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16x2_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
 // x rounded to the nearest bf16 value (ties to even), kept as fp32.
 __device__ __forceinline__ float bf16_round_f32(float x) {
   return __uint_as_float(f32_to_bf16_bits(x) << 16);
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return f32_to_bf16_bits(lo) | (f32_to_bf16_bits(hi) << 16);
-}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) { return cvt_bf16x2(lo, hi); }
 
 }  // namespace bdh

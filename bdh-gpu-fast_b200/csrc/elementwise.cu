@@ -50,6 +50,16 @@ __device__ __forceinline__ void rotate_pair(float x0, float x1, float c0, float 
   }
 }
 
+// bf16 pair rotation with packed conversions: the four products are rounded to bf16 two at a
+// time, added in fp32, and the sums rounded once more into the packed output word
+// (y0 in the low half, y1 in the high half) — the reference's cast-then-add sequence.
+__device__ __forceinline__ uint32_t rotate_pair_bf16x2(float x0, float x1, float c0, float s0,
+                                                       float c1, float s1) {
+  const uint32_t a = cvt_bf16x2(__fmul_rn(x0, c0), __fmul_rn(x1, c1));   // x0 c0 | x1 c1
+  const uint32_t b = cvt_bf16x2(__fmul_rn(-x1, s0), __fmul_rn(x0, s1));  // -x1 s0 | x0 s1
+  return cvt_bf16x2(__fadd_rn(bf16x2_lo(a), bf16x2_lo(b)), __fadd_rn(bf16x2_hi(a), bf16x2_hi(b)));
+}
+
 __device__ __forceinline__ void load8(const uint16_t* p, float (&v)[8]) {
   const uint4 u = *reinterpret_cast<const uint4*>(p);
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -192,11 +202,30 @@ __global__ void __launch_bounds__(256) rope_kernel(const TX* __restrict__ x, TY*
 #pragma unroll
           for (int i = 0; i < 8; ++i) v[i] = fmaxf(v[i], 0.0f);
         }
-#pragma unroll
-        for (int p = 0; p < 4; ++p)
-          rotate_pair<BF16_IN>(v[2 * p], v[2 * p + 1], c[2 * p], s[2 * p], c[2 * p + 1],
-                               s[2 * p + 1], o[2 * p], o[2 * p + 1]);
         const int64_t yo = b * ysb + h * ysh + t * yst + n0;
+        if (BF16_IN && sizeof(TY) == 2 && y_lo == nullptr) {
+          uint4 w;
+          w.x = rotate_pair_bf16x2(v[0], v[1], c[0], s[0], c[1], s[1]);
+          w.y = rotate_pair_bf16x2(v[2], v[3], c[2], s[2], c[3], s[3]);
+          w.z = rotate_pair_bf16x2(v[4], v[5], c[4], s[4], c[5], s[5]);
+          w.w = rotate_pair_bf16x2(v[6], v[7], c[6], s[6], c[7], s[7]);
+          __stcs(reinterpret_cast<uint4*>(y + yo), w);
+          continue;
+        }
+        if (BF16_IN) {
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const uint32_t w = rotate_pair_bf16x2(v[2 * p], v[2 * p + 1], c[2 * p], s[2 * p],
+                                                  c[2 * p + 1], s[2 * p + 1]);
+            o[2 * p] = bf16x2_lo(w);
+            o[2 * p + 1] = bf16x2_hi(w);
+          }
+        } else {
+#pragma unroll
+          for (int p = 0; p < 4; ++p)
+            rotate_pair<false>(v[2 * p], v[2 * p + 1], c[2 * p], s[2 * p], c[2 * p + 1],
+                               s[2 * p + 1], o[2 * p], o[2 * p + 1]);
+        }
         if (y_lo != nullptr) {
           float lo[8];
 #pragma unroll

@@ -116,10 +116,25 @@ struct ScoreProb {
     const int gj_base = tl.ni * BN + c0;
     const bool diag = tl.ni * BN < (tl.mi + 1) * S::BM && (tl.ni + 1) * BN > tl.mi * S::BM;
     uint32_t hi[32], lo[32];
+    if (ELEM == 2) {
+      // packed conversions: one cvt per pair for hi, one for lo
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      const float x = gj_base + e < gi ? __uint_as_float(r[e]) : 0.0f;
-      split(x, hi[e], lo[e]);
+      for (int e = 0; e < 32; e += 2) {
+        const float x0 = gj_base + e < gi ? __uint_as_float(r[e]) : 0.0f;
+        const float x1 = gj_base + e + 1 < gi ? __uint_as_float(r[e + 1]) : 0.0f;
+        const uint32_t wh = cvt_bf16x2(x0, x1);
+        const uint32_t wl = cvt_bf16x2(x0 - bf16x2_lo(wh), x1 - bf16x2_hi(wh));
+        hi[e] = wh & 0xFFFFu;
+        hi[e + 1] = wh >> 16;
+        lo[e] = wl & 0xFFFFu;
+        lo[e + 1] = wl >> 16;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const float x = gj_base + e < gi ? __uint_as_float(r[e]) : 0.0f;
+        split(x, hi[e], lo[e]);
+      }
     }
     const size_t unit_off = static_cast<size_t>(tl.unit) * p.T;
     // ---- direct store S[i][j] (vectorised unless it must skip the upper part of a diagonal tile)
