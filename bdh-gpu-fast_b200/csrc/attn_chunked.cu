@@ -1,0 +1,321 @@
+// Chunked long-sequence forward (bf16): the same strict-causal product computed as
+//
+//   out[c-th chunk rows] = tril(Q_c K_c^T, -1) V_c  +  Q_c S_{c-1},   S_c = sum_{c' <= c} K_c'^T V_c'
+//
+// with chunks of C = 256 keys. Work per (b,h) unit drops from T(T-1)(N+D) to about
+// T(C-1)(N+D) + 4 T N D flops (for T = 8192: 86 instead of 553 GFLOP), at the cost of streaming
+// the N x D prefix states through HBM once written, once read.
+//
+// Three persistent tcgen05 passes (tc_engine.cuh):
+//   1. score pass restricted to each 128-row block's own chunk (score_pass.cuh, chunk > 0),
+//      P stored per row relative to the chunk start: [u][T][C] hi/lo;
+//   2. state pass: S = K^T V accumulated over keys in chunk-sized accumulation rounds; after
+//      each chunk the running fp32 sum (in registers) is written as the bf16 hi/lo prefix
+//      S_c ([u][chunk][N][D]) used by the next chunk; operands read MN-major straight from the
+//      latents (keys are the contraction dimension);
+//   3. chunk value pass: per 128-row block, K-segment 1 = intra-chunk P V, K-segment 2 = Q S_{c-1}
+//      over the latent width, both accumulated into the same TMEM tile.
+// The reference computes this path quadratically (kernels/attention.py:27-40, 676-777;
+// csrc/tril_attn_cuda.cu:129-249); the chunked form is the north-star formulation.
+#include <algorithm>
+
+#include "bdh_sm100.h"
+#include "internal.h"
+#include "score_pass.cuh"
+#include "tc_engine.cuh"
+#include "tma_host.h"
+
+namespace bdh {
+
+namespace {
+
+constexpr int kChunk = 256;
+
+// ------------------------------------------------------------------- state pass ----
+template <int STAGES>
+struct StateProb {
+  using S = TcShape<2, 128, true, true, 1, 1, STAGES, kChunk / 64>;
+  static constexpr int kEmitEveryChunk = 1;
+  struct Params {
+    CUtensorMap a_map[1];  // K (B,H,T,N) read MN-major: box 64 (n) x 64 (t)
+    CUtensorMap b_map[1];  // V (B,Hv,T,D) read MN-major: box 64 (d) x 64 (t)
+    int H, Hv, T, N, D;
+    int nn, nd;            // 128-wide latent / value tiles
+    int units, nchunks;
+    uint16_t* s_hi;        // [units][nchunks][N][D]
+    uint16_t* s_lo;
+    int* err;
+  };
+  struct Tile {
+    int unit, ni, di;
+  };
+  __device__ static int num_tiles(const Params& p) { return p.units * p.nn * p.nd; }
+  __device__ static Tile tile(const Params& p, int t) {
+    Tile tl;
+    tl.unit = t / (p.nn * p.nd);
+    const int r = t - tl.unit * p.nn * p.nd;
+    tl.ni = r / p.nd;
+    tl.di = r - tl.ni * p.nd;
+    return tl;
+  }
+  // the last chunk's total is never needed
+  __device__ static int k_blocks(const Params& p, const Tile&) { return (p.nchunks - 1) * (kChunk / 64); }
+  __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x1u; }
+  __device__ static void prefetch(const Params& p) {
+    tma_prefetch_desc(&p.a_map[0]);
+    tma_prefetch_desc(&p.b_map[0]);
+  }
+  __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint64_t* bar,
+                                    uint8_t* a_dst, uint8_t* b_dst) {
+    const int b = tl.unit / p.H, h = tl.unit - (tl.unit / p.H) * p.H;
+    const int hv = p.Hv == 1 ? 0 : h;
+    const int t0 = kb * 64;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      tma_load_4d(&p.a_map[0], bar, a_dst + c * 64 * 128, tl.ni * 128 + c * 64, t0, h, b);
+      tma_load_4d(&p.b_map[0], bar, b_dst + c * 64 * 128, tl.di * 128 + c * 64, t0, hv, b);
+    }
+  }
+  __device__ static void epilogue(const Params&, const Tile&, int, int, const uint32_t (&)[32]) {}
+  // After chunk ch the running sum is S_ch, the prefix state of chunk ch + 1.
+  __device__ static void epilogue_chunk(const Params& p, const Tile& tl, int row, int ch, int nch,
+                                        int c0, const uint32_t (&r)[32]) {
+    const int n = tl.ni * 128 + row;
+    const int d0 = tl.di * 128 + c0;
+    if (n >= p.N || d0 >= p.D) return;
+    const size_t off = ((static_cast<size_t>(tl.unit) * p.nchunks + (ch + 1)) * p.N + n) *
+                           static_cast<size_t>(p.D) + d0;
+    uint16_t* dh = p.s_hi + off;
+    uint16_t* dl = p.s_lo + off;
+    const bool vec = d0 + 32 <= p.D && (p.D % 8) == 0;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      uint32_t wh[4], wl[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float x0 = __uint_as_float(r[8 * v + 2 * e]), x1 = __uint_as_float(r[8 * v + 2 * e + 1]);
+        wh[e] = cvt_bf16x2(x0, x1);
+        wl[e] = cvt_bf16x2(x0 - bf16x2_lo(wh[e]), x1 - bf16x2_hi(wh[e]));
+      }
+      if (vec) {
+        *reinterpret_cast<uint4*>(dh + 8 * v) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+        *reinterpret_cast<uint4*>(dl + 8 * v) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+      } else {
+        for (int e = 0; e < 8 && d0 + 8 * v + e < p.D; ++e) {
+          dh[8 * v + e] = static_cast<uint16_t>(wh[e / 2] >> (16 * (e & 1)));
+          dl[8 * v + e] = static_cast<uint16_t>(wl[e / 2] >> (16 * (e & 1)));
+        }
+      }
+    }
+    (void)nch;
+  }
+};
+
+// -------------------------------------------------------------- chunk value pass ----
+template <int STAGES>
+struct ChunkValueProb {
+  static constexpr int BN = 128;
+  using S = TcShape<2, BN, false, true, 2, 2, STAGES>;
+  static constexpr int kVarStageTx = 1;
+  struct Params {
+    CUtensorMap p_map[2];  // P hi/lo over [units][T][C], box 64 x 128
+    CUtensorMap v_map;     // V (B,Hv,T,D), box 64 (d) x 64 (t)
+    CUtensorMap q_map;     // Q (B,H,T,N), box 64 (n) x 128 (t)
+    CUtensorMap s_map[2];  // S hi/lo over [units][nchunks][N][D], box 64 (d) x 64 (n)
+    int H, Hv, T, N, D;
+    int mt, nd, units, nchunks;
+    void* out;             // (B,H,T,D) strided
+    int64_t os_b, os_h, os_t;
+    int out_f32, vec_ok;
+    int* err;
+  };
+  struct Tile {
+    int unit, mi, ni;
+  };
+  __device__ static int num_tiles(const Params& p) { return p.units * p.mt * p.nd; }
+  __device__ static Tile tile(const Params& p, int t) {
+    Tile tl;
+    tl.unit = t / (p.mt * p.nd);
+    const int r = t - tl.unit * p.mt * p.nd;
+    tl.mi = r / p.nd;
+    tl.ni = r - tl.mi * p.nd;
+    return tl;
+  }
+  __device__ static int cs(const Tile& tl) { return (tl.mi * 128 / kChunk) * kChunk; }
+  __device__ static int n_intra(const Params& p, const Tile& tl) {
+    return ceil_div_d(min(p.T, (tl.mi + 1) * 128) - cs(tl), 64);
+  }
+  __device__ static int n_inter(const Params& p, const Tile& tl) {
+    return cs(tl) > 0 ? ceil_div_d(p.N, 64) : 0;
+  }
+  __device__ static int k_blocks(const Params& p, const Tile& tl) { return n_intra(p, tl) + n_inter(p, tl); }
+  // intra: A0 A1 (P hi, lo) x B0 (V); inter: A0 (Q) x B0 B1 (S hi, lo)
+  __device__ static uint32_t pair_mask(const Params& p, const Tile& tl, int kb) {
+    return kb < n_intra(p, tl) ? 0x3u : 0x5u;
+  }
+  __device__ static uint32_t stage_tx(const Params& p, const Tile& tl, int kb) {
+    return kb < n_intra(p, tl) ? 2 * S::A_TILE + S::B_TILE : S::A_TILE + 2 * S::B_TILE;
+  }
+  __device__ static void prefetch(const Params& p) {
+    tma_prefetch_desc(&p.p_map[0]);
+    tma_prefetch_desc(&p.p_map[1]);
+    tma_prefetch_desc(&p.v_map);
+    tma_prefetch_desc(&p.q_map);
+    tma_prefetch_desc(&p.s_map[0]);
+    tma_prefetch_desc(&p.s_map[1]);
+  }
+  __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint64_t* bar,
+                                    uint8_t* a_dst, uint8_t* b_dst) {
+    const int b = tl.unit / p.H, h = tl.unit - (tl.unit / p.H) * p.H;
+    const int ni = n_intra(p, tl);
+    if (kb < ni) {
+      const int hv = p.Hv == 1 ? 0 : h;
+      for (int i = 0; i < 2; ++i)
+        tma_load_4d(&p.p_map[i], bar, a_dst + i * S::A_TILE, kb * 64, tl.mi * 128, tl.unit, 0);
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+        tma_load_4d(&p.v_map, bar, b_dst + c * 64 * 128, tl.ni * BN + c * 64, cs(tl) + kb * 64, hv, b);
+    } else {
+      const int n0 = (kb - ni) * 64;
+      const int chunk = cs(tl) / kChunk;
+      tma_load_4d(&p.q_map, bar, a_dst, n0, tl.mi * 128, h, b);
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          tma_load_4d(&p.s_map[i], bar, b_dst + i * S::B_TILE + c * 64 * 128, tl.ni * BN + c * 64,
+                      n0, chunk, tl.unit);
+    }
+  }
+  __device__ static void epilogue(const Params& p, const Tile& tl, int row, int c0,
+                                  const uint32_t (&r)[32]) {
+    const int gi = tl.mi * 128 + row;
+    if (gi >= p.T) return;
+    const int b = tl.unit / p.H, h = tl.unit - (tl.unit / p.H) * p.H;
+    const int gd0 = tl.ni * BN + c0;
+    if (gd0 >= p.D) return;
+    const int64_t off = b * p.os_b + h * p.os_h + gi * p.os_t + gd0;
+    if (p.out_f32) {
+      float* o = static_cast<float*>(p.out) + off;
+      for (int e = 0; e < 32 && gd0 + e < p.D; ++e) o[e] = __uint_as_float(r[e]);
+      return;
+    }
+    uint16_t* o = static_cast<uint16_t*>(p.out) + off;
+    if (p.vec_ok && gd0 + 32 <= p.D) {
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        *reinterpret_cast<uint4*>(o + 8 * v) = make_uint4(
+            cvt_bf16x2(__uint_as_float(r[8 * v]), __uint_as_float(r[8 * v + 1])),
+            cvt_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3])),
+            cvt_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5])),
+            cvt_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7])));
+    } else {
+      for (int e = 0; e < 32 && gd0 + e < p.D; ++e)
+        o[e] = static_cast<uint16_t>(f32_to_bf16_bits(__uint_as_float(r[e])));
+    }
+  }
+};
+
+using StateBf16 = StateProb<6>;
+using ChunkValueBf16 = ChunkValueProb<3>;
+
+}  // namespace
+
+int chunk_len() { return kChunk; }
+
+size_t chunked_p_bytes(int64_t B, int64_t H, int64_t T) {
+  return static_cast<size_t>(B * H * T * kChunk) * 2;
+}
+size_t chunked_s_bytes(int64_t B, int64_t H, int64_t T, int64_t N, int64_t D) {
+  const int64_t nch = (T + kChunk - 1) / kChunk;
+  return static_cast<size_t>(B * H * nch * N * D) * 2;
+}
+
+int launch_chunked_forward(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi, void* s_lo,
+                           cudaStream_t stream, int* err) {
+  if (a.dtype != BDH_DTYPE_BF16) {
+    set_error("chunked forward: bf16 inputs only");
+    return BDH_ERR_INVALID;
+  }
+  const int64_t units = a.B * a.H;
+  const int nchunks = static_cast<int>((a.T + kChunk - 1) / kChunk);
+  // 1. intra-chunk scores
+  ScoreArgs sa;
+  sa.elem = 2;
+  sa.a[0] = a.q;
+  sa.b[0] = a.k;
+  for (int i = 0; i < 4; ++i) {
+    sa.a_strides[i] = a.q_strides[i];
+    sa.b_strides[i] = a.k_strides[i];
+  }
+  sa.B = a.B; sa.H = a.H; sa.Hb = a.H; sa.T = a.T; sa.K = a.N;
+  sa.mode = kStoreDirect;
+  sa.chunk = kChunk;
+  sa.p_hi = p_hi;
+  sa.p_lo = p_lo;
+  int rc = launch_score_pass(sa, stream, err);
+  if (rc) return rc;
+  // 2. prefix states S_1 .. S_{nchunks-1}
+  if (nchunks > 1) {
+    StateBf16::Params prm{};
+    const int64_t kd[4] = {a.N, a.T, a.H, a.B};
+    const int64_t ks[3] = {a.k_strides[2] * 2, a.k_strides[1] * 2, a.k_strides[0] * 2};
+    const int64_t vd[4] = {a.D, a.T, a.Hv, a.B};
+    const int64_t vs[3] = {a.v_strides[2] * 2, a.v_strides[1] * 2, a.v_strides[0] * 2};
+    if (!make_map_4d(&prm.a_map[0], a.k, 2, kd, ks, 64, 64, "state pass: K")) return BDH_ERR_INVALID;
+    if (!make_map_4d(&prm.b_map[0], a.v, 2, vd, vs, 64, 64, "state pass: V")) return BDH_ERR_INVALID;
+    prm.H = static_cast<int>(a.H);
+    prm.Hv = static_cast<int>(a.Hv);
+    prm.T = static_cast<int>(a.T);
+    prm.N = static_cast<int>(a.N);
+    prm.D = static_cast<int>(a.D);
+    prm.nn = static_cast<int>((a.N + 127) / 128);
+    prm.nd = static_cast<int>((a.D + 127) / 128);
+    prm.units = static_cast<int>(units);
+    prm.nchunks = nchunks;
+    prm.s_hi = static_cast<uint16_t*>(s_hi);
+    prm.s_lo = static_cast<uint16_t*>(s_lo);
+    prm.err = err;
+    rc = launch_tc<StateBf16::S, StateBf16>(prm, prm.units * prm.nn * prm.nd, stream, kProfState);
+    if (rc) return rc;
+  }
+  // 3. intra P V + inter Q S
+  ChunkValueBf16::Params prm{};
+  const int64_t pd[4] = {kChunk, a.T, units, 1};
+  const int64_t ps[3] = {int64_t(kChunk) * 2, a.T * kChunk * 2, units * a.T * kChunk * 2};
+  if (!make_map_4d(&prm.p_map[0], p_hi, 2, pd, ps, 64, 128, "chunk value pass: P hi")) return BDH_ERR_INVALID;
+  if (!make_map_4d(&prm.p_map[1], p_lo, 2, pd, ps, 64, 128, "chunk value pass: P lo")) return BDH_ERR_INVALID;
+  const int64_t vd[4] = {a.D, a.T, a.Hv, a.B};
+  const int64_t vs[3] = {a.v_strides[2] * 2, a.v_strides[1] * 2, a.v_strides[0] * 2};
+  if (!make_map_4d(&prm.v_map, a.v, 2, vd, vs, 64, 64, "chunk value pass: V")) return BDH_ERR_INVALID;
+  const int64_t qd[4] = {a.N, a.T, a.H, a.B};
+  const int64_t qs[3] = {a.q_strides[2] * 2, a.q_strides[1] * 2, a.q_strides[0] * 2};
+  if (!make_map_4d(&prm.q_map, a.q, 2, qd, qs, 64, 128, "chunk value pass: Q")) return BDH_ERR_INVALID;
+  const int64_t sd[4] = {a.D, a.N, nchunks, units};
+  const int64_t ss[3] = {a.D * 2, a.N * a.D * 2, int64_t(nchunks) * a.N * a.D * 2};
+  if (!make_map_4d(&prm.s_map[0], s_hi, 2, sd, ss, 64, 64, "chunk value pass: S hi")) return BDH_ERR_INVALID;
+  if (!make_map_4d(&prm.s_map[1], s_lo, 2, sd, ss, 64, 64, "chunk value pass: S lo")) return BDH_ERR_INVALID;
+  prm.H = static_cast<int>(a.H);
+  prm.Hv = static_cast<int>(a.Hv);
+  prm.T = static_cast<int>(a.T);
+  prm.N = static_cast<int>(a.N);
+  prm.D = static_cast<int>(a.D);
+  prm.mt = static_cast<int>((a.T + 127) / 128);
+  prm.nd = static_cast<int>((a.D + ChunkValueBf16::BN - 1) / ChunkValueBf16::BN);
+  prm.units = static_cast<int>(units);
+  prm.nchunks = nchunks;
+  prm.out = a.out;
+  prm.os_b = a.out_strides[0];
+  prm.os_h = a.out_strides[1];
+  prm.os_t = a.out_strides[2];
+  prm.out_f32 = a.out_dtype == BDH_DTYPE_F32 ? 1 : 0;
+  const int oes = prm.out_f32 ? 4 : 2;
+  prm.vec_ok = ((reinterpret_cast<uintptr_t>(a.out) & 15u) == 0 && (a.out_strides[0] * oes) % 16 == 0 &&
+                (a.out_strides[1] * oes) % 16 == 0 && (a.out_strides[2] * oes) % 16 == 0)
+                   ? 1
+                   : 0;
+  prm.err = err;
+  return launch_tc<ChunkValueBf16::S, ChunkValueBf16>(prm, prm.units * prm.mt * prm.nd, stream,
+                                                       kProfValue);
+}
+
+}  // namespace bdh

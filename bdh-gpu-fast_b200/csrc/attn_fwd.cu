@@ -153,7 +153,8 @@ int launch_score_pass(const ScoreArgs& a, cudaStream_t stream, int* err) {
     int tpu = 0;
     for (int mi = 0; mi < prm.mt; ++mi) {
       const int64_t lim = std::min<int64_t>(a.T, int64_t(mi + 1) * 128);
-      tpu += static_cast<int>((lim + bn - 1) / bn);
+      const int64_t k0 = a.chunk > 0 ? (int64_t(mi) * 128 / a.chunk) * a.chunk : 0;
+      tpu += static_cast<int>((lim + bn - 1) / bn - k0 / bn);
     }
     prm.tiles_per_unit = tpu;
     prm.units = static_cast<int>(a.B * a.H);
@@ -161,7 +162,8 @@ int launch_score_pass(const ScoreArgs& a, cudaStream_t stream, int* err) {
     prm.p_lo = a.p_lo;
     prm.p2_hi = a.p2_hi;
     prm.p2_lo = a.p2_lo;
-    prm.ldp = score_ld(a.T);
+    prm.ldp = a.chunk > 0 ? a.chunk : score_ld(a.T);
+    prm.chunk = a.chunk;
     prm.err = err;
     return true;
   };

@@ -1,5 +1,6 @@
 // extern "C" boundary of libbdh_sm100.so: argument validation, workspace carving and kernel
 // sequencing. No torch types cross this boundary and nothing here allocates device memory.
+#include <atomic>
 #include <cstring>
 #include <sstream>
 #include <string>
@@ -36,9 +37,21 @@ int esize(int d) { return d == BDH_DTYPE_F32 ? 4 : 2; }
 
 size_t align_up(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+std::atomic<int> g_fwd_algo{BDH_FWD_AUTO};
+
+bool use_chunked(int dtype, int64_t T) {
+  if (dtype != BDH_DTYPE_BF16) return false;
+  const int algo = g_fwd_algo.load();
+  if (algo == BDH_FWD_CHUNKED) return T > chunk_len();
+  if (algo == BDH_FWD_QUADRATIC) return false;
+  return T >= 1536;
+}
+
 // Workspace layout of the forward (byte offsets), shared by the size query and the call.
 struct FwdLayout {
   size_t q_hi = 0, q_lo = 0, k_hi = 0, k_lo = 0, v_hi = 0, v_lo = 0, p_hi = 0, p_lo = 0;
+  size_t s_hi = 0, s_lo = 0;
+  bool chunked = false;
   size_t total = 0;
 };
 
@@ -47,6 +60,17 @@ FwdLayout fwd_layout(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T, int
   FwdLayout L;
   size_t off = 0;
   const int e = esize(dtype);
+  if (use_chunked(dtype, T)) {
+    L.chunked = true;
+    const size_t pb = align_up(chunked_p_bytes(B, H, T));
+    const size_t sb = align_up(chunked_s_bytes(B, H, T, N, D));
+    L.p_hi = off; off += pb;
+    L.p_lo = off; off += pb;
+    L.s_hi = off; off += sb;
+    L.s_lo = off; off += sb;
+    L.total = off;
+    return L;
+  }
   if (dtype == BDH_DTYPE_F32) {
     const size_t qbytes = align_up(static_cast<size_t>(B * H * T * N) * 4);
     const size_t vbytes = align_up(static_cast<size_t>(B * Hv * D * vt_ld(T)) * 4);
@@ -248,9 +272,17 @@ int bdh_tril_score_v(const void* q, const int64_t q_strides[4], const void* k,
     std::memcpy(a.k_strides, k_strides, sizeof(a.k_strides));
     std::memcpy(a.v_strides, v_strides, sizeof(a.v_strides));
   }
+  if (L.chunked)
+    return launch_chunked_forward(a, ws + L.p_hi, ws + L.p_lo, ws + L.s_hi, ws + L.s_lo, st, err);
   int rc = launch_score(a, ws + L.p_hi, ws + L.p_lo, st, err);
   if (rc) return rc;
   return launch_value(a, ws + L.p_hi, ws + L.p_lo, st, err);
+}
+
+int bdh_set_forward_algo(int algo) {
+  if (algo != BDH_FWD_AUTO && algo != BDH_FWD_QUADRATIC && algo != BDH_FWD_CHUNKED)
+    return -1;
+  return g_fwd_algo.exchange(algo);
 }
 
 size_t bdh_tril_decode_workspace_size(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t D) {

@@ -11,7 +11,8 @@ namespace bdh {
 
 // Launch timing hooks (prof.cpp); kinds as documented at bdh_profile_end.
 enum ProfKind : int { kProfScore = 0, kProfValue = 1, kProfRope = 2, kProfDecode = 3,
-                      kProfGradQ = 4, kProfGradV = 5, kProfSplit = 6, kProfOther = 7 };
+                      kProfGradQ = 4, kProfGradV = 5, kProfSplit = 6, kProfOther = 7,
+                      kProfState = 8 };
 void prof_start(int kind, cudaStream_t s);
 void prof_stop(int kind, cudaStream_t s);
 
@@ -47,6 +48,7 @@ struct ScoreArgs {
   int64_t b_strides[4] = {0, 0, 0, 1};
   int64_t B = 0, H = 0, Hb = 0, T = 0, K = 0;
   int mode = kStoreDirect;
+  int chunk = 0;  // > 0 (kStoreDirect only): keys limited to each row block's chunk, [u][T][chunk]
   void* p_hi = nullptr;
   void* p_lo = nullptr;
   void* p2_hi = nullptr;
@@ -60,6 +62,13 @@ int64_t vt_ld(int64_t T);
 int launch_score(const FwdArgs& a, void* p_hi, void* p_lo, cudaStream_t stream, int* err);
 int launch_value(const FwdArgs& a, const void* p_hi, const void* p_lo, cudaStream_t stream,
                  int* err);
+
+// Chunked long-sequence forward (attn_chunked.cu), bf16 only.
+int chunk_len();
+size_t chunked_p_bytes(int64_t B, int64_t H, int64_t T);
+size_t chunked_s_bytes(int64_t B, int64_t H, int64_t T, int64_t N, int64_t D);
+int launch_chunked_forward(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi, void* s_lo,
+                           cudaStream_t stream, int* err);
 
 // Backward passes (attn_bwd.cu).
 // out[u] = Gs[u] X[u] with Gs a hi/lo score pair ([B*H][T][score_ld(T)]); krange 0: all keys,

@@ -49,14 +49,19 @@ struct ScoreProb {
     void* p2_hi;           // kStoreLU: transposed destination
     void* p2_lo;
     int64_t ldp;
+    int chunk;             // > 0: keys restricted to the query block's chunk, stored relative
     int* err;
   };
   struct Tile {
     int unit, mi, ni;
   };
 
+  // First key column of row block mi: 0, or the start of its chunk (chunked forward).
+  __device__ static int key0(const Params& p, int mi) {
+    return p.chunk > 0 ? (mi * S::BM / p.chunk) * p.chunk : 0;
+  }
   __device__ static int nt_for(const Params& p, int mi) {
-    return ceil_div_d(min(p.T, (mi + 1) * S::BM), BN);
+    return ceil_div_d(min(p.T, (mi + 1) * S::BM), BN) - key0(p, mi) / BN;
   }
   __device__ static int num_tiles(const Params& p) { return p.units * p.tiles_per_unit; }
   __device__ static Tile tile(const Params& p, int t) {
@@ -70,7 +75,7 @@ struct ScoreProb {
       r -= c;
     }
     tl.mi = mi;
-    tl.ni = r;
+    tl.ni = r + key0(p, mi) / BN;
     return tl;
   }
   __device__ static int k_blocks(const Params& p, const Tile&) { return ceil_div_d(p.K, S::BK); }
@@ -139,14 +144,16 @@ struct ScoreProb {
     const size_t unit_off = static_cast<size_t>(tl.unit) * p.T;
     // ---- direct store S[i][j] (vectorised unless it must skip the upper part of a diagonal tile)
     if (p.mode == kStoreDirect || p.mode == kStoreLU || (p.mode == kStoreSym && !diag)) {
-      const size_t row_off = (unit_off + gi) * static_cast<size_t>(p.ldp);
+      // chunked forward: columns are stored relative to the chunk's first key
+      const int cb = key0(p, tl.mi);
+      const size_t row_off = (unit_off + gi) * static_cast<size_t>(p.ldp) - static_cast<size_t>(cb);
       if (ELEM == 2) {
         uint16_t* dh = static_cast<uint16_t*>(p.p_hi) + row_off;
         uint16_t* dl = static_cast<uint16_t*>(p.p_lo) + row_off;
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           const int gj0 = gj_base + 8 * v;
-          if (gj0 + 8 > p.ldp) continue;
+          if (gj0 - cb + 8 > p.ldp) continue;
           *reinterpret_cast<uint4*>(dh + gj0) =
               make_uint4(hi[8 * v] | (hi[8 * v + 1] << 16), hi[8 * v + 2] | (hi[8 * v + 3] << 16),
                          hi[8 * v + 4] | (hi[8 * v + 5] << 16), hi[8 * v + 6] | (hi[8 * v + 7] << 16));
@@ -160,7 +167,7 @@ struct ScoreProb {
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           const int gj0 = gj_base + 4 * v;
-          if (gj0 + 4 > p.ldp) continue;
+          if (gj0 - cb + 4 > p.ldp) continue;
           *reinterpret_cast<uint4*>(dh + gj0) = make_uint4(hi[4 * v], hi[4 * v + 1], hi[4 * v + 2], hi[4 * v + 3]);
           *reinterpret_cast<uint4*>(dl + gj0) = make_uint4(lo[4 * v], lo[4 * v + 1], lo[4 * v + 2], lo[4 * v + 3]);
         }

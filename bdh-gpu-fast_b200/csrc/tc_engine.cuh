@@ -16,9 +16,24 @@
 // the MMA issues hi*hi (+ hi*lo + lo*hi) products; the lo*lo product is dropped.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace bdh {
+
+// Optional policy hooks (detected at compile time):
+//   P::stage_tx(prm, tile, kb) -> bytes the TMA loads of k-block kb deliver (default: all terms)
+//   P::epilogue_chunk(prm, tile, row, ch, nch, c0, r) -> called with the running fp32 sums
+//       after every accumulation chunk (KCHUNK > 0), instead of the final P::epilogue.
+template <class P, class = void>
+struct HasStageTx : std::false_type {};
+template <class P>
+struct HasStageTx<P, std::void_t<decltype(P::kVarStageTx)>> : std::true_type {};
+template <class P, class = void>
+struct HasChunkEmit : std::false_type {};
+template <class P>
+struct HasChunkEmit<P, std::void_t<decltype(P::kEmitEveryChunk)>> : std::true_type {};
 
 constexpr int kTcThreads = 192;
 constexpr int kEpiThreads = 128;
@@ -141,7 +156,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(full + stage, S::STAGE_BYTES);
+          uint32_t tx = S::STAGE_BYTES;
+          if constexpr (HasStageTx<P>::value) tx = P::stage_tx(prm, tile, kb);
+          mbar_arrive_expect_tx(full + stage, tx);
           uint8_t* a_dst = smem + stage * S::STAGE_BYTES;
           uint8_t* b_dst = a_dst + S::A_TERMS * S::A_TILE;
           P::load_stage(prm, tile, kb, full + stage, a_dst, b_dst);
@@ -278,14 +295,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           tc_fence_before();
           mbar_arrive(tempty + acc);
+          if constexpr (HasChunkEmit<P>::value) {
+#pragma unroll
+            for (int c0 = 0; c0 < BNC; c0 += 32) {
+              uint32_t r[32];
+#pragma unroll
+              for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(sum[c0 + e]);
+              P::epilogue_chunk(prm, tile, row, ch, nch, c0, r);
+            }
+          }
         }
         if (!ok) break;
+        if constexpr (!HasChunkEmit<P>::value) {
 #pragma unroll
-        for (int c0 = 0; c0 < BNC; c0 += 32) {
-          uint32_t r[32];
+          for (int c0 = 0; c0 < BNC; c0 += 32) {
+            uint32_t r[32];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(sum[c0 + e]);
-          P::epilogue(prm, tile, row, c0, r);
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(sum[c0 + e]);
+            P::epilogue(prm, tile, row, c0, r);
+          }
         }
       }
     }

@@ -51,6 +51,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.bdh_rope_rotate.argtypes = [_vp, ctypes.c_int, P, _vp, ctypes.c_int, P, _vp, _vp,
                                     _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _vp]
     lib.bdh_relu_mul.argtypes = [_vp, P, _vp, P, _vp, P, ctypes.c_int, _i64, _i64, _i64, _i64, _vp]
+    lib.bdh_set_forward_algo.argtypes = [ctypes.c_int]
+    lib.bdh_set_forward_algo.restype = ctypes.c_int
     lib.bdh_tril_score_v_workspace_size.restype = ctypes.c_size_t
     lib.bdh_tril_score_v_workspace_size.argtypes = [ctypes.c_int, _i64, _i64, _i64, _i64, _i64,
                                                     _i64, ctypes.c_int]
@@ -217,6 +219,18 @@ def _tma_ready(x: torch.Tensor) -> torch.Tensor:
     y = torch.zeros(*x.shape[:-1], npad, dtype=x.dtype, device=x.device)
     y[..., :n].copy_(x)
     return y
+
+
+FWD_ALGOS = {"auto": 0, "quadratic": 1, "chunked": 2}
+
+
+def set_forward_algo(algo: str) -> str:
+    """Select the forward form process-wide: ``auto`` (chunked for bf16 at T >= 1536),
+    ``quadratic`` or ``chunked``. Returns the previous setting."""
+    if algo not in FWD_ALGOS:
+        raise ValueError(f"forward algo must be one of {sorted(FWD_ALGOS)}, got {algo!r}")
+    prev = _require_lib().bdh_set_forward_algo(FWD_ALGOS[algo])
+    return {v: k for k, v in FWD_ALGOS.items()}[prev]
 
 
 # -------------------------------------------------------------------------- forward
@@ -439,4 +453,5 @@ __all__ = [
     "tril_score_v_bwd",
     "rope_rotate",
     "relu_mul",
+    "set_forward_algo",
 ]

@@ -137,12 +137,12 @@ def profile_end():
     import ctypes
 
     lib = _prof_lib()
-    ms = (ctypes.c_double * 8)()
-    cnt = (ctypes.c_int * 8)()
+    ms = (ctypes.c_double * 9)()
+    cnt = (ctypes.c_int * 9)()
     rc = lib.bdh_profile_end(ms, cnt)
     if rc != 0:
         raise RuntimeError(lib.bdh_last_error().decode())
-    kinds = ["score", "value", "rope", "decode", "grad_q", "grad_v", "split", "other"]
+    kinds = ["score", "value", "rope", "decode", "grad_q", "grad_v", "split", "gated_product", "state"]
     return {k: {"ms": ms[i], "launches": cnt[i]} for i, k in enumerate(kinds)}
 
 

@@ -77,6 +77,18 @@ int bdh_relu_mul(const void* x, const int64_t x_strides[4], const void* y,
                  const int64_t y_strides[4], void* out, const int64_t out_strides[4], int dtype,
                  int64_t B, int64_t H, int64_t T, int64_t N, void* stream);
 
+/*
+ * Forward algorithm selection (process-wide): BDH_FWD_AUTO picks the chunked form for bf16
+ * inputs when T >= 1536 (fewer flops: about T*C*(N+D) + 4*T*N*D per unit with C = 256 instead of
+ * T*T*(N+D)), else the quadratic form; the other values force one form (the chunked form needs
+ * bf16 inputs and falls back to quadratic for fp32). Returns the previous setting.
+ * No counterpart in the reference (its forward is always quadratic).
+ */
+#define BDH_FWD_AUTO 0
+#define BDH_FWD_QUADRATIC 1
+#define BDH_FWD_CHUNKED 2
+int bdh_set_forward_algo(int algo);
+
 /* Scratch bytes bdh_tril_score_v needs for these sizes (dtype of q/k/v). */
 size_t bdh_tril_score_v_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,
                                        int64_t N, int64_t D, int k_is_q);
@@ -168,9 +180,9 @@ int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* 
  * this library is bracketed by CUDA events on its own stream; end synchronises them and
  * returns the summed device milliseconds and launch counts per kernel kind:
  *   0 score pass, 1 value pass, 2 RoPE, 3 decode, 4 grad-Q pass, 5 grad-V pass, 6 split/transpose,
- *   7 gated product (bdh_relu_mul).
+ *   7 gated product (bdh_relu_mul), 8 state pass of the chunked forward.
  */
-#define BDH_PROF_KINDS 8
+#define BDH_PROF_KINDS 9
 int bdh_profile_begin(void);
 int bdh_profile_end(double ms[BDH_PROF_KINDS], int launches[BDH_PROF_KINDS]);
 

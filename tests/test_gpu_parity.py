@@ -400,3 +400,47 @@ def test_relu_mul_matches_torch_on_einsum_layouts(dt):
     out = sa().relu_mul(x, y)
     ref = torch.relu(x) * torch.relu(y)
     assert out.is_contiguous() and torch.equal(out, ref)
+
+
+# ------------------------------------------------------------- chunked long-T forward
+@pytest.fixture
+def chunked_algo():
+    prev = sa().set_forward_algo("chunked")
+    yield
+    sa().set_forward_algo(prev)
+
+
+@pytest.mark.parametrize("T", [257, 300, 512, 768, 1000])
+@pytest.mark.parametrize("Hv", [1, 2])
+def test_chunked_forward_vs_oracle(T, Hv, chunked_algo):
+    B, H, N, D = 1, 2, 512, 256
+    q = torch.relu(torch.randn(B, H, T, N, device=DEV)).to(torch.bfloat16)
+    v = torch.randn(B, Hv, T, D, device=DEV).to(torch.bfloat16)
+    out = sa().tril_score_v(q, q, v)
+    ref = O.tril_score_v(np64(q), np64(q), np64(v))
+    assert rel(out.float().cpu().numpy(), ref) <= 3e-3
+    assert torch.all(out[:, :, 0] == 0)
+
+
+def test_chunked_forward_distinct_k_permuted(chunked_algo):
+    B, H, T, N, D = 2, 2, 600, 256, 128
+    q = torch.relu(torch.randn(B, T, H, N, device=DEV)).to(torch.bfloat16).permute(0, 2, 1, 3)
+    k = torch.relu(torch.randn(B, T, H, N, device=DEV)).to(torch.bfloat16).permute(0, 2, 1, 3)
+    v = torch.randn(B, T, D, device=DEV).to(torch.bfloat16).unsqueeze(1)
+    out = sa().tril_score_v(q, k, v)
+    ref = O.tril_score_v(np64(q), np64(k), np64(v))
+    assert rel(out.float().cpu().numpy(), ref) <= 3e-3
+
+
+def test_chunked_forward_config3_shape_vs_fp64():
+    """Config-3 shapes for two (b, h) units: T = 8192, N = 8192, ~5% dense latents,
+    LayerNormed V; the automatic selection takes the chunked form at this length."""
+    B, H, T, N, D = 1, 2, 8192, 8192, 256
+    g = torch.Generator(device=DEV).manual_seed(3)
+    q = torch.relu(torch.randn(B, H, T, N, device=DEV, generator=g) - 1.645).to(torch.bfloat16)
+    v = torch.nn.functional.layer_norm(torch.randn(B, 1, T, D, device=DEV, generator=g), (D,)).to(torch.bfloat16)
+    out = sa().tril_score_v(q, q, v).double()
+    for h in range(H):
+        qd = q[0, h].double()
+        ref = (qd @ qd.T).tril(-1) @ v[0, 0].double()
+        assert ((out[0, h] - ref).norm() / ref.norm()).item() <= 3e-3
