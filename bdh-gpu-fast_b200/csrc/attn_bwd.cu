@@ -15,11 +15,13 @@
 // accuracy; bf16 Q/K/dO are used as stored (MN-major where needed), fp32 inputs use tf32
 // hi/lo copies laid out K-major.
 #include <algorithm>
+#include <cstdlib>
 
 #include "bdh_sm100.h"
 #include "internal.h"
 #include "score_pass.cuh"
 #include "tc_engine.cuh"
+#include "tc_pair_engine.cuh"
 #include "tma_host.h"
 
 namespace bdh {
@@ -241,6 +243,70 @@ struct GradVProb {
 };
 
 using GradQBf16 = GradQProb<2, 3>;
+
+// CTA-pair grad-Q pass: 256 (query rows) x 256 (latent columns) tiles; each CTA stages its 128
+// rows of the hi/lo score pair and its 128 columns of X (MN-major), and stores its 128 rows with
+// the single-CTA epilogue (including the RoPE adjoint).
+struct GradQPair {
+  using Base = GradQBf16;
+  using Params = Base::Params;  // b_map box 64 x BK as in the single-CTA pass
+  using S = PairShape<false, true, 2, 1, 4>;
+  struct Tile {
+    int unit, m, n;
+  };
+  __device__ static int mt2(const Params& p) { return ceil_div_d(p.T, 256); }
+  __device__ static int num_tiles(const Params& p) { return p.units * mt2(p) * p.nn; }
+  __device__ static Tile tile(const Params& p, int t) {
+    Tile tl;
+    const int per = mt2(p) * p.nn;
+    tl.unit = t / per;
+    const int r = t - tl.unit * per;
+    tl.m = r / p.nn;
+    tl.n = r - tl.m * p.nn;
+    return tl;
+  }
+  __device__ static int kb_begin(const Params& p, const Tile& tl) {
+    return p.krange == 2 ? (tl.m * 256) / 64 : 0;
+  }
+  __device__ static int k_blocks(const Params& p, const Tile& tl) {
+    const int end = p.krange == 1 ? ceil_div_d(min(p.T, (tl.m + 1) * 256), 64) : ceil_div_d(p.T, 64);
+    return end - kb_begin(p, tl);
+  }
+  __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x3u; }
+  __device__ static uint32_t stage_tx(const Params&, const Tile&, int) { return 2 * S::STAGE_BYTES; }
+  __device__ static void prefetch(const Params& p) {
+    tma_prefetch_desc(&p.a_map[0]);
+    tma_prefetch_desc(&p.a_map[1]);
+    tma_prefetch_desc(&p.b_map[0]);
+  }
+  __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint32_t rank,
+                                    uint32_t bar, uint8_t* a_dst, uint8_t* b_dst) {
+    const int j0 = (kb + kb_begin(p, tl)) * 64;
+    const int r128 = static_cast<int>(rank) * 128;
+    for (int i = 0; i < 2; ++i)
+      tma_load_4d_pair(&p.a_map[i], bar, a_dst + i * S::A_TILE, j0, tl.m * 256 + r128, tl.unit, 0);
+    const int b = tl.unit / p.H, h = tl.unit - (tl.unit / p.H) * p.H;
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+      tma_load_4d_pair(&p.b_map[0], bar, b_dst + c * 64 * 128, tl.n * 256 + r128 + c * 64, j0, h, b);
+  }
+  __device__ static void epilogue(const Params& p, const Tile& tl, int rank, int row, int c0,
+                                  const uint32_t (&r)[32]) {
+    Base::Tile t;
+    t.unit = tl.unit;
+    t.mi = 2 * tl.m + rank;
+    t.ni = tl.n;
+    Base::epilogue(p, t, row, c0, r);
+  }
+};
+
+bool use_pairs_bwd() {
+  static int on = [] {
+    const char* e = std::getenv("BDH_SM100_PAIR");
+    return (e != nullptr && std::atoi(e) == 0) ? 0 : 1;
+  }();
+  return on != 0;
+}
 using GradQTf32 = GradQProb<4, 3>;
 using GradVBf16 = GradVProb<2, 3>;
 using GradVTf32 = GradVProb<4, 3>;
@@ -290,6 +356,12 @@ int launch_grad_q(const GradQArgs& a, cudaStream_t stream, int* err) {
     prm.err = err;
     return true;
   };
+  if (elem == 2 && use_pairs_bwd()) {
+    GradQPair::Params prm{};
+    if (!fill(prm, GradQBf16::S::BK, GradQBf16::BN)) return BDH_ERR_INVALID;
+    const int tiles = prm.units * static_cast<int>((a.T + 255) / 256) * prm.nn;
+    return launch_pair<GradQPair::S, GradQPair>(prm, tiles, stream, kProfGradQ);
+  }
   if (elem == 2) {
     GradQBf16::Params prm{};
     if (!fill(prm, GradQBf16::S::BK, GradQBf16::BN)) return BDH_ERR_INVALID;

@@ -12,11 +12,13 @@
 // (kernels/attention.py:27-40): no softmax, no scale, diagonal excluded, V broadcast over
 // heads when it has one head.
 #include <algorithm>
+#include <cstdlib>
 
 #include "bdh_sm100.h"
 #include "internal.h"
 #include "score_pass.cuh"
 #include "tc_engine.cuh"
+#include "tc_pair_engine.cuh"
 #include "tma_host.h"
 
 namespace bdh {
@@ -125,6 +127,81 @@ struct ValueProb {
 
 // ----------------------------------------------------------------- launchers ----
 using ScoreBf16 = ScoreProb<2, 128, 6>;
+using ScoreBf16Wide = ScoreProb<2, 256, 4>;  // 128 x 256 tiles: 25% fewer operand bytes per flop
+
+// CTA-pair score pass: 256 x 256 tiles (each CTA 128 query rows x all 256 keys of the tile in
+// TMEM, staging 128 query rows and 128 key rows per stage). Epilogue and parameters are those of
+// the single-CTA 128 x 256 score pass, applied to each CTA's 128-row half.
+struct ScorePair {
+  using Base = ScoreBf16Wide;
+  using Params = Base::Params;  // b_map box is 64 x 128 (one CTA's key rows)
+  using S = PairShape<false, false, 1, 1, 6>;
+  struct Tile {
+    int unit, m, n;  // 256-row query block, 256-key block
+  };
+  __device__ static int key0(const Params& p, int m) {
+    return p.chunk > 0 ? (m * 256 / p.chunk) * p.chunk : 0;
+  }
+  __device__ static int nt_for(const Params& p, int m) {
+    return ceil_div_d(min(p.T, (m + 1) * 256), 256) - key0(p, m) / 256;
+  }
+  __device__ static int num_tiles(const Params& p) { return p.units * p.tiles_per_unit; }
+  __device__ static Tile tile(const Params& p, int t) {
+    Tile tl;
+    tl.unit = t / p.tiles_per_unit;
+    int r = t - tl.unit * p.tiles_per_unit;
+    int m = 0;
+    for (;; ++m) {
+      const int c = nt_for(p, m);
+      if (r < c) break;
+      r -= c;
+    }
+    tl.m = m;
+    tl.n = r + key0(p, m) / 256;
+    return tl;
+  }
+  __device__ static int k_blocks(const Params& p, const Tile&) { return ceil_div_d(p.K, 64); }
+  __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x1u; }
+  __device__ static uint32_t stage_tx(const Params&, const Tile&, int) { return 2 * S::STAGE_BYTES; }
+  __device__ static void prefetch(const Params& p) {
+    tma_prefetch_desc(&p.a_map[0]);
+    tma_prefetch_desc(&p.b_map[0]);
+  }
+  __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint32_t rank,
+                                    uint32_t bar, uint8_t* a_dst, uint8_t* b_dst) {
+    const int b = tl.unit / p.H, h = tl.unit - (tl.unit / p.H) * p.H;
+    const int hb = p.b_shared ? 0 : h;
+    const int r128 = static_cast<int>(rank) * 128;
+    tma_load_4d_pair(&p.a_map[0], bar, a_dst, kb * 64, tl.m * 256 + r128, h, b);
+    tma_load_4d_pair(&p.b_map[0], bar, b_dst, kb * 64, tl.n * 256 + r128, hb, b);
+  }
+  __device__ static void epilogue(const Params& p, const Tile& tl, int rank, int row, int c0,
+                                  const uint32_t (&r)[32]) {
+    Base::Tile t;
+    t.unit = tl.unit;
+    t.mi = 2 * tl.m + rank;
+    t.ni = tl.n;
+    Base::epilogue(p, t, row, c0, r);
+  }
+};
+
+// CTA pairs for the bf16 tensor passes (BDH_SM100_PAIR=0 selects single-CTA tiles instead).
+bool use_pairs() {
+  static int on = [] {
+    const char* e = std::getenv("BDH_SM100_PAIR");
+    return (e != nullptr && std::atoi(e) == 0) ? 0 : 1;
+  }();
+  return on != 0;
+}
+
+// Score-pass tile width for bf16: 128 or 256 keys (BDH_SM100_SCORE_BN, read once; default 128).
+int score_tile_n() {
+  static int bn = [] {
+    const char* e = std::getenv("BDH_SM100_SCORE_BN");
+    return (e != nullptr && std::atoi(e) == 256) ? 256 : 128;
+  }();
+  return bn;
+}
 using ScoreTf32 = ScoreProb<4, 128, 3>;
 using ValueBf16 = ValueProb<2, 3>;
 using ValueTf32 = ValueProb<4, 3>;
@@ -167,7 +244,24 @@ int launch_score_pass(const ScoreArgs& a, cudaStream_t stream, int* err) {
     prm.err = err;
     return true;
   };
-  if (elem == 2) {
+  if (elem == 2 && use_pairs()) {
+    ScorePair::Params prm{};
+    if (!fill(prm, 64, 128)) return BDH_ERR_INVALID;
+    int tpu = 0;  // pair tiles per unit (256 x 256)
+    for (int m = 0; m < (a.T + 255) / 256; ++m) {
+      const int64_t lim = std::min<int64_t>(a.T, int64_t(m + 1) * 256);
+      const int64_t k0 = a.chunk > 0 ? (int64_t(m) * 256 / a.chunk) * a.chunk : 0;
+      tpu += static_cast<int>((lim + 255) / 256 - k0 / 256);
+    }
+    prm.tiles_per_unit = tpu;
+    return launch_pair<ScorePair::S, ScorePair>(prm, prm.units * tpu, stream, kProfScore);
+  }
+  if (elem == 2 && score_tile_n() == 256) {
+    ScoreBf16Wide::Params prm{};
+    if (!fill(prm, ScoreBf16Wide::S::BK, 256)) return BDH_ERR_INVALID;
+    return launch_tc<ScoreBf16Wide::S, ScoreBf16Wide>(prm, prm.units * prm.tiles_per_unit, stream,
+                                                      kProfScore);
+  } else if (elem == 2) {
     ScoreBf16::Params prm{};
     if (!fill(prm, ScoreBf16::S::BK, 128)) return BDH_ERR_INVALID;
     return launch_tc<ScoreBf16::S, ScoreBf16>(prm, prm.units * prm.tiles_per_unit, stream, kProfScore);

@@ -26,7 +26,9 @@ namespace {
 
 constexpr int kDecThreads = 256;
 constexpr int kDecWarps = kDecThreads / 32;
-constexpr int kDecRows = 64;  // cached rows per CTA
+constexpr int kDecRowsMax = 128;  // cached rows per CTA: 64 for fp32 caches, 128 for bf16 (same bytes)
+
+__host__ __device__ constexpr int dec_rows(int kv_elem_bytes) { return kv_elem_bytes == 4 ? 64 : 128; }
 
 __device__ __forceinline__ float bf16_round_d(float x) { return bf16_round_f32(x); }
 
@@ -118,6 +120,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_partial_kernel(
     int H, int Hv, int Tq, int S, int N, int D, int64_t qsb, int64_t qsh, int64_t qst,
     int64_t ksb, int64_t ksh, int64_t kst, int64_t vsb, int64_t vsh, int64_t vst, int64_t ssb,
     int64_t ssh, int64_t sst, int64_t pos) {
+  constexpr int kDecRows = dec_rows(sizeof(TK));
   extern __shared__ float dsm[];
   float* qs = dsm;              // N floats
   float* sc = dsm + N;          // kDecRows scores
@@ -181,6 +184,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_partial_kernel(
   float* dst = partial + ((static_cast<int64_t>(split) * gridDim.y + bh) * Tq + tq) * D;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float acc = 0.f;
+#pragma unroll 8
     for (int r = 0; r < rows; ++r) acc = fmaf(sc[r], ld_elem(vbase + (j0 + r) * vst, d), acc);
     dst[d] = acc;
   }
@@ -206,17 +210,22 @@ __global__ void decode_reduce_kernel(const float* __restrict__ partial, TO* __re
 
 }  // namespace
 
-int decode_splits(int64_t S) { return static_cast<int>(std::max<int64_t>(1, (S + kDecRows - 1) / kDecRows)); }
+int decode_splits(int64_t S, int kv_dtype) {
+  const int rows = dec_rows(kv_dtype == BDH_DTYPE_F32 ? 4 : 2);
+  return static_cast<int>(std::max<int64_t>(1, (S + rows - 1) / rows));
+}
 
+// Sized for the most splits any cache dtype uses (fp32: 64 rows per split).
 size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t D) {
-  return static_cast<size_t>(decode_splits(S)) * static_cast<size_t>(B * H * Tq * D) * sizeof(float);
+  return static_cast<size_t>(decode_splits(S, BDH_DTYPE_F32)) * static_cast<size_t>(B * H * Tq * D) *
+         sizeof(float);
 }
 
 int launch_decode(const DecodeArgs& a, float* partial, cudaStream_t stream) {
   if (a.B * a.H * a.Tq == 0 || a.D == 0) {
     return BDH_OK;
   }
-  const int nsplit = decode_splits(a.S);
+  const int nsplit = decode_splits(a.S, a.kv_dtype);
   const int ke = a.kv_dtype == BDH_DTYPE_F32 ? 4 : 2;
   bool vec = (a.N % (16 / ke) == 0) && ((reinterpret_cast<uintptr_t>(a.k) & 15u) == 0) &&
              (a.k_strides[0] * ke) % 16 == 0 && (a.k_strides[1] * ke) % 16 == 0 &&
@@ -227,7 +236,7 @@ int launch_decode(const DecodeArgs& a, float* partial, cudaStream_t stream) {
   }
   const dim3 grid(static_cast<unsigned>(nsplit), static_cast<unsigned>(a.B * a.H),
                   static_cast<unsigned>(a.Tq));
-  const size_t smem = (static_cast<size_t>(a.N) + kDecRows) * sizeof(float);
+  const size_t smem = (static_cast<size_t>(a.N) + kDecRowsMax) * sizeof(float);
   if (smem > 200 * 1024) {
     set_error("decode: latent width too large for the shared-memory q stage");
     return BDH_ERR_INVALID;

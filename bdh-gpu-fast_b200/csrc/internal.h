@@ -138,7 +138,7 @@ struct DecodeArgs {
   void* slot = nullptr;
   int64_t slot_strides[4] = {0, 0, 0, 1};
 };
-int decode_splits(int64_t S);
+int decode_splits(int64_t S, int kv_dtype);
 size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t D);
 int launch_decode(const DecodeArgs& a, float* partial, cudaStream_t stream);
 

@@ -179,8 +179,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer
+    // The issue loop is kept lean: at N = 128 one MMA covers only 64 tensor cycles, so every
+    // scalar instruction of this thread is on the critical path. Descriptors are built once
+    // and advanced by adding the 16-byte-unit offset of each stage / K slice to their low field.
     if (elect_one()) {
+      const uint32_t base = smem_u32(smem);
+      const uint64_t a0 = S::a_desc(base);
+      const uint64_t b0 = S::b_desc(base + S::A_TERMS * S::A_TILE);
       int stage = 0;
+      uint32_t soff16 = 0;  // stage * STAGE_BYTES / 16
       uint32_t ph = 0;
       int lc = 0;  // accumulation chunks issued by this CTA (selects the TMEM buffer)
       bool ok = true;
@@ -205,8 +212,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t a_base = smem_u32(smem + stage * S::STAGE_BYTES);
-            const uint32_t b_base = a_base + S::A_TERMS * S::A_TILE;
             const uint32_t pair_mask = P::pair_mask(prm, tile, kb);
 #pragma unroll
             for (int kk = 0; kk < S::BK / S::UK; ++kk) {
@@ -216,8 +221,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 // pair 0: A0*B0; pair 1: A1*B0 (or A0*B1 when only B is split); pair 2: A0*B1
                 const int ta = (pr == 1 && S::A_TERMS == 2) ? 1 : 0;
                 const int tb = (pr == 2 || (pr == 1 && S::A_TERMS == 1)) ? 1 : 0;
-                const uint64_t ad = S::a_desc(a_base + ta * S::A_TILE + S::a_koff(kk));
-                const uint64_t bd = S::b_desc(b_base + tb * S::B_TILE + S::b_koff(kk));
+                const uint64_t ad = a0 + (soff16 + ((ta * S::A_TILE + S::a_koff(kk)) >> 4));
+                const uint64_t bd = b0 + (soff16 + ((tb * S::B_TILE + S::b_koff(kk)) >> 4));
                 const uint32_t accumulate = (kb > kb0 || kk > 0 || pr > 0) ? 1u : 0u;
                 if (S::ELEM == 2)
                   umma_f16(d_tmem, ad, bd, S::IDESC, accumulate);
@@ -228,7 +233,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             umma_commit(empty + stage);
             if (++stage == S::STAGES) {
               stage = 0;
+              soff16 = 0;
               ph ^= 1u;
+            } else {
+              soff16 += S::STAGE_BYTES >> 4;
             }
           }
           if (!ok) break;

@@ -347,18 +347,18 @@ def bench_config2(args, world, rank, dev):
 
 
 # ----------------------------------------------------------- standalone op configs
-def _op_inputs(cfg_id, dev, rank):
+def _op_inputs(cfg_id, dev, rank, batch=0):
     g = torch.Generator(device=dev).manual_seed(rank_seed(1000 + cfg_id, rank))
     if cfg_id == 1:
-        B, H, T, N, D, dt = 4, 4, 512, N_LAT, D_MODEL, torch.float32
+        B, H, T, N, D, dt = batch or 4, 4, 512, N_LAT, D_MODEL, torch.float32
         q = torch.relu(torch.randn(B, H, T, N, device=dev, generator=g))
         v = torch.randn(B, 1, T, D, device=dev, generator=g)
     elif cfg_id == 3:
-        B, H, T, N, D, dt = 8, 4, 8192, N_LAT, D_MODEL, torch.bfloat16
+        B, H, T, N, D, dt = batch or 8, 4, 8192, N_LAT, D_MODEL, torch.bfloat16
         q = torch.relu(torch.randn(B, H, T, N, device=dev, generator=g) - 1.645).to(dt)
         v = torch.nn.functional.layer_norm(torch.randn(B, 1, T, D, device=dev, generator=g), (D,)).to(dt)
     else:  # 5
-        B, H, T, N, D, dt = 16, 4, 2048, N_LAT, D_MODEL, torch.bfloat16
+        B, H, T, N, D, dt = batch or 16, 4, 2048, N_LAT, D_MODEL, torch.bfloat16
         q = torch.relu(torch.randn(B, H, T, N, device=dev, generator=g)).to(dt)
         v = torch.randn(B, 1, T, D, device=dev, generator=g).to(dt)
     return q, v, (B, H, T, N, D, dt)
@@ -369,7 +369,7 @@ def bench_op(args, world, rank, dev):
     from kernels.attention_dispatch import bdh_rope_attn
 
     cfg_id = args.config
-    q, v, (B, H, T, N, D, dt) = _op_inputs(cfg_id, dev, rank)
+    q, v, (B, H, T, N, D, dt) = _op_inputs(cfg_id, dev, rank, args.batch)
     freqs = bdh_model.get_freqs(N, 2 ** 16, torch.float32).to(dev)
     if cfg_id == 5:
         dO = torch.randn(B, H, T, D, device=dev).to(dt)
@@ -392,16 +392,23 @@ def bench_op(args, world, rank, dev):
     ms = timed(step, args.steps, world, dev)
     prof = profile_end()
     clk = clocks.stop()
-    fwd = B * H * T * (T - 1) * (N + D)
+    # executed-algorithm flops (per (b,h) unit): quadratic causal T(T-1)(N+D), or the chunked
+    # form (T/C) C(C-1)(N+D) + 4 (T-C) N D when the library takes it (bf16 and T >= 1536)
+    C = 256
+    chunked = dt == torch.bfloat16 and T >= 1536
+    quad_fwd = B * H * T * (T - 1) * (N + D)
+    fwd = B * H * ((T // C) * C * (C - 1) * (N + D) + 4 * (T - C) * N * D) if chunked else quad_fwd
     bwd = B * H * T * (T - 1) * (3 * N + 2 * D) if cfg_id == 5 else 0
     flops = (fwd + bwd) * args.steps * world
+    effective = (quad_fwd + bwd) * args.steps * world
     peaks, src = load_peaks()
     sc = prof["score"]
-    per_launch = None
-    if sc["launches"]:
-        per_launch = sc["ms"] / sc["launches"]
+    per_launch = sc["ms"] / sc["launches"] if sc["launches"] else None
     line = {
-        "metric": f"tril-attn TFLOP/s (config {cfg_id}, causal flops)", "value": flops / (ms / 1e3) / 1e12,
+        "metric": f"tril-attn TFLOP/s (config {cfg_id}, executed-algorithm causal flops)",
+        "value": flops / (ms / 1e3) / 1e12,
+        "effective_tflops_quadratic_equivalent": effective / (ms / 1e3) / 1e12,
+        "forward_form": "chunked C=256" if chunked else "quadratic",
         "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32" if dt == torch.float32 else "bf16", "data": "synthetic",
@@ -499,7 +506,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode-bf16", action="store_true")
     ap.add_argument("--batch", type=int, default=0,
-                    help="config 2 per-GPU batch override (profiling aid; default 32)")
+                    help="per-GPU batch override (profiling aid; defaults: the config's own)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl != "reference":
         args.warmup = 3
