@@ -32,18 +32,24 @@ namespace {
 constexpr int kChunk = 256;
 
 // ------------------------------------------------------------------- state pass ----
+// Each tile is a 128 (latent) x 128 (value) block of the N x D state; its epilogue emits one
+// bf16 hi/lo prefix per chunk (64 KB per tile per chunk), so the pass is bound by HBM writes.
+// Every epilogue warp stages its 32 rows in shared memory in the 128B-swizzled layout of the
+// store tensor map and writes them with four TMA bulk stores (whole 128-byte lines), then
+// reuses the staging once the previous chunk's stores have read it.
 template <int STAGES>
 struct StateProb {
   using S = TcShape<2, 128, true, true, 1, 1, STAGES, kChunk / 64>;
   static constexpr int kEmitEveryChunk = 1;
+  static constexpr int kWarpStage = 4 * 32 * 128;  // hi/lo x two 64-column boxes x 32 rows
+  static constexpr int kEpiSmemBytes = 4 * kWarpStage;
   struct Params {
     CUtensorMap a_map[1];  // K (B,H,T,N) read MN-major: box 64 (n) x 64 (t)
     CUtensorMap b_map[1];  // V (B,Hv,T,D) read MN-major: box 64 (d) x 64 (t)
+    CUtensorMap s_map[2];  // S hi/lo over [units][nchunks][N][D], store box 64 (d) x 32 (n)
     int H, Hv, T, N, D;
     int nn, nd;            // 128-wide latent / value tiles
     int units, nchunks;
-    uint16_t* s_hi;        // [units][nchunks][N][D]
-    uint16_t* s_lo;
     int* err;
   };
   struct Tile {
@@ -78,16 +84,20 @@ struct StateProb {
   }
   __device__ static void epilogue(const Params&, const Tile&, int, int, const uint32_t (&)[32]) {}
   // After chunk ch the running sum is S_ch, the prefix state of chunk ch + 1.
-  __device__ static void epilogue_chunk(const Params& p, const Tile& tl, int row, int ch, int nch,
-                                        int c0, const uint32_t (&r)[32]) {
-    const int n = tl.ni * 128 + row;
-    const int d0 = tl.di * 128 + c0;
-    if (n >= p.N || d0 >= p.D) return;
-    const size_t off = ((static_cast<size_t>(tl.unit) * p.nchunks + (ch + 1)) * p.N + n) *
-                           static_cast<size_t>(p.D) + d0;
-    uint16_t* dh = p.s_hi + off;
-    uint16_t* dl = p.s_lo + off;
-    const bool vec = d0 + 32 <= p.D && (p.D % 8) == 0;
+  __device__ static void epilogue_chunk(const Params& p, const Tile& tl, int row, int ch, int,
+                                        int c0, const uint32_t (&r)[32], uint8_t* epi) {
+    const int quad = row >> 5, lr = row & 31;
+    const bool leader = lr == 0;
+    uint8_t* st = epi + quad * kWarpStage;
+    if (c0 == 0) {
+      // the previous chunk's stores must have read the staging before it is overwritten
+      if (leader) bulk_wait_read_all();
+      __syncwarp();
+    }
+    const int half = c0 >> 6;
+    const int j0 = (c0 & 63) >> 3;
+    uint8_t* hi_row = st + half * 4096 + lr * 128;
+    uint8_t* lo_row = hi_row + 2 * 4096;
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
       uint32_t wh[4], wl[4];
@@ -97,17 +107,30 @@ struct StateProb {
         wh[e] = cvt_bf16x2(x0, x1);
         wl[e] = cvt_bf16x2(x0 - bf16x2_lo(wh[e]), x1 - bf16x2_hi(wh[e]));
       }
-      if (vec) {
-        *reinterpret_cast<uint4*>(dh + 8 * v) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
-        *reinterpret_cast<uint4*>(dl + 8 * v) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
-      } else {
-        for (int e = 0; e < 8 && d0 + 8 * v + e < p.D; ++e) {
-          dh[8 * v + e] = static_cast<uint16_t>(wh[e / 2] >> (16 * (e & 1)));
-          dl[8 * v + e] = static_cast<uint16_t>(wl[e / 2] >> (16 * (e & 1)));
+      const int sw = ((j0 + v) ^ (lr & 7)) << 4;
+      *reinterpret_cast<uint4*>(hi_row + sw) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+      *reinterpret_cast<uint4*>(lo_row + sw) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+    }
+    if (c0 + 32 == S::BN) {
+      fence_async_smem();
+      __syncwarp();
+      const int n0 = tl.ni * 128 + quad * 32;
+      if (leader && n0 < p.N) {
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          const int x = tl.di * 128 + hb * 64;
+          if (x < p.D) {
+            tma_store_4d(&p.s_map[0], st + hb * 4096, x, n0, ch + 1, tl.unit);
+            tma_store_4d(&p.s_map[1], st + (2 + hb) * 4096, x, n0, ch + 1, tl.unit);
+          }
         }
+        bulk_commit();
       }
     }
-    (void)nch;
+  }
+  __device__ static void epilogue_end(const Params&, int row, uint8_t*) {
+    if ((row & 31) == 0) bulk_wait_all();
+    __syncwarp();
   }
 };
 
@@ -215,7 +238,7 @@ struct ChunkValueProb {
   }
 };
 
-using StateBf16 = StateProb<6>;
+using StateBf16 = StateProb<4>;
 using ChunkValueBf16 = ChunkValueProb<3>;
 
 }  // namespace
@@ -272,8 +295,10 @@ int launch_chunked_forward(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi,
     prm.nd = static_cast<int>((a.D + 127) / 128);
     prm.units = static_cast<int>(units);
     prm.nchunks = nchunks;
-    prm.s_hi = static_cast<uint16_t*>(s_hi);
-    prm.s_lo = static_cast<uint16_t*>(s_lo);
+    const int64_t sd[4] = {a.D, a.N, nchunks, units};
+    const int64_t ss[3] = {a.D * 2, a.N * a.D * 2, int64_t(nchunks) * a.N * a.D * 2};
+    if (!make_map_4d(&prm.s_map[0], s_hi, 2, sd, ss, 64, 32, "state pass: S hi")) return BDH_ERR_INVALID;
+    if (!make_map_4d(&prm.s_map[1], s_lo, 2, sd, ss, 64, 32, "state pass: S lo")) return BDH_ERR_INVALID;
     prm.err = err;
     rc = launch_tc<StateBf16::S, StateBf16>(prm, prm.units * prm.nn * prm.nd, stream, kProfState);
     if (rc) return rc;

@@ -210,7 +210,7 @@ static int launch_tc(const typename P::Params& prm, int ntiles, cudaStream_t str
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<S, P>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         S::SMEM_BYTES);
+                                         tc_smem_bytes<S, P>());
     if (e != cudaSuccess) {
       set_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
       return BDH_ERR_CUDA;
@@ -219,7 +219,7 @@ static int launch_tc(const typename P::Params& prm, int ntiles, cudaStream_t str
   }
   const int grid = std::min(ntiles, sm_count(dev));
   prof_start(kind, stream);
-  tc_gemm_kernel<S, P><<<grid, kTcThreads, S::SMEM_BYTES, stream>>>(prm);
+  tc_gemm_kernel<S, P><<<grid, kTcThreads, tc_smem_bytes<S, P>(), stream>>>(prm);
   prof_stop(kind, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

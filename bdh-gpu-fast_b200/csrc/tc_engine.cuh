@@ -34,6 +34,17 @@ template <class P, class = void>
 struct HasChunkEmit : std::false_type {};
 template <class P>
 struct HasChunkEmit<P, std::void_t<decltype(P::kEmitEveryChunk)>> : std::true_type {};
+//   P::kEpiSmemBytes -> shared memory reserved for the epilogue warps (1024-aligned), passed to
+//       P::epilogue_chunk(..., epi) and P::epilogue_end(prm, row, epi) (called once per thread
+//       after the tile loop, e.g. to drain bulk stores reading that memory).
+template <class P, class = void>
+struct EpiSmem {
+  static constexpr int value = 0;
+};
+template <class P>
+struct EpiSmem<P, std::void_t<decltype(P::kEpiSmemBytes)>> {
+  static constexpr int value = P::kEpiSmemBytes;
+};
 
 constexpr int kTcThreads = 192;
 constexpr int kEpiThreads = 128;
@@ -90,6 +101,14 @@ struct TcShape {
   }
 };
 
+// Dynamic shared memory of one CTA: the stage ring, a 1 KB barrier block, the epilogue's own
+// region (if any) and 1 KB of alignment slack.
+template <class S, class P>
+constexpr int tc_smem_bytes() {
+  return EpiSmem<P>::value == 0 ? S::SMEM_BYTES
+                                : S::STAGES * S::STAGE_BYTES + 1024 + EpiSmem<P>::value + 1024;
+}
+
 // Spin on `bar` ignoring the abort flag (used to drain in-flight async work before exit).
 __device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -106,6 +125,7 @@ __device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity, int* 
 template <class S, class P>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ typename P::Params prm) {
+  static_assert(tc_smem_bytes<S, P>() <= 232448, "shared memory budget");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -251,6 +271,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---------------------------------------------------------------- epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + static_cast<int>(lane_id());
+    uint8_t* epi = smem + S::STAGES * S::STAGE_BYTES + 1024;
+    (void)epi;
     int lc = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -309,7 +331,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               uint32_t r[32];
 #pragma unroll
               for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(sum[c0 + e]);
-              P::epilogue_chunk(prm, tile, row, ch, nch, c0, r);
+              P::epilogue_chunk(prm, tile, row, ch, nch, c0, r, epi);
             }
           }
         }
@@ -325,6 +347,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
     }
+    if constexpr (HasChunkEmit<P>::value) P::epilogue_end(prm, row, epi);
   }
 
   tc_fence_before();
