@@ -25,6 +25,7 @@ from __future__ import annotations
 
 import dataclasses
 import math
+import os
 from typing import Optional
 
 import torch
@@ -152,6 +153,59 @@ class BDH(nn.Module):
     def _ln(self, x: torch.Tensor) -> torch.Tensor:
         return F.layer_norm(x, (x.size(-1),), eps=self.ln.eps)
 
+    def _bf16_param(self, name: str) -> torch.Tensor:
+        """bf16 copy of a parameter, refreshed when the parameter changes (the cast that
+        autocast would make on every use)."""
+        p = getattr(self, name)
+        if p.dtype == torch.bfloat16:
+            return p
+        cache = self.__dict__.setdefault("_bf16_cache", {})
+        key = (p.data_ptr(), p._version, p.device)
+        hit = cache.get(name)
+        if hit is None or hit[0] != key:
+            hit = (key, p.detach().to(torch.bfloat16))
+            cache[name] = hit
+        return hit[1]
+
+    def _latent_fusable(self, impl: str, T: int, cache, device) -> bool:
+        """The fused encode / gate kernels serve bf16 prefill blocks without a past."""
+        if impl != "cuda_sm100" or T < 64 or device.type != "cuda":
+            return False
+        if torch.is_grad_enabled() or (self.training and self.drop.p != 0.0):
+            return False
+        if cache is not None and cache.seq_len != 0:
+            return False
+        bf16 = (torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16) \
+            or self.encoder.dtype == torch.bfloat16
+        return bf16 and os.environ.get("BDH_SM100_LATENT", "1") != "0"
+
+    def _layer_latent(self, x: torch.Tensor, level: int, rope_start: int, cache) -> torch.Tensor:
+        """One layer on the fused latent kernels: encode (+ReLU +RoPE) -> tril attention ->
+        LN -> encoder_v gate (xs * relu(.)) -> decoder -> residual LN. Same arithmetic as the
+        bf16-autocast layer of bdh.py:991-1052."""
+        from kernels.sm100_attn import latent_encode, latent_gate, tril_score_v
+
+        B, T, _ = x.shape
+        nh = self.config.n_head
+        xb = x.to(torch.bfloat16)
+        v_tok = x.unsqueeze(1)
+        qr_slot = None
+        dst_kr = None
+        if cache is not None:
+            dst_kr, dst_v = cache.reserve(level, T)
+            dst_v.copy_(v_tok)
+            if dst_kr.dtype == torch.bfloat16:
+                qr_slot = dst_kr
+        xs, qr = latent_encode(xb, self._bf16_param("encoder"), self.attn.freqs, rope_start,
+                               qr_out=qr_slot)
+        if dst_kr is not None and qr_slot is None:
+            dst_kr.copy_(qr)
+        y_kv = tril_score_v(qr, qr, v_tok.to(torch.bfloat16))
+        yn = self._ln(y_kv.float()).to(torch.bfloat16)
+        xy = latent_gate(yn, self._bf16_param("encoder_v"), xs)
+        y_mlp = F.linear(xy.view(B, T, nh * xy.size(-1)), self._bf16_param("decoder").t())
+        return self._ln(x + self._ln(y_mlp))
+
     def forward(self, idx: torch.Tensor, targets: Optional[torch.Tensor] = None,
                 cache: Optional[CacheManager] = None, *, logits_out: Optional[torch.Tensor] = None):
         """Logits ``(B, T, V)`` (and the CE loss with ``targets``).
@@ -170,7 +224,11 @@ class BDH(nn.Module):
         # Inference on B200: both ReLUs are folded into native kernels (the RoPE read and the
         # gated product), so the latents are never rewritten just to clamp them.
         fused = impl == "cuda_sm100" and not grad and (not self.training or self.drop.p == 0.0)
+        latent = self._latent_fusable(impl, T, cache, x.device)
         for level in range(C.n_layer):
+            if latent:
+                x = self._layer_latent(x, level, rope_start, cache)
+                continue
             x_lat = torch.einsum("btd,hdn->bthn", x, self.encoder)  # (B, T, nh, N)
             x_bthn = x_lat if fused else F.relu(x_lat)
             x_sparse = x_bthn.permute(0, 2, 1, 3)  # (B, nh, T, N) view

@@ -28,13 +28,6 @@ namespace bdh {
 
 namespace {
 
-__device__ __forceinline__ void rope_cis_bwd(float pos, float f, float& c, float& s) {
-  float ph = __fmul_rn(pos, f);
-  ph = __fsub_rn(ph, floorf(ph));
-  ph = __fmul_rn(ph, __int_as_float(0x40C90FDB));
-  sincosf(ph, &s, &c);
-}
-
 // Store 32 consecutive fp32 values of one output row (bf16 or fp32, vectorised when aligned).
 __device__ __forceinline__ void store_row32(void* base, int64_t off, bool f32, bool vec, int valid,
                                             const float (&v)[32]) {
@@ -145,12 +138,12 @@ struct GradQProb {
         if (n >= p.N) break;
         float cc0, ss0, cc1, ss1;
         const float f0 = __ldg(p.freqs + n), f1 = __ldg(p.freqs + n + 1);
-        rope_cis_bwd(pos, f0, cc0, ss0);
+        rope_cis(pos, f0, cc0, ss0);
         if (f1 == f0) {
           cc1 = cc0;
           ss1 = ss0;
         } else {
-          rope_cis_bwd(pos, f1, cc1, ss1);
+          rope_cis(pos, f1, cc1, ss1);
         }
         const float g0 = v[e], g1 = v[e + 1];
         v[e] = fmaf(g0, cc0, g1 * ss1);

@@ -144,6 +144,27 @@ bool check_rows(const char* what, const int64_t s[4], int elem, std::string* msg
   return true;
 }
 
+bool strides_ok(const int64_t* s, int n) {
+  if (s[n - 1] != 1) return false;
+  for (int i = 0; i < n - 1; ++i)
+    if (s[i] <= 0 || (s[i] % 8) != 0) return false;
+  return true;
+}
+bool latent_sizes_ok(int64_t B, int64_t T, int64_t H, int64_t D, int64_t N, std::string* msg) {
+  if (B < 0 || T < 0 || H < 0 || D < 0 || N < 0) {
+    *msg = "negative size";
+    return false;
+  }
+  if ((N % 2) != 0) {
+    *msg = "latent width N must be even (RoPE pairs)";
+    return false;
+  }
+  if (B * H * ((T + 127) / 128) * ((N + 127) / 128) >= (int64_t(1) << 31) || T >= (int64_t(1) << 24)) {
+    *msg = "sizes beyond the supported range";
+    return false;
+  }
+  return true;
+}
 }  // namespace
 }  // namespace bdh
 
@@ -197,6 +218,60 @@ int bdh_relu_mul(const void* x, const int64_t x_strides[4], const void* y,
     return fail(BDH_ERR_INVALID, "relu_mul: last dimension must be contiguous");
   return launch_relu_mul(x, x_strides, y, y_strides, out, out_strides, dtype, B, H, T, N,
                          static_cast<cudaStream_t>(stream));
+}
+
+int bdh_latent_encode(const void* x, const int64_t x_strides[3], const void* enc,
+                      const int64_t enc_strides[3], void* xs, const int64_t xs_strides[4],
+                      void* qr, const int64_t qr_strides[4], const float* freqs, int64_t B,
+                      int64_t T, int64_t H, int64_t D, int64_t N, int64_t pos0, void* stream) {
+  std::string msg;
+  if (!latent_sizes_ok(B, T, H, D, N, &msg)) return fail(BDH_ERR_INVALID, "latent_encode: " + msg);
+  if (B * T * H * N == 0) return BDH_OK;
+  if (D == 0) return fail(BDH_ERR_INVALID, "latent_encode: D must be positive");
+  if (!strides_ok(x_strides, 3) || !strides_ok(enc_strides, 3) || !strides_ok(xs_strides, 4) ||
+      !strides_ok(qr_strides, 4))
+    return fail(BDH_ERR_INVALID,
+                "latent_encode: last stride must be 1 and the others positive multiples of 8");
+  if (freqs == nullptr) return fail(BDH_ERR_INVALID, "latent_encode: freqs is null");
+  if (pos0 < 0 || pos0 + T > (int64_t(1) << 24))
+    return fail(BDH_ERR_INVALID, "latent_encode: positions beyond the supported range");
+  LatentArgs a;
+  a.x = x;
+  std::memcpy(a.x_strides, x_strides, sizeof(a.x_strides));
+  a.w = enc;
+  std::memcpy(a.w_strides, enc_strides, sizeof(a.w_strides));
+  a.xs = xs;
+  std::memcpy(a.xs_strides, xs_strides, sizeof(a.xs_strides));
+  a.qr = qr;
+  std::memcpy(a.qr_strides, qr_strides, sizeof(a.qr_strides));
+  a.freqs = freqs;
+  a.B = B; a.T = T; a.H = H; a.D = D; a.N = N; a.pos0 = pos0;
+  return launch_latent_encode(a, static_cast<cudaStream_t>(stream), device_error_ptr());
+}
+
+int bdh_latent_gate(const void* y, const int64_t y_strides[4], const void* encv,
+                    const int64_t encv_strides[3], const void* xs, const int64_t xs_strides[4],
+                    void* xy, const int64_t xy_strides[4], int64_t B, int64_t T, int64_t H,
+                    int64_t D, int64_t N, void* stream) {
+  std::string msg;
+  if (!latent_sizes_ok(B, T, H, D, N, &msg)) return fail(BDH_ERR_INVALID, "latent_gate: " + msg);
+  if (B * T * H * N == 0) return BDH_OK;
+  if (D == 0) return fail(BDH_ERR_INVALID, "latent_gate: D must be positive");
+  if (!strides_ok(y_strides, 4) || !strides_ok(encv_strides, 3) || !strides_ok(xs_strides, 4) ||
+      !strides_ok(xy_strides, 4))
+    return fail(BDH_ERR_INVALID,
+                "latent_gate: last stride must be 1 and the others positive multiples of 8");
+  LatentArgs a;
+  a.y = y;
+  std::memcpy(a.y_strides, y_strides, sizeof(a.y_strides));
+  a.w = encv;
+  std::memcpy(a.w_strides, encv_strides, sizeof(a.w_strides));
+  a.xs = const_cast<void*>(xs);
+  std::memcpy(a.xs_strides, xs_strides, sizeof(a.xs_strides));
+  a.xy = xy;
+  std::memcpy(a.xy_strides, xy_strides, sizeof(a.xy_strides));
+  a.B = B; a.T = T; a.H = H; a.D = D; a.N = N;
+  return launch_latent_gate(a, static_cast<cudaStream_t>(stream), device_error_ptr());
 }
 
 size_t bdh_tril_score_v_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,

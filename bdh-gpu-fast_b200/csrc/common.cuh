@@ -268,4 +268,26 @@ __device__ __forceinline__ float bf16_round_f32(float x) {
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) { return cvt_bf16x2(lo, hi); }
 
+
+// ----------------------------------------------------------------- BDH RoPE ----
+// cos / sin of the reference phase for position `pos` and frequency `f` (bdh.py:119-122,
+// 142-150): fp32 product, exact fractional part (the product is >= 0), times fp32 2*pi as
+// torch rounds the Python scalar (0x40C90FDB), then sincosf.
+__device__ __forceinline__ void rope_cis(float pos, float f, float& c, float& s) {
+  float ph = __fmul_rn(pos, f);
+  ph = __fsub_rn(ph, floorf(ph));
+  ph = __fmul_rn(ph, __int_as_float(0x40C90FDB));
+  sincosf(ph, &s, &c);
+}
+
+// bf16 pair rotation (kernels/rope.py:108-126 with bf16 values and fp32 cos/sin): the four
+// products are rounded to bf16 two at a time, added in fp32 and the sums rounded once more
+// into the packed output word (y0 in the low half, y1 in the high half).
+__device__ __forceinline__ uint32_t rotate_pair_bf16x2(float x0, float x1, float c0, float s0,
+                                                       float c1, float s1) {
+  const uint32_t a = cvt_bf16x2(__fmul_rn(x0, c0), __fmul_rn(x1, c1));   // x0 c0 | x1 c1
+  const uint32_t b = cvt_bf16x2(__fmul_rn(-x1, s0), __fmul_rn(x0, s1));  // -x1 s0 | x0 s1
+  return cvt_bf16x2(__fadd_rn(bf16x2_lo(a), bf16x2_lo(b)), __fadd_rn(bf16x2_hi(a), bf16x2_hi(b)));
+}
+
 }  // namespace bdh

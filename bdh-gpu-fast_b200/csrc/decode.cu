@@ -32,13 +32,6 @@ __host__ __device__ constexpr int dec_rows(int kv_elem_bytes) { return kv_elem_b
 
 __device__ __forceinline__ float bf16_round_d(float x) { return bf16_round_f32(x); }
 
-__device__ __forceinline__ void rope_cis_d(float pos, float f, float& c, float& s) {
-  float ph = __fmul_rn(pos, f);
-  ph = __fsub_rn(ph, floorf(ph));
-  ph = __fmul_rn(ph, __int_as_float(0x40C90FDB));
-  sincosf(ph, &s, &c);
-}
-
 template <typename T>
 __device__ __forceinline__ float ld_elem(const T* p, int64_t i);
 template <>
@@ -138,8 +131,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_partial_kernel(
     const float p = static_cast<float>(pos + tq);
     for (int n = threadIdx.x * 2; n < N; n += blockDim.x * 2) {
       float c0, s0, c1, s1;
-      rope_cis_d(p, freqs[n], c0, s0);
-      rope_cis_d(p, freqs[n + 1], c1, s1);
+      rope_cis(p, freqs[n], c0, s0);
+      rope_cis(p, freqs[n + 1], c1, s1);
       const float x0 = ld_elem(qr, n), x1 = ld_elem(qr, n + 1);
       float y0, y1;
       if (BF16) {

@@ -18,23 +18,12 @@ namespace bdh {
 
 namespace {
 
-// fp32 2*pi exactly as torch rounds the Python scalar (0x40C90FDB).
-__device__ __forceinline__ float two_pi_f32() { return __int_as_float(0x40C90FDB); }
-
 __device__ __forceinline__ float bf16_round(float x) { return bf16_round_f32(x); }
 
 __device__ __forceinline__ float tf32_round(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
-}
-
-// cos / sin of the reference phase for position `pos` and frequency `f`.
-__device__ __forceinline__ void rope_cis(float pos, float f, float& c, float& s) {
-  float ph = __fmul_rn(pos, f);
-  ph = __fsub_rn(ph, floorf(ph));  // exact fractional part (ph >= 0)
-  ph = __fmul_rn(ph, two_pi_f32());
-  sincosf(ph, &s, &c);
 }
 
 // Rotate one (x0, x1) pair. BF16 = the input dtype is bf16 (products rounded before the add).
@@ -48,16 +37,6 @@ __device__ __forceinline__ void rotate_pair(float x0, float x1, float c0, float 
     y0 = __fsub_rn(__fmul_rn(x0, c0), __fmul_rn(x1, s0));
     y1 = __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(x0, s1));
   }
-}
-
-// bf16 pair rotation with packed conversions: the four products are rounded to bf16 two at a
-// time, added in fp32, and the sums rounded once more into the packed output word
-// (y0 in the low half, y1 in the high half) — the reference's cast-then-add sequence.
-__device__ __forceinline__ uint32_t rotate_pair_bf16x2(float x0, float x1, float c0, float s0,
-                                                       float c1, float s1) {
-  const uint32_t a = cvt_bf16x2(__fmul_rn(x0, c0), __fmul_rn(x1, c1));   // x0 c0 | x1 c1
-  const uint32_t b = cvt_bf16x2(__fmul_rn(-x1, s0), __fmul_rn(x0, s1));  // -x1 s0 | x0 s1
-  return cvt_bf16x2(__fadd_rn(bf16x2_lo(a), bf16x2_lo(b)), __fadd_rn(bf16x2_hi(a), bf16x2_hi(b)));
 }
 
 __device__ __forceinline__ void load8(const uint16_t* p, float (&v)[8]) {

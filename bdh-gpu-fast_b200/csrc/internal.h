@@ -12,7 +12,7 @@ namespace bdh {
 // Launch timing hooks (prof.cpp); kinds as documented at bdh_profile_end.
 enum ProfKind : int { kProfScore = 0, kProfValue = 1, kProfRope = 2, kProfDecode = 3,
                       kProfGradQ = 4, kProfGradV = 5, kProfSplit = 6, kProfOther = 7,
-                      kProfState = 8 };
+                      kProfState = 8, kProfEncode = 9, kProfGate = 10 };
 void prof_start(int kind, cudaStream_t s);
 void prof_stop(int kind, cudaStream_t s);
 
@@ -119,6 +119,26 @@ int launch_split_tf32(const float* x, const int64_t xs[4], float* hi, float* lo,
 // x (B, H, T, N) strided fp32 -> transposed hi/lo [B*H][N][ldt] (T contiguous, ldt >= T).
 int launch_split_tf32_t(const float* x, const int64_t xs[4], float* hi, float* lo, int64_t B,
                         int64_t H, int64_t T, int64_t N, int64_t ldt, cudaStream_t stream);
+
+// Fused latent projections (latent_proj.cu), bf16; strides in elements.
+struct LatentArgs {
+  const void* x = nullptr;       // encode: (B,T,D) {b,t,d}
+  int64_t x_strides[3] = {0, 0, 1};
+  const void* y = nullptr;       // gate: (B,H,T,D) {b,h,t,d}
+  int64_t y_strides[4] = {0, 0, 0, 1};
+  const void* w = nullptr;       // enc / encv (H,D,N) {h,d,n}
+  int64_t w_strides[3] = {0, 0, 1};
+  void* xs = nullptr;            // (B,T,H,N) {b,t,h,n}: written by encode, read by gate
+  int64_t xs_strides[4] = {0, 0, 0, 1};
+  void* qr = nullptr;            // (B,H,T,N) {b,h,t,n}
+  int64_t qr_strides[4] = {0, 0, 0, 1};
+  void* xy = nullptr;            // (B,T,H,N) {b,t,h,n}
+  int64_t xy_strides[4] = {0, 0, 0, 1};
+  const float* freqs = nullptr;
+  int64_t B = 0, T = 0, H = 0, D = 0, N = 0, pos0 = 0;
+};
+int launch_latent_encode(const LatentArgs& a, cudaStream_t stream, int* err);
+int launch_latent_gate(const LatentArgs& a, cudaStream_t stream, int* err);
 
 // Decode (decode.cu).
 struct DecodeArgs {

@@ -37,6 +37,42 @@ struct HasChunkEmit<P, std::void_t<decltype(P::kEmitEveryChunk)>> : std::true_ty
 //   P::kEpiSmemBytes -> shared memory reserved for the epilogue warps (1024-aligned), passed to
 //       P::epilogue_chunk(..., epi) and P::epilogue_end(prm, row, epi) (called once per thread
 //       after the tile loop, e.g. to drain bulk stores reading that memory).
+//   P::kCustomEpilogue -> the policy drains the accumulator itself (no KCHUNK):
+//       P::EpiState st (per epilogue thread, lives across tiles),
+//       P::epilogue_begin(prm, row, epi, st, has_first, first_tile)   once, before the tiles;
+//       P::epilogue_prefetch(prm, tile, has_next, next_tile, row, epi, st)
+//                                                         before the accumulator is ready;
+//       P::epilogue_tile(prm, tile, row, taddr, epi, st, abort_flag) -> bool
+//                                                         tcgen05.ld of the tile (lane quadrant
+//                                                         base `taddr`), all loads waited;
+//       P::epilogue_after(prm, tile, row, epi, st)        after the TMEM buffer is released;
+//       P::epilogue_end(prm, row, epi, st)                once, after the last tile.
+//   P::kContiguousTiles -> CTA i walks the contiguous tile range [i n / G, (i+1) n / G) instead
+//       of the strided list i, i + G, ... (consecutive tiles of a CTA then share operands or
+//       epilogue state).
+template <class P, class = void>
+struct HasCustomEpi : std::false_type {};
+template <class P>
+struct HasCustomEpi<P, std::void_t<decltype(P::kCustomEpilogue)>> : std::true_type {};
+template <class P, class = void>
+struct HasContigTiles : std::false_type {};
+template <class P>
+struct HasContigTiles<P, std::void_t<decltype(P::kContiguousTiles)>> : std::true_type {};
+
+// Tile walk of this CTA: t = begin, begin + step, ... < end.
+template <class P>
+__device__ __forceinline__ void tile_walk(int ntiles, int& begin, int& end, int& step) {
+  if constexpr (HasContigTiles<P>::value) {
+    begin = static_cast<int>(static_cast<long long>(blockIdx.x) * ntiles / gridDim.x);
+    end = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * ntiles / gridDim.x);
+    step = 1;
+  } else {
+    begin = static_cast<int>(blockIdx.x);
+    end = ntiles;
+    step = static_cast<int>(gridDim.x);
+  }
+}
+
 template <class P, class = void>
 struct EpiSmem {
   static constexpr int value = 0;
@@ -139,6 +175,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int ntiles = P::num_tiles(prm);
+  int t_begin, t_end, t_step;
+  tile_walk<P>(ntiles, t_begin, t_end, t_step);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::STAGES; ++s) {
@@ -167,7 +205,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t ph = 0;
       uint32_t n_issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (int t = t_begin; t < t_end && ok; t += t_step) {
         typename P::Tile tile = P::tile(prm, t);
         const int nkb = P::k_blocks(prm, tile);
         for (int kb = 0; kb < nkb; ++kb) {
@@ -211,7 +249,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t ph = 0;
       int lc = 0;  // accumulation chunks issued by this CTA (selects the TMEM buffer)
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (int t = t_begin; t < t_end && ok; t += t_step) {
         typename P::Tile tile = P::tile(prm, t);
         const int nkb = P::k_blocks(prm, tile);
         const int nch = S::chunks(nkb);
@@ -275,7 +313,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     (void)epi;
     int lc = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+    if constexpr (HasCustomEpi<P>::value) {
+      typename P::EpiState st{};
+      P::epilogue_begin(prm, row, epi, st, t_begin < t_end, P::tile(prm, t_begin < t_end ? t_begin : 0));
+      for (int t = t_begin; t < t_end && ok; t += t_step) {
+        typename P::Tile tile = P::tile(prm, t);
+        const bool has_next = t + t_step < t_end;
+        P::epilogue_prefetch(prm, tile, has_next, P::tile(prm, has_next ? t + t_step : t), row, epi, st);
+        const int acc = lc & 1;
+        const uint32_t aph = static_cast<uint32_t>(lc >> 1) & 1u;
+        ok = wait_bounded(tfull + acc, aph, abort_flag, prm.err, kErrTimeoutEpilogue);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tbase =
+            tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * S::BN);
+        ok = P::epilogue_tile(prm, tile, row, tbase, epi, st, abort_flag);
+        tc_fence_before();
+        mbar_arrive(tempty + acc);
+        ++lc;
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        P::epilogue_after(prm, tile, row, epi, st);
+      }
+      P::epilogue_end(prm, row, epi, st);
+    } else {
+    for (int t = t_begin; t < t_end && ok; t += t_step) {
       typename P::Tile tile = P::tile(prm, t);
       if (S::KCHUNK == 0) {
         const int acc = lc & 1;
@@ -348,6 +415,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
     if constexpr (HasChunkEmit<P>::value) P::epilogue_end(prm, row, epi);
+    }
   }
 
   tc_fence_before();

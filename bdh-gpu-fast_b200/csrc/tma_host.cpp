@@ -46,6 +46,13 @@ int sm_count(int device) {
 
 bool make_map_4d(CUtensorMap* map, const void* base, int elem_bytes, const int64_t dims[4],
                  const int64_t strides_bytes[3], int box0, int box1, const char* what) {
+  const int box[4] = {box0, box1, 1, 1};
+  return make_map_4d_box(map, base, elem_bytes, dims, strides_bytes, box, what);
+}
+
+bool make_map_4d_box(CUtensorMap* map, const void* base, int elem_bytes, const int64_t dims[4],
+                     const int64_t strides_bytes[3], const int box_in[4], const char* what) {
+  const int box0 = box_in[0], box1 = box_in[1];
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) {
     set_error("cuTensorMapEncodeTiled is not available from the CUDA driver");
@@ -73,7 +80,8 @@ bool make_map_4d(CUtensorMap* map, const void* base, int elem_bytes, const int64
     }
     gstride[i] = static_cast<cuuint64_t>(s);
   }
-  cuuint32_t box[4] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1), 1, 1};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1),
+                        static_cast<cuuint32_t>(box_in[2]), static_cast<cuuint32_t>(box_in[3])};
   cuuint32_t estride[4] = {1, 1, 1, 1};
   CUtensorMapDataType dt =
       elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -85,7 +93,8 @@ bool make_map_4d(CUtensorMap* map, const void* base, int elem_bytes, const int64
     os << what << ": cuTensorMapEncodeTiled failed (CUresult " << static_cast<int>(r)
        << "), dims=[" << dims[0] << "," << dims[1] << "," << dims[2] << "," << dims[3]
        << "] strides_bytes=[" << strides_bytes[0] << "," << strides_bytes[1] << ","
-       << strides_bytes[2] << "] box=[" << box0 << "," << box1 << "]";
+       << strides_bytes[2] << "] box=[" << box0 << "," << box1 << "," << box_in[2] << ","
+       << box_in[3] << "]";
     set_error(os.str());
     return false;
   }

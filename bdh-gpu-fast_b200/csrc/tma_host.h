@@ -25,5 +25,8 @@ int sm_count(int device);
 // Returns false (and sets the error message) when the driver rejects the layout.
 bool make_map_4d(CUtensorMap* map, const void* base, int elem_bytes, const int64_t dims[4],
                  const int64_t strides_bytes[3], int box0, int box1, const char* what);
+// Same with a full 4-D box (extents along d0..d3).
+bool make_map_4d_box(CUtensorMap* map, const void* base, int elem_bytes, const int64_t dims[4],
+                     const int64_t strides_bytes[3], const int box[4], const char* what);
 
 }  // namespace bdh

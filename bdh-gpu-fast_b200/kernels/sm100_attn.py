@@ -69,8 +69,13 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.bdh_tril_score_v_bwd.argtypes = [_vp, P, _vp, P, _vp, P, _vp, P, ctypes.c_int, _vp, P,
                                          _vp, P, _vp, P, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
                                          _i64, _vp, ctypes.c_size_t, _vp]
+    _c_i64_3p = ctypes.POINTER(ctypes.c_int64)
+    lib.bdh_latent_encode.argtypes = [_vp, _c_i64_3p, _vp, _c_i64_3p, _vp, P, _vp, P, _vp,
+                                      _i64, _i64, _i64, _i64, _i64, _i64, _vp]
+    lib.bdh_latent_gate.argtypes = [_vp, P, _vp, _c_i64_3p, _vp, P, _vp, P,
+                                    _i64, _i64, _i64, _i64, _i64, _vp]
     for name in ("bdh_rope_rotate", "bdh_tril_score_v", "bdh_tril_decode", "bdh_tril_score_v_bwd",
-                 "bdh_relu_mul"):
+                 "bdh_relu_mul", "bdh_latent_encode", "bdh_latent_gate"):
         getattr(lib, name).restype = ctypes.c_int
 
 
@@ -221,6 +226,30 @@ def _tma_ready(x: torch.Tensor) -> torch.Tensor:
     return y
 
 
+# Kernel kinds of the launch-timing hook, in the order of bdh_profile_end's arrays
+# (BDH_PROF_KINDS in include/bdh_sm100.h).
+PROF_KINDS = ("score", "value", "rope", "decode", "grad_q", "grad_v", "split", "gated_product",
+              "state", "encode", "gate")
+
+
+def profile_begin() -> None:
+    """Start timing every launch of the library (CUDA events around each kernel)."""
+    lib = _require_lib()
+    lib.bdh_profile_begin.restype = ctypes.c_int
+    _check(lib.bdh_profile_begin(), "profile_begin")
+
+
+def profile_end() -> dict:
+    """Stop timing; returns {kind: {"ms": summed device ms, "launches": count}}."""
+    lib = _require_lib()
+    n = len(PROF_KINDS)
+    ms = (ctypes.c_double * n)()
+    cnt = (ctypes.c_int * n)()
+    lib.bdh_profile_end.restype = ctypes.c_int
+    _check(lib.bdh_profile_end(ms, cnt), "profile_end")
+    return {k: {"ms": ms[i], "launches": cnt[i]} for i, k in enumerate(PROF_KINDS)}
+
+
 FWD_ALGOS = {"auto": 0, "quadratic": 1, "chunked": 2}
 
 
@@ -326,6 +355,106 @@ def relu_mul(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
         rc = lib.bdh_relu_mul(x.data_ptr(), _strides(x), y.data_ptr(), _strides(y), out.data_ptr(),
                               _strides(out), _code(x.dtype), B, H, T, N, _stream(dev))
     _check(rc, "relu_mul")
+    return out
+
+
+# ------------------------------------------------------------ latent projections
+_PAIRED: dict = {}
+
+
+def _check_paired_freqs(f: torch.Tensor) -> None:
+    """The fused encode shares one (cos, sin) per column pair: freqs[2p] must equal freqs[2p+1]
+    (BDH's get_freqs, bdh.py:41-49). Checked once per freqs tensor version."""
+    key = (f.data_ptr(), f._version, f.numel())
+    ok = _PAIRED.get(key)
+    if ok is None:
+        ok = bool(torch.equal(f[0::2], f[1::2]))
+        _PAIRED[key] = ok
+    if not ok:
+        raise ValueError("latent_encode requires paired frequencies (freqs[2p] == freqs[2p+1])")
+
+
+_c_i64_3 = ctypes.c_int64 * 3
+
+
+def _check_latent(name: str, *ts: torch.Tensor) -> None:
+    for t in ts:
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"{name}: bf16 tensors required, got {t.dtype}")
+        if t.stride(-1) != 1 or t.data_ptr() % 16 != 0 or any(
+                st % 8 != 0 for st, sz in zip(t.stride()[:-1], t.shape[:-1]) if sz > 1):
+            raise ValueError(f"{name}: tensors need a contiguous last dim, 16-byte aligned base "
+                             "and strides that are multiples of 8 elements")
+
+
+def _st(t: torch.Tensor, n: int):
+    # strides of size-1 dims are never stepped; give them a legal value
+    st = [s if (sz > 1 or s % 8 == 0) else 8 for s, sz in zip(t.stride(), t.shape)]
+    st[-1] = t.stride(-1)
+    return (_c_i64_3 if n == 3 else _c_i64_4)(*st)
+
+
+def latent_encode(x: torch.Tensor, enc: torch.Tensor, freqs: torch.Tensor, pos0: int = 0, *,
+                  xs_out: Optional[torch.Tensor] = None,
+                  qr_out: Optional[torch.Tensor] = None):
+    """Fused ``xs = relu(x @ enc)`` (B,T,H,N) and ``qr = RoPE(xs)`` (B,H,T,N), bf16.
+
+    ``x`` (B,T,D), ``enc`` (H,D,N). ``qr_out`` may be a strided view (a cache slot); returns
+    ``(xs, qr)``. Replaces ``BDH._encoder_relu`` (bdh.py:861-889) followed by the attention's
+    RoPE apply (bdh.py:396-412).
+    """
+    if x.dim() != 3 or enc.dim() != 3 or x.size(-1) != enc.size(1):
+        raise ValueError("latent_encode expects x (B,T,D) and enc (H,D,N)")
+    dev = _require_cuda(x, enc, freqs)
+    lib = _require_lib()
+    B, T, D = x.shape
+    H, _, N = enc.shape
+    f = freqs.reshape(-1)
+    if f.dtype != torch.float32 or f.numel() != N:
+        raise ValueError("freqs must be float32 with one entry per latent dimension")
+    f = f.contiguous()
+    _check_paired_freqs(f)
+    if xs_out is None:
+        xs_out = torch.empty(B, T, H, N, dtype=torch.bfloat16, device=dev)
+    if qr_out is None:
+        qr_out = torch.empty(B, H, T, N, dtype=torch.bfloat16, device=dev)
+    if tuple(xs_out.shape) != (B, T, H, N) or tuple(qr_out.shape) != (B, H, T, N):
+        raise ValueError("latent_encode: xs_out must be (B,T,H,N) and qr_out (B,H,T,N)")
+    _check_latent("latent_encode", x, enc, xs_out, qr_out)
+    with torch.cuda.device(dev):
+        rc = lib.bdh_latent_encode(x.data_ptr(), _st(x, 3), enc.data_ptr(), _st(enc, 3),
+                                   xs_out.data_ptr(), _st(xs_out, 4), qr_out.data_ptr(),
+                                   _st(qr_out, 4), f.data_ptr(), B, T, H, D, N, int(pos0),
+                                   _stream(dev))
+    _check(rc, "latent_encode")
+    return xs_out, qr_out
+
+
+def latent_gate(y: torch.Tensor, encv: torch.Tensor, xs: torch.Tensor, *,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Fused ``xy = xs * relu(y @ encv)`` in the (B,T,H,N) latent layout, bf16.
+
+    ``y`` (B,H,T,D) (the LayerNormed attention output), ``encv`` (H,D,N), ``xs`` (B,T,H,N).
+    Replaces ``BDH._encoder_v_relu`` and the product of ``_mlp_merge`` (bdh.py:914-945).
+    """
+    if y.dim() != 4 or encv.dim() != 3 or xs.dim() != 4 or y.size(-1) != encv.size(1):
+        raise ValueError("latent_gate expects y (B,H,T,D), encv (H,D,N), xs (B,T,H,N)")
+    dev = _require_cuda(y, encv, xs)
+    lib = _require_lib()
+    B, H, T, D = y.shape
+    N = encv.size(-1)
+    if tuple(xs.shape) != (B, T, H, N) or encv.size(0) != H:
+        raise ValueError("latent_gate: shapes of y, encv and xs disagree")
+    if out is None:
+        out = torch.empty(B, T, H, N, dtype=torch.bfloat16, device=dev)
+    elif tuple(out.shape) != (B, T, H, N):
+        raise ValueError("latent_gate: out must be (B,T,H,N)")
+    _check_latent("latent_gate", y, encv, xs, out)
+    with torch.cuda.device(dev):
+        rc = lib.bdh_latent_gate(y.data_ptr(), _st(y, 4), encv.data_ptr(), _st(encv, 3),
+                                 xs.data_ptr(), _st(xs, 4), out.data_ptr(), _st(out, 4),
+                                 B, T, H, D, N, _stream(dev))
+    _check(rc, "latent_gate")
     return out
 
 

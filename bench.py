@@ -56,23 +56,54 @@ def load_peaks():
 
 # ------------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi sampling of SM clock / throttle reasons during the timed region."""
+    """SM clock / clock-event reasons sampled every 20 ms during the timed region.
 
+    Reads NVML (``nvidia_ml_py``) from a Python thread; falls back to ``nvidia-smi -lms 200``.
+    Only reads: no clock, power or mode setting is touched.
+    """
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
     FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device: torch.device):
+    def __init__(self, device: torch.device, period_s: float = 0.02):
         self.uuid = None
         try:
             self.uuid = str(torch.cuda.get_device_properties(device).uuid)
         except Exception:  # noqa: BLE001
             pass
+        self.period = period_s
+        self.samples: list[tuple[float, float, set]] = []
         self.proc = None
         self.lines: list[str] = []
         self.thread = None
+        self.stop_ev = threading.Event()
+        self.nvml = None
+        self.handle = None
+
+    def _nvml_open(self) -> bool:
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uid = self.uuid if self.uuid.startswith("GPU-") else "GPU-" + self.uuid
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(uid)
+            self.nvml = pynvml
+            return True
+        except Exception:  # noqa: BLE001
+            self.nvml = None
+            return False
 
     def start(self):
+        if self.uuid and self._nvml_open():
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
@@ -83,11 +114,33 @@ class ClockSampler:
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
 
+    def _poll(self):
+        nv, h = self.nvml, self.handle
+        while not self.stop_ev.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                active = {name for name, const in self.REASONS if mask & getattr(nv, const, 0)}
+                self.samples.append((sm, mx, active))
+            except Exception:  # noqa: BLE001
+                pass
+            self.stop_ev.wait(self.period)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self) -> dict:
+        if self.nvml is not None:
+            self.stop_ev.set()
+            if self.thread:
+                self.thread.join(timeout=2)
+            sm = [s[0] for s in self.samples]
+            reasons = set().union(*[s[2] for s in self.samples]) if self.samples else set()
+            mx = self.samples[-1][1] if self.samples else None
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                    "reasons": sorted(reasons), "samples": len(sm), "source": "nvml 20 ms"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -114,36 +167,20 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi 200 ms"}
 
 
 # ------------------------------------------------------------------ native timing
-def _prof_lib():
-    import ctypes
-
+def profile_begin():
     from kernels import sm100_attn
 
-    lib = sm100_attn.load_library()
-    lib.bdh_profile_begin.restype = ctypes.c_int
-    lib.bdh_profile_end.restype = ctypes.c_int
-    return lib
-
-
-def profile_begin():
-    _prof_lib().bdh_profile_begin()
+    sm100_attn.profile_begin()
 
 
 def profile_end():
-    import ctypes
+    from kernels import sm100_attn
 
-    lib = _prof_lib()
-    ms = (ctypes.c_double * 9)()
-    cnt = (ctypes.c_int * 9)()
-    rc = lib.bdh_profile_end(ms, cnt)
-    if rc != 0:
-        raise RuntimeError(lib.bdh_last_error().decode())
-    kinds = ["score", "value", "rope", "decode", "grad_q", "grad_v", "split", "gated_product", "state"]
-    return {k: {"ms": ms[i], "launches": cnt[i]} for i, k in enumerate(kinds)}
+    return sm100_attn.profile_end()
 
 
 # ---------------------------------------------------------------------- helpers
@@ -190,14 +227,25 @@ def timed(fn, steps: int, world: int, dev) -> float:
     return max_over_ranks(s.elapsed_time(e), world, dev)
 
 
-def load_traffic(name: str):
+def load_traffic(name: str, batch: int | None = None):
+    """DRAM bytes (read + write) of one launch from a committed ncu summary.
+
+    ``profiles/<name>.json`` holds the bytes ncu measured on a capture of ``captured_batch``
+    rows of batch; the traffic of every kernel here grows in proportion to the batch (independent
+    (b,h) units), so it is scaled to this run's batch.
+    """
     p = REPO / "profiles" / f"{name}.json"
-    if p.exists():
-        try:
-            return json.loads(p.read_text()).get("traffic_bytes_per_launch")
-        except Exception:  # noqa: BLE001
-            return None
-    return None
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        t = float(d["traffic_bytes_per_captured_launch"])
+        cb = d.get("captured_batch")
+        if batch and cb:
+            t *= batch / cb
+        return t
+    except Exception:  # noqa: BLE001
+        return None
 
 
 # ------------------------------------------------------------------ CPU reference
@@ -327,11 +375,13 @@ def bench_config2(args, world, rank, dev):
                    "cache": "inputs larger than L2 (1 GB latent per layer per GPU); no flush"},
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": idx_host.numel() * 8,
                 "d2h_bytes_per_step": logits_host.numel() * 2},
-        "roofline": {"kernel": "score pass tril(QR QR^T,-1) (tc_gemm_kernel<ScoreProb<bf16>>)",
+        "roofline": {"kernel": ("score pass tril(QR QR^T,-1) (tc_pair_kernel<ScorePair>, cta_group::2 "
+                                "256x256 tiles)" if os.environ.get("BDH_SM100_PAIR", "1") != "0"
+                                else "score pass tril(QR QR^T,-1) (tc_gemm_kernel<ScoreProb<bf16>>)"),
                      "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": (achieved / peak) if achieved else None,
                      "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
-                     "traffic": load_traffic("score_pass_config2"),
+                     "traffic": load_traffic("score_pass_config2", B),
                      "avg_launch_ms": sc["ms"] / sc["launches"] if sc["launches"] else None,
                      "flops_per_launch": flops_launch},
         "attn_tflops": attn_flops / (attn_ms / 1e3) / 1e12 if attn_ms else None,
@@ -362,6 +412,82 @@ def _op_inputs(cfg_id, dev, rank, batch=0):
         q = torch.relu(torch.randn(B, H, T, N, device=dev, generator=g)).to(dt)
         v = torch.randn(B, 1, T, D, device=dev, generator=g).to(dt)
     return q, v, (B, H, T, N, D, dt)
+
+
+_TF32_PEAK = {}
+
+
+def measured_tf32_tflops(dev) -> float:
+    """cuBLAS TF32 GEMM throughput on this GPU (fp32 8192^3 with TF32 allowed, best of 5)."""
+    if dev in _TF32_PEAK:
+        return _TF32_PEAK[dev]
+    n = 8192
+    a = torch.randn(n, n, device=dev)
+    b = torch.randn(n, n, device=dev)
+    c = torch.empty(n, n, device=dev)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        for _ in range(3):
+            torch.mm(a, b, out=c)
+        best = float("inf")
+        for _ in range(5):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            torch.mm(a, b, out=c)
+            e.record()
+            torch.cuda.synchronize(dev)
+            best = min(best, s.elapsed_time(e))
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b, c
+    _TF32_PEAK[dev] = 2 * n ** 3 / (best / 1e3) / 1e12
+    return _TF32_PEAK[dev]
+
+
+def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev):
+    """Roofline of the dominant kernel of an op config (algorithmic work per launch / time).
+
+    * config 1 (fp32): score pass, causal Q K^T flops B H T(T-1) N against a measured cuBLAS
+      TF32 GEMM peak (the pass issues 3 TF32 products per algorithmic product for fp32 accuracy);
+    * config 3 (chunked): prefix-state pass, HBM bytes = K and V read once + the bf16 hi/lo
+      prefix states written, (T/C - 1) N D 4 bytes per (b,h);
+    * config 5: grad-Q pass, dQ_total = dS Q + dS^T Q, causal flops 2 T(T-1) N per (b,h).
+    """
+    B, H, T, N, D = shape
+    units = B * H
+    if cfg_id == 1:
+        k = prof["score"]
+        work = units * T * (T - 1) * N
+        peak, unit, bound = measured_tf32_tflops(dev), "TFLOP/s", "tensor"
+        psrc = "measured in this run: cuBLAS TF32 GEMM 8192^3, best of 5 (burst)"
+        kern = "score pass (tc_gemm_kernel<ScoreProb<tf32>>, 3-product split)"
+        tname = "score_pass_config1"
+    elif cfg_id == 3 and chunked:
+        k = prof["state"]
+        C = 256
+        work = units * ((T // C - 1) * N * D * 4 + T * N * 2) + B * T * D * 2
+        peak, unit, bound = peaks["hbm_gbs"], "GB/s", "hbm"
+        psrc = f"{src} hbm_gbs"
+        kern = "prefix-state pass (tc_gemm_kernel<StateProb>), bf16 hi/lo state writes"
+        tname = "state_pass_config3"
+    else:
+        k = prof["grad_q"] if cfg_id == 5 else prof["score"]
+        work = units * T * (T - 1) * N * (2 if cfg_id == 5 else 1)
+        peak, unit, bound = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]), "TFLOP/s", "tensor"
+        psrc = f"{src} bf16_tflops_sustained"
+        kern = ("grad-Q pass (tc_pair_kernel<GradQPair>, cta_group::2)" if cfg_id == 5
+                else "score pass")
+        tname = "grad_q_config5" if cfg_id == 5 else "score_pass_config3"
+    if not k["launches"]:
+        return None
+    per = k["ms"] / k["launches"]
+    scale = 1e12 if unit == "TFLOP/s" else 1e9
+    achieved = work / (per / 1e3) / scale
+    return {"kernel": kern, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+            "frac": achieved / peak, "peak_source": psrc,
+            "traffic": load_traffic(tname, B),
+            "avg_launch_ms": per, "work_per_launch": work}
 
 
 def bench_op(args, world, rank, dev):
@@ -404,6 +530,7 @@ def bench_op(args, world, rank, dev):
     peaks, src = load_peaks()
     sc = prof["score"]
     per_launch = sc["ms"] / sc["launches"] if sc["launches"] else None
+    roof = op_roofline(cfg_id, prof, (B, H, T, N, D), chunked, peaks, src, dev)
     line = {
         "metric": f"tril-attn TFLOP/s (config {cfg_id}, executed-algorithm causal flops)",
         "value": flops / (ms / 1e3) / 1e12,
@@ -415,6 +542,7 @@ def bench_op(args, world, rank, dev):
         "config": {"workload": f"config {cfg_id} op", "B": B, "H": H, "T": T, "N": N, "D": D,
                    "tokens_per_s": world * B * T * args.steps / (ms / 1e3),
                    "cache": "inputs larger than L2"},
+        "roofline": roof,
         "kernel_ms": {k: v_["ms"] / args.steps for k, v_ in prof.items() if v_["launches"]},
         "score_ms_per_launch": per_launch,
         "gpu_launches": sum(v_["launches"] for v_ in prof.values()),
@@ -424,11 +552,24 @@ def bench_op(args, world, rank, dev):
 
 
 # ------------------------------------------------------------------ config 4 decode
+def decode_traffic(name: str, batch: int, s_mean: float):
+    """Per-launch DRAM bytes of the decode kernels, scaled from a capture by batch x past length."""
+    p = REPO / "profiles" / f"{name}.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return float(d["traffic_bytes_per_captured_launch"]) * (batch * s_mean) / (
+            d["captured_batch"] * d["captured_past_len"])
+    except Exception:  # noqa: BLE001
+        return None
+
+
 def bench_decode(args, world, rank, dev):
     import bdh_model
     from bdh_cache import CacheManager
 
-    B, P = 64, 512
+    B, P = args.batch or 64, 512
     cfg = bdh_model.BDHConfig(n_layer=N_LAYER, n_embd=D_MODEL, n_head=N_HEAD,
                               mlp_internal_dim_multiplier=128, vocab_size=VOCAB, dropout=0.0)
     torch.manual_seed(1004)
@@ -453,9 +594,12 @@ def bench_decode(args, world, rank, dev):
             step()
         torch.cuda.synchronize(dev)
         S0 = pos[0]
+        clocks = ClockSampler(dev)
+        clocks.start()
         profile_begin()
         ms = timed(step, args.steps, world, dev)
         prof = profile_end()
+        clk = clocks.stop()
     esz = 2 if storage is not None else 4
     S_mean = S0 + (args.steps - 1) / 2
     bytes_step = N_LAYER * (B * N_HEAD * S_mean * N_LAT * esz + B * S_mean * D_MODEL * esz)
@@ -466,13 +610,20 @@ def bench_decode(args, world, rank, dev):
         "metric": "BDH decode tokens/s (config 4)", "value": world * B * args.steps / (ms / 1e3),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16 cache" if storage is not None else "f32",
+        "vs_baseline": None, "dtype": "bf16" if storage is not None else "f32",
+        "cache_dtype": "bf16" if storage is not None else "f32",
         "data": "synthetic", "config": {"workload": "config 4 decode", "B": B, "prompt": P,
                                         "S_mean": S_mean},
-        "roofline": {"kernel": "decode", "bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"],
-                     "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"] if gbs else None},
+        "roofline": {"kernel": "decode (decode_partial_kernel + decode_reduce_kernel)", "bound": "hbm",
+                     "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"] if gbs else None,
+                     "peak_source": f"{src} hbm_gbs",
+                     "bytes_per_launch": bytes_step / N_LAYER,
+                     "traffic": decode_traffic("decode_config4_bf16" if storage is not None
+                                               else "decode_config4", B, S_mean)},
         "kernel_ms": {k: v_["ms"] / args.steps for k, v_ in prof.items() if v_["launches"]},
         "gpu_launches": sum(v_["launches"] for v_ in prof.values()),
+        "clocks": clk,
     }
 
 

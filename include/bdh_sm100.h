@@ -175,14 +175,45 @@ int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* 
                          void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Fused latent projections around the attention path (bf16 only; the step before and the
+ * step after it in a BDH layer). Both are K = D tensor-core contractions with their
+ * elementwise work in the epilogue, so the (B, T, nh, N) latent crosses HBM once per output.
+ *
+ * bdh_latent_encode replaces the encoder projection + ReLU of bdh.py:861-912
+ * (BDH._encoder_relu / _encoder_relu_fwd) and the RoPE apply of the attention input,
+ * bdh.py:396-412 with kernels/rope.py:220-240 (bdh_rope_rotate into Attention.forward's
+ * out_kr):
+ *   xs[b,t,h,n] = relu(bf16(sum_k x[b,t,k] enc[h,k,n]))          x (B,T,D), enc (H,D,N)
+ *   qr[b,h,t,n] = RoPE(xs[b,t,h,:])[n] at position pos0 + t       qr (B,H,T,N) strided
+ * freqs must come in equal pairs (freqs[2p] == freqs[2p+1], as bdh.py:41-49 builds them).
+ * Strides are in elements: x_strides {b,t,d}, enc_strides {h,d,n}, xs_strides {b,t,h,n},
+ * qr_strides {b,h,t,n}; the last stride of each must be 1, the others multiples of 8.
+ *
+ * bdh_latent_gate replaces the encoder_v projection + ReLU and the sparse product of
+ * bdh.py:914-945 (BDH._encoder_v_relu and the x * y of _mlp_merge):
+ *   xy[b,t,h,n] = bf16(xs[b,t,h,n] * relu(bf16(sum_k y[b,h,t,k] encv[h,k,n])))
+ * y (B,H,T,D) strides {b,h,t,d}; encv (H,D,N); xs and xy (B,T,H,N) strides {b,t,h,n}.
+ * Neither call allocates; both are stream-ordered and graph-capturable.
+ */
+int bdh_latent_encode(const void* x, const int64_t x_strides[3], const void* enc,
+                      const int64_t enc_strides[3], void* xs, const int64_t xs_strides[4],
+                      void* qr, const int64_t qr_strides[4], const float* freqs, int64_t B,
+                      int64_t T, int64_t H, int64_t D, int64_t N, int64_t pos0, void* stream);
+int bdh_latent_gate(const void* y, const int64_t y_strides[4], const void* encv,
+                    const int64_t encv_strides[3], const void* xs, const int64_t xs_strides[4],
+                    void* xy, const int64_t xy_strides[4], int64_t B, int64_t T, int64_t H,
+                    int64_t D, int64_t N, void* stream);
+
+/*
  * Launch timing for benchmarks (no counterpart in the reference, which timed whole calls with
  * perf_counter, benchmarks/bench_gpu_attn.py:263-280). Between begin and end, every kernel of
  * this library is bracketed by CUDA events on its own stream; end synchronises them and
  * returns the summed device milliseconds and launch counts per kernel kind:
  *   0 score pass, 1 value pass, 2 RoPE, 3 decode, 4 grad-Q pass, 5 grad-V pass, 6 split/transpose,
- *   7 gated product (bdh_relu_mul), 8 state pass of the chunked forward.
+ *   7 gated product (bdh_relu_mul), 8 state pass of the chunked forward,
+ *   9 latent encode (bdh_latent_encode), 10 latent gate (bdh_latent_gate).
  */
-#define BDH_PROF_KINDS 9
+#define BDH_PROF_KINDS 11
 int bdh_profile_begin(void);
 int bdh_profile_end(double ms[BDH_PROF_KINDS], int launches[BDH_PROF_KINDS]);
 

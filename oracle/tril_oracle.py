@@ -197,6 +197,78 @@ def bdh_forward(idx: np.ndarray, weights: dict, n_layer: int, n_head: int, acc=n
     return x.reshape(B, T, D) @ head
 
 
+def bdh_forward_bf16(idx: np.ndarray, weights: dict, n_layer: int, n_head: int,
+                     rounding: bool = True):
+    """Logits of the BDH forward under bf16 autocast with fp32 accumulation everywhere.
+
+    The layer of bdh.py:991-1052 as torch.autocast(bfloat16) runs it, except that the
+    attention keeps fp32 accumulation over the T x T scores (the reference's native
+    tril_score_v, csrc/tril_attn_cuda.cu, instead of the eager bf16 matmul that rounds every
+    score): every GEMM takes bf16 operands, accumulates exactly and rounds its output to bf16;
+    LayerNorm runs in fp32 on its (bf16 or fp32) input; the RoPE rotates bf16 values with fp32
+    cos/sin as kernels/rope.py:108-126; the sparse product is rounded to bf16.
+    rounding=False gives the same sequence with every bf16 rounding removed.
+    """
+    r = bf16_round if rounding else (lambda a: np.asarray(a, np.float32))
+    emb = np.asarray(weights["embed"], np.float32)
+    enc = r(np.asarray(weights["encoder"], np.float32)).astype(np.float64)
+    enc_v = r(np.asarray(weights["encoder_v"], np.float32)).astype(np.float64)
+    dec = r(np.asarray(weights["decoder"], np.float32)).astype(np.float64)
+    head = r(np.asarray(weights["lm_head"], np.float32)).astype(np.float64)
+    freqs = np.asarray(weights["freqs"], dtype=np.float32)
+    B, T = idx.shape
+    nh = n_head
+    N = enc.shape[-1]
+
+    def gemm(a, w, eq):
+        return r(np.einsum(eq, r(a).astype(np.float64), w, optimize=True).astype(np.float32))
+
+    x = layer_norm(emb[idx]).astype(np.float32)  # B,T,D fp32
+    for _ in range(n_layer):
+        xs = np.maximum(gemm(x, enc, "btd,hdn->bthn"), np.float32(0.0))  # B,T,nh,N
+        qr = rope(np.swapaxes(xs, 1, 2), freqs, bf16=rounding)  # B,nh,T,N
+        v = r(x)[:, None]
+        y = r(tril_score_v(qr.astype(np.float64), qr.astype(np.float64),
+                           v.astype(np.float64)).astype(np.float32))
+        yn = layer_norm(y).astype(np.float32)
+        ys = np.maximum(gemm(yn, enc_v, "bhtd,hdn->bthn"), np.float32(0.0))
+        xy = r(xs * ys)
+        ymlp = gemm(xy.reshape(B, T, nh * N), dec, "btk,kd->btd")
+        x = layer_norm(x + layer_norm(ymlp).astype(np.float32)).astype(np.float32)
+    return gemm(x, head, "btd,dv->btv")
+
+
+def latent_encode(x: np.ndarray, enc: np.ndarray, freqs: np.ndarray, pos0: int = 0,
+                  bf16: bool = True, acc=np.float64):
+    """Encoder projection + ReLU, then the RoPE of the attention input.
+
+    xs[b,t,h,n] = relu(x[b,t,:] . enc[h,:,n])   (BDH._encoder_relu, bdh.py:861-889)
+    qr[b,h,t,n] = rope(xs[b,:,h,:])[t,n]          (Attention.rope, bdh.py:396-412)
+    bf16: the projection output is rounded to bf16 before the ReLU (a bf16 GEMM with fp32
+    accumulation, as under autocast) and the rotation rounds as kernels/rope.py:108-126 does
+    for bf16 values. Returns (xs (B,T,H,N), qr (B,H,T,N)) as float32.
+    """
+    lat = np.einsum("btd,hdn->bthn", np.asarray(x, acc), np.asarray(enc, acc))
+    lat = lat.astype(np.float32)
+    if bf16:
+        lat = bf16_round(lat)
+    xs = np.maximum(lat, np.float32(0.0))
+    qr = rope(np.swapaxes(xs, 1, 2), freqs, pos0, bf16=bf16)
+    return xs, qr
+
+
+def latent_gate(y: np.ndarray, encv: np.ndarray, xs: np.ndarray, bf16: bool = True,
+                acc=np.float64) -> np.ndarray:
+    """xy[b,t,h,n] = xs[b,t,h,n] * relu(y[b,h,t,:] . encv[h,:,n])  (BDH._encoder_v_relu and the
+    product of _mlp_merge, bdh.py:914-945); bf16 rounds the projection and the product."""
+    lat = np.einsum("bhtd,hdn->bthn", np.asarray(y, acc), np.asarray(encv, acc)).astype(np.float32)
+    if bf16:
+        lat = bf16_round(lat)
+    ys = np.maximum(lat, np.float32(0.0))
+    xy = np.asarray(xs, np.float32) * ys
+    return bf16_round(xy) if bf16 else xy
+
+
 def rel_fro(a, b) -> float:
     """Relative Frobenius error ||a - b|| / ||b|| in float64."""
     a = np.asarray(a, dtype=np.float64)

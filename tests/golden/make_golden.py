@@ -151,7 +151,35 @@ def main(reference: Path) -> None:
             steps.append(_f32(lg[:, -1]))
         mod["logits_cached_steps"] = np.stack(steps)
     np.savez_compressed(HERE / "golden_model.npz", **mod)
+    latent_fixture(bdh, HERE)
     print("wrote", sorted(p.name for p in HERE.glob("golden_*.npz")))
+
+
+def latent_fixture(bdh, out_dir: Path) -> None:
+    """The two latent projections around the attention, in bf16 as the model runs them:
+    BDH._encoder_relu + Attention.rope (bdh.py:861-889, 396-412) and BDH._encoder_v_relu + the
+    product of _mlp_merge (bdh.py:914-945)."""
+    import torch
+    import torch.nn.functional as F
+
+    lat = {}
+    cfg = bdh.BDHConfig(n_layer=1, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4, dropout=0.0)
+    att = bdh.Attention(cfg)  # N = 64
+    g = torch.Generator().manual_seed(7)
+    B, T, D, nh, N, pos0 = 2, 20, 32, 2, 64, 37
+    x = F.layer_norm(torch.randn(B, T, D, generator=g), (D,)).to(torch.bfloat16)
+    enc = (torch.randn(nh, D, N, generator=g) * 0.3).to(torch.bfloat16)
+    encv = (torch.randn(nh, D, N, generator=g) * 0.3).to(torch.bfloat16)
+    y = F.layer_norm(torch.randn(B, nh, T, D, generator=g), (D,)).to(torch.bfloat16)
+    with torch.no_grad():
+        xs = bdh.BDH._encoder_relu(x, enc)  # (B,T,nh,N) bf16
+        cs = att.rope_cos_sin(T, pos0, torch.device("cpu"))
+        qr = att.rope(None, xs.permute(0, 2, 1, 3), cos_sin=cs)  # (B,nh,T,N) bf16
+        ys = bdh.BDH._encoder_v_relu(y, encv)  # (B,T,nh,N) bf16
+        xy = xs * ys
+    lat.update(x=_f32(x), enc=_f32(enc), encv=_f32(encv), y=_f32(y), xs=_f32(xs), qr=_f32(qr),
+               ys=_f32(ys), xy=_f32(xy), freqs=att.freqs.reshape(-1).numpy(), pos0=np.int64(pos0))
+    np.savez_compressed(out_dir / "golden_latent.npz", **lat)
 
 
 def dataclasses_asdict(c):
@@ -161,4 +189,11 @@ def dataclasses_asdict(c):
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))
+    ref = Path(sys.argv[1]) if len(sys.argv) > 1 and not sys.argv[1].startswith("--") else Path("/root/reference")
+    if "--latent-only" in sys.argv:
+        sys.path.insert(0, str(ref))
+        import bdh as _bdh
+
+        latent_fixture(_bdh, HERE)
+    else:
+        main(ref)

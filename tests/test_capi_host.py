@@ -81,3 +81,27 @@ def test_build_recipe_targets_sm100a():
 
     assert "arch=compute_100a,code=sm_100a" in " ".join(build_lib.ARCH)
     assert "-lineinfo" in build_lib.NVCC_FLAGS
+
+
+def test_profile_kinds_match_header():
+    from kernels import sm100_attn as sa
+
+    m = re.search(r"#define BDH_PROF_KINDS (\d+)", HEADER.read_text())
+    assert m and int(m.group(1)) == len(sa.PROF_KINDS)
+
+
+def test_latent_entry_points_validate_on_host():
+    from kernels import sm100_attn as sa
+
+    lib = sa.load_library()
+    s3 = (ctypes.c_int64 * 3)(512, 256, 1)
+    s4 = _i64x4(4096, 1024, 64, 1)
+    # odd latent width (RoPE pairs)
+    rc = lib.bdh_latent_encode(None, s3, None, s3, None, s4, None, s4, None, 1, 16, 2, 256, 63, 0, None)
+    assert rc == 1 and b"even" in lib.bdh_last_error()
+    # a non-contiguous last dimension
+    bad = _i64x4(4096, 1024, 64, 2)
+    rc = lib.bdh_latent_gate(None, bad, None, s3, None, s4, None, s4, 1, 16, 2, 256, 64, None)
+    assert rc == 1 and b"stride" in lib.bdh_last_error()
+    # empty problems are a no-op
+    assert lib.bdh_latent_encode(None, s3, None, s3, None, s4, None, s4, None, 0, 16, 2, 256, 64, 0, None) == 0

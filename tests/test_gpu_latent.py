@@ -1,0 +1,231 @@
+"""GPU parity of the fused latent projections (bdh_latent_encode / bdh_latent_gate) against
+the reference's own bf16 outputs (tests/golden/golden_latent.npz), the pinned numpy oracle and
+torch's cuBLAS path, and of the BDH model layer that uses them.
+
+The projections are K = D dot products accumulated in fp32 and rounded once to bf16, so a
+different accumulation order can move an output to the neighbouring bf16 value; those flips
+are bounded by a mismatch fraction, everything else is compared exactly. Model stages use the
+bf16 tolerance (relative Frobenius <= 3e-3).
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import tril_oracle as O
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def sa():
+    from kernels import sm100_attn
+
+    return sm100_attn
+
+
+def b16(x):
+    return torch.as_tensor(np.asarray(x, dtype=np.float32)).to(DEV).to(torch.bfloat16)
+
+
+def f32(t):
+    return t.detach().float().cpu().numpy()
+
+
+@pytest.fixture(autouse=True)
+def _device_error_clean():
+    yield
+    assert sa().device_error() == 0, "a kernel reported a pipeline timeout"
+
+
+def test_latent_encode_golden():
+    g = golden("latent")
+    freqs = torch.as_tensor(g["freqs"]).to(DEV)
+    xs, qr = sa().latent_encode(b16(g["x"]), b16(g["enc"]), freqs, int(g["pos0"]))
+    assert np.mean(f32(xs) != g["xs"]) < 0.01
+    assert O.rel_fro(f32(xs), g["xs"]) < 3e-3
+    assert np.mean(f32(qr) != g["qr"]) < 0.01
+    assert O.rel_fro(f32(qr), g["qr"]) < 3e-3
+
+
+def test_latent_gate_golden():
+    g = golden("latent")
+    xy = sa().latent_gate(b16(g["y"]), b16(g["encv"]), b16(g["xs"]))
+    assert np.mean(f32(xy) != g["xy"]) < 0.01
+    assert O.rel_fro(f32(xy), g["xy"]) < 3e-3
+
+
+@pytest.mark.parametrize("B,T,D,H,N,pos0", [(2, 200, 256, 4, 1024, 5), (1, 128, 64, 2, 200, 0),
+                                            (3, 77, 96, 1, 520, 4090)])
+def test_latent_encode_vs_oracle(B, T, D, H, N, pos0):
+    g = torch.Generator().manual_seed(B * 1000 + T)
+    x = F.layer_norm(torch.randn(B, T, D, generator=g), (D,)).to(torch.bfloat16)
+    enc = (torch.randn(H, D, N, generator=g) * 0.1).to(torch.bfloat16)
+    freqs = O.get_freqs(N)
+    xs, qr = sa().latent_encode(x.to(DEV), enc.to(DEV), torch.as_tensor(freqs).to(DEV), pos0)
+    xs_o, qr_o = O.latent_encode(x.float().numpy(), enc.float().numpy(), freqs, pos0)
+    assert np.mean(f32(xs) != xs_o) < 2e-3
+    assert O.rel_fro(f32(xs), xs_o) < 3e-3
+    assert O.rel_fro(f32(qr), qr_o) < 3e-3
+    # the rotation of the kernel's own xs is the library's RoPE, element for element
+    qr_r = sa().rope_rotate(xs.permute(0, 2, 1, 3), torch.as_tensor(freqs).to(DEV), pos0)
+    assert torch.equal(qr, qr_r)
+
+
+@pytest.mark.parametrize("B,T,D,H,N", [(2, 200, 256, 4, 1024), (1, 130, 32, 3, 136)])
+def test_latent_gate_vs_oracle(B, T, D, H, N):
+    g = torch.Generator().manual_seed(B * 77 + T)
+    y = F.layer_norm(torch.randn(B, H, T, D, generator=g), (D,)).to(torch.bfloat16)
+    encv = (torch.randn(H, D, N, generator=g) * 0.1).to(torch.bfloat16)
+    xs = torch.relu(torch.randn(B, T, H, N, generator=g)).to(torch.bfloat16)
+    xy = sa().latent_gate(y.to(DEV), encv.to(DEV), xs.to(DEV))
+    xy_o = O.latent_gate(y.float().numpy(), encv.float().numpy(), xs.float().numpy())
+    assert np.mean(f32(xy) != xy_o) < 2e-3
+    assert O.rel_fro(f32(xy), xy_o) < 3e-3
+
+
+def test_latent_encode_into_strided_cache_slot():
+    B, T, D, H, N, cap, pos0 = 2, 150, 256, 4, 512, 400, 100
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(B, T, D, generator=g).to(torch.bfloat16).to(DEV)
+    enc = (torch.randn(H, D, N, generator=g) * 0.05).to(torch.bfloat16).to(DEV)
+    freqs = torch.as_tensor(O.get_freqs(N)).to(DEV)
+    buf = torch.full((B, H, cap, N), 7.0, dtype=torch.bfloat16, device=DEV)
+    slot = buf.narrow(2, pos0, T)
+    xs, qr = sa().latent_encode(x, enc, freqs, pos0, qr_out=slot)
+    assert qr.data_ptr() == slot.data_ptr()
+    _, qr_ref = sa().latent_encode(x, enc, freqs, pos0)
+    assert torch.equal(slot, qr_ref)
+    assert bool((buf[:, :, :pos0] == 7.0).all()) and bool((buf[:, :, pos0 + T:] == 7.0).all())
+
+
+def test_latent_kernels_full_size_vs_cublas():
+    """Config-2 layer shapes (B=8 of 32, T=512, D=256, nh=4, N=8192) against torch's bf16
+    einsum + ReLU (cuBLAS) and the library's RoPE / gated product on the same operands."""
+    B, T, D, H, N = 8, 512, 256, 4, 8192
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = F.layer_norm(torch.randn(B, T, D, device=DEV, generator=g), (D,)).to(torch.bfloat16)
+    enc = (torch.randn(H, D, N, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    encv = (torch.randn(H, D, N, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    y = F.layer_norm(torch.randn(B, H, T, D, device=DEV, generator=g), (D,)).to(torch.bfloat16)
+    freqs = torch.as_tensor(O.get_freqs(N)).to(DEV)
+    xs, qr = sa().latent_encode(x, enc, freqs, 0)
+    xs_ref = torch.relu(torch.einsum("btd,hdn->bthn", x, enc))
+    assert (xs != xs_ref).float().mean().item() < 2e-3
+    d = (xs.float() - xs_ref.float()).norm() / xs_ref.float().norm()
+    assert d.item() < 3e-3
+    assert torch.equal(qr, sa().rope_rotate(xs.permute(0, 2, 1, 3), freqs, 0))
+    xy = sa().latent_gate(y, encv, xs)
+    xy_ref = xs * torch.relu(torch.einsum("bhtd,hdn->bthn", y, encv))
+    assert (xy != xy_ref).float().mean().item() < 2e-3
+    d = (xy.float() - xy_ref.float()).norm() / xy_ref.float().norm()
+    assert d.item() < 3e-3
+
+
+def _model(n_layer=2, n_embd=256, n_head=4, mult=128):
+    import bdh_model
+
+    cfg = bdh_model.BDHConfig(n_layer=n_layer, n_embd=n_embd, n_head=n_head,
+                              mlp_internal_dim_multiplier=mult, vocab_size=256, dropout=0.0)
+    torch.manual_seed(3)
+    m = bdh_model.BDH(cfg).to(DEV).eval()
+    m.attn._attn_impl_override = "cuda_sm100"
+    return m
+
+
+def _launch_counts(fn):
+    """Run fn() between the library's profile_begin / profile_end; launches per kernel kind."""
+    sa().profile_begin()
+    fn()
+    return {k: v["launches"] for k, v in sa().profile_end().items()}
+
+
+def test_model_latent_layer_matches_unfused_and_oracle(monkeypatch):
+    """Fused latent layers vs the unfused sm100 layers (the same arithmetic: bf16 GEMM outputs,
+    bf16 RoPE and product), and vs the float64 oracle of the bf16-autocast forward.
+
+    End to end, bf16 activations put a noise floor under any comparison of two independent
+    implementations of this randomly initialised model: the oracle against itself with the
+    attention accumulated in float32 instead of float64 already moves the logits by 2.5e-3
+    (LayerNorm of the attention output amplifies its last-bit rounding). The end-to-end bound
+    is therefore 1e-2, and the 3e-3 bound is applied stage by stage below."""
+    m = _model(n_layer=2)
+    idx = torch.randint(0, 256, (2, 128), generator=torch.Generator().manual_seed(9)).to(DEV)
+    res = {}
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        monkeypatch.setenv("BDH_SM100_LATENT", "1")
+        assert m._latent_fusable("cuda_sm100", 128, None, idx.device)
+        cnt = _launch_counts(lambda: res.setdefault("fused", m(idx)[0].float()))
+        assert cnt["encode"] == 2 and cnt["gate"] == 2 and cnt["rope"] == 0, cnt
+        monkeypatch.setenv("BDH_SM100_LATENT", "0")
+        cnt = _launch_counts(lambda: res.setdefault("plain", m(idx)[0].float()))
+        assert cnt["encode"] == 0 and cnt["rope"] == 2, cnt
+    fused, plain = res["fused"], res["plain"]
+    assert ((fused - plain).norm() / plain.norm()).item() < 1e-3
+    w = {k: getattr(m, k).detach().to(torch.bfloat16).float().cpu().numpy()
+         for k in ("encoder", "encoder_v", "decoder", "lm_head")}
+    w["embed"] = m.embed.weight.detach().float().cpu().numpy()
+    w["freqs"] = m.attn.freqs.reshape(-1).cpu().numpy()
+    ref16 = O.bdh_forward_bf16(idx.cpu().numpy(), w, n_layer=2, n_head=4)
+    assert O.rel_fro(f32(fused), ref16) < 1e-2
+
+
+def test_model_latent_layer_stagewise_vs_oracle():
+    """One fused layer stage by stage, each stage fed the GPU's own inputs: encode (xs, qr),
+    attention output, gate, decoder projection — each within the bf16 bound."""
+    m = _model(n_layer=1)
+    B, T = 2, 128
+    idx = torch.randint(0, 256, (B, T), generator=torch.Generator().manual_seed(9)).to(DEV)
+    freqs = m.attn.freqs.reshape(-1).cpu().numpy()
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        x = m._ln(m.embed(idx))
+        xb = x.to(torch.bfloat16)
+        enc, encv, dec = (m._bf16_param(k) for k in ("encoder", "encoder_v", "decoder"))
+        xs, qr = sa().latent_encode(xb, enc, m.attn.freqs, 0)
+        v = x.unsqueeze(1).to(torch.bfloat16)
+        y = sa().tril_score_v(qr, qr, v)
+        yn = m._ln(y.float()).to(torch.bfloat16)
+        xy = sa().latent_gate(yn, encv, xs)
+        ym = F.linear(xy.view(B, T, -1), dec.t())
+    xs_o, qr_o = O.latent_encode(f32(xb), f32(enc), freqs, 0)
+    assert O.rel_fro(f32(xs), xs_o) < 3e-3 and O.rel_fro(f32(qr), qr_o) < 3e-3
+    q64 = f32(qr).astype(np.float64)
+    y_o = O.tril_score_v(q64, q64, f32(v).astype(np.float64))
+    assert O.rel_fro(f32(y), y_o) < 3e-3
+    assert O.rel_fro(f32(xy), O.latent_gate(f32(yn), f32(encv), f32(xs))) < 3e-3
+    ym_o = np.einsum("btk,kd->btd", f32(xy).reshape(B, T, -1).astype(np.float64),
+                     f32(dec).astype(np.float64))
+    assert O.rel_fro(f32(ym), ym_o) < 3e-3
+
+
+def test_model_latent_prefill_then_decode(monkeypatch):
+    """Cached prefill on the fused kernels (QR written into the cache slot), then T=1 steps;
+    logits agree with the unfused path step by step."""
+    from bdh_cache import CacheManager
+
+    m = _model(n_layer=2)
+    B, P, steps = 2, 192, 4
+    idx = torch.randint(0, 256, (B, P + steps), generator=torch.Generator().manual_seed(4)).to(DEV)
+
+    def run(flag, storage):
+        monkeypatch.setenv("BDH_SM100_LATENT", flag)
+        cache = CacheManager.from_config(m.config, B, P + steps, idx.device, storage_dtype=storage)
+        out = []
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            lg, _ = m(idx[:, :P], cache=cache)
+            out.append(lg[:, -1].float())
+            for t in range(P, P + steps):
+                lg, _ = m(idx[:, t:t + 1], cache=cache)
+                out.append(lg[:, -1].float())
+        return torch.stack(out)
+
+    for storage in (None, torch.bfloat16):
+        a = run("1", storage)
+        b = run("0", storage)
+        r = ((a - b).norm() / b.norm()).item()
+        assert r < 3e-3, (storage, r)

@@ -121,3 +121,40 @@ def test_model_forward_matches_reference_baseline():
     logits = O.bdh_forward(g["idx"], _model_weights(g), n_layer=2, n_head=2)
     assert O.rel_fro(logits, g["logits_baseline"]) < 1e-5
     assert O.rel_fro(g["logits_opt"], g["logits_baseline"]) < 1e-5
+
+
+def test_latent_encode_matches_reference():
+    """Oracle encode (projection, bf16 rounding, ReLU, bf16 RoPE) vs the reference's own
+    BDH._encoder_relu + Attention.rope run in bf16 (golden_latent.npz)."""
+    g = golden("latent")
+    xs, qr = O.latent_encode(g["x"], g["enc"], g["freqs"], int(g["pos0"]))
+    # the reference's CPU bf16 GEMM and the float64 oracle may round a few outputs to
+    # neighbouring bf16 values; everything else is bit-identical
+    assert np.mean(xs != g["xs"]) < 0.01
+    assert O.rel_fro(xs, g["xs"]) < 3e-3
+    assert np.mean(qr != g["qr"]) < 0.01
+    assert O.rel_fro(qr, g["qr"]) < 3e-3
+    # given the reference's xs, the rotation is exact
+    qr2 = O.rope(np.swapaxes(g["xs"], 1, 2), g["freqs"], int(g["pos0"]), bf16=True)
+    assert np.mean(qr2 != g["qr"]) < 1e-3
+
+
+def test_latent_gate_matches_reference():
+    g = golden("latent")
+    xy = O.latent_gate(g["y"], g["encv"], g["xs"])
+    assert np.mean(xy != g["xy"]) < 0.01
+    assert O.rel_fro(xy, g["xy"]) < 3e-3
+    # the product itself is one bf16 rounding of an exact fp32 product
+    np.testing.assert_array_equal(O.bf16_round(g["xs"] * g["ys"]), g["xy"])
+
+
+def test_bf16_autocast_oracle_pinned_to_reference_model():
+    """The bf16-autocast restatement of the layer has the reference baseline's structure:
+    without its bf16 roundings it reproduces the reference logits; with them it stays within
+    the bf16 error of those logits."""
+    g = golden("model")
+    w = _model_weights(g)
+    exact = O.bdh_forward_bf16(g["idx"], w, n_layer=2, n_head=2, rounding=False)
+    assert O.rel_fro(exact, g["logits_baseline"]) < 1e-5
+    rounded = O.bdh_forward_bf16(g["idx"], w, n_layer=2, n_head=2)
+    assert O.rel_fro(rounded, g["logits_baseline"]) < 2e-2
