@@ -153,18 +153,20 @@ class BDH(nn.Module):
     def _ln(self, x: torch.Tensor) -> torch.Tensor:
         return F.layer_norm(x, (x.size(-1),), eps=self.ln.eps)
 
-    def _bf16_param(self, name: str) -> torch.Tensor:
+    def _bf16_param(self, name: str, k_major: bool = False) -> torch.Tensor:
         """bf16 copy of a parameter, refreshed when the parameter changes (the cast that
-        autocast would make on every use)."""
+        autocast would make on every use). k_major: an (H, D, N) weight as a view of a
+        contiguous (H, N, D) copy, the layout the latent kernels read fastest."""
         p = getattr(self, name)
-        if p.dtype == torch.bfloat16:
-            return p
         cache = self.__dict__.setdefault("_bf16_cache", {})
-        key = (p.data_ptr(), p._version, p.device)
-        hit = cache.get(name)
+        key = (p.data_ptr(), p._version, p.device, k_major)
+        hit = cache.get((name, k_major))
         if hit is None or hit[0] != key:
-            hit = (key, p.detach().to(torch.bfloat16))
-            cache[name] = hit
+            w = p.detach().to(torch.bfloat16)
+            if k_major:
+                w = w.transpose(1, 2).contiguous().transpose(1, 2)
+            hit = (key, w)
+            cache[(name, k_major)] = hit
         return hit[1]
 
     def _latent_fusable(self, impl: str, T: int, cache, device) -> bool:
@@ -179,15 +181,20 @@ class BDH(nn.Module):
             or self.encoder.dtype == torch.bfloat16
         return bf16 and os.environ.get("BDH_SM100_LATENT", "1") != "0"
 
-    def _layer_latent(self, x: torch.Tensor, level: int, rope_start: int, cache) -> torch.Tensor:
-        """One layer on the fused latent kernels: encode (+ReLU +RoPE) -> tril attention ->
-        LN -> encoder_v gate (xs * relu(.)) -> decoder -> residual LN. Same arithmetic as the
-        bf16-autocast layer of bdh.py:991-1052."""
-        from kernels.sm100_attn import latent_encode, latent_gate, tril_score_v
+    def _layer_latent(self, x: torch.Tensor, xb: Optional[torch.Tensor], level: int,
+                      rope_start: int, cache):
+        """One layer on the fused kernels: encode (+ReLU +RoPE) -> tril attention -> LN ->
+        encoder_v gate (xs * relu(.)) -> decoder (cuBLAS) -> residual double LN. Same arithmetic
+        as the bf16-autocast layer of bdh.py:991-1052. ``xb`` is the bf16 copy of ``x`` (made
+        here when None); returns the new ``(x, xb)``."""
+        from kernels.sm100_attn import (latent_encode, latent_gate, layer_norm,
+                                        residual_layer_norm, tril_score_v)
 
         B, T, _ = x.shape
         nh = self.config.n_head
-        xb = x.to(torch.bfloat16)
+        eps = self.ln.eps
+        if xb is None:
+            xb = x.to(torch.bfloat16)
         v_tok = x.unsqueeze(1)
         qr_slot = None
         dst_kr = None
@@ -196,15 +203,19 @@ class BDH(nn.Module):
             dst_v.copy_(v_tok)
             if dst_kr.dtype == torch.bfloat16:
                 qr_slot = dst_kr
-        xs, qr = latent_encode(xb, self._bf16_param("encoder"), self.attn.freqs, rope_start,
+        kmaj = os.environ.get("BDH_SM100_WEIGHT_KMAJOR", "1") != "0"
+        xs, qr = latent_encode(xb, self._bf16_param("encoder", kmaj), self.attn.freqs, rope_start,
                                qr_out=qr_slot)
         if dst_kr is not None and qr_slot is None:
             dst_kr.copy_(qr)
-        y_kv = tril_score_v(qr, qr, v_tok.to(torch.bfloat16))
-        yn = self._ln(y_kv.float()).to(torch.bfloat16)
-        xy = latent_gate(yn, self._bf16_param("encoder_v"), xs)
+        y_kv = tril_score_v(qr, qr, xb.unsqueeze(1))
+        yn = layer_norm(y_kv, eps, out_dtype=torch.bfloat16)
+        xy = latent_gate(yn, self._bf16_param("encoder_v", kmaj), xs)
         y_mlp = F.linear(xy.view(B, T, nh * xy.size(-1)), self._bf16_param("decoder").t())
-        return self._ln(x + self._ln(y_mlp))
+        if x.dtype == torch.float32:
+            return residual_layer_norm(x, y_mlp, eps, want_bf16=True)
+        x = self._ln(x + self._ln(y_mlp))
+        return x, x.to(torch.bfloat16)
 
     def forward(self, idx: torch.Tensor, targets: Optional[torch.Tensor] = None,
                 cache: Optional[CacheManager] = None, *, logits_out: Optional[torch.Tensor] = None):
@@ -225,9 +236,10 @@ class BDH(nn.Module):
         # gated product), so the latents are never rewritten just to clamp them.
         fused = impl == "cuda_sm100" and not grad and (not self.training or self.drop.p == 0.0)
         latent = self._latent_fusable(impl, T, cache, x.device)
+        xb = None
         for level in range(C.n_layer):
             if latent:
-                x = self._layer_latent(x, level, rope_start, cache)
+                x, xb = self._layer_latent(x, xb, level, rope_start, cache)
                 continue
             x_lat = torch.einsum("btd,hdn->bthn", x, self.encoder)  # (B, T, nh, N)
             x_bthn = x_lat if fused else F.relu(x_lat)

@@ -150,6 +150,12 @@ bool strides_ok(const int64_t* s, int n) {
     if (s[i] <= 0 || (s[i] % 8) != 0) return false;
   return true;
 }
+// (H, D, N) weights: n contiguous, or d contiguous (a transposed copy); other strides multiples of 8.
+bool weight_strides_ok(const int64_t* s) {
+  if (s[2] == 1) return strides_ok(s, 3);
+  if (s[1] != 1) return false;
+  return s[0] > 0 && s[0] % 8 == 0 && s[2] > 0 && s[2] % 8 == 0;
+}
 bool latent_sizes_ok(int64_t B, int64_t T, int64_t H, int64_t D, int64_t N, std::string* msg) {
   if (B < 0 || T < 0 || H < 0 || D < 0 || N < 0) {
     *msg = "negative size";
@@ -228,7 +234,7 @@ int bdh_latent_encode(const void* x, const int64_t x_strides[3], const void* enc
   if (!latent_sizes_ok(B, T, H, D, N, &msg)) return fail(BDH_ERR_INVALID, "latent_encode: " + msg);
   if (B * T * H * N == 0) return BDH_OK;
   if (D == 0) return fail(BDH_ERR_INVALID, "latent_encode: D must be positive");
-  if (!strides_ok(x_strides, 3) || !strides_ok(enc_strides, 3) || !strides_ok(xs_strides, 4) ||
+  if (!strides_ok(x_strides, 3) || !weight_strides_ok(enc_strides) || !strides_ok(xs_strides, 4) ||
       !strides_ok(qr_strides, 4))
     return fail(BDH_ERR_INVALID,
                 "latent_encode: last stride must be 1 and the others positive multiples of 8");
@@ -257,7 +263,7 @@ int bdh_latent_gate(const void* y, const int64_t y_strides[4], const void* encv,
   if (!latent_sizes_ok(B, T, H, D, N, &msg)) return fail(BDH_ERR_INVALID, "latent_gate: " + msg);
   if (B * T * H * N == 0) return BDH_OK;
   if (D == 0) return fail(BDH_ERR_INVALID, "latent_gate: D must be positive");
-  if (!strides_ok(y_strides, 4) || !strides_ok(encv_strides, 3) || !strides_ok(xs_strides, 4) ||
+  if (!strides_ok(y_strides, 4) || !weight_strides_ok(encv_strides) || !strides_ok(xs_strides, 4) ||
       !strides_ok(xy_strides, 4))
     return fail(BDH_ERR_INVALID,
                 "latent_gate: last stride must be 1 and the others positive multiples of 8");
@@ -272,6 +278,44 @@ int bdh_latent_gate(const void* y, const int64_t y_strides[4], const void* encv,
   std::memcpy(a.xy_strides, xy_strides, sizeof(a.xy_strides));
   a.B = B; a.T = T; a.H = H; a.D = D; a.N = N;
   return launch_latent_gate(a, static_cast<cudaStream_t>(stream), device_error_ptr());
+}
+
+int bdh_layernorm(const void* x, int x_dtype, int64_t x_row_stride, void* y, int y_dtype,
+                  int64_t y_row_stride, int64_t rows, int64_t D, float eps, void* stream) {
+  if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype))
+    return fail(BDH_ERR_INVALID, "layernorm: dtype must be f32 or bf16");
+  if (rows < 0 || D <= 0 || D > 1024 || (D % 8) != 0)
+    return fail(BDH_ERR_INVALID, "layernorm: D must be a positive multiple of 8, at most 1024");
+  if ((rows > 1 && (x_row_stride % 8 != 0 || y_row_stride % 8 != 0 || x_row_stride < D ||
+                    y_row_stride < D)) ||
+      (reinterpret_cast<uintptr_t>(x) & 15u) != 0 || (reinterpret_cast<uintptr_t>(y) & 15u) != 0)
+    return fail(BDH_ERR_INVALID, "layernorm: row strides must be multiples of 8 >= D, bases 16-byte aligned");
+  if (!(eps >= 0.0f)) return fail(BDH_ERR_INVALID, "layernorm: eps must be >= 0");
+  return launch_layernorm(x, x_dtype, x_row_stride, y, y_dtype, y_row_stride, rows,
+                          static_cast<int>(D), eps, static_cast<cudaStream_t>(stream));
+}
+
+int bdh_residual_layernorm(const float* x, int64_t x_row_stride, const void* y, int y_dtype,
+                           int64_t y_row_stride, float* out, int64_t out_row_stride,
+                           void* out_bf16, int64_t out_bf16_row_stride, int64_t rows, int64_t D,
+                           float eps, void* stream) {
+  if (!dtype_ok(y_dtype)) return fail(BDH_ERR_INVALID, "residual_layernorm: dtype must be f32 or bf16");
+  if (rows < 0 || D <= 0 || D > 1024 || (D % 8) != 0)
+    return fail(BDH_ERR_INVALID, "residual_layernorm: D must be a positive multiple of 8, at most 1024");
+  const bool strides =
+      rows <= 1 || (x_row_stride % 8 == 0 && y_row_stride % 8 == 0 && out_row_stride % 8 == 0 &&
+                    x_row_stride >= D && y_row_stride >= D && out_row_stride >= D &&
+                    (out_bf16 == nullptr || (out_bf16_row_stride % 8 == 0 && out_bf16_row_stride >= D)));
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                         reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(out_bf16)) &
+                        15u) == 0;
+  if (!strides || !aligned)
+    return fail(BDH_ERR_INVALID,
+                "residual_layernorm: row strides must be multiples of 8 >= D, bases 16-byte aligned");
+  if (!(eps >= 0.0f)) return fail(BDH_ERR_INVALID, "residual_layernorm: eps must be >= 0");
+  return launch_residual_layernorm(x, x_row_stride, y, y_dtype, y_row_stride, out, out_row_stride,
+                                   static_cast<uint16_t*>(out_bf16), out_bf16_row_stride, rows,
+                                   static_cast<int>(D), eps, static_cast<cudaStream_t>(stream));
 }
 
 size_t bdh_tril_score_v_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,

@@ -121,6 +121,37 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// L2 cache policies for TMA copies: operands that many tiles re-read stay (evict_last);
+// streams that are read or written once go first (evict_first).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void tma_load_4d_hint(const CUtensorMap* map, uint64_t* bar, void* dst,
+                                                 int c0, int c1, int c2, int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(c3), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_4d_hint(const CUtensorMap* map, const void* src, int c0,
+                                                  int c1, int c2, int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group.L2::cache_hint"
+      " [%0, {%2, %3, %4, %5}], [%1], %6;"
+      ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(c3), "l"(policy)
+      : "memory");
+}
+
 // 4-D tiled store from shared memory (bulk-group completion). The source must be visible to
 // the async proxy: every writing thread executes fence_async_smem() before the issuing thread
 // is released.
@@ -258,6 +289,26 @@ __device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
+// relu then round, packed: {lo, hi} = {bf16(max(lo, 0)), bf16(max(hi, 0))} (NaN stays NaN).
+__device__ __forceinline__ uint32_t cvt_relu_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Packed bf16 add / multiply, each the exact result rounded once to bf16 (round to nearest
+// even): the same values as forming the sum / product in fp32 and rounding that, because the
+// sum or product of two bf16 values needs at most 18 significant bits before the final
+// rounding (fp32 then bf16 rounds innocuously, 24 >= 2 x 8 + 2).
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
 __device__ __forceinline__ float bf16x2_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16x2_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
@@ -281,13 +332,13 @@ __device__ __forceinline__ void rope_cis(float pos, float f, float& c, float& s)
 }
 
 // bf16 pair rotation (kernels/rope.py:108-126 with bf16 values and fp32 cos/sin): the four
-// products are rounded to bf16 two at a time, added in fp32 and the sums rounded once more
-// into the packed output word (y0 in the low half, y1 in the high half).
+// products are rounded to bf16 two at a time and the two bf16 sums rounded once more into the
+// packed output word (y0 in the low half, y1 in the high half).
 __device__ __forceinline__ uint32_t rotate_pair_bf16x2(float x0, float x1, float c0, float s0,
                                                        float c1, float s1) {
   const uint32_t a = cvt_bf16x2(__fmul_rn(x0, c0), __fmul_rn(x1, c1));   // x0 c0 | x1 c1
   const uint32_t b = cvt_bf16x2(__fmul_rn(-x1, s0), __fmul_rn(x0, s1));  // -x1 s0 | x0 s1
-  return cvt_bf16x2(__fadd_rn(bf16x2_lo(a), bf16x2_lo(b)), __fadd_rn(bf16x2_hi(a), bf16x2_hi(b)));
+  return add_bf16x2(a, b);
 }
 
 }  // namespace bdh

@@ -12,7 +12,7 @@ namespace bdh {
 // Launch timing hooks (prof.cpp); kinds as documented at bdh_profile_end.
 enum ProfKind : int { kProfScore = 0, kProfValue = 1, kProfRope = 2, kProfDecode = 3,
                       kProfGradQ = 4, kProfGradV = 5, kProfSplit = 6, kProfOther = 7,
-                      kProfState = 8, kProfEncode = 9, kProfGate = 10 };
+                      kProfState = 8, kProfEncode = 9, kProfGate = 10, kProfNorm = 11 };
 void prof_start(int kind, cudaStream_t s);
 void prof_stop(int kind, cudaStream_t s);
 
@@ -139,6 +139,13 @@ struct LatentArgs {
 };
 int launch_latent_encode(const LatentArgs& a, cudaStream_t stream, int* err);
 int launch_latent_gate(const LatentArgs& a, cudaStream_t stream, int* err);
+
+// Row LayerNorms (layernorm.cu); strides in elements.
+int launch_layernorm(const void* x, int x_dtype, int64_t xs, void* y, int y_dtype, int64_t ys,
+                     int64_t rows, int D, float eps, cudaStream_t stream);
+int launch_residual_layernorm(const float* x, int64_t xs, const void* y, int y_dtype, int64_t ys,
+                              float* out, int64_t os, uint16_t* out16, int64_t os16, int64_t rows,
+                              int D, float eps, cudaStream_t stream);
 
 // Decode (decode.cu).
 struct DecodeArgs {

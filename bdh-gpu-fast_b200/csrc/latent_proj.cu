@@ -19,6 +19,8 @@
 // (t block, n block) outer and (b, h) inner, so a thread's 64 (cos, sin) pairs are computed
 // once and reused across all B x H tiles that share its positions and columns.
 #include <algorithm>
+#include <cstdlib>
+#include <type_traits>
 #include <string>
 
 #include "bdh_sm100.h"
@@ -57,82 +59,182 @@ __device__ __forceinline__ LatentTile latent_tile(int t, int B, int H, int nb_n)
   return tl;
 }
 
-// ------------------------------------------------------------------------ encode ----
-struct EncodeProb {
-  using S = TcShape<2, 128, false, true, 1, 1, 3>;
-  static constexpr int kCustomEpilogue = 1;
+struct EncodeParams {
+  CUtensorMap a_map;   // x (B,T,D): box 64 (k) x 128 (t)
+  CUtensorMap b_map;   // enc (H,D,N): n-contiguous box 64 (n) x 64 (k), or d-contiguous 64 x 128
+  CUtensorMap xs_map;  // xs (B,T,H,N) as {N,H,T,B}: box 64 x 1 x 32 x 1
+  CUtensorMap qr_map;  // qr (B,H,T,N) as {N,T,H,B}: box 64 x 32 x 1 x 1
+  const float* freqs;
+  int B, T, H, D, N, pos0;
+  int tb_n, nb_n;
+  int walk_chunk;        // row blocks per chunk of the chunked walk (divides B * tb_n)
+  int* err;
+};
+
+struct GateParams {
+  CUtensorMap a_map;   // y (B,H,T,D): box 64 (k) x 128 (t)
+  CUtensorMap b_map;   // encv (H,D,N): n-contiguous box 64 (n) x 64 (k), or d-contiguous 64 x 128
+  CUtensorMap xs_map;  // xs (B,T,H,N) as {N,H,T,B}: box 64 x 1 x 32 x 1 (load)
+  CUtensorMap xy_map;  // xy (B,T,H,N) as {N,H,T,B}: box 64 x 1 x 32 x 1 (store)
+  int B, T, H, D, N;
+  int tb_n, nb_n;
+  int walk_chunk;        // row blocks per chunk of the chunked walk (divides B * tb_n)
+  int* err;
+};
+
+// The epilogue uses eight warps: two per TMEM lane quadrant, each draining one 64-column half
+// of the 128 x 128 tile (warp slot ew = quadrant + 4 * half owns its staging buffers).
+
+struct ContiguousWalk {
   static constexpr int kContiguousTiles = 1;
+};
+struct StridedWalk {};
+// Chunks of walk_chunk row blocks of one column block (h, nb), the column block fastest across
+// chunks: a CTA keeps the column block's weights resident for the whole chunk, and the CTAs
+// running at one time write neighbouring column blocks of the same row chunk.
+struct ChunkedResidentWalk {
+  static constexpr int kChunkedWalk = 1;
+  static constexpr int kResidentB = 4;  // D <= 256
+};
+
+__device__ __forceinline__ LatentTile latent_tile_chunked(int t, int B, int H, int nb_n, int ch) {
+  LatentTile tl;
+  const int c = t / ch;
+  const int i = t - c * ch;
+  const int ncb = H * nb_n;
+  const int cb = c % ncb;
+  // each chunk starts at a different row block of the row chunk, so the CTAs running at one time
+  // read different activation tiles instead of all requesting the same L2 lines together
+  const int rb = (c / ncb) * ch + (i + c) % ch;
+  tl.b = rb % B;
+  tl.tb = rb / B;
+  tl.h = cb / nb_n;
+  tl.nb = cb - tl.h * nb_n;
+  return tl;
+}
+
+template <int ORDER>
+using LatentWalk = std::conditional_t<
+    ORDER == 0, ContiguousWalk, std::conditional_t<ORDER == 3, ChunkedResidentWalk, StridedWalk>>;
+
+// Tile order across the grid: n block fastest, so the CTAs running at one time write adjacent
+// column blocks of the same rows.
+__device__ __forceinline__ LatentTile latent_tile_nfast(int t, int B, int H, int tb_n, int nb_n) {
+  LatentTile tl;
+  tl.nb = t % nb_n;
+  int r = t / nb_n;
+  tl.h = r % H;
+  r /= H;
+  tl.tb = r % tb_n;
+  tl.b = r / tb_n;
+  return tl;
+}
+
+// ------------------------------------------------------------------------ encode ----
+// Tile order for a grid of G = k * nb_n CTAs walking with stride G: every CTA keeps one n block,
+// the CTAs running at one time cover adjacent n blocks of the same rows, and the position
+// block (slowest index) changes only every B*H*nb_n/G tiles of a CTA.
+__device__ __forceinline__ LatentTile latent_tile_colfixed(int t, int B, int H, int nb_n) {
+  LatentTile tl;
+  tl.nb = t % nb_n;
+  int r = t / nb_n;
+  tl.h = r % H;
+  r /= H;
+  tl.b = r % B;
+  tl.tb = r / B;
+  return tl;
+}
+
+template <int STAGES, int BUFS, int ORDER = 0, bool KW = false>
+struct EncodeProb : LatentWalk<ORDER> {
+  using S = TcShape<2, 128, false, !KW, 1, 1, STAGES>;
+  static constexpr int kCustomEpilogue = 1;
+  static constexpr int kEpiWarps = 8;
   static constexpr int kBox = 32 * 128;           // one 64-column x 32-row swizzled box
-  static constexpr int kBuf = 4 * kBox;           // xs (2 boxes) + qr (2 boxes)
-  static constexpr int kWarpStage = 2 * kBuf;     // double buffered
-  static constexpr int kEpiSmemBytes = 4 * kWarpStage;
-  struct Params {
-    CUtensorMap a_map;   // x (B,T,D): box 64 (k) x 128 (t)
-    CUtensorMap b_map;   // enc (H,D,N) read MN-major: box 64 (n) x 64 (k)
-    CUtensorMap xs_map;  // xs (B,T,H,N) as {N,H,T,B}: box 64 x 1 x 32 x 1
-    CUtensorMap qr_map;  // qr (B,H,T,N) as {N,T,H,B}: box 64 x 32 x 1 x 1
-    const float* freqs;
-    int B, T, H, D, N, pos0;
-    int tb_n, nb_n;
-    int* err;
-  };
+  static constexpr int kBuf = 2 * kBox;           // xs box + qr box
+  static constexpr int kWarpStage = BUFS * kBuf;  // BUFS staging buffers per warp
+  static constexpr int kEpiSmemBytes = 8 * kWarpStage;
+  using Params = EncodeParams;
   using Tile = LatentTile;
   struct EpiState {
-    float c[64], s[64];
-    int key;   // tb * nb_n + nb of the cached phases
-    int iter;  // tiles finished by this thread (selects the staging buffer)
+    float c[32], s[32];  // (cos, sin) of this thread's row for its 32 column pairs
+    int key;             // tb * nb_n + nb of the cached phases
+    int iter;            // tiles finished by this thread (selects the staging buffer)
   };
   __device__ static int num_tiles(const Params& p) { return p.B * p.H * p.tb_n * p.nb_n; }
-  __device__ static Tile tile(const Params& p, int t) { return latent_tile(t, p.B, p.H, p.nb_n); }
+  __device__ static Tile tile(const Params& p, int t) {
+    return ORDER == 0   ? latent_tile(t, p.B, p.H, p.nb_n)
+           : ORDER == 1 ? latent_tile_nfast(t, p.B, p.H, p.tb_n, p.nb_n)
+           : ORDER == 2 ? latent_tile_colfixed(t, p.B, p.H, p.nb_n)
+                        : latent_tile_chunked(t, p.B, p.H, p.nb_n, p.walk_chunk);
+  }
+  __device__ static int walk_chunk(const Params& p) { return p.walk_chunk; }
+  __device__ static int b_key(const Params& p, const Tile& tl) { return tl.h * p.nb_n + tl.nb; }
+  static int max_ctas(const Params& p, int sms) {
+    if (ORDER != 2) return sms;
+    return p.nb_n <= sms ? (sms / p.nb_n) * p.nb_n : sms;
+  }
   __device__ static int k_blocks(const Params& p, const Tile&) { return (p.D + 63) / 64; }
   __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x1u; }
   __device__ static void prefetch(const Params& p) {
     tma_prefetch_desc(&p.a_map);
     tma_prefetch_desc(&p.b_map);
   }
-  __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint64_t* bar,
-                                    uint8_t* a_dst, uint8_t* b_dst) {
-    tma_load_4d(&p.a_map, bar, a_dst, kb * 64, tl.tb * 128, tl.b, 0);
+  __device__ static void load_b(const Params& p, const Tile& tl, int kb, uint64_t* bar,
+                                uint8_t* dst) {
+    const uint64_t keep = l2_policy_evict_last();
+    if (KW) {  // K-major weights: one 64 (k) x 128 (n) box
+      tma_load_4d_hint(&p.b_map, bar, dst, kb * 64, tl.nb * 128, tl.h, 0, keep);
+      return;
+    }
 #pragma unroll
     for (int c = 0; c < 2; ++c)
-      tma_load_4d(&p.b_map, bar, b_dst + c * 64 * 128, tl.nb * 128 + c * 64, kb * 64, tl.h, 0);
+      tma_load_4d_hint(&p.b_map, bar, dst + c * 64 * 128, tl.nb * 128 + c * 64, kb * 64, tl.h, 0,
+                       keep);
+  }
+  __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint64_t* bar,
+                                    uint8_t* a_dst, uint8_t* b_dst) {
+    const uint64_t keep = l2_policy_evict_last();
+    tma_load_4d_hint(&p.a_map, bar, a_dst, kb * 64, tl.tb * 128, tl.b, 0, keep);
+    if (ORDER != 3) load_b(p, tl, kb, bar, b_dst);
+  }
+  __device__ static uint8_t* stage(uint8_t* epi, int row, int part, int iter) {
+    return epi + ((row >> 5) + 4 * part) * kWarpStage + (iter % BUFS) * kBuf;
   }
 
-  __device__ static void epilogue_begin(const Params&, int, uint8_t*, EpiState& st, bool,
+  __device__ static void epilogue_begin(const Params&, int, int, uint8_t*, EpiState& st, bool,
                                         const Tile&) {
     st.key = -1;
     st.iter = 0;
   }
-  // (cos, sin) of this thread's row for the tile's 64 column pairs, when they changed.
+  // (cos, sin) for the tile's positions and this warp's columns, when they changed.
   __device__ static void epilogue_prefetch(const Params& p, const Tile& tl, bool, const Tile&,
-                                           int row, uint8_t*, EpiState& st) {
+                                           int row, int part, uint8_t*, EpiState& st) {
     const int key = tl.tb * p.nb_n + tl.nb;
     if (key == st.key) return;
     st.key = key;
     const float pos = static_cast<float>(p.pos0 + tl.tb * 128 + row);
-    const int n0 = tl.nb * 128;
+    const int n0 = tl.nb * 128 + part * 64;
 #pragma unroll
-    for (int q = 0; q < 64; ++q) {
+    for (int q = 0; q < 32; ++q) {
       const int n = n0 + 2 * q;
       const float f = n < p.N ? __ldg(p.freqs + n) : 0.0f;
       rope_cis(pos, f, st.c[q], st.s[q]);
     }
   }
-  __device__ static bool epilogue_tile(const Params&, const Tile&, int row, uint32_t taddr,
+  __device__ static bool epilogue_tile(const Params&, const Tile&, int row, int part, uint32_t taddr,
                                        uint8_t* epi, EpiState& st, volatile int*) {
-    const int quad = row >> 5, lr = row & 31;
-    uint8_t* buf = epi + quad * kWarpStage + (st.iter & 1) * kBuf;
-    // the stores that last read this buffer were committed two tiles ago
-    if (lr == 0) bulk_wait_read<1>();
+    const int lr = row & 31;
+    uint8_t* xs_box = stage(epi, row, part, st.iter);
+    uint8_t* qr_box = xs_box + kBox;
+    // the stores that last read this buffer were committed BUFS tiles ago
+    if (lr == 0) bulk_wait_read<BUFS - 1>();
     __syncwarp();
 #pragma unroll
-    for (int c0 = 0; c0 < 128; c0 += 32) {
+    for (int c0 = 0; c0 < 64; c0 += 32) {
       uint32_t r[32];
-      tmem_ld32(taddr + static_cast<uint32_t>(c0), r);
+      tmem_ld32(taddr + static_cast<uint32_t>(part * 64 + c0), r);
       tmem_ld_wait();
-      uint8_t* xs_box = buf + (c0 >> 6) * kBox;
-      uint8_t* qr_box = buf + (2 + (c0 >> 6)) * kBox;
-      const int j0 = (c0 & 63) >> 3;
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
         uint32_t xw[4], qw[4];
@@ -140,71 +242,66 @@ struct EncodeProb {
         for (int e = 0; e < 4; ++e) {
           const int i = 8 * v + 2 * e;
           const int q = (c0 >> 1) + 4 * v + e;
-          xw[e] = cvt_bf16x2(fmaxf(__uint_as_float(r[i]), 0.0f), fmaxf(__uint_as_float(r[i + 1]), 0.0f));
+          xw[e] = cvt_relu_bf16x2(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
           qw[e] = rotate_pair_bf16x2(bf16x2_lo(xw[e]), bf16x2_hi(xw[e]), st.c[q], st.s[q], st.c[q],
                                      st.s[q]);
         }
-        const int off = sw128(lr, j0 + v);
+        const int off = sw128(lr, (c0 >> 3) + v);
         *reinterpret_cast<uint4*>(xs_box + off) = make_uint4(xw[0], xw[1], xw[2], xw[3]);
         *reinterpret_cast<uint4*>(qr_box + off) = make_uint4(qw[0], qw[1], qw[2], qw[3]);
       }
     }
     return true;
   }
-  __device__ static void epilogue_after(const Params& p, const Tile& tl, int row, uint8_t* epi,
-                                        EpiState& st) {
-    const int quad = row >> 5;
-    uint8_t* buf = epi + quad * kWarpStage + (st.iter & 1) * kBuf;
+  __device__ static void epilogue_after(const Params& p, const Tile& tl, int row, int part,
+                                        uint8_t* epi, EpiState& st) {
+    uint8_t* xs_box = stage(epi, row, part, st.iter);
     fence_async_smem();
     __syncwarp();
-    const int t0 = tl.tb * 128 + quad * 32;
-    if ((row & 31) == 0 && t0 < p.T) {
-#pragma unroll
-      for (int hb = 0; hb < 2; ++hb) {
-        const int n = tl.nb * 128 + hb * 64;
-        if (n < p.N) {
-          tma_store_4d(&p.xs_map, buf + hb * kBox, n, tl.h, t0, tl.b);
-          tma_store_4d(&p.qr_map, buf + (2 + hb) * kBox, n, t0, tl.h, tl.b);
-        }
+    if ((row & 31) == 0) {
+      const int t0 = tl.tb * 128 + (row & ~31);
+      const int n = tl.nb * 128 + part * 64;
+      if (t0 < p.T && n < p.N) {
+        const uint64_t stream = l2_policy_evict_first();
+        tma_store_4d_hint(&p.xs_map, xs_box, n, tl.h, t0, tl.b, stream);
+        tma_store_4d_hint(&p.qr_map, xs_box + kBox, n, t0, tl.h, tl.b, stream);
       }
+      bulk_commit();  // one group per tile (possibly empty)
     }
-    if ((row & 31) == 0) bulk_commit();  // one group per tile (possibly empty)
     ++st.iter;
   }
-  __device__ static void epilogue_end(const Params&, int row, uint8_t*, EpiState&) {
+  __device__ static void epilogue_end(const Params&, int row, int, uint8_t*, EpiState&) {
     if ((row & 31) == 0) bulk_wait_all();
     __syncwarp();
   }
 };
 
 // -------------------------------------------------------------------------- gate ----
-struct GateProb {
-  using S = TcShape<2, 128, false, true, 1, 1, 3>;
+template <int STAGES, int SLOTS, int ORDER = 0, bool KW = false>
+struct GateProb : LatentWalk<ORDER> {
+  using S = TcShape<2, 128, false, !KW, 1, 1, STAGES>;
   static constexpr int kCustomEpilogue = 1;
-  static constexpr int kContiguousTiles = 1;
-  static constexpr int kBox = 32 * 128;
-  static constexpr int kBuf = 2 * kBox;           // one 32 x 128 slice: xs in, xy out in place
-  static constexpr int kSlots = 3;                // load one tile ahead while the previous
-                                                  // tile's stores may still read their slot
-  static constexpr int kWarpStage = kSlots * kBuf;
-  static constexpr int kBarOff = 4 * kWarpStage;  // kSlots mbarriers per warp after the buffers
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kBox = 32 * 128;           // one 32 x 64 slice: xs in, xy out in place
+  static constexpr int kSlots = SLOTS;            // >= 2: the next tile's slice loads while
+                                                  // this tile is drained
+  static constexpr int kWarpStage = kSlots * kBox;
+  static constexpr int kBarOff = 8 * kWarpStage;  // kSlots mbarriers per warp after the buffers
   static constexpr int kEpiSmemBytes = kBarOff + 1024;
-  struct Params {
-    CUtensorMap a_map;   // y (B,H,T,D): box 64 (k) x 128 (t)
-    CUtensorMap b_map;   // encv (H,D,N) read MN-major: box 64 (n) x 64 (k)
-    CUtensorMap xs_map;  // xs (B,T,H,N) as {N,H,T,B}: box 64 x 1 x 32 x 1 (load)
-    CUtensorMap xy_map;  // xy (B,T,H,N) as {N,H,T,B}: box 64 x 1 x 32 x 1 (store)
-    int B, T, H, D, N;
-    int tb_n, nb_n;
-    int* err;
-  };
+  using Params = GateParams;
   using Tile = LatentTile;
   struct EpiState {
     int iter;     // tiles finished by this thread
     int loaded;   // tiles whose xs slice load was issued
   };
   __device__ static int num_tiles(const Params& p) { return p.B * p.H * p.tb_n * p.nb_n; }
-  __device__ static Tile tile(const Params& p, int t) { return latent_tile(t, p.B, p.H, p.nb_n); }
+  __device__ static Tile tile(const Params& p, int t) {
+    return ORDER == 0   ? latent_tile(t, p.B, p.H, p.nb_n)
+           : ORDER == 3 ? latent_tile_chunked(t, p.B, p.H, p.nb_n, p.walk_chunk)
+                        : latent_tile_nfast(t, p.B, p.H, p.tb_n, p.nb_n);
+  }
+  __device__ static int walk_chunk(const Params& p) { return p.walk_chunk; }
+  __device__ static int b_key(const Params& p, const Tile& tl) { return tl.h * p.nb_n + tl.nb; }
   __device__ static int k_blocks(const Params& p, const Tile&) { return (p.D + 63) / 64; }
   __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x1u; }
   __device__ static void prefetch(const Params& p) {
@@ -212,34 +309,44 @@ struct GateProb {
     tma_prefetch_desc(&p.b_map);
     tma_prefetch_desc(&p.xs_map);
   }
-  __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint64_t* bar,
-                                    uint8_t* a_dst, uint8_t* b_dst) {
-    tma_load_4d(&p.a_map, bar, a_dst, kb * 64, tl.tb * 128, tl.h, tl.b);
+  __device__ static void load_b(const Params& p, const Tile& tl, int kb, uint64_t* bar,
+                                uint8_t* dst) {
+    const uint64_t keep = l2_policy_evict_last();
+    if (KW) {  // K-major weights: one 64 (k) x 128 (n) box
+      tma_load_4d_hint(&p.b_map, bar, dst, kb * 64, tl.nb * 128, tl.h, 0, keep);
+      return;
+    }
 #pragma unroll
     for (int c = 0; c < 2; ++c)
-      tma_load_4d(&p.b_map, bar, b_dst + c * 64 * 128, tl.nb * 128 + c * 64, kb * 64, tl.h, 0);
+      tma_load_4d_hint(&p.b_map, bar, dst + c * 64 * 128, tl.nb * 128 + c * 64, kb * 64, tl.h, 0,
+                       keep);
   }
-
-  __device__ static uint64_t* bar(uint8_t* epi, int quad, int slot) {
-    return reinterpret_cast<uint64_t*>(epi + kBarOff) + quad * kSlots + slot;
+  __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint64_t* bar,
+                                    uint8_t* a_dst, uint8_t* b_dst) {
+    const uint64_t keep = l2_policy_evict_last();
+    tma_load_4d_hint(&p.a_map, bar, a_dst, kb * 64, tl.tb * 128, tl.h, tl.b, keep);
+    if (ORDER != 3) load_b(p, tl, kb, bar, b_dst);
+  }
+  __device__ static int slot_warp(int row, int part) { return (row >> 5) + 4 * part; }
+  __device__ static uint64_t* bar(uint8_t* epi, int w, int slot) {
+    return reinterpret_cast<uint64_t*>(epi + kBarOff) + w * kSlots + slot;
   }
   // Load the xs slice of tile number `st.loaded` (of this CTA's walk) into its slot.
-  __device__ static void load_xs(const Params& p, const Tile& tl, int row, uint8_t* epi,
+  __device__ static void load_xs(const Params& p, const Tile& tl, int row, int part, uint8_t* epi,
                                  EpiState& st) {
-    const int quad = row >> 5;
+    const int w = slot_warp(row, part);
     const int slot = st.loaded % kSlots;
     if ((row & 31) == 0) {
       // the slot was last read by the stores of tile (loaded - kSlots); at most the
       // kSlots - 2 most recent store groups may still be reading
       bulk_wait_read<kSlots - 2>();
-      uint64_t* b = bar(epi, quad, slot);
-      uint8_t* buf = epi + quad * kWarpStage + slot * kBuf;
-      const int t0 = tl.tb * 128 + quad * 32;
-      if (t0 < p.T) {
-        mbar_arrive_expect_tx(b, 2 * kBox);
-#pragma unroll
-        for (int hb = 0; hb < 2; ++hb)
-          tma_load_4d(&p.xs_map, b, buf + hb * kBox, tl.nb * 128 + hb * 64, tl.h, t0, tl.b);
+      uint64_t* b = bar(epi, w, slot);
+      uint8_t* buf = epi + w * kWarpStage + slot * kBox;
+      const int t0 = tl.tb * 128 + (row & ~31);
+      const int n = tl.nb * 128 + part * 64;
+      if (t0 < p.T && n < p.N) {
+        mbar_arrive_expect_tx(b, kBox);
+        tma_load_4d_hint(&p.xs_map, b, buf, n, tl.h, t0, tl.b, l2_policy_evict_first());
       } else {
         mbar_arrive(b);
       }
@@ -247,80 +354,104 @@ struct GateProb {
     __syncwarp();
     ++st.loaded;
   }
-  __device__ static void epilogue_begin(const Params& p, int row, uint8_t* epi, EpiState& st,
-                                        bool has_first, const Tile& first) {
+  __device__ static void epilogue_begin(const Params& p, int row, int part, uint8_t* epi,
+                                        EpiState& st, bool has_first, const Tile& first) {
     if ((row & 31) == 0) {
-      for (int i = 0; i < kSlots; ++i) mbar_init(bar(epi, row >> 5, i), 1);
+      for (int i = 0; i < kSlots; ++i) mbar_init(bar(epi, slot_warp(row, part), i), 1);
       fence_mbar_init();
     }
     __syncwarp();
     st.iter = 0;
     st.loaded = 0;
-    if (has_first) load_xs(p, first, row, epi, st);
+    if (has_first) load_xs(p, first, row, part, epi, st);
   }
   // One tile ahead: the next tile's xs slice is requested before this tile is drained.
   __device__ static void epilogue_prefetch(const Params& p, const Tile&, bool has_next,
-                                           const Tile& next, int row, uint8_t* epi, EpiState& st) {
-    if (has_next) load_xs(p, next, row, epi, st);
+                                           const Tile& next, int row, int part, uint8_t* epi,
+                                           EpiState& st) {
+    if (has_next) load_xs(p, next, row, part, epi, st);
   }
-  __device__ static bool epilogue_tile(const Params& p, const Tile&, int row, uint32_t taddr,
-                                       uint8_t* epi, EpiState& st, volatile int* abort_flag) {
-    const int quad = row >> 5, lr = row & 31;
+  __device__ static bool epilogue_tile(const Params& p, const Tile&, int row, int part,
+                                       uint32_t taddr, uint8_t* epi, EpiState& st,
+                                       volatile int* abort_flag) {
+    const int lr = row & 31;
+    const int w = slot_warp(row, part);
     const int slot = st.iter % kSlots;
-    uint8_t* buf = epi + quad * kWarpStage + slot * kBuf;
+    uint8_t* box = epi + w * kWarpStage + slot * kBox;
     const uint32_t parity = static_cast<uint32_t>(st.iter / kSlots) & 1u;
-    if (!wait_bounded(bar(epi, quad, slot), parity, abort_flag, p.err, kErrTimeoutEpilogue))
+    if (!wait_bounded(bar(epi, w, slot), parity, abort_flag, p.err, kErrTimeoutEpilogue))
       return false;
+    uint32_t rr[2][32];
+    tmem_ld32(taddr + static_cast<uint32_t>(part * 64), rr[0]);
+    tmem_ld32(taddr + static_cast<uint32_t>(part * 64 + 32), rr[1]);
+    tmem_ld_wait();
 #pragma unroll
-    for (int c0 = 0; c0 < 128; c0 += 32) {
-      uint32_t r[32];
-      tmem_ld32(taddr + static_cast<uint32_t>(c0), r);
-      tmem_ld_wait();
-      uint8_t* box = buf + (c0 >> 6) * kBox;
-      const int j0 = (c0 & 63) >> 3;
+    for (int c0 = 0; c0 < 64; c0 += 32) {
+      const uint32_t(&r)[32] = rr[c0 >> 5];
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
-        const int off = sw128(lr, j0 + v);
+        const int off = sw128(lr, (c0 >> 3) + v);
         const uint4 xsv = *reinterpret_cast<const uint4*>(box + off);
         const uint32_t xw[4] = {xsv.x, xsv.y, xsv.z, xsv.w};
         uint32_t o[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int i = 8 * v + 2 * e;
-          const uint32_t yw =
-              cvt_bf16x2(fmaxf(__uint_as_float(r[i]), 0.0f), fmaxf(__uint_as_float(r[i + 1]), 0.0f));
-          o[e] = cvt_bf16x2(__fmul_rn(bf16x2_lo(xw[e]), bf16x2_lo(yw)),
-                            __fmul_rn(bf16x2_hi(xw[e]), bf16x2_hi(yw)));
+          o[e] = mul_bf16x2(xw[e], cvt_relu_bf16x2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])));
         }
         *reinterpret_cast<uint4*>(box + off) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
     return true;
   }
-  __device__ static void epilogue_after(const Params& p, const Tile& tl, int row, uint8_t* epi,
-                                        EpiState& st) {
-    const int quad = row >> 5;
-    uint8_t* buf = epi + quad * kWarpStage + (st.iter % kSlots) * kBuf;
+  __device__ static void epilogue_after(const Params& p, const Tile& tl, int row, int part,
+                                        uint8_t* epi, EpiState& st) {
+    uint8_t* box = epi + slot_warp(row, part) * kWarpStage + (st.iter % kSlots) * kBox;
     fence_async_smem();
     __syncwarp();
-    const int t0 = tl.tb * 128 + quad * 32;
     if ((row & 31) == 0) {
-      if (t0 < p.T) {
-#pragma unroll
-        for (int hb = 0; hb < 2; ++hb) {
-          const int n = tl.nb * 128 + hb * 64;
-          if (n < p.N) tma_store_4d(&p.xy_map, buf + hb * kBox, n, tl.h, t0, tl.b);
-        }
-      }
+      const int t0 = tl.tb * 128 + (row & ~31);
+      const int n = tl.nb * 128 + part * 64;
+      if (t0 < p.T && n < p.N)
+        tma_store_4d_hint(&p.xy_map, box, n, tl.h, t0, tl.b, l2_policy_evict_first());
       bulk_commit();
     }
     ++st.iter;
   }
-  __device__ static void epilogue_end(const Params&, int row, uint8_t*, EpiState&) {
+  __device__ static void epilogue_end(const Params&, int row, int, uint8_t*, EpiState&) {
     if ((row & 31) == 0) bulk_wait_all();
     __syncwarp();
   }
 };
+
+// Pipeline forms. Default: weights resident per column block, chunked walk, six 16 KB
+// activation stages (Encode / Gate; EncodeK / GateK read d-contiguous weights K-major).
+// BDH_SM100_LATENT_VARIANT=1 selects the streamed-operand forms (both operands through the
+// stage ring; contiguous walk for encode, column-fastest strided walk for gate), kept for
+// measurement and used for D > 256.
+using Encode = EncodeProb<6, 1, 3>;
+using EncodeK = EncodeProb<6, 1, 3, true>;
+using EncodeS = EncodeProb<5, 1, 0>;
+using EncodeSK = EncodeProb<5, 1, 0, true>;
+using Gate = GateProb<6, 2, 3>;
+using GateK = GateProb<6, 2, 3, true>;
+using GateS = GateProb<5, 2, 1>;
+using GateSK = GateProb<5, 2, 1, true>;
+
+// Row blocks per chunk of the chunked walk: the largest divisor of the row-block count <= 32.
+int walk_chunk_for(int64_t row_blocks) {
+  for (int c = 32; c > 1; --c)
+    if (row_blocks % c == 0) return c;
+  return 1;
+}
+
+int latent_variant() {
+  static int v = [] {
+    const char* e = std::getenv("BDH_SM100_LATENT_VARIANT");
+    return e ? std::atoi(e) : 0;
+  }();
+  return v;
+}
 
 bool map_x_btd(CUtensorMap* m, const void* x, const int64_t s[3], int64_t B, int64_t T, int64_t D,
                const char* what) {
@@ -334,8 +465,16 @@ bool map_bhtd(CUtensorMap* m, const void* y, const int64_t s[4], int64_t B, int6
   const int64_t st[3] = {s[2] * 2, s[1] * 2, s[0] * 2};
   return make_map_4d(m, y, 2, dims, st, 64, 128, what);
 }
+// Weights (H, D, N) with either n contiguous (s[2] == 1, read MN-major in 64 x 64 boxes) or d
+// contiguous (s[1] == 1, a transposed copy read K-major in 64 (k) x 128 (n) boxes).
+bool weight_k_major(const int64_t s[3]) { return s[1] == 1 && s[2] != 1; }
 bool map_weight(CUtensorMap* m, const void* w, const int64_t s[3], int64_t H, int64_t D, int64_t N,
                 const char* what) {
+  if (weight_k_major(s)) {
+    const int64_t dims[4] = {D, N, H, 1};
+    const int64_t st[3] = {s[2] * 2, s[0] * 2, 16};
+    return make_map_4d(m, w, 2, dims, st, 64, 128, what);
+  }
   const int64_t dims[4] = {N, D, H, 1};
   const int64_t st[3] = {s[1] * 2, s[0] * 2, 16};
   return make_map_4d(m, w, 2, dims, st, 64, 64, what);
@@ -359,7 +498,7 @@ bool map_bhtn_store(CUtensorMap* m, const void* p, const int64_t s[4], int64_t B
 }  // namespace
 
 int launch_latent_encode(const LatentArgs& a, cudaStream_t stream, int* err) {
-  EncodeProb::Params prm{};
+  EncodeParams prm{};
   if (!map_x_btd(&prm.a_map, a.x, a.x_strides, a.B, a.T, a.D, "latent_encode: x")) return BDH_ERR_INVALID;
   if (!map_weight(&prm.b_map, a.w, a.w_strides, a.H, a.D, a.N, "latent_encode: enc")) return BDH_ERR_INVALID;
   if (!map_bthn(&prm.xs_map, a.xs, a.xs_strides, a.B, a.T, a.H, a.N, "latent_encode: xs"))
@@ -375,13 +514,20 @@ int launch_latent_encode(const LatentArgs& a, cudaStream_t stream, int* err) {
   prm.pos0 = static_cast<int>(a.pos0);
   prm.tb_n = static_cast<int>((a.T + 127) / 128);
   prm.nb_n = static_cast<int>((a.N + 127) / 128);
+  prm.walk_chunk = walk_chunk_for(a.B * int64_t(prm.tb_n));
   prm.err = err;
   const int64_t ntiles = a.B * a.H * int64_t(prm.tb_n) * prm.nb_n;
-  return launch_tc<EncodeProb::S, EncodeProb>(prm, static_cast<int>(ntiles), stream, kProfEncode);
+  const bool kw = weight_k_major(a.w_strides);
+  if (a.D > 256 || latent_variant() == 1)  // resident weights hold D <= 256
+    return kw ? launch_tc<EncodeSK::S, EncodeSK>(prm, static_cast<int>(ntiles), stream, kProfEncode)
+              : launch_tc<EncodeS::S, EncodeS>(prm, static_cast<int>(ntiles), stream, kProfEncode);
+  if (kw)
+    return launch_tc<EncodeK::S, EncodeK>(prm, static_cast<int>(ntiles), stream, kProfEncode);
+  return launch_tc<Encode::S, Encode>(prm, static_cast<int>(ntiles), stream, kProfEncode);
 }
 
 int launch_latent_gate(const LatentArgs& a, cudaStream_t stream, int* err) {
-  GateProb::Params prm{};
+  GateParams prm{};
   if (!map_bhtd(&prm.a_map, a.y, a.y_strides, a.B, a.H, a.T, a.D, "latent_gate: y")) return BDH_ERR_INVALID;
   if (!map_weight(&prm.b_map, a.w, a.w_strides, a.H, a.D, a.N, "latent_gate: encv")) return BDH_ERR_INVALID;
   if (!map_bthn(&prm.xs_map, a.xs, a.xs_strides, a.B, a.T, a.H, a.N, "latent_gate: xs"))
@@ -395,9 +541,16 @@ int launch_latent_gate(const LatentArgs& a, cudaStream_t stream, int* err) {
   prm.N = static_cast<int>(a.N);
   prm.tb_n = static_cast<int>((a.T + 127) / 128);
   prm.nb_n = static_cast<int>((a.N + 127) / 128);
+  prm.walk_chunk = walk_chunk_for(a.B * int64_t(prm.tb_n));
   prm.err = err;
   const int64_t ntiles = a.B * a.H * int64_t(prm.tb_n) * prm.nb_n;
-  return launch_tc<GateProb::S, GateProb>(prm, static_cast<int>(ntiles), stream, kProfGate);
+  const bool kw = weight_k_major(a.w_strides);
+  if (a.D > 256 || latent_variant() == 1)
+    return kw ? launch_tc<GateSK::S, GateSK>(prm, static_cast<int>(ntiles), stream, kProfGate)
+              : launch_tc<GateS::S, GateS>(prm, static_cast<int>(ntiles), stream, kProfGate);
+  if (kw)
+    return launch_tc<GateK::S, GateK>(prm, static_cast<int>(ntiles), stream, kProfGate);
+  return launch_tc<Gate::S, Gate>(prm, static_cast<int>(ntiles), stream, kProfGate);
 }
 
 }  // namespace bdh

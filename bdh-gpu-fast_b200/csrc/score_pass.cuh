@@ -217,9 +217,10 @@ static int launch_tc(const typename P::Params& prm, int ntiles, cudaStream_t str
     }
     attr_set[dev] = true;
   }
-  const int grid = std::min(ntiles, sm_count(dev));
+  int grid = std::min(ntiles, sm_count(dev));
+  if constexpr (HasMaxCtas<P>::value) grid = std::max(1, std::min(grid, P::max_ctas(prm, sm_count(dev))));
   prof_start(kind, stream);
-  tc_gemm_kernel<S, P><<<grid, kTcThreads, tc_smem_bytes<S, P>(), stream>>>(prm);
+  tc_gemm_kernel<S, P><<<grid, tc_threads<P>(), tc_smem_bytes<S, P>(), stream>>>(prm);
   prof_stop(kind, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

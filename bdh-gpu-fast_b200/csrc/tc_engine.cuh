@@ -17,6 +17,7 @@
 #pragma once
 
 #include <type_traits>
+#include <utility>
 
 #include "common.cuh"
 
@@ -39,14 +40,15 @@ struct HasChunkEmit<P, std::void_t<decltype(P::kEmitEveryChunk)>> : std::true_ty
 //       after the tile loop, e.g. to drain bulk stores reading that memory).
 //   P::kCustomEpilogue -> the policy drains the accumulator itself (no KCHUNK):
 //       P::EpiState st (per epilogue thread, lives across tiles),
-//       P::epilogue_begin(prm, row, epi, st, has_first, first_tile)   once, before the tiles;
-//       P::epilogue_prefetch(prm, tile, has_next, next_tile, row, epi, st)
+//       P::epilogue_begin(prm, row, part, epi, st, has_first, first_tile)  once, before the tiles;
+//       P::epilogue_prefetch(prm, tile, has_next, next_tile, row, part, epi, st)
 //                                                         before the accumulator is ready;
-//       P::epilogue_tile(prm, tile, row, taddr, epi, st, abort_flag) -> bool
+//       P::epilogue_tile(prm, tile, row, part, taddr, epi, st, abort_flag) -> bool
 //                                                         tcgen05.ld of the tile (lane quadrant
 //                                                         base `taddr`), all loads waited;
-//       P::epilogue_after(prm, tile, row, epi, st)        after the TMEM buffer is released;
-//       P::epilogue_end(prm, row, epi, st)                once, after the last tile.
+//       P::epilogue_after(prm, tile, row, part, epi, st)  after the TMEM buffer is released;
+//       P::epilogue_end(prm, row, part, epi, st)          once, after the last tile.
+//   (`row` is the tile row = TMEM lane of the thread, `part` its column half, see kEpiWarps.)
 //   P::kContiguousTiles -> CTA i walks the contiguous tile range [i n / G, (i+1) n / G) instead
 //       of the strided list i, i + G, ... (consecutive tiles of a CTA then share operands or
 //       epilogue state).
@@ -59,19 +61,64 @@ struct HasContigTiles : std::false_type {};
 template <class P>
 struct HasContigTiles<P, std::void_t<decltype(P::kContiguousTiles)>> : std::true_type {};
 
-// Tile walk of this CTA: t = begin, begin + step, ... < end.
+//   P::kChunkedWalk + P::walk_chunk(prm) -> the tile list is cut into chunks of walk_chunk
+//       consecutive tiles; CTA i takes chunks i, i + G, ... and walks each chunk in order (the
+//       CTAs running at one time hold neighbouring chunks, each CTA keeps a chunk's operands).
+template <class P, class = void>
+struct HasChunkedWalk : std::false_type {};
 template <class P>
-__device__ __forceinline__ void tile_walk(int ntiles, int& begin, int& end, int& step) {
-  if constexpr (HasContigTiles<P>::value) {
-    begin = static_cast<int>(static_cast<long long>(blockIdx.x) * ntiles / gridDim.x);
-    end = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * ntiles / gridDim.x);
-    step = 1;
-  } else {
-    begin = static_cast<int>(blockIdx.x);
-    end = ntiles;
-    step = static_cast<int>(gridDim.x);
+struct HasChunkedWalk<P, std::void_t<decltype(P::kChunkedWalk)>> : std::true_type {};
+
+// Tile walk of this CTA: t = first, next(first), ... while t < end.
+struct TileWalk {
+  int first, end, step, chunk;  // chunk > 0: chunked walk
+  __device__ __forceinline__ int next(int t) const {
+    if (chunk > 0) return ((t + 1) % chunk != 0) ? t + 1 : t + 1 + (step - 1) * chunk;
+    return t + step;
   }
+};
+template <class P>
+__device__ __forceinline__ TileWalk tile_walk(const typename P::Params& prm, int ntiles) {
+  TileWalk w;
+  if constexpr (HasChunkedWalk<P>::value) {
+    w.chunk = P::walk_chunk(prm);
+    w.first = static_cast<int>(blockIdx.x) * w.chunk;
+    w.end = ntiles;
+    w.step = static_cast<int>(gridDim.x);
+  } else if constexpr (HasContigTiles<P>::value) {
+    w.chunk = 0;
+    w.first = static_cast<int>(static_cast<long long>(blockIdx.x) * ntiles / gridDim.x);
+    w.end = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * ntiles / gridDim.x);
+    w.step = 1;
+  } else {
+    w.chunk = 0;
+    w.first = static_cast<int>(blockIdx.x);
+    w.end = ntiles;
+    w.step = static_cast<int>(gridDim.x);
+  }
+  return w;
 }
+
+//   P::kResidentB = KBR -> the B operand of a tile (all its k-blocks, at most KBR) is kept in a
+//       dedicated shared-memory region while consecutive tiles of the CTA share it:
+//       P::b_key(prm, tile) identifies it, P::load_b(prm, tile, kb, bar, dst) loads k-block kb;
+//       the stage ring then carries only A. Needs B_TERMS == 1.
+template <class P, class = void>
+struct ResidentB {
+  static constexpr int value = 0;
+};
+template <class P>
+struct ResidentB<P, std::void_t<decltype(P::kResidentB)>> {
+  static constexpr int value = P::kResidentB;
+};
+
+//   P::max_ctas(prm, sm_count) (host) -> cap on the persistent grid (e.g. a multiple of the
+//       column-block count, so every CTA of a strided walk keeps one column block).
+template <class P, class = void>
+struct HasMaxCtas : std::false_type {};
+template <class P>
+struct HasMaxCtas<P, std::void_t<decltype(P::max_ctas(std::declval<const typename P::Params&>(), 0))>>
+    : std::true_type {};
 
 template <class P, class = void>
 struct EpiSmem {
@@ -84,6 +131,22 @@ struct EpiSmem<P, std::void_t<decltype(P::kEpiSmemBytes)>> {
 
 constexpr int kTcThreads = 192;
 constexpr int kEpiThreads = 128;
+
+//   P::kEpiWarps = 8 (custom epilogues only) -> two epilogue warps per TMEM lane quadrant, each
+//       draining half of the tile's columns (`part` 0 / 1 in the custom hooks); the CTA then
+//       has 64 + 256 threads.
+template <class P, class = void>
+struct EpiWarps {
+  static constexpr int value = 4;
+};
+template <class P>
+struct EpiWarps<P, std::void_t<decltype(P::kEpiWarps)>> {
+  static constexpr int value = P::kEpiWarps;
+};
+template <class P>
+constexpr int tc_threads() {
+  return 64 + 32 * EpiWarps<P>::value;
+}
 
 // KCHUNK_ > 0: the K-loop of a tile is cut into chunks of KCHUNK_ k-blocks, each accumulated in
 // its own TMEM buffer and summed by the epilogue in fp32 registers (round-to-nearest). This
@@ -120,7 +183,6 @@ struct TcShape {
   __host__ __device__ static int chunks(int nkb) {
     return KCHUNK == 0 ? 1 : (nkb + KCHUNK - 1) / KCHUNK;
   }
-  static_assert(STAGES * STAGE_BYTES + BAR_BYTES + 1024 <= 232448, "shared memory budget");
 
   // Byte offset of the kk-th MMA's K slice inside one term tile.
   __device__ static __forceinline__ uint32_t a_koff(int kk) {
@@ -137,12 +199,22 @@ struct TcShape {
   }
 };
 
-// Dynamic shared memory of one CTA: the stage ring, a 1 KB barrier block, the epilogue's own
-// region (if any) and 1 KB of alignment slack.
+// Bytes of one ring stage (A only when B is resident), of the ring, and of the resident B.
+template <class S, class P>
+constexpr int tc_stage_bytes() {
+  return ResidentB<P>::value > 0 ? S::A_TILE * S::A_TERMS : S::STAGE_BYTES;
+}
+template <class S, class P>
+constexpr int tc_ring_bytes() {
+  return S::STAGES * tc_stage_bytes<S, P>() + ResidentB<P>::value * S::B_TILE;
+}
+// Dynamic shared memory of one CTA: the stage ring (+ resident B), a barrier block, the
+// epilogue's own region (if any) and 1 KB of alignment slack.
 template <class S, class P>
 constexpr int tc_smem_bytes() {
-  return EpiSmem<P>::value == 0 ? S::SMEM_BYTES
-                                : S::STAGES * S::STAGE_BYTES + 1024 + EpiSmem<P>::value + 1024;
+  return EpiSmem<P>::value == 0 && ResidentB<P>::value == 0
+             ? S::SMEM_BYTES
+             : tc_ring_bytes<S, P>() + 1024 + EpiSmem<P>::value + 1024;
 }
 
 // Spin on `bar` ignoring the abort flag (used to drain in-flight async work before exit).
@@ -159,24 +231,32 @@ __device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity, int* 
 }
 
 template <class S, class P>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(tc_threads<P>(), 1)
     tc_gemm_kernel(const __grid_constant__ typename P::Params prm) {
+  static_assert(EpiWarps<P>::value == 4 || (EpiWarps<P>::value == 8 && HasCustomEpi<P>::value),
+                "eight epilogue warps need a custom epilogue");
   static_assert(tc_smem_bytes<S, P>() <= 232448, "shared memory budget");
+  static_assert(ResidentB<P>::value == 0 || S::B_TERMS == 1, "resident B holds one term");
+  static_assert(S::STAGES <= 8, "barrier block layout");
+  constexpr bool kRes = ResidentB<P>::value > 0;
+  constexpr int SB = tc_stage_bytes<S, P>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::STAGES * S::STAGE_BYTES);
+  uint8_t* bres = smem + S::STAGES * SB;  // resident B (kRes)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + tc_ring_bytes<S, P>());
   uint64_t* empty = full + S::STAGES;
   uint64_t* tfull = empty + S::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* full_b = drain + 1;
+  uint64_t* empty_b = full_b + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(empty_b + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int ntiles = P::num_tiles(prm);
-  int t_begin, t_end, t_step;
-  tile_walk<P>(ntiles, t_begin, t_end, t_step);
+  const TileWalk walk = tile_walk<P>(prm, ntiles);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::STAGES; ++s) {
@@ -185,9 +265,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull + a, 1);
-      mbar_init(tempty + a, kEpiThreads);
+      mbar_init(tempty + a, 32 * EpiWarps<P>::value);
     }
     mbar_init(drain, 1);
+    mbar_init(full_b, 1);
+    mbar_init(empty_b, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -204,21 +286,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int stage = 0;
       uint32_t ph = 0;
       uint32_t n_issued = 0;
+      int b_loads = 0;
+      int b_key = 0;
       bool ok = true;
-      for (int t = t_begin; t < t_end && ok; t += t_step) {
+      for (int t = walk.first; t < walk.end && ok; t = walk.next(t)) {
         typename P::Tile tile = P::tile(prm, t);
         const int nkb = P::k_blocks(prm, tile);
+        if constexpr (kRes) {
+          const int key = P::b_key(prm, tile);
+          if (b_loads == 0 || key != b_key) {
+            // the MMAs that read the previous B must have completed
+            if (b_loads > 0 &&
+                !wait_bounded(empty_b, static_cast<uint32_t>(b_loads - 1) & 1u, abort_flag, prm.err,
+                              kErrTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(full_b, static_cast<uint32_t>(nkb * S::B_TILE));
+            for (int kb = 0; kb < nkb; ++kb) P::load_b(prm, tile, kb, full_b, bres + kb * S::B_TILE);
+            ++b_loads;
+            b_key = key;
+          }
+        }
         for (int kb = 0; kb < nkb; ++kb) {
           if (*abort_flag ||
               !wait_bounded(empty + stage, ph ^ 1u, abort_flag, prm.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
-          uint32_t tx = S::STAGE_BYTES;
+          uint32_t tx = SB;
           if constexpr (HasStageTx<P>::value) tx = P::stage_tx(prm, tile, kb);
           mbar_arrive_expect_tx(full + stage, tx);
-          uint8_t* a_dst = smem + stage * S::STAGE_BYTES;
-          uint8_t* b_dst = a_dst + S::A_TERMS * S::A_TILE;
+          uint8_t* a_dst = smem + stage * SB;
+          uint8_t* b_dst = kRes ? nullptr : a_dst + S::A_TERMS * S::A_TILE;
           P::load_stage(prm, tile, kb, full + stage, a_dst, b_dst);
           ++n_issued;
           if (++stage == S::STAGES) {
@@ -234,6 +334,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           wait_drain(full + s, k_last & 1u, prm.err);
         }
       }
+      if (kRes && b_loads > 0) wait_drain(full_b, static_cast<uint32_t>(b_loads - 1) & 1u, prm.err);
     }
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer
@@ -243,16 +344,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (elect_one()) {
       const uint32_t base = smem_u32(smem);
       const uint64_t a0 = S::a_desc(base);
-      const uint64_t b0 = S::b_desc(base + S::A_TERMS * S::A_TILE);
+      // ring-relative B (stage offset added) or the resident region (k-block offset added)
+      const uint64_t b0 = kRes ? S::b_desc(smem_u32(bres)) : S::b_desc(base + S::A_TERMS * S::A_TILE);
       int stage = 0;
-      uint32_t soff16 = 0;  // stage * STAGE_BYTES / 16
+      uint32_t soff16 = 0;  // stage * SB / 16
       uint32_t ph = 0;
       int lc = 0;  // accumulation chunks issued by this CTA (selects the TMEM buffer)
+      int b_uses = 0;
+      int b_key = 0;
       bool ok = true;
-      for (int t = t_begin; t < t_end && ok; t += t_step) {
+      for (int t = walk.first; t < walk.end && ok; t = walk.next(t)) {
         typename P::Tile tile = P::tile(prm, t);
         const int nkb = P::k_blocks(prm, tile);
         const int nch = S::chunks(nkb);
+        if constexpr (kRes) {
+          const int key = P::b_key(prm, tile);
+          if (b_uses == 0 || key != b_key) {
+            if (b_uses > 0) umma_commit(empty_b);  // arrives once the old B's MMAs complete
+            if (!wait_bounded(full_b, static_cast<uint32_t>(b_uses) & 1u, abort_flag, prm.err,
+                              kErrTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            ++b_uses;
+            b_key = key;
+          }
+        }
         for (int ch = 0; ch < nch && ok; ++ch, ++lc) {
           const int acc = lc & 1;
           const uint32_t aph = static_cast<uint32_t>(lc >> 1) & 1u;
@@ -280,7 +398,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int ta = (pr == 1 && S::A_TERMS == 2) ? 1 : 0;
                 const int tb = (pr == 2 || (pr == 1 && S::A_TERMS == 1)) ? 1 : 0;
                 const uint64_t ad = a0 + (soff16 + ((ta * S::A_TILE + S::a_koff(kk)) >> 4));
-                const uint64_t bd = b0 + (soff16 + ((tb * S::B_TILE + S::b_koff(kk)) >> 4));
+                const uint64_t bd =
+                    kRes ? b0 + static_cast<uint32_t>((kb * S::B_TILE + S::b_koff(kk)) >> 4)
+                         : b0 + (soff16 + ((tb * S::B_TILE + S::b_koff(kk)) >> 4));
                 const uint32_t accumulate = (kb > kb0 || kk > 0 || pr > 0) ? 1u : 0u;
                 if (S::ELEM == 2)
                   umma_f16(d_tmem, ad, bd, S::IDESC, accumulate);
@@ -294,7 +414,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               soff16 = 0;
               ph ^= 1u;
             } else {
-              soff16 += S::STAGE_BYTES >> 4;
+              soff16 += SB >> 4;
             }
           }
           if (!ok) break;
@@ -309,17 +429,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---------------------------------------------------------------- epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + static_cast<int>(lane_id());
-    uint8_t* epi = smem + S::STAGES * S::STAGE_BYTES + 1024;
+    const int part = (warp - 2) >> 2;  // column half (eight epilogue warps) or 0
+    uint8_t* epi = smem + tc_ring_bytes<S, P>() + 1024;
     (void)epi;
     int lc = 0;
     bool ok = true;
     if constexpr (HasCustomEpi<P>::value) {
       typename P::EpiState st{};
-      P::epilogue_begin(prm, row, epi, st, t_begin < t_end, P::tile(prm, t_begin < t_end ? t_begin : 0));
-      for (int t = t_begin; t < t_end && ok; t += t_step) {
+      P::epilogue_begin(prm, row, part, epi, st, walk.first < walk.end,
+                        P::tile(prm, walk.first < walk.end ? walk.first : 0));
+      for (int t = walk.first; t < walk.end && ok; t = walk.next(t)) {
         typename P::Tile tile = P::tile(prm, t);
-        const bool has_next = t + t_step < t_end;
-        P::epilogue_prefetch(prm, tile, has_next, P::tile(prm, has_next ? t + t_step : t), row, epi, st);
+        const int tn = walk.next(t);
+        const bool has_next = tn < walk.end;
+        P::epilogue_prefetch(prm, tile, has_next, P::tile(prm, has_next ? tn : t), row, part, epi,
+                             st);
         const int acc = lc & 1;
         const uint32_t aph = static_cast<uint32_t>(lc >> 1) & 1u;
         ok = wait_bounded(tfull + acc, aph, abort_flag, prm.err, kErrTimeoutEpilogue);
@@ -330,7 +454,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_after();
         const uint32_t tbase =
             tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * S::BN);
-        ok = P::epilogue_tile(prm, tile, row, tbase, epi, st, abort_flag);
+        ok = P::epilogue_tile(prm, tile, row, part, tbase, epi, st, abort_flag);
         tc_fence_before();
         mbar_arrive(tempty + acc);
         ++lc;
@@ -338,11 +462,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           ok = false;
           break;
         }
-        P::epilogue_after(prm, tile, row, epi, st);
+        P::epilogue_after(prm, tile, row, part, epi, st);
       }
-      P::epilogue_end(prm, row, epi, st);
+      P::epilogue_end(prm, row, part, epi, st);
     } else {
-    for (int t = t_begin; t < t_end && ok; t += t_step) {
+    for (int t = walk.first; t < walk.end && ok; t = walk.next(t)) {
       typename P::Tile tile = P::tile(prm, t);
       if (S::KCHUNK == 0) {
         const int acc = lc & 1;

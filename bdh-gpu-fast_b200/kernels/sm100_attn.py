@@ -74,8 +74,13 @@ def _declare(lib: ctypes.CDLL) -> None:
                                       _i64, _i64, _i64, _i64, _i64, _i64, _vp]
     lib.bdh_latent_gate.argtypes = [_vp, P, _vp, _c_i64_3p, _vp, P, _vp, P,
                                     _i64, _i64, _i64, _i64, _i64, _vp]
+    lib.bdh_layernorm.argtypes = [_vp, ctypes.c_int, _i64, _vp, ctypes.c_int, _i64, _i64, _i64,
+                                  ctypes.c_float, _vp]
+    lib.bdh_residual_layernorm.argtypes = [_vp, _i64, _vp, ctypes.c_int, _i64, _vp, _i64, _vp,
+                                           _i64, _i64, _i64, ctypes.c_float, _vp]
     for name in ("bdh_rope_rotate", "bdh_tril_score_v", "bdh_tril_decode", "bdh_tril_score_v_bwd",
-                 "bdh_relu_mul", "bdh_latent_encode", "bdh_latent_gate"):
+                 "bdh_relu_mul", "bdh_latent_encode", "bdh_latent_gate", "bdh_layernorm",
+                 "bdh_residual_layernorm"):
         getattr(lib, name).restype = ctypes.c_int
 
 
@@ -229,7 +234,7 @@ def _tma_ready(x: torch.Tensor) -> torch.Tensor:
 # Kernel kinds of the launch-timing hook, in the order of bdh_profile_end's arrays
 # (BDH_PROF_KINDS in include/bdh_sm100.h).
 PROF_KINDS = ("score", "value", "rope", "decode", "grad_q", "grad_v", "split", "gated_product",
-              "state", "encode", "gate")
+              "state", "encode", "gate", "norm")
 
 
 def profile_begin() -> None:
@@ -377,7 +382,7 @@ def _check_paired_freqs(f: torch.Tensor) -> None:
 _c_i64_3 = ctypes.c_int64 * 3
 
 
-def _check_latent(name: str, *ts: torch.Tensor) -> None:
+def _check_latent(name: str, *ts: torch.Tensor, weight: Optional[torch.Tensor] = None) -> None:
     for t in ts:
         if t.dtype != torch.bfloat16:
             raise TypeError(f"{name}: bf16 tensors required, got {t.dtype}")
@@ -385,11 +390,26 @@ def _check_latent(name: str, *ts: torch.Tensor) -> None:
                 st % 8 != 0 for st, sz in zip(t.stride()[:-1], t.shape[:-1]) if sz > 1):
             raise ValueError(f"{name}: tensors need a contiguous last dim, 16-byte aligned base "
                              "and strides that are multiples of 8 elements")
+    if weight is not None:
+        if weight.dtype != torch.bfloat16:
+            raise TypeError(f"{name}: bf16 weights required, got {weight.dtype}")
+        s = weight.stride()
+        k_major = s[1] == 1 and s[2] != 1 and s[0] % 8 == 0 and s[2] % 8 == 0
+        if not k_major:
+            _check_latent(name, weight)
+        elif weight.data_ptr() % 16 != 0:
+            raise ValueError(f"{name}: weights need a 16-byte aligned base")
+
+
+def weight_k_major(w: torch.Tensor) -> torch.Tensor:
+    """(H, D, N) weights as a view of a contiguous (H, N, D) copy: the layout the latent kernels
+    read K-major (faster than the n-contiguous layout)."""
+    return w.transpose(1, 2).contiguous().transpose(1, 2)
 
 
 def _st(t: torch.Tensor, n: int):
     # strides of size-1 dims are never stepped; give them a legal value
-    st = [s if (sz > 1 or s % 8 == 0) else 8 for s, sz in zip(t.stride(), t.shape)]
+    st = [s if (sz > 1 or s % 8 == 0 or s == 1) else 8 for s, sz in zip(t.stride(), t.shape)]
     st[-1] = t.stride(-1)
     return (_c_i64_3 if n == 3 else _c_i64_4)(*st)
 
@@ -420,7 +440,7 @@ def latent_encode(x: torch.Tensor, enc: torch.Tensor, freqs: torch.Tensor, pos0:
         qr_out = torch.empty(B, H, T, N, dtype=torch.bfloat16, device=dev)
     if tuple(xs_out.shape) != (B, T, H, N) or tuple(qr_out.shape) != (B, H, T, N):
         raise ValueError("latent_encode: xs_out must be (B,T,H,N) and qr_out (B,H,T,N)")
-    _check_latent("latent_encode", x, enc, xs_out, qr_out)
+    _check_latent("latent_encode", x, xs_out, qr_out, weight=enc)
     with torch.cuda.device(dev):
         rc = lib.bdh_latent_encode(x.data_ptr(), _st(x, 3), enc.data_ptr(), _st(enc, 3),
                                    xs_out.data_ptr(), _st(xs_out, 4), qr_out.data_ptr(),
@@ -449,13 +469,75 @@ def latent_gate(y: torch.Tensor, encv: torch.Tensor, xs: torch.Tensor, *,
         out = torch.empty(B, T, H, N, dtype=torch.bfloat16, device=dev)
     elif tuple(out.shape) != (B, T, H, N):
         raise ValueError("latent_gate: out must be (B,T,H,N)")
-    _check_latent("latent_gate", y, encv, xs, out)
+    _check_latent("latent_gate", y, xs, out, weight=encv)
     with torch.cuda.device(dev):
         rc = lib.bdh_latent_gate(y.data_ptr(), _st(y, 4), encv.data_ptr(), _st(encv, 3),
                                  xs.data_ptr(), _st(xs, 4), out.data_ptr(), _st(out, 4),
                                  B, T, H, D, N, _stream(dev))
     _check(rc, "latent_gate")
     return out
+
+
+# ---------------------------------------------------------------------- layer norms
+def _rows_view(t: torch.Tensor):
+    """(rows, D) with one row stride, or None when t's leading dims do not flatten to one."""
+    if t.stride(-1) != 1:
+        return None
+    try:
+        v = t.view(-1, t.size(-1))
+    except RuntimeError:
+        return None
+    return v
+
+
+def layer_norm(x: torch.Tensor, eps: float = 1e-5, out_dtype: Optional[torch.dtype] = None,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Affine-free LayerNorm over the last dim (``F.layer_norm(x, (D,), eps=eps)``), fp32 math,
+    result stored in ``out_dtype`` (default: x's dtype). One kernel, no fp32 intermediate."""
+    dev = _require_cuda(x)
+    lib = _require_lib()
+    D = x.size(-1)
+    xv = _rows_view(x)
+    if xv is None:
+        xv = x.contiguous().view(-1, D)
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=dev)
+    ov = _rows_view(out)
+    if ov is None or ov.size(0) != xv.size(0):
+        raise ValueError("layer_norm: out must be row-contiguous with x's shape")
+    with torch.cuda.device(dev):
+        rc = lib.bdh_layernorm(xv.data_ptr(), _code(xv.dtype), xv.stride(0) if xv.size(0) > 1 else D,
+                               ov.data_ptr(), _code(ov.dtype), ov.stride(0) if ov.size(0) > 1 else D,
+                               xv.size(0), D, float(eps), _stream(dev))
+    _check(rc, "layer_norm")
+    return out
+
+
+def residual_layer_norm(x: torch.Tensor, y: torch.Tensor, eps: float = 1e-5,
+                        want_bf16: bool = False):
+    """``LN(x + LN(y))`` over the last dim (BDH._residual_ln): x fp32, y fp32 or bf16. Returns
+    the fp32 result and, with ``want_bf16``, its bf16 copy (else None)."""
+    if x.dtype != torch.float32 or x.shape != y.shape:
+        raise ValueError("residual_layer_norm: x must be fp32 and y of x's shape")
+    dev = _require_cuda(x, y)
+    lib = _require_lib()
+    D = x.size(-1)
+    xv = _rows_view(x)
+    if xv is None:
+        xv = x.contiguous().view(-1, D)
+    yv = _rows_view(y)
+    if yv is None:
+        yv = y.contiguous().view(-1, D)
+    out = torch.empty(x.shape, dtype=torch.float32, device=dev)
+    out16 = torch.empty(x.shape, dtype=torch.bfloat16, device=dev) if want_bf16 else None
+    rs = lambda v: v.stride(0) if v.size(0) > 1 else D  # noqa: E731
+    with torch.cuda.device(dev):
+        rc = lib.bdh_residual_layernorm(
+            xv.data_ptr(), rs(xv), yv.data_ptr(), _code(yv.dtype), rs(yv), out.data_ptr(), D,
+            out16.data_ptr() if out16 is not None else None, D, xv.size(0), D, float(eps),
+            _stream(dev))
+    _check(rc, "residual_layer_norm")
+    return out, out16
 
 
 # --------------------------------------------------------------------------- decode

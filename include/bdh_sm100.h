@@ -187,7 +187,9 @@ int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* 
  *   qr[b,h,t,n] = RoPE(xs[b,t,h,:])[n] at position pos0 + t       qr (B,H,T,N) strided
  * freqs must come in equal pairs (freqs[2p] == freqs[2p+1], as bdh.py:41-49 builds them).
  * Strides are in elements: x_strides {b,t,d}, enc_strides {h,d,n}, xs_strides {b,t,h,n},
- * qr_strides {b,h,t,n}; the last stride of each must be 1, the others multiples of 8.
+ * qr_strides {b,h,t,n}; the last stride of each must be 1, the others multiples of 8 — except
+ * the weights, which may instead have d contiguous (a transposed (H,N,D) copy seen as (H,D,N),
+ * enc_strides {N*D, 1, D}); that layout is read K-major and is the faster one.
  *
  * bdh_latent_gate replaces the encoder_v projection + ReLU and the sparse product of
  * bdh.py:914-945 (BDH._encoder_v_relu and the x * y of _mlp_merge):
@@ -205,15 +207,34 @@ int bdh_latent_gate(const void* y, const int64_t y_strides[4], const void* encv,
                     int64_t D, int64_t N, void* stream);
 
 /*
+ * Affine-free LayerNorm over the last dimension, as the BDH layer applies it with F.layer_norm
+ * (BDH._ln, bdh.py:565-575; on the attention output at bdh.py:1044):
+ *   y[r, :] = (x[r, :] - mean_r) / sqrt(var_r + eps),  r < rows, biased variance, fp32 math.
+ * x and y are f32 or bf16 (BDH_DTYPE_*), rows of D elements at the given row strides (elements).
+ * D must be a multiple of 8 and at most 1024; strides multiples of 8; bases 16-byte aligned.
+ */
+int bdh_layernorm(const void* x, int x_dtype, int64_t x_row_stride, void* y, int y_dtype,
+                  int64_t y_row_stride, int64_t rows, int64_t D, float eps, void* stream);
+/*
+ * Residual double LayerNorm of the BDH layer, out = LN(x + LN(y)) (BDH._residual_ln,
+ * bdh.py:731-750): x and out f32, y f32 or bf16 (the decoder output). out_bf16 (may be NULL)
+ * receives bf16(out), the copy the next layer's encoder projection reads.
+ */
+int bdh_residual_layernorm(const float* x, int64_t x_row_stride, const void* y, int y_dtype,
+                           int64_t y_row_stride, float* out, int64_t out_row_stride,
+                           void* out_bf16, int64_t out_bf16_row_stride, int64_t rows, int64_t D,
+                           float eps, void* stream);
+
+/*
  * Launch timing for benchmarks (no counterpart in the reference, which timed whole calls with
  * perf_counter, benchmarks/bench_gpu_attn.py:263-280). Between begin and end, every kernel of
  * this library is bracketed by CUDA events on its own stream; end synchronises them and
  * returns the summed device milliseconds and launch counts per kernel kind:
  *   0 score pass, 1 value pass, 2 RoPE, 3 decode, 4 grad-Q pass, 5 grad-V pass, 6 split/transpose,
  *   7 gated product (bdh_relu_mul), 8 state pass of the chunked forward,
- *   9 latent encode (bdh_latent_encode), 10 latent gate (bdh_latent_gate).
+ *   9 latent encode (bdh_latent_encode), 10 latent gate (bdh_latent_gate), 11 LayerNorms.
  */
-#define BDH_PROF_KINDS 11
+#define BDH_PROF_KINDS 12
 int bdh_profile_begin(void);
 int bdh_profile_end(double ms[BDH_PROF_KINDS], int launches[BDH_PROF_KINDS]);
 

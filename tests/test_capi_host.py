@@ -105,3 +105,14 @@ def test_latent_entry_points_validate_on_host():
     assert rc == 1 and b"stride" in lib.bdh_last_error()
     # empty problems are a no-op
     assert lib.bdh_latent_encode(None, s3, None, s3, None, s4, None, s4, None, 0, 16, 2, 256, 64, 0, None) == 0
+
+
+def test_layernorm_entry_points_validate_on_host():
+    from kernels import sm100_attn as sa
+
+    lib = sa.load_library()
+    rc = lib.bdh_layernorm(None, 1, 12, None, 1, 12, 4, 12, 1e-5, None)
+    assert rc == 1 and b"multiple of 8" in lib.bdh_last_error()
+    rc = lib.bdh_residual_layernorm(None, 256, None, 7, 256, None, 256, None, 256, 4, 256, 1e-5, None)
+    assert rc == 1 and b"dtype" in lib.bdh_last_error()
+    assert lib.bdh_layernorm(None, 1, 256, None, 1, 256, 0, 256, 1e-5, None) == 0

@@ -229,3 +229,49 @@ def test_model_latent_prefill_then_decode(monkeypatch):
         b = run("0", storage)
         r = ((a - b).norm() / b.norm()).item()
         assert r < 3e-3, (storage, r)
+
+
+@pytest.mark.parametrize("D,N", [(256, 1024), (96, 520)])
+def test_latent_k_major_weights_match_n_major(D, N):
+    """Weights given as a transposed (H, N, D) copy (read K-major) give the same bits as the
+    n-contiguous (H, D, N) layout: the MMAs accumulate over the same k order."""
+    B, T, H = 2, 150, 3
+    g = torch.Generator().manual_seed(D + N)
+    x = torch.randn(B, T, D, generator=g).to(torch.bfloat16).to(DEV)
+    y = torch.randn(B, H, T, D, generator=g).to(torch.bfloat16).to(DEV)
+    enc = (torch.randn(H, D, N, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    encv = (torch.randn(H, D, N, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    freqs = torch.as_tensor(O.get_freqs(N)).to(DEV)
+    xs_n, qr_n = sa().latent_encode(x, enc, freqs, 3)
+    enc_k = sa().weight_k_major(enc)
+    assert enc_k.stride(1) == 1 and torch.equal(enc_k, enc)
+    xs_k, qr_k = sa().latent_encode(x, enc_k, freqs, 3)
+    assert torch.equal(xs_n, xs_k) and torch.equal(qr_n, qr_k)
+    xy_n = sa().latent_gate(y, encv, xs_n)
+    xy_k = sa().latent_gate(y, sa().weight_k_major(encv), xs_n)
+    assert torch.equal(xy_n, xy_k)
+
+
+@pytest.mark.parametrize("shape", [(2, 4, 300, 256), (3, 200), (5, 7, 520)])
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_layer_norm_matches_torch(shape, dt):
+    g = torch.Generator(device=DEV).manual_seed(len(shape))
+    x = (torch.randn(*shape, device=DEV, generator=g) * 3 + 1).to(dt)
+    ref = F.layer_norm(x.float(), (shape[-1],), eps=1e-5)
+    y32 = sa().layer_norm(x, 1e-5, out_dtype=torch.float32)
+    assert ((y32 - ref).norm() / ref.norm()).item() < 1e-6
+    y16 = sa().layer_norm(x, 1e-5, out_dtype=torch.bfloat16)
+    assert (y16 != ref.to(torch.bfloat16)).float().mean().item() < 1e-2
+    assert torch.equal(y16, y32.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("D", [256, 200])
+@pytest.mark.parametrize("ydt", [torch.float32, torch.bfloat16])
+def test_residual_layer_norm_matches_torch(D, ydt):
+    g = torch.Generator(device=DEV).manual_seed(D)
+    x = torch.randn(4, 150, D, device=DEV, generator=g)
+    y = (torch.randn(4, 150, D, device=DEV, generator=g) * 0.1).to(ydt)
+    out, out16 = sa().residual_layer_norm(x, y, 1e-5, want_bf16=True)
+    ref = F.layer_norm(x + F.layer_norm(y.float(), (D,), eps=1e-5), (D,), eps=1e-5)
+    assert ((out - ref).norm() / ref.norm()).item() < 1e-6
+    assert torch.equal(out16, out.to(torch.bfloat16))
