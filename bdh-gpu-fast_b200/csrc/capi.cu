@@ -172,6 +172,37 @@ bool latent_sizes_ok(int64_t B, int64_t T, int64_t H, int64_t D, int64_t N, std:
   return true;
 }
 }  // namespace
+
+// Validated decode of the C entry points (bdh_tril_decode, bdh_tril_decode_noalloc); `qrot`
+// (B*H*Tq*N fp32) receives the rotated queries when freqs is given, or is null to rotate them
+// inside the decode kernel.
+int decode_entry(const void* q, const int64_t q_strides[4], int q_dtype, const void* k_past,
+                 const int64_t k_strides[4], const void* v_past, const int64_t v_strides[4],
+                 int kv_dtype, void* out, const int64_t out_strides[4], int64_t B, int64_t H,
+                 int64_t Hv, int64_t Tq, int64_t S, int64_t N, int64_t D, const float* freqs,
+                 int64_t pos, void* kr_slot, const int64_t slot_strides[4], float* partial,
+                 float* qrot, int64_t max_splits, void* stream) {
+  if (!dtype_ok(q_dtype) || !dtype_ok(kv_dtype)) return fail(BDH_ERR_INVALID, "tril_decode: dtype must be f32 or bf16");
+  if (B < 0 || H < 0 || Tq < 0 || S < 0 || N < 0 || D < 0) return fail(BDH_ERR_INVALID, "tril_decode: negative size");
+  if (Hv != 1 && Hv != H) return fail(BDH_ERR_INVALID, "tril_decode: v_past heads must equal q heads or 1");
+  if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || out_strides[3] != 1)
+    return fail(BDH_ERR_INVALID, "tril_decode: last dimension must be contiguous");
+  if (kr_slot != nullptr && (freqs == nullptr || slot_strides == nullptr || slot_strides[3] != 1))
+    return fail(BDH_ERR_INVALID, "tril_decode: kr_slot needs freqs and contiguous slot rows");
+  if (B * H * Tq == 0) return BDH_OK;
+  if (S > (int64_t(1) << 30) || N > 48 * 1024) return fail(BDH_ERR_INVALID, "tril_decode: sizes beyond the supported range");
+  if (freqs != nullptr && (N % 2) != 0) return fail(BDH_ERR_INVALID, "tril_decode: fused RoPE needs an even latent width");
+  DecodeArgs a;
+  a.q = q; a.q_dtype = q_dtype; a.k = k_past; a.v = v_past; a.kv_dtype = kv_dtype; a.out = out;
+  std::memcpy(a.q_strides, q_strides, sizeof(a.q_strides));
+  std::memcpy(a.k_strides, k_strides, sizeof(a.k_strides));
+  std::memcpy(a.v_strides, v_strides, sizeof(a.v_strides));
+  std::memcpy(a.out_strides, out_strides, sizeof(a.out_strides));
+  a.B = B; a.H = H; a.Hv = Hv; a.Tq = Tq; a.S = S; a.N = N; a.D = D;
+  a.freqs = freqs; a.pos = pos; a.slot = kr_slot;
+  if (slot_strides != nullptr) std::memcpy(a.slot_strides, slot_strides, sizeof(a.slot_strides));
+  return launch_decode(a, partial, qrot, max_splits, static_cast<cudaStream_t>(stream));
+}
 }  // namespace bdh
 
 using namespace bdh;
@@ -404,8 +435,10 @@ int bdh_set_forward_algo(int algo) {
   return g_fwd_algo.exchange(algo);
 }
 
-size_t bdh_tril_decode_workspace_size(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t D) {
-  return decode_workspace_bytes(B, H, Tq, S, D);
+size_t bdh_tril_decode_workspace_size(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N,
+                                      int64_t D) {
+  if (B < 0 || H < 0 || Tq < 0 || S < 0 || N < 0 || D < 0) return 0;
+  return decode_workspace_bytes(B, H, Tq, S, N, D);
 }
 
 int bdh_tril_decode(const void* q, const int64_t q_strides[4], int q_dtype, const void* k_past,
@@ -414,31 +447,21 @@ int bdh_tril_decode(const void* q, const int64_t q_strides[4], int q_dtype, cons
                     int64_t Hv, int64_t Tq, int64_t S, int64_t N, int64_t D, const float* freqs,
                     int64_t pos, void* kr_slot, const int64_t slot_strides[4], void* workspace,
                     size_t workspace_bytes, void* stream) {
-  if (!dtype_ok(q_dtype) || !dtype_ok(kv_dtype)) return fail(BDH_ERR_INVALID, "tril_decode: dtype must be f32 or bf16");
-  if (B < 0 || H < 0 || Tq < 0 || S < 0 || N < 0 || D < 0) return fail(BDH_ERR_INVALID, "tril_decode: negative size");
-  if (Hv != 1 && Hv != H) return fail(BDH_ERR_INVALID, "tril_decode: v_past heads must equal q heads or 1");
-  if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || out_strides[3] != 1)
-    return fail(BDH_ERR_INVALID, "tril_decode: last dimension must be contiguous");
-  if (kr_slot != nullptr && (freqs == nullptr || slot_strides == nullptr || slot_strides[3] != 1))
-    return fail(BDH_ERR_INVALID, "tril_decode: kr_slot needs freqs and contiguous slot rows");
+  if (B < 0 || H < 0 || Tq < 0 || S < 0 || N < 0 || D < 0)
+    return fail(BDH_ERR_INVALID, "tril_decode: negative size");
   if (B * H * Tq == 0) return BDH_OK;
-  if (S > (int64_t(1) << 30) || N > 48 * 1024) return fail(BDH_ERR_INVALID, "tril_decode: sizes beyond the supported range");
-  const size_t need = decode_workspace_bytes(B, H, Tq, S, D);
+  const size_t need = decode_workspace_bytes(B, H, Tq, S, N, D);
   if (workspace == nullptr || workspace_bytes < need) {
     std::ostringstream os;
     os << "tril_decode: workspace of " << need << " bytes required, got " << workspace_bytes;
     return fail(BDH_ERR_WORKSPACE, os.str());
   }
-  DecodeArgs a;
-  a.q = q; a.q_dtype = q_dtype; a.k = k_past; a.v = v_past; a.kv_dtype = kv_dtype; a.out = out;
-  std::memcpy(a.q_strides, q_strides, sizeof(a.q_strides));
-  std::memcpy(a.k_strides, k_strides, sizeof(a.k_strides));
-  std::memcpy(a.v_strides, v_strides, sizeof(a.v_strides));
-  std::memcpy(a.out_strides, out_strides, sizeof(a.out_strides));
-  a.B = B; a.H = H; a.Hv = Hv; a.Tq = Tq; a.S = S; a.N = N; a.D = D;
-  a.freqs = freqs; a.pos = pos; a.slot = kr_slot;
-  if (slot_strides != nullptr) std::memcpy(a.slot_strides, slot_strides, sizeof(a.slot_strides));
-  return launch_decode(a, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream));
+  float* partial = static_cast<float*>(workspace);
+  float* qrot = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                         decode_partial_bytes(B, H, Tq, S, N, D));
+  return decode_entry(q, q_strides, q_dtype, k_past, k_strides, v_past, v_strides, kv_dtype, out,
+                      out_strides, B, H, Hv, Tq, S, N, D, freqs, pos, kr_slot, slot_strides, partial,
+                      qrot, 0, stream);
 }
 
 size_t bdh_tril_score_v_bwd_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,

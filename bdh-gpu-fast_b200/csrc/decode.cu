@@ -12,6 +12,7 @@
 //   3. the CTA forms its partial out = sum_j s_j V_j (one thread per output column);
 //   4. a second small kernel sums the per-split partials in a fixed order (deterministic).
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <sstream>
 #include <string>
@@ -26,9 +27,7 @@ namespace {
 
 constexpr int kDecThreads = 256;
 constexpr int kDecWarps = kDecThreads / 32;
-constexpr int kDecRowsMax = 128;  // cached rows per CTA: 64 for fp32 caches, 128 for bf16 (same bytes)
-
-__host__ __device__ constexpr int dec_rows(int kv_elem_bytes) { return kv_elem_bytes == 4 ? 64 : 128; }
+constexpr int kDecRowsMax = 128;  // cached rows per CTA at most (the plan picks 16..128)
 
 __device__ __forceinline__ float bf16_round_d(float x) { return bf16_round_f32(x); }
 
@@ -112,11 +111,10 @@ __global__ void __launch_bounds__(kDecThreads) decode_partial_kernel(
     float* __restrict__ partial, TK* __restrict__ slot, const float* __restrict__ freqs,
     int H, int Hv, int Tq, int S, int N, int D, int64_t qsb, int64_t qsh, int64_t qst,
     int64_t ksb, int64_t ksh, int64_t kst, int64_t vsb, int64_t vsh, int64_t vst, int64_t ssb,
-    int64_t ssh, int64_t sst, int64_t pos) {
-  constexpr int kDecRows = dec_rows(sizeof(TK));
+    int64_t ssh, int64_t sst, int64_t pos, int kDecRows) {
   extern __shared__ float dsm[];
   float* qs = dsm;              // N floats
-  float* sc = dsm + N;          // kDecRows scores
+  float* sc = dsm + N;          // kDecRows (<= kDecRowsMax) scores
   const int split = blockIdx.x;
   const int bh = blockIdx.y;
   const int tq = blockIdx.z;
@@ -150,6 +148,12 @@ __global__ void __launch_bounds__(kDecThreads) decode_partial_kernel(
         st_elem(sr, n + 1, y1);
       }
     }
+  } else if (sizeof(TQ) == 4 && (N & 3) == 0 && (reinterpret_cast<uintptr_t>(qr) & 15u) == 0) {
+    // fp32 rows (the rotated queries): 16-byte loads, all of a thread's loads in flight at once
+    const float4* q4 = reinterpret_cast<const float4*>(qr);
+    float4* s4 = reinterpret_cast<float4*>(qs);
+#pragma unroll 8
+    for (int n = threadIdx.x; n < (N >> 2); n += kDecThreads) s4[n] = __ldg(q4 + n);
   } else {
     for (int n = threadIdx.x; n < N; n += blockDim.x) qs[n] = ld_elem(qr, n);
   }
@@ -203,22 +207,93 @@ __global__ void decode_reduce_kernel(const float* __restrict__ partial, TO* __re
 
 }  // namespace
 
-int decode_splits(int64_t S, int kv_dtype) {
-  const int rows = dec_rows(kv_dtype == BDH_DTYPE_F32 ? 4 : 2);
-  return static_cast<int>(std::max<int64_t>(1, (S + rows - 1) / rows));
+// Rows per CTA and split count. Measured on B200 (config-4 model, S ~ 520, N = 8192): the
+// split-S stream runs best with about four or more resident waves of CTAs (B = 64: 32 rows per
+// CTA, 0.85 / 0.74 of HBM for fp32 / bf16 caches vs 0.69 / 0.58 with 128 rows), and small
+// batches need short splits to fill the GPU at all (B = 4: 16 rows beat 8, 32 and more). Rule:
+// the largest of 64, 32, 16 rows that still gives >= 4 x resident CTAs, else 16; `max_splits`
+// caps the split count.
+DecodePlan plan_decode(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N, int64_t max_splits) {
+  DecodePlan pl;
+  const int64_t units = std::max<int64_t>(1, B * H * Tq);
+  if (S <= 0) {
+    pl.splits = 1;
+    pl.rows = 1;
+    return pl;
+  }
+  static const int forced_rows = [] {
+    const char* e = std::getenv("BDH_SM100_DECODE_ROWS");
+    return e ? std::atoi(e) : 0;
+  }();
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int occ = 0;
+  const size_t smem = (static_cast<size_t>(std::max<int64_t>(N, 1)) + kDecRowsMax) * sizeof(float);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_partial_kernel<float, float, true>,
+                                                    kDecThreads, smem) != cudaSuccess || occ <= 0) {
+    cudaGetLastError();
+    occ = 4;
+  }
+  const int64_t resident = static_cast<int64_t>(sm_count(dev)) * occ;
+  int rows = 16;
+  if (forced_rows >= 8 && forced_rows <= kDecRowsMax) {
+    rows = forced_rows;
+  } else {
+    for (int r = 64; r >= 16; r /= 2) {
+      if (units * ((S + r - 1) / r) >= 4 * resident) {
+        rows = r;
+        break;
+      }
+    }
+  }
+  if (max_splits > 0)
+    while (rows < kDecRowsMax && (S + rows - 1) / rows > max_splits) rows *= 2;
+  pl.rows = static_cast<int>(std::min<int64_t>(rows, S));
+  pl.splits = static_cast<int>((S + rows - 1) / rows);
+  return pl;
 }
 
-// Sized for the most splits any cache dtype uses (fp32: 64 rows per split).
-size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t D) {
-  return static_cast<size_t>(decode_splits(S, BDH_DTYPE_F32)) * static_cast<size_t>(B * H * Tq * D) *
-         sizeof(float);
+size_t decode_partial_bytes(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N, int64_t D,
+                            int64_t max_splits) {
+  const DecodePlan pl = plan_decode(B, H, Tq, S, N, max_splits);
+  return (static_cast<size_t>(pl.splits) * static_cast<size_t>(B * H * Tq * D) * sizeof(float) + 255) &
+         ~static_cast<size_t>(255);
 }
 
-int launch_decode(const DecodeArgs& a, float* partial, cudaStream_t stream) {
-  if (a.B * a.H * a.Tq == 0 || a.D == 0) {
+// Partial sums, then (fused RoPE only) the rotated queries as fp32 (B*H*Tq*N).
+size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N, int64_t D) {
+  return decode_partial_bytes(B, H, Tq, S, N, D, 0) + static_cast<size_t>(B * H * Tq * N) * sizeof(float);
+}
+
+int launch_decode(const DecodeArgs& a_in, float* partial, float* qrot, int64_t max_splits,
+                  cudaStream_t stream) {
+  if (a_in.B * a_in.H * a_in.Tq == 0 || a_in.D == 0) {
     return BDH_OK;
   }
-  const int nsplit = decode_splits(a.S, a.kv_dtype);
+  DecodeArgs a = a_in;
+  // the output keeps the caller's query dtype even when the kernel reads rotated fp32 queries
+  const bool out_f32 = a_in.q_dtype == BDH_DTYPE_F32;
+  if (a.freqs != nullptr && qrot != nullptr) {
+    // RoPE of the new queries once, with each (position, column) phase shared by all B*H rows
+    // (the elementwise RoPE kernel), instead of once per split CTA: an fp32 copy for the dot
+    // products and the storage-dtype copy in this step's cache slot.
+    const int64_t qs[4] = {a.H * a.Tq * a.N, a.Tq * a.N, a.N, 1};
+    int rc = launch_rope(a.q, a.q_dtype, a.q_strides, qrot, BDH_DTYPE_F32, qs, nullptr, a.freqs, a.B,
+                         a.H, a.Tq, a.N, a.pos, 0, stream);
+    if (rc) return rc;
+    if (a.slot != nullptr) {
+      rc = launch_rope(a.q, a.q_dtype, a.q_strides, a.slot, a.kv_dtype, a.slot_strides, nullptr,
+                       a.freqs, a.B, a.H, a.Tq, a.N, a.pos, 0, stream);
+      if (rc) return rc;
+    }
+    a.q = qrot;
+    a.q_dtype = BDH_DTYPE_F32;
+    for (int i = 0; i < 4; ++i) a.q_strides[i] = qs[i];
+    a.freqs = nullptr;
+    a.slot = nullptr;
+  }
+  const DecodePlan pl = plan_decode(a.B, a.H, a.Tq, a.S, a.N, max_splits);
+  const int nsplit = pl.splits;
   const int ke = a.kv_dtype == BDH_DTYPE_F32 ? 4 : 2;
   bool vec = (a.N % (16 / ke) == 0) && ((reinterpret_cast<uintptr_t>(a.k) & 15u) == 0) &&
              (a.k_strides[0] * ke) % 16 == 0 && (a.k_strides[1] * ke) % 16 == 0 &&
@@ -247,7 +322,7 @@ int launch_decode(const DecodeArgs& a, float* partial, cudaStream_t stream) {
         partial, static_cast<TK*>(a.slot), a.freqs, Hi, Hvi, Tqi, Si, Ni, Di, a.q_strides[0],     \
         a.q_strides[1], a.q_strides[2], a.k_strides[0], a.k_strides[1], a.k_strides[2],           \
         a.v_strides[0], a.v_strides[1], a.v_strides[2], a.slot_strides[0], a.slot_strides[1],     \
-        a.slot_strides[2], a.pos);                                                                \
+        a.slot_strides[2], a.pos, pl.rows);                                                       \
   } while (0)
   const bool qf = a.q_dtype == BDH_DTYPE_F32, kf = a.kv_dtype == BDH_DTYPE_F32;
   prof_start(kProfDecode, stream);
@@ -268,7 +343,7 @@ int launch_decode(const DecodeArgs& a, float* partial, cudaStream_t stream) {
   }
   const int64_t bht = a.B * a.H * a.Tq;
   const int threads = static_cast<int>(std::min<int64_t>(256, std::max<int64_t>(32, a.D)));
-  if (qf)
+  if (out_f32)
     decode_reduce_kernel<float><<<static_cast<unsigned>(bht), threads, 0, stream>>>(
         partial, static_cast<float*>(a.out), nsplit, Hi, Tqi, Di, bht, a.out_strides[0],
         a.out_strides[1], a.out_strides[2]);
@@ -343,20 +418,24 @@ extern "C" int bdh_tril_decode_noalloc(const void* q, const int64_t q_strides[4]
     bdh::set_error("tril_decode_noalloc: negative size");
     return BDH_ERR_INVALID;
   }
-  const size_t need = bdh::decode_workspace_bytes(B, H, Tq, S, D);
+  const int64_t bhtd = std::max<int64_t>(1, B * H * Tq * D);
+  const int64_t cap_splits = std::max<int64_t>(1, static_cast<int64_t>(bdh::kNoAllocScratchBytes / sizeof(float)) / bhtd);
+  const size_t need = bdh::decode_partial_bytes(B, H, Tq, S, N, D, cap_splits);
   if (need > bdh::kNoAllocScratchBytes) {
     std::ostringstream os;
     os << "tril_decode_noalloc: this problem needs " << need << " bytes of scratch "
-       << "(ceil(S/64) * B * H * Tq * D * 4) but the built-in array holds "
-       << bdh::kNoAllocScratchBytes << " bytes; use bdh_tril_decode with a workspace";
+       << "(splits * B * H * Tq * D * 4, splits = ceil(S / rows) with 16..128 rows per split) "
+       << "but the built-in array holds " << bdh::kNoAllocScratchBytes
+       << " bytes; use bdh_tril_decode with a workspace";
     bdh::set_error(os.str());
     return BDH_ERR_INVALID;
   }
   int rc = BDH_OK;
   float* scratch = bdh::noalloc_scratch(&rc);
   if (scratch == nullptr) return rc;
-  return bdh_tril_decode(q, q_strides, q_dtype, k_past, k_strides, v_past, v_strides, kv_dtype, out,
-                         out_strides, B, H, Hv, Tq, S, N, D, freqs, pos, kr_slot, slot_strides,
-                         scratch, bdh::kNoAllocScratchBytes, stream);
+  // the partial sums only: the new queries are rotated inside the decode kernel
+  return bdh::decode_entry(q, q_strides, q_dtype, k_past, k_strides, v_past, v_strides, kv_dtype,
+                           out, out_strides, B, H, Hv, Tq, S, N, D, freqs, pos, kr_slot,
+                           slot_strides, scratch, nullptr, cap_splits, stream);
 }
 

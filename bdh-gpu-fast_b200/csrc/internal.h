@@ -165,8 +165,23 @@ struct DecodeArgs {
   void* slot = nullptr;
   int64_t slot_strides[4] = {0, 0, 0, 1};
 };
-int decode_splits(int64_t S, int kv_dtype);
-size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t D);
-int launch_decode(const DecodeArgs& a, float* partial, cudaStream_t stream);
+struct DecodePlan {
+  int splits = 1;  // CTAs per (b, h, tq)
+  int rows = 1;    // cached rows per CTA (<= 128)
+};
+// max_splits > 0 caps the split count (longer splits), e.g. to fit a fixed scratch.
+DecodePlan plan_decode(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N, int64_t max_splits = 0);
+size_t decode_partial_bytes(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N, int64_t D,
+                            int64_t max_splits = 0);
+size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N, int64_t D);
+// partial: split partial sums; qrot: rotated fp32 queries (null: rotate inside the kernel).
+int launch_decode(const DecodeArgs& a, float* partial, float* qrot, int64_t max_splits,
+                  cudaStream_t stream);
+int decode_entry(const void* q, const int64_t q_strides[4], int q_dtype, const void* k_past,
+                 const int64_t k_strides[4], const void* v_past, const int64_t v_strides[4],
+                 int kv_dtype, void* out, const int64_t out_strides[4], int64_t B, int64_t H,
+                 int64_t Hv, int64_t Tq, int64_t S, int64_t N, int64_t D, const float* freqs,
+                 int64_t pos, void* kr_slot, const int64_t slot_strides[4], float* partial,
+                 float* qrot, int64_t max_splits, void* stream);
 
 }  // namespace bdh

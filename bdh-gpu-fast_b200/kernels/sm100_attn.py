@@ -59,7 +59,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.bdh_tril_score_v.argtypes = [_vp, P, _vp, P, _vp, P, ctypes.c_int, _vp, P, ctypes.c_int,
                                      _i64, _i64, _i64, _i64, _i64, _i64, _vp, ctypes.c_size_t, _vp]
     lib.bdh_tril_decode_workspace_size.restype = ctypes.c_size_t
-    lib.bdh_tril_decode_workspace_size.argtypes = [_i64, _i64, _i64, _i64, _i64]
+    lib.bdh_tril_decode_workspace_size.argtypes = [_i64, _i64, _i64, _i64, _i64, _i64]
     lib.bdh_tril_decode.argtypes = [_vp, P, ctypes.c_int, _vp, P, _vp, P, ctypes.c_int, _vp, P,
                                     _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, P,
                                     _vp, ctypes.c_size_t, _vp]
@@ -94,7 +94,7 @@ def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
         lib = ctypes.CDLL(str(p))
         _declare(lib)
         ver = lib.bdh_abi_version()
-        if ver != 1:
+        if ver != 2:
             raise RuntimeError(f"{p}: unexpected ABI version {ver}")
     except BaseException as exc:  # noqa: BLE001 - remembered for ext_status()
         _lib_error = exc
@@ -584,7 +584,7 @@ def tril_decode(q: torch.Tensor, k_past: torch.Tensor, v_past: torch.Tensor, *,
             raise ValueError("kr_slot must match q's shape, the cache dtype and have unit last stride")
         slot_ptr = kr_slot.data_ptr()
         slot_strides = _strides(kr_slot)
-    wsz = lib.bdh_tril_decode_workspace_size(B, H, Tq, S, D)
+    wsz = lib.bdh_tril_decode_workspace_size(B, H, Tq, S, N, D)
     ws = torch.empty(max(int(wsz), 4), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         rc = lib.bdh_tril_decode(

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define BDH_ABI_VERSION 1
+#define BDH_ABI_VERSION 2
 
 #define BDH_DTYPE_F32 0
 #define BDH_DTYPE_BF16 1
@@ -106,8 +106,10 @@ int bdh_tril_score_v(const void* q, const int64_t q_strides[4], const void* k,
                      int64_t B, int64_t H, int64_t Hv, int64_t T, int64_t N, int64_t D,
                      void* workspace, size_t workspace_bytes, void* stream);
 
-/* Scratch bytes bdh_tril_decode needs. */
-size_t bdh_tril_decode_workspace_size(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t D);
+/* Scratch bytes bdh_tril_decode needs: the split partial sums, plus B*H*Tq*N*4 for the rotated
+ * queries (used when freqs is given). */
+size_t bdh_tril_decode_workspace_size(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N,
+                                      int64_t D);
 
 /*
  * Decode against a packed past: out[b,h] = (q[b,h] k_past[b,h]^T) v_past[b,hv].
@@ -133,8 +135,12 @@ int bdh_tril_decode(const void* q, const int64_t q_strides[4], int q_dtype, cons
  * front, a host binding without a device allocator, a loop that must not risk the implicit
  * synchronisation of an allocation). The per-split partial sums live in one 8 MiB array
  * compiled into the library, which every device that loads the library keeps until exit.
- * Limit: ceil(S / 64) * B * H * Tq * D * 4 bytes must not exceed 8 MiB (e.g. B*H = 256,
- * Tq = 1, D = 256 allows S <= 2048); larger problems return BDH_ERR_INVALID with a message.
+ * Limit: splits * B * H * Tq * D * 4 bytes must not exceed 8 MiB, where splits = ceil(S / rows)
+ * and rows (16..128 cached rows per CTA, longer when needed to fit) is chosen to fill the GPU
+ * (e.g. B*H = 256, Tq = 1, D = 256 allows S <= 32 * 128 = 4096); larger problems return
+ * BDH_ERR_INVALID with a message.
+ * The new queries are rotated inside the decode kernel here (the workspace form rotates them
+ * once in a separate pass).
  * The first call on each device looks the array's device address up (cudaGetSymbolAddress)
  * with that device current: make that first call before any stream capture begins.
  * All calls on a device share the array and it keeps the last call's contents; every

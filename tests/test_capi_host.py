@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
     lib = sa.load_library()
     for name in _declared():
         assert hasattr(lib, name), f"{name} missing from {sa._LIB_PATH}"
-    assert lib.bdh_abi_version() == 1
+    assert lib.bdh_abi_version() == 2
 
 
 def test_workspace_queries_are_host_only():
@@ -42,7 +42,9 @@ def test_workspace_queries_are_host_only():
     assert bf >= 2 * B * H * T * ldp * 2
     f32 = lib.bdh_tril_score_v_workspace_size(0, B, H, 1, T, N, D, 1)
     assert f32 > 2 * B * H * T * N * 4  # tf32 hi/lo operand copies + score pair
-    assert lib.bdh_tril_decode_workspace_size(64, 4, 1, 1000, 256) == 16 * 64 * 4 * 256 * 4
+    # split partials (at least ceil(S/128) splits) + the rotated fp32 queries
+    dws = lib.bdh_tril_decode_workspace_size(64, 4, 1, 1000, 8192, 256)
+    assert dws >= 8 * 64 * 4 * 256 * 4 + 64 * 4 * 8192 * 4
     assert lib.bdh_tril_score_v_bwd_workspace_size(1, B, H, 1, T, N, D, 1) > 0
 
 

@@ -244,6 +244,40 @@ def test_decode_fused_rope_writes_slot(kvdt):
     assert rel(out.cpu().numpy(), ref) < 1e-5
 
 
+@pytest.mark.parametrize("kvdt", [torch.float32, torch.bfloat16])
+def test_decode_fused_rope_bf16_query(kvdt):
+    """bf16 queries with fused RoPE (the bf16-autocast model's decode step): the rotation runs in
+    a separate pass, the kernel reads fp32 rotated queries, the output stays bf16."""
+    B, H, S, cap, N, D = 3, 4, 150, 160, 1024, 256
+    f = O.get_freqs(N)
+    kbuf = torch.randn(B, H, cap, N, device=DEV).to(kvdt)
+    vbuf = torch.randn(B, 1, cap, D, device=DEV).to(kvdt)
+    q = torch.relu(torch.randn(B, 1, H, N, device=DEV)).to(torch.bfloat16).permute(0, 2, 1, 3)
+    slot = kbuf.narrow(2, S, 1)
+    guard = kbuf.narrow(2, S + 1, cap - S - 1).clone()
+    out = sa().tril_decode(q, kbuf.narrow(2, 0, S), vbuf.narrow(2, 0, S),
+                           freqs=torch.tensor(f, device=DEV), pos=S, kr_slot=slot)
+    assert out.dtype == torch.bfloat16 and out.shape == (B, H, 1, D)
+    qr = O.rope(q.float().cpu().numpy(), f, S, bf16=True)
+    np.testing.assert_allclose(slot.float().cpu().numpy(), qr if kvdt == torch.float32 else O.bf16_round(qr),
+                               rtol=0, atol=2e-2)
+    assert torch.equal(kbuf.narrow(2, S + 1, cap - S - 1), guard)
+    ref = O.tril_decode(qr.astype(np.float64), np64(kbuf[:, :, :S]), np64(vbuf[:, :, :S]))
+    assert rel(out.float().cpu().numpy(), ref) < 3e-3
+
+
+@pytest.mark.parametrize("B,S", [(1, 700), (4, 1023), (64, 40)])
+def test_decode_split_plans(B, S):
+    """Batch sizes that pick different split plans (16..128 cached rows per CTA)."""
+    H, N, D = 4, 2048, 256
+    k = torch.randn(B, H, S, N, device=DEV)
+    v = torch.randn(B, 1, S, D, device=DEV)
+    q = torch.randn(B, H, 1, N, device=DEV)
+    out = sa().tril_decode(q, k, v)
+    ref = (q.double() @ k.double().mT) @ v.double()
+    assert ((out.double() - ref).norm() / ref.norm()).item() < 1e-5
+
+
 # ----------------------------------------------------------------------- backward
 def test_backward_golden_fp32():
     g = golden("bwd")

@@ -111,8 +111,9 @@ def test_noalloc_decode_fused_rope_slot_write_twice():
 def test_noalloc_rejects_problems_beyond_the_fixed_scratch():
     lib = _lib()
     s = (ctypes.c_int64 * 4)(0, 0, 0, 1)
-    # B*H = 256, Tq = 1, D = 256: S = 2048 fits 8 MiB exactly, S = 2049 does not.
-    rc = lib.bdh_tril_decode_noalloc(None, s, 0, None, s, None, s, 0, None, s, 64, 4, 1, 1, 2049,
+    # B*H = 256, Tq = 1, D = 256: 8 MiB holds 32 split partials of 256 x 256 floats, i.e.
+    # S <= 32 splits x 128 rows = 4096; S = 4097 does not fit.
+    rc = lib.bdh_tril_decode_noalloc(None, s, 0, None, s, None, s, 0, None, s, 64, 4, 1, 1, 4097,
                                      8192, 256, None, 0, None, None, None)
     assert rc == 1
     msg = lib.bdh_last_error().decode()
