@@ -24,6 +24,8 @@ import torch
 class CacheManager:
     """Per-layer packed KR/V in contiguous layer-major buffers (see module docstring)."""
 
+    kind = "kv"
+
     def __init__(self, n_layer: int, max_seq: int, batch_size: int, n_head: int, n_latent: int,
                  n_embd: int, device, *, compute_dtype: torch.dtype = torch.float32,
                  storage_dtype: Optional[torch.dtype] = None, page_size: Optional[int] = None):
@@ -64,10 +66,17 @@ class CacheManager:
     def from_config(cls, config, batch_size: int, max_seq: int, device, *,
                     compute_dtype: torch.dtype = torch.float32,
                     storage_dtype: Optional[torch.dtype] = None,
-                    page_size: Optional[int] = None) -> "CacheManager":
+                    page_size: Optional[int] = None, storage_kind: str = "kv"):
+        """``storage_kind="state"`` returns the opt-in N x D recurrent-state cache
+        (``StateCache``) instead of the key/value history."""
         nh = config.n_head
         D = config.n_embd
         N = config.mlp_internal_dim_multiplier * D // nh
+        if storage_kind == "state":
+            return StateCache(config.n_layer, batch_size, nh, N, D, device, max_seq=max_seq,
+                              compute_dtype=compute_dtype)
+        if storage_kind != "kv":
+            raise ValueError(f"storage_kind must be 'kv' or 'state', got {storage_kind!r}")
         return cls(config.n_layer, max_seq, batch_size, nh, N, D, device,
                    compute_dtype=compute_dtype, storage_dtype=storage_dtype, page_size=page_size)
 
@@ -179,3 +188,64 @@ class CacheManager:
     def bytes_allocated(self) -> int:
         return (self._kr_buf.numel() * self._kr_buf.element_size()
                 + self._v_buf.numel() * self._v_buf.element_size())
+
+
+class StateCache:
+    """Opt-in recurrent-state cache: per layer and (b, h) the N x D fp32 state
+    S = sum over the cached positions of k_j v_j^T (k = the rotated latent, K is Q).
+
+    The strictly causal linear attention of a new position t only needs q_t . S_t, so the
+    cache stays (n_layer, B, nh, N, D) however long the sequence grows: a decode step reads and
+    writes the state once (2 * nh * N * D * 4 bytes per batch row and layer) instead of reading
+    the whole key/value history (nh * S * (N + D) * esz). It wins over the history once S
+    exceeds about 2 N D / (N + D) * 4 / esz positions (~500 for fp32 histories at N = 8192,
+    D = 256). It keeps the CacheManager bookkeeping (``seq_len``, pending block, ``commit``),
+    but a past can no longer be read back as keys, so ``get_past`` does not exist here.
+    """
+
+    kind = "state"
+
+    def __init__(self, n_layer: int, batch_size: int, n_head: int, n_latent: int, n_embd: int,
+                 device, *, max_seq: Optional[int] = None,
+                 compute_dtype: torch.dtype = torch.float32):
+        self.n_layer = n_layer
+        self.batch_size = batch_size
+        self.n_head = n_head
+        self.n_latent = n_latent
+        self.n_embd = n_embd
+        self.device = torch.device(device)
+        self.compute_dtype = compute_dtype
+        self.max_seq = max_seq
+        self.seq_len = 0
+        self._pending_t: Optional[int] = None
+        self._state = torch.zeros(n_layer, batch_size, n_head, n_latent, n_embd,
+                                  dtype=torch.float32, device=self.device)
+
+    def state(self, level: int) -> torch.Tensor:
+        """The (B, nh, N, D) fp32 state of ``level`` (updated in place by the step)."""
+        return self._state[level]
+
+    def advance(self, T: int) -> None:
+        """Record that every layer of the current step folds a block of T positions in."""
+        end = self.seq_len + T
+        if self.max_seq is not None and end > self.max_seq:
+            raise RuntimeError(f"cache overflow: need {end} positions but max_seq={self.max_seq}")
+        if self._pending_t is None:
+            self._pending_t = T
+        elif self._pending_t != T:
+            raise RuntimeError(f"inconsistent block T: layer folded {T}, pending={self._pending_t}")
+
+    def commit(self) -> None:
+        if self._pending_t is None:
+            return
+        self.seq_len += self._pending_t
+        self._pending_t = None
+
+    def reset(self) -> None:
+        self.seq_len = 0
+        self._pending_t = None
+        self._state.zero_()
+
+    @property
+    def bytes_allocated(self) -> int:
+        return self._state.numel() * self._state.element_size()

@@ -169,13 +169,47 @@ class BDH(nn.Module):
             cache[(name, k_major)] = hit
         return hit[1]
 
+    def _attn_state(self, Q: torch.Tensor, V: torch.Tensor, level: int, rope_start: int, cache,
+                    impl: str, relu_input: bool) -> torch.Tensor:
+        """Attention of a block against a StateCache, folding the block into the state.
+
+        T = 1 on the sm100 path: one fused step (``state_decode``). Otherwise: RoPE, the strictly
+        causal attention inside the block, plus the past as QR . S, then S += QR^T V (fp32)."""
+        S = cache.state(level)
+        B, nh, T, N = Q.shape
+        if impl == "cuda_sm100" and T == 1 and Q.is_cuda:
+            from kernels.sm100_attn import state_decode
+
+            out = state_decode(Q, S, V, self.attn.freqs, rope_start, relu_input=relu_input)
+            cache.advance(1)
+            return out
+        if relu_input:
+            Q = F.relu(Q)
+        cos, sin = rope_tables(self.attn.freqs, T, rope_start, Q.device)
+        if impl == "cuda_sm100":
+            from kernels.sm100_attn import rope_rotate
+
+            QR = rope_rotate(Q, self.attn.freqs, rope_start)
+        else:
+            QR = eager_rope_rotate(Q, cos, sin)
+        Vq = V.to(QR.dtype)
+        out = bdh_attn(QR, QR, Vq, impl=impl)
+        chunk = max(1, (1 << 28) // max(1, nh * T * N))  # bound the fp32 copies of QR
+        for b0 in range(0, B, chunk):
+            qf = QR[b0:b0 + chunk].float()
+            if cache.seq_len > 0:
+                out[b0:b0 + chunk] += (qf @ S[b0:b0 + chunk]).to(out.dtype)
+            S[b0:b0 + chunk].add_(qf.transpose(-1, -2) @ V[b0:b0 + chunk].float())
+        cache.advance(T)
+        return out
+
     def _latent_fusable(self, impl: str, T: int, cache, device) -> bool:
         """The fused encode / gate kernels serve bf16 prefill blocks without a past."""
         if impl != "cuda_sm100" or T < 64 or device.type != "cuda":
             return False
         if torch.is_grad_enabled() or (self.training and self.drop.p != 0.0):
             return False
-        if cache is not None and cache.seq_len != 0:
+        if cache is not None and (cache.seq_len != 0 or getattr(cache, "kind", "kv") != "kv"):
             return False
         bf16 = (torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16) \
             or self.encoder.dtype == torch.bfloat16
@@ -245,6 +279,19 @@ class BDH(nn.Module):
             x_bthn = x_lat if fused else F.relu(x_lat)
             x_sparse = x_bthn.permute(0, 2, 1, 3)  # (B, nh, T, N) view
             v_tok = x.unsqueeze(1)
+            if cache is not None and getattr(cache, "kind", "kv") == "state":
+                y_kv = self._attn_state(x_sparse, v_tok, level, rope_start, cache, impl, fused)
+                y_kv = self._ln(y_kv)
+                y_lat = torch.einsum("bhtd,hdn->bthn", y_kv, self.encoder_v)
+                if fused:
+                    from kernels.sm100_attn import relu_mul
+
+                    xy = relu_mul(x_lat, y_lat)
+                else:
+                    xy = self.drop(x_bthn * F.relu(y_lat))
+                y_mlp = F.linear(xy.reshape(B, T, nh * N), self.decoder.t())
+                x = self._ln(x + self._ln(y_mlp))
+                continue
             past_kr = past_v = out_kr = None
             raw = False
             if cache is not None:
@@ -294,13 +341,14 @@ class BDH(nn.Module):
     @torch.inference_mode()
     def generate(self, idx: torch.Tensor, max_new_tokens: int, temperature: float = 1.0,
                  top_k: Optional[int] = None, *, cache_dtype: Optional[torch.dtype] = None,
-                 amp_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
-        """Autoregressive sampling with the packed cache (prefill, then T=1 steps)."""
+                 amp_dtype: Optional[torch.dtype] = None, cache_kind: str = "kv") -> torch.Tensor:
+        """Autoregressive sampling with the packed cache (prefill, then T=1 steps);
+        ``cache_kind="state"`` keeps the N x D recurrent state instead of the history."""
         was_training = self.training
         self.eval()
         B, T0 = idx.shape
         cache = CacheManager.from_config(self.config, B, T0 + max_new_tokens, idx.device,
-                                         storage_dtype=cache_dtype)
+                                         storage_dtype=cache_dtype, storage_kind=cache_kind)
         out = torch.empty(B, T0 + max_new_tokens, dtype=idx.dtype, device=idx.device)
         out[:, :T0] = idx
         ctx = (torch.autocast(idx.device.type, dtype=amp_dtype) if amp_dtype is not None

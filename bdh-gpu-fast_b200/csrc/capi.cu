@@ -464,6 +464,50 @@ int bdh_tril_decode(const void* q, const int64_t q_strides[4], int q_dtype, cons
                       qrot, 0, stream);
 }
 
+size_t bdh_state_decode_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D) {
+  if (B < 0 || H < 0 || N < 0 || D < 0) return 0;
+  return state_decode_workspace_bytes(B, H, N, D);
+}
+
+int bdh_state_decode(const void* q, const int64_t q_strides[4], int q_dtype, float* state,
+                     const int64_t state_strides[4], const void* v, const int64_t v_strides[4],
+                     int v_dtype, void* out, const int64_t out_strides[4], int64_t B, int64_t H,
+                     int64_t Hv, int64_t N, int64_t D, const float* freqs, int64_t pos,
+                     int relu_input, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!dtype_ok(q_dtype) || !dtype_ok(v_dtype)) return fail(BDH_ERR_INVALID, "state_decode: dtype must be f32 or bf16");
+  if (B < 0 || H < 0 || N < 0 || D < 0) return fail(BDH_ERR_INVALID, "state_decode: negative size");
+  if (Hv != 1 && Hv != H) return fail(BDH_ERR_INVALID, "state_decode: v heads must equal q heads or 1");
+  if (B * H == 0 || D == 0) return BDH_OK;
+  if (D != 128 && D != 256 && D != 512) return fail(BDH_ERR_INVALID, "state_decode: D must be 128, 256 or 512");
+  if (N <= 0 || (N % 2) != 0 || N > (int64_t(1) << 24))
+    return fail(BDH_ERR_INVALID, "state_decode: latent width N must be even and positive");
+  if (freqs == nullptr) return fail(BDH_ERR_INVALID, "state_decode: freqs is required (the step rotates q)");
+  if (q_strides[3] != 1 || v_strides[3] != 1 || out_strides[3] != 1 || state_strides[3] != 1)
+    return fail(BDH_ERR_INVALID, "state_decode: last dimension must be contiguous");
+  if ((reinterpret_cast<uintptr_t>(state) & 15u) != 0 || state_strides[0] % 4 != 0 ||
+      state_strides[1] % 4 != 0 || state_strides[2] % 4 != 0)
+    return fail(BDH_ERR_INVALID, "state_decode: state base and strides must be 16-byte aligned");
+  if (pos < 0 || pos >= (int64_t(1) << 24)) return fail(BDH_ERR_INVALID, "state_decode: position out of range");
+  const size_t need = state_decode_workspace_bytes(B, H, N, D);
+  if (workspace == nullptr || workspace_bytes < need) {
+    std::ostringstream os;
+    os << "state_decode: workspace of " << need << " bytes required, got " << workspace_bytes;
+    return fail(BDH_ERR_WORKSPACE, os.str());
+  }
+  StateDecodeArgs a;
+  a.q = q; a.q_dtype = q_dtype; a.state = state; a.v = v; a.v_dtype = v_dtype; a.out = out;
+  std::memcpy(a.q_strides, q_strides, sizeof(a.q_strides));
+  std::memcpy(a.state_strides, state_strides, sizeof(a.state_strides));
+  std::memcpy(a.v_strides, v_strides, sizeof(a.v_strides));
+  std::memcpy(a.out_strides, out_strides, sizeof(a.out_strides));
+  a.B = B; a.H = H; a.Hv = Hv; a.N = N; a.D = D; a.freqs = freqs; a.pos = pos;
+  a.relu_input = relu_input ? 1 : 0;
+  float* partial = static_cast<float*>(workspace);
+  float* qrot = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                         state_decode_partial_bytes(B, H, N, D));
+  return launch_state_decode(a, partial, qrot, static_cast<cudaStream_t>(stream));
+}
+
 size_t bdh_tril_score_v_bwd_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,
                                            int64_t N, int64_t D, int k_is_q) {
   if (!dtype_ok(dtype)) return 0;

@@ -184,4 +184,25 @@ int decode_entry(const void* q, const int64_t q_strides[4], int q_dtype, const v
                  int64_t pos, void* kr_slot, const int64_t slot_strides[4], float* partial,
                  float* qrot, int64_t max_splits, void* stream);
 
+// Recurrent-state decode (state_decode.cu). state: (B,H,N,D) fp32 strides {b,h,n,1}.
+struct StateDecodeArgs {
+  const void* q = nullptr;
+  int64_t q_strides[4] = {0, 0, 0, 1};
+  int q_dtype = BDH_DTYPE_F32;
+  float* state = nullptr;
+  int64_t state_strides[4] = {0, 0, 0, 1};
+  const void* v = nullptr;
+  int64_t v_strides[4] = {0, 0, 0, 1};
+  int v_dtype = BDH_DTYPE_F32;
+  void* out = nullptr;
+  int64_t out_strides[4] = {0, 0, 0, 1};
+  int64_t B = 0, H = 0, Hv = 0, N = 0, D = 0;
+  const float* freqs = nullptr;
+  int64_t pos = 0;
+  int relu_input = 0;
+};
+size_t state_decode_partial_bytes(int64_t B, int64_t H, int64_t N, int64_t D);
+size_t state_decode_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D);
+int launch_state_decode(const StateDecodeArgs& a, float* partial, float* qrot, cudaStream_t stream);
+
 }  // namespace bdh

@@ -78,9 +78,14 @@ def _declare(lib: ctypes.CDLL) -> None:
                                   ctypes.c_float, _vp]
     lib.bdh_residual_layernorm.argtypes = [_vp, _i64, _vp, ctypes.c_int, _i64, _vp, _i64, _vp,
                                            _i64, _i64, _i64, ctypes.c_float, _vp]
+    lib.bdh_state_decode_workspace_size.restype = ctypes.c_size_t
+    lib.bdh_state_decode_workspace_size.argtypes = [_i64, _i64, _i64, _i64]
+    lib.bdh_state_decode.argtypes = [_vp, P, ctypes.c_int, _vp, P, _vp, P, ctypes.c_int, _vp, P,
+                                     _i64, _i64, _i64, _i64, _i64, _vp, _i64, ctypes.c_int, _vp,
+                                     ctypes.c_size_t, _vp]
     for name in ("bdh_rope_rotate", "bdh_tril_score_v", "bdh_tril_decode", "bdh_tril_score_v_bwd",
                  "bdh_relu_mul", "bdh_latent_encode", "bdh_latent_gate", "bdh_layernorm",
-                 "bdh_residual_layernorm"):
+                 "bdh_residual_layernorm", "bdh_state_decode"):
         getattr(lib, name).restype = ctypes.c_int
 
 
@@ -592,6 +597,45 @@ def tril_decode(q: torch.Tensor, k_past: torch.Tensor, v_past: torch.Tensor, *,
             _strides(v_past), kd, out.data_ptr(), _strides(out), B, H, v_past.size(1), Tq, S, N, D,
             fptr, int(pos), slot_ptr, slot_strides, ws.data_ptr(), int(wsz), _stream(dev))
     _check(rc, "tril_decode")
+    return out
+
+
+def state_decode(q: torch.Tensor, state: torch.Tensor, v: torch.Tensor, freqs: torch.Tensor,
+                 pos: int, *, relu_input: bool = False) -> torch.Tensor:
+    """One decode step against an N x D recurrent state (updated in place).
+
+    ``q`` (B,H,1,N) un-rotated query (``relu_input``: pre-activation), ``state`` (B,H,N,D) fp32
+    holding sum_j k_j v_j^T over the past, ``v`` (B,Hv,1,D) this step's value. Returns
+    ``RoPE(q) . state`` (the past only) in q's dtype and folds ``RoPE(q)^T v`` into the state.
+    """
+    if q.dim() != 4 or q.size(2) != 1 or state.dim() != 4 or v.dim() != 4:
+        raise ValueError("state_decode expects q (B,H,1,N), state (B,H,N,D), v (B,Hv,1,D)")
+    B, H, _, N = q.shape
+    D = state.size(-1)
+    if tuple(state.shape) != (B, H, N, D) or state.dtype != torch.float32:
+        raise ValueError("state must be fp32 (B,H,N,D) matching q")
+    if v.size(0) != B or v.size(1) not in (1, H) or v.size(2) != 1 or v.size(3) != D:
+        raise ValueError("v must be (B,1 or H,1,D)")
+    dev = _require_cuda(q, state, v, freqs)
+    lib = _require_lib()
+    f = freqs.reshape(-1)
+    if f.dtype != torch.float32 or f.numel() != N:
+        raise ValueError("freqs must be float32 with one entry per latent dimension")
+    f = f.contiguous()
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if v.stride(-1) != 1:
+        v = v.contiguous()
+    out = torch.empty(B, H, 1, D, dtype=q.dtype, device=dev)
+    wsz = lib.bdh_state_decode_workspace_size(B, H, N, D)
+    ws = torch.empty(max(int(wsz), 4), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.bdh_state_decode(q.data_ptr(), _strides(q), _code(q.dtype), state.data_ptr(),
+                                  _strides(state), v.data_ptr(), _strides(v), _code(v.dtype),
+                                  out.data_ptr(), _strides(out), B, H, v.size(1), N, D,
+                                  f.data_ptr(), int(pos), 1 if relu_input else 0, ws.data_ptr(),
+                                  int(wsz), _stream(dev))
+    _check(rc, "state_decode")
     return out
 
 

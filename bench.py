@@ -579,7 +579,9 @@ def bench_decode(args, world, rank, dev):
     g = torch.Generator().manual_seed(rank_seed(2004, rank))
     toks = torch.randint(0, VOCAB, (B, P + steps_total), generator=g).to(dev)
     storage = torch.bfloat16 if args.decode_bf16 else None
-    cache = CacheManager.from_config(cfg, B, P + steps_total, dev, storage_dtype=storage)
+    kind = "state" if args.decode_state else "kv"
+    cache = CacheManager.from_config(cfg, B, P + steps_total, dev, storage_dtype=storage,
+                                     storage_kind=kind)
     buf = torch.empty(B, VOCAB, dtype=torch.float32, device=dev)
     with torch.inference_mode():
         model(toks[:, :P], cache=cache)
@@ -603,6 +605,10 @@ def bench_decode(args, world, rank, dev):
     esz = 2 if storage is not None else 4
     S_mean = S0 + (args.steps - 1) / 2
     bytes_step = N_LAYER * (B * N_HEAD * S_mean * N_LAT * esz + B * S_mean * D_MODEL * esz)
+    if kind == "state":
+        # fp32 state read + written once per step for every row whose rotated query is nonzero;
+        # counted at full density (an upper bound on the bytes moved, so GB/s is a lower bound)
+        bytes_step = N_LAYER * 2 * B * N_HEAD * N_LAT * D_MODEL * 4
     dec = prof["decode"]
     peaks, src = load_peaks()
     gbs = bytes_step * args.steps / (dec["ms"] / 1e3) / 1e9 if dec["ms"] else None
@@ -611,15 +617,20 @@ def bench_decode(args, world, rank, dev):
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16" if storage is not None else "f32",
-        "cache_dtype": "bf16" if storage is not None else "f32",
+        "cache_dtype": "bf16" if storage is not None else "f32", "cache_kind": kind,
         "data": "synthetic", "config": {"workload": "config 4 decode", "B": B, "prompt": P,
                                         "S_mean": S_mean},
-        "roofline": {"kernel": "decode (decode_partial_kernel + decode_reduce_kernel)", "bound": "hbm",
-                     "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": gbs / peaks["hbm_gbs"] if gbs else None,
+        "roofline": {"kernel": ("state decode (state_decode_kernel + state_reduce_kernel)" if kind == "state"
+                                else "decode (decode_partial_kernel + decode_reduce_kernel)"),
+                     "bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     # state mode skips the rows of zero rotated query, so the dense-equivalent
+                     # rate can exceed the copy bandwidth: no fraction is claimed for it
+                     "frac": (gbs / peaks["hbm_gbs"] if gbs else None) if kind == "kv" else None,
+                     "bytes_counted": ("dense state, read + write (upper bound of bytes moved)"
+                                       if kind == "state" else "history read once"),
                      "peak_source": f"{src} hbm_gbs",
                      "bytes_per_launch": bytes_step / N_LAYER,
-                     "traffic": decode_traffic("decode_config4_bf16" if storage is not None
+                     "traffic": None if kind == "state" else decode_traffic("decode_config4_bf16" if storage is not None
                                                else "decode_config4", B, S_mean)},
         "kernel_ms": {k: v_["ms"] / args.steps for k, v_ in prof.items() if v_["launches"]},
         "gpu_launches": sum(v_["launches"] for v_ in prof.values()),
@@ -656,6 +667,8 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode-bf16", action="store_true")
+    ap.add_argument("--decode-state", action="store_true",
+                    help="config 4 with the N x D recurrent-state cache instead of the history")
     ap.add_argument("--batch", type=int, default=0,
                     help="per-GPU batch override (profiling aid; defaults: the config's own)")
     args = ap.parse_args()

@@ -156,6 +156,25 @@ int bdh_tril_decode_noalloc(const void* q, const int64_t q_strides[4], int q_dty
                             int64_t pos, void* kr_slot, const int64_t slot_strides[4],
                             void* stream);
 
+/*
+ * Recurrent-state decode step, the N x D state form of the cached T = 1 attention (an opt-in
+ * alternative to the key/value history of bdh_cache.py:38-111,226-324 and the decode of
+ * kernels/attention.py:193-219; no counterpart function in the reference):
+ *   qr        = RoPE(relu_input ? relu(q) : q) at position pos          (freqs required)
+ *   out[b,h]  = qr[b,h] . S[b,h]                 S = sum over the past of k_j v_j^T (k = qr)
+ *   S[b,h]   += qr[b,h]^T v[b,hv]                in place, after out is formed
+ * q (B,H,1,N) f32/bf16; state (B,H,N,D) fp32 (strides {b,h,n,1}, n stride a multiple of 4);
+ * v (B,Hv,1,D) f32/bf16 with Hv in {1,H}; out (B,H,1,D) in q's dtype. D must be 128, 256 or
+ * 512. Latent rows whose rotated query is zero are neither read nor written. One step costs
+ * 2 * B * H * nnz(qr) * D * 4 bytes of state traffic, independent of the past length.
+ */
+size_t bdh_state_decode_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D);
+int bdh_state_decode(const void* q, const int64_t q_strides[4], int q_dtype, float* state,
+                     const int64_t state_strides[4], const void* v, const int64_t v_strides[4],
+                     int v_dtype, void* out, const int64_t out_strides[4], int64_t B, int64_t H,
+                     int64_t Hv, int64_t N, int64_t D, const float* freqs, int64_t pos,
+                     int relu_input, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Scratch bytes bdh_tril_score_v_bwd needs. */
 size_t bdh_tril_score_v_bwd_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,
                                            int64_t N, int64_t D, int k_is_q);

@@ -137,6 +137,27 @@ def tril_decode(q: np.ndarray, k_past: np.ndarray, v_past: np.ndarray, acc=np.fl
     return (q @ np.swapaxes(k_past, -1, -2)) @ v_past
 
 
+def state_from_history(k_past: np.ndarray, v_past: np.ndarray, acc=np.float64) -> np.ndarray:
+    """N x D recurrent state of a key/value history: S[b,h] = sum_j k_j^T v_j (v heads 1 or H)."""
+    k = np.asarray(k_past, dtype=acc)
+    v = np.asarray(v_past, dtype=acc)
+    if v.shape[1] == 1 and k.shape[1] != 1:
+        v = np.broadcast_to(v, (v.shape[0], k.shape[1]) + v.shape[2:])
+    return np.swapaxes(k, -1, -2) @ v
+
+
+def state_decode(q_rot: np.ndarray, state: np.ndarray, v_new: np.ndarray, acc=np.float64):
+    """One step of the state form of tril_decode: out = q . S (the past only), then
+    S_new = S + q^T v_new. q_rot (B,H,1,N), state (B,H,N,D), v_new (B,Hv,1,D)."""
+    q = np.asarray(q_rot, dtype=acc)
+    S = np.asarray(state, dtype=acc)
+    v = np.asarray(v_new, dtype=acc)
+    if v.shape[1] == 1 and q.shape[1] != 1:
+        v = np.broadcast_to(v, (v.shape[0], q.shape[1]) + v.shape[2:])
+    out = q @ S
+    return out, S + np.swapaxes(q, -1, -2) @ v
+
+
 def tril_backward(q, k, v, dout, acc=np.float64, k_is_q: bool = False):
     """Analytic gradients of O = tril(q k^T, -1) v (kernels/attention_bwd.py:45-83).
 

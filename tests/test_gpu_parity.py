@@ -478,3 +478,62 @@ def test_chunked_forward_config3_shape_vs_fp64():
         qd = q[0, h].double()
         ref = (qd @ qd.T).tril(-1) @ v[0, 0].double()
         assert ((out[0, h] - ref).norm() / ref.norm()).item() <= 3e-3
+
+
+# --------------------------------------------------------------- recurrent-state decode
+@pytest.mark.parametrize("qdt,vdt", [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16),
+                                     (torch.float32, torch.bfloat16)])
+def test_state_decode_equals_history_decode(qdt, vdt):
+    """One state step equals the history decode (same past, same rotated query), updates the
+    state by q^T v, and leaves the rows of zero rotated query untouched."""
+    B, H, S, N, D = 3, 4, 300, 1024, 256
+    f = torch.tensor(O.get_freqs(N), device=DEV)
+    k = torch.relu(torch.randn(B, H, S, N, device=DEV))
+    v = torch.randn(B, 1, S, D, device=DEV)
+    state = (k.double().transpose(-1, -2) @ v.double().expand(-1, H, -1, -1)).float()
+    x = torch.randn(B, H, 1, N, device=DEV)
+    x[..., 0:N // 2:2] = -1.0            # pairs where both entries are negative: relu -> 0
+    x[..., 1:N // 2:2] = -1.0
+    q = x.to(qdt)
+    v_new = torch.randn(B, 1, 1, D, device=DEV).to(vdt)
+    s0 = state.clone()
+    out = sa().state_decode(q, state, v_new, f, S, relu_input=True)
+    assert out.dtype == qdt and out.shape == (B, H, 1, D)
+    qr = sa().rope_rotate(torch.relu(q), f, S).float()
+    ref = sa().tril_decode(qr, k.to(torch.float32), v)
+    tol = 1e-5 if qdt == torch.float32 else 3e-3
+    assert ((out.double() - ref.double()).norm() / ref.double().norm()).item() < tol
+    upd = s0.double() + qr.double().transpose(-1, -2) @ v_new.double().expand(-1, H, -1, -1)
+    assert ((state.double() - upd).norm() / upd.norm()).item() < 1e-6
+    zero_rows = (qr[:, :, 0, :] == 0)
+    assert bool(zero_rows[:, :, : N // 2].all())
+    assert torch.equal(state[zero_rows], s0[zero_rows])
+
+
+@pytest.mark.parametrize("amp", [False, True])
+def test_model_state_cache_matches_history(amp):
+    """Prefill + decode on the sm100 path with the N x D state cache vs the history cache."""
+    import bdh_model
+    from bdh_cache import CacheManager
+
+    cfg = bdh_model.BDHConfig(n_layer=2, n_embd=256, n_head=4, mlp_internal_dim_multiplier=32,
+                              vocab_size=256, dropout=0.0)
+    torch.manual_seed(11)
+    m = bdh_model.BDH(cfg).to(DEV).eval()
+    m.attn._attn_impl_override = "cuda_sm100"
+    B, P, steps = 3, 96, 6
+    idx = torch.randint(0, 256, (B, P + steps), generator=torch.Generator().manual_seed(12)).to(DEV)
+    res = {}
+    for kind in ("kv", "state"):
+        cache = CacheManager.from_config(m.config, B, P + steps, DEV, storage_kind=kind)
+        ctx = torch.autocast("cuda", dtype=torch.bfloat16) if amp else torch.autocast("cuda", enabled=False)
+        out = []
+        with torch.no_grad(), ctx:
+            lg, _ = m(idx[:, :P], cache=cache)
+            out.append(lg[:, -1].float())
+            for t in range(P, P + steps):
+                lg, _ = m(idx[:, t:t + 1], cache=cache)
+                out.append(lg[:, -1].float())
+        res[kind] = torch.stack(out)
+    r = ((res["state"] - res["kv"]).norm() / res["kv"].norm()).item()
+    assert r < (1e-2 if amp else 1e-5), r

@@ -158,3 +158,19 @@ def test_bf16_autocast_oracle_pinned_to_reference_model():
     assert O.rel_fro(exact, g["logits_baseline"]) < 1e-5
     rounded = O.bdh_forward_bf16(g["idx"], w, n_layer=2, n_head=2)
     assert O.rel_fro(rounded, g["logits_baseline"]) < 2e-2
+
+
+def test_state_decode_oracle_equals_history_decode():
+    """The N x D state form reproduces the reference decode (golden_decode, the reference CPU
+    extension's tril_decode_cpu) step by step."""
+    g = golden("decode")
+    kbuf, vbuf, q = g["kbuf"], g["vbuf"], g["q"]
+    # out at past length 25 from a state built over the first 25 keys equals the golden decode
+    S25 = O.state_from_history(kbuf[:, :, :25], vbuf[:, :, :25])
+    out25, _ = O.state_decode(q, S25, vbuf[:, :, 25:26])
+    assert O.rel_fro(out25, g["out_ext_S25"]) < 1e-6
+    # stepping the state one key at a time gives the same state as building it at once
+    S = O.state_from_history(kbuf[:, :, :1], vbuf[:, :, :1])
+    for s in range(1, 25):
+        _, S = O.state_decode(kbuf[:, :, s:s + 1], S, vbuf[:, :, s:s + 1])
+    assert O.rel_fro(S, S25) < 1e-12
