@@ -320,6 +320,32 @@ __device__ __forceinline__ float bf16_round_f32(float x) {
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) { return cvt_bf16x2(lo, hi); }
 
 
+// ------------------------------------------------------------- fast division ----
+// Division of 0 <= n < 2^31 by a divisor fixed at launch: q = umulhi(n, m) >> s with
+// m = ceil(2^(31 + ceil(log2 d)) / d) (Granlund & Montgomery, "Division by invariant integers
+// using multiplication", 1994), a multiply-high and a shift instead of the ~20-instruction
+// integer division, for tile-index arithmetic on the issue paths of persistent kernels.
+struct FastDiv {
+  uint32_t d = 1, m = 0, s = 0;
+  FastDiv() = default;
+  __host__ explicit FastDiv(uint32_t divisor) : d(divisor) {
+    if (d <= 1) return;  // m = 0 marks the identity
+    uint32_t l = 0;
+    while ((1ull << l) < d) ++l;  // ceil(log2 d)
+    const uint64_t p = 31 + l;
+    m = static_cast<uint32_t>(((1ull << p) + d - 1) / d);
+    s = static_cast<uint32_t>(p - 32);
+  }
+  __device__ __forceinline__ int div(int n) const {
+    if (m == 0) return n;
+    return static_cast<int>(__umulhi(static_cast<uint32_t>(n), m) >> s);
+  }
+  __device__ __forceinline__ void divmod(int n, int& q, int& r) const {
+    q = div(n);
+    r = n - q * static_cast<int>(d);
+  }
+};
+
 // ----------------------------------------------------------------- BDH RoPE ----
 // cos / sin of the reference phase for position `pos` and frequency `f` (bdh.py:119-122,
 // 142-150): fp32 product, exact fractional part (the product is >= 0), times fp32 2*pi as

@@ -68,6 +68,7 @@ struct EncodeParams {
   int B, T, H, D, N, pos0;
   int tb_n, nb_n;
   int walk_chunk;        // row blocks per chunk of the chunked walk (divides B * tb_n)
+  FastDiv fd_chunk, fd_ncb, fd_b, fd_nb;  // by walk_chunk, H * nb_n, B, nb_n
   int* err;
 };
 
@@ -79,6 +80,7 @@ struct GateParams {
   int B, T, H, D, N;
   int tb_n, nb_n;
   int walk_chunk;        // row blocks per chunk of the chunked walk (divides B * tb_n)
+  FastDiv fd_chunk, fd_ncb, fd_b, fd_nb;  // by walk_chunk, H * nb_n, B, nb_n
   int* err;
 };
 
@@ -97,19 +99,18 @@ struct ChunkedResidentWalk {
   static constexpr int kResidentB = 4;  // D <= 256
 };
 
-__device__ __forceinline__ LatentTile latent_tile_chunked(int t, int B, int H, int nb_n, int ch) {
+template <class Prm>
+__device__ __forceinline__ LatentTile latent_tile_chunked(int t, const Prm& p) {
   LatentTile tl;
-  const int c = t / ch;
-  const int i = t - c * ch;
-  const int ncb = H * nb_n;
-  const int cb = c % ncb;
+  int c, i, rc, cb, q, j;
+  p.fd_chunk.divmod(t, c, i);
+  p.fd_ncb.divmod(c, rc, cb);
   // each chunk starts at a different row block of the row chunk, so the CTAs running at one time
   // read different activation tiles instead of all requesting the same L2 lines together
-  const int rb = (c / ncb) * ch + (i + c) % ch;
-  tl.b = rb % B;
-  tl.tb = rb / B;
-  tl.h = cb / nb_n;
-  tl.nb = cb - tl.h * nb_n;
+  p.fd_chunk.divmod(i + c - p.fd_chunk.div(c) * static_cast<int>(p.fd_chunk.d), q, j);
+  const int rb = rc * static_cast<int>(p.fd_chunk.d) + j;
+  p.fd_b.divmod(rb, tl.tb, tl.b);
+  p.fd_nb.divmod(cb, tl.h, tl.nb);
   return tl;
 }
 
@@ -166,9 +167,9 @@ struct EncodeProb : LatentWalk<ORDER> {
     return ORDER == 0   ? latent_tile(t, p.B, p.H, p.nb_n)
            : ORDER == 1 ? latent_tile_nfast(t, p.B, p.H, p.tb_n, p.nb_n)
            : ORDER == 2 ? latent_tile_colfixed(t, p.B, p.H, p.nb_n)
-                        : latent_tile_chunked(t, p.B, p.H, p.nb_n, p.walk_chunk);
+                        : latent_tile_chunked(t, p);
   }
-  __device__ static int walk_chunk(const Params& p) { return p.walk_chunk; }
+  __device__ static const FastDiv& walk_chunk(const Params& p) { return p.fd_chunk; }
   __device__ static int b_key(const Params& p, const Tile& tl) { return tl.h * p.nb_n + tl.nb; }
   static int max_ctas(const Params& p, int sms) {
     if (ORDER != 2) return sms;
@@ -297,10 +298,10 @@ struct GateProb : LatentWalk<ORDER> {
   __device__ static int num_tiles(const Params& p) { return p.B * p.H * p.tb_n * p.nb_n; }
   __device__ static Tile tile(const Params& p, int t) {
     return ORDER == 0   ? latent_tile(t, p.B, p.H, p.nb_n)
-           : ORDER == 3 ? latent_tile_chunked(t, p.B, p.H, p.nb_n, p.walk_chunk)
+           : ORDER == 3 ? latent_tile_chunked(t, p)
                         : latent_tile_nfast(t, p.B, p.H, p.tb_n, p.nb_n);
   }
-  __device__ static int walk_chunk(const Params& p) { return p.walk_chunk; }
+  __device__ static const FastDiv& walk_chunk(const Params& p) { return p.fd_chunk; }
   __device__ static int b_key(const Params& p, const Tile& tl) { return tl.h * p.nb_n + tl.nb; }
   __device__ static int k_blocks(const Params& p, const Tile&) { return (p.D + 63) / 64; }
   __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x1u; }
@@ -515,6 +516,10 @@ int launch_latent_encode(const LatentArgs& a, cudaStream_t stream, int* err) {
   prm.tb_n = static_cast<int>((a.T + 127) / 128);
   prm.nb_n = static_cast<int>((a.N + 127) / 128);
   prm.walk_chunk = walk_chunk_for(a.B * int64_t(prm.tb_n));
+  prm.fd_chunk = FastDiv(static_cast<uint32_t>(prm.walk_chunk));
+  prm.fd_ncb = FastDiv(static_cast<uint32_t>(prm.H * prm.nb_n));
+  prm.fd_b = FastDiv(static_cast<uint32_t>(prm.B));
+  prm.fd_nb = FastDiv(static_cast<uint32_t>(prm.nb_n));
   prm.err = err;
   const int64_t ntiles = a.B * a.H * int64_t(prm.tb_n) * prm.nb_n;
   const bool kw = weight_k_major(a.w_strides);
@@ -542,6 +547,10 @@ int launch_latent_gate(const LatentArgs& a, cudaStream_t stream, int* err) {
   prm.tb_n = static_cast<int>((a.T + 127) / 128);
   prm.nb_n = static_cast<int>((a.N + 127) / 128);
   prm.walk_chunk = walk_chunk_for(a.B * int64_t(prm.tb_n));
+  prm.fd_chunk = FastDiv(static_cast<uint32_t>(prm.walk_chunk));
+  prm.fd_ncb = FastDiv(static_cast<uint32_t>(prm.H * prm.nb_n));
+  prm.fd_b = FastDiv(static_cast<uint32_t>(prm.B));
+  prm.fd_nb = FastDiv(static_cast<uint32_t>(prm.nb_n));
   prm.err = err;
   const int64_t ntiles = a.B * a.H * int64_t(prm.tb_n) * prm.nb_n;
   const bool kw = weight_k_major(a.w_strides);

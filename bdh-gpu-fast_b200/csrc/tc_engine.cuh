@@ -61,7 +61,8 @@ struct HasContigTiles : std::false_type {};
 template <class P>
 struct HasContigTiles<P, std::void_t<decltype(P::kContiguousTiles)>> : std::true_type {};
 
-//   P::kChunkedWalk + P::walk_chunk(prm) -> the tile list is cut into chunks of walk_chunk
+//   P::kChunkedWalk + P::walk_chunk(prm) (a FastDiv by the chunk length) -> the tile list is cut
+//       into chunks of walk_chunk
 //       consecutive tiles; CTA i takes chunks i, i + G, ... and walks each chunk in order (the
 //       CTAs running at one time hold neighbouring chunks, each CTA keeps a chunk's operands).
 template <class P, class = void>
@@ -72,8 +73,12 @@ struct HasChunkedWalk<P, std::void_t<decltype(P::kChunkedWalk)>> : std::true_typ
 // Tile walk of this CTA: t = first, next(first), ... while t < end.
 struct TileWalk {
   int first, end, step, chunk;  // chunk > 0: chunked walk
+  FastDiv fd;                    // division by chunk
   __device__ __forceinline__ int next(int t) const {
-    if (chunk > 0) return ((t + 1) % chunk != 0) ? t + 1 : t + 1 + (step - 1) * chunk;
+    if (chunk > 0) {
+      const int u = t + 1;
+      return (u - fd.div(u) * chunk != 0) ? u : u + (step - 1) * chunk;
+    }
     return t + step;
   }
 };
@@ -81,7 +86,8 @@ template <class P>
 __device__ __forceinline__ TileWalk tile_walk(const typename P::Params& prm, int ntiles) {
   TileWalk w;
   if constexpr (HasChunkedWalk<P>::value) {
-    w.chunk = P::walk_chunk(prm);
+    w.fd = P::walk_chunk(prm);
+    w.chunk = static_cast<int>(w.fd.d);
     w.first = static_cast<int>(blockIdx.x) * w.chunk;
     w.end = ntiles;
     w.step = static_cast<int>(gridDim.x);
