@@ -352,13 +352,40 @@ def bench_config2(args, world, rank, dev):
     torch.cuda.synchronize(dev)
     e2e = world * B * T * args.steps / (ms_e2e / 1e3)
 
-    # roofline of the score pass (dominant kernel of the path): algorithmic flops of the
-    # causal Q K^T per launch = B * H * T * (T - 1) * N  (T(T-1)/2 pairs x 2N flops)
+    # rooflines of the three largest kernels of the step; "roofline" is the one with the most
+    # device time. Algorithmic work per launch (one layer, the whole batch):
+    #   score pass  B H T (T-1) N flops (causal Q K^T, T(T-1)/2 pairs x 2N)       tensor
+    #   encode      2 B T H N x 2 bytes written (xs, QR) + x and weights read      HBM
+    #   gate        B T H N x 2 read (xs) + B T H N x 2 written (xy) + y, weights  HBM
     peaks, src = load_peaks()
-    sc = prof["score"]
-    flops_launch = B * N_HEAD * T * (T - 1) * N_LAT
-    achieved = flops_launch / (sc["ms"] / sc["launches"] / 1e3) / 1e12 if sc["launches"] else None
-    peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    tpeak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    lat = B * T * N_HEAD * N_LAT * 2
+    small = B * T * D_MODEL * 2 + N_HEAD * D_MODEL * N_LAT * 2
+    specs = {
+        "score": ("score pass tril(QR QR^T,-1) (tc_pair_kernel<ScorePair>, cta_group::2 256x256 tiles)"
+                  if os.environ.get("BDH_SM100_PAIR", "1") != "0"
+                  else "score pass tril(QR QR^T,-1) (tc_gemm_kernel<ScoreProb<bf16>>)",
+                  "tensor", B * N_HEAD * T * (T - 1) * N_LAT, 1e12, "TFLOP/s", tpeak,
+                  f"{src} bf16_tflops_sustained (kernel timed inside a long step)", "score_pass_config2"),
+        "encode": ("latent encode x@enc + ReLU + RoPE (tc_gemm_kernel<EncodeProb>), xs and QR written",
+                   "hbm", 2 * lat + small, 1e9, "GB/s", peaks["hbm_gbs"], f"{src} hbm_gbs",
+                   "latent_encode_config2"),
+        "gate": ("latent gate xs * relu(y@encv) (tc_gemm_kernel<GateProb>), xs read, xy written",
+                 "hbm", 2 * lat + small + B * N_HEAD * T * D_MODEL * 2, 1e9, "GB/s", peaks["hbm_gbs"],
+                 f"{src} hbm_gbs", "latent_gate_config2"),
+    }
+    rooflines = {}
+    for k, (name, bound, work, scale, unit, peak, psrc, tname) in specs.items():
+        kp = prof.get(k)
+        if not kp or not kp["launches"]:
+            continue
+        per = kp["ms"] / kp["launches"]
+        ach = work / (per / 1e3) / scale
+        rooflines[k] = {"kernel": name, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
+                        "frac": ach / peak, "peak_source": psrc, "traffic": load_traffic(tname, B),
+                        "avg_launch_ms": per, "work_per_launch": work,
+                        "ms_per_step": kp["ms"] / args.steps}
+    dominant = max(rooflines, key=lambda k: rooflines[k]["ms_per_step"]) if rooflines else None
     attn_ms = sum(prof[k]["ms"] for k in ("score", "value", "rope"))
     attn_flops = N_LAYER * args.steps * B * N_HEAD * T * (T - 1) * (N_LAT + D_MODEL)
     launches = sum(v["launches"] for v in prof.values())
@@ -375,15 +402,8 @@ def bench_config2(args, world, rank, dev):
                    "cache": "inputs larger than L2 (1 GB latent per layer per GPU); no flush"},
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": idx_host.numel() * 8,
                 "d2h_bytes_per_step": logits_host.numel() * 2},
-        "roofline": {"kernel": ("score pass tril(QR QR^T,-1) (tc_pair_kernel<ScorePair>, cta_group::2 "
-                                "256x256 tiles)" if os.environ.get("BDH_SM100_PAIR", "1") != "0"
-                                else "score pass tril(QR QR^T,-1) (tc_gemm_kernel<ScoreProb<bf16>>)"),
-                     "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": (achieved / peak) if achieved else None,
-                     "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
-                     "traffic": load_traffic("score_pass_config2", B),
-                     "avg_launch_ms": sc["ms"] / sc["launches"] if sc["launches"] else None,
-                     "flops_per_launch": flops_launch},
+        "roofline": rooflines.get(dominant),
+        "rooflines": rooflines,
         "attn_tflops": attn_flops / (attn_ms / 1e3) / 1e12 if attn_ms else None,
         "attn_share_of_step": attn_ms / ms if ms else None,
         "kernel_ms": {k: v["ms"] / args.steps for k, v in prof.items() if v["launches"]},
