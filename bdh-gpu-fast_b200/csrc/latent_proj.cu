@@ -151,6 +151,7 @@ struct EncodeProb : LatentWalk<ORDER> {
   using S = TcShape<2, 128, false, !KW, 1, 1, STAGES>;
   static constexpr int kCustomEpilogue = 1;
   static constexpr int kEpiWarps = 8;
+  static constexpr int kAccBuffers = 4;
   static constexpr int kBox = 32 * 128;           // one 64-column x 32-row swizzled box
   static constexpr int kBuf = 2 * kBox;           // xs box + qr box
   static constexpr int kWarpStage = BUFS * kBuf;  // BUFS staging buffers per warp
@@ -283,6 +284,7 @@ struct GateProb : LatentWalk<ORDER> {
   using S = TcShape<2, 128, false, !KW, 1, 1, STAGES>;
   static constexpr int kCustomEpilogue = 1;
   static constexpr int kEpiWarps = 8;
+  static constexpr int kAccBuffers = 4;
   static constexpr int kBox = 32 * 128;           // one 32 x 64 slice: xs in, xy out in place
   static constexpr int kSlots = SLOTS;            // >= 2: the next tile's slice loads while
                                                   // this tile is drained

@@ -126,6 +126,18 @@ template <class P>
 struct HasMaxCtas<P, std::void_t<decltype(P::max_ctas(std::declval<const typename P::Params&>(), 0))>>
     : std::true_type {};
 
+//   P::kAccBuffers = 4 (BN <= 128) -> four TMEM accumulators instead of two, so the MMA issuer
+//       can run up to three tiles ahead of the epilogue (short-K tiles otherwise stall on the
+//       accumulator hand-back of the tile before last).
+template <class P, class = void>
+struct AccBufs {
+  static constexpr int value = 2;
+};
+template <class P>
+struct AccBufs<P, std::void_t<decltype(P::kAccBuffers)>> {
+  static constexpr int value = P::kAccBuffers;
+};
+
 template <class P, class = void>
 struct EpiSmem {
   static constexpr int value = 0;
@@ -243,8 +255,11 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
                 "eight epilogue warps need a custom epilogue");
   static_assert(tc_smem_bytes<S, P>() <= 232448, "shared memory budget");
   static_assert(ResidentB<P>::value == 0 || S::B_TERMS == 1, "resident B holds one term");
-  static_assert(S::STAGES <= 8, "barrier block layout");
+  static_assert(S::STAGES <= 8, "barrier block layout (2 x 8 stages + 2 x 4 accumulators + 5)");
   constexpr bool kRes = ResidentB<P>::value > 0;
+  constexpr int NACC = AccBufs<P>::value;
+  static_assert(NACC == 2 || (NACC == 4 && S::BN <= 128), "four accumulators need BN <= 128");
+  constexpr uint32_t kTmemCols = static_cast<uint32_t>(NACC * S::BN);
   constexpr int SB = tc_stage_bytes<S, P>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -253,8 +268,8 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + tc_ring_bytes<S, P>());
   uint64_t* empty = full + S::STAGES;
   uint64_t* tfull = empty + S::STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
+  uint64_t* tempty = tfull + NACC;
+  uint64_t* drain = tempty + NACC;
   uint64_t* full_b = drain + 1;
   uint64_t* empty_b = full_b + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(empty_b + 1);
@@ -269,7 +284,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < NACC; ++a) {
       mbar_init(tfull + a, 1);
       mbar_init(tempty + a, 32 * EpiWarps<P>::value);
     }
@@ -279,7 +294,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, S::TMEM_COLS);
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -378,8 +393,8 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
           }
         }
         for (int ch = 0; ch < nch && ok; ++ch, ++lc) {
-          const int acc = lc & 1;
-          const uint32_t aph = static_cast<uint32_t>(lc >> 1) & 1u;
+          const int acc = lc % NACC;
+          const uint32_t aph = static_cast<uint32_t>(lc / NACC) & 1u;
           if (!wait_bounded(tempty + acc, aph ^ 1u, abort_flag, prm.err, kErrTimeoutMma)) {
             ok = false;
             break;
@@ -450,8 +465,8 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
         const bool has_next = tn < walk.end;
         P::epilogue_prefetch(prm, tile, has_next, P::tile(prm, has_next ? tn : t), row, part, epi,
                              st);
-        const int acc = lc & 1;
-        const uint32_t aph = static_cast<uint32_t>(lc >> 1) & 1u;
+        const int acc = lc % NACC;
+        const uint32_t aph = static_cast<uint32_t>(lc / NACC) & 1u;
         ok = wait_bounded(tfull + acc, aph, abort_flag, prm.err, kErrTimeoutEpilogue);
         if (!__all_sync(0xffffffffu, ok)) {
           ok = false;
@@ -475,8 +490,8 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
     for (int t = walk.first; t < walk.end && ok; t = walk.next(t)) {
       typename P::Tile tile = P::tile(prm, t);
       if (S::KCHUNK == 0) {
-        const int acc = lc & 1;
-        const uint32_t aph = static_cast<uint32_t>(lc >> 1) & 1u;
+        const int acc = lc % NACC;
+        const uint32_t aph = static_cast<uint32_t>(lc / NACC) & 1u;
         ok = wait_bounded(tfull + acc, aph, abort_flag, prm.err, kErrTimeoutEpilogue);
         if (!__all_sync(0xffffffffu, ok)) {
           ok = false;
@@ -502,8 +517,8 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
         for (int i = 0; i < BNC; ++i) sum[i] = 0.0f;
         const int nch = S::chunks(P::k_blocks(prm, tile));
         for (int ch = 0; ch < nch; ++ch, ++lc) {
-          const int acc = lc & 1;
-          const uint32_t aph = static_cast<uint32_t>(lc >> 1) & 1u;
+          const int acc = lc % NACC;
+          const uint32_t aph = static_cast<uint32_t>(lc / NACC) & 1u;
           ok = wait_bounded(tfull + acc, aph, abort_flag, prm.err, kErrTimeoutEpilogue);
           if (!__all_sync(0xffffffffu, ok)) {
             ok = false;
@@ -552,7 +567,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, S::TMEM_COLS);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
