@@ -206,6 +206,25 @@ using ScoreTf32 = ScoreProb<4, 128, 3>;
 using ValueBf16 = ValueProb<2, 3>;
 using ValueTf32 = ValueProb<4, 3>;
 
+// One row of the fp32 score pair from its K-split partials: columns of the row's stored tiles
+// (up to the end of its diagonal 128-block), strictly lower part kept, tf32 hi + fp32 lo.
+__global__ void score_split_reduce_kernel(const float* __restrict__ part, float* __restrict__ p_hi,
+                                          float* __restrict__ p_lo, int ksplit, int T, int64_t ldp,
+                                          int64_t rows) {
+  const int64_t r = blockIdx.x;  // unit * T + i
+  const int i = static_cast<int>(r % T);
+  const int64_t cap = static_cast<int64_t>(i / 128 + 1) * 128;
+  const int jend = static_cast<int>(ldp < cap ? ldp : cap);
+  for (int j = threadIdx.x; j < jend; j += blockDim.x) {
+    float x = 0.0f;
+    if (j < i)
+      for (int k = 0; k < ksplit; ++k) x += part[(k * rows + r) * ldp + j];
+    const float h = tf32_rna(x);
+    p_hi[r * ldp + j] = h;
+    p_lo[r * ldp + j] = x - h;
+  }
+}
+
 int64_t score_ld(int64_t T) { return (T + 7) / 8 * 8; }
 int64_t vt_ld(int64_t T) { return (T + 3) / 4 * 4; }
 
@@ -241,6 +260,16 @@ int launch_score_pass(const ScoreArgs& a, cudaStream_t stream, int* err) {
     prm.p2_lo = a.p2_lo;
     prm.ldp = a.chunk > 0 ? a.chunk : score_ld(a.T);
     prm.chunk = a.chunk;
+    prm.ksplit = 1;
+    prm.kb_per_split = 0;
+    prm.part = nullptr;
+    if (elem == 4 && a.ksplit > 1 && a.mode == kStoreDirect && a.chunk == 0 && a.part != nullptr) {
+      const int total = static_cast<int>((a.K + bk - 1) / bk);
+      const int per = (total + a.ksplit - 1) / a.ksplit;
+      prm.kb_per_split = (per + 7) / 8 * 8;  // whole 256-wide accumulation chunks
+      prm.ksplit = (total + prm.kb_per_split - 1) / prm.kb_per_split;
+      prm.part = a.part;
+    }
     prm.err = err;
     return true;
   };
@@ -268,12 +297,51 @@ int launch_score_pass(const ScoreArgs& a, cudaStream_t stream, int* err) {
   } else {
     ScoreTf32::Params prm{};
     if (!fill(prm, ScoreTf32::S::BK, 128)) return BDH_ERR_INVALID;
-    return launch_tc<ScoreTf32::S, ScoreTf32>(prm, prm.units * prm.tiles_per_unit, stream, kProfScore);
+    const int rc = launch_tc<ScoreTf32::S, ScoreTf32>(
+        prm, prm.units * prm.tiles_per_unit * std::max(1, prm.ksplit), stream, kProfScore);
+    if (rc || prm.ksplit <= 1) return rc;
+    // sum the K-split partials in order, mask j >= i, split into tf32 hi + fp32 lo
+    const int64_t rows = a.B * a.H * a.T;
+    prof_start(kProfScore, stream);
+    score_split_reduce_kernel<<<static_cast<unsigned>(rows), 128, 0, stream>>>(
+        prm.part, static_cast<float*>(a.p_hi), static_cast<float*>(a.p_lo), prm.ksplit,
+        static_cast<int>(a.T), prm.ldp, rows);
+    prof_stop(kProfScore, stream);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      set_error(std::string("score_split_reduce_kernel launch: ") + cudaGetErrorString(e));
+      return BDH_ERR_CUDA;
+    }
+    return 0;
   }
 }
 
-// Score pass of the forward: P = tril(Q K^T, -1) as a hi/lo pair in p_hi / p_lo.
-int launch_score(const FwdArgs& a, void* p_hi, void* p_lo, cudaStream_t stream, int* err) {
+// Wave-quantisation efficiency decides the split: ntiles * k tiles over the SMs, K / k >= 512.
+int score_ksplit_f32(int64_t units, int64_t T, int64_t K) {
+  const int64_t mt = (T + 127) / 128;
+  const int64_t tiles = units * mt * (mt + 1) / 2;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int64_t sms = sm_count(dev);
+  int best = 1;
+  double best_eff = 0.0;
+  for (int k = 1; k <= 16; k *= 2) {
+    if (k > 1 && K / k < 512) break;
+    const int64_t n = tiles * k;
+    const int64_t waves = (n + sms - 1) / sms;
+    const double eff = static_cast<double>(n) / static_cast<double>(waves * sms);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = k;
+    }
+  }
+  return best;
+}
+
+// Score pass of the forward: P = tril(Q K^T, -1) as a hi/lo pair in p_hi / p_lo. fp32: `part`
+// (null for none) holds the K-split partials.
+int launch_score(const FwdArgs& a, void* p_hi, void* p_lo, float* part, cudaStream_t stream,
+                 int* err) {
   ScoreArgs s;
   s.elem = a.dtype == BDH_DTYPE_F32 ? 4 : 2;
   s.a[0] = a.q;
@@ -292,6 +360,10 @@ int launch_score(const FwdArgs& a, void* p_hi, void* p_lo, cudaStream_t stream, 
   s.mode = kStoreDirect;
   s.p_hi = p_hi;
   s.p_lo = p_lo;
+  if (s.elem == 4 && part != nullptr) {
+    s.ksplit = score_ksplit_f32(a.B * a.H, a.T, a.N);
+    s.part = part;
+  }
   return launch_score_pass(s, stream, err);
 }
 

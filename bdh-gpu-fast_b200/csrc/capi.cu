@@ -51,6 +51,7 @@ bool use_chunked(int dtype, int64_t T) {
 struct FwdLayout {
   size_t q_hi = 0, q_lo = 0, k_hi = 0, k_lo = 0, v_hi = 0, v_lo = 0, p_hi = 0, p_lo = 0;
   size_t s_hi = 0, s_lo = 0;
+  size_t part = 0;  // fp32 K-split partials of the score pass (0 when not split)
   bool chunked = false;
   size_t total = 0;
 };
@@ -86,6 +87,13 @@ FwdLayout fwd_layout(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T, int
   const size_t pbytes = align_up(static_cast<size_t>(B * H * T * score_ld(T)) * e);
   L.p_hi = off; off += pbytes;
   L.p_lo = off; off += pbytes;
+  if (dtype == BDH_DTYPE_F32) {
+    const int ks = score_ksplit_f32(B * H, T, N);
+    if (ks > 1) {
+      L.part = off;
+      off += align_up(static_cast<size_t>(ks) * static_cast<size_t>(B * H * T * score_ld(T)) * 4);
+    }
+  }
   L.total = off;
   return L;
 }
@@ -424,7 +432,8 @@ int bdh_tril_score_v(const void* q, const int64_t q_strides[4], const void* k,
   }
   if (L.chunked)
     return launch_chunked_forward(a, ws + L.p_hi, ws + L.p_lo, ws + L.s_hi, ws + L.s_lo, st, err);
-  int rc = launch_score(a, ws + L.p_hi, ws + L.p_lo, st, err);
+  int rc = launch_score(a, ws + L.p_hi, ws + L.p_lo,
+                        L.part ? reinterpret_cast<float*>(ws + L.part) : nullptr, st, err);
   if (rc) return rc;
   return launch_value(a, ws + L.p_hi, ws + L.p_lo, st, err);
 }

@@ -53,13 +53,20 @@ struct ScoreArgs {
   void* p_lo = nullptr;
   void* p2_hi = nullptr;
   void* p2_lo = nullptr;
+  // split-K (fp32 direct forward only): ksplit > 1 partial tiles in part [ksplit][u][T][ldp]
+  // fp32, then summed in order and split into (p_hi, p_lo) by a reduce pass
+  int ksplit = 1;
+  float* part = nullptr;
 };
 int launch_score_pass(const ScoreArgs& a, cudaStream_t stream, int* err);
+// K-split count of the fp32 forward score pass (1 = none) for units x T x K.
+int score_ksplit_f32(int64_t units, int64_t T, int64_t K);
 
 int64_t score_ld(int64_t T);
 // Row length (keys) of the transposed tf32 V operand: [B*Hv][D][vt_ld(T)].
 int64_t vt_ld(int64_t T);
-int launch_score(const FwdArgs& a, void* p_hi, void* p_lo, cudaStream_t stream, int* err);
+int launch_score(const FwdArgs& a, void* p_hi, void* p_lo, float* part, cudaStream_t stream,
+                 int* err);
 int launch_value(const FwdArgs& a, const void* p_hi, const void* p_lo, cudaStream_t stream,
                  int* err);
 

@@ -50,10 +50,13 @@ struct ScoreProb {
     void* p2_lo;
     int64_t ldp;
     int chunk;             // > 0: keys restricted to the query block's chunk, stored relative
+    int ksplit;            // > 1: K-split partial tiles (fp32, direct mode) into part
+    int kb_per_split;      // k-blocks per split (a multiple of the accumulation chunk)
+    float* part;           // [ksplit][units][T][ldp]
     int* err;
   };
   struct Tile {
-    int unit, mi, ni;
+    int unit, mi, ni, ks;
   };
 
   // First key column of row block mi: 0, or the start of its chunk (chunked forward).
@@ -63,9 +66,14 @@ struct ScoreProb {
   __device__ static int nt_for(const Params& p, int mi) {
     return ceil_div_d(min(p.T, (mi + 1) * S::BM), BN) - key0(p, mi) / BN;
   }
-  __device__ static int num_tiles(const Params& p) { return p.units * p.tiles_per_unit; }
+  __device__ static int num_tiles(const Params& p) { return p.units * p.tiles_per_unit * max(1, p.ksplit); }
   __device__ static Tile tile(const Params& p, int t) {
     Tile tl;
+    tl.ks = 0;
+    if (p.ksplit > 1) {  // the split index fastest: the splits of a tile run side by side
+      tl.ks = t % p.ksplit;
+      t /= p.ksplit;
+    }
     tl.unit = t / p.tiles_per_unit;
     int r = t - tl.unit * p.tiles_per_unit;
     int mi = 0;
@@ -78,7 +86,11 @@ struct ScoreProb {
     tl.ni = r + key0(p, mi) / BN;
     return tl;
   }
-  __device__ static int k_blocks(const Params& p, const Tile&) { return ceil_div_d(p.K, S::BK); }
+  __device__ static int k_blocks(const Params& p, const Tile& tl) {
+    const int total = ceil_div_d(p.K, S::BK);
+    if (p.ksplit <= 1) return total;
+    return max(0, min(total, (tl.ks + 1) * p.kb_per_split) - tl.ks * p.kb_per_split);
+  }
   __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x7u; }
   __device__ static void prefetch(const Params& p) {
     for (int i = 0; i < TERMS; ++i) {
@@ -90,9 +102,10 @@ struct ScoreProb {
                                     uint8_t* a_dst, uint8_t* b_dst) {
     const int b = tl.unit / p.H, h = tl.unit - (tl.unit / p.H) * p.H;
     const int hb = p.b_shared ? 0 : h;
+    const int kg = kb + (p.ksplit > 1 ? tl.ks * p.kb_per_split : 0);
     for (int i = 0; i < TERMS; ++i) {
-      tma_load_4d(&p.a_map[i], bar, a_dst + i * S::A_TILE, kb * S::BK, tl.mi * S::BM, h, b);
-      tma_load_4d(&p.b_map[i], bar, b_dst + i * S::B_TILE, kb * S::BK, tl.ni * BN, hb, b);
+      tma_load_4d(&p.a_map[i], bar, a_dst + i * S::A_TILE, kg * S::BK, tl.mi * S::BM, h, b);
+      tma_load_4d(&p.b_map[i], bar, b_dst + i * S::B_TILE, kg * S::BK, tl.ni * BN, hb, b);
     }
   }
 
@@ -119,6 +132,18 @@ struct ScoreProb {
     const int gi = tl.mi * S::BM + row;
     if (gi >= p.T) return;
     const int gj_base = tl.ni * BN + c0;
+    if (ELEM == 4 && p.ksplit > 1) {
+      // K-split partial: raw fp32 sums, masked and split by the reduce pass
+      float* dst = p.part + ((static_cast<size_t>(tl.ks) * p.units + tl.unit) * p.T + gi) *
+                                static_cast<size_t>(p.ldp);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const int gj0 = gj_base + 4 * v;
+        if (gj0 + 4 > p.ldp) continue;
+        *reinterpret_cast<uint4*>(dst + gj0) = make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+      }
+      return;
+    }
     const bool diag = tl.ni * BN < (tl.mi + 1) * S::BM && (tl.ni + 1) * BN > tl.mi * S::BM;
     uint32_t hi[32], lo[32];
     if (ELEM == 2) {

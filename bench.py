@@ -465,6 +465,13 @@ def measured_tf32_tflops(dev) -> float:
     return _TF32_PEAK[dev]
 
 
+_STEPS = {"n": 1}
+
+
+def launches_per_step(prof, kind):
+    return _STEPS["n"]
+
+
 def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev):
     """Roofline of the dominant kernel of an op config (algorithmic work per launch / time).
 
@@ -481,7 +488,8 @@ def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev):
         work = units * T * (T - 1) * N
         peak, unit, bound = measured_tf32_tflops(dev), "TFLOP/s", "tensor"
         psrc = "measured in this run: cuBLAS TF32 GEMM 8192^3, best of 5 (burst)"
-        kern = "score pass (tc_gemm_kernel<ScoreProb<tf32>>, 3-product split)"
+        kern = ("score pass (tc_gemm_kernel<ScoreProb<tf32>>, 3-product split, K-split partials + "
+                "in-order reduce), per step")
         tname = "score_pass_config1"
     elif cfg_id == 3 and chunked:
         k = prof["state"]
@@ -502,6 +510,10 @@ def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev):
     if not k["launches"]:
         return None
     per = k["ms"] / k["launches"]
+    if cfg_id == 1:
+        # the fp32 score pass may be K-split: main pass + in-order reduce, both timed as "score";
+        # one score pass per step
+        per = k["ms"] / max(1, launches_per_step(prof, "score"))
     scale = 1e12 if unit == "TFLOP/s" else 1e9
     achieved = work / (per / 1e3) / scale
     return {"kernel": kern, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
@@ -550,6 +562,7 @@ def bench_op(args, world, rank, dev):
     peaks, src = load_peaks()
     sc = prof["score"]
     per_launch = sc["ms"] / sc["launches"] if sc["launches"] else None
+    _STEPS["n"] = args.steps
     roof = op_roofline(cfg_id, prof, (B, H, T, N, D), chunked, peaks, src, dev)
     line = {
         "metric": f"tril-attn TFLOP/s (config {cfg_id}, executed-algorithm causal flops)",
