@@ -465,14 +465,7 @@ def measured_tf32_tflops(dev) -> float:
     return _TF32_PEAK[dev]
 
 
-_STEPS = {"n": 1}
-
-
-def launches_per_step(prof, kind):
-    return _STEPS["n"]
-
-
-def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev):
+def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev, steps):
     """Roofline of the dominant kernel of an op config (algorithmic work per launch / time).
 
     * config 1 (fp32): score pass, causal Q K^T flops B H T(T-1) N against a measured cuBLAS
@@ -513,7 +506,7 @@ def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev):
     if cfg_id == 1:
         # the fp32 score pass may be K-split: main pass + in-order reduce, both timed as "score";
         # one score pass per step
-        per = k["ms"] / max(1, launches_per_step(prof, "score"))
+        per = k["ms"] / max(1, steps)
     scale = 1e12 if unit == "TFLOP/s" else 1e9
     achieved = work / (per / 1e3) / scale
     return {"kernel": kern, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
@@ -562,8 +555,7 @@ def bench_op(args, world, rank, dev):
     peaks, src = load_peaks()
     sc = prof["score"]
     per_launch = sc["ms"] / sc["launches"] if sc["launches"] else None
-    _STEPS["n"] = args.steps
-    roof = op_roofline(cfg_id, prof, (B, H, T, N, D), chunked, peaks, src, dev)
+    roof = op_roofline(cfg_id, prof, (B, H, T, N, D), chunked, peaks, src, dev, args.steps)
     line = {
         "metric": f"tril-attn TFLOP/s (config {cfg_id}, executed-algorithm causal flops)",
         "value": flops / (ms / 1e3) / 1e12,
