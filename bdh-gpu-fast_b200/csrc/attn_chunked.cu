@@ -23,6 +23,7 @@
 #include "internal.h"
 #include "score_pass.cuh"
 #include "tc_engine.cuh"
+#include "tc_pair_engine.cuh"
 #include "tma_host.h"
 
 namespace bdh {
@@ -238,6 +239,88 @@ struct ChunkValueProb {
   }
 };
 
+// CTA-pair form of the chunk value pass: one 256-row pair tile is exactly one chunk (C = 256),
+// both row blocks at once (M = 256 across the pair), N = 256 value columns. Each CTA stages its
+// own 128 rows of P / Q and its own 128 columns of V / S, so the operand bytes per SM per flop
+// halve against the single-CTA form (whose inter-chunk Q S segment is bound by L2 -> shared
+// memory ingress). Needs P written over whole chunks (the pair score pass does: it stores every
+// key of the chunk, zero above the diagonal).
+struct ChunkValuePair {
+  using Base = ChunkValueProb<3>;
+  using Params = Base::Params;
+  using S = PairShape<false, true, 2, 2, 3>;
+  struct Tile {
+    int unit, c, n;
+  };
+  __device__ static int nchunk(const Params& p) { return ceil_div_d(p.T, kChunk); }
+  __device__ static int nd2(const Params& p) { return ceil_div_d(p.D, 256); }
+  __device__ static int num_tiles(const Params& p) { return p.units * nchunk(p) * nd2(p); }
+  __device__ static Tile tile(const Params& p, int t) {
+    Tile tl;
+    const int per = nchunk(p) * nd2(p);
+    tl.unit = t / per;
+    const int r = t - tl.unit * per;
+    tl.c = r / nd2(p);
+    tl.n = r - tl.c * nd2(p);
+    return tl;
+  }
+  __device__ static int n_intra(const Params& p, const Tile& tl) {
+    return ceil_div_d(min(p.T, (tl.c + 1) * kChunk) - tl.c * kChunk, 64);
+  }
+  __device__ static int n_inter(const Params& p, const Tile& tl) {
+    return tl.c > 0 ? ceil_div_d(p.N, 64) : 0;
+  }
+  __device__ static int k_blocks(const Params& p, const Tile& tl) { return n_intra(p, tl) + n_inter(p, tl); }
+  __device__ static uint32_t pair_mask(const Params& p, const Tile& tl, int kb) {
+    return kb < n_intra(p, tl) ? 0x3u : 0x5u;
+  }
+  __device__ static uint32_t stage_tx(const Params& p, const Tile& tl, int kb) {
+    return 2u * (kb < n_intra(p, tl) ? 2 * S::A_TILE + S::B_TILE : S::A_TILE + 2 * S::B_TILE);
+  }
+  __device__ static void prefetch(const Params& p) { Base::prefetch(p); }
+  __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint32_t rank,
+                                    uint32_t bar, uint8_t* a_dst, uint8_t* b_dst) {
+    const int b = tl.unit / p.H, h = tl.unit - (tl.unit / p.H) * p.H;
+    const int r128 = static_cast<int>(rank) * 128;
+    const int row0 = tl.c * kChunk + r128;  // this CTA's 128 rows
+    const int col0 = tl.n * 256 + r128;     // this CTA's 128 value columns
+    const int ni = n_intra(p, tl);
+    if (kb < ni) {
+      const int hv = p.Hv == 1 ? 0 : h;
+      for (int i = 0; i < 2; ++i)
+        tma_load_4d_pair(&p.p_map[i], bar, a_dst + i * S::A_TILE, kb * 64, row0, tl.unit, 0);
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+        tma_load_4d_pair(&p.v_map, bar, b_dst + c * 64 * 128, col0 + c * 64, tl.c * kChunk + kb * 64,
+                         hv, b);
+    } else {
+      const int n0 = (kb - ni) * 64;
+      tma_load_4d_pair(&p.q_map, bar, a_dst, n0, row0, h, b);
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          tma_load_4d_pair(&p.s_map[i], bar, b_dst + i * S::B_TILE + c * 64 * 128, col0 + c * 64, n0,
+                           tl.c, tl.unit);
+    }
+  }
+  __device__ static void epilogue(const Params& p, const Tile& tl, int rank, int row, int c0,
+                                  const uint32_t (&r)[32]) {
+    Base::Tile t;
+    t.unit = tl.unit;
+    t.mi = 2 * tl.c + rank;
+    t.ni = 2 * tl.n;  // Base columns: ni * 128 + c0 with c0 in [0, 256)
+    Base::epilogue(p, t, row, c0, r);
+  }
+};
+
+bool use_pairs_chunked() {
+  static int on = [] {
+    const char* e = std::getenv("BDH_SM100_PAIR");
+    return (e != nullptr && std::atoi(e) == 0) ? 0 : 1;
+  }();
+  return on != 0;
+}
+
 using StateBf16 = StateProb<4>;
 using ChunkValueBf16 = ChunkValueProb<3>;
 
@@ -339,6 +422,10 @@ int launch_chunked_forward(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi,
                    ? 1
                    : 0;
   prm.err = err;
+  if (use_pairs_chunked() && kChunk == 256) {
+    const int tiles = prm.units * nchunks * static_cast<int>((a.D + 255) / 256);
+    return launch_pair<ChunkValuePair::S, ChunkValuePair>(prm, tiles, stream, kProfValue);
+  }
   return launch_tc<ChunkValueBf16::S, ChunkValueBf16>(prm, prm.units * prm.mt * prm.nd, stream,
                                                        kProfValue);
 }
