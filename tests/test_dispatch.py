@@ -167,3 +167,31 @@ def test_rope_out_alias_rejected():
 def test_backend_info_reports_native_status():
     info = ad.backend_info()
     assert info["BDH_ATTN_IMPL"] == "eager" and "ext_status" in info
+
+
+def test_cuda_attn_module_mirrors_reference_names():
+    """kernels.cuda_attn keeps the reference module's public names; its eager references work
+    on CPU, and the native entry points refuse CPU tensors (no silent fallback)."""
+    import numpy as np
+    import pytest
+    import torch
+
+    import tril_oracle as O
+    from conftest import golden
+    from kernels import cuda_attn
+
+    for name in ("tril_score_v", "tril_decode", "tril_score_v_ref", "tril_decode_ref",
+                 "tril_score_v_tiled_ref", "tril_decode_tiled_ref", "has_cuda_ext",
+                 "has_cuda_kernel", "ext_status", "pick_cuda_cold_tiles", "pick_cuda_decode_tile_n"):
+        assert callable(getattr(cuda_attn, name)), name
+    g = golden("fwd")
+    q, v = torch.tensor(g["shared_v_q"]), torch.tensor(g["shared_v_v"])
+    out = cuda_attn.tril_score_v_ref(q, q, v)
+    np.testing.assert_allclose(out.numpy(), g["shared_v_out_ref"], rtol=1e-5, atol=1e-5)
+    d = golden("decode")
+    kb, vb, qd = torch.tensor(d["kbuf"]), torch.tensor(d["vbuf"]), torch.tensor(d["q"])
+    assert O.rel_fro(cuda_attn.tril_decode_ref(qd, kb[:, :, :25], vb[:, :, :25]).numpy(),
+                     d["out_ext_S25"]) < 1e-6
+    assert float(cuda_attn.tril_decode_ref(qd, kb[:, :, :0], vb[:, :, :0]).abs().sum()) == 0.0
+    with pytest.raises(RuntimeError):
+        cuda_attn.tril_score_v(q, q, v)
