@@ -213,6 +213,22 @@ def max_over_ranks(x: float, world: int, dev) -> float:
     return float(t.item())
 
 
+def cross_rank_check(logits_fn, world: int, dev) -> dict:
+    """Verification outside the timed region: every rank evaluates the same small batch
+    (``logits_fn``), an all_gather brings each rank's logits checksum to every rank, and the
+    ranks must agree exactly (deterministic kernels, identical weights and inputs)."""
+    lg = logits_fn().double()
+    c = torch.stack([lg.sum(), lg.abs().sum(), (lg * lg).sum()]).to(dev)
+    if world == 1:
+        return {"ranks": 1, "identical": True}
+    gathered = [torch.zeros_like(c) for _ in range(world)]
+    dist.all_gather(gathered, c)
+    ref = gathered[0]
+    diff = max(float(((x - ref).abs() / ref.abs().clamp_min(1e-30)).max()) for x in gathered)
+    return {"ranks": world, "identical": all(bool(torch.equal(x, ref)) for x in gathered),
+            "max_rel_diff": diff, "collective": "all_gather (verification only, untimed)"}
+
+
 def timed(fn, steps: int, world: int, dev) -> float:
     """Device time (ms) of `steps` calls, bracketed by barrier + synchronize; max over ranks."""
     barrier(world)
@@ -346,6 +362,13 @@ def bench_config2(args, world, rank, dev):
             logits = model(idx_dev)[0]
         logits_host.copy_(logits, non_blocking=True)
 
+    def verify_logits():
+        gv = torch.Generator().manual_seed(4242)  # the same batch on every rank
+        iv = torch.randint(0, VOCAB, (2, 256), generator=gv).to(dev)
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+            return model(iv)[0].float()
+
+    xcheck = cross_rank_check(verify_logits, world, dev)
     for _ in range(max(1, args.warmup)):
         e2e_step()
     ms_e2e = timed(e2e_step, args.steps, world, dev)
@@ -409,6 +432,7 @@ def bench_config2(args, world, rank, dev):
         "kernel_ms": {k: v["ms"] / args.steps for k, v in prof.items() if v["launches"]},
         "gpu_launches": launches,
         "clocks": clk,
+        "cross_rank_check": xcheck,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, kind, cores, sample = cpu_reference_model(1, T, 1)

@@ -40,7 +40,13 @@ def _worker(rank, world, port, q):
         dist.all_gather(ws, wsum)
         xs = [torch.zeros(2, 8, dtype=torch.long) for _ in range(world)]
         dist.all_gather(xs, idx)
-        q.put((rank, t, [float(w) for w in ws], bool(torch.equal(xs[0], xs[1]))))
+        # the untimed cross-rank verification: same batch on every rank, checksums gathered
+        m.attn._attn_impl_override = "eager"
+        gv = torch.Generator().manual_seed(4242)
+        iv = torch.randint(0, 32, (2, 8), generator=gv)
+        with torch.no_grad():
+            chk = bench.cross_rank_check(lambda: m(iv)[0], world, torch.device("cpu"))
+        q.put((rank, t, [float(w) for w in ws], bool(torch.equal(xs[0], xs[1])), chk["identical"]))
     finally:
         dist.destroy_process_group()
 
@@ -61,7 +67,8 @@ def test_two_rank_gloo_weak_scaling_logic():
         p.join(timeout=120)
         assert p.exitcode == 0
     res = sorted(q.get(timeout=5) for _ in range(2))
-    for rank, t, ws, same_inputs in res:
+    for rank, t, ws, same_inputs, identical in res:
         assert t == 11.0          # max over ranks
         assert ws[0] == ws[1]     # replicated weights
         assert not same_inputs    # per-rank batches differ
+        assert identical          # the verification batch gives the same logits on every rank
