@@ -220,8 +220,15 @@ class BDH(nn.Module):
         """One layer on the fused kernels: encode (+ReLU +RoPE) -> tril attention -> LN ->
         encoder_v gate (xs * relu(.)) -> decoder (cuBLAS) -> residual double LN. Same arithmetic
         as the bf16-autocast layer of bdh.py:991-1052. ``xb`` is the bf16 copy of ``x`` (made
-        here when None); returns the new ``(x, xb)``."""
-        from kernels.sm100_attn import (latent_encode, latent_gate, layer_norm,
+        here when None); returns the new ``(x, xb)``.
+
+        ``BDH_SM100_GATE_X=1`` (D <= 256): the encode writes only the rotated latent and the
+        gate recomputes xs = relu(x @ enc) next to y @ encv (``latent_gate_x``, bit-identical
+        xs), so the (B, T, nh, N) xs latent is never stored. It trades 12.9 GB of HBM traffic
+        per config-2 step for a second K = 256 GEMM in the gate and measures slower on one
+        B200 (1.68M vs 1.74M tokens/s: the gate becomes tensor-bound under the power cap), so
+        the default stores xs."""
+        from kernels.sm100_attn import (latent_encode, latent_gate, latent_gate_x, layer_norm,
                                         residual_layer_norm, tril_score_v)
 
         B, T, _ = x.shape
@@ -238,13 +245,16 @@ class BDH(nn.Module):
             if dst_kr.dtype == torch.bfloat16:
                 qr_slot = dst_kr
         kmaj = os.environ.get("BDH_SM100_WEIGHT_KMAJOR", "1") != "0"
-        xs, qr = latent_encode(xb, self._bf16_param("encoder", kmaj), self.attn.freqs, rope_start,
-                               qr_out=qr_slot)
+        gate_x = x.size(-1) <= 256 and os.environ.get("BDH_SM100_GATE_X", "0") == "1"
+        enc = self._bf16_param("encoder", kmaj)
+        xs, qr = latent_encode(xb, enc, self.attn.freqs, rope_start, qr_out=qr_slot,
+                               want_xs=not gate_x)
         if dst_kr is not None and qr_slot is None:
             dst_kr.copy_(qr)
         y_kv = tril_score_v(qr, qr, xb.unsqueeze(1))
         yn = layer_norm(y_kv, eps, out_dtype=torch.bfloat16)
-        xy = latent_gate(yn, self._bf16_param("encoder_v", kmaj), xs)
+        encv = self._bf16_param("encoder_v", kmaj)
+        xy = latent_gate_x(yn, encv, xb, enc) if gate_x else latent_gate(yn, encv, xs)
         y_mlp = F.linear(xy.view(B, T, nh * xy.size(-1)), self._bf16_param("decoder").t())
         if x.dtype == torch.float32:
             return residual_layer_norm(x, y_mlp, eps, want_bf16=True)

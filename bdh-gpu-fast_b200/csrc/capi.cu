@@ -273,8 +273,8 @@ int bdh_latent_encode(const void* x, const int64_t x_strides[3], const void* enc
   if (!latent_sizes_ok(B, T, H, D, N, &msg)) return fail(BDH_ERR_INVALID, "latent_encode: " + msg);
   if (B * T * H * N == 0) return BDH_OK;
   if (D == 0) return fail(BDH_ERR_INVALID, "latent_encode: D must be positive");
-  if (!strides_ok(x_strides, 3) || !weight_strides_ok(enc_strides) || !strides_ok(xs_strides, 4) ||
-      !strides_ok(qr_strides, 4))
+  if (!strides_ok(x_strides, 3) || !weight_strides_ok(enc_strides) ||
+      (xs != nullptr && !strides_ok(xs_strides, 4)) || !strides_ok(qr_strides, 4))
     return fail(BDH_ERR_INVALID,
                 "latent_encode: last stride must be 1 and the others positive multiples of 8");
   if (freqs == nullptr) return fail(BDH_ERR_INVALID, "latent_encode: freqs is null");
@@ -286,7 +286,7 @@ int bdh_latent_encode(const void* x, const int64_t x_strides[3], const void* enc
   a.w = enc;
   std::memcpy(a.w_strides, enc_strides, sizeof(a.w_strides));
   a.xs = xs;
-  std::memcpy(a.xs_strides, xs_strides, sizeof(a.xs_strides));
+  if (xs != nullptr) std::memcpy(a.xs_strides, xs_strides, sizeof(a.xs_strides));
   a.qr = qr;
   std::memcpy(a.qr_strides, qr_strides, sizeof(a.qr_strides));
   a.freqs = freqs;
@@ -317,6 +317,34 @@ int bdh_latent_gate(const void* y, const int64_t y_strides[4], const void* encv,
   std::memcpy(a.xy_strides, xy_strides, sizeof(a.xy_strides));
   a.B = B; a.T = T; a.H = H; a.D = D; a.N = N;
   return launch_latent_gate(a, static_cast<cudaStream_t>(stream), device_error_ptr());
+}
+
+int bdh_latent_gate_x(const void* y, const int64_t y_strides[4], const void* encv,
+                      const int64_t encv_strides[3], const void* x, const int64_t x_strides[3],
+                      const void* enc, const int64_t enc_strides[3], void* xy,
+                      const int64_t xy_strides[4], int64_t B, int64_t T, int64_t H, int64_t D,
+                      int64_t N, void* stream) {
+  std::string msg;
+  if (!latent_sizes_ok(B, T, H, D, N, &msg)) return fail(BDH_ERR_INVALID, "latent_gate_x: " + msg);
+  if (B * T * H * N == 0) return BDH_OK;
+  if (D <= 0 || D > 256) return fail(BDH_ERR_INVALID, "latent_gate_x: D must be in 1..256");
+  if (!strides_ok(y_strides, 4) || !weight_strides_ok(encv_strides) || !strides_ok(x_strides, 3) ||
+      !weight_strides_ok(enc_strides) || !strides_ok(xy_strides, 4))
+    return fail(BDH_ERR_INVALID,
+                "latent_gate_x: last stride must be 1 and the others positive multiples of 8");
+  LatentArgs a;
+  a.y = y;
+  std::memcpy(a.y_strides, y_strides, sizeof(a.y_strides));
+  a.w = encv;
+  std::memcpy(a.w_strides, encv_strides, sizeof(a.w_strides));
+  a.x = x;
+  std::memcpy(a.x_strides, x_strides, sizeof(a.x_strides));
+  a.w2 = enc;
+  std::memcpy(a.w2_strides, enc_strides, sizeof(a.w2_strides));
+  a.xy = xy;
+  std::memcpy(a.xy_strides, xy_strides, sizeof(a.xy_strides));
+  a.B = B; a.T = T; a.H = H; a.D = D; a.N = N;
+  return launch_latent_gate_x(a, static_cast<cudaStream_t>(stream), device_error_ptr());
 }
 
 int bdh_layernorm(const void* x, int x_dtype, int64_t x_row_stride, void* y, int y_dtype,

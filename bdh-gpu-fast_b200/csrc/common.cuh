@@ -133,6 +133,40 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
+// 16-byte global store with an L2 cache policy.
+__device__ __forceinline__ void st_global_v4_hint(void* p, uint4 v, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w), "l"(policy)
+               : "memory");
+}
+
+// Transpose of an 8 x 8 matrix of 16-byte chunks inside each group of 8 lanes of a warp
+// (three exchange stages of 4 chunks with the lane at distance 4, 2, 1). On entry lane i of a
+// group holds row i (c[k] = element (i, k)); on exit lane j holds column j (c[k] = element (k, j)).
+// A thread that owns one tile row can then store 8 consecutive chunks of one row per group:
+// 128 contiguous bytes per 8 lanes instead of 32 rows per warp instruction.
+__device__ __forceinline__ void transpose_chunks8(uint4 (&c)[8], int lane) {
+#pragma unroll
+  for (int m = 4; m >= 1; m >>= 1) {
+    const bool hi = (lane & m) != 0;
+#pragma unroll
+    for (int k0 = 0; k0 < 8; ++k0) {
+      if (k0 & m) continue;
+      const int k1 = k0 | m;
+      const uint4 s = hi ? c[k0] : c[k1];
+      uint4 r;
+      r.x = __shfl_xor_sync(0xffffffffu, s.x, m);
+      r.y = __shfl_xor_sync(0xffffffffu, s.y, m);
+      r.z = __shfl_xor_sync(0xffffffffu, s.z, m);
+      r.w = __shfl_xor_sync(0xffffffffu, s.w, m);
+      if (hi)
+        c[k0] = r;
+      else
+        c[k1] = r;
+    }
+  }
+}
+
 __device__ __forceinline__ void tma_load_4d_hint(const CUtensorMap* map, uint64_t* bar, void* dst,
                                                  int c0, int c1, int c2, int c3, uint64_t policy) {
   asm volatile(

@@ -135,6 +135,8 @@ struct LatentArgs {
   int64_t y_strides[4] = {0, 0, 0, 1};
   const void* w = nullptr;       // enc / encv (H,D,N) {h,d,n}
   int64_t w_strides[3] = {0, 0, 1};
+  const void* w2 = nullptr;      // gate_x: enc (H,D,N) {h,d,n}
+  int64_t w2_strides[3] = {0, 0, 1};
   void* xs = nullptr;            // (B,T,H,N) {b,t,h,n}: written by encode, read by gate
   int64_t xs_strides[4] = {0, 0, 0, 1};
   void* qr = nullptr;            // (B,H,T,N) {b,h,t,n}
@@ -145,6 +147,7 @@ struct LatentArgs {
   int64_t B = 0, T = 0, H = 0, D = 0, N = 0, pos0 = 0;
 };
 int launch_latent_encode(const LatentArgs& a, cudaStream_t stream, int* err);
+int launch_latent_gate_x(const LatentArgs& a, cudaStream_t stream, int* err);
 int launch_latent_gate(const LatentArgs& a, cudaStream_t stream, int* err);
 
 // Row LayerNorms (layernorm.cu); strides in elements.

@@ -84,6 +84,21 @@ struct GateParams {
   int* err;
 };
 
+struct GateXParams {
+  CUtensorMap a_map;   // y (B,H,T,D): box 64 (k) x 128 (t)
+  CUtensorMap a2_map;  // x (B,T,D): box 64 (k) x 128 (t)
+  CUtensorMap b_map;   // encv (H,D,N), as the gate's b_map
+  CUtensorMap b2_map;  // enc (H,D,N), same layout as encv
+  uint16_t* xy;        // xy (B,T,H,N) bf16, element strides below (n contiguous)
+  int64_t xy_sb, xy_st, xy_sh;
+  int B, T, H, D, N;
+  int tb_n, nb_n;
+  int kbs;               // k-blocks of one product, ceil(D / 64)
+  int walk_chunk;
+  FastDiv fd_chunk, fd_ncb, fd_b, fd_nb;
+  int* err;
+};
+
 // The epilogue uses eight warps: two per TMEM lane quadrant, each draining one 64-column half
 // of the 128 x 128 tile (warp slot ew = quadrant + 4 * half owns its staging buffers).
 
@@ -94,10 +109,12 @@ struct StridedWalk {};
 // Chunks of walk_chunk row blocks of one column block (h, nb), the column block fastest across
 // chunks: a CTA keeps the column block's weights resident for the whole chunk, and the CTAs
 // running at one time write neighbouring column blocks of the same row chunk.
-struct ChunkedResidentWalk {
+template <int KBR>
+struct ChunkedResidentWalkT {
   static constexpr int kChunkedWalk = 1;
-  static constexpr int kResidentB = 4;  // D <= 256
+  static constexpr int kResidentB = KBR;
 };
+using ChunkedResidentWalk = ChunkedResidentWalkT<4>;  // D <= 256
 
 template <class Prm>
 __device__ __forceinline__ LatentTile latent_tile_chunked(int t, const Prm& p) {
@@ -146,14 +163,15 @@ __device__ __forceinline__ LatentTile latent_tile_colfixed(int t, int B, int H, 
   return tl;
 }
 
-template <int STAGES, int BUFS, int ORDER = 0, bool KW = false>
+// WX = false: qr only (xs is recomputed by the fused gate, bdh_latent_gate_x).
+template <int STAGES, int BUFS, int ORDER = 0, bool KW = false, bool WX = true>
 struct EncodeProb : LatentWalk<ORDER> {
   using S = TcShape<2, 128, false, !KW, 1, 1, STAGES>;
   static constexpr int kCustomEpilogue = 1;
   static constexpr int kEpiWarps = 8;
   static constexpr int kAccBuffers = 4;
   static constexpr int kBox = 32 * 128;           // one 64-column x 32-row swizzled box
-  static constexpr int kBuf = 2 * kBox;           // xs box + qr box
+  static constexpr int kBuf = WX ? 2 * kBox : kBox;  // (xs box +) qr box
   static constexpr int kWarpStage = BUFS * kBuf;  // BUFS staging buffers per warp
   static constexpr int kEpiSmemBytes = 8 * kWarpStage;
   using Params = EncodeParams;
@@ -228,15 +246,17 @@ struct EncodeProb : LatentWalk<ORDER> {
                                        uint8_t* epi, EpiState& st, volatile int*) {
     const int lr = row & 31;
     uint8_t* xs_box = stage(epi, row, part, st.iter);
-    uint8_t* qr_box = xs_box + kBox;
+    uint8_t* qr_box = WX ? xs_box + kBox : xs_box;
     // the stores that last read this buffer were committed BUFS tiles ago
     if (lr == 0) bulk_wait_read<BUFS - 1>();
     __syncwarp();
+    uint32_t r2[2][32];
+    tmem_ld32(taddr + static_cast<uint32_t>(part * 64), r2[0]);
+    tmem_ld32(taddr + static_cast<uint32_t>(part * 64 + 32), r2[1]);
+    tmem_ld_wait();
 #pragma unroll
     for (int c0 = 0; c0 < 64; c0 += 32) {
-      uint32_t r[32];
-      tmem_ld32(taddr + static_cast<uint32_t>(part * 64 + c0), r);
-      tmem_ld_wait();
+      const uint32_t(&r)[32] = r2[c0 >> 5];
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
         uint32_t xw[4], qw[4];
@@ -249,7 +269,7 @@ struct EncodeProb : LatentWalk<ORDER> {
                                      st.s[q]);
         }
         const int off = sw128(lr, (c0 >> 3) + v);
-        *reinterpret_cast<uint4*>(xs_box + off) = make_uint4(xw[0], xw[1], xw[2], xw[3]);
+        if (WX) *reinterpret_cast<uint4*>(xs_box + off) = make_uint4(xw[0], xw[1], xw[2], xw[3]);
         *reinterpret_cast<uint4*>(qr_box + off) = make_uint4(qw[0], qw[1], qw[2], qw[3]);
       }
     }
@@ -265,8 +285,8 @@ struct EncodeProb : LatentWalk<ORDER> {
       const int n = tl.nb * 128 + part * 64;
       if (t0 < p.T && n < p.N) {
         const uint64_t stream = l2_policy_evict_first();
-        tma_store_4d_hint(&p.xs_map, xs_box, n, tl.h, t0, tl.b, stream);
-        tma_store_4d_hint(&p.qr_map, xs_box + kBox, n, t0, tl.h, tl.b, stream);
+        if (WX) tma_store_4d_hint(&p.xs_map, xs_box, n, tl.h, t0, tl.b, stream);
+        tma_store_4d_hint(&p.qr_map, WX ? xs_box + kBox : xs_box, n, t0, tl.h, tl.b, stream);
       }
       bulk_commit();  // one group per tile (possibly empty)
     }
@@ -427,6 +447,120 @@ struct GateProb : LatentWalk<ORDER> {
   }
 };
 
+// ------------------------------------------------------------ gate, xs recomputed ----
+// xy = bf16(relu(bf16(x enc_h)) * relu(bf16(y_h encv_h))) for one 128 x 128 tile: the tile's
+// k-blocks [0, kbs) accumulate y encv into TMEM columns 0..127 and [kbs, 2 kbs) accumulate
+// x enc into columns 128..255 (kSubAcc), both weight blocks resident for the chunk of row
+// blocks. The x enc product repeats the encode kernel's MMAs on the same operands in the same
+// order, so xs is bit-identical to the encoder's, and it never crosses HBM: the encode then
+// writes qr only, halving its stores, and the gate reads no latent at all.
+template <int STAGES, bool KW = false>
+struct GateXProb : ChunkedResidentWalkT<8> {
+  using S = TcShape<2, 128, false, !KW, 1, 1, STAGES>;
+  static constexpr int kCustomEpilogue = 1;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kSubAcc = 2;
+  using Params = GateXParams;
+  using Tile = LatentTile;
+  // The xy slice of this thread (its row, 64 columns as eight 16-byte chunks) between the
+  // TMEM drain and the stores, which follow the accumulator's release.
+  struct EpiState {
+    uint4 c[8];
+  };
+  __device__ static int num_tiles(const Params& p) { return p.B * p.H * p.tb_n * p.nb_n; }
+  __device__ static Tile tile(const Params& p, int t) { return latent_tile_chunked(t, p); }
+  __device__ static const FastDiv& walk_chunk(const Params& p) { return p.fd_chunk; }
+  __device__ static int b_key(const Params& p, const Tile& tl) { return tl.h * p.nb_n + tl.nb; }
+  __device__ static int k_blocks(const Params& p, const Tile&) { return 2 * p.kbs; }
+  __device__ static int sub_k_blocks(const Params& p, const Tile&) { return p.kbs; }
+  __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x1u; }
+  __device__ static void prefetch(const Params& p) {
+    tma_prefetch_desc(&p.a_map);
+    tma_prefetch_desc(&p.a2_map);
+    tma_prefetch_desc(&p.b_map);
+    tma_prefetch_desc(&p.b2_map);
+  }
+  __device__ static void load_b(const Params& p, const Tile& tl, int kb, uint64_t* bar,
+                                uint8_t* dst) {
+    const uint64_t keep = l2_policy_evict_last();
+    const CUtensorMap* m = kb < p.kbs ? &p.b_map : &p.b2_map;
+    const int k = (kb < p.kbs ? kb : kb - p.kbs) * 64;
+    if (KW) {
+      tma_load_4d_hint(m, bar, dst, k, tl.nb * 128, tl.h, 0, keep);
+      return;
+    }
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+      tma_load_4d_hint(m, bar, dst + c * 64 * 128, tl.nb * 128 + c * 64, k, tl.h, 0, keep);
+  }
+  __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint64_t* bar,
+                                    uint8_t* a_dst, uint8_t*) {
+    const uint64_t keep = l2_policy_evict_last();
+    if (kb < p.kbs)
+      tma_load_4d_hint(&p.a_map, bar, a_dst, kb * 64, tl.tb * 128, tl.h, tl.b, keep);
+    else
+      tma_load_4d_hint(&p.a2_map, bar, a_dst, (kb - p.kbs) * 64, tl.tb * 128, tl.b, 0, keep);
+  }
+  __device__ static void epilogue_begin(const Params&, int, int, uint8_t*, EpiState&, bool,
+                                        const Tile&) {}
+  __device__ static void epilogue_prefetch(const Params&, const Tile&, bool, const Tile&, int, int,
+                                           uint8_t*, EpiState&) {}
+  __device__ static bool epilogue_tile(const Params&, const Tile&, int, int part, uint32_t taddr,
+                                       uint8_t*, EpiState& st, volatile int*) {
+    // all four loads in flight before the one wait
+    uint32_t ry2[2][32], rx2[2][32];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      tmem_ld32(taddr + static_cast<uint32_t>(part * 64 + 32 * h), ry2[h]);
+      tmem_ld32(taddr + static_cast<uint32_t>(128 + part * 64 + 32 * h), rx2[h]);
+    }
+    tmem_ld_wait();
+#pragma unroll
+    for (int c0 = 0; c0 < 64; c0 += 32) {
+      const uint32_t(&ry)[32] = ry2[c0 >> 5];
+      const uint32_t(&rx)[32] = rx2[c0 >> 5];
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = 8 * v + 2 * e;
+          o[e] = mul_bf16x2(cvt_relu_bf16x2(__uint_as_float(rx[i]), __uint_as_float(rx[i + 1])),
+                            cvt_relu_bf16x2(__uint_as_float(ry[i]), __uint_as_float(ry[i + 1])));
+        }
+        st.c[(c0 >> 3) + v] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    return true;
+  }
+  // After the release: lane (g, j) of the warp stores chunk j of tile rows 8g..8g+7 of its
+  // 32-row quadrant, so every 8 lanes write one contiguous 128-byte row segment.
+  __device__ static void epilogue_after(const Params& p, const Tile& tl, int row, int part,
+                                        uint8_t*, EpiState& st) {
+    const int lane = row & 31;
+    transpose_chunks8(st.c, lane);
+    const int n = tl.nb * 128 + part * 64 + (lane & 7) * 8;
+    const int t0 = tl.tb * 128 + (row & ~31) + (lane >> 3) * 8;
+    uint16_t* base = p.xy + tl.b * p.xy_sb + tl.h * p.xy_sh + n;
+    const uint64_t stream = l2_policy_evict_first();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int t = t0 + k;
+      if (t >= p.T || n >= p.N) continue;
+      uint16_t* dst = base + static_cast<int64_t>(t) * p.xy_st;
+      if (n + 8 <= p.N) {
+        st_global_v4_hint(dst, st.c[k], stream);
+      } else {  // ragged last chunk (N even): whole bf16 pairs
+        const uint32_t w[4] = {st.c[k].x, st.c[k].y, st.c[k].z, st.c[k].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (2 * e < p.N - n) reinterpret_cast<uint32_t*>(dst)[e] = w[e];
+      }
+    }
+  }
+  __device__ static void epilogue_end(const Params&, int, int, uint8_t*, EpiState&) {}
+};
+
 // Pipeline forms. Default: weights resident per column block, chunked walk, six 16 KB
 // activation stages (Encode / Gate; EncodeK / GateK read d-contiguous weights K-major).
 // BDH_SM100_LATENT_VARIANT=1 selects the streamed-operand forms (both operands through the
@@ -440,6 +574,13 @@ using Gate = GateProb<6, 2, 3>;
 using GateK = GateProb<6, 2, 3, true>;
 using GateS = GateProb<5, 2, 1>;
 using GateSK = GateProb<5, 2, 1, true>;
+// qr-only encode (two staging buffers per warp in the room xs used) and the fused gate
+using EncodeQ = EncodeProb<6, 2, 3, false, false>;
+using EncodeQK = EncodeProb<6, 2, 3, true, false>;
+using EncodeSQ = EncodeProb<5, 2, 0, false, false>;
+using EncodeSQK = EncodeProb<5, 2, 0, true, false>;
+using GateX = GateXProb<6>;
+using GateXK = GateXProb<6, true>;
 
 // Row blocks per chunk of the chunked walk: the largest divisor of the row-block count <= 32.
 int walk_chunk_for(int64_t row_blocks) {
@@ -504,7 +645,8 @@ int launch_latent_encode(const LatentArgs& a, cudaStream_t stream, int* err) {
   EncodeParams prm{};
   if (!map_x_btd(&prm.a_map, a.x, a.x_strides, a.B, a.T, a.D, "latent_encode: x")) return BDH_ERR_INVALID;
   if (!map_weight(&prm.b_map, a.w, a.w_strides, a.H, a.D, a.N, "latent_encode: enc")) return BDH_ERR_INVALID;
-  if (!map_bthn(&prm.xs_map, a.xs, a.xs_strides, a.B, a.T, a.H, a.N, "latent_encode: xs"))
+  const bool wx = a.xs != nullptr;
+  if (wx && !map_bthn(&prm.xs_map, a.xs, a.xs_strides, a.B, a.T, a.H, a.N, "latent_encode: xs"))
     return BDH_ERR_INVALID;
   if (!map_bhtn_store(&prm.qr_map, a.qr, a.qr_strides, a.B, a.H, a.T, a.N, "latent_encode: qr"))
     return BDH_ERR_INVALID;
@@ -525,12 +667,60 @@ int launch_latent_encode(const LatentArgs& a, cudaStream_t stream, int* err) {
   prm.err = err;
   const int64_t ntiles = a.B * a.H * int64_t(prm.tb_n) * prm.nb_n;
   const bool kw = weight_k_major(a.w_strides);
-  if (a.D > 256 || latent_variant() == 1)  // resident weights hold D <= 256
-    return kw ? launch_tc<EncodeSK::S, EncodeSK>(prm, static_cast<int>(ntiles), stream, kProfEncode)
-              : launch_tc<EncodeS::S, EncodeS>(prm, static_cast<int>(ntiles), stream, kProfEncode);
-  if (kw)
-    return launch_tc<EncodeK::S, EncodeK>(prm, static_cast<int>(ntiles), stream, kProfEncode);
-  return launch_tc<Encode::S, Encode>(prm, static_cast<int>(ntiles), stream, kProfEncode);
+  const int nt = static_cast<int>(ntiles);
+  if (a.D > 256 || latent_variant() == 1) {  // resident weights hold D <= 256
+    if (!wx)
+      return kw ? launch_tc<EncodeSQK::S, EncodeSQK>(prm, nt, stream, kProfEncode)
+                : launch_tc<EncodeSQ::S, EncodeSQ>(prm, nt, stream, kProfEncode);
+    return kw ? launch_tc<EncodeSK::S, EncodeSK>(prm, nt, stream, kProfEncode)
+              : launch_tc<EncodeS::S, EncodeS>(prm, nt, stream, kProfEncode);
+  }
+  if (!wx)
+    return kw ? launch_tc<EncodeQK::S, EncodeQK>(prm, nt, stream, kProfEncode)
+              : launch_tc<EncodeQ::S, EncodeQ>(prm, nt, stream, kProfEncode);
+  if (kw) return launch_tc<EncodeK::S, EncodeK>(prm, nt, stream, kProfEncode);
+  return launch_tc<Encode::S, Encode>(prm, nt, stream, kProfEncode);
+}
+
+int launch_latent_gate_x(const LatentArgs& a, cudaStream_t stream, int* err) {
+  GateXParams prm{};
+  if (a.D > 256) {
+    set_error("latent_gate_x: D must be at most 256 (both weight blocks stay resident)");
+    return BDH_ERR_INVALID;
+  }
+  if (weight_k_major(a.w_strides) != weight_k_major(a.w2_strides)) {
+    set_error("latent_gate_x: enc and encv must have the same layout (n or d contiguous)");
+    return BDH_ERR_INVALID;
+  }
+  if (!map_bhtd(&prm.a_map, a.y, a.y_strides, a.B, a.H, a.T, a.D, "latent_gate_x: y")) return BDH_ERR_INVALID;
+  if (!map_x_btd(&prm.a2_map, a.x, a.x_strides, a.B, a.T, a.D, "latent_gate_x: x")) return BDH_ERR_INVALID;
+  if (!map_weight(&prm.b_map, a.w, a.w_strides, a.H, a.D, a.N, "latent_gate_x: encv")) return BDH_ERR_INVALID;
+  if (!map_weight(&prm.b2_map, a.w2, a.w2_strides, a.H, a.D, a.N, "latent_gate_x: enc")) return BDH_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(a.xy) & 15u) != 0) {
+    set_error("latent_gate_x: xy must be 16-byte aligned");
+    return BDH_ERR_INVALID;
+  }
+  prm.xy = static_cast<uint16_t*>(a.xy);
+  prm.xy_sb = a.xy_strides[0];
+  prm.xy_st = a.xy_strides[1];
+  prm.xy_sh = a.xy_strides[2];
+  prm.B = static_cast<int>(a.B);
+  prm.T = static_cast<int>(a.T);
+  prm.H = static_cast<int>(a.H);
+  prm.D = static_cast<int>(a.D);
+  prm.N = static_cast<int>(a.N);
+  prm.tb_n = static_cast<int>((a.T + 127) / 128);
+  prm.nb_n = static_cast<int>((a.N + 127) / 128);
+  prm.kbs = static_cast<int>((a.D + 63) / 64);
+  prm.walk_chunk = walk_chunk_for(a.B * int64_t(prm.tb_n));
+  prm.fd_chunk = FastDiv(static_cast<uint32_t>(prm.walk_chunk));
+  prm.fd_ncb = FastDiv(static_cast<uint32_t>(prm.H * prm.nb_n));
+  prm.fd_b = FastDiv(static_cast<uint32_t>(prm.B));
+  prm.fd_nb = FastDiv(static_cast<uint32_t>(prm.nb_n));
+  prm.err = err;
+  const int nt = static_cast<int>(a.B * a.H * int64_t(prm.tb_n) * prm.nb_n);
+  if (weight_k_major(a.w_strides)) return launch_tc<GateXK::S, GateXK>(prm, nt, stream, kProfGate);
+  return launch_tc<GateX::S, GateX>(prm, nt, stream, kProfGate);
 }
 
 int launch_latent_gate(const LatentArgs& a, cudaStream_t stream, int* err) {

@@ -138,6 +138,20 @@ struct AccBufs<P, std::void_t<decltype(P::kAccBuffers)>> {
   static constexpr int value = P::kAccBuffers;
 };
 
+//   P::kSubAcc = 2 (no KCHUNK) -> a tile accumulates kSubAcc independent products side by side:
+//       k-blocks [i * P::sub_k_blocks(prm, tile), (i + 1) * ...) form product i, accumulated from
+//       zero into TMEM columns [i * BN, (i + 1) * BN) of the tile's buffer, so the epilogue sees
+//       kSubAcc * BN columns (e.g. two projections of the same rows that it multiplies
+//       elementwise).
+template <class P, class = void>
+struct SubAcc {
+  static constexpr int value = 1;
+};
+template <class P>
+struct SubAcc<P, std::void_t<decltype(P::kSubAcc)>> {
+  static constexpr int value = P::kSubAcc;
+};
+
 template <class P, class = void>
 struct EpiSmem {
   static constexpr int value = 0;
@@ -258,8 +272,12 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
   static_assert(S::STAGES <= 8, "barrier block layout (2 x 8 stages + 2 x 4 accumulators + 5)");
   constexpr bool kRes = ResidentB<P>::value > 0;
   constexpr int NACC = AccBufs<P>::value;
-  static_assert(NACC == 2 || (NACC == 4 && S::BN <= 128), "four accumulators need BN <= 128");
-  constexpr uint32_t kTmemCols = static_cast<uint32_t>(NACC * S::BN);
+  constexpr int NSUB = SubAcc<P>::value;
+  constexpr int ACC_COLS = NSUB * S::BN;  // TMEM columns of one tile's accumulator buffer
+  static_assert(NACC == 2 || NACC == 4, "two or four accumulator buffers");
+  static_assert(NACC * ACC_COLS <= 512, "accumulator buffers exceed the 512 TMEM columns");
+  static_assert(NSUB == 1 || S::KCHUNK == 0, "side-by-side products need unchunked accumulation");
+  constexpr uint32_t kTmemCols = static_cast<uint32_t>(NACC * ACC_COLS);
   constexpr int SB = tc_stage_bytes<S, P>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -400,9 +418,12 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
             break;
           }
           tc_fence_after();
-          const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * S::BN);
+          uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * ACC_COLS);
           const int kb0 = S::KCHUNK == 0 ? 0 : ch * S::KCHUNK;
           const int kb1 = S::KCHUNK == 0 ? nkb : min(nkb, kb0 + S::KCHUNK);
+          int sub_kbs = 0;  // k-blocks per side-by-side product (NSUB > 1)
+          if constexpr (NSUB > 1) sub_kbs = P::sub_k_blocks(prm, tile);
+          int in_sub = 0;   // k-blocks already accumulated into the current product
           for (int kb = kb0; kb < kb1; ++kb) {
             if (!wait_bounded(full + stage, ph, abort_flag, prm.err, kErrTimeoutMma)) {
               ok = false;
@@ -422,7 +443,8 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
                 const uint64_t bd =
                     kRes ? b0 + static_cast<uint32_t>((kb * S::B_TILE + S::b_koff(kk)) >> 4)
                          : b0 + (soff16 + ((tb * S::B_TILE + S::b_koff(kk)) >> 4));
-                const uint32_t accumulate = (kb > kb0 || kk > 0 || pr > 0) ? 1u : 0u;
+                const bool first_kb = NSUB > 1 ? in_sub == 0 : kb == kb0;
+                const uint32_t accumulate = (!first_kb || kk > 0 || pr > 0) ? 1u : 0u;
                 if (S::ELEM == 2)
                   umma_f16(d_tmem, ad, bd, S::IDESC, accumulate);
                 else
@@ -430,6 +452,12 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
               }
             }
             umma_commit(empty + stage);
+            if constexpr (NSUB > 1) {
+              if (++in_sub == sub_kbs) {
+                in_sub = 0;
+                d_tmem += static_cast<uint32_t>(S::BN);
+              }
+            }
             if (++stage == S::STAGES) {
               stage = 0;
               soff16 = 0;
@@ -474,7 +502,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
         }
         tc_fence_after();
         const uint32_t tbase =
-            tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * S::BN);
+            tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * ACC_COLS);
         ok = P::epilogue_tile(prm, tile, row, part, tbase, epi, st, abort_flag);
         tc_fence_before();
         mbar_arrive(tempty + acc);
@@ -499,7 +527,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
         }
         tc_fence_after();
         const uint32_t tbase =
-            tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * S::BN);
+            tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * ACC_COLS);
 #pragma unroll 1
         for (int c0 = 0; c0 < S::BN; c0 += 32) {
           uint32_t r[32];
@@ -526,7 +554,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
           }
           tc_fence_after();
           const uint32_t tbase =
-              tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * S::BN);
+              tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * ACC_COLS);
 #pragma unroll
           for (int c0 = 0; c0 < BNC; c0 += 32) {
             uint32_t r[32];

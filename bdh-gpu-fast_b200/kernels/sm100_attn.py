@@ -39,6 +39,7 @@ _F32 = 0
 _BF16 = 1
 
 _c_i64_4 = ctypes.c_int64 * 4
+ABI_VERSION = 3  # BDH_ABI_VERSION of include/bdh_sm100.h
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 
@@ -74,6 +75,8 @@ def _declare(lib: ctypes.CDLL) -> None:
                                       _i64, _i64, _i64, _i64, _i64, _i64, _vp]
     lib.bdh_latent_gate.argtypes = [_vp, P, _vp, _c_i64_3p, _vp, P, _vp, P,
                                     _i64, _i64, _i64, _i64, _i64, _vp]
+    lib.bdh_latent_gate_x.argtypes = [_vp, P, _vp, _c_i64_3p, _vp, _c_i64_3p, _vp, _c_i64_3p,
+                                      _vp, P, _i64, _i64, _i64, _i64, _i64, _vp]
     lib.bdh_layernorm.argtypes = [_vp, ctypes.c_int, _i64, _vp, ctypes.c_int, _i64, _i64, _i64,
                                   ctypes.c_float, _vp]
     lib.bdh_residual_layernorm.argtypes = [_vp, _i64, _vp, ctypes.c_int, _i64, _vp, _i64, _vp,
@@ -84,7 +87,8 @@ def _declare(lib: ctypes.CDLL) -> None:
                                      _i64, _i64, _i64, _i64, _i64, _vp, _i64, ctypes.c_int, _vp,
                                      ctypes.c_size_t, _vp]
     for name in ("bdh_rope_rotate", "bdh_tril_score_v", "bdh_tril_decode", "bdh_tril_score_v_bwd",
-                 "bdh_relu_mul", "bdh_latent_encode", "bdh_latent_gate", "bdh_layernorm",
+                 "bdh_relu_mul", "bdh_latent_encode", "bdh_latent_gate", "bdh_latent_gate_x",
+                 "bdh_layernorm",
                  "bdh_residual_layernorm", "bdh_state_decode"):
         getattr(lib, name).restype = ctypes.c_int
 
@@ -99,7 +103,7 @@ def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
         lib = ctypes.CDLL(str(p))
         _declare(lib)
         ver = lib.bdh_abi_version()
-        if ver != 2:
+        if ver != ABI_VERSION:
             raise RuntimeError(f"{p}: unexpected ABI version {ver}")
     except BaseException as exc:  # noqa: BLE001 - remembered for ext_status()
         _lib_error = exc
@@ -421,12 +425,13 @@ def _st(t: torch.Tensor, n: int):
 
 def latent_encode(x: torch.Tensor, enc: torch.Tensor, freqs: torch.Tensor, pos0: int = 0, *,
                   xs_out: Optional[torch.Tensor] = None,
-                  qr_out: Optional[torch.Tensor] = None):
+                  qr_out: Optional[torch.Tensor] = None, want_xs: bool = True):
     """Fused ``xs = relu(x @ enc)`` (B,T,H,N) and ``qr = RoPE(xs)`` (B,H,T,N), bf16.
 
     ``x`` (B,T,D), ``enc`` (H,D,N). ``qr_out`` may be a strided view (a cache slot); returns
-    ``(xs, qr)``. Replaces ``BDH._encoder_relu`` (bdh.py:861-889) followed by the attention's
-    RoPE apply (bdh.py:396-412).
+    ``(xs, qr)``, with ``xs`` None when ``want_xs`` is False (qr only: the caller recomputes xs
+    in ``latent_gate_x``). Replaces ``BDH._encoder_relu`` (bdh.py:861-889) followed by the
+    attention's RoPE apply (bdh.py:396-412).
     """
     if x.dim() != 3 or enc.dim() != 3 or x.size(-1) != enc.size(1):
         raise ValueError("latent_encode expects x (B,T,D) and enc (H,D,N)")
@@ -439,16 +444,20 @@ def latent_encode(x: torch.Tensor, enc: torch.Tensor, freqs: torch.Tensor, pos0:
         raise ValueError("freqs must be float32 with one entry per latent dimension")
     f = f.contiguous()
     _check_paired_freqs(f)
-    if xs_out is None:
+    if xs_out is None and want_xs:
         xs_out = torch.empty(B, T, H, N, dtype=torch.bfloat16, device=dev)
     if qr_out is None:
         qr_out = torch.empty(B, H, T, N, dtype=torch.bfloat16, device=dev)
-    if tuple(xs_out.shape) != (B, T, H, N) or tuple(qr_out.shape) != (B, H, T, N):
+    if (xs_out is not None and tuple(xs_out.shape) != (B, T, H, N)) or \
+            tuple(qr_out.shape) != (B, H, T, N):
         raise ValueError("latent_encode: xs_out must be (B,T,H,N) and qr_out (B,H,T,N)")
-    _check_latent("latent_encode", x, xs_out, qr_out, weight=enc)
+    outs = (qr_out,) if xs_out is None else (xs_out, qr_out)
+    _check_latent("latent_encode", x, *outs, weight=enc)
+    xs_ptr = None if xs_out is None else xs_out.data_ptr()
+    xs_st = None if xs_out is None else _st(xs_out, 4)
     with torch.cuda.device(dev):
         rc = lib.bdh_latent_encode(x.data_ptr(), _st(x, 3), enc.data_ptr(), _st(enc, 3),
-                                   xs_out.data_ptr(), _st(xs_out, 4), qr_out.data_ptr(),
+                                   xs_ptr, xs_st, qr_out.data_ptr(),
                                    _st(qr_out, 4), f.data_ptr(), B, T, H, D, N, int(pos0),
                                    _stream(dev))
     _check(rc, "latent_encode")
@@ -480,6 +489,38 @@ def latent_gate(y: torch.Tensor, encv: torch.Tensor, xs: torch.Tensor, *,
                                  xs.data_ptr(), _st(xs, 4), out.data_ptr(), _st(out, 4),
                                  B, T, H, D, N, _stream(dev))
     _check(rc, "latent_gate")
+    return out
+
+
+def latent_gate_x(y: torch.Tensor, encv: torch.Tensor, x: torch.Tensor, enc: torch.Tensor, *,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``xy = relu(x @ enc) * relu(y @ encv)`` in the (B,T,H,N) latent layout, bf16, with the
+    encoder product recomputed in the gate kernel instead of read back (bit-identical to
+    ``latent_encode``'s xs), so no xs latent is stored.
+
+    ``y`` (B,H,T,D), ``encv`` and ``enc`` (H,D,N) with one layout, ``x`` (B,T,D); D <= 256.
+    Replaces ``BDH._encoder_relu``'s output use, ``_encoder_v_relu`` and the product of
+    ``_mlp_merge`` (bdh.py:861-945).
+    """
+    if y.dim() != 4 or encv.dim() != 3 or enc.dim() != 3 or x.dim() != 3:
+        raise ValueError("latent_gate_x expects y (B,H,T,D), encv (H,D,N), x (B,T,D), enc (H,D,N)")
+    dev = _require_cuda(y, encv, x, enc)
+    lib = _require_lib()
+    B, H, T, D = y.shape
+    N = encv.size(-1)
+    if tuple(x.shape) != (B, T, D) or tuple(enc.shape) != (H, D, N) or tuple(encv.shape) != (H, D, N):
+        raise ValueError("latent_gate_x: shapes of y, encv, x and enc disagree")
+    if out is None:
+        out = torch.empty(B, T, H, N, dtype=torch.bfloat16, device=dev)
+    elif tuple(out.shape) != (B, T, H, N):
+        raise ValueError("latent_gate_x: out must be (B,T,H,N)")
+    _check_latent("latent_gate_x", y, x, out, weight=encv)
+    _check_latent("latent_gate_x", weight=enc)
+    with torch.cuda.device(dev):
+        rc = lib.bdh_latent_gate_x(y.data_ptr(), _st(y, 4), encv.data_ptr(), _st(encv, 3),
+                                   x.data_ptr(), _st(x, 3), enc.data_ptr(), _st(enc, 3),
+                                   out.data_ptr(), _st(out, 4), B, T, H, D, N, _stream(dev))
+    _check(rc, "latent_gate_x")
     return out
 
 

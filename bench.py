@@ -378,24 +378,41 @@ def bench_config2(args, world, rank, dev):
     # rooflines of the three largest kernels of the step; "roofline" is the one with the most
     # device time. Algorithmic work per launch (one layer, the whole batch):
     #   score pass  B H T (T-1) N flops (causal Q K^T, T(T-1)/2 pairs x 2N)       tensor
+    # With xs recomputed in the gate (BDH_SM100_GATE_X=1):
+    #   encode      B T H N x 2 bytes written (QR) + x and weights read            HBM
+    #   gate        2 x 2 B T H N D flops (x enc and y encv), xy written           tensor
+    # With xs stored (default):
     #   encode      2 B T H N x 2 bytes written (xs, QR) + x and weights read      HBM
     #   gate        B T H N x 2 read (xs) + B T H N x 2 written (xy) + y, weights  HBM
     peaks, src = load_peaks()
     tpeak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    tsrc = f"{src} bf16_tflops_sustained (kernel timed inside a long step)"
     lat = B * T * N_HEAD * N_LAT * 2
     small = B * T * D_MODEL * 2 + N_HEAD * D_MODEL * N_LAT * 2
+    gate_x = os.environ.get("BDH_SM100_GATE_X", "0") == "1"
+    if gate_x:
+        enc_spec = ("latent encode x@enc + ReLU + RoPE (tc_gemm_kernel<EncodeProb<..., WX=false>>), "
+                    "QR written", "hbm", lat + small, 1e9, "GB/s", peaks["hbm_gbs"],
+                    f"{src} hbm_gbs", "latent_encode_config2")
+        gate_spec = ("latent gate relu(x@enc) * relu(y@encv), xs recomputed (tc_gemm_kernel<GateXProb>, "
+                     "two side-by-side TMEM products), xy written", "tensor",
+                     4 * B * T * N_HEAD * N_LAT * D_MODEL, 1e12, "TFLOP/s", tpeak, tsrc,
+                     "latent_gate_config2")
+    else:
+        enc_spec = ("latent encode x@enc + ReLU + RoPE (tc_gemm_kernel<EncodeProb>), xs and QR written",
+                    "hbm", 2 * lat + small, 1e9, "GB/s", peaks["hbm_gbs"], f"{src} hbm_gbs",
+                    "latent_encode_config2")
+        gate_spec = ("latent gate xs * relu(y@encv) (tc_gemm_kernel<GateProb>), xs read, xy written",
+                     "hbm", 2 * lat + small + B * N_HEAD * T * D_MODEL * 2, 1e9, "GB/s",
+                     peaks["hbm_gbs"], f"{src} hbm_gbs", "latent_gate_config2")
     specs = {
         "score": ("score pass tril(QR QR^T,-1) (tc_pair_kernel<ScorePair>, cta_group::2 256x256 tiles)"
                   if os.environ.get("BDH_SM100_PAIR", "1") != "0"
                   else "score pass tril(QR QR^T,-1) (tc_gemm_kernel<ScoreProb<bf16>>)",
-                  "tensor", B * N_HEAD * T * (T - 1) * N_LAT, 1e12, "TFLOP/s", tpeak,
-                  f"{src} bf16_tflops_sustained (kernel timed inside a long step)", "score_pass_config2"),
-        "encode": ("latent encode x@enc + ReLU + RoPE (tc_gemm_kernel<EncodeProb>), xs and QR written",
-                   "hbm", 2 * lat + small, 1e9, "GB/s", peaks["hbm_gbs"], f"{src} hbm_gbs",
-                   "latent_encode_config2"),
-        "gate": ("latent gate xs * relu(y@encv) (tc_gemm_kernel<GateProb>), xs read, xy written",
-                 "hbm", 2 * lat + small + B * N_HEAD * T * D_MODEL * 2, 1e9, "GB/s", peaks["hbm_gbs"],
-                 f"{src} hbm_gbs", "latent_gate_config2"),
+                  "tensor", B * N_HEAD * T * (T - 1) * N_LAT, 1e12, "TFLOP/s", tpeak, tsrc,
+                  "score_pass_config2"),
+        "encode": enc_spec,
+        "gate": gate_spec,
     }
     rooflines = {}
     for k, (name, bound, work, scale, unit, peak, psrc, tname) in specs.items():

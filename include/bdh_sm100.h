@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define BDH_ABI_VERSION 2
+#define BDH_ABI_VERSION 3
 
 #define BDH_DTYPE_F32 0
 #define BDH_DTYPE_BF16 1
@@ -212,7 +212,8 @@ int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* 
  *   qr[b,h,t,n] = RoPE(xs[b,t,h,:])[n] at position pos0 + t       qr (B,H,T,N) strided
  * freqs must come in equal pairs (freqs[2p] == freqs[2p+1], as bdh.py:41-49 builds them).
  * Strides are in elements: x_strides {b,t,d}, enc_strides {h,d,n}, xs_strides {b,t,h,n},
- * qr_strides {b,h,t,n}; the last stride of each must be 1, the others multiples of 8 — except
+ * qr_strides {b,h,t,n}; xs may be NULL (not written); the last stride of each must be 1, the
+ * others multiples of 8 — except
  * the weights, which may instead have d contiguous (a transposed (H,N,D) copy seen as (H,D,N),
  * enc_strides {N*D, 1, D}); that layout is read K-major and is the faster one.
  *
@@ -220,7 +221,13 @@ int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* 
  * bdh.py:914-945 (BDH._encoder_v_relu and the x * y of _mlp_merge):
  *   xy[b,t,h,n] = bf16(xs[b,t,h,n] * relu(bf16(sum_k y[b,h,t,k] encv[h,k,n])))
  * y (B,H,T,D) strides {b,h,t,d}; encv (H,D,N); xs and xy (B,T,H,N) strides {b,t,h,n}.
- * Neither call allocates; both are stream-ordered and graph-capturable.
+ *
+ * bdh_latent_gate_x is bdh_latent_gate with xs recomputed from x and enc in the same kernel
+ * (the encoder's MMAs on the same operands, so xs is bit-identical) instead of read back:
+ *   xy[b,t,h,n] = bf16(relu(bf16(sum_k x[b,t,k] enc[h,k,n])) * relu(bf16(sum_k y[b,h,t,k] encv[h,k,n])))
+ * With it, bdh_latent_encode may be called with xs == NULL (qr only) and the (B,T,nh,N) xs
+ * latent never exists. D <= 256; enc and encv must share one weight layout.
+ * None of these calls allocates; all are stream-ordered and graph-capturable.
  */
 int bdh_latent_encode(const void* x, const int64_t x_strides[3], const void* enc,
                       const int64_t enc_strides[3], void* xs, const int64_t xs_strides[4],
@@ -230,6 +237,11 @@ int bdh_latent_gate(const void* y, const int64_t y_strides[4], const void* encv,
                     const int64_t encv_strides[3], const void* xs, const int64_t xs_strides[4],
                     void* xy, const int64_t xy_strides[4], int64_t B, int64_t T, int64_t H,
                     int64_t D, int64_t N, void* stream);
+int bdh_latent_gate_x(const void* y, const int64_t y_strides[4], const void* encv,
+                      const int64_t encv_strides[3], const void* x, const int64_t x_strides[3],
+                      const void* enc, const int64_t enc_strides[3], void* xy,
+                      const int64_t xy_strides[4], int64_t B, int64_t T, int64_t H, int64_t D,
+                      int64_t N, void* stream);
 
 /*
  * Affine-free LayerNorm over the last dimension, as the BDH layer applies it with F.layer_norm

@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
     lib = sa.load_library()
     for name in _declared():
         assert hasattr(lib, name), f"{name} missing from {sa._LIB_PATH}"
-    assert lib.bdh_abi_version() == 2
+    assert lib.bdh_abi_version() == sa.ABI_VERSION == 3
 
 
 def test_workspace_queries_are_host_only():
@@ -107,6 +107,20 @@ def test_latent_entry_points_validate_on_host():
     assert rc == 1 and b"stride" in lib.bdh_last_error()
     # empty problems are a no-op
     assert lib.bdh_latent_encode(None, s3, None, s3, None, s4, None, s4, None, 0, 16, 2, 256, 64, 0, None) == 0
+    # the fused gate keeps both weight blocks resident: D <= 256, one weight layout
+    w_n = (ctypes.c_int64 * 3)(512 * 64, 64, 1)      # (H, D, N) with n contiguous
+    w_d = (ctypes.c_int64 * 3)(512 * 64, 1, 512)     # d contiguous (transposed copy)
+    rc = lib.bdh_latent_gate_x(None, s4, None, w_n, None, s3, None, w_n, None, s4,
+                               1, 16, 2, 512, 64, None)
+    assert rc == 1 and b"256" in lib.bdh_last_error()
+    rc = lib.bdh_latent_gate_x(None, s4, None, w_n, None, s3, None, w_d, None, s4,
+                               1, 16, 2, 256, 64, None)
+    assert rc == 1 and b"same layout" in lib.bdh_last_error()
+    rc = lib.bdh_latent_gate_x(None, bad, None, w_n, None, s3, None, w_n, None, s4,
+                               1, 16, 2, 256, 64, None)
+    assert rc == 1 and b"stride" in lib.bdh_last_error()
+    assert lib.bdh_latent_gate_x(None, s4, None, w_n, None, s3, None, w_n, None, s4,
+                                 1, 0, 2, 256, 64, None) == 0
 
 
 def test_layernorm_entry_points_validate_on_host():

@@ -1,6 +1,6 @@
-"""GPU parity of the fused latent projections (bdh_latent_encode / bdh_latent_gate) against
-the reference's own bf16 outputs (tests/golden/golden_latent.npz), the pinned numpy oracle and
-torch's cuBLAS path, and of the BDH model layer that uses them.
+"""GPU parity of the fused latent projections (bdh_latent_encode / bdh_latent_gate /
+bdh_latent_gate_x) against the reference's own bf16 outputs (tests/golden/golden_latent.npz),
+the pinned numpy oracle and torch's cuBLAS path, and of the BDH model layer that uses them.
 
 The projections are K = D dot products accumulated in fp32 and rounded once to bf16, so a
 different accumulation order can move an output to the neighbouring bf16 value; those flips
@@ -58,6 +58,74 @@ def test_latent_gate_golden():
     xy = sa().latent_gate(b16(g["y"]), b16(g["encv"]), b16(g["xs"]))
     assert np.mean(f32(xy) != g["xy"]) < 0.01
     assert O.rel_fro(f32(xy), g["xy"]) < 3e-3
+
+
+def test_latent_gate_x_golden():
+    """The fused gate recomputes xs from x and enc: the reference's xy within the bf16 bound."""
+    g = golden("latent")
+    xy = sa().latent_gate_x(b16(g["y"]), b16(g["encv"]), b16(g["x"]), b16(g["enc"]))
+    assert np.mean(f32(xy) != g["xy"]) < 0.01
+    assert O.rel_fro(f32(xy), g["xy"]) < 3e-3
+
+
+@pytest.mark.parametrize("B,T,D,H,N,kmaj", [(2, 200, 256, 4, 1024, False),
+                                             (2, 200, 256, 4, 1024, True),
+                                             (1, 130, 32, 3, 136, False),
+                                             (3, 77, 96, 2, 520, True),
+                                             (1, 1, 64, 1, 64, False)])
+def test_latent_gate_x_equals_encode_then_gate(B, T, D, H, N, kmaj):
+    """qr-only encode + fused gate give exactly the bits of encode (xs, qr) + gate: the gate's
+    x enc product is the encoder's MMA sequence on the same operands."""
+    g = torch.Generator().manual_seed(B * 31 + T + D)
+    x = F.layer_norm(torch.randn(B, T, D, generator=g), (D,)).to(torch.bfloat16).to(DEV)
+    y = F.layer_norm(torch.randn(B, H, T, D, generator=g), (D,)).to(torch.bfloat16).to(DEV)
+    enc = (torch.randn(H, D, N, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    encv = (torch.randn(H, D, N, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    if kmaj:
+        enc, encv = sa().weight_k_major(enc), sa().weight_k_major(encv)
+    freqs = torch.as_tensor(O.get_freqs(N)).to(DEV)
+    xs, qr = sa().latent_encode(x, enc, freqs, 7)
+    none, qr_only = sa().latent_encode(x, enc, freqs, 7, want_xs=False)
+    assert none is None and torch.equal(qr_only, qr)
+    xy = sa().latent_gate(y, encv, xs)
+    xy_x = sa().latent_gate_x(y, encv, x, enc)
+    assert torch.equal(xy_x, xy)
+    xy_o = O.latent_gate(f32(y), f32(encv), O.latent_encode(f32(x), f32(enc), O.get_freqs(N), 7)[0])
+    assert O.rel_fro(f32(xy_x), xy_o) < 3e-3
+
+
+def test_latent_gate_x_ragged_latent_width():
+    """N = 130 (not a multiple of the 8-element store chunk) through padded views: the ragged
+    last chunk of every row is written pair by pair and nothing past N is touched."""
+    B, T, D, H, N, NP = 2, 100, 64, 2, 130, 136
+    g = torch.Generator().manual_seed(130)
+
+    def padded(*shape):
+        return torch.empty(*shape[:-1], NP, dtype=torch.bfloat16, device=DEV)[..., :shape[-1]]
+
+    x = torch.randn(B, T, D, generator=g).to(torch.bfloat16).to(DEV)
+    y = torch.randn(B, H, T, D, generator=g).to(torch.bfloat16).to(DEV)
+    enc, encv = padded(H, D, N), padded(H, D, N)
+    enc.copy_((torch.randn(H, D, N, generator=g) * 0.1).to(torch.bfloat16))
+    encv.copy_((torch.randn(H, D, N, generator=g) * 0.1).to(torch.bfloat16))
+    freqs = torch.as_tensor(O.get_freqs(N)).to(DEV)
+    xs = padded(B, T, H, N)
+    sa().latent_encode(x, enc, freqs, 0, xs_out=xs, qr_out=padded(B, H, T, N))
+    ref = padded(B, T, H, N)
+    sa().latent_gate(y, encv, xs, out=ref)
+    full = torch.full((B, T, H, NP), 5.0, dtype=torch.bfloat16, device=DEV)
+    out = sa().latent_gate_x(y, encv, x, enc, out=full[..., :N])
+    assert torch.equal(out, ref)
+    assert bool((full[..., N:] == 5.0).all())
+
+
+def test_latent_gate_x_rejects_mixed_weight_layouts():
+    B, T, D, H, N = 1, 64, 64, 2, 128
+    x = torch.zeros(B, T, D, dtype=torch.bfloat16, device=DEV)
+    y = torch.zeros(B, H, T, D, dtype=torch.bfloat16, device=DEV)
+    w = torch.zeros(H, D, N, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(RuntimeError, match="same layout"):
+        sa().latent_gate_x(y, w, x, sa().weight_k_major(w))
 
 
 @pytest.mark.parametrize("B,T,D,H,N,pos0", [(2, 200, 256, 4, 1024, 5), (1, 128, 64, 2, 200, 0),
@@ -125,6 +193,9 @@ def test_latent_kernels_full_size_vs_cublas():
     assert (xy != xy_ref).float().mean().item() < 2e-3
     d = (xy.float() - xy_ref.float()).norm() / xy_ref.float().norm()
     assert d.item() < 3e-3
+    # the model's form: qr-only encode + gate with xs recomputed, same bits
+    assert torch.equal(sa().latent_encode(x, enc, freqs, 0, want_xs=False)[1], qr)
+    assert torch.equal(sa().latent_gate_x(y, encv, x, enc), xy)
 
 
 def _model(n_layer=2, n_embd=256, n_head=4, mult=128):
@@ -173,6 +244,20 @@ def test_model_latent_layer_matches_unfused_and_oracle(monkeypatch):
     w["freqs"] = m.attn.freqs.reshape(-1).cpu().numpy()
     ref16 = O.bdh_forward_bf16(idx.cpu().numpy(), w, n_layer=2, n_head=4)
     assert O.rel_fro(f32(fused), ref16) < 1e-2
+
+
+def test_model_gate_x_matches_stored_xs(monkeypatch):
+    """The model's fused layer with xs recomputed in the gate (BDH_SM100_GATE_X=1) and with xs
+    stored and re-read (default) give identical logits."""
+    m = _model(n_layer=2)
+    idx = torch.randint(0, 256, (2, 256), generator=torch.Generator().manual_seed(19)).to(DEV)
+    out = {}
+    monkeypatch.setenv("BDH_SM100_LATENT", "1")
+    for flag in ("1", "0"):
+        monkeypatch.setenv("BDH_SM100_GATE_X", flag)
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            out[flag] = m(idx)[0].float()
+    assert torch.equal(out["1"], out["0"])
 
 
 def test_model_latent_layer_stagewise_vs_oracle():
