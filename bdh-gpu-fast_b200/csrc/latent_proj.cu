@@ -84,6 +84,33 @@ struct GateParams {
   int* err;
 };
 
+// xy stores from registers: lane (g, j) of a warp that holds tile rows quadrant*32 + lane (64
+// columns from n0 as eight 16-byte chunks) transposes them so that it stores chunk j of rows
+// 8g..8g+7; every 8 lanes then write one contiguous 128-byte row segment.
+__device__ __forceinline__ void store_xy_rows(uint16_t* xy, int64_t sb, int64_t st, int64_t sh,
+                                              int T, int N, int b, int h, int t_quad, int n0,
+                                              int lane, uint4 (&c)[8]) {
+  transpose_chunks8(c, lane);
+  const int n = n0 + (lane & 7) * 8;
+  const int t0 = t_quad + (lane >> 3) * 8;
+  uint16_t* base = xy + b * sb + h * sh + n;
+  const uint64_t stream = l2_policy_evict_first();
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int t = t0 + k;
+    if (t >= T || n >= N) continue;
+    uint16_t* dst = base + static_cast<int64_t>(t) * st;
+    if (n + 8 <= N) {
+      st_global_v4_hint(dst, c[k], stream);
+    } else {  // ragged last chunk (N even): whole bf16 pairs
+      const uint32_t w[4] = {c[k].x, c[k].y, c[k].z, c[k].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (2 * e < N - n) reinterpret_cast<uint32_t*>(dst)[e] = w[e];
+    }
+  }
+}
+
 struct GateXParams {
   CUtensorMap a_map;   // y (B,H,T,D): box 64 (k) x 128 (t)
   CUtensorMap a2_map;  // x (B,T,D): box 64 (k) x 128 (t)
@@ -537,26 +564,8 @@ struct GateXProb : ChunkedResidentWalkT<8> {
   // 32-row quadrant, so every 8 lanes write one contiguous 128-byte row segment.
   __device__ static void epilogue_after(const Params& p, const Tile& tl, int row, int part,
                                         uint8_t*, EpiState& st) {
-    const int lane = row & 31;
-    transpose_chunks8(st.c, lane);
-    const int n = tl.nb * 128 + part * 64 + (lane & 7) * 8;
-    const int t0 = tl.tb * 128 + (row & ~31) + (lane >> 3) * 8;
-    uint16_t* base = p.xy + tl.b * p.xy_sb + tl.h * p.xy_sh + n;
-    const uint64_t stream = l2_policy_evict_first();
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int t = t0 + k;
-      if (t >= p.T || n >= p.N) continue;
-      uint16_t* dst = base + static_cast<int64_t>(t) * p.xy_st;
-      if (n + 8 <= p.N) {
-        st_global_v4_hint(dst, st.c[k], stream);
-      } else {  // ragged last chunk (N even): whole bf16 pairs
-        const uint32_t w[4] = {st.c[k].x, st.c[k].y, st.c[k].z, st.c[k].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (2 * e < p.N - n) reinterpret_cast<uint32_t*>(dst)[e] = w[e];
-      }
-    }
+    store_xy_rows(p.xy, p.xy_sb, p.xy_st, p.xy_sh, p.T, p.N, tl.b, tl.h,
+                  tl.tb * 128 + (row & ~31), tl.nb * 128 + part * 64, row & 31, st.c);
   }
   __device__ static void epilogue_end(const Params&, int, int, uint8_t*, EpiState&) {}
 };
