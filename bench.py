@@ -319,6 +319,116 @@ def cpu_reference_model(B_cpu: int, T: int, steps: int):
     return B_cpu * T * steps / dt, kind, cores, sample
 
 
+def _ref_ext():
+    """The reference CPU extension from oracle/_ref, or None (then the numpy port is timed)."""
+    try:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import build_ref
+
+        return build_ref.load_module()
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def _cpu_model_name() -> str:
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except Exception:  # noqa: BLE001
+        pass
+    return ""
+
+
+def cpu_op_baseline(cfg_id: int):
+    """Reference CPU attention on a bounded sample of an op config, in the op line's unit
+    (executed-algorithm causal TFLOP/s, fp32 on the host cores). Config 1: the whole op (16
+    (b,h) units, T = 512); config 3: one unit at T = 8192; config 5: one unit at T = 2048,
+    forward by the reference extension and backward by the numpy port of the analytic backward
+    (the reference's backward is Python over torch and does not travel). RoPE is applied to the
+    sample beforehand, untimed (O(T N) against the O(T^2 N) attention)."""
+    import numpy as np
+
+    sys.path.insert(0, str(REPO / "oracle"))
+    import tril_oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    ext = _ref_ext()
+    units, T = {1: (16, 512), 3: (1, 8192), 5: (1, 2048)}[cfg_id]
+    N, D = N_LAT, D_MODEL
+    g = torch.Generator().manual_seed(3000 + cfg_id)
+    shift = 1.645 if cfg_id == 3 else 0.0
+    q = torch.relu(torch.randn(1, units, T, N, generator=g) - shift)
+    v = torch.randn(1, 1, T, D, generator=g)
+    if cfg_id == 3:
+        v = torch.nn.functional.layer_norm(v, (D,))
+    qr = torch.from_numpy(tril_oracle.rope(q.numpy(), tril_oracle.get_freqs(N)).astype(np.float32))
+    if ext is not None:
+        fwd = lambda: ext.tril_score_v_cpu(qr, qr, v)  # noqa: E731
+    else:
+        fwd = lambda: tril_oracle.tril_score_v(qr.numpy(), qr.numpy(), v.numpy(), acc=np.float32)  # noqa: E731
+    dout = torch.randn(1, units, T, D, generator=g).numpy()
+    reps = 3 if cfg_id == 1 else 1
+    fwd()  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        fwd()
+        if cfg_id == 5:
+            tril_oracle.tril_backward(qr.numpy(), qr.numpy(), v.numpy(), dout, acc=np.float32,
+                                      k_is_q=True)
+    dt = time.perf_counter() - t0
+    flops = units * T * (T - 1) * ((N + D) + ((3 * N + 2 * D) if cfg_id == 5 else 0)) * reps
+    kind = "reference" if ext is not None and cfg_id != 5 else "port"
+    how = ("reference CPU extension tril_score_v_cpu" if ext is not None else "numpy port")
+    if cfg_id == 5:
+        how += " forward + numpy port of the analytic backward"
+    sample = (f"{units} (b,h) unit(s) x T={T}, N={N}, D={D}, fp32, {reps} timed call(s) after 1 "
+              f"warm-up; {how}; {cores} threads; {_cpu_model_name()}")
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": kind,
+            "sample": sample}
+
+
+def cpu_decode_baseline(steps: int = 4):
+    """BDH cached decode on the host: the config-4 model at B = 1 after a 512-token prompt, the
+    reference CPU extension's tril_decode_cpu / tril_score_v_cpu inside the model (fp32 cache),
+    `steps` timed T = 1 steps. Returns the cpu_baseline object (tokens/s)."""
+    import bdh_model
+    from bdh_cache import CacheManager
+    from kernels import attention_dispatch as ad
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    ext = _ref_ext()
+    cfg = bdh_model.BDHConfig(n_layer=N_LAYER, n_embd=D_MODEL, n_head=N_HEAD,
+                              mlp_internal_dim_multiplier=128, vocab_size=VOCAB, dropout=0.0)
+    torch.manual_seed(1004)
+    model = bdh_model.BDH(cfg).eval()
+    model.attn._attn_impl_override = "eager"
+    P = 512
+    toks = torch.randint(0, VOCAB, (1, P + steps + 1), generator=torch.Generator().manual_seed(2004))
+    cache = CacheManager.from_config(cfg, 1, P + steps + 1, torch.device("cpu"))
+    orig = (ad.eager_tril_attn, ad.eager_decode_attn)
+    if ext is not None:
+        ad.eager_tril_attn = lambda q, k, v: ext.tril_score_v_cpu(q, k, v)  # noqa: E731
+        ad.eager_decode_attn = lambda q, k, v: ext.tril_decode_cpu(q, k, v)  # noqa: E731
+    try:
+        with torch.inference_mode():
+            model(toks[:, :P], cache=cache)
+            model(toks[:, P:P + 1], cache=cache)  # warm-up step
+            t0 = time.perf_counter()
+            for i in range(steps):
+                model(toks[:, P + 1 + i:P + 2 + i], cache=cache)
+            dt = time.perf_counter() - t0
+    finally:
+        ad.eager_tril_attn, ad.eager_decode_attn = orig
+    kind = "reference" if ext is not None else "port"
+    sample = (f"config-4 model, B=1, {P}-token prompt, {steps} timed decode steps after 1 warm-up, "
+              f"fp32 cache; attention by the {'reference CPU extension' if ext is not None else 'eager torch path'}; "
+              f"{cores} threads; {_cpu_model_name()}")
+    return {"value": steps / dt, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
+
+
 # --------------------------------------------------------------------- config 2
 def bench_config2(args, world, rank, dev):
     import bdh_model
@@ -614,6 +724,8 @@ def bench_op(args, world, rank, dev):
         "gpu_launches": sum(v_["launches"] for v_ in prof.values()),
         "clocks": clk, "peak_source": src,
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_op_baseline(cfg_id)
     return line
 
 
@@ -678,7 +790,8 @@ def bench_decode(args, world, rank, dev):
     dec = prof["decode"]
     peaks, src = load_peaks()
     gbs = bytes_step * args.steps / (dec["ms"] / 1e3) / 1e9 if dec["ms"] else None
-    return {
+    cpu = cpu_decode_baseline() if rank == 0 and world == 1 and not args.no_cpu_baseline else None
+    line = {
         "metric": "BDH decode tokens/s (config 4)", "value": world * B * args.steps / (ms / 1e3),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -702,6 +815,9 @@ def bench_decode(args, world, rank, dev):
         "gpu_launches": sum(v_["launches"] for v_ in prof.values()),
         "clocks": clk,
     }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
 
 
 # ------------------------------------------------------------------- reference arm
