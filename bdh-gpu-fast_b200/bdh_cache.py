@@ -12,6 +12,13 @@ Same interface and layout as the reference ``bdh_cache.CacheManager`` (``bdh_cac
 Addition for the B200 decode kernel: ``get_past_raw(level)`` returns the storage-dtype views
 without any cast; the kernel reads bf16 or fp32 storage directly and widens in registers, so a
 bf16 cache never costs a full-past conversion per step.
+
+Opt-in fp8 key storage (``storage_dtype=torch.float8_e4m3fn``, no reference counterpart): each
+cached key row is e4m3 with one fp32 scale (``_kr_scale (n_layer, B, n_head, capacity)``,
+row ~= e4m3 * scale, scale = max|row| / 448), values stay bf16. ``get_past_scale`` /
+``reserve_scale`` give the scale views beside ``get_past_raw`` / ``reserve``; ``get_past``
+dequantizes. The decode stream is then ~1 byte per cached key element instead of 2 (bf16) or
+4 (fp32); the format is lossy (3 mantissa bits).
 """
 
 from __future__ import annotations
@@ -19,6 +26,32 @@ from __future__ import annotations
 from typing import List, Optional, Tuple
 
 import torch
+
+FP8 = torch.float8_e4m3fn
+
+
+def quantize_rows_fp8_torch(x: torch.Tensor):
+    """Row-scaled e4m3 of the last axis with torch ops (CPU caches): the same arithmetic as the
+    native bdh_quantize_rows_fp8 (inv = 448 / amax in fp32, products rounded to fp32, e4m3 round
+    to nearest even). Returns (q float8_e4m3fn, scale fp32)."""
+    x = x.float()
+    amax = x.abs().amax(dim=-1)
+    inv = torch.where(amax > 0, 448.0 / amax, torch.zeros_like(amax))
+    q = (x * inv.unsqueeze(-1)).to(FP8)
+    return q, amax / 448.0
+
+
+def _quantize_into(x: torch.Tensor, out: torch.Tensor, scale: torch.Tensor) -> None:
+    """Quantize rows of x (B,H,T,N) into the fp8 slot `out` and its `scale` (B,H,T): the native
+    kernel for CUDA tensors (it raises if the library is missing), torch ops on the CPU."""
+    if x.is_cuda:
+        from kernels.sm100_attn import quantize_rows_fp8
+
+        quantize_rows_fp8(x, out=out, scale=scale)
+        return
+    q, sc = quantize_rows_fp8_torch(x)
+    out.copy_(q)
+    scale.copy_(sc)
 
 
 class CacheManager:
@@ -42,6 +75,9 @@ class CacheManager:
         self.device = torch.device(device)
         self.compute_dtype = compute_dtype
         self.storage_dtype = storage_dtype or compute_dtype
+        self.kr_fp8 = self.storage_dtype == FP8
+        # fp8 keys keep bf16 values (V is 1/32 of the key bytes per position at nh N = 32 D)
+        self.v_dtype = torch.bfloat16 if self.kr_fp8 else self.storage_dtype
         self.storage_matches_compute = self.storage_dtype == self.compute_dtype
         self.page_size = page_size
         self.seq_len = 0
@@ -52,7 +88,10 @@ class CacheManager:
         self._kr_buf = torch.zeros(n_layer, batch_size, n_head, self.capacity, n_latent,
                                    dtype=self.storage_dtype, device=self.device)
         self._v_buf = torch.zeros(n_layer, batch_size, 1, self.capacity, n_embd,
-                                  dtype=self.storage_dtype, device=self.device)
+                                  dtype=self.v_dtype, device=self.device)
+        self._kr_scale = (torch.zeros(n_layer, batch_size, n_head, self.capacity,
+                                      dtype=torch.float32, device=self.device)
+                          if self.kr_fp8 else None)
 
     @property
     def _kr(self) -> List[torch.Tensor]:
@@ -104,14 +143,20 @@ class CacheManager:
         kr = torch.empty(self.n_layer, self.batch_size, self.n_head, new_cap, self.n_latent,
                          dtype=self.storage_dtype, device=self.device)
         v = torch.empty(self.n_layer, self.batch_size, 1, new_cap, self.n_embd,
-                        dtype=self.storage_dtype, device=self.device)
+                        dtype=self.v_dtype, device=self.device)
+        sc = (torch.empty(self.n_layer, self.batch_size, self.n_head, new_cap,
+                          dtype=torch.float32, device=self.device) if self.kr_fp8 else None)
         used = self.seq_len + (self._pending_t or 0)
         if used > 0:
             kr[:, :, :, :used].copy_(self._kr_buf[:, :, :, :used])
             v[:, :, :, :used].copy_(self._v_buf[:, :, :, :used])
+            if sc is not None:
+                sc[:, :, :, :used].copy_(self._kr_scale[:, :, :, :used])
             self.bytes_copied_on_grow += used * self.n_layer * self.batch_size * (
-                self.n_head * self.n_latent + self.n_embd) * self._kr_buf.element_size()
+                self.n_head * self.n_latent * self._kr_buf.element_size()
+                + self.n_embd * self._v_buf.element_size())
         self._kr_buf, self._v_buf = kr, v
+        self._kr_scale = sc
         self.capacity = new_cap
         self.n_grows += 1
 
@@ -123,10 +168,26 @@ class CacheManager:
         return (self._kr_buf[level].narrow(2, 0, self.seq_len),
                 self._v_buf[level].narrow(2, 0, self.seq_len))
 
+    def get_past_scale(self, level: int) -> Optional[torch.Tensor]:
+        """fp8 keys: the (B, n_head, seq_len) fp32 row scales of the committed prefix."""
+        if not self.kr_fp8 or self.seq_len == 0:
+            return None
+        return self._kr_scale[level].narrow(2, 0, self.seq_len)
+
+    def reserve_scale(self, level: int, T: int) -> torch.Tensor:
+        """fp8 keys: the scale slots of the block ``reserve(level, T)`` returned."""
+        if not self.kr_fp8:
+            raise RuntimeError("reserve_scale needs fp8 key storage")
+        return self._kr_scale[level].narrow(2, self.seq_len, T)
+
     def get_past(self, level: int) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor]]:
-        """Committed prefix of ``level``, cast to ``compute_dtype`` when storage differs."""
+        """Committed prefix of ``level``, cast to ``compute_dtype`` when storage differs
+        (fp8 keys: dequantized, row * scale)."""
         kr, v = self.get_past_raw(level)
-        if kr is not None and not self.storage_matches_compute:
+        if kr is not None and self.kr_fp8:
+            kr = (kr.float() * self.get_past_scale(level).unsqueeze(-1)).to(self.compute_dtype)
+            v = v.to(self.compute_dtype)
+        elif kr is not None and not self.storage_matches_compute:
             kr = kr.to(self.compute_dtype)
             v = v.to(self.compute_dtype)
         return kr, v
@@ -156,7 +217,11 @@ class CacheManager:
         if T != new_v.size(2):
             raise ValueError(f"kr T={T} != v T={new_v.size(2)}")
         end = self._track_pending(T)
-        self._kr_buf[level].narrow(2, self.seq_len, T).copy_(new_kr)
+        if self.kr_fp8:
+            _quantize_into(new_kr, self._kr_buf[level].narrow(2, self.seq_len, T),
+                           self._kr_scale[level].narrow(2, self.seq_len, T))
+        else:
+            self._kr_buf[level].narrow(2, self.seq_len, T).copy_(new_kr)
         self._v_buf[level].narrow(2, self.seq_len, T).copy_(new_v)
         return end
 
@@ -168,7 +233,10 @@ class CacheManager:
         end = self._write_block(level, new_kr, new_v)
         kr = self._kr_buf[level].narrow(2, 0, end)
         v = self._v_buf[level].narrow(2, 0, end)
-        if not self.storage_matches_compute:
+        if self.kr_fp8:
+            sc = self._kr_scale[level].narrow(2, 0, end).unsqueeze(-1)
+            kr, v = (kr.float() * sc).to(self.compute_dtype), v.to(self.compute_dtype)
+        elif not self.storage_matches_compute:
             kr, v = kr.to(self.compute_dtype), v.to(self.compute_dtype)
         return kr, v
 
@@ -186,8 +254,11 @@ class CacheManager:
 
     @property
     def bytes_allocated(self) -> int:
-        return (self._kr_buf.numel() * self._kr_buf.element_size()
-                + self._v_buf.numel() * self._v_buf.element_size())
+        n = (self._kr_buf.numel() * self._kr_buf.element_size()
+             + self._v_buf.numel() * self._v_buf.element_size())
+        if self._kr_scale is not None:
+            n += self._kr_scale.numel() * self._kr_scale.element_size()
+        return n
 
 
 class StateCache:

@@ -87,23 +87,41 @@ class Attention(nn.Module):
         return rope_tables(self.freqs, T, rope_start, device)
 
     def forward(self, Q, K, V, rope_start: int = 0, past_kr=None, past_v=None, out_kr=None,
-                past_is_raw: bool = False, relu_input: bool = False):
+                past_is_raw: bool = False, relu_input: bool = False, past_kr_scale=None,
+                out_kr_scale=None):
         """Returns ``(out, QR, V)``; QR/V are this block's keys/values for the cache.
 
         ``past_kr``/``past_v``: packed past (``past_is_raw``: in the cache storage dtype).
         ``out_kr``: optional cache slot receiving QR. ``relu_input``: Q is the encoder
         pre-activation; the latent is ``relu(Q)`` (folded into the RoPE read when possible).
+        fp8 key cache: ``past_kr_scale`` / ``out_kr_scale`` are the row scales beside the raw
+        fp8 past and the fp8 slot (QR is quantized into the slot).
         """
         assert K is Q
         impl = self._attn_impl_override or resolve_attn_impl()
         B, nh, T, _ = Q.shape
+        fp8_slot = out_kr is not None and out_kr.dtype == torch.float8_e4m3fn
         if past_kr is None:
-            out, QR = bdh_rope_attn(Q, V, self.freqs, rope_start, impl=impl, qr_out=out_kr,
-                                    relu_input=relu_input)
+            out, QR = bdh_rope_attn(Q, V, self.freqs, rope_start, impl=impl,
+                                    qr_out=None if fp8_slot else out_kr, relu_input=relu_input)
+            if fp8_slot:
+                from kernels.sm100_attn import quantize_rows_fp8
+
+                quantize_rows_fp8(QR, out=out_kr, scale=out_kr_scale)
             return out, QR, V
         if relu_input:
             Q = F.relu(Q)
         S = past_kr.size(2)
+        if past_kr.dtype == torch.float8_e4m3fn and impl == "cuda_sm100" and T == 1:
+            from kernels.sm100_attn import rope_rotate, tril_decode_fp8
+
+            out = tril_decode_fp8(Q, past_kr, past_kr_scale, past_v, freqs=self.freqs,
+                                  pos=rope_start, kr_slot=out_kr, slot_scale=out_kr_scale)
+            return out, out_kr, V
+        if past_kr.dtype == torch.float8_e4m3fn:  # multi-token block: dequantized past
+            past_kr = past_kr.float() * past_kr_scale.unsqueeze(-1)
+            past_v = past_v.float()
+            past_is_raw = True
         if impl == "cuda_sm100" and T == 1:
             if out_kr is not None:
                 out = bdh_rope_attn_decode(Q, past_kr, past_v, self.freqs, rope_start, impl=impl,
@@ -115,11 +133,16 @@ class Attention(nn.Module):
             return tril_decode(QR, past_kr, past_v), QR, V
         # eager T=1 decode, or a multi-token block continuing a past
         cos, sin = rope_tables(self.freqs, T, rope_start, Q.device)
-        QR = eager_rope_rotate(Q, cos, sin, out=out_kr) if impl == "eager" else None
+        qr_out = None if fp8_slot else out_kr
+        QR = eager_rope_rotate(Q, cos, sin, out=qr_out) if impl == "eager" else None
         if QR is None:
             from kernels.sm100_attn import rope_rotate
 
-            QR = rope_rotate(Q, self.freqs, rope_start, out=out_kr)
+            QR = rope_rotate(Q, self.freqs, rope_start, out=qr_out)
+        if fp8_slot:
+            from bdh_cache import _quantize_into
+
+            _quantize_into(QR, out_kr, out_kr_scale)
         if past_is_raw and past_kr.dtype != QR.dtype:
             past_kr, past_v = past_kr.to(QR.dtype), past_v.to(QR.dtype)
         if T == 1:
@@ -250,7 +273,12 @@ class BDH(nn.Module):
         xs, qr = latent_encode(xb, enc, self.attn.freqs, rope_start, qr_out=qr_slot,
                                want_xs=not gate_x)
         if dst_kr is not None and qr_slot is None:
-            dst_kr.copy_(qr)
+            if dst_kr.dtype == torch.float8_e4m3fn:
+                from kernels.sm100_attn import quantize_rows_fp8
+
+                quantize_rows_fp8(qr, out=dst_kr, scale=cache.reserve_scale(level, T))
+            else:
+                dst_kr.copy_(qr)
         y_kv = tril_score_v(qr, qr, xb.unsqueeze(1))
         yn = layer_norm(y_kv, eps, out_dtype=torch.bfloat16)
         encv = self._bf16_param("encoder_v", kmaj)
@@ -302,7 +330,7 @@ class BDH(nn.Module):
                 y_mlp = F.linear(xy.reshape(B, T, nh * N), self.decoder.t())
                 x = self._ln(x + self._ln(y_mlp))
                 continue
-            past_kr = past_v = out_kr = None
+            past_kr = past_v = out_kr = past_scale = out_scale = None
             raw = False
             if cache is not None:
                 native = impl == "cuda_sm100" and not grad
@@ -313,6 +341,9 @@ class BDH(nn.Module):
                     if native:
                         past_kr, past_v = cache.get_past_raw(level)
                         raw = True
+                        if getattr(cache, "kr_fp8", False):
+                            past_scale = cache.get_past_scale(level)
+                            out_scale = cache.reserve_scale(level, T)
                     else:
                         past_kr, past_v = cache.get_past(level)
                     dst_v.copy_(v_tok)
@@ -322,7 +353,8 @@ class BDH(nn.Module):
                     past_kr, past_v = cache.get_past(level)
             y_kv, new_kr, new_v = self.attn(x_sparse, x_sparse, v_tok, rope_start=rope_start,
                                             past_kr=past_kr, past_v=past_v, out_kr=out_kr,
-                                            past_is_raw=raw, relu_input=fused)
+                                            past_is_raw=raw, relu_input=fused,
+                                            past_kr_scale=past_scale, out_kr_scale=out_scale)
             if cache is not None and out_kr is None:
                 cache.append(level, new_kr, new_v)
             y_kv = self._ln(y_kv)

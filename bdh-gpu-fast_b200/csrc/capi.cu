@@ -347,6 +347,76 @@ int bdh_latent_gate_x(const void* y, const int64_t y_strides[4], const void* enc
   return launch_latent_gate_x(a, static_cast<cudaStream_t>(stream), device_error_ptr());
 }
 
+int bdh_quantize_rows_fp8(const void* x, const int64_t x_strides[4], int x_dtype, int64_t B,
+                          int64_t H, int64_t T, int64_t N, void* out,
+                          const int64_t out_strides[4], float* scale,
+                          const int64_t scale_strides[3], void* stream) {
+  if (!dtype_ok(x_dtype)) return fail(BDH_ERR_INVALID, "quantize_rows_fp8: dtype must be f32 or bf16");
+  if (B < 0 || H < 0 || T < 0 || N < 0) return fail(BDH_ERR_INVALID, "quantize_rows_fp8: negative size");
+  if (N % 2 != 0) return fail(BDH_ERR_INVALID, "quantize_rows_fp8: N must be even");
+  if (x_strides[3] != 1 || out_strides[3] != 1)
+    return fail(BDH_ERR_INVALID, "quantize_rows_fp8: last dimension must be contiguous");
+  if (B * H * T * N == 0) return BDH_OK;
+  if (x == nullptr || out == nullptr || scale == nullptr)
+    return fail(BDH_ERR_INVALID, "quantize_rows_fp8: null pointer");
+  if (B * H * T >= (int64_t(1) << 31) || N > (int64_t(1) << 30))
+    return fail(BDH_ERR_INVALID, "quantize_rows_fp8: sizes beyond the supported range");
+  return launch_quantize_rows_fp8(x, x_dtype, x_strides, B, H, T, N, static_cast<uint8_t*>(out),
+                                  out_strides, scale, scale_strides,
+                                  static_cast<cudaStream_t>(stream));
+}
+
+int bdh_tril_decode_fp8(const void* q, const int64_t q_strides[4], int q_dtype,
+                        const void* k_past, const int64_t k_strides[4], const float* k_scale,
+                        const int64_t ks_strides[3], const void* v_past,
+                        const int64_t v_strides[4], int v_dtype, void* out,
+                        const int64_t out_strides[4], int64_t B, int64_t H, int64_t Hv,
+                        int64_t Tq, int64_t S, int64_t N, int64_t D, const float* freqs,
+                        int64_t pos, void* kr_slot, const int64_t slot_strides[4],
+                        float* slot_scale, const int64_t slot_scale_strides[3],
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (!dtype_ok(q_dtype) || !dtype_ok(v_dtype))
+    return fail(BDH_ERR_INVALID, "tril_decode_fp8: q and v dtypes must be f32 or bf16");
+  if (B < 0 || H < 0 || Tq < 0 || S < 0 || N < 0 || D < 0)
+    return fail(BDH_ERR_INVALID, "tril_decode_fp8: negative size");
+  if (Hv != 1 && Hv != H) return fail(BDH_ERR_INVALID, "tril_decode_fp8: v_past heads must equal q heads or 1");
+  if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || out_strides[3] != 1)
+    return fail(BDH_ERR_INVALID, "tril_decode_fp8: last dimension must be contiguous");
+  if (kr_slot != nullptr && (freqs == nullptr || slot_strides == nullptr || slot_strides[3] != 1 ||
+                             slot_scale == nullptr || slot_scale_strides == nullptr))
+    return fail(BDH_ERR_INVALID, "tril_decode_fp8: kr_slot needs freqs, contiguous slot rows and a slot scale");
+  if (S > 0 && (k_scale == nullptr || ks_strides == nullptr))
+    return fail(BDH_ERR_INVALID, "tril_decode_fp8: k_scale is required");
+  if (B * H * Tq == 0) return BDH_OK;
+  if (S > (int64_t(1) << 30) || N > 48 * 1024) return fail(BDH_ERR_INVALID, "tril_decode_fp8: sizes beyond the supported range");
+  if (freqs != nullptr && (N % 2) != 0) return fail(BDH_ERR_INVALID, "tril_decode_fp8: fused RoPE needs an even latent width");
+  const size_t need = decode_workspace_bytes(B, H, Tq, S, N, D);
+  if (workspace == nullptr || workspace_bytes < need) {
+    std::ostringstream os;
+    os << "tril_decode_fp8: workspace of " << need << " bytes required, got " << workspace_bytes;
+    return fail(BDH_ERR_WORKSPACE, os.str());
+  }
+  DecodeFp8Args a;
+  a.q = q; a.q_dtype = q_dtype; a.k = static_cast<const uint8_t*>(k_past); a.k_scale = k_scale;
+  a.v = v_past; a.v_dtype = v_dtype; a.out = out;
+  std::memcpy(a.q_strides, q_strides, sizeof(a.q_strides));
+  std::memcpy(a.k_strides, k_strides, sizeof(a.k_strides));
+  if (ks_strides != nullptr) std::memcpy(a.ks_strides, ks_strides, sizeof(a.ks_strides));
+  std::memcpy(a.v_strides, v_strides, sizeof(a.v_strides));
+  std::memcpy(a.out_strides, out_strides, sizeof(a.out_strides));
+  a.B = B; a.H = H; a.Hv = Hv; a.Tq = Tq; a.S = S; a.N = N; a.D = D;
+  a.freqs = freqs; a.pos = pos;
+  a.slot = static_cast<uint8_t*>(kr_slot);
+  if (slot_strides != nullptr) std::memcpy(a.slot_strides, slot_strides, sizeof(a.slot_strides));
+  a.slot_scale = slot_scale;
+  if (slot_scale_strides != nullptr)
+    std::memcpy(a.slot_scale_strides, slot_scale_strides, sizeof(a.slot_scale_strides));
+  float* partial = static_cast<float*>(workspace);
+  float* qrot = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                         decode_partial_bytes(B, H, Tq, S, N, D));
+  return launch_decode_fp8(a, partial, qrot, static_cast<cudaStream_t>(stream));
+}
+
 int bdh_layernorm(const void* x, int x_dtype, int64_t x_row_stride, void* y, int y_dtype,
                   int64_t y_row_stride, int64_t rows, int64_t D, float eps, void* stream) {
   if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype))

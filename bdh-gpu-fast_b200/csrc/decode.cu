@@ -188,6 +188,122 @@ __global__ void __launch_bounds__(kDecThreads) decode_partial_kernel(
   (void)nsplit;
 }
 
+// ---------------------------------------------------------------- fp8 key history
+// The e4m3 byte in bits 24-31 of `t` (lower bits arbitrary) to
+// fp32, scaled by 2^-120, with integer operations only: shifting right arithmetically by 4
+// puts s eeee mmm at bits 27-20 with the sign copied into bits 31-28, and the mask keeps the
+// sign bit and the seven exponent/mantissa bits. An e4m3 value 2^(e-7) (1 + m/8) becomes the
+// fp32 value 2^(e-127) (1 + m/8), and a subnormal 2^-6 (m/8) the fp32 denormal 2^-126 (m/8):
+// both exactly 2^-120 times the e4m3 value. (The conversion instructions run on a narrow pipe
+// that capped the fp8 stream at about half the HBM rate.)
+__device__ __forceinline__ float e4m3_top_to_f32_2m120(uint32_t t) {
+  return __int_as_float((static_cast<int32_t>(t) >> 4) & static_cast<int32_t>(0x87F00000u));
+}
+constexpr float kE4m3QScale = 18446744073709551616.0f;  // 2^64, folded into the staged query
+constexpr float kE4m3RowScale = 72057594037927936.0f;   // 2^56 = 2^120 / 2^64, into each score
+
+// Dot products of q (shared, fp32, pre-multiplied by 2^64) with two e4m3 key rows (unscaled,
+// each value read as 2^-120 times itself); VEC = 16-byte loads.
+template <bool VEC>
+__device__ __forceinline__ void dot2_fp8(const float* __restrict__ qs, const uint8_t* __restrict__ k0,
+                                         const uint8_t* __restrict__ k1, int N, bool has1,
+                                         float& d0, float& d1) {
+  const int lane = threadIdx.x & 31;
+  float a0 = 0.f, a1 = 0.f;
+  if (VEC) {
+#pragma unroll 2
+    for (int n = lane * 16; n < N; n += 32 * 16) {
+      const uint4 u0 = __ldcs(reinterpret_cast<const uint4*>(k0 + n));
+      uint4 u1 = make_uint4(0, 0, 0, 0);
+      if (has1) u1 = __ldcs(reinterpret_cast<const uint4*>(k1 + n));
+      const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w};
+      const uint32_t w1[4] = {u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 qv = *reinterpret_cast<const float4*>(qs + n + 4 * i);
+        a0 = fmaf(qv.x, e4m3_top_to_f32_2m120(w0[i] << 24), a0);
+        a0 = fmaf(qv.y, e4m3_top_to_f32_2m120(w0[i] << 16), a0);
+        a0 = fmaf(qv.z, e4m3_top_to_f32_2m120(w0[i] << 8), a0);
+        a0 = fmaf(qv.w, e4m3_top_to_f32_2m120(w0[i]), a0);
+        a1 = fmaf(qv.x, e4m3_top_to_f32_2m120(w1[i] << 24), a1);
+        a1 = fmaf(qv.y, e4m3_top_to_f32_2m120(w1[i] << 16), a1);
+        a1 = fmaf(qv.z, e4m3_top_to_f32_2m120(w1[i] << 8), a1);
+        a1 = fmaf(qv.w, e4m3_top_to_f32_2m120(w1[i]), a1);
+      }
+    }
+  } else {
+    for (int n = lane; n < N; n += 32) {
+      a0 = fmaf(qs[n], e4m3_top_to_f32_2m120(static_cast<uint32_t>(k0[n]) << 24), a0);
+      if (has1) a1 = fmaf(qs[n], e4m3_top_to_f32_2m120(static_cast<uint32_t>(k1[n]) << 24), a1);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+    a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+  }
+  d0 = a0;
+  d1 = a1;
+}
+
+// Same split-S structure as decode_partial_kernel; the score of cached row j is
+// scale_j * (q . e4m3_j).
+template <typename TQ, typename TV, bool VEC>
+__global__ void __launch_bounds__(kDecThreads) decode_partial_fp8_kernel(
+    const TQ* __restrict__ q, const uint8_t* __restrict__ kp, const float* __restrict__ ksc,
+    const TV* __restrict__ vp, float* __restrict__ partial, int H, int Hv, int Tq, int S, int N,
+    int D, int64_t qsb, int64_t qsh, int64_t qst, int64_t ksb, int64_t ksh, int64_t kst,
+    int64_t csb, int64_t csh, int64_t cst, int64_t vsb, int64_t vsh, int64_t vst, int kDecRows) {
+  extern __shared__ float dsm[];
+  float* qs = dsm;
+  float* sc = dsm + N;
+  const int split = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int tq = blockIdx.z;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int hv = Hv == 1 ? 0 : h;
+  const TQ* qr = q + b * qsb + h * qsh + tq * qst;
+  // q * 2^64 (exact): with keys read as 2^-120 times their value, products of ordinary
+  // magnitudes stay normal fp32 numbers
+  if (sizeof(TQ) == 4 && (N & 3) == 0 && (reinterpret_cast<uintptr_t>(qr) & 15u) == 0) {
+    const float4* q4 = reinterpret_cast<const float4*>(qr);
+    float4* s4 = reinterpret_cast<float4*>(qs);
+#pragma unroll 8
+    for (int n = threadIdx.x; n < (N >> 2); n += kDecThreads) {
+      float4 t = __ldg(q4 + n);
+      t.x *= kE4m3QScale; t.y *= kE4m3QScale; t.z *= kE4m3QScale; t.w *= kE4m3QScale;
+      s4[n] = t;
+    }
+  } else {
+    for (int n = threadIdx.x; n < N; n += blockDim.x) qs[n] = ld_elem(qr, n) * kE4m3QScale;
+  }
+  __syncthreads();
+  const int j0 = split * kDecRows;
+  const int rows = max(0, min(kDecRows, S - j0));
+  const int warp = threadIdx.x >> 5;
+  const uint8_t* kbase = kp + b * ksb + h * ksh;
+  const float* cbase = ksc + b * csb + h * csh;
+  for (int r = warp * 2; r < rows; r += kDecWarps * 2) {
+    const bool has1 = r + 1 < rows;
+    float d0, d1;
+    dot2_fp8<VEC>(qs, kbase + (j0 + r) * kst, kbase + (j0 + r + (has1 ? 1 : 0)) * kst, N, has1,
+                  d0, d1);
+    if ((threadIdx.x & 31) == 0) {
+      sc[r] = (d0 * kE4m3RowScale) * cbase[(j0 + r) * cst];
+      if (has1) sc[r + 1] = (d1 * kE4m3RowScale) * cbase[(j0 + r + 1) * cst];
+    }
+  }
+  __syncthreads();
+  const TV* vbase = vp + b * vsb + hv * vsh;
+  float* dst = partial + ((static_cast<int64_t>(split) * gridDim.y + bh) * Tq + tq) * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll 8
+    for (int r = 0; r < rows; ++r) acc = fmaf(sc[r], ld_elem(vbase + (j0 + r) * vst, d), acc);
+    dst[d] = acc;
+  }
+}
+
 template <typename TO>
 __global__ void decode_reduce_kernel(const float* __restrict__ partial, TO* __restrict__ out,
                                      int nsplit, int H, int Tq, int D, int64_t BHT, int64_t osb,
@@ -350,6 +466,89 @@ int launch_decode(const DecodeArgs& a_in, float* partial, float* qrot, int64_t m
   else
     decode_reduce_kernel<uint16_t><<<static_cast<unsigned>(bht), threads, 0, stream>>>(
         partial, static_cast<uint16_t*>(a.out), nsplit, Hi, Tqi, Di, bht, a.out_strides[0],
+        a.out_strides[1], a.out_strides[2]);
+  prof_stop(kProfDecode, stream);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("decode_reduce_kernel launch: ") + cudaGetErrorString(e));
+    return BDH_ERR_CUDA;
+  }
+  return BDH_OK;
+}
+
+int launch_decode_fp8(const DecodeFp8Args& a_in, float* partial, float* qrot, cudaStream_t stream) {
+  if (a_in.B * a_in.H * a_in.Tq == 0 || a_in.D == 0) return BDH_OK;
+  DecodeFp8Args a = a_in;
+  const bool out_f32 = a_in.q_dtype == BDH_DTYPE_F32;
+  if (a.freqs != nullptr) {
+    // the new queries rotated once (fp32), then quantized into this step's cache slot
+    const int64_t qs[4] = {a.H * a.Tq * a.N, a.Tq * a.N, a.N, 1};
+    int rc = launch_rope(a.q, a.q_dtype, a.q_strides, qrot, BDH_DTYPE_F32, qs, nullptr, a.freqs,
+                         a.B, a.H, a.Tq, a.N, a.pos, 0, stream);
+    if (rc) return rc;
+    if (a.slot != nullptr) {
+      rc = launch_quantize_rows_fp8(qrot, BDH_DTYPE_F32, qs, a.B, a.H, a.Tq, a.N, a.slot,
+                                    a.slot_strides, a.slot_scale, a.slot_scale_strides, stream);
+      if (rc) return rc;
+    }
+    a.q = qrot;
+    a.q_dtype = BDH_DTYPE_F32;
+    for (int i = 0; i < 4; ++i) a.q_strides[i] = qs[i];
+  }
+  const DecodePlan pl = plan_decode(a.B, a.H, a.Tq, a.S, a.N, 0);
+  const bool vec = (a.N % 16) == 0 && (reinterpret_cast<uintptr_t>(a.k) & 15u) == 0 &&
+                   a.k_strides[0] % 16 == 0 && a.k_strides[1] % 16 == 0 && a.k_strides[2] % 16 == 0;
+  const dim3 grid(static_cast<unsigned>(pl.splits), static_cast<unsigned>(a.B * a.H),
+                  static_cast<unsigned>(a.Tq));
+  const size_t smem = (static_cast<size_t>(a.N) + kDecRowsMax) * sizeof(float);
+  if (smem > 200 * 1024) {
+    set_error("decode: latent width too large for the shared-memory q stage");
+    return BDH_ERR_INVALID;
+  }
+  const int Hi = static_cast<int>(a.H), Hvi = static_cast<int>(a.Hv), Tqi = static_cast<int>(a.Tq);
+  const int Si = static_cast<int>(a.S), Ni = static_cast<int>(a.N), Di = static_cast<int>(a.D);
+#define BDH_DEC8_LAUNCH(TQ, TV, V)                                                               \
+  do {                                                                                           \
+    auto kern = decode_partial_fp8_kernel<TQ, TV, V>;                                            \
+    if (smem > 48 * 1024)                                                                        \
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,                    \
+                           static_cast<int>(smem));                                              \
+    kern<<<grid, kDecThreads, smem, stream>>>(                                                   \
+        static_cast<const TQ*>(a.q), a.k, a.k_scale, static_cast<const TV*>(a.v), partial, Hi,   \
+        Hvi, Tqi, Si, Ni, Di, a.q_strides[0], a.q_strides[1], a.q_strides[2], a.k_strides[0],    \
+        a.k_strides[1], a.k_strides[2], a.ks_strides[0], a.ks_strides[1], a.ks_strides[2],       \
+        a.v_strides[0], a.v_strides[1], a.v_strides[2], pl.rows);                                \
+  } while (0)
+#define BDH_DEC8_V(TQ, TV) \
+  do {                      \
+    if (vec)                \
+      BDH_DEC8_LAUNCH(TQ, TV, true); \
+    else                    \
+      BDH_DEC8_LAUNCH(TQ, TV, false); \
+  } while (0)
+  const bool qf = a.q_dtype == BDH_DTYPE_F32, vf = a.v_dtype == BDH_DTYPE_F32;
+  prof_start(kProfDecode, stream);
+  if (qf && vf) BDH_DEC8_V(float, float);
+  else if (qf) BDH_DEC8_V(float, uint16_t);
+  else if (vf) BDH_DEC8_V(uint16_t, float);
+  else BDH_DEC8_V(uint16_t, uint16_t);
+#undef BDH_DEC8_V
+#undef BDH_DEC8_LAUNCH
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    prof_stop(kProfDecode, stream);
+    set_error(std::string("decode_partial_fp8_kernel launch: ") + cudaGetErrorString(e));
+    return BDH_ERR_CUDA;
+  }
+  const int64_t bht = a.B * a.H * a.Tq;
+  const int threads = static_cast<int>(std::min<int64_t>(256, std::max<int64_t>(32, a.D)));
+  if (out_f32)
+    decode_reduce_kernel<float><<<static_cast<unsigned>(bht), threads, 0, stream>>>(
+        partial, static_cast<float*>(a.out), pl.splits, Hi, Tqi, Di, bht, a.out_strides[0],
+        a.out_strides[1], a.out_strides[2]);
+  else
+    decode_reduce_kernel<uint16_t><<<static_cast<unsigned>(bht), threads, 0, stream>>>(
+        partial, static_cast<uint16_t*>(a.out), pl.splits, Hi, Tqi, Di, bht, a.out_strides[0],
         a.out_strides[1], a.out_strides[2]);
   prof_stop(kProfDecode, stream);
   e = cudaGetLastError();

@@ -175,6 +175,34 @@ struct DecodeArgs {
   void* slot = nullptr;
   int64_t slot_strides[4] = {0, 0, 0, 1};
 };
+// Decode against an fp8 key history (e4m3 rows with one fp32 scale each, kr_fp8.cu); values
+// in f32 or bf16. With freqs the new queries are rotated first and, with slot, quantized into
+// this step's cache slot (row + scale).
+struct DecodeFp8Args {
+  const void* q = nullptr;
+  int64_t q_strides[4] = {0, 0, 0, 1};
+  int q_dtype = BDH_DTYPE_F32;
+  const uint8_t* k = nullptr;
+  int64_t k_strides[4] = {0, 0, 0, 1};
+  const float* k_scale = nullptr;
+  int64_t ks_strides[3] = {0, 0, 1};
+  const void* v = nullptr;
+  int64_t v_strides[4] = {0, 0, 0, 1};
+  int v_dtype = BDH_DTYPE_F32;
+  void* out = nullptr;
+  int64_t out_strides[4] = {0, 0, 0, 1};
+  int64_t B = 0, H = 0, Hv = 0, Tq = 0, S = 0, N = 0, D = 0;
+  const float* freqs = nullptr;
+  int64_t pos = 0;
+  uint8_t* slot = nullptr;
+  int64_t slot_strides[4] = {0, 0, 0, 1};
+  float* slot_scale = nullptr;
+  int64_t slot_scale_strides[3] = {0, 0, 1};
+};
+int launch_decode_fp8(const DecodeFp8Args& a, float* partial, float* qrot, cudaStream_t stream);
+int launch_quantize_rows_fp8(const void* x, int x_dtype, const int64_t xs[4], int64_t B,
+                             int64_t H, int64_t T, int64_t N, uint8_t* out, const int64_t os[4],
+                             float* scale, const int64_t ss[3], cudaStream_t stream);
 struct DecodePlan {
   int splits = 1;  // CTAs per (b, h, tq)
   int rows = 1;    // cached rows per CTA (<= 128)

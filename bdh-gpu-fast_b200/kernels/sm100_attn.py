@@ -39,7 +39,8 @@ _F32 = 0
 _BF16 = 1
 
 _c_i64_4 = ctypes.c_int64 * 4
-ABI_VERSION = 3  # BDH_ABI_VERSION of include/bdh_sm100.h
+ABI_VERSION = 4  # BDH_ABI_VERSION of include/bdh_sm100.h
+FP8 = torch.float8_e4m3fn  # the opt-in fp8 key-cache storage dtype
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 
@@ -77,6 +78,11 @@ def _declare(lib: ctypes.CDLL) -> None:
                                     _i64, _i64, _i64, _i64, _i64, _vp]
     lib.bdh_latent_gate_x.argtypes = [_vp, P, _vp, _c_i64_3p, _vp, _c_i64_3p, _vp, _c_i64_3p,
                                       _vp, P, _i64, _i64, _i64, _i64, _i64, _vp]
+    lib.bdh_quantize_rows_fp8.argtypes = [_vp, P, ctypes.c_int, _i64, _i64, _i64, _i64, _vp, P,
+                                          _vp, P, _vp]
+    lib.bdh_tril_decode_fp8.argtypes = [_vp, P, ctypes.c_int, _vp, P, _vp, P, _vp, P, ctypes.c_int,
+                                        _vp, P, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
+                                        _i64, _vp, P, _vp, P, _vp, ctypes.c_size_t, _vp]
     lib.bdh_layernorm.argtypes = [_vp, ctypes.c_int, _i64, _vp, ctypes.c_int, _i64, _i64, _i64,
                                   ctypes.c_float, _vp]
     lib.bdh_residual_layernorm.argtypes = [_vp, _i64, _vp, ctypes.c_int, _i64, _vp, _i64, _vp,
@@ -88,7 +94,7 @@ def _declare(lib: ctypes.CDLL) -> None:
                                      ctypes.c_size_t, _vp]
     for name in ("bdh_rope_rotate", "bdh_tril_score_v", "bdh_tril_decode", "bdh_tril_score_v_bwd",
                  "bdh_relu_mul", "bdh_latent_encode", "bdh_latent_gate", "bdh_latent_gate_x",
-                 "bdh_layernorm",
+                 "bdh_layernorm", "bdh_quantize_rows_fp8", "bdh_tril_decode_fp8",
                  "bdh_residual_layernorm", "bdh_state_decode"):
         getattr(lib, name).restype = ctypes.c_int
 
@@ -638,6 +644,91 @@ def tril_decode(q: torch.Tensor, k_past: torch.Tensor, v_past: torch.Tensor, *,
             _strides(v_past), kd, out.data_ptr(), _strides(out), B, H, v_past.size(1), Tq, S, N, D,
             fptr, int(pos), slot_ptr, slot_strides, ws.data_ptr(), int(wsz), _stream(dev))
     _check(rc, "tril_decode")
+    return out
+
+
+def _strides3(t: torch.Tensor):
+    return (ctypes.c_int64 * 3)(*t.stride())
+
+
+def quantize_rows_fp8(x: torch.Tensor, *, out: Optional[torch.Tensor] = None,
+                      scale: Optional[torch.Tensor] = None):
+    """Row-scaled e4m3 of ``x`` (B,H,T,N) f32 / bf16: ``out`` (B,H,T,N) float8_e4m3fn with
+    x ~= out * scale[..., None], ``scale`` (B,H,T) fp32 = max|row| / 448. Either may be a
+    strided view (a cache slot). Returns ``(out, scale)``."""
+    if x.dim() != 4:
+        raise ValueError("quantize_rows_fp8 expects x (B,H,T,N)")
+    dev = _require_cuda(x)
+    lib = _require_lib()
+    B, H, T, N = x.shape
+    if out is None:
+        out = torch.empty(B, H, T, N, dtype=FP8, device=dev)
+    if scale is None:
+        scale = torch.empty(B, H, T, dtype=torch.float32, device=dev)
+    if out.dtype != FP8 or tuple(out.shape) != (B, H, T, N) or out.stride(-1) != 1:
+        raise ValueError("quantize_rows_fp8: out must be float8_e4m3fn (B,H,T,N) with unit last stride")
+    if scale.dtype != torch.float32 or tuple(scale.shape) != (B, H, T):
+        raise ValueError("quantize_rows_fp8: scale must be float32 (B,H,T)")
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    with torch.cuda.device(dev):
+        rc = lib.bdh_quantize_rows_fp8(x.data_ptr(), _strides(x), _code(x.dtype), B, H, T, N,
+                                       out.data_ptr(), _strides(out), scale.data_ptr(),
+                                       _strides3(scale), _stream(dev))
+    _check(rc, "quantize_rows_fp8")
+    return out, scale
+
+
+def tril_decode_fp8(q: torch.Tensor, k_past: torch.Tensor, k_scale: torch.Tensor,
+                    v_past: torch.Tensor, *, freqs: Optional[torch.Tensor] = None, pos: int = 0,
+                    kr_slot: Optional[torch.Tensor] = None,
+                    slot_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``tril_decode`` against an fp8 key history: ``k_past`` (B,H,S,N) float8_e4m3fn rows
+    with ``k_scale`` (B,H,S) fp32, ``v_past`` f32 / bf16 (capacity-strided views read in place).
+    With ``freqs`` the query is rotated first; with ``kr_slot`` / ``slot_scale`` the rotated
+    rows are quantized into this step's cache slot."""
+    B, H, Tq, S, D = _check_decode_shapes(q, k_past, v_past)
+    dev = _require_cuda(q, k_past, v_past, k_scale)
+    lib = _require_lib()
+    if k_past.dtype != FP8:
+        raise TypeError("tril_decode_fp8: k_past must be float8_e4m3fn")
+    if k_scale.dtype != torch.float32 or tuple(k_scale.shape) != (B, H, S):
+        raise ValueError("tril_decode_fp8: k_scale must be float32 (B,H,S)")
+    out = torch.empty(B, H, Tq, D, dtype=q.dtype, device=dev)
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if k_past.stride(-1) != 1 or v_past.stride(-1) != 1:
+        raise ValueError("cache views must have a contiguous last dimension")
+    N = q.size(-1)
+    fptr = None
+    if freqs is not None:
+        f = freqs.reshape(-1)
+        if f.dtype != torch.float32 or f.numel() != N:
+            raise ValueError("freqs must be float32 with one entry per latent dimension")
+        f = f.contiguous()
+        fptr = f.data_ptr()
+    slot_ptr = slot_st = sc_ptr = sc_st = None
+    if kr_slot is not None:
+        if freqs is None or slot_scale is None:
+            raise ValueError("kr_slot requires freqs and slot_scale")
+        if kr_slot.shape != q.shape or kr_slot.dtype != FP8 or kr_slot.stride(-1) != 1:
+            raise ValueError("kr_slot must be float8_e4m3fn with q's shape and unit last stride")
+        if slot_scale.dtype != torch.float32 or tuple(slot_scale.shape) != (B, H, Tq):
+            raise ValueError("slot_scale must be float32 (B,H,Tq)")
+        slot_ptr, slot_st = kr_slot.data_ptr(), _strides(kr_slot)
+        sc_ptr, sc_st = slot_scale.data_ptr(), _strides3(slot_scale)
+    if out.numel() == 0:
+        return out
+    wsz = lib.bdh_tril_decode_workspace_size(B, H, Tq, S, N, D)
+    ws = torch.empty(max(int(wsz), 4), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.bdh_tril_decode_fp8(
+            q.data_ptr(), _strides(q), _code(q.dtype), k_past.data_ptr(), _strides(k_past),
+            k_scale.data_ptr(), _strides3(k_scale), v_past.data_ptr(), _strides(v_past),
+            _code(v_past.dtype), out.data_ptr(), _strides(out), B, H, v_past.size(1), Tq, S, N, D,
+            fptr, int(pos), slot_ptr, slot_st, sc_ptr, sc_st, ws.data_ptr(), int(wsz),
+            _stream(dev))
+    _check(rc, "tril_decode_fp8")
     return out
 
 

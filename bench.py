@@ -756,7 +756,8 @@ def bench_decode(args, world, rank, dev):
     steps_total = args.warmup + args.steps
     g = torch.Generator().manual_seed(rank_seed(2004, rank))
     toks = torch.randint(0, VOCAB, (B, P + steps_total), generator=g).to(dev)
-    storage = torch.bfloat16 if args.decode_bf16 else None
+    storage = (torch.float8_e4m3fn if args.decode_fp8 else
+               torch.bfloat16 if args.decode_bf16 else None)
     kind = "state" if args.decode_state else "kv"
     cache = CacheManager.from_config(cfg, B, P + steps_total, dev, storage_dtype=storage,
                                      storage_kind=kind)
@@ -780,9 +781,12 @@ def bench_decode(args, world, rank, dev):
         ms = timed(step, args.steps, world, dev)
         prof = profile_end()
         clk = clocks.stop()
-    esz = 2 if storage is not None else 4
     S_mean = S0 + (args.steps - 1) / 2
-    bytes_step = N_LAYER * (B * N_HEAD * S_mean * N_LAT * esz + B * S_mean * D_MODEL * esz)
+    if storage == torch.float8_e4m3fn:  # e4m3 keys + one fp32 scale per row, bf16 values
+        bytes_step = N_LAYER * (B * N_HEAD * S_mean * (N_LAT + 4) + B * S_mean * D_MODEL * 2)
+    else:
+        esz = 2 if storage is not None else 4
+        bytes_step = N_LAYER * (B * N_HEAD * S_mean * N_LAT * esz + B * S_mean * D_MODEL * esz)
     if kind == "state":
         # fp32 state read + written once per step for every row whose rotated query is nonzero;
         # counted at full density (an upper bound on the bytes moved, so GB/s is a lower bound)
@@ -796,10 +800,13 @@ def bench_decode(args, world, rank, dev):
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16" if storage is not None else "f32",
-        "cache_dtype": "bf16" if storage is not None else "f32", "cache_kind": kind,
+        "cache_dtype": ("fp8 e4m3 keys (row scales) + bf16 values" if storage == torch.float8_e4m3fn
+                        else "bf16" if storage is not None else "f32"), "cache_kind": kind,
         "data": "synthetic", "config": {"workload": "config 4 decode", "B": B, "prompt": P,
                                         "S_mean": S_mean},
         "roofline": {"kernel": ("state decode (state_decode_kernel + state_reduce_kernel)" if kind == "state"
+                                else "decode (decode_partial_fp8_kernel + decode_reduce_kernel)"
+                                if storage == torch.float8_e4m3fn
                                 else "decode (decode_partial_kernel + decode_reduce_kernel)"),
                      "bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      # state mode skips the rows of zero rotated query, so the dense-equivalent
@@ -809,8 +816,10 @@ def bench_decode(args, world, rank, dev):
                                        if kind == "state" else "history read once"),
                      "peak_source": f"{src} hbm_gbs",
                      "bytes_per_launch": bytes_step / N_LAYER,
-                     "traffic": None if kind == "state" else decode_traffic("decode_config4_bf16" if storage is not None
-                                               else "decode_config4", B, S_mean)},
+                     "traffic": None if kind == "state" else decode_traffic(
+                         "decode_config4_fp8" if storage == torch.float8_e4m3fn
+                         else "decode_config4_bf16" if storage is not None
+                         else "decode_config4", B, S_mean)},
         "kernel_ms": {k: v_["ms"] / args.steps for k, v_ in prof.items() if v_["launches"]},
         "gpu_launches": sum(v_["launches"] for v_ in prof.values()),
         "clocks": clk,
@@ -849,6 +858,8 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode-bf16", action="store_true")
+    ap.add_argument("--decode-fp8", action="store_true",
+                    help="config 4: e4m3 key cache with row scales, bf16 values (lossy, opt-in)")
     ap.add_argument("--decode-state", action="store_true",
                     help="config 4 with the N x D recurrent-state cache instead of the history")
     ap.add_argument("--batch", type=int, default=0,

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define BDH_ABI_VERSION 3
+#define BDH_ABI_VERSION 4
 
 #define BDH_DTYPE_F32 0
 #define BDH_DTYPE_BF16 1
@@ -242,6 +242,37 @@ int bdh_latent_gate_x(const void* y, const int64_t y_strides[4], const void* enc
                       const void* enc, const int64_t enc_strides[3], void* xy,
                       const int64_t xy_strides[4], int64_t B, int64_t T, int64_t H, int64_t D,
                       int64_t N, void* stream);
+
+/*
+ * fp8 wire format of the cached rotated keys (opt-in cache storage; the reference keeps its
+ * cache in fp32 / fp16 / bf16, bdh_cache.py:62-80,240-243, so this has no reference entry and
+ * is lossy). Every row x[b,h,t,:] of N values becomes e4m3 bytes plus one fp32 scale:
+ *   amax = max |x|,  q8 = e4m3_rn_satfinite(x * (448 / amax)),  scale = amax / 448
+ * (all-zero rows: q8 = 0, scale = 0), so that x ~= q8 * scale.
+ *
+ * bdh_quantize_rows_fp8: x (B,H,T,N) f32 or bf16 (x_strides {b,h,t,n}, last 1) into out
+ * (B,H,T,N) bytes (out_strides, last 1) and scale (B,H,T) fp32 (scale_strides {b,h,t}). N even.
+ *
+ * bdh_tril_decode_fp8 is bdh_tril_decode (same shapes, workspace from
+ * bdh_tril_decode_workspace_size, same RoPE / slot semantics) against such a key history:
+ *   out[b,h,tq] = sum_j k_scale[b,h,j] (q[b,h,tq] . k8[b,h,j]) v_past[b,hv,j]
+ * k_past (B,H,S,N) bytes with k_strides, k_scale (B,H,S) fp32 with ks_strides; v_past f32 or
+ * bf16 (v_dtype). With kr_slot, the rotated queries are quantized into the slot's bytes and
+ * slot_scale (B,H,Tq) with slot_scale_strides.
+ */
+int bdh_quantize_rows_fp8(const void* x, const int64_t x_strides[4], int x_dtype, int64_t B,
+                          int64_t H, int64_t T, int64_t N, void* out,
+                          const int64_t out_strides[4], float* scale,
+                          const int64_t scale_strides[3], void* stream);
+int bdh_tril_decode_fp8(const void* q, const int64_t q_strides[4], int q_dtype,
+                        const void* k_past, const int64_t k_strides[4], const float* k_scale,
+                        const int64_t ks_strides[3], const void* v_past,
+                        const int64_t v_strides[4], int v_dtype, void* out,
+                        const int64_t out_strides[4], int64_t B, int64_t H, int64_t Hv,
+                        int64_t Tq, int64_t S, int64_t N, int64_t D, const float* freqs,
+                        int64_t pos, void* kr_slot, const int64_t slot_strides[4],
+                        float* slot_scale, const int64_t slot_scale_strides[3],
+                        void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Affine-free LayerNorm over the last dimension, as the BDH layer applies it with F.layer_norm

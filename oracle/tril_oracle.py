@@ -16,6 +16,10 @@ citing the reference lines it follows:
 * ``tril_backward``    kernels/attention_bwd.py:45-83 (+ the K-is-Q sum of :284-291)
 * ``rope_backward``    kernels/rope.py:540-557 (analytic adjoint of the rotation)
 * ``bdh_forward``      bdh_baseline.py:96-139 (eval mode, dropout 0)
+* ``quantize_rows_fp8`` / ``tril_decode_fp8``  the opt-in fp8 key-cache wire format (no
+                        reference counterpart: the reference caches fp32 / fp16 / bf16,
+                        bdh_cache.py:62-80,240-243); the decode over it is ``tril_decode`` on the
+                        dequantized keys
 
 Parity pinning: tests/golden/*.npz hold outputs of the reference itself (generated in the
 build container by tests/golden/make_golden.py from the reference sources); the tests check
@@ -135,6 +139,40 @@ def tril_decode(q: np.ndarray, k_past: np.ndarray, v_past: np.ndarray, acc=np.fl
     if k_past.shape[2] == 0:
         return np.zeros((B, H, Tq, D), dtype=acc)
     return (q @ np.swapaxes(k_past, -1, -2)) @ v_past
+
+
+# ------------------------------------------------------------------ fp8 key cache
+def e4m3_rne(y: np.ndarray) -> np.ndarray:
+    """float32 values rounded to the nearest finite e4m3 value (1 sign, 4 exponent bits with
+    bias 7, 3 mantissa bits; smallest normal 2^-6, subnormal step 2^-9, largest 448), ties to
+    even, saturating at +-448. Returns the rounded values as float32."""
+    y = np.asarray(y, dtype=np.float32).astype(np.float64)
+    a = np.abs(y)
+    _, ex = np.frexp(np.maximum(a, 2.0 ** -6))  # a = m 2^ex, m in [0.5, 1): binade 2^(ex-1)
+    quantum = np.ldexp(1.0, ex - 1 - 3)         # 3 mantissa bits (the subnormal step below 2^-6)
+    r = np.round(a / quantum) * quantum          # exact division by a power of two; half to even
+    r = np.minimum(r, 448.0)
+    return np.copysign(r, y).astype(np.float32)
+
+
+def quantize_rows_fp8(x: np.ndarray):
+    """Row-scaled e4m3 of the last axis: amax = max |x|, inv = 448 / amax (0 for an all-zero
+    row), q = e4m3(x * inv) (products in float32), scale = amax / 448 (float32).
+    Returns (q as float32 e4m3 values, scale) with x ~= q * scale[..., None]."""
+    x = np.asarray(x, dtype=np.float32)
+    amax = np.max(np.abs(x), axis=-1)
+    with np.errstate(divide="ignore"):
+        inv = np.where(amax > 0, np.float32(448.0) / amax, np.float32(0.0)).astype(np.float32)
+    q = e4m3_rne((x * inv[..., None]).astype(np.float32))
+    scale = (amax / np.float32(448.0)).astype(np.float32)
+    return q, scale
+
+
+def tril_decode_fp8(q: np.ndarray, k8: np.ndarray, k_scale: np.ndarray, v_past: np.ndarray,
+                    acc=np.float64) -> np.ndarray:
+    """``tril_decode`` against the dequantized fp8 key history k8 * k_scale."""
+    k = np.asarray(k8, dtype=acc) * np.asarray(k_scale, dtype=acc)[..., None]
+    return tril_decode(q, k, v_past, acc=acc)
 
 
 def state_from_history(k_past: np.ndarray, v_past: np.ndarray, acc=np.float64) -> np.ndarray:
