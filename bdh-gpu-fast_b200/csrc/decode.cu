@@ -211,7 +211,7 @@ __device__ __forceinline__ void dot2_fp8(const float* __restrict__ qs, const uin
   const int lane = threadIdx.x & 31;
   float a0 = 0.f, a1 = 0.f;
   if (VEC) {
-#pragma unroll 2
+#pragma unroll 4
     for (int n = lane * 16; n < N; n += 32 * 16) {
       const uint4 u0 = __ldcs(reinterpret_cast<const uint4*>(k0 + n));
       uint4 u1 = make_uint4(0, 0, 0, 0);
