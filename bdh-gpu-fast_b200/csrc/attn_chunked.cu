@@ -2,9 +2,12 @@
 //
 //   out[c-th chunk rows] = tril(Q_c K_c^T, -1) V_c  +  Q_c S_{c-1},   S_c = sum_{c' <= c} K_c'^T V_c'
 //
-// with chunks of C = 256 keys. Work per (b,h) unit drops from T(T-1)(N+D) to about
-// T(C-1)(N+D) + 4 T N D flops (for T = 8192: 86 instead of 553 GFLOP), at the cost of streaming
-// the N x D prefix states through HBM once written, once read.
+// with chunks of C keys. Work per (b,h) unit drops from T(T-1)(N+D) to about
+// T(C-1)(N+D) + 4 T N D flops (for T = 8192, C = 256: 86 instead of 553 GFLOP), at the cost of
+// streaming the N x D prefix states (bf16 hi/lo, 4 bytes per element) through HBM once written,
+// once read. C is 256 below T = 4096 and 512 from there on (chunk_len): the longer chunk doubles
+// the intra-chunk score work but halves the prefix-state traffic, which bounds the state and
+// value passes at long T (BDH_SM100_CHUNK=256|512 forces one).
 //
 // Three persistent tcgen05 passes (tc_engine.cuh):
 //   1. score pass restricted to each 128-row block's own chunk (score_pass.cuh, chunk > 0),
@@ -18,6 +21,7 @@
 // The reference computes this path quadratically (kernels/attention.py:27-40, 676-777;
 // csrc/tril_attn_cuda.cu:129-249); the chunked form is the north-star formulation.
 #include <algorithm>
+#include <cstdlib>
 
 #include "bdh_sm100.h"
 #include "internal.h"
@@ -30,7 +34,14 @@ namespace bdh {
 
 namespace {
 
-constexpr int kChunk = 256;
+int forced_chunk() {
+  static int c = [] {
+    const char* e = std::getenv("BDH_SM100_CHUNK");
+    const int v = e ? std::atoi(e) : 0;
+    return (v == 256 || v == 512) ? v : 0;
+  }();
+  return c;
+}
 
 // ------------------------------------------------------------------- state pass ----
 // Each tile is a 128 (latent) x 128 (value) block of the N x D state; its epilogue emits one
@@ -38,9 +49,9 @@ constexpr int kChunk = 256;
 // Every epilogue warp stages its 32 rows in shared memory in the 128B-swizzled layout of the
 // store tensor map and writes them with four TMA bulk stores (whole 128-byte lines), then
 // reuses the staging once the previous chunk's stores have read it.
-template <int STAGES>
+template <int STAGES, int CKB>  // CKB = k-blocks (64 keys) per chunk
 struct StateProb {
-  using S = TcShape<2, 128, true, true, 1, 1, STAGES, kChunk / 64>;
+  using S = TcShape<2, 128, true, true, 1, 1, STAGES, CKB>;
   static constexpr int kEmitEveryChunk = 1;
   static constexpr int kWarpStage = 4 * 32 * 128;  // hi/lo x two 64-column boxes x 32 rows
   static constexpr int kEpiSmemBytes = 4 * kWarpStage;
@@ -66,7 +77,7 @@ struct StateProb {
     return tl;
   }
   // the last chunk's total is never needed
-  __device__ static int k_blocks(const Params& p, const Tile&) { return (p.nchunks - 1) * (kChunk / 64); }
+  __device__ static int k_blocks(const Params& p, const Tile&) { return (p.nchunks - 1) * CKB; }
   __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x1u; }
   __device__ static void prefetch(const Params& p) {
     tma_prefetch_desc(&p.a_map[0]);
@@ -148,6 +159,7 @@ struct ChunkValueProb {
     CUtensorMap s_map[2];  // S hi/lo over [units][nchunks][N][D], box 64 (d) x 64 (n)
     int H, Hv, T, N, D;
     int mt, nd, units, nchunks;
+    int chunk;             // keys per chunk (256 or 512)
     void* out;             // (B,H,T,D) strided
     int64_t os_b, os_h, os_t;
     int out_f32, vec_ok;
@@ -165,12 +177,14 @@ struct ChunkValueProb {
     tl.ni = r - tl.mi * p.nd;
     return tl;
   }
-  __device__ static int cs(const Tile& tl) { return (tl.mi * 128 / kChunk) * kChunk; }
+  __device__ static int cs(const Params& p, const Tile& tl) {
+    return (tl.mi * 128 / p.chunk) * p.chunk;
+  }
   __device__ static int n_intra(const Params& p, const Tile& tl) {
-    return ceil_div_d(min(p.T, (tl.mi + 1) * 128) - cs(tl), 64);
+    return ceil_div_d(min(p.T, (tl.mi + 1) * 128) - cs(p, tl), 64);
   }
   __device__ static int n_inter(const Params& p, const Tile& tl) {
-    return cs(tl) > 0 ? ceil_div_d(p.N, 64) : 0;
+    return cs(p, tl) > 0 ? ceil_div_d(p.N, 64) : 0;
   }
   __device__ static int k_blocks(const Params& p, const Tile& tl) { return n_intra(p, tl) + n_inter(p, tl); }
   // intra: A0 A1 (P hi, lo) x B0 (V); inter: A0 (Q) x B0 B1 (S hi, lo)
@@ -198,10 +212,10 @@ struct ChunkValueProb {
         tma_load_4d(&p.p_map[i], bar, a_dst + i * S::A_TILE, kb * 64, tl.mi * 128, tl.unit, 0);
 #pragma unroll
       for (int c = 0; c < 2; ++c)
-        tma_load_4d(&p.v_map, bar, b_dst + c * 64 * 128, tl.ni * BN + c * 64, cs(tl) + kb * 64, hv, b);
+        tma_load_4d(&p.v_map, bar, b_dst + c * 64 * 128, tl.ni * BN + c * 64, cs(p, tl) + kb * 64, hv, b);
     } else {
       const int n0 = (kb - ni) * 64;
-      const int chunk = cs(tl) / kChunk;
+      const int chunk = cs(p, tl) / p.chunk;
       tma_load_4d(&p.q_map, bar, a_dst, n0, tl.mi * 128, h, b);
       for (int i = 0; i < 2; ++i)
 #pragma unroll
@@ -239,36 +253,38 @@ struct ChunkValueProb {
   }
 };
 
-// CTA-pair form of the chunk value pass: one 256-row pair tile is exactly one chunk (C = 256),
-// both row blocks at once (M = 256 across the pair), N = 256 value columns. Each CTA stages its
-// own 128 rows of P / Q and its own 128 columns of V / S, so the operand bytes per SM per flop
-// halve against the single-CTA form (whose inter-chunk Q S segment is bound by L2 -> shared
-// memory ingress). Needs P written over whole chunks (the pair score pass does: it stores every
-// key of the chunk, zero above the diagonal).
+// CTA-pair form of the chunk value pass: one 256-row pair tile (a whole chunk at C = 256, half
+// of one at C = 512), both row blocks at once (M = 256 across the pair), N = 256 value columns.
+// Each CTA stages its own 128 rows of P / Q and its own 128 columns of V / S, so the operand
+// bytes per SM per flop halve against the single-CTA form (whose inter-chunk Q S segment is
+// bound by L2 -> shared memory ingress). The intra segment of a pair tile covers the keys from
+// its chunk's start to the tile's last row; P holds zeros above the diagonal there (the pair
+// score pass stores whole 256-key tiles).
 struct ChunkValuePair {
   using Base = ChunkValueProb<3>;
   using Params = Base::Params;
   using S = PairShape<false, true, 2, 2, 3>;
   struct Tile {
-    int unit, c, n;
+    int unit, c, n;  // c: 256-row pair tile of the unit
   };
-  __device__ static int nchunk(const Params& p) { return ceil_div_d(p.T, kChunk); }
+  __device__ static int ntile(const Params& p) { return ceil_div_d(p.T, 256); }
   __device__ static int nd2(const Params& p) { return ceil_div_d(p.D, 256); }
-  __device__ static int num_tiles(const Params& p) { return p.units * nchunk(p) * nd2(p); }
+  __device__ static int num_tiles(const Params& p) { return p.units * ntile(p) * nd2(p); }
   __device__ static Tile tile(const Params& p, int t) {
     Tile tl;
-    const int per = nchunk(p) * nd2(p);
+    const int per = ntile(p) * nd2(p);
     tl.unit = t / per;
     const int r = t - tl.unit * per;
     tl.c = r / nd2(p);
     tl.n = r - tl.c * nd2(p);
     return tl;
   }
+  __device__ static int chunk(const Params& p, const Tile& tl) { return tl.c * 256 / p.chunk; }
   __device__ static int n_intra(const Params& p, const Tile& tl) {
-    return ceil_div_d(min(p.T, (tl.c + 1) * kChunk) - tl.c * kChunk, 64);
+    return ceil_div_d(min(p.T, (tl.c + 1) * 256) - chunk(p, tl) * p.chunk, 64);
   }
   __device__ static int n_inter(const Params& p, const Tile& tl) {
-    return tl.c > 0 ? ceil_div_d(p.N, 64) : 0;
+    return chunk(p, tl) > 0 ? ceil_div_d(p.N, 64) : 0;
   }
   __device__ static int k_blocks(const Params& p, const Tile& tl) { return n_intra(p, tl) + n_inter(p, tl); }
   __device__ static uint32_t pair_mask(const Params& p, const Tile& tl, int kb) {
@@ -282,8 +298,9 @@ struct ChunkValuePair {
                                     uint32_t bar, uint8_t* a_dst, uint8_t* b_dst) {
     const int b = tl.unit / p.H, h = tl.unit - (tl.unit / p.H) * p.H;
     const int r128 = static_cast<int>(rank) * 128;
-    const int row0 = tl.c * kChunk + r128;  // this CTA's 128 rows
-    const int col0 = tl.n * 256 + r128;     // this CTA's 128 value columns
+    const int row0 = tl.c * 256 + r128;  // this CTA's 128 rows
+    const int col0 = tl.n * 256 + r128;  // this CTA's 128 value columns
+    const int ch = chunk(p, tl);
     const int ni = n_intra(p, tl);
     if (kb < ni) {
       const int hv = p.Hv == 1 ? 0 : h;
@@ -291,7 +308,7 @@ struct ChunkValuePair {
         tma_load_4d_pair(&p.p_map[i], bar, a_dst + i * S::A_TILE, kb * 64, row0, tl.unit, 0);
 #pragma unroll
       for (int c = 0; c < 2; ++c)
-        tma_load_4d_pair(&p.v_map, bar, b_dst + c * 64 * 128, col0 + c * 64, tl.c * kChunk + kb * 64,
+        tma_load_4d_pair(&p.v_map, bar, b_dst + c * 64 * 128, col0 + c * 64, ch * p.chunk + kb * 64,
                          hv, b);
     } else {
       const int n0 = (kb - ni) * 64;
@@ -300,7 +317,7 @@ struct ChunkValuePair {
 #pragma unroll
         for (int c = 0; c < 2; ++c)
           tma_load_4d_pair(&p.s_map[i], bar, b_dst + i * S::B_TILE + c * 64 * 128, col0 + c * 64, n0,
-                           tl.c, tl.unit);
+                           ch, tl.unit);
     }
   }
   __device__ static void epilogue(const Params& p, const Tile& tl, int rank, int row, int c0,
@@ -321,20 +338,55 @@ bool use_pairs_chunked() {
   return on != 0;
 }
 
-using StateBf16 = StateProb<4>;
+using StateBf16C256 = StateProb<4, 4>;
+using StateBf16C512 = StateProb<4, 8>;
 using ChunkValueBf16 = ChunkValueProb<3>;
 
 }  // namespace
 
-int chunk_len() { return kChunk; }
+int chunk_len(int64_t T) {
+  const int f = forced_chunk();
+  if (f > 0) return f;
+  return T >= 4096 ? 512 : 256;
+}
 
 size_t chunked_p_bytes(int64_t B, int64_t H, int64_t T) {
-  return static_cast<size_t>(B * H * T * kChunk) * 2;
+  return static_cast<size_t>(B * H * T * chunk_len(T)) * 2;
 }
 size_t chunked_s_bytes(int64_t B, int64_t H, int64_t T, int64_t N, int64_t D) {
-  const int64_t nch = (T + kChunk - 1) / kChunk;
+  const int64_t C = chunk_len(T);
+  const int64_t nch = (T + C - 1) / C;
   return static_cast<size_t>(B * H * nch * N * D) * 2;
 }
+
+namespace {
+template <class SP>
+int launch_state_pass(const FwdArgs& a, void* s_hi, void* s_lo, int nchunks, cudaStream_t stream,
+                      int* err) {
+  typename SP::Params prm{};
+  const int64_t kd[4] = {a.N, a.T, a.H, a.B};
+  const int64_t ks[3] = {a.k_strides[2] * 2, a.k_strides[1] * 2, a.k_strides[0] * 2};
+  const int64_t vd[4] = {a.D, a.T, a.Hv, a.B};
+  const int64_t vs[3] = {a.v_strides[2] * 2, a.v_strides[1] * 2, a.v_strides[0] * 2};
+  if (!make_map_4d(&prm.a_map[0], a.k, 2, kd, ks, 64, 64, "state pass: K")) return BDH_ERR_INVALID;
+  if (!make_map_4d(&prm.b_map[0], a.v, 2, vd, vs, 64, 64, "state pass: V")) return BDH_ERR_INVALID;
+  prm.H = static_cast<int>(a.H);
+  prm.Hv = static_cast<int>(a.Hv);
+  prm.T = static_cast<int>(a.T);
+  prm.N = static_cast<int>(a.N);
+  prm.D = static_cast<int>(a.D);
+  prm.nn = static_cast<int>((a.N + 127) / 128);
+  prm.nd = static_cast<int>((a.D + 127) / 128);
+  prm.units = static_cast<int>(a.B * a.H);
+  prm.nchunks = nchunks;
+  const int64_t sd[4] = {a.D, a.N, nchunks, a.B * a.H};
+  const int64_t ss[3] = {a.D * 2, a.N * a.D * 2, int64_t(nchunks) * a.N * a.D * 2};
+  if (!make_map_4d(&prm.s_map[0], s_hi, 2, sd, ss, 64, 32, "state pass: S hi")) return BDH_ERR_INVALID;
+  if (!make_map_4d(&prm.s_map[1], s_lo, 2, sd, ss, 64, 32, "state pass: S lo")) return BDH_ERR_INVALID;
+  prm.err = err;
+  return launch_tc<typename SP::S, SP>(prm, prm.units * prm.nn * prm.nd, stream, kProfState);
+}
+}  // namespace
 
 int launch_chunked_forward(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi, void* s_lo,
                            cudaStream_t stream, int* err) {
@@ -343,7 +395,8 @@ int launch_chunked_forward(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi,
     return BDH_ERR_INVALID;
   }
   const int64_t units = a.B * a.H;
-  const int nchunks = static_cast<int>((a.T + kChunk - 1) / kChunk);
+  const int C = chunk_len(a.T);
+  const int nchunks = static_cast<int>((a.T + C - 1) / C);
   // 1. intra-chunk scores
   ScoreArgs sa;
   sa.elem = 2;
@@ -355,41 +408,21 @@ int launch_chunked_forward(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi,
   }
   sa.B = a.B; sa.H = a.H; sa.Hb = a.H; sa.T = a.T; sa.K = a.N;
   sa.mode = kStoreDirect;
-  sa.chunk = kChunk;
+  sa.chunk = C;
   sa.p_hi = p_hi;
   sa.p_lo = p_lo;
   int rc = launch_score_pass(sa, stream, err);
   if (rc) return rc;
   // 2. prefix states S_1 .. S_{nchunks-1}
   if (nchunks > 1) {
-    StateBf16::Params prm{};
-    const int64_t kd[4] = {a.N, a.T, a.H, a.B};
-    const int64_t ks[3] = {a.k_strides[2] * 2, a.k_strides[1] * 2, a.k_strides[0] * 2};
-    const int64_t vd[4] = {a.D, a.T, a.Hv, a.B};
-    const int64_t vs[3] = {a.v_strides[2] * 2, a.v_strides[1] * 2, a.v_strides[0] * 2};
-    if (!make_map_4d(&prm.a_map[0], a.k, 2, kd, ks, 64, 64, "state pass: K")) return BDH_ERR_INVALID;
-    if (!make_map_4d(&prm.b_map[0], a.v, 2, vd, vs, 64, 64, "state pass: V")) return BDH_ERR_INVALID;
-    prm.H = static_cast<int>(a.H);
-    prm.Hv = static_cast<int>(a.Hv);
-    prm.T = static_cast<int>(a.T);
-    prm.N = static_cast<int>(a.N);
-    prm.D = static_cast<int>(a.D);
-    prm.nn = static_cast<int>((a.N + 127) / 128);
-    prm.nd = static_cast<int>((a.D + 127) / 128);
-    prm.units = static_cast<int>(units);
-    prm.nchunks = nchunks;
-    const int64_t sd[4] = {a.D, a.N, nchunks, units};
-    const int64_t ss[3] = {a.D * 2, a.N * a.D * 2, int64_t(nchunks) * a.N * a.D * 2};
-    if (!make_map_4d(&prm.s_map[0], s_hi, 2, sd, ss, 64, 32, "state pass: S hi")) return BDH_ERR_INVALID;
-    if (!make_map_4d(&prm.s_map[1], s_lo, 2, sd, ss, 64, 32, "state pass: S lo")) return BDH_ERR_INVALID;
-    prm.err = err;
-    rc = launch_tc<StateBf16::S, StateBf16>(prm, prm.units * prm.nn * prm.nd, stream, kProfState);
+    rc = C == 512 ? launch_state_pass<StateBf16C512>(a, s_hi, s_lo, nchunks, stream, err)
+                  : launch_state_pass<StateBf16C256>(a, s_hi, s_lo, nchunks, stream, err);
     if (rc) return rc;
   }
   // 3. intra P V + inter Q S
   ChunkValueBf16::Params prm{};
-  const int64_t pd[4] = {kChunk, a.T, units, 1};
-  const int64_t ps[3] = {int64_t(kChunk) * 2, a.T * kChunk * 2, units * a.T * kChunk * 2};
+  const int64_t pd[4] = {C, a.T, units, 1};
+  const int64_t ps[3] = {int64_t(C) * 2, a.T * C * 2, units * a.T * C * 2};
   if (!make_map_4d(&prm.p_map[0], p_hi, 2, pd, ps, 64, 128, "chunk value pass: P hi")) return BDH_ERR_INVALID;
   if (!make_map_4d(&prm.p_map[1], p_lo, 2, pd, ps, 64, 128, "chunk value pass: P lo")) return BDH_ERR_INVALID;
   const int64_t vd[4] = {a.D, a.T, a.Hv, a.B};
@@ -411,6 +444,7 @@ int launch_chunked_forward(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi,
   prm.nd = static_cast<int>((a.D + ChunkValueBf16::BN - 1) / ChunkValueBf16::BN);
   prm.units = static_cast<int>(units);
   prm.nchunks = nchunks;
+  prm.chunk = C;
   prm.out = a.out;
   prm.os_b = a.out_strides[0];
   prm.os_h = a.out_strides[1];
@@ -422,8 +456,8 @@ int launch_chunked_forward(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi,
                    ? 1
                    : 0;
   prm.err = err;
-  if (use_pairs_chunked() && kChunk == 256) {
-    const int tiles = prm.units * nchunks * static_cast<int>((a.D + 255) / 256);
+  if (use_pairs_chunked()) {
+    const int tiles = prm.units * static_cast<int>((a.T + 255) / 256) * static_cast<int>((a.D + 255) / 256);
     return launch_pair<ChunkValuePair::S, ChunkValuePair>(prm, tiles, stream, kProfValue);
   }
   return launch_tc<ChunkValueBf16::S, ChunkValueBf16>(prm, prm.units * prm.mt * prm.nd, stream,

@@ -42,7 +42,7 @@ std::atomic<int> g_fwd_algo{BDH_FWD_AUTO};
 bool use_chunked(int dtype, int64_t T) {
   if (dtype != BDH_DTYPE_BF16) return false;
   const int algo = g_fwd_algo.load();
-  if (algo == BDH_FWD_CHUNKED) return T > chunk_len();
+  if (algo == BDH_FWD_CHUNKED) return T > chunk_len(T);
   if (algo == BDH_FWD_QUADRATIC) return false;
   return T >= 1536;
 }

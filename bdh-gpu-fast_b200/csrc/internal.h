@@ -71,7 +71,7 @@ int launch_value(const FwdArgs& a, const void* p_hi, const void* p_lo, cudaStrea
                  int* err);
 
 // Chunked long-sequence forward (attn_chunked.cu), bf16 only.
-int chunk_len();
+int chunk_len(int64_t T);  // keys per chunk of the chunked forward at sequence length T
 size_t chunked_p_bytes(int64_t B, int64_t H, int64_t T);
 size_t chunked_s_bytes(int64_t B, int64_t H, int64_t T, int64_t N, int64_t D);
 int launch_chunked_forward(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi, void* s_lo,

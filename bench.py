@@ -616,6 +616,14 @@ def measured_tf32_tflops(dev) -> float:
     return _TF32_PEAK[dev]
 
 
+def chunk_len(T: int) -> int:
+    """Keys per chunk of the library's chunked forward (csrc/attn_chunked.cu chunk_len)."""
+    forced = os.environ.get("BDH_SM100_CHUNK", "")
+    if forced in ("256", "512"):
+        return int(forced)
+    return 512 if T >= 4096 else 256
+
+
 def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev, steps):
     """Roofline of the dominant kernel of an op config (algorithmic work per launch / time).
 
@@ -637,7 +645,7 @@ def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev, steps):
         tname = "score_pass_config1"
     elif cfg_id == 3 and chunked:
         k = prof["state"]
-        C = 256
+        C = chunk_len(T)
         work = units * ((T // C - 1) * N * D * 4 + T * N * 2) + B * T * D * 2
         peak, unit, bound = peaks["hbm_gbs"], "GB/s", "hbm"
         psrc = f"{src} hbm_gbs"
@@ -696,7 +704,7 @@ def bench_op(args, world, rank, dev):
     clk = clocks.stop()
     # executed-algorithm flops (per (b,h) unit): quadratic causal T(T-1)(N+D), or the chunked
     # form (T/C) C(C-1)(N+D) + 4 (T-C) N D when the library takes it (bf16 and T >= 1536)
-    C = 256
+    C = chunk_len(T)
     chunked = dt == torch.bfloat16 and T >= 1536
     quad_fwd = B * H * T * (T - 1) * (N + D)
     fwd = B * H * ((T // C) * C * (C - 1) * (N + D) + 4 * (T - C) * N * D) if chunked else quad_fwd
@@ -711,7 +719,7 @@ def bench_op(args, world, rank, dev):
         "metric": f"tril-attn TFLOP/s (config {cfg_id}, executed-algorithm causal flops)",
         "value": flops / (ms / 1e3) / 1e12,
         "effective_tflops_quadratic_equivalent": effective / (ms / 1e3) / 1e12,
-        "forward_form": "chunked C=256" if chunked else "quadratic",
+        "forward_form": f"chunked C={C}" if chunked else "quadratic",
         "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32" if dt == torch.float32 else "bf16", "data": "synthetic",

@@ -466,6 +466,20 @@ def test_chunked_forward_distinct_k_permuted(chunked_algo):
     assert rel(out.float().cpu().numpy(), ref) <= 3e-3
 
 
+@pytest.mark.parametrize("T,Hv", [(4096, 1), (4100, 2), (5000, 1)])
+def test_chunked_forward_c512_vs_oracle(T, Hv):
+    """From T = 4096 the chunked form uses 512-key chunks (256-row pair tiles covering half a
+    chunk each, 8-k-block accumulation rounds in the state pass); ragged last chunks included."""
+    B, H, N, D = 1, 2, 512, 256
+    g = torch.Generator(device=DEV).manual_seed(T)
+    q = torch.relu(torch.randn(B, H, T, N, device=DEV, generator=g)).to(torch.bfloat16)
+    v = torch.randn(B, Hv, T, D, device=DEV, generator=g).to(torch.bfloat16)
+    out = sa().tril_score_v(q, q, v)
+    ref = O.tril_score_v(np64(q), np64(q), np64(v))
+    assert rel(out.float().cpu().numpy(), ref) <= 3e-3
+    assert torch.all(out[:, :, 0] == 0)
+
+
 def test_chunked_forward_config3_shape_vs_fp64():
     """Config-3 shapes for two (b, h) units: T = 8192, N = 8192, ~5% dense latents,
     LayerNormed V; the automatic selection takes the chunked form at this length."""
