@@ -58,6 +58,11 @@ bool make_map_4d_box(CUtensorMap* map, const void* base, int elem_bytes, const i
     set_error("cuTensorMapEncodeTiled is not available from the CUDA driver");
     return false;
   }
+  // The driver call needs a current context. A thread that has not made a runtime call that
+  // binds one yet (autograd's device thread, when the backward's first CUDA work is this
+  // library) has none: bind the current device's primary context first.
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaSetDevice(dev);
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) {
     std::ostringstream os;
     os << what << ": base address must be 16-byte aligned for TMA";

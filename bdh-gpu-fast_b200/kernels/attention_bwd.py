@@ -131,12 +131,16 @@ class RopeTrilSelfAttnFn(torch.autograd.Function):
         else:
             ctx.save_for_backward(QR, V, freqs)
         ctx.mark_non_differentiable(QR)
+        # QR carries no gradient: do not let autograd build a zero (B, H, T, N) tensor for it
+        ctx.set_materialize_grads(False)
         return out, QR
 
     @staticmethod
     def backward(ctx, dO, _dQR):
         from .sm100_attn import tril_score_v_bwd
 
+        if dO is None:
+            return None, None, None, None, None, None
         QR, V, freqs = ctx.saved_tensors[:3]
         dQ, _, dV = tril_score_v_bwd(QR, QR, V, dO.contiguous(), freqs=freqs, pos0=ctx.pos0)
         if ctx.relu_input:

@@ -687,6 +687,10 @@ def bench_op(args, world, rank, dev):
         vg = v.clone().requires_grad_(True)
 
         def step():
+            # a training step's gradients start empty (zero_grad(set_to_none=True)), so the
+            # backward writes them instead of accumulating into last step's
+            qg.grad = None
+            vg.grad = None
             out, _ = bdh_rope_attn(qg, vg, freqs, 0, impl="cuda_sm100")
             out.backward(dO)
     else:
