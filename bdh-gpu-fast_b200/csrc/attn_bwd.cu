@@ -8,7 +8,8 @@
 //   1. score pass over (dO, V), K-loop over D -> G = dS + dS^T (K is Q) or dS / dS^T (else)
 //   2. grad-Q pass: dQ_total = G QR over all keys (K is Q), or dS K / dS^T Q over the causal
 //      key ranges; optional RoPE adjoint R(t)^T in the epilogue (gradient of the unrotated
-//      latent), computed in registers from freqs like the forward rotation
+//      latent), its phases computed in registers from freqs with the hardware sin / cos
+//      (rope_cis_grad: the exact software sincos of the forward cost a third of the pass)
 //   3. score pass over (Q, K) writing M^T (transposed store: the K-major A operand of dV)
 //   4. grad-V pass: dV[j] = sum_h sum_{i > j} M^T_h[j][i] dO_h[i], longest key blocks first
 // Every score-like operand is an exact hi/lo split, so the tensor cores keep fp32-level
@@ -138,12 +139,12 @@ struct GradQProb {
         if (n >= p.N) break;
         float cc0, ss0, cc1, ss1;
         const float f0 = __ldg(p.freqs + n), f1 = __ldg(p.freqs + n + 1);
-        rope_cis(pos, f0, cc0, ss0);
+        rope_cis_grad(pos, f0, cc0, ss0);
         if (f1 == f0) {
           cc1 = cc0;
           ss1 = ss0;
         } else {
-          rope_cis(pos, f1, cc1, ss1);
+          rope_cis_grad(pos, f1, cc1, ss1);
         }
         const float g0 = v[e], g1 = v[e + 1];
         v[e] = fmaf(g0, cc0, g1 * ss1);

@@ -384,6 +384,16 @@ struct FastDiv {
 // cos / sin of the reference phase for position `pos` and frequency `f` (bdh.py:119-122,
 // 142-150): fp32 product, exact fractional part (the product is >= 0), times fp32 2*pi as
 // torch rounds the Python scalar (0x40C90FDB), then sincosf.
+// (cos, sin) of the same phase with the hardware approximations (__sincosf) after reducing the
+// phase to [-pi, pi), where their absolute error is below 2^-21. For gradients only (the RoPE
+// adjoint of the backward): the forward rotation keeps rope_cis, whose values match the
+// reference's fp32 cos / sin of the phase.
+__device__ __forceinline__ void rope_cis_grad(float pos, float f, float& c, float& s) {
+  float ph = __fmul_rn(pos, f);
+  ph = __fsub_rn(ph, floorf(ph));
+  if (ph >= 0.5f) ph -= 1.0f;
+  __sincosf(__fmul_rn(ph, __int_as_float(0x40C90FDB)), &s, &c);
+}
 __device__ __forceinline__ void rope_cis(float pos, float f, float& c, float& s) {
   float ph = __fmul_rn(pos, f);
   ph = __fsub_rn(ph, floorf(ph));
