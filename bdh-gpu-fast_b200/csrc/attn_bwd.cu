@@ -245,6 +245,7 @@ struct GradQPair {
   using Base = GradQBf16;
   using Params = Base::Params;  // b_map box 64 x BK as in the single-CTA pass
   using S = PairShape<false, true, 2, 1, 4>;
+  static constexpr int kEpiWarps = 8;  // the RoPE adjoint makes the epilogue long
   struct Tile {
     int unit, m, n;
   };

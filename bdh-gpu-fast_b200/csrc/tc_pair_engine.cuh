@@ -24,7 +24,12 @@
 
 namespace bdh {
 
-constexpr int kPairThreads = 192;
+// P::kEpiWarps = 8 -> two epilogue warps per TMEM lane quadrant, each draining one half of the
+// tile's columns (more warps to hide the epilogue's latency); default four.
+template <class P>
+constexpr int pair_threads() {
+  return 64 + 32 * EpiWarps<P>::value;
+}
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -127,8 +132,10 @@ struct PairShape {
 };
 
 template <class S, class P>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<P>(), 1)
     tc_pair_kernel(const __grid_constant__ typename P::Params prm) {
+  constexpr int EW = EpiWarps<P>::value;
+  static_assert(EW == 4 || EW == 8, "four or eight epilogue warps");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -154,7 +161,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull + a, 1);
-      mbar_init(tempty + a, 2 * kEpiThreads);
+      mbar_init(tempty + a, 2 * 32 * EW);  // every epilogue thread of both CTAs
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -260,6 +267,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quad = warp & 3;
     const int row = quad * 32 + static_cast<int>(lane_id());
+    const int part = (warp - 2) >> 2;  // column half (eight epilogue warps) or 0
+    const int c_begin = EW == 8 ? part * (S::BN / 2) : 0;
+    const int c_end = EW == 8 ? c_begin + S::BN / 2 : S::BN;
     const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
     int lt = 0;
     for (int t = pair; t < ntiles; t += npairs, ++lt) {
@@ -272,7 +282,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       const uint32_t tbase =
           tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * S::BN);
 #pragma unroll 1
-      for (int c0 = 0; c0 < S::BN; c0 += 32) {
+      for (int c0 = c_begin; c0 < c_end; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tbase + static_cast<uint32_t>(c0), r);
         tmem_ld_wait();
@@ -307,7 +317,7 @@ static int launch_pair(const typename P::Params& prm, int ntiles, cudaStream_t s
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 74);
-    cfg.blockDim = dim3(kPairThreads);
+    cfg.blockDim = dim3(pair_threads<P>());
     cfg.dynamicSmemBytes = S::SMEM_BYTES;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
@@ -323,7 +333,7 @@ static int launch_pair(const typename P::Params& prm, int ntiles, cudaStream_t s
   }
   const int pairs = std::min(ntiles, max_pairs[(dev >= 0 && dev < 64) ? dev : 0]);
   prof_start(kind, stream);
-  tc_pair_kernel<S, P><<<2 * pairs, kPairThreads, S::SMEM_BYTES, stream>>>(prm);
+  tc_pair_kernel<S, P><<<2 * pairs, pair_threads<P>(), S::SMEM_BYTES, stream>>>(prm);
   prof_stop(kind, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
