@@ -22,7 +22,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 REF_OUT = HERE / "_ref"
-DEFAULT_REFERENCE = Path("/root/reference")
+DEFAULT_REFERENCE = Path(os.environ.get("BDH_REFERENCE", "/root/reference"))
 NAME = "bdh_ref_ext"
 
 

@@ -2,7 +2,9 @@
 
 Run in the build container (the reference checkout is not available on GPU hosts):
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /root/reference
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py <reference checkout>
+
+(default: the ``BDH_REFERENCE`` environment variable, else the checkout path build_ref.py uses)
 
 It imports the reference's own Python modules (``bdh``, ``bdh_baseline``, ``bdh_cache``,
 ``kernels``) and its CPU extension built by ``oracle/build_ref.py`` (``csrc/tril_attn_cpu.cpp``),
@@ -189,7 +191,13 @@ def dataclasses_asdict(c):
 
 
 if __name__ == "__main__":
-    ref = Path(sys.argv[1]) if len(sys.argv) > 1 and not sys.argv[1].startswith("--") else Path("/root/reference")
+    if len(sys.argv) > 1 and not sys.argv[1].startswith("--"):
+        ref = Path(sys.argv[1])
+    else:
+        sys.path.insert(0, str(HERE.parent.parent / "oracle"))
+        import build_ref
+
+        ref = build_ref.DEFAULT_REFERENCE
     if "--latent-only" in sys.argv:
         sys.path.insert(0, str(ref))
         import bdh as _bdh
