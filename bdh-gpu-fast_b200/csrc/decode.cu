@@ -304,6 +304,249 @@ __global__ void __launch_bounds__(kDecThreads) decode_partial_fp8_kernel(
   }
 }
 
+// ------------------------------------------------------------ column-slice stream
+// The same split-S decode with the query in registers and one continuous load pipeline per
+// lane. Warp w of a CTA owns the column chunks c = w + 8 i (i < QC) of 32 x E elements
+// (E = 16 / key size), keeps its q elements of those chunks in registers for the whole CTA,
+// and streams all of the CTA's cached rows over those columns: each lane's 16-byte key loads
+// form one sequence (row by row, QC loads per row) issued kSliceAhead loads before their use,
+// so the stream does not drain between rows. The eight partial dots of a group of eight rows
+// are reduced across the warp with nine shuffles, and the warps' partials are summed in shared
+// memory. Measured on B200 at the config-4 shapes (B = 64, H = 4, S = 520, N = 8192): 7.2 /
+// 7.1 / 5.0 TB/s for fp32 / bf16 / fp8 keys, against 5.8 / 5.0 / 3.6 TB/s for the row-per-warp
+// kernels above (q staged in shared memory, loads drained at every row pair), which remain the
+// path for unaligned rows and latent widths beyond the register budget.
+constexpr int kSliceWarps = 8;
+constexpr int kSliceAhead = 8;  // 16-byte key loads in flight per lane
+
+template <typename TK>
+__device__ __forceinline__ float dot16(const float* qv, const uint4 u) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float a = 0.f;
+  if (sizeof(TK) == 4) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a = fmaf(qv[i], __uint_as_float(w[i]), a);
+  } else if (sizeof(TK) == 2) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      a = fmaf(qv[2 * i], __uint_as_float(w[i] << 16), a);
+      a = fmaf(qv[2 * i + 1], __uint_as_float(w[i] & 0xFFFF0000u), a);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      a = fmaf(qv[4 * i], e4m3_top_to_f32_2m120(w[i] << 24), a);
+      a = fmaf(qv[4 * i + 1], e4m3_top_to_f32_2m120(w[i] << 16), a);
+      a = fmaf(qv[4 * i + 2], e4m3_top_to_f32_2m120(w[i] << 8), a);
+      a = fmaf(qv[4 * i + 3], e4m3_top_to_f32_2m120(w[i]), a);
+    }
+  }
+  return a;
+}
+
+// Four consecutive query elements; vec: one 16-byte (fp32) or 8-byte (bf16) load.
+__device__ __forceinline__ void load_q4(const float* p, bool vec, float (&x)[4]) {
+  if (vec) {
+    const float4 t = __ldg(reinterpret_cast<const float4*>(p));
+    x[0] = t.x; x[1] = t.y; x[2] = t.z; x[3] = t.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = p[j];
+  }
+}
+__device__ __forceinline__ void load_q4(const uint16_t* p, bool vec, float (&x)[4]) {
+  if (vec) {
+    const uint2 t = __ldg(reinterpret_cast<const uint2*>(p));
+    x[0] = __uint_as_float(t.x << 16); x[1] = __uint_as_float(t.x & 0xFFFF0000u);
+    x[2] = __uint_as_float(t.y << 16); x[3] = __uint_as_float(t.y & 0xFFFF0000u);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = bf16_bits_to_f32(p[j]);
+  }
+}
+
+// F8: TK = uint8_t e4m3 keys with one fp32 scale per row (ksc); the fused RoPE / slot write
+// (freqs) is only used with F8 = false.
+template <typename TQ, typename TK, typename TV, int QC, bool F8>
+__global__ void __launch_bounds__(kSliceWarps * 32, 2) decode_slice_kernel(
+    const TQ* __restrict__ q, const TK* __restrict__ kp, const float* __restrict__ ksc,
+    const TV* __restrict__ vp, float* __restrict__ partial, TK* __restrict__ slot,
+    const float* __restrict__ freqs, int H, int Hv, int S, int N, int D, int64_t qsb,
+    int64_t qsh, int64_t qst, int64_t ksb, int64_t ksh, int64_t kst, int64_t csb, int64_t csh,
+    int64_t cst, int64_t vsb, int64_t vsh, int64_t vst, int64_t ssb, int64_t ssh, int64_t sst,
+    int64_t pos, int rows_per_cta, bool qvec) {
+  constexpr int E = 16 / sizeof(TK);
+  constexpr int CS = kSliceWarps * 32 * E;  // elements of one chunk row across the CTA
+  constexpr int L = 8 * QC;                 // loads of a group of eight rows
+  constexpr int DP = kSliceAhead;
+  static_assert(DP % QC == 0 && L % DP == 0, "the prefetch distance covers whole rows");
+  __shared__ float red[kSliceWarps][kDecRowsMax];
+  __shared__ float sc[kDecRowsMax];
+  const int split = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int tq = blockIdx.z;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int hv = Hv == 1 ? 0 : h;
+  const int j0 = split * rows_per_cta;
+  const int rows = max(0, min(rows_per_cta, S - j0));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int coff0 = (warp * 32 + lane) * E;  // this lane's chunk i starts at coff0 + i * CS
+  const int nval = coff0 < N ? (N - coff0 + CS - 1) / CS : 0;
+
+  // 1. the first kSliceAhead key loads
+  const TK* lp = kp + b * ksb + h * ksh + static_cast<int64_t>(j0) * kst + coff0;
+  int lr = 0;  // row of lp
+  uint4 ring[DP];
+#pragma unroll
+  for (int t = 0; t < DP; ++t) {
+    const int i = t % QC;
+    ring[t] = make_uint4(0, 0, 0, 0);
+    if (lr < rows && i < nval) ring[t] = __ldcs(reinterpret_cast<const uint4*>(lp + i * CS));
+    if (i == QC - 1) {
+      lp += kst;
+      ++lr;
+    }
+  }
+
+  // 2. this lane's query elements (rotated with freqs; split 0 then writes the cache slot)
+  float qv[QC][E];
+  const TQ* qr = q + b * qsb + h * qsh + tq * qst;
+  const float ph = static_cast<float>(pos + tq);
+#pragma unroll
+  for (int i = 0; i < QC; ++i) {
+#pragma unroll
+    for (int e = 0; e < E; e += 4) {
+      const int n = coff0 + i * CS + e;
+      float x[4] = {0.f, 0.f, 0.f, 0.f};
+      if (i < nval) {
+        load_q4(qr + n, qvec, x);
+        if constexpr (!F8) {
+          if (freqs != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 4; j += 2) {
+              float c0, s0, c1, s1;
+              rope_cis(ph, freqs[n + j], c0, s0);
+              rope_cis(ph, freqs[n + j + 1], c1, s1);
+              const float x0 = x[j], x1 = x[j + 1];
+              if (sizeof(TQ) == 2) {
+                x[j] = bf16_round_d(__fadd_rn(bf16_round_d(__fmul_rn(x0, c0)),
+                                              bf16_round_d(__fmul_rn(-x1, s0))));
+                x[j + 1] = bf16_round_d(__fadd_rn(bf16_round_d(__fmul_rn(x1, c1)),
+                                                  bf16_round_d(__fmul_rn(x0, s1))));
+              } else {
+                x[j] = __fsub_rn(__fmul_rn(x0, c0), __fmul_rn(x1, s0));
+                x[j + 1] = __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(x0, s1));
+              }
+            }
+            if (slot != nullptr && split == 0) {
+              TK* sr = slot + b * ssb + h * ssh + tq * sst;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) st_elem(sr, n + j, x[j]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) qv[i][e + j] = F8 ? x[j] * kE4m3QScale : x[j];
+    }
+  }
+
+  // 3. the rows, eight at a time; loads run kSliceAhead ahead across group boundaries
+  const int groups = (rows + 7) >> 3;
+  for (int g = 0; g < groups; ++g) {
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+#pragma unroll
+    for (int t = 0; t < L; ++t) {
+      const uint4 u = ring[t % DP];
+      const int i = t % QC;
+      uint4 nx = make_uint4(0, 0, 0, 0);
+      if (lr < rows && i < nval) nx = __ldcs(reinterpret_cast<const uint4*>(lp + i * CS));
+      ring[t % DP] = nx;
+      if (i == QC - 1) {
+        lp += kst;
+        ++lr;
+      }
+      acc[t / QC] += dot16<TK>(qv[i], u);
+    }
+    // eight values per lane -> lane (b4 b3 b2) holds the warp's sum for row 4 b4 + 2 b3 + b2
+    const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+    float u4[4], u2[2];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float keep = b4 ? acc[k + 4] : acc[k], send = b4 ? acc[k] : acc[k + 4];
+      u4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float keep = b3 ? u4[k + 2] : u4[k], send = b3 ? u4[k] : u4[k + 2];
+      u2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    float u1 = (b2 ? u2[1] : u2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? u2[0] : u2[1], 4);
+    u1 += __shfl_xor_sync(0xffffffffu, u1, 2);
+    u1 += __shfl_xor_sync(0xffffffffu, u1, 1);
+    if ((lane & 3) == 0) red[warp][g * 8 + 4 * b4 + 2 * b3 + b2] = u1;
+  }
+  __syncthreads();
+
+  // 4. scores, then partial out = sum_j s_j V_j
+  const float* cbase = F8 ? ksc + b * csb + h * csh : nullptr;
+  for (int r = threadIdx.x; r < rows; r += kSliceWarps * 32) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kSliceWarps; ++w) s += red[w][r];
+    sc[r] = F8 ? (s * kE4m3RowScale) * cbase[(j0 + r) * cst] : s;
+  }
+  __syncthreads();
+  const TV* vbase = vp + b * vsb + hv * vsh;
+  float* dst = partial + ((static_cast<int64_t>(split) * gridDim.y + bh) * gridDim.z + tq) * D;
+  for (int d = threadIdx.x; d < D; d += kSliceWarps * 32) {
+    float acc = 0.f;
+#pragma unroll 8
+    for (int r = 0; r < rows; ++r) acc = fmaf(sc[r], ld_elem(vbase + (j0 + r) * vst, d), acc);
+    dst[d] = acc;
+  }
+}
+
+// Chunks per warp for the column-slice kernel: the smallest of 1, 2, 4, 8 (fp8: 1, 2, 4) with
+// QC * 8 warps * 32 lanes * E >= N, or 0 when N is wider (the row-per-warp kernel then runs).
+int slice_qc(int64_t N, int key_bytes) {
+  const int64_t per = static_cast<int64_t>(kSliceWarps) * 32 * (16 / key_bytes);
+  const int qmax = key_bytes == 1 ? 4 : 8;
+  for (int qc = 1; qc <= qmax; qc *= 2)
+    if (qc * per >= N) return qc;
+  return 0;
+}
+
+template <typename TQ, typename TK, typename TV, bool F8>
+void launch_slice(int qc, dim3 grid, cudaStream_t stream, const TQ* q, const TK* k,
+                  const float* ksc, const TV* v, float* partial, TK* slot, const float* freqs,
+                  int H, int Hv, int S, int N, int D, const int64_t qs[4], const int64_t ks[4],
+                  const int64_t cs[3], const int64_t vs[4], const int64_t ss[4], int64_t pos,
+                  int rows, bool qvec) {
+#define BDH_SLICE(QC)                                                                             \
+  decode_slice_kernel<TQ, TK, TV, QC, F8><<<grid, kSliceWarps * 32, 0, stream>>>(                \
+      q, k, ksc, v, partial, slot, freqs, H, Hv, S, N, D, qs[0], qs[1], qs[2], ks[0], ks[1],      \
+      ks[2], cs[0], cs[1], cs[2], vs[0], vs[1], vs[2], ss[0], ss[1], ss[2], pos, rows, qvec)
+  switch (qc) {
+    case 1: BDH_SLICE(1); break;
+    case 2: BDH_SLICE(2); break;
+    case 4: BDH_SLICE(4); break;
+    default:
+      if constexpr (!F8) BDH_SLICE(8);
+      break;
+  }
+#undef BDH_SLICE
+}
+
+// 16-byte (fp32) / 8-byte (bf16) vector loads of the query rows.
+bool q_vec_ok(const void* q, int q_dtype, const int64_t qs[4]) {
+  const uintptr_t al = q_dtype == BDH_DTYPE_F32 ? 15u : 7u;
+  return (reinterpret_cast<uintptr_t>(q) & al) == 0 && qs[0] % 4 == 0 && qs[1] % 4 == 0 &&
+         qs[2] % 4 == 0;
+}
+
 template <typename TO>
 __global__ void decode_reduce_kernel(const float* __restrict__ partial, TO* __restrict__ out,
                                      int nsplit, int H, int Tq, int D, int64_t BHT, int64_t osb,
@@ -324,11 +567,11 @@ __global__ void decode_reduce_kernel(const float* __restrict__ partial, TO* __re
 }  // namespace
 
 // Rows per CTA and split count. Measured on B200 (config-4 model, S ~ 520, N = 8192): the
-// split-S stream runs best with about four or more resident waves of CTAs (B = 64: 32 rows per
-// CTA, 0.85 / 0.74 of HBM for fp32 / bf16 caches vs 0.69 / 0.58 with 128 rows), and small
-// batches need short splits to fill the GPU at all (B = 4: 16 rows beat 8, 32 and more). Rule:
-// the largest of 64, 32, 16 rows that still gives >= 4 x resident CTAs, else 16; `max_splits`
-// caps the split count.
+// split-S stream runs best with about four or more resident waves of CTAs, and small batches
+// need short splits to fill the GPU at all (B = 4: 16 rows beat 8, 32 and more). Rule: the
+// largest of 64, 32, 16 rows that still gives >= 4 x resident CTAs (resident = the column-slice
+// kernel's occupancy, two CTAs per SM), else 16; at B = 64 that is 64 rows, which the
+// column-slice kernel streams as fast as 32. `max_splits` caps the split count.
 DecodePlan plan_decode(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N, int64_t max_splits) {
   DecodePlan pl;
   const int64_t units = std::max<int64_t>(1, B * H * Tq);
@@ -344,11 +587,12 @@ DecodePlan plan_decode(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N, i
   int dev = 0;
   cudaGetDevice(&dev);
   int occ = 0;
-  const size_t smem = (static_cast<size_t>(std::max<int64_t>(N, 1)) + kDecRowsMax) * sizeof(float);
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_partial_kernel<float, float, true>,
-                                                    kDecThreads, smem) != cudaSuccess || occ <= 0) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+          &occ, decode_slice_kernel<float, float, float, 8, false>, kSliceWarps * 32, 0) !=
+          cudaSuccess ||
+      occ <= 0) {
     cudaGetLastError();
-    occ = 4;
+    occ = 2;
   }
   const int64_t resident = static_cast<int64_t>(sm_count(dev)) * occ;
   int rows = 16;
@@ -441,8 +685,23 @@ int launch_decode(const DecodeArgs& a_in, float* partial, float* qrot, int64_t m
         a.slot_strides[2], a.pos, pl.rows);                                                       \
   } while (0)
   const bool qf = a.q_dtype == BDH_DTYPE_F32, kf = a.kv_dtype == BDH_DTYPE_F32;
+  const int qc = vec ? slice_qc(a.N, ke) : 0;
   prof_start(kProfDecode, stream);
-  if (qf && kf) {
+  if (qc > 0) {
+    const bool qv = q_vec_ok(a.q, a.q_dtype, a.q_strides);
+    const int64_t cs[3] = {0, 0, 0};
+#define BDH_SLICE_GO(TQ, TK)                                                                      \
+  launch_slice<TQ, TK, TK, false>(qc, grid, stream, static_cast<const TQ*>(a.q),                 \
+                                  static_cast<const TK*>(a.k), nullptr,                          \
+                                  static_cast<const TK*>(a.v), partial, static_cast<TK*>(a.slot), \
+                                  a.freqs, Hi, Hvi, Si, Ni, Di, a.q_strides, a.k_strides, cs,     \
+                                  a.v_strides, a.slot_strides, a.pos, pl.rows, qv)
+    if (qf && kf) BDH_SLICE_GO(float, float);
+    else if (qf) BDH_SLICE_GO(float, uint16_t);
+    else if (kf) BDH_SLICE_GO(uint16_t, float);
+    else BDH_SLICE_GO(uint16_t, uint16_t);
+#undef BDH_SLICE_GO
+  } else if (qf && kf) {
     if (vec) BDH_DEC_LAUNCH(float, float, true); else BDH_DEC_LAUNCH(float, float, false);
   } else if (qf) {
     if (vec) BDH_DEC_LAUNCH(float, uint16_t, true); else BDH_DEC_LAUNCH(float, uint16_t, false);
@@ -527,8 +786,22 @@ int launch_decode_fp8(const DecodeFp8Args& a_in, float* partial, float* qrot, cu
       BDH_DEC8_LAUNCH(TQ, TV, false); \
   } while (0)
   const bool qf = a.q_dtype == BDH_DTYPE_F32, vf = a.v_dtype == BDH_DTYPE_F32;
+  const int qc = vec ? slice_qc(a.N, 1) : 0;
   prof_start(kProfDecode, stream);
-  if (qf && vf) BDH_DEC8_V(float, float);
+  if (qc > 0) {
+    const bool qv = q_vec_ok(a.q, a.q_dtype, a.q_strides);
+    const int64_t ss[4] = {0, 0, 0, 1};
+#define BDH_SLICE8_GO(TQ, TV)                                                                    \
+  launch_slice<TQ, uint8_t, TV, true>(qc, grid, stream, static_cast<const TQ*>(a.q), a.k,       \
+                                      a.k_scale, static_cast<const TV*>(a.v), partial, nullptr,  \
+                                      nullptr, Hi, Hvi, Si, Ni, Di, a.q_strides, a.k_strides,    \
+                                      a.ks_strides, a.v_strides, ss, 0, pl.rows, qv)
+    if (qf && vf) BDH_SLICE8_GO(float, float);
+    else if (qf) BDH_SLICE8_GO(float, uint16_t);
+    else if (vf) BDH_SLICE8_GO(uint16_t, float);
+    else BDH_SLICE8_GO(uint16_t, uint16_t);
+#undef BDH_SLICE8_GO
+  } else if (qf && vf) BDH_DEC8_V(float, float);
   else if (qf) BDH_DEC8_V(float, uint16_t);
   else if (vf) BDH_DEC8_V(uint16_t, float);
   else BDH_DEC8_V(uint16_t, uint16_t);

@@ -817,9 +817,9 @@ def bench_decode(args, world, rank, dev):
         "data": "synthetic", "config": {"workload": "config 4 decode", "B": B, "prompt": P,
                                         "S_mean": S_mean},
         "roofline": {"kernel": ("state decode (state_decode_kernel + state_reduce_kernel)" if kind == "state"
-                                else "decode (decode_partial_fp8_kernel + decode_reduce_kernel)"
-                                if storage == torch.float8_e4m3fn
-                                else "decode (decode_partial_kernel + decode_reduce_kernel)"),
+                                else "decode over e4m3 keys (decode_slice_kernel<..., uint8, ..., fp8> "
+                                "+ decode_reduce_kernel)" if storage == torch.float8_e4m3fn
+                                else "decode (decode_slice_kernel + decode_reduce_kernel)"),
                      "bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      # state mode skips the rows of zero rotated query, so the dense-equivalent
                      # rate can exceed the copy bandwidth: no fraction is claimed for it
