@@ -3,12 +3,14 @@
 // _two_gemm_decode; every cached key precedes the query, so there is no mask).
 //
 // HBM-bound: the whole key history is streamed once per step. Grid = (split, b*h, tq); each
-// CTA owns DEC_ROWS consecutive cached rows of one (b, h):
-//   1. q (optionally RoPE-rotated in registers, and then also written to this step's cache
-//      slot by split 0) is staged in shared memory as fp32;
-//   2. each warp streams two key rows at a time with 16-byte coalesced loads straight from
-//      the capacity-strided cache view (no contiguous copy), widening bf16 in registers, and
-//      reduces the dot products with warp shuffles;
+// CTA owns a run of consecutive cached rows of one (b, h) and one query:
+//   1. the query (optionally RoPE-rotated in registers, and then also written to this step's
+//      cache slot by split 0) is held as fp32: in registers, per warp column slice
+//      (decode_slice_kernel, the default), or staged in shared memory (decode_partial_kernel,
+//      for unaligned rows and very wide latents);
+//   2. the key rows are streamed with 16-byte coalesced loads straight from the
+//      capacity-strided cache view (no contiguous copy), widened in registers (bf16, e4m3),
+//      and the dot products are reduced with warp shuffles;
 //   3. the CTA forms its partial out = sum_j s_j V_j (one thread per output column);
 //   4. a second small kernel sums the per-split partials in a fixed order (deterministic).
 #include <algorithm>
