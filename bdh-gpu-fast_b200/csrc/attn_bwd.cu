@@ -12,9 +12,10 @@
 //      (rope_cis_grad: the exact software sincos of the forward cost a third of the pass)
 //   3. score pass over (Q, K) writing M^T (transposed store: the K-major A operand of dV)
 //   4. grad-V pass: dV[j] = sum_h sum_{i > j} M^T_h[j][i] dO_h[i], longest key blocks first
-// Every score-like operand is an exact hi/lo split, so the tensor cores keep fp32-level
-// accuracy; bf16 Q/K/dO are used as stored (MN-major where needed), fp32 inputs use tf32
-// hi/lo copies laid out K-major.
+// Score-like operands: bf16 inputs give one bf16 term (fp32 sums rounded once, as the
+// reference's bf16 matmul chain rounds dM and M; BDH_SM100_SPLIT_SCORES=1 keeps an exact bf16
+// hi + lo split), fp32 inputs an exact tf32 hi/lo split. bf16 Q/K/dO are used as stored
+// (MN-major where needed); fp32 inputs use tf32 hi/lo copies laid out K-major.
 #include <algorithm>
 #include <cstdlib>
 
@@ -58,12 +59,13 @@ __device__ __forceinline__ void store_row32(void* base, int64_t off, bool f32, b
 // ------------------------------------------------------------------ grad-Q pass ----
 // out[u][i][n] = sum_j Gs[u][i][j] X[u][j][n] with Gs a hi/lo score matrix ([u][T][ldp]).
 // krange 0: all keys; 1: keys j < (i-block+1)*128 (dS K); 2: keys j >= i-block*128 (dS^T Q).
-template <int ELEM, int STAGES>
+// AT = 1: Gs is a single bf16 term (the bf16 path's default, see launch_grad_q).
+template <int ELEM, int STAGES, int AT = 2>
 struct GradQProb {
   static constexpr int BN = ELEM == 2 ? 256 : 128;
   static constexpr bool B_MN = ELEM == 2;
   static constexpr int B_TERMS = ELEM == 2 ? 1 : 2;
-  using S = TcShape<ELEM, BN, false, B_MN, 2, B_TERMS, STAGES, ELEM == 4 ? 8 : 0>;
+  using S = TcShape<ELEM, BN, false, B_MN, AT, B_TERMS, STAGES, ELEM == 4 ? 8 : 0>;
   static constexpr int CHUNK = 128 / ELEM;
   struct Params {
     CUtensorMap a_map[2];  // Gs hi/lo over [units][T][T(ldp)], box BK x 128
@@ -102,14 +104,13 @@ struct GradQProb {
   }
   __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x7u; }
   __device__ static void prefetch(const Params& p) {
-    tma_prefetch_desc(&p.a_map[0]);
-    tma_prefetch_desc(&p.a_map[1]);
+    for (int i = 0; i < AT; ++i) tma_prefetch_desc(&p.a_map[i]);
     for (int i = 0; i < B_TERMS; ++i) tma_prefetch_desc(&p.b_map[i]);
   }
   __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint64_t* bar,
                                     uint8_t* a_dst, uint8_t* b_dst) {
     const int j0 = (kb + kb_begin(p, tl)) * S::BK;
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < AT; ++i)
       tma_load_4d(&p.a_map[i], bar, a_dst + i * S::A_TILE, j0, tl.mi * S::BM, tl.unit, 0);
     if (B_MN) {
       const int b = tl.unit / p.H, h = tl.unit - (tl.unit / p.H) * p.H;
@@ -160,12 +161,12 @@ struct GradQProb {
 // ------------------------------------------------------------------ grad-V pass ----
 // dV[b,hv][j][d] = sum over heads h sharing (b,hv) of sum_{i} Mt_h[j][i] dO_h[i][d],
 // Mt = M^T as a hi/lo pair ([units][T][ldp], rows j). Keys i < j-block start are all zero.
-template <int ELEM, int STAGES>
+template <int ELEM, int STAGES, int AT = 2>
 struct GradVProb {
   static constexpr int BN = ELEM == 2 ? 256 : 128;
   static constexpr bool B_MN = ELEM == 2;
   static constexpr int B_TERMS = ELEM == 2 ? 1 : 2;
-  using S = TcShape<ELEM, BN, false, B_MN, 2, B_TERMS, STAGES, ELEM == 4 ? 8 : 0>;
+  using S = TcShape<ELEM, BN, false, B_MN, AT, B_TERMS, STAGES, ELEM == 4 ? 8 : 0>;
   static constexpr int CHUNK = 128 / ELEM;
   struct Params {
     CUtensorMap a_map[2];  // Mt hi/lo over [units][T][T(ldp)], box BK x 128
@@ -198,8 +199,7 @@ struct GradVProb {
   __device__ static int k_blocks(const Params& p, const Tile& tl) { return heads(p) * per_head(p, tl); }
   __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x7u; }
   __device__ static void prefetch(const Params& p) {
-    tma_prefetch_desc(&p.a_map[0]);
-    tma_prefetch_desc(&p.a_map[1]);
+    for (int i = 0; i < AT; ++i) tma_prefetch_desc(&p.a_map[i]);
     for (int i = 0; i < B_TERMS; ++i) tma_prefetch_desc(&p.b_map[i]);
   }
   __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint64_t* bar,
@@ -210,7 +210,7 @@ struct GradVProb {
     const int b = tl.vunit / p.Hv, hv = tl.vunit - (tl.vunit / p.Hv) * p.Hv;
     const int h = heads(p) > 1 ? hh : hv;
     const int unit = b * p.H + h;
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < AT; ++i)
       tma_load_4d(&p.a_map[i], bar, a_dst + i * S::A_TILE, i0, tl.mi * S::BM, unit, 0);
     if (B_MN) {
 #pragma unroll
@@ -239,12 +239,13 @@ struct GradVProb {
 using GradQBf16 = GradQProb<2, 3>;
 
 // CTA-pair grad-Q pass: 256 (query rows) x 256 (latent columns) tiles; each CTA stages its 128
-// rows of the hi/lo score pair and its 128 columns of X (MN-major), and stores its 128 rows with
-// the single-CTA epilogue (including the RoPE adjoint).
-struct GradQPair {
+// rows of the score matrix (AT terms: hi/lo, or the single bf16 term) and its 128 columns of X
+// (MN-major), and stores its 128 rows with the single-CTA epilogue (including the RoPE adjoint).
+template <int AT, int STG>
+struct GradQPairT {
   using Base = GradQBf16;
   using Params = Base::Params;  // b_map box 64 x BK as in the single-CTA pass
-  using S = PairShape<false, true, 2, 1, 4>;
+  using S = PairShape<false, true, AT, 1, STG>;
   static constexpr int kEpiWarps = 8;  // the RoPE adjoint makes the epilogue long
   struct Tile {
     int unit, m, n;
@@ -267,18 +268,17 @@ struct GradQPair {
     const int end = p.krange == 1 ? ceil_div_d(min(p.T, (tl.m + 1) * 256), 64) : ceil_div_d(p.T, 64);
     return end - kb_begin(p, tl);
   }
-  __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x3u; }
+  __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return AT == 2 ? 0x3u : 0x1u; }
   __device__ static uint32_t stage_tx(const Params&, const Tile&, int) { return 2 * S::STAGE_BYTES; }
   __device__ static void prefetch(const Params& p) {
-    tma_prefetch_desc(&p.a_map[0]);
-    tma_prefetch_desc(&p.a_map[1]);
+    for (int i = 0; i < AT; ++i) tma_prefetch_desc(&p.a_map[i]);
     tma_prefetch_desc(&p.b_map[0]);
   }
   __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint32_t rank,
                                     uint32_t bar, uint8_t* a_dst, uint8_t* b_dst) {
     const int j0 = (kb + kb_begin(p, tl)) * 64;
     const int r128 = static_cast<int>(rank) * 128;
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < AT; ++i)
       tma_load_4d_pair(&p.a_map[i], bar, a_dst + i * S::A_TILE, j0, tl.m * 256 + r128, tl.unit, 0);
     const int b = tl.unit / p.H, h = tl.unit - (tl.unit / p.H) * p.H;
 #pragma unroll
@@ -294,6 +294,8 @@ struct GradQPair {
     Base::epilogue(p, t, row, c0, r);
   }
 };
+using GradQPair = GradQPairT<2, 4>;
+using GradQPair1 = GradQPairT<1, 6>;
 
 bool use_pairs_bwd() {
   static int on = [] {
@@ -303,7 +305,9 @@ bool use_pairs_bwd() {
   return on != 0;
 }
 using GradQTf32 = GradQProb<4, 3>;
+using GradQBf16One = GradQProb<2, 4, 1>;
 using GradVBf16 = GradVProb<2, 3>;
+using GradVBf16One = GradVProb<2, 4, 1>;
 using GradVTf32 = GradVProb<4, 3>;
 
 bool out_vec_ok(const void* p, const int64_t s[4], int esz) {
@@ -321,7 +325,9 @@ int launch_grad_q(const GradQArgs& a, cudaStream_t stream, int* err) {
     const int64_t gd[4] = {a.T, a.T, units, 1};
     const int64_t gs[3] = {ldp * elem, a.T * ldp * elem, units * a.T * ldp * elem};
     if (!make_map_4d(&prm.a_map[0], a.g_hi, elem, gd, gs, bk, 128, "grad-q pass: score hi")) return false;
-    if (!make_map_4d(&prm.a_map[1], a.g_lo, elem, gd, gs, bk, 128, "grad-q pass: score lo")) return false;
+    if (a.g_lo != nullptr &&
+        !make_map_4d(&prm.a_map[1], a.g_lo, elem, gd, gs, bk, 128, "grad-q pass: score lo"))
+      return false;
     if (elem == 2) {
       int64_t xd[4] = {a.N, a.T, a.H, a.B};
       int64_t xs[3] = {a.x_strides[2] * 2, a.x_strides[1] * 2, a.x_strides[0] * 2};
@@ -351,11 +357,23 @@ int launch_grad_q(const GradQArgs& a, cudaStream_t stream, int* err) {
     prm.err = err;
     return true;
   };
+  if (elem != 2 && a.g_lo == nullptr) {
+    set_error("grad-q pass: the fp32 path needs the tf32 hi/lo score pair");
+    return BDH_ERR_INVALID;
+  }
+  const bool one = a.g_lo == nullptr;  // bf16 path: Gs is one bf16 term
   if (elem == 2 && use_pairs_bwd()) {
     GradQPair::Params prm{};
     if (!fill(prm, GradQBf16::S::BK, GradQBf16::BN)) return BDH_ERR_INVALID;
     const int tiles = prm.units * static_cast<int>((a.T + 255) / 256) * prm.nn;
-    return launch_pair<GradQPair::S, GradQPair>(prm, tiles, stream, kProfGradQ);
+    return one ? launch_pair<GradQPair1::S, GradQPair1>(prm, tiles, stream, kProfGradQ)
+               : launch_pair<GradQPair::S, GradQPair>(prm, tiles, stream, kProfGradQ);
+  }
+  if (elem == 2 && one) {
+    GradQBf16One::Params prm{};
+    if (!fill(prm, GradQBf16One::S::BK, GradQBf16One::BN)) return BDH_ERR_INVALID;
+    return launch_tc<GradQBf16One::S, GradQBf16One>(prm, prm.units * prm.mt * prm.nn, stream,
+                                                    kProfGradQ);
   }
   if (elem == 2) {
     GradQBf16::Params prm{};
@@ -375,7 +393,9 @@ int launch_grad_v(const GradVArgs& a, cudaStream_t stream, int* err) {
     const int64_t md[4] = {a.T, a.T, units, 1};
     const int64_t ms[3] = {ldp * elem, a.T * ldp * elem, units * a.T * ldp * elem};
     if (!make_map_4d(&prm.a_map[0], a.mt_hi, elem, md, ms, bk, 128, "grad-v pass: M^T hi")) return false;
-    if (!make_map_4d(&prm.a_map[1], a.mt_lo, elem, md, ms, bk, 128, "grad-v pass: M^T lo")) return false;
+    if (a.mt_lo != nullptr &&
+        !make_map_4d(&prm.a_map[1], a.mt_lo, elem, md, ms, bk, 128, "grad-v pass: M^T lo"))
+      return false;
     if (elem == 2) {
       int64_t dd[4] = {a.D, a.T, a.H, a.B};
       int64_t ds[3] = {a.do_strides[2] * 2, a.do_strides[1] * 2, a.do_strides[0] * 2};
@@ -403,6 +423,16 @@ int launch_grad_v(const GradVArgs& a, cudaStream_t stream, int* err) {
     prm.err = err;
     return true;
   };
+  if (elem != 2 && a.mt_lo == nullptr) {
+    set_error("grad-v pass: the fp32 path needs the tf32 hi/lo score pair");
+    return BDH_ERR_INVALID;
+  }
+  if (elem == 2 && a.mt_lo == nullptr) {
+    GradVBf16One::Params prm{};
+    if (!fill(prm, GradVBf16One::S::BK, GradVBf16One::BN)) return BDH_ERR_INVALID;
+    return launch_tc<GradVBf16One::S, GradVBf16One>(prm, prm.vunits * prm.mt * prm.nd, stream,
+                                                    kProfGradV);
+  }
   if (elem == 2) {
     GradVBf16::Params prm{};
     if (!fill(prm, GradVBf16::S::BK, GradVBf16::BN)) return BDH_ERR_INVALID;

@@ -3,17 +3,19 @@
 //   out[c-th chunk rows] = tril(Q_c K_c^T, -1) V_c  +  Q_c S_{c-1},   S_c = sum_{c' <= c} K_c'^T V_c'
 //
 // with chunks of C keys. Work per (b,h) unit drops from T(T-1)(N+D) to about
-// T(C-1)(N+D) + 4 T N D flops (for T = 8192, C = 256: 86 instead of 553 GFLOP), at the cost of
-// streaming the N x D prefix states (bf16 hi/lo, 4 bytes per element) through HBM once written,
-// once read. C is 256 below T = 4096 and 512 from there on (chunk_len): the longer chunk doubles
+// T(C-1)(N+D) + 2 T N D flops (for T = 8192, C = 256: 52 instead of 567 GFLOP), at the cost of
+// streaming the N x D prefix states through HBM once written, once read (one bf16 term by
+// default, 2 bytes per element; bf16 hi/lo with BDH_SM100_SPLIT_SCORES=1, which doubles the
+// inter-chunk product and its bytes). C is 256 below T = 4096 and 512 from there on
+// (chunk_len): the longer chunk doubles
 // the intra-chunk score work but halves the prefix-state traffic, which bounds the state and
 // value passes at long T (BDH_SM100_CHUNK=256|512 forces one).
 //
 // Three persistent tcgen05 passes (tc_engine.cuh):
 //   1. score pass restricted to each 128-row block's own chunk (score_pass.cuh, chunk > 0),
-//      P stored per row relative to the chunk start: [u][T][C] hi/lo;
+//      P stored per row relative to the chunk start: [u][T][C] (bf16, or hi/lo);
 //   2. state pass: S = K^T V accumulated over keys in chunk-sized accumulation rounds; after
-//      each chunk the running fp32 sum (in registers) is written as the bf16 hi/lo prefix
+//      each chunk the running fp32 sum (in registers) is written as the bf16 (or hi/lo) prefix
 //      S_c ([u][chunk][N][D]) used by the next chunk; operands read MN-major straight from the
 //      latents (keys are the contraction dimension);
 //   3. chunk value pass: per 128-row block, K-segment 1 = intra-chunk P V, K-segment 2 = Q S_{c-1}
@@ -45,15 +47,17 @@ int forced_chunk() {
 
 // ------------------------------------------------------------------- state pass ----
 // Each tile is a 128 (latent) x 128 (value) block of the N x D state; its epilogue emits one
-// bf16 hi/lo prefix per chunk (64 KB per tile per chunk), so the pass is bound by HBM writes.
+// bf16 prefix per chunk (32 KB per tile per chunk, 64 KB as hi/lo), so the pass is bound by HBM
+// writes.
 // Every epilogue warp stages its 32 rows in shared memory in the 128B-swizzled layout of the
 // store tensor map and writes them with four TMA bulk stores (whole 128-byte lines), then
 // reuses the staging once the previous chunk's stores have read it.
-template <int STAGES, int CKB>  // CKB = k-blocks (64 keys) per chunk
+// ST = 2: S as bf16 hi + lo; ST = 1: S as one bf16 term.
+template <int STAGES, int CKB, int ST = 2>  // CKB = k-blocks (64 keys) per chunk
 struct StateProb {
   using S = TcShape<2, 128, true, true, 1, 1, STAGES, CKB>;
   static constexpr int kEmitEveryChunk = 1;
-  static constexpr int kWarpStage = 4 * 32 * 128;  // hi/lo x two 64-column boxes x 32 rows
+  static constexpr int kWarpStage = 2 * ST * 32 * 128;  // terms x two 64-column boxes x 32 rows
   static constexpr int kEpiSmemBytes = 4 * kWarpStage;
   struct Params {
     CUtensorMap a_map[1];  // K (B,H,T,N) read MN-major: box 64 (n) x 64 (t)
@@ -117,11 +121,11 @@ struct StateProb {
       for (int e = 0; e < 4; ++e) {
         const float x0 = __uint_as_float(r[8 * v + 2 * e]), x1 = __uint_as_float(r[8 * v + 2 * e + 1]);
         wh[e] = cvt_bf16x2(x0, x1);
-        wl[e] = cvt_bf16x2(x0 - bf16x2_lo(wh[e]), x1 - bf16x2_hi(wh[e]));
+        if (ST == 2) wl[e] = cvt_bf16x2(x0 - bf16x2_lo(wh[e]), x1 - bf16x2_hi(wh[e]));
       }
       const int sw = ((j0 + v) ^ (lr & 7)) << 4;
       *reinterpret_cast<uint4*>(hi_row + sw) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
-      *reinterpret_cast<uint4*>(lo_row + sw) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+      if (ST == 2) *reinterpret_cast<uint4*>(lo_row + sw) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
     }
     if (c0 + 32 == S::BN) {
       fence_async_smem();
@@ -133,7 +137,7 @@ struct StateProb {
           const int x = tl.di * 128 + hb * 64;
           if (x < p.D) {
             tma_store_4d(&p.s_map[0], st + hb * 4096, x, n0, ch + 1, tl.unit);
-            tma_store_4d(&p.s_map[1], st + (2 + hb) * 4096, x, n0, ch + 1, tl.unit);
+            if (ST == 2) tma_store_4d(&p.s_map[1], st + (2 + hb) * 4096, x, n0, ch + 1, tl.unit);
           }
         }
         bulk_commit();
@@ -147,10 +151,11 @@ struct StateProb {
 };
 
 // -------------------------------------------------------------- chunk value pass ----
-template <int STAGES>
+// ONE: P and S as one bf16 term each (one product per k-block in both segments).
+template <int STAGES, bool ONE = false>
 struct ChunkValueProb {
   static constexpr int BN = 128;
-  using S = TcShape<2, BN, false, true, 2, 2, STAGES>;
+  using S = TcShape<2, BN, false, true, ONE ? 1 : 2, ONE ? 1 : 2, STAGES>;
   static constexpr int kVarStageTx = 1;
   struct Params {
     CUtensorMap p_map[2];  // P hi/lo over [units][T][C], box 64 x 128
@@ -187,20 +192,22 @@ struct ChunkValueProb {
     return cs(p, tl) > 0 ? ceil_div_d(p.N, 64) : 0;
   }
   __device__ static int k_blocks(const Params& p, const Tile& tl) { return n_intra(p, tl) + n_inter(p, tl); }
-  // intra: A0 A1 (P hi, lo) x B0 (V); inter: A0 (Q) x B0 B1 (S hi, lo)
+  // intra: A0 A1 (P hi, lo) x B0 (V); inter: A0 (Q) x B0 B1 (S hi, lo); ONE: A0 x B0 in both
   __device__ static uint32_t pair_mask(const Params& p, const Tile& tl, int kb) {
+    if (ONE) return 0x1u;
     return kb < n_intra(p, tl) ? 0x3u : 0x5u;
   }
   __device__ static uint32_t stage_tx(const Params& p, const Tile& tl, int kb) {
+    if (ONE) return S::A_TILE + S::B_TILE;
     return kb < n_intra(p, tl) ? 2 * S::A_TILE + S::B_TILE : S::A_TILE + 2 * S::B_TILE;
   }
   __device__ static void prefetch(const Params& p) {
     tma_prefetch_desc(&p.p_map[0]);
-    tma_prefetch_desc(&p.p_map[1]);
+    if (!ONE) tma_prefetch_desc(&p.p_map[1]);
     tma_prefetch_desc(&p.v_map);
     tma_prefetch_desc(&p.q_map);
     tma_prefetch_desc(&p.s_map[0]);
-    tma_prefetch_desc(&p.s_map[1]);
+    if (!ONE) tma_prefetch_desc(&p.s_map[1]);
   }
   __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint64_t* bar,
                                     uint8_t* a_dst, uint8_t* b_dst) {
@@ -208,7 +215,7 @@ struct ChunkValueProb {
     const int ni = n_intra(p, tl);
     if (kb < ni) {
       const int hv = p.Hv == 1 ? 0 : h;
-      for (int i = 0; i < 2; ++i)
+      for (int i = 0; i < (ONE ? 1 : 2); ++i)
         tma_load_4d(&p.p_map[i], bar, a_dst + i * S::A_TILE, kb * 64, tl.mi * 128, tl.unit, 0);
 #pragma unroll
       for (int c = 0; c < 2; ++c)
@@ -217,7 +224,7 @@ struct ChunkValueProb {
       const int n0 = (kb - ni) * 64;
       const int chunk = cs(p, tl) / p.chunk;
       tma_load_4d(&p.q_map, bar, a_dst, n0, tl.mi * 128, h, b);
-      for (int i = 0; i < 2; ++i)
+      for (int i = 0; i < (ONE ? 1 : 2); ++i)
 #pragma unroll
         for (int c = 0; c < 2; ++c)
           tma_load_4d(&p.s_map[i], bar, b_dst + i * S::B_TILE + c * 64 * 128, tl.ni * BN + c * 64,
@@ -260,10 +267,11 @@ struct ChunkValueProb {
 // bound by L2 -> shared memory ingress). The intra segment of a pair tile covers the keys from
 // its chunk's start to the tile's last row; P holds zeros above the diagonal there (the pair
 // score pass stores whole 256-key tiles).
-struct ChunkValuePair {
-  using Base = ChunkValueProb<3>;
-  using Params = Base::Params;
-  using S = PairShape<false, true, 2, 2, 3>;
+template <bool ONE>
+struct ChunkValuePairT {
+  using Base = ChunkValueProb<ONE ? 4 : 3, ONE>;  // parameters and epilogue
+  using Params = typename Base::Params;
+  using S = PairShape<false, true, ONE ? 1 : 2, ONE ? 1 : 2, ONE ? 6 : 3>;
   struct Tile {
     int unit, c, n;  // c: 256-row pair tile of the unit
   };
@@ -288,9 +296,11 @@ struct ChunkValuePair {
   }
   __device__ static int k_blocks(const Params& p, const Tile& tl) { return n_intra(p, tl) + n_inter(p, tl); }
   __device__ static uint32_t pair_mask(const Params& p, const Tile& tl, int kb) {
+    if (ONE) return 0x1u;
     return kb < n_intra(p, tl) ? 0x3u : 0x5u;
   }
   __device__ static uint32_t stage_tx(const Params& p, const Tile& tl, int kb) {
+    if (ONE) return 2u * (S::A_TILE + S::B_TILE);
     return 2u * (kb < n_intra(p, tl) ? 2 * S::A_TILE + S::B_TILE : S::A_TILE + 2 * S::B_TILE);
   }
   __device__ static void prefetch(const Params& p) { Base::prefetch(p); }
@@ -304,7 +314,7 @@ struct ChunkValuePair {
     const int ni = n_intra(p, tl);
     if (kb < ni) {
       const int hv = p.Hv == 1 ? 0 : h;
-      for (int i = 0; i < 2; ++i)
+      for (int i = 0; i < (ONE ? 1 : 2); ++i)
         tma_load_4d_pair(&p.p_map[i], bar, a_dst + i * S::A_TILE, kb * 64, row0, tl.unit, 0);
 #pragma unroll
       for (int c = 0; c < 2; ++c)
@@ -313,7 +323,7 @@ struct ChunkValuePair {
     } else {
       const int n0 = (kb - ni) * 64;
       tma_load_4d_pair(&p.q_map, bar, a_dst, n0, row0, h, b);
-      for (int i = 0; i < 2; ++i)
+      for (int i = 0; i < (ONE ? 1 : 2); ++i)
 #pragma unroll
         for (int c = 0; c < 2; ++c)
           tma_load_4d_pair(&p.s_map[i], bar, b_dst + i * S::B_TILE + c * 64 * 128, col0 + c * 64, n0,
@@ -322,13 +332,15 @@ struct ChunkValuePair {
   }
   __device__ static void epilogue(const Params& p, const Tile& tl, int rank, int row, int c0,
                                   const uint32_t (&r)[32]) {
-    Base::Tile t;
+    typename Base::Tile t;
     t.unit = tl.unit;
     t.mi = 2 * tl.c + rank;
     t.ni = 2 * tl.n;  // Base columns: ni * 128 + c0 with c0 in [0, 256)
     Base::epilogue(p, t, row, c0, r);
   }
 };
+using ChunkValuePair = ChunkValuePairT<false>;
+using ChunkValuePairOne = ChunkValuePairT<true>;
 
 bool use_pairs_chunked() {
   static int on = [] {
@@ -340,7 +352,8 @@ bool use_pairs_chunked() {
 
 using StateBf16C256 = StateProb<4, 4>;
 using StateBf16C512 = StateProb<4, 8>;
-using ChunkValueBf16 = ChunkValueProb<3>;
+using StateBf16C256One = StateProb<4, 4, 1>;
+using StateBf16C512One = StateProb<4, 8, 1>;
 
 }  // namespace
 
@@ -382,9 +395,62 @@ int launch_state_pass(const FwdArgs& a, void* s_hi, void* s_lo, int nchunks, cud
   const int64_t sd[4] = {a.D, a.N, nchunks, a.B * a.H};
   const int64_t ss[3] = {a.D * 2, a.N * a.D * 2, int64_t(nchunks) * a.N * a.D * 2};
   if (!make_map_4d(&prm.s_map[0], s_hi, 2, sd, ss, 64, 32, "state pass: S hi")) return BDH_ERR_INVALID;
-  if (!make_map_4d(&prm.s_map[1], s_lo, 2, sd, ss, 64, 32, "state pass: S lo")) return BDH_ERR_INVALID;
+  if (s_lo != nullptr && !make_map_4d(&prm.s_map[1], s_lo, 2, sd, ss, 64, 32, "state pass: S lo"))
+    return BDH_ERR_INVALID;
   prm.err = err;
   return launch_tc<typename SP::S, SP>(prm, prm.units * prm.nn * prm.nd, stream, kProfState);
+}
+
+// 3. intra P V + inter Q S (ONE: P and S as one bf16 term each).
+template <bool ONE>
+int launch_chunk_value(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi, void* s_lo, int C,
+                       int nchunks, cudaStream_t stream, int* err) {
+  using CP = ChunkValuePairT<ONE>;
+  using CV = typename CP::Base;
+  const int64_t units = a.B * a.H;
+  typename CP::Params prm{};
+  const int64_t pd[4] = {C, a.T, units, 1};
+  const int64_t ps[3] = {int64_t(C) * 2, a.T * C * 2, units * a.T * C * 2};
+  if (!make_map_4d(&prm.p_map[0], p_hi, 2, pd, ps, 64, 128, "chunk value pass: P hi")) return BDH_ERR_INVALID;
+  if (!ONE && !make_map_4d(&prm.p_map[1], p_lo, 2, pd, ps, 64, 128, "chunk value pass: P lo"))
+    return BDH_ERR_INVALID;
+  const int64_t vd[4] = {a.D, a.T, a.Hv, a.B};
+  const int64_t vs[3] = {a.v_strides[2] * 2, a.v_strides[1] * 2, a.v_strides[0] * 2};
+  if (!make_map_4d(&prm.v_map, a.v, 2, vd, vs, 64, 64, "chunk value pass: V")) return BDH_ERR_INVALID;
+  const int64_t qd[4] = {a.N, a.T, a.H, a.B};
+  const int64_t qs[3] = {a.q_strides[2] * 2, a.q_strides[1] * 2, a.q_strides[0] * 2};
+  if (!make_map_4d(&prm.q_map, a.q, 2, qd, qs, 64, 128, "chunk value pass: Q")) return BDH_ERR_INVALID;
+  const int64_t sd[4] = {a.D, a.N, nchunks, units};
+  const int64_t ss[3] = {a.D * 2, a.N * a.D * 2, int64_t(nchunks) * a.N * a.D * 2};
+  if (!make_map_4d(&prm.s_map[0], s_hi, 2, sd, ss, 64, 64, "chunk value pass: S hi")) return BDH_ERR_INVALID;
+  if (!ONE && !make_map_4d(&prm.s_map[1], s_lo, 2, sd, ss, 64, 64, "chunk value pass: S lo"))
+    return BDH_ERR_INVALID;
+  prm.H = static_cast<int>(a.H);
+  prm.Hv = static_cast<int>(a.Hv);
+  prm.T = static_cast<int>(a.T);
+  prm.N = static_cast<int>(a.N);
+  prm.D = static_cast<int>(a.D);
+  prm.mt = static_cast<int>((a.T + 127) / 128);
+  prm.nd = static_cast<int>((a.D + CV::BN - 1) / CV::BN);
+  prm.units = static_cast<int>(units);
+  prm.nchunks = nchunks;
+  prm.chunk = C;
+  prm.out = a.out;
+  prm.os_b = a.out_strides[0];
+  prm.os_h = a.out_strides[1];
+  prm.os_t = a.out_strides[2];
+  prm.out_f32 = a.out_dtype == BDH_DTYPE_F32 ? 1 : 0;
+  const int oes = prm.out_f32 ? 4 : 2;
+  prm.vec_ok = ((reinterpret_cast<uintptr_t>(a.out) & 15u) == 0 && (a.out_strides[0] * oes) % 16 == 0 &&
+                (a.out_strides[1] * oes) % 16 == 0 && (a.out_strides[2] * oes) % 16 == 0)
+                   ? 1
+                   : 0;
+  prm.err = err;
+  if (use_pairs_chunked()) {
+    const int tiles = prm.units * static_cast<int>((a.T + 255) / 256) * static_cast<int>((a.D + 255) / 256);
+    return launch_pair<typename CP::S, CP>(prm, tiles, stream, kProfValue);
+  }
+  return launch_tc<typename CV::S, CV>(prm, prm.units * prm.mt * prm.nd, stream, kProfValue);
 }
 }  // namespace
 
@@ -394,7 +460,12 @@ int launch_chunked_forward(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi,
     set_error("chunked forward: bf16 inputs only");
     return BDH_ERR_INVALID;
   }
-  const int64_t units = a.B * a.H;
+  // p_lo / s_lo null: P and the prefix states as one bf16 term each
+  const bool one = p_lo == nullptr || s_lo == nullptr;
+  if (one && (p_lo != nullptr || s_lo != nullptr)) {
+    set_error("chunked forward: P and S are both split or both single bf16 terms");
+    return BDH_ERR_INVALID;
+  }
   const int C = chunk_len(a.T);
   const int nchunks = static_cast<int>((a.T + C - 1) / C);
   // 1. intra-chunk scores
@@ -415,53 +486,17 @@ int launch_chunked_forward(const FwdArgs& a, void* p_hi, void* p_lo, void* s_hi,
   if (rc) return rc;
   // 2. prefix states S_1 .. S_{nchunks-1}
   if (nchunks > 1) {
-    rc = C == 512 ? launch_state_pass<StateBf16C512>(a, s_hi, s_lo, nchunks, stream, err)
-                  : launch_state_pass<StateBf16C256>(a, s_hi, s_lo, nchunks, stream, err);
+    if (one)
+      rc = C == 512 ? launch_state_pass<StateBf16C512One>(a, s_hi, nullptr, nchunks, stream, err)
+                    : launch_state_pass<StateBf16C256One>(a, s_hi, nullptr, nchunks, stream, err);
+    else
+      rc = C == 512 ? launch_state_pass<StateBf16C512>(a, s_hi, s_lo, nchunks, stream, err)
+                    : launch_state_pass<StateBf16C256>(a, s_hi, s_lo, nchunks, stream, err);
     if (rc) return rc;
   }
   // 3. intra P V + inter Q S
-  ChunkValueBf16::Params prm{};
-  const int64_t pd[4] = {C, a.T, units, 1};
-  const int64_t ps[3] = {int64_t(C) * 2, a.T * C * 2, units * a.T * C * 2};
-  if (!make_map_4d(&prm.p_map[0], p_hi, 2, pd, ps, 64, 128, "chunk value pass: P hi")) return BDH_ERR_INVALID;
-  if (!make_map_4d(&prm.p_map[1], p_lo, 2, pd, ps, 64, 128, "chunk value pass: P lo")) return BDH_ERR_INVALID;
-  const int64_t vd[4] = {a.D, a.T, a.Hv, a.B};
-  const int64_t vs[3] = {a.v_strides[2] * 2, a.v_strides[1] * 2, a.v_strides[0] * 2};
-  if (!make_map_4d(&prm.v_map, a.v, 2, vd, vs, 64, 64, "chunk value pass: V")) return BDH_ERR_INVALID;
-  const int64_t qd[4] = {a.N, a.T, a.H, a.B};
-  const int64_t qs[3] = {a.q_strides[2] * 2, a.q_strides[1] * 2, a.q_strides[0] * 2};
-  if (!make_map_4d(&prm.q_map, a.q, 2, qd, qs, 64, 128, "chunk value pass: Q")) return BDH_ERR_INVALID;
-  const int64_t sd[4] = {a.D, a.N, nchunks, units};
-  const int64_t ss[3] = {a.D * 2, a.N * a.D * 2, int64_t(nchunks) * a.N * a.D * 2};
-  if (!make_map_4d(&prm.s_map[0], s_hi, 2, sd, ss, 64, 64, "chunk value pass: S hi")) return BDH_ERR_INVALID;
-  if (!make_map_4d(&prm.s_map[1], s_lo, 2, sd, ss, 64, 64, "chunk value pass: S lo")) return BDH_ERR_INVALID;
-  prm.H = static_cast<int>(a.H);
-  prm.Hv = static_cast<int>(a.Hv);
-  prm.T = static_cast<int>(a.T);
-  prm.N = static_cast<int>(a.N);
-  prm.D = static_cast<int>(a.D);
-  prm.mt = static_cast<int>((a.T + 127) / 128);
-  prm.nd = static_cast<int>((a.D + ChunkValueBf16::BN - 1) / ChunkValueBf16::BN);
-  prm.units = static_cast<int>(units);
-  prm.nchunks = nchunks;
-  prm.chunk = C;
-  prm.out = a.out;
-  prm.os_b = a.out_strides[0];
-  prm.os_h = a.out_strides[1];
-  prm.os_t = a.out_strides[2];
-  prm.out_f32 = a.out_dtype == BDH_DTYPE_F32 ? 1 : 0;
-  const int oes = prm.out_f32 ? 4 : 2;
-  prm.vec_ok = ((reinterpret_cast<uintptr_t>(a.out) & 15u) == 0 && (a.out_strides[0] * oes) % 16 == 0 &&
-                (a.out_strides[1] * oes) % 16 == 0 && (a.out_strides[2] * oes) % 16 == 0)
-                   ? 1
-                   : 0;
-  prm.err = err;
-  if (use_pairs_chunked()) {
-    const int tiles = prm.units * static_cast<int>((a.T + 255) / 256) * static_cast<int>((a.D + 255) / 256);
-    return launch_pair<ChunkValuePair::S, ChunkValuePair>(prm, tiles, stream, kProfValue);
-  }
-  return launch_tc<ChunkValueBf16::S, ChunkValueBf16>(prm, prm.units * prm.mt * prm.nd, stream,
-                                                       kProfValue);
+  return one ? launch_chunk_value<true>(a, p_hi, p_lo, s_hi, s_lo, C, nchunks, stream, err)
+             : launch_chunk_value<false>(a, p_hi, p_lo, s_hi, s_lo, C, nchunks, stream, err);
 }
 
 }  // namespace bdh

@@ -5,7 +5,8 @@
 //   1. score pass : P = tril(Q K^T, -1) over the lower-triangular 128 x BN tiles, K-loop
 //                   over the latent width N. P is written once as an exact split pair
 //                   (bf16 hi + bf16 lo, or tf32 hi + fp32 lo for fp32 inputs) so that the
-//                   second pass keeps fp32-level accuracy on tensor cores.
+//                   second pass keeps fp32-level accuracy on tensor cores
+//                   (BDH_SM100_SPLIT_SCORES=0: P as one bf16 term, the reference's rounding).
 //   2. value pass : out = P V with the K-loop over keys limited to the causal prefix of each
 //                   128-row query block (longest blocks scheduled first).
 // Semantics follow the reference kernels (csrc/tril_attn_cuda.cu:129-249) and eager path
@@ -27,12 +28,12 @@ namespace bdh {
 // A = P (K-major over keys, hi/lo terms).
 // ELEM 2: B = V as stored, MN-major (D contiguous); bf16 P hi/lo x bf16 V (2 products).
 // ELEM 4: B = V^T hi/lo written by the tf32 split (K-major, keys contiguous); 3 products.
-template <int ELEM, int STAGES>
+template <int ELEM, int STAGES, int AT = 2>  // AT = 1: P as one bf16 term
 struct ValueProb {
   static constexpr int BN = ELEM == 2 ? 256 : 128;
   static constexpr bool B_MN = ELEM == 2;
   static constexpr int B_TERMS = ELEM == 2 ? 1 : 2;
-  using S = TcShape<ELEM, BN, false, B_MN, 2, B_TERMS, STAGES, ELEM == 4 ? 8 : 0>;
+  using S = TcShape<ELEM, BN, false, B_MN, AT, B_TERMS, STAGES, ELEM == 4 ? 8 : 0>;
   static constexpr int CHUNK = 128 / ELEM;  // MN elements per 128-byte chunk
   struct Params {
     CUtensorMap a_map[2];  // P hi / lo over [units][T][T], box BK x 128
@@ -66,15 +67,14 @@ struct ValueProb {
   }
   __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x7u; }
   __device__ static void prefetch(const Params& p) {
-    tma_prefetch_desc(&p.a_map[0]);
-    tma_prefetch_desc(&p.a_map[1]);
+    for (int i = 0; i < AT; ++i) tma_prefetch_desc(&p.a_map[i]);
     for (int i = 0; i < B_TERMS; ++i) tma_prefetch_desc(&p.b_map[i]);
   }
   __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint64_t* bar,
                                     uint8_t* a_dst, uint8_t* b_dst) {
     const int b = tl.unit / p.H, h = tl.unit - (tl.unit / p.H) * p.H;
     const int hv = p.Hv == 1 ? 0 : h;
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < AT; ++i)
       tma_load_4d(&p.a_map[i], bar, a_dst + i * S::A_TILE, kb * S::BK, tl.mi * S::BM, tl.unit, 0);
     if (B_MN) {
 #pragma unroll
@@ -204,6 +204,7 @@ int score_tile_n() {
 }
 using ScoreTf32 = ScoreProb<4, 128, 3>;
 using ValueBf16 = ValueProb<2, 3>;
+using ValueBf16One = ValueProb<2, 4, 1>;
 using ValueTf32 = ValueProb<4, 3>;
 
 // One row of the fp32 score pair from its K-split partials: columns of the row's stored tiles
@@ -367,7 +368,7 @@ int launch_score(const FwdArgs& a, void* p_hi, void* p_lo, float* part, cudaStre
   return launch_score_pass(s, stream, err);
 }
 
-// Value pass: out = P V from the hi/lo score pair.
+// Value pass: out = P V from the hi/lo score pair (bf16: p_lo null = P as one bf16 term).
 int launch_value(const FwdArgs& a, const void* p_hi, const void* p_lo, cudaStream_t stream,
                  int* err) {
   const int elem = a.dtype == BDH_DTYPE_F32 ? 4 : 2;
@@ -377,7 +378,8 @@ int launch_value(const FwdArgs& a, const void* p_hi, const void* p_lo, cudaStrea
     const int64_t pd[4] = {a.T, a.T, units, 1};
     const int64_t ps[3] = {ldp * elem, a.T * ldp * elem, units * a.T * ldp * elem};
     if (!make_map_4d(&prm.a_map[0], p_hi, elem, pd, ps, bk, 128, "value pass: P hi")) return false;
-    if (!make_map_4d(&prm.a_map[1], p_lo, elem, pd, ps, bk, 128, "value pass: P lo")) return false;
+    if (p_lo != nullptr && !make_map_4d(&prm.a_map[1], p_lo, elem, pd, ps, bk, 128, "value pass: P lo"))
+      return false;
     if (elem == 2) {
       int64_t vd[4] = {a.D, a.T, a.Hv, a.B};
       int64_t vs[3] = {a.v_strides[2] * elem, a.v_strides[1] * elem, a.v_strides[0] * elem};
@@ -411,6 +413,16 @@ int launch_value(const FwdArgs& a, const void* p_hi, const void* p_lo, cudaStrea
     prm.err = err;
     return true;
   };
+  if (elem != 2 && p_lo == nullptr) {
+    set_error("value pass: the fp32 path needs the tf32 hi/lo score pair");
+    return BDH_ERR_INVALID;
+  }
+  if (elem == 2 && p_lo == nullptr) {
+    ValueBf16One::Params prm{};
+    if (!fill(prm, ValueBf16One::S::BK, ValueBf16One::BN)) return BDH_ERR_INVALID;
+    return launch_tc<ValueBf16One::S, ValueBf16One>(prm, prm.units * prm.mt * prm.nd, stream,
+                                                    kProfValue);
+  }
   if (elem == 2) {
     ValueBf16::Params prm{};
     if (!fill(prm, ValueBf16::S::BK, ValueBf16::BN)) return BDH_ERR_INVALID;

@@ -1,6 +1,7 @@
 // extern "C" boundary of libbdh_sm100.so: argument validation, workspace carving and kernel
 // sequencing. No torch types cross this boundary and nothing here allocates device memory.
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <sstream>
 #include <string>
@@ -47,12 +48,37 @@ bool use_chunked(int dtype, int64_t T) {
   return T >= 1536;
 }
 
+// bf16 inputs: which score-like operands enter their tensor-core passes as one bf16 term (fp32
+// sums rounded once to bf16, as the reference's bf16 matmul chain rounds P = Q K^T and
+// dM = dO V^T before the next product: kernels/attention.py:27-40,
+// kernels/attention_bwd.py:72-78) instead of an exact bf16 hi + lo split (twice the tensor work
+// of the products that consume them, and twice their bytes). Default: the chunked forward's P
+// and prefix states S and the backward's dS / G and M^T are one term; the quadratic forward's P
+// stays split (its product is a small share of the forward). BDH_SM100_SPLIT_SCORES=1 splits
+// every one of them, =0 none. The fp32 path always uses the tf32 hi/lo split.
+enum ScoreTerms { kTermsDefault = -1, kTermsOne = 0, kTermsSplit = 1 };
+int bf16_score_terms_env() {
+  static const int v = [] {
+    const char* e = std::getenv("BDH_SM100_SPLIT_SCORES");
+    if (e == nullptr || *e == 0) return static_cast<int>(kTermsDefault);
+    return std::atoi(e) == 1 ? static_cast<int>(kTermsSplit) : static_cast<int>(kTermsOne);
+  }();
+  return v;
+}
+// One bf16 term for this operand? `split_by_default`: the operand is split unless forced.
+bool bf16_one_term(bool split_by_default) {
+  const int v = bf16_score_terms_env();
+  if (v == kTermsDefault) return !split_by_default;
+  return v == kTermsOne;
+}
+
 // Workspace layout of the forward (byte offsets), shared by the size query and the call.
 struct FwdLayout {
   size_t q_hi = 0, q_lo = 0, k_hi = 0, k_lo = 0, v_hi = 0, v_lo = 0, p_hi = 0, p_lo = 0;
   size_t s_hi = 0, s_lo = 0;
   size_t part = 0;  // fp32 K-split partials of the score pass (0 when not split)
   bool chunked = false;
+  bool one = false;  // bf16: P (and S) as one bf16 term, no lo buffers
   size_t total = 0;
 };
 
@@ -61,14 +87,17 @@ FwdLayout fwd_layout(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T, int
   FwdLayout L;
   size_t off = 0;
   const int e = esize(dtype);
-  if (use_chunked(dtype, T)) {
+  const bool chunked = use_chunked(dtype, T);
+  const bool one = dtype == BDH_DTYPE_BF16 && bf16_one_term(/*split_by_default=*/!chunked);
+  L.one = one;
+  if (chunked) {
     L.chunked = true;
     const size_t pb = align_up(chunked_p_bytes(B, H, T));
     const size_t sb = align_up(chunked_s_bytes(B, H, T, N, D));
     L.p_hi = off; off += pb;
-    L.p_lo = off; off += pb;
+    L.p_lo = off; off += one ? 0 : pb;
     L.s_hi = off; off += sb;
-    L.s_lo = off; off += sb;
+    L.s_lo = off; off += one ? 0 : sb;
     L.total = off;
     return L;
   }
@@ -86,7 +115,7 @@ FwdLayout fwd_layout(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T, int
   }
   const size_t pbytes = align_up(static_cast<size_t>(B * H * T * score_ld(T)) * e);
   L.p_hi = off; off += pbytes;
-  L.p_lo = off; off += pbytes;
+  L.p_lo = off; off += one ? 0 : pbytes;
   if (dtype == BDH_DTYPE_F32) {
     const int ks = score_ksplit_f32(B * H, T, N);
     if (ks > 1) {
@@ -117,11 +146,12 @@ BwdLayout bwd_layout(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T, int
     return o;
   };
   const size_t pbytes = static_cast<size_t>(B * H * T * score_ld(T)) * e;
+  const size_t lobytes = dtype == BDH_DTYPE_BF16 && bf16_one_term(false) ? 0 : pbytes;
   L.s1_hi = take(pbytes);
-  L.s1_lo = take(pbytes);
+  L.s1_lo = take(lobytes);
   if (!k_is_q) {
     L.s2_hi = take(pbytes);
-    L.s2_lo = take(pbytes);
+    L.s2_lo = take(lobytes);
   }
   if (dtype == BDH_DTYPE_F32) {
     const int64_t ldt = vt_ld(T);
@@ -528,12 +558,14 @@ int bdh_tril_score_v(const void* q, const int64_t q_strides[4], const void* k,
     std::memcpy(a.k_strides, k_strides, sizeof(a.k_strides));
     std::memcpy(a.v_strides, v_strides, sizeof(a.v_strides));
   }
+  void* p_lo = L.one ? nullptr : ws + L.p_lo;
   if (L.chunked)
-    return launch_chunked_forward(a, ws + L.p_hi, ws + L.p_lo, ws + L.s_hi, ws + L.s_lo, st, err);
-  int rc = launch_score(a, ws + L.p_hi, ws + L.p_lo,
+    return launch_chunked_forward(a, ws + L.p_hi, p_lo, ws + L.s_hi,
+                                  L.one ? nullptr : ws + L.s_lo, st, err);
+  int rc = launch_score(a, ws + L.p_hi, p_lo,
                         L.part ? reinterpret_cast<float*>(ws + L.part) : nullptr, st, err);
   if (rc) return rc;
-  return launch_value(a, ws + L.p_hi, ws + L.p_lo, st, err);
+  return launch_value(a, ws + L.p_hi, p_lo, st, err);
 }
 
 int bdh_set_forward_algo(int algo) {
@@ -705,8 +737,10 @@ int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* 
       if ((rc = split_t(k, k_strides, H, N, L.kt_hi, L.kt_lo, kT))) return rc;
     }
   }
+  const bool one = !f32 && bf16_one_term(false);
   void* g_hi = ws + L.s1_hi;
-  void* g_lo = ws + L.s1_lo;
+  void* g_lo = one ? nullptr : ws + L.s1_lo;
+  void* g2_lo = one ? nullptr : ws + L.s2_lo;
   // 1. dS = tril(dO V^T, -1) -> G (K is Q) or L / U.
   ScoreArgs sa;
   sa.elem = elem;
@@ -717,7 +751,7 @@ int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* 
   sa.B = B; sa.H = H; sa.Hb = Hv; sa.T = T; sa.K = D;
   sa.mode = k_is_q ? kStoreSym : kStoreLU;
   sa.p_hi = g_hi; sa.p_lo = g_lo;
-  sa.p2_hi = ws + L.s2_hi; sa.p2_lo = ws + L.s2_lo;
+  sa.p2_hi = ws + L.s2_hi; sa.p2_lo = g2_lo;
   if ((rc = launch_score_pass(sa, st, err))) return rc;
   // 2. dQ (and dK).
   GradQArgs ga;
@@ -740,7 +774,7 @@ int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* 
     std::memcpy(ga.x_strides, k_strides, sizeof(ga.x_strides));
     if ((rc = launch_grad_q(ga, st, err))) return rc;
     ga.krange = 2;
-    ga.g_hi = ws + L.s2_hi; ga.g_lo = ws + L.s2_lo;
+    ga.g_hi = ws + L.s2_hi; ga.g_lo = g2_lo;
     ga.x[0] = qT[0]; ga.x[1] = qT[1];
     std::memcpy(ga.x_strides, q_strides, sizeof(ga.x_strides));
     ga.out = dk;

@@ -9,7 +9,8 @@
 //   kStoreSym    : S + S^T at [u][i][j]                 (backward G = dS + dS^T, K is Q)
 //   kStoreLU     : S at out1[u][i][j], S^T at out2      (backward dS / dS^T, K distinct)
 // Transposed stores are coalesced across the warp: lanes own consecutive rows i, so for a
-// fixed column j the 32 lanes write 32 consecutive elements of row j of the transpose.
+// fixed column j the 32 lanes write 32 consecutive elements of row j of the transpose. A null
+// lo destination (bf16 only) stores the bf16-rounded scores alone.
 #pragma once
 
 #include <algorithm>
@@ -182,9 +183,10 @@ struct ScoreProb {
           *reinterpret_cast<uint4*>(dh + gj0) =
               make_uint4(hi[8 * v] | (hi[8 * v + 1] << 16), hi[8 * v + 2] | (hi[8 * v + 3] << 16),
                          hi[8 * v + 4] | (hi[8 * v + 5] << 16), hi[8 * v + 6] | (hi[8 * v + 7] << 16));
-          *reinterpret_cast<uint4*>(dl + gj0) =
-              make_uint4(lo[8 * v] | (lo[8 * v + 1] << 16), lo[8 * v + 2] | (lo[8 * v + 3] << 16),
-                         lo[8 * v + 4] | (lo[8 * v + 5] << 16), lo[8 * v + 6] | (lo[8 * v + 7] << 16));
+          if (p.p_lo != nullptr)
+            *reinterpret_cast<uint4*>(dl + gj0) =
+                make_uint4(lo[8 * v] | (lo[8 * v + 1] << 16), lo[8 * v + 2] | (lo[8 * v + 3] << 16),
+                           lo[8 * v + 4] | (lo[8 * v + 5] << 16), lo[8 * v + 6] | (lo[8 * v + 7] << 16));
         }
       } else {
         uint32_t* dh = static_cast<uint32_t*>(p.p_hi) + row_off;
@@ -205,7 +207,7 @@ struct ScoreProb {
         const int gj = gj_base + e;
         if (gj <= gi) {
           store1(p.p_hi, row_off + gj, hi[e]);
-          store1(p.p_lo, row_off + gj, lo[e]);
+          if (p.p_lo != nullptr) store1(p.p_lo, row_off + gj, lo[e]);
         }
       }
     }
@@ -220,7 +222,7 @@ struct ScoreProb {
         if (gj >= p.T || (strict && gj >= gi)) continue;
         const size_t idx = (unit_off + gj) * static_cast<size_t>(p.ldp) + gi;
         store1(th, idx, hi[e]);
-        store1(tlo, idx, lo[e]);
+        if (tlo != nullptr) store1(tlo, idx, lo[e]);
       }
     }
   }

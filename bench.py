@@ -624,13 +624,19 @@ def chunk_len(T: int) -> int:
     return 512 if T >= 4096 else 256
 
 
+def state_terms() -> int:
+    """bf16 terms per prefix-state element of the chunked forward (csrc/capi.cu
+    bf16_one_term): one by default, hi + lo with BDH_SM100_SPLIT_SCORES=1."""
+    return 2 if os.environ.get("BDH_SM100_SPLIT_SCORES", "") == "1" else 1
+
+
 def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev, steps):
     """Roofline of the dominant kernel of an op config (algorithmic work per launch / time).
 
     * config 1 (fp32): score pass, causal Q K^T flops B H T(T-1) N against a measured cuBLAS
       TF32 GEMM peak (the pass issues 3 TF32 products per algorithmic product for fp32 accuracy);
-    * config 3 (chunked): prefix-state pass, HBM bytes = K and V read once + the bf16 hi/lo
-      prefix states written, (T/C - 1) N D 4 bytes per (b,h);
+    * config 3 (chunked): prefix-state pass, HBM bytes = K and V read once + the bf16 prefix
+      states written, (T/C - 1) N D 2 bytes per (b,h) (4 with the hi/lo split);
     * config 5: grad-Q pass, dQ_total = dS Q + dS^T Q, causal flops 2 T(T-1) N per (b,h).
     """
     B, H, T, N, D = shape
@@ -646,10 +652,12 @@ def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev, steps):
     elif cfg_id == 3 and chunked:
         k = prof["state"]
         C = chunk_len(T)
-        work = units * ((T // C - 1) * N * D * 4 + T * N * 2) + B * T * D * 2
+        st = state_terms()
+        work = units * ((T // C - 1) * N * D * 2 * st + T * N * 2) + B * T * D * 2
         peak, unit, bound = peaks["hbm_gbs"], "GB/s", "hbm"
         psrc = f"{src} hbm_gbs"
-        kern = "prefix-state pass (tc_gemm_kernel<StateProb>), bf16 hi/lo state writes"
+        kern = ("prefix-state pass (tc_gemm_kernel<StateProb>), bf16 "
+                + ("hi/lo" if st == 2 else "single-term") + " state writes")
         tname = "state_pass_config3"
     else:
         k = prof["grad_q"] if cfg_id == 5 else prof["score"]
@@ -706,12 +714,13 @@ def bench_op(args, world, rank, dev):
     ms = timed(step, args.steps, world, dev)
     prof = profile_end()
     clk = clocks.stop()
-    # executed-algorithm flops (per (b,h) unit): quadratic causal T(T-1)(N+D), or the chunked
-    # form (T/C) C(C-1)(N+D) + 4 (T-C) N D when the library takes it (bf16 and T >= 1536)
+    # executed-algorithm flops (per (b,h) unit, one product per multiply-add pair whatever the
+    # operand split): quadratic causal T(T-1)(N+D), or the chunked form
+    # (T/C) C(C-1)(N+D) + 2 (T-C) N D when the library takes it (bf16 and T >= 1536)
     C = chunk_len(T)
     chunked = dt == torch.bfloat16 and T >= 1536
     quad_fwd = B * H * T * (T - 1) * (N + D)
-    fwd = B * H * ((T // C) * C * (C - 1) * (N + D) + 4 * (T - C) * N * D) if chunked else quad_fwd
+    fwd = B * H * ((T // C) * C * (C - 1) * (N + D) + 2 * (T - C) * N * D) if chunked else quad_fwd
     bwd = B * H * T * (T - 1) * (3 * N + 2 * D) if cfg_id == 5 else 0
     flops = (fwd + bwd) * args.steps * world
     effective = (quad_fwd + bwd) * args.steps * world
