@@ -40,7 +40,9 @@ __device__ __forceinline__ void store_row32(void* base, int64_t off, bool f32, b
       for (int i = 0; i < 8; ++i)
         *reinterpret_cast<float4*>(o + 4 * i) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     } else {
-      for (int e = 0; e < 32 && e < valid; ++e) o[e] = v[e];
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (e < valid) o[e] = v[e];
     }
   } else {
     uint16_t* o = static_cast<uint16_t*>(base) + off;
@@ -51,7 +53,9 @@ __device__ __forceinline__ void store_row32(void* base, int64_t off, bool f32, b
             make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
                        pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
     } else {
-      for (int e = 0; e < 32 && e < valid; ++e) o[e] = static_cast<uint16_t>(f32_to_bf16_bits(v[e]));
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (e < valid) o[e] = static_cast<uint16_t>(f32_to_bf16_bits(v[e]));
     }
   }
 }
@@ -134,10 +138,12 @@ struct GradQProb {
     if (p.freqs != nullptr) {
       // gradient of the unrotated latent: dx0 = g0 c0 + g1 s1, dx1 = -g0 s0 + g1 c1
       const float pos = static_cast<float>(p.pos0 + gi);
-#pragma unroll 4
+      // fully unrolled so that v stays in registers (a partly unrolled loop indexes v at run
+      // time and moves it to local memory)
+#pragma unroll
       for (int e = 0; e < 32; e += 2) {
         const int n = gn0 + e;
-        if (n >= p.N) break;
+        if (n >= p.N) continue;
         float cc0, ss0, cc1, ss1;
         const float f0 = __ldg(p.freqs + n), f1 = __ldg(p.freqs + n + 1);
         rope_cis_grad(pos, f0, cc0, ss0);
