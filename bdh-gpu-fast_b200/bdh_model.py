@@ -179,7 +179,8 @@ class BDH(nn.Module):
     def _bf16_param(self, name: str, k_major: bool = False) -> torch.Tensor:
         """bf16 copy of a parameter, refreshed when the parameter changes (the cast that
         autocast would make on every use). k_major: an (H, D, N) weight as a view of a
-        contiguous (H, N, D) copy, the layout the latent kernels read fastest."""
+        contiguous (H, N, D) copy, the layout the latent kernels read fastest; a (K, D) matrix
+        (the decoder) as a view of a contiguous (D, K) copy."""
         p = getattr(self, name)
         cache = self.__dict__.setdefault("_bf16_cache", {})
         key = (p.data_ptr(), p._version, p.device, k_major)
@@ -187,7 +188,8 @@ class BDH(nn.Module):
         if hit is None or hit[0] != key:
             w = p.detach().to(torch.bfloat16)
             if k_major:
-                w = w.transpose(1, 2).contiguous().transpose(1, 2)
+                w = (w.t().contiguous().t() if w.dim() == 2
+                     else w.transpose(1, 2).contiguous().transpose(1, 2))
             hit = (key, w)
             cache[(name, k_major)] = hit
         return hit[1]
@@ -241,8 +243,10 @@ class BDH(nn.Module):
     def _layer_latent(self, x: torch.Tensor, xb: Optional[torch.Tensor], level: int,
                       rope_start: int, cache):
         """One layer on the fused kernels: encode (+ReLU +RoPE) -> tril attention -> LN ->
-        encoder_v gate (xs * relu(.)) -> decoder (cuBLAS) -> residual double LN. Same arithmetic
-        as the bf16-autocast layer of bdh.py:991-1052. ``xb`` is the bf16 copy of ``x`` (made
+        encoder_v gate (xs * relu(.)) -> decoder -> residual double LN. Same arithmetic as the
+        bf16-autocast layer of bdh.py:991-1052. With D = 256 and N a multiple of 128 the gate and
+        the decoder product run as one kernel (``latent_gate_dec``, ``BDH_SM100_GATE_DEC=0``
+        keeps the gate + cuBLAS decoder), so the (B, T, nh, N) xy latent is never stored. ``xb`` is the bf16 copy of ``x`` (made
         here when None); returns the new ``(x, xb)``.
 
         ``BDH_SM100_GATE_X=1`` (D <= 256): the encode writes only the rotated latent and the
@@ -251,8 +255,9 @@ class BDH(nn.Module):
         per config-2 step for a second K = 256 GEMM in the gate and measures slower on one
         B200 (1.68M vs 1.74M tokens/s: the gate becomes tensor-bound under the power cap), so
         the default stores xs."""
-        from kernels.sm100_attn import (latent_encode, latent_gate, latent_gate_x, layer_norm,
-                                        residual_layer_norm, tril_score_v)
+        from kernels.sm100_attn import (latent_encode, latent_gate, latent_gate_dec,
+                                        latent_gate_x, layer_norm, residual_layer_norm,
+                                        tril_score_v)
 
         B, T, _ = x.shape
         nh = self.config.n_head
@@ -282,8 +287,14 @@ class BDH(nn.Module):
         y_kv = tril_score_v(qr, qr, xb.unsqueeze(1))
         yn = layer_norm(y_kv, eps, out_dtype=torch.bfloat16)
         encv = self._bf16_param("encoder_v", kmaj)
-        xy = latent_gate_x(yn, encv, xb, enc) if gate_x else latent_gate(yn, encv, xs)
-        y_mlp = F.linear(xy.view(B, T, nh * xy.size(-1)), self._bf16_param("decoder").t())
+        N = enc.size(-1)
+        gate_dec = (not gate_x and kmaj and x.size(-1) == 256 and N % 128 == 0
+                    and os.environ.get("BDH_SM100_GATE_DEC", "1") != "0")
+        if gate_dec:  # gate and decoder in one kernel, xy never stored
+            y_mlp = latent_gate_dec(yn, encv, xs, self._bf16_param("decoder", True))
+        else:
+            xy = latent_gate_x(yn, encv, xb, enc) if gate_x else latent_gate(yn, encv, xs)
+            y_mlp = F.linear(xy.view(B, T, nh * xy.size(-1)), self._bf16_param("decoder").t())
         if x.dtype == torch.float32:
             return residual_layer_norm(x, y_mlp, eps, want_bf16=True)
         x = self._ln(x + self._ln(y_mlp))

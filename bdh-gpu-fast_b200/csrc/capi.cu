@@ -377,6 +377,45 @@ int bdh_latent_gate_x(const void* y, const int64_t y_strides[4], const void* enc
   return launch_latent_gate_x(a, static_cast<cudaStream_t>(stream), device_error_ptr());
 }
 
+int bdh_latent_gate_dec(const void* y, const int64_t y_strides[4], const void* encv,
+                        const int64_t encv_strides[3], const void* xs, const int64_t xs_strides[4],
+                        const void* dec, const int64_t dec_strides[2], void* out,
+                        const int64_t out_strides[3], int64_t B, int64_t T, int64_t H, int64_t D,
+                        int64_t N, void* stream) {
+  std::string msg;
+  if (!latent_sizes_ok(B, T, H, D, N, &msg)) return fail(BDH_ERR_INVALID, "latent_gate_dec: " + msg);
+  if (D != 256 || N % 128 != 0)
+    return fail(BDH_ERR_INVALID, "latent_gate_dec: needs D = 256 and N a multiple of 128");
+  if (B * T == 0) return BDH_OK;
+  if (H == 0 || N == 0) return fail(BDH_ERR_INVALID, "latent_gate_dec: H and N must be positive");
+  if (!strides_ok(y_strides, 4) || !strides_ok(xs_strides, 4) || !strides_ok(out_strides, 3))
+    return fail(BDH_ERR_INVALID,
+                "latent_gate_dec: last stride must be 1 and the others positive multiples of 8");
+  if (!(encv_strides[1] == 1 && encv_strides[2] > 0 && encv_strides[2] % 8 == 0 &&
+        encv_strides[0] > 0 && encv_strides[0] % 8 == 0))
+    return fail(BDH_ERR_INVALID,
+                "latent_gate_dec: encv must have d contiguous (a transposed (H,N,D) copy seen as (H,D,N))");
+  if (!(dec_strides[0] == 1 && dec_strides[1] > 0 && dec_strides[1] % 8 == 0))
+    return fail(BDH_ERR_INVALID,
+                "latent_gate_dec: the decoder must have the latent index contiguous (a transposed "
+                "(D, H*N) copy seen as (H*N, D))");
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0)
+    return fail(BDH_ERR_INVALID, "latent_gate_dec: out must be 16-byte aligned");
+  GateDecArgs a;
+  a.y = y;
+  std::memcpy(a.y_strides, y_strides, sizeof(a.y_strides));
+  a.encv = encv;
+  std::memcpy(a.encv_strides, encv_strides, sizeof(a.encv_strides));
+  a.xs = xs;
+  std::memcpy(a.xs_strides, xs_strides, sizeof(a.xs_strides));
+  a.dec = dec;
+  std::memcpy(a.dec_strides, dec_strides, sizeof(a.dec_strides));
+  a.out = out;
+  std::memcpy(a.out_strides, out_strides, sizeof(a.out_strides));
+  a.B = B; a.T = T; a.H = H; a.D = D; a.N = N;
+  return launch_latent_gate_dec(a, static_cast<cudaStream_t>(stream), device_error_ptr());
+}
+
 int bdh_quantize_rows_fp8(const void* x, const int64_t x_strides[4], int x_dtype, int64_t B,
                           int64_t H, int64_t T, int64_t N, void* out,
                           const int64_t out_strides[4], float* scale,

@@ -146,6 +146,23 @@ struct LatentArgs {
   const float* freqs = nullptr;
   int64_t B = 0, T = 0, H = 0, D = 0, N = 0, pos0 = 0;
 };
+// Fused gate + decoder (gate_decoder.cu): y_mlp = bf16(sum_{h,n} bf16(xs * relu(bf16(y encv)))
+// dec), D = 256, N a multiple of 128; encv (H,D,N) with d contiguous, dec (H*N, D) with the
+// latent index contiguous (a transposed copy), out (B,T,D) bf16.
+struct GateDecArgs {
+  const void* y = nullptr;       // (B,H,T,D) {b,h,t,d}
+  int64_t y_strides[4] = {0, 0, 0, 1};
+  const void* encv = nullptr;    // (H,D,N) {h,d,n}, d contiguous
+  int64_t encv_strides[3] = {0, 1, 0};
+  const void* xs = nullptr;      // (B,T,H,N) {b,t,h,n}
+  int64_t xs_strides[4] = {0, 0, 0, 1};
+  const void* dec = nullptr;     // (H*N, D) {k,d}, k contiguous
+  int64_t dec_strides[2] = {1, 0};
+  void* out = nullptr;           // (B,T,D) {b,t,d}
+  int64_t out_strides[3] = {0, 0, 1};
+  int64_t B = 0, T = 0, H = 0, D = 0, N = 0;
+};
+int launch_latent_gate_dec(const GateDecArgs& a, cudaStream_t stream, int* err);
 int launch_latent_encode(const LatentArgs& a, cudaStream_t stream, int* err);
 int launch_latent_gate_x(const LatentArgs& a, cudaStream_t stream, int* err);
 int launch_latent_gate(const LatentArgs& a, cudaStream_t stream, int* err);

@@ -39,7 +39,7 @@ _F32 = 0
 _BF16 = 1
 
 _c_i64_4 = ctypes.c_int64 * 4
-ABI_VERSION = 4  # BDH_ABI_VERSION of include/bdh_sm100.h
+ABI_VERSION = 5  # BDH_ABI_VERSION of include/bdh_sm100.h
 FP8 = torch.float8_e4m3fn  # the opt-in fp8 key-cache storage dtype
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -78,6 +78,9 @@ def _declare(lib: ctypes.CDLL) -> None:
                                     _i64, _i64, _i64, _i64, _i64, _vp]
     lib.bdh_latent_gate_x.argtypes = [_vp, P, _vp, _c_i64_3p, _vp, _c_i64_3p, _vp, _c_i64_3p,
                                       _vp, P, _i64, _i64, _i64, _i64, _i64, _vp]
+    _c_i64_2p = ctypes.POINTER(ctypes.c_int64)
+    lib.bdh_latent_gate_dec.argtypes = [_vp, P, _vp, _c_i64_3p, _vp, P, _vp, _c_i64_2p, _vp,
+                                        _c_i64_3p, _i64, _i64, _i64, _i64, _i64, _vp]
     lib.bdh_quantize_rows_fp8.argtypes = [_vp, P, ctypes.c_int, _i64, _i64, _i64, _i64, _vp, P,
                                           _vp, P, _vp]
     lib.bdh_tril_decode_fp8.argtypes = [_vp, P, ctypes.c_int, _vp, P, _vp, P, _vp, P, ctypes.c_int,
@@ -94,6 +97,7 @@ def _declare(lib: ctypes.CDLL) -> None:
                                      ctypes.c_size_t, _vp]
     for name in ("bdh_rope_rotate", "bdh_tril_score_v", "bdh_tril_decode", "bdh_tril_score_v_bwd",
                  "bdh_relu_mul", "bdh_latent_encode", "bdh_latent_gate", "bdh_latent_gate_x",
+                 "bdh_latent_gate_dec",
                  "bdh_layernorm", "bdh_quantize_rows_fp8", "bdh_tril_decode_fp8",
                  "bdh_residual_layernorm", "bdh_state_decode"):
         getattr(lib, name).restype = ctypes.c_int
@@ -394,6 +398,7 @@ def _check_paired_freqs(f: torch.Tensor) -> None:
         raise ValueError("latent_encode requires paired frequencies (freqs[2p] == freqs[2p+1])")
 
 
+_c_i64_2 = ctypes.c_int64 * 2
 _c_i64_3 = ctypes.c_int64 * 3
 
 
@@ -426,7 +431,7 @@ def _st(t: torch.Tensor, n: int):
     # strides of size-1 dims are never stepped; give them a legal value
     st = [s if (sz > 1 or s % 8 == 0 or s == 1) else 8 for s, sz in zip(t.stride(), t.shape)]
     st[-1] = t.stride(-1)
-    return (_c_i64_3 if n == 3 else _c_i64_4)(*st)
+    return {2: _c_i64_2, 3: _c_i64_3, 4: _c_i64_4}[n](*st)
 
 
 def latent_encode(x: torch.Tensor, enc: torch.Tensor, freqs: torch.Tensor, pos0: int = 0, *,
@@ -527,6 +532,49 @@ def latent_gate_x(y: torch.Tensor, encv: torch.Tensor, x: torch.Tensor, enc: tor
                                    x.data_ptr(), _st(x, 3), enc.data_ptr(), _st(enc, 3),
                                    out.data_ptr(), _st(out, 4), B, T, H, D, N, _stream(dev))
     _check(rc, "latent_gate_x")
+    return out
+
+
+def decoder_k_major(dec: torch.Tensor) -> torch.Tensor:
+    """(H*N, D) decoder as a view of a contiguous (D, H*N) copy: the layout
+    ``latent_gate_dec`` reads (the latent index contiguous)."""
+    return dec.t().contiguous().t()
+
+
+def latent_gate_dec(y: torch.Tensor, encv: torch.Tensor, xs: torch.Tensor, dec: torch.Tensor, *,
+                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``(xs * relu(y @ encv)) @ dec`` in one kernel: the gate of ``latent_gate`` followed by
+    the decoder product (bdh.py:914-945 and :1050 under bf16 autocast), each xy tile kept in
+    shared memory, never written to HBM. Returns (B, T, D) bf16.
+
+    ``y`` (B,H,T,D), ``encv`` (H,D,N) with d contiguous (``weight_k_major``), ``xs``
+    (B,T,H,N), ``dec`` (H*N, D) with the latent index contiguous (``decoder_k_major``);
+    D = 256 and N a multiple of 128.
+    """
+    if y.dim() != 4 or encv.dim() != 3 or xs.dim() != 4 or dec.dim() != 2:
+        raise ValueError("latent_gate_dec expects y (B,H,T,D), encv (H,D,N), xs (B,T,H,N), "
+                         "dec (H*N,D)")
+    dev = _require_cuda(y, encv, xs, dec)
+    lib = _require_lib()
+    B, H, T, D = y.shape
+    N = encv.size(-1)
+    if tuple(xs.shape) != (B, T, H, N) or tuple(encv.shape) != (H, D, N) or \
+            tuple(dec.shape) != (H * N, D):
+        raise ValueError("latent_gate_dec: shapes of y, encv, xs and dec disagree")
+    if D != 256 or N % 128 != 0:
+        raise ValueError("latent_gate_dec: needs D = 256 and N a multiple of 128")
+    if dec.dtype != torch.bfloat16 or encv.dtype != torch.bfloat16:
+        raise TypeError("latent_gate_dec: bf16 weights required")
+    if out is None:
+        out = torch.empty(B, T, D, dtype=torch.bfloat16, device=dev)
+    elif tuple(out.shape) != (B, T, D):
+        raise ValueError("latent_gate_dec: out must be (B,T,D)")
+    _check_latent("latent_gate_dec", y, xs, out, weight=encv)
+    with torch.cuda.device(dev):
+        rc = lib.bdh_latent_gate_dec(y.data_ptr(), _st(y, 4), encv.data_ptr(), _st(encv, 3),
+                                     xs.data_ptr(), _st(xs, 4), dec.data_ptr(), _st(dec, 2),
+                                     out.data_ptr(), _st(out, 3), B, T, H, D, N, _stream(dev))
+    _check(rc, "latent_gate_dec")
     return out
 
 

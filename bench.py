@@ -493,7 +493,9 @@ def bench_config2(args, world, rank, dev):
     #   gate        2 x 2 B T H N D flops (x enc and y encv), xy written           tensor
     # With xs stored (default):
     #   encode      2 B T H N x 2 bytes written (xs, QR) + x and weights read      HBM
-    #   gate        B T H N x 2 read (xs) + B T H N x 2 written (xy) + y, weights  HBM
+    #   gate + decoder in one kernel (default, BDH_SM100_GATE_DEC=0 splits them):
+    #               2 x 2 B T H N D flops (y encv, xy dec), xs read, xy never stored  tensor
+    #   gate alone  B T H N x 2 read (xs) + B T H N x 2 written (xy) + y, weights  HBM
     peaks, src = load_peaks()
     tpeak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
     tsrc = f"{src} bf16_tflops_sustained (kernel timed inside a long step)"
@@ -512,9 +514,15 @@ def bench_config2(args, world, rank, dev):
         enc_spec = ("latent encode x@enc + ReLU + RoPE (tc_gemm_kernel<EncodeProb>), xs and QR written",
                     "hbm", 2 * lat + small, 1e9, "GB/s", peaks["hbm_gbs"], f"{src} hbm_gbs",
                     "latent_encode_config2")
-        gate_spec = ("latent gate xs * relu(y@encv) (tc_gemm_kernel<GateProb>), xs read, xy written",
-                     "hbm", 2 * lat + small + B * N_HEAD * T * D_MODEL * 2, 1e9, "GB/s",
-                     peaks["hbm_gbs"], f"{src} hbm_gbs", "latent_gate_config2")
+        if os.environ.get("BDH_SM100_GATE_DEC", "1") != "0":
+            gate_spec = ("latent gate + decoder (xs * relu(y@encv)) @ dec (gate_dec_kernel, "
+                         "cta_group::2, xy kept in shared memory)", "tensor",
+                         4 * B * T * N_HEAD * N_LAT * D_MODEL, 1e12, "TFLOP/s", tpeak, tsrc,
+                         "gate_dec_config2")
+        else:
+            gate_spec = ("latent gate xs * relu(y@encv) (tc_gemm_kernel<GateProb>), xs read, xy written",
+                         "hbm", 2 * lat + small + B * N_HEAD * T * D_MODEL * 2, 1e9, "GB/s",
+                         peaks["hbm_gbs"], f"{src} hbm_gbs", "latent_gate_config2")
     specs = {
         "score": ("score pass tril(QR QR^T,-1) (tc_pair_kernel<ScorePair>, cta_group::2 256x256 tiles)"
                   if os.environ.get("BDH_SM100_PAIR", "1") != "0"

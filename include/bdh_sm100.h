@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define BDH_ABI_VERSION 4
+#define BDH_ABI_VERSION 5
 
 #define BDH_DTYPE_F32 0
 #define BDH_DTYPE_BF16 1
@@ -227,6 +227,14 @@ int bdh_tril_score_v_bwd(const void* q, const int64_t q_strides[4], const void* 
  *   xy[b,t,h,n] = bf16(relu(bf16(sum_k x[b,t,k] enc[h,k,n])) * relu(bf16(sum_k y[b,h,t,k] encv[h,k,n])))
  * With it, bdh_latent_encode may be called with xs == NULL (qr only) and the (B,T,nh,N) xs
  * latent never exists. D <= 256; enc and encv must share one weight layout.
+ *
+ * bdh_latent_gate_dec is bdh_latent_gate followed by the decoder product of bdh.py:1050
+ * ((x_sparse * y_sparse) @ decoder under bf16 autocast), in one kernel that keeps each xy tile
+ * in shared memory as the decoder's operand, so xy never reaches HBM:
+ *   out[b,t,d] = bf16(sum_{h,n} xy[b,t,h,n] dec[h*N + n, d])     xy as in bdh_latent_gate
+ * D = 256 and N a multiple of 128; encv (H,D,N) must have d contiguous (encv_strides {N*D, 1, D});
+ * dec (H*N, D) must have the latent index contiguous (a transposed copy, dec_strides {1, H*N});
+ * out (B,T,D) bf16 strides {b,t,d}.
  * None of these calls allocates; all are stream-ordered and graph-capturable.
  */
 int bdh_latent_encode(const void* x, const int64_t x_strides[3], const void* enc,
@@ -242,6 +250,11 @@ int bdh_latent_gate_x(const void* y, const int64_t y_strides[4], const void* enc
                       const void* enc, const int64_t enc_strides[3], void* xy,
                       const int64_t xy_strides[4], int64_t B, int64_t T, int64_t H, int64_t D,
                       int64_t N, void* stream);
+int bdh_latent_gate_dec(const void* y, const int64_t y_strides[4], const void* encv,
+                        const int64_t encv_strides[3], const void* xs, const int64_t xs_strides[4],
+                        const void* dec, const int64_t dec_strides[2], void* out,
+                        const int64_t out_strides[3], int64_t B, int64_t T, int64_t H, int64_t D,
+                        int64_t N, void* stream);
 
 /*
  * fp8 wire format of the cached rotated keys (opt-in cache storage; the reference keeps its

@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
     lib = sa.load_library()
     for name in _declared():
         assert hasattr(lib, name), f"{name} missing from {sa._LIB_PATH}"
-    assert lib.bdh_abi_version() == sa.ABI_VERSION == 4
+    assert lib.bdh_abi_version() == sa.ABI_VERSION == 5
 
 
 def test_workspace_queries_are_host_only():
@@ -121,6 +121,32 @@ def test_latent_entry_points_validate_on_host():
     assert rc == 1 and b"stride" in lib.bdh_last_error()
     assert lib.bdh_latent_gate_x(None, s4, None, w_n, None, s3, None, w_n, None, s4,
                                  1, 0, 2, 256, 64, None) == 0
+
+
+def test_gate_dec_entry_point_validates_on_host():
+    """bdh_latent_gate_dec: D = 256, N a multiple of 128, d-contiguous encv, latent-contiguous
+    decoder; all checked before any device work."""
+    from kernels import sm100_attn as sa
+
+    lib = sa.load_library()
+    H, N, D = 2, 256, 256
+    s4 = (ctypes.c_int64 * 4)(16 * H * N, H * N, N, 1)
+    y4 = (ctypes.c_int64 * 4)(H * 16 * D, 16 * D, D, 1)
+    s3 = (ctypes.c_int64 * 3)(16 * D, D, 1)
+    ev_d = (ctypes.c_int64 * 3)(N * D, 1, D)        # d contiguous (transposed copy)
+    ev_n = (ctypes.c_int64 * 3)(N * D, N, 1)        # n contiguous
+    dec_k = (ctypes.c_int64 * 2)(1, H * N)           # latent contiguous (transposed copy)
+    dec_d = (ctypes.c_int64 * 2)(D, 1)               # d contiguous
+    call = lambda *a: lib.bdh_latent_gate_dec(*a)
+    rc = call(None, y4, None, ev_d, None, s4, None, dec_k, None, s3, 1, 16, H, 128, N, None)
+    assert rc == 1 and b"D = 256" in lib.bdh_last_error()
+    rc = call(None, y4, None, ev_d, None, s4, None, dec_k, None, s3, 1, 16, H, D, 192, None)
+    assert rc == 1 and b"multiple of 128" in lib.bdh_last_error()
+    rc = call(None, y4, None, ev_n, None, s4, None, dec_k, None, s3, 1, 16, H, D, N, None)
+    assert rc == 1 and b"d contiguous" in lib.bdh_last_error()
+    rc = call(None, y4, None, ev_d, None, s4, None, dec_d, None, s3, 1, 16, H, D, N, None)
+    assert rc == 1 and b"latent index contiguous" in lib.bdh_last_error()
+    assert call(None, y4, None, ev_d, None, s4, None, dec_k, None, s3, 1, 0, H, D, N, None) == 0
 
 
 def test_layernorm_entry_points_validate_on_host():

@@ -253,6 +253,7 @@ def test_model_gate_x_matches_stored_xs(monkeypatch):
     idx = torch.randint(0, 256, (2, 256), generator=torch.Generator().manual_seed(19)).to(DEV)
     out = {}
     monkeypatch.setenv("BDH_SM100_LATENT", "1")
+    monkeypatch.setenv("BDH_SM100_GATE_DEC", "0")  # both forms through cuBLAS's decoder
     for flag in ("1", "0"):
         monkeypatch.setenv("BDH_SM100_GATE_X", flag)
         with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
