@@ -165,6 +165,9 @@ def test_model_fp8_cache_fused_latent_prefill(monkeypatch):
     B, P, steps = 2, 128, 4
     idx = torch.randint(0, 256, (B, P + steps), generator=torch.Generator().manual_seed(9)).to(DEV)
     res = {}
+    # the gate followed by cuBLAS's decoder on both sides, so that only the QR path differs (the
+    # fused gate + decoder has its own model test in test_gpu_gate_dec.py)
+    monkeypatch.setenv("BDH_SM100_GATE_DEC", "0")
     for flag in ("1", "0"):
         monkeypatch.setenv("BDH_SM100_LATENT", flag)
         with torch.autocast("cuda", dtype=torch.bfloat16):

@@ -233,11 +233,18 @@ def test_model_latent_layer_matches_unfused_and_oracle(monkeypatch):
         assert m._latent_fusable("cuda_sm100", 128, None, idx.device)
         cnt = _launch_counts(lambda: res.setdefault("fused", m(idx)[0].float()))
         assert cnt["encode"] == 2 and cnt["gate"] == 2 and cnt["rope"] == 0, cnt
+        # the same arithmetic as the unfused layers: the gate followed by cuBLAS's decoder (the
+        # fused gate + decoder sums the decoder product in its own order, which at these small
+        # shapes cuBLAS may not share; its own model test is in test_gpu_gate_dec.py)
+        monkeypatch.setenv("BDH_SM100_GATE_DEC", "0")
+        res["fused_cublas_dec"] = m(idx)[0].float()
         monkeypatch.setenv("BDH_SM100_LATENT", "0")
         cnt = _launch_counts(lambda: res.setdefault("plain", m(idx)[0].float()))
         assert cnt["encode"] == 0 and cnt["rope"] == 2, cnt
     fused, plain = res["fused"], res["plain"]
-    assert ((fused - plain).norm() / plain.norm()).item() < 1e-3
+    fc = res["fused_cublas_dec"]
+    assert ((fc - plain).norm() / plain.norm()).item() < 1e-3
+    assert ((fused - plain).norm() / plain.norm()).item() < 1e-2
     w = {k: getattr(m, k).detach().to(torch.bfloat16).float().cpu().numpy()
          for k in ("encoder", "encoder_v", "decoder", "lm_head")}
     w["embed"] = m.embed.weight.detach().float().cpu().numpy()
@@ -310,6 +317,9 @@ def test_model_latent_prefill_then_decode(monkeypatch):
                 out.append(lg[:, -1].float())
         return torch.stack(out)
 
+    # the gate followed by cuBLAS's decoder on both sides, so that only the cache-slot path
+    # differs (the fused gate + decoder has its own model test in test_gpu_gate_dec.py)
+    monkeypatch.setenv("BDH_SM100_GATE_DEC", "0")
     for storage in (None, torch.bfloat16):
         a = run("1", storage)
         b = run("0", storage)
