@@ -248,7 +248,8 @@ def load_traffic(name: str, batch: int | None = None):
 
     ``profiles/<name>.json`` holds the bytes ncu measured on a capture of ``captured_batch``
     rows of batch; the traffic of every kernel here grows in proportion to the batch (independent
-    (b,h) units), so it is scaled to this run's batch.
+    (b,h) units), so it is scaled to this run's batch, except an optional
+    ``traffic_fixed_bytes`` part that does not (weights read once per launch).
     """
     p = REPO / "profiles" / f"{name}.json"
     if not p.exists():
@@ -256,9 +257,10 @@ def load_traffic(name: str, batch: int | None = None):
     try:
         d = json.loads(p.read_text())
         t = float(d["traffic_bytes_per_captured_launch"])
+        fixed = float(d.get("traffic_fixed_bytes", 0.0))
         cb = d.get("captured_batch")
         if batch and cb:
-            t *= batch / cb
+            t = fixed + (t - fixed) * batch / cb
         return t
     except Exception:  # noqa: BLE001
         return None
