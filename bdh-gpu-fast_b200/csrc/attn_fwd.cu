@@ -175,13 +175,16 @@ struct ScorePair {
     tma_load_4d_pair(&p.a_map[0], bar, a_dst, kb * 64, tl.m * 256 + r128, h, b);
     tma_load_4d_pair(&p.b_map[0], bar, b_dst, kb * 64, tl.n * 256 + r128, hb, b);
   }
+  // 4 KB per epilogue warp: the transposed stores of the backward's G and M^T go through
+  // shared memory (whole 64-byte column segments instead of two-byte element stores)
+  static constexpr int kEpiScratch = 2 * 32 * 32 * 2;
   __device__ static void epilogue(const Params& p, const Tile& tl, int rank, int row, int c0,
-                                  const uint32_t (&r)[32]) {
+                                  const uint32_t (&r)[32], uint8_t* scratch) {
     Base::Tile t;
     t.unit = tl.unit;
     t.mi = 2 * tl.m + rank;
     t.ni = tl.n;
-    Base::epilogue(p, t, row, c0, r);
+    Base::epilogue(p, t, row, c0, r, scratch);
   }
 };
 

@@ -128,12 +128,55 @@ struct ScoreProb {
       static_cast<uint32_t*>(base)[idx] = bits;
   }
 
+  // Transposed store S^T[j][i] of one warp's 32 consecutive rows x 32 columns staged through
+  // `scratch` (4 KB: hi and lo, 32 x 32 bf16 each): the warp writes the values column by column,
+  // then every column's 32 rows leave as 64 contiguous bytes in four 16-byte stores, instead of
+  // one two-byte store per element and lane. All 32 lanes take part (rows at or beyond T are
+  // not written). bf16 only.
+  __device__ static void store_trans_staged(const Params& p, void* th, void* tlo, size_t unit_off,
+                                            int gi, int gj_base, const uint32_t (&hi)[32],
+                                            const uint32_t (&lo)[32], uint8_t* scratch) {
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    uint16_t* sh = reinterpret_cast<uint16_t*>(scratch);
+    uint16_t* sl = sh + 32 * 32;
+    __syncwarp();  // the previous chunk's reads of the staging are done
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      sh[e * 32 + lane] = static_cast<uint16_t>(hi[e]);
+      if (tlo != nullptr) sl[e * 32 + lane] = static_cast<uint16_t>(lo[e]);
+    }
+    __syncwarp();
+    const int gi0 = gi - lane;  // the warp's first row
+    const int q = lane & 3;     // 16-byte quarter of a column: rows gi0 + 8q .. + 7
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = (lane >> 2) + 8 * k;
+      const int gj = gj_base + e;
+      if (gj >= p.T) continue;
+      const int r0 = gi0 + 8 * q;
+      const size_t idx = (unit_off + gj) * static_cast<size_t>(p.ldp) + r0;
+      for (int t = 0; t < (tlo != nullptr ? 2 : 1); ++t) {
+        const uint16_t* src = (t == 0 ? sh : sl) + e * 32 + 8 * q;
+        uint16_t* dst = static_cast<uint16_t*>(t == 0 ? th : tlo) + idx;
+        if (r0 + 8 <= p.T) {
+          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+        } else {
+          for (int u = 0; u < 8 && r0 + u < p.T; ++u) dst[u] = src[u];
+        }
+      }
+    }
+  }
+
+  // scratch (pair engine only): 4 KB of this warp's shared memory for the staged transposed
+  // store; with it all lanes stay in the call, rows at or beyond T write nothing.
   __device__ static void epilogue(const Params& p, const Tile& tl, int row, int c0,
-                                  const uint32_t (&r)[32]) {
+                                  const uint32_t (&r)[32], uint8_t* scratch = nullptr) {
     const int gi = tl.mi * S::BM + row;
-    if (gi >= p.T) return;
+    const bool row_ok = gi < p.T;
+    if (!row_ok && scratch == nullptr) return;
     const int gj_base = tl.ni * BN + c0;
     if (ELEM == 4 && p.ksplit > 1) {
+      if (!row_ok) return;
       // K-split partial: raw fp32 sums, masked and split by the reduce pass
       float* dst = p.part + ((static_cast<size_t>(tl.ks) * p.units + tl.unit) * p.T + gi) *
                                 static_cast<size_t>(p.ldp);
@@ -169,7 +212,9 @@ struct ScoreProb {
     }
     const size_t unit_off = static_cast<size_t>(tl.unit) * p.T;
     // ---- direct store S[i][j] (vectorised unless it must skip the upper part of a diagonal tile)
-    if (p.mode == kStoreDirect || p.mode == kStoreLU || (p.mode == kStoreSym && !diag)) {
+    if (!row_ok) {
+      // nothing of this row is stored (staged transposed store below only)
+    } else if (p.mode == kStoreDirect || p.mode == kStoreLU || (p.mode == kStoreSym && !diag)) {
       // chunked forward: columns are stored relative to the chunk's first key
       const int cb = key0(p, tl.mi);
       const size_t row_off = (unit_off + gi) * static_cast<size_t>(p.ldp) - static_cast<size_t>(cb);
@@ -216,6 +261,11 @@ struct ScoreProb {
       void* th = p.mode == kStoreLU ? p.p2_hi : p.p_hi;
       void* tlo = p.mode == kStoreLU ? p.p2_lo : p.p_lo;
       const bool strict = p.mode == kStoreSym && diag;  // Sym diagonal: only j < i here
+      if (ELEM == 2 && scratch != nullptr && !strict) {
+        store_trans_staged(p, th, tlo, unit_off, gi, gj_base, hi, lo, scratch);
+        return;
+      }
+      if (!row_ok) return;
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         const int gj = gj_base + e;

@@ -31,6 +31,21 @@ constexpr int pair_threads() {
   return 64 + 32 * EpiWarps<P>::value;
 }
 
+// P::kEpiScratch > 0: every epilogue warp gets that many bytes of shared memory after the
+// barriers, passed to P::epilogue as a last argument (staging for stores that need a transpose).
+template <class P, class = void>
+struct EpiScratch {
+  static constexpr int value = 0;
+};
+template <class P>
+struct EpiScratch<P, std::void_t<decltype(P::kEpiScratch)>> {
+  static constexpr int value = P::kEpiScratch;
+};
+template <class S, class P>
+constexpr int pair_smem_bytes() {
+  return S::SMEM_BYTES + EpiWarps<P>::value * EpiScratch<P>::value;
+}
+
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -291,7 +306,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<P>(), 1
         uint32_t r[32];
         tmem_ld32(tbase + static_cast<uint32_t>(c0), r);
         tmem_ld_wait();
-        P::epilogue(prm, tile, static_cast<int>(rank), row, c0, r);
+        if constexpr (EpiScratch<P>::value > 0)
+          P::epilogue(prm, tile, static_cast<int>(rank), row, c0, r,
+                      smem + S::STAGES * S::STAGE_BYTES + 256 + (warp - 2) * EpiScratch<P>::value);
+        else
+          P::epilogue(prm, tile, static_cast<int>(rank), row, c0, r);
       }
       tc_fence_before();
       __syncwarp();
@@ -316,7 +335,8 @@ static int launch_pair(const typename P::Params& prm, int ntiles, cudaStream_t s
   static int max_pairs[64] = {0};
   if (dev >= 0 && dev < 64 && max_pairs[dev] == 0) {
     cudaError_t e = cudaFuncSetAttribute(tc_pair_kernel<S, P>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         pair_smem_bytes<S, P>());
     if (e != cudaSuccess) {
       set_error(std::string("cudaFuncSetAttribute (pair): ") + cudaGetErrorString(e));
       return BDH_ERR_CUDA;
@@ -324,7 +344,7 @@ static int launch_pair(const typename P::Params& prm, int ntiles, cudaStream_t s
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 74);
     cfg.blockDim = dim3(pair_threads<P>());
-    cfg.dynamicSmemBytes = S::SMEM_BYTES;
+    cfg.dynamicSmemBytes = pair_smem_bytes<S, P>();
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
     attr.val.clusterDim.x = 2;
@@ -339,7 +359,7 @@ static int launch_pair(const typename P::Params& prm, int ntiles, cudaStream_t s
   }
   const int pairs = std::min(ntiles, max_pairs[(dev >= 0 && dev < 64) ? dev : 0]);
   prof_start(kind, stream);
-  tc_pair_kernel<S, P><<<2 * pairs, pair_threads<P>(), S::SMEM_BYTES, stream>>>(prm);
+  tc_pair_kernel<S, P><<<2 * pairs, pair_threads<P>(), pair_smem_bytes<S, P>(), stream>>>(prm);
   prof_stop(kind, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
