@@ -17,8 +17,11 @@ Per layer (all LayerNorms affine-free)::
 
 With ``BDH_ATTN_IMPL=cuda_sm100`` the RoPE is fused into the attention (in-register cos/sin,
 no tables), the cached decode step rotates the new query and writes it into the cache slot
-inside the decode kernel, and the cache is read in its storage dtype without copies. The
-encoder / decoder projections stay cuBLAS GEMMs (torch).
+inside the decode kernel, and the cache is read in its storage dtype without copies. Prefill
+layers in bf16 run on the library's fused latent kernels (``_layer_latent``: encoder GEMM +
+ReLU + RoPE, the attention, the encoder_v GEMM + ReLU + product + decoder GEMM in one kernel,
+the LayerNorms); the other paths (fp32, decode steps, training) use torch GEMMs for the
+projections.
 """
 
 from __future__ import annotations
