@@ -212,9 +212,12 @@ struct ScoreProb {
     }
     const size_t unit_off = static_cast<size_t>(tl.unit) * p.T;
     // ---- direct store S[i][j] (vectorised unless it must skip the upper part of a diagonal tile)
-    if (!row_ok) {
-      // nothing of this row is stored (staged transposed store below only)
-    } else if (p.mode == kStoreDirect || p.mode == kStoreLU || (p.mode == kStoreSym && !diag)) {
+    // On a diagonal tile of G only chunks that cross the diagonal need element stores: a chunk
+    // wholly below row i is stored whole, one wholly above it is the other orientation's.
+    const bool below = gj_base + 31 < gi;
+    if (!row_ok || (p.mode == kStoreSym && diag && gj_base > gi)) {
+      // nothing of this row and chunk is stored here (staged transposed store below only)
+    } else if (p.mode == kStoreDirect || p.mode == kStoreLU || (p.mode == kStoreSym && (!diag || below))) {
       // chunked forward: columns are stored relative to the chunk's first key
       const int cb = key0(p, tl.mi);
       const size_t row_off = (unit_off + gi) * static_cast<size_t>(p.ldp) - static_cast<size_t>(cb);
@@ -261,9 +264,14 @@ struct ScoreProb {
       void* th = p.mode == kStoreLU ? p.p2_hi : p.p_hi;
       void* tlo = p.mode == kStoreLU ? p.p2_lo : p.p_lo;
       const bool strict = p.mode == kStoreSym && diag;  // Sym diagonal: only j < i here
-      if (ELEM == 2 && scratch != nullptr && !strict) {
-        store_trans_staged(p, th, tlo, unit_off, gi, gj_base, hi, lo, scratch);
-        return;
+      if (ELEM == 2 && scratch != nullptr) {
+        // warp-uniform: the warp's rows are gi0 .. gi0 + 31
+        const int gi0 = gi - static_cast<int>(threadIdx.x & 31);
+        if (!strict || gj_base + 31 < gi0) {  // every (i, j) of the chunk has j < i
+          store_trans_staged(p, th, tlo, unit_off, gi, gj_base, hi, lo, scratch);
+          return;
+        }
+        if (gj_base >= gi0 + 31) return;  // no (i, j) of the chunk has j < i
       }
       if (!row_ok) return;
 #pragma unroll
