@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_partial_fp8_kernel(
 // so the stream does not drain between rows. The eight partial dots of a group of eight rows
 // are reduced across the warp with nine shuffles, and the warps' partials are summed in shared
 // memory. Measured on B200 at the config-4 shapes (B = 64, H = 4, S = 520, N = 8192): 7.2 /
-// 7.1 / 5.0 TB/s for fp32 / bf16 / fp8 keys, against 5.8 / 5.0 / 3.6 TB/s for the row-per-warp
+// 7.1 / 6.0 TB/s for fp32 / bf16 / fp8 keys, against 5.8 / 5.0 / 3.6 TB/s for the row-per-warp
 // kernels above (q staged in shared memory, loads drained at every row pair), which remain the
 // path for unaligned rows and latent widths beyond the register budget.
 constexpr int kSliceWarps = 8;
@@ -348,24 +348,28 @@ __device__ __forceinline__ float dot16(const float* qv, const uint4 u) {
   return a;
 }
 
-// e4m3 keys: of each 32-bit word of four key bytes, bytes 0 and 1 are widened by the conversion
-// instructions (cvt.rn.f16x2.e4m3x2, exact, then fp16 -> fp32) against unscaled query elements
-// into `ac`, bytes 2 and 3 by the integer form (2^-120 times the value) against query elements
-// pre-multiplied by 2^64 into `ai`; the row's dot product is ai * 2^56 + ac. Splitting the work
-// between the integer and the conversion pipes streamed 5.4 TB/s against 4.9 TB/s for the integer
-// form alone in a probe at the config-4 shapes (the decode is bound by this widening).
-__device__ __forceinline__ void dot16_e4m3(const float* qv, const uint4 u, float& ai, float& ac) {
+// e4m3 keys widened by the conversion instructions: two bytes at a time to fp16
+// (cvt.rn.f16x2.e4m3x2, exact: every e4m3 value is a normal fp16) and on to fp32, against
+// unscaled query elements. In a probe at the config-4 shapes this streamed 6.0 TB/s, against
+// 4.9 TB/s for the integer widening above (the decode is bound by the widening) and 5.5 TB/s
+// for half of the bytes each way.
+__device__ __forceinline__ float dot16_e4m3(const float* qv, const uint4 u) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float a = 0.f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    uint32_t h2;
-    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(w[i] & 0xFFFFu)));
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
-    ac = fmaf(qv[4 * i], f.x, ac);
-    ac = fmaf(qv[4 * i + 1], f.y, ac);
-    ai = fmaf(qv[4 * i + 2], e4m3_top_to_f32_2m120(w[i] << 8), ai);
-    ai = fmaf(qv[4 * i + 3], e4m3_top_to_f32_2m120(w[i]), ai);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t h2;
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;"
+          : "=r"(h2)
+          : "h"(static_cast<uint16_t>(half ? (w[i] >> 16) : (w[i] & 0xFFFFu))));
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+      a = fmaf(qv[4 * i + 2 * half], f.x, a);
+      a = fmaf(qv[4 * i + 2 * half + 1], f.y, a);
+    }
   }
+  return a;
 }
 
 // Four consecutive query elements; vec: one 16-byte (fp32) or 8-byte (bf16) load.
@@ -471,20 +475,16 @@ __global__ void __launch_bounds__(kSliceWarps * 32, 2) decode_slice_kernel(
         }
       }
 #pragma unroll
-      // e4m3: query elements 2 and 3 of every four meet the integer-widened keys (x 2^64)
-      for (int j = 0; j < 4; ++j) qv[i][e + j] = (F8 && j >= 2) ? x[j] * kE4m3QScale : x[j];
+      for (int j = 0; j < 4; ++j) qv[i][e + j] = x[j];
     }
   }
 
   // 3. the rows, eight at a time; loads run kSliceAhead ahead across group boundaries
   const int groups = (rows + 7) >> 3;
   for (int g = 0; g < groups; ++g) {
-    float acc[8], acc_c[8];
+    float acc[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      acc[k] = 0.f;
-      acc_c[k] = 0.f;
-    }
+    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
 #pragma unroll
     for (int t = 0; t < L; ++t) {
       const uint4 u = ring[t % DP];
@@ -497,13 +497,9 @@ __global__ void __launch_bounds__(kSliceWarps * 32, 2) decode_slice_kernel(
         ++lr;
       }
       if constexpr (F8)
-        dot16_e4m3(qv[i], u, acc[t / QC], acc_c[t / QC]);
+        acc[t / QC] += dot16_e4m3(qv[i], u);
       else
         acc[t / QC] += dot16<TK>(qv[i], u);
-    }
-    if constexpr (F8) {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) acc[k] = fmaf(acc[k], kE4m3RowScale, acc_c[k]);
     }
     // eight values per lane -> lane (b4 b3 b2) holds the warp's sum for row 4 b4 + 2 b3 + b2
     const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
