@@ -243,6 +243,22 @@ class BDH(nn.Module):
             or self.encoder.dtype == torch.bfloat16
         return bf16 and os.environ.get("BDH_SM100_LATENT", "1") != "0"
 
+    def _decoder_product(self, xy: torch.Tensor, B: int, T: int, impl: str,
+                         grad: bool) -> torch.Tensor:
+        """y_mlp = xy @ decoder (bdh.py:1050) for xy (B, T, nh, N). An fp32 decode step (at most
+        256 rows B*T, no autocast, no autograd) on the native path runs bdh_decoder_f32, which
+        splits K = nh*N across the GPU (a library GEMM launches a few CTAs for this shape);
+        BDH_SM100_DEC_F32=0 keeps torch's linear for every shape."""
+        x2 = xy.reshape(B * T, xy.size(-2) * xy.size(-1))
+        if (impl == "cuda_sm100" and not grad and x2.is_cuda and B * T <= 256
+                and x2.dtype == torch.float32 and self.decoder.dtype == torch.float32
+                and not torch.is_autocast_enabled()
+                and os.environ.get("BDH_SM100_DEC_F32", "1") != "0"):
+            from kernels.sm100_attn import decoder_f32
+
+            return decoder_f32(x2, self.decoder).view(B, T, -1)
+        return F.linear(x2.view(B, T, -1), self.decoder.t())
+
     def _layer_latent(self, x: torch.Tensor, xb: Optional[torch.Tensor], level: int,
                       rope_start: int, cache):
         """One layer on the fused kernels: encode (+ReLU +RoPE) -> tril attention -> LN ->
@@ -341,7 +357,7 @@ class BDH(nn.Module):
                     xy = relu_mul(x_lat, y_lat)
                 else:
                     xy = self.drop(x_bthn * F.relu(y_lat))
-                y_mlp = F.linear(xy.reshape(B, T, nh * N), self.decoder.t())
+                y_mlp = self._decoder_product(xy, B, T, impl, grad)
                 x = self._ln(x + self._ln(y_mlp))
                 continue
             past_kr = past_v = out_kr = past_scale = out_scale = None
@@ -379,7 +395,7 @@ class BDH(nn.Module):
                 xy = relu_mul(x_lat, y_lat)
             else:
                 xy = self.drop(x_bthn * F.relu(y_lat))
-            y_mlp = F.linear(xy.reshape(B, T, nh * N), self.decoder.t())
+            y_mlp = self._decoder_product(xy, B, T, impl, grad)
             x = self._ln(x + self._ln(y_mlp))
         if cache is not None:
             cache.commit()

@@ -295,6 +295,25 @@ int bdh_relu_mul(const void* x, const int64_t x_strides[4], const void* y,
                          static_cast<cudaStream_t>(stream));
 }
 
+int64_t bdh_decoder_f32_slices(int64_t K) { return K > 0 ? bdh::decoder_f32_slices(K) : 0; }
+
+int bdh_decoder_f32(const float* x, int64_t ldx, const float* w, int64_t ldw, float* out,
+                    int64_t ldo, float* partial, int64_t M, int64_t K, int64_t D, void* stream) {
+  if (M < 0 || K < 0 || D < 0) return fail(BDH_ERR_INVALID, "decoder_f32: negative size");
+  if (M == 0 || D == 0) return BDH_OK;
+  if (M > 65535) return fail(BDH_ERR_INVALID, "decoder_f32: more than 65535 rows");
+  if (D % 4 != 0 || ldw % 4 != 0 || ldw < D || ldo < D || (K > 0 && ldx < K))
+    return fail(BDH_ERR_INVALID,
+                "decoder_f32: D and ldw must be multiples of 4, and ldx >= K, ldw >= D, ldo >= D");
+  if (out == nullptr || (K > 0 && (x == nullptr || w == nullptr || partial == nullptr)))
+    return fail(BDH_ERR_INVALID, "decoder_f32: null pointer");
+  if (K > 0 && ((reinterpret_cast<uintptr_t>(w) & 15u) != 0 ||
+                (reinterpret_cast<uintptr_t>(partial) & 15u) != 0))
+    return fail(BDH_ERR_INVALID, "decoder_f32: w and partial must be 16-byte aligned");
+  return bdh::launch_decoder_f32(x, ldx, w, ldw, out, ldo, partial, M, K, D,
+                                 static_cast<cudaStream_t>(stream));
+}
+
 int bdh_latent_encode(const void* x, const int64_t x_strides[3], const void* enc,
                       const int64_t enc_strides[3], void* xs, const int64_t xs_strides[4],
                       void* qr, const int64_t qr_strides[4], const float* freqs, int64_t B,

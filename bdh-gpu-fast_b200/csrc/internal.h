@@ -12,7 +12,8 @@ namespace bdh {
 // Launch timing hooks (prof.cpp); kinds as documented at bdh_profile_end.
 enum ProfKind : int { kProfScore = 0, kProfValue = 1, kProfRope = 2, kProfDecode = 3,
                       kProfGradQ = 4, kProfGradV = 5, kProfSplit = 6, kProfOther = 7,
-                      kProfState = 8, kProfEncode = 9, kProfGate = 10, kProfNorm = 11 };
+                      kProfState = 8, kProfEncode = 9, kProfGate = 10, kProfNorm = 11,
+                      kProfDecoder = 12 };
 void prof_start(int kind, cudaStream_t s);
 void prof_stop(int kind, cudaStream_t s);
 
@@ -117,6 +118,12 @@ int launch_rope(const void* x, int x_dtype, const int64_t xs[4], void* y, int y_
                 const int64_t ys[4], float* y_lo, const float* freqs, int64_t B, int64_t H,
                 int64_t T, int64_t N, int64_t pos0, int relu_in, cudaStream_t stream);
 // out = relu(x) * relu(y), all (B,H,T,N) with a contiguous last dimension.
+// fp32 decoder product of a decode step (decoder_f32.cu): out (M, D) = X (M, K) @ W (K, D),
+// K split into decoder_f32_slices(K) slices whose fp32 partials go to part (slices x M x D).
+int64_t decoder_f32_slices(int64_t K);
+int launch_decoder_f32(const float* x, int64_t ldx, const float* w, int64_t ldw, float* out,
+                       int64_t ldo, float* part, int64_t M, int64_t K, int64_t D,
+                       cudaStream_t stream);
 int launch_relu_mul(const void* x, const int64_t xs[4], const void* y, const int64_t ys[4],
                     void* out, const int64_t os[4], int dtype, int64_t B, int64_t H, int64_t T,
                     int64_t N, cudaStream_t stream);

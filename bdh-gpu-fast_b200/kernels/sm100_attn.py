@@ -39,7 +39,7 @@ _F32 = 0
 _BF16 = 1
 
 _c_i64_4 = ctypes.c_int64 * 4
-ABI_VERSION = 5  # BDH_ABI_VERSION of include/bdh_sm100.h
+ABI_VERSION = 6  # BDH_ABI_VERSION of include/bdh_sm100.h
 FP8 = torch.float8_e4m3fn  # the opt-in fp8 key-cache storage dtype
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -53,6 +53,9 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.bdh_rope_rotate.argtypes = [_vp, ctypes.c_int, P, _vp, ctypes.c_int, P, _vp, _vp,
                                     _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _vp]
     lib.bdh_relu_mul.argtypes = [_vp, P, _vp, P, _vp, P, ctypes.c_int, _i64, _i64, _i64, _i64, _vp]
+    lib.bdh_decoder_f32_slices.argtypes = [_i64]
+    lib.bdh_decoder_f32_slices.restype = _i64
+    lib.bdh_decoder_f32.argtypes = [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _vp]
     lib.bdh_set_forward_algo.argtypes = [ctypes.c_int]
     lib.bdh_set_forward_algo.restype = ctypes.c_int
     lib.bdh_tril_score_v_workspace_size.restype = ctypes.c_size_t
@@ -253,7 +256,7 @@ def _tma_ready(x: torch.Tensor) -> torch.Tensor:
 # Kernel kinds of the launch-timing hook, in the order of bdh_profile_end's arrays
 # (BDH_PROF_KINDS in include/bdh_sm100.h).
 PROF_KINDS = ("score", "value", "rope", "decode", "grad_q", "grad_v", "split", "gated_product",
-              "state", "encode", "gate", "norm")
+              "state", "encode", "gate", "norm", "decoder")
 
 
 def profile_begin() -> None:
@@ -379,6 +382,35 @@ def relu_mul(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
         rc = lib.bdh_relu_mul(x.data_ptr(), _strides(x), y.data_ptr(), _strides(y), out.data_ptr(),
                               _strides(out), _code(x.dtype), B, H, T, N, _stream(dev))
     _check(rc, "relu_mul")
+    return out
+
+
+def decoder_f32(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp32 ``x @ w`` for a decode step's decoder product (x: (M, K) with unit column stride,
+    w: (K, D) row-major, D a multiple of 4), K split across the GPU and summed in a fixed order
+    (bdh_decoder_f32). ``out``: optional (M, D) fp32 destination with unit column stride."""
+    if x.dim() != 2 or w.dim() != 2 or x.size(1) != w.size(0):
+        raise ValueError("decoder_f32 expects x (M, K) and w (K, D)")
+    if x.dtype != torch.float32 or w.dtype != torch.float32:
+        raise ValueError("decoder_f32 expects fp32 tensors")
+    dev = _require_cuda(x, w)
+    lib = _require_lib()
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    if w.stride(1) != 1 or w.stride(0) % 4 != 0 or w.data_ptr() % 16 != 0:
+        w = w.contiguous()
+    M, K = x.shape
+    D = w.size(1)
+    if out is None:
+        out = torch.empty((M, D), dtype=torch.float32, device=dev)
+    elif out.shape != (M, D) or out.dtype != torch.float32 or out.stride(1) != 1:
+        raise ValueError("decoder_f32: out must be an fp32 (M, D) tensor with unit column stride")
+    part = torch.empty(int(lib.bdh_decoder_f32_slices(K)) * M * D, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.bdh_decoder_f32(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0),
+                                 out.data_ptr(), out.stride(0), part.data_ptr(), M, K, D,
+                                 _stream(dev))
+    _check(rc, "decoder_f32")
     return out
 
 

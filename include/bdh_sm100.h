@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define BDH_ABI_VERSION 5
+#define BDH_ABI_VERSION 6
 
 #define BDH_DTYPE_F32 0
 #define BDH_DTYPE_BF16 1
@@ -307,15 +307,30 @@ int bdh_residual_layernorm(const float* x, int64_t x_row_stride, const void* y, 
                            float eps, void* stream);
 
 /*
+ * fp32 decoder product of a decode step: out (M, D) = x (M, K) @ w (K, D), all fp32, with M =
+ * B * T small and K = nh * N large. Replaces, for the fp32 model's decode steps, the reference's
+ * y_mlp = xy @ decoder (bdh.py:1050, torch.matmul / F.linear outside autocast). K is split into
+ * bdh_decoder_f32_slices(K) slices of 256 rows summed in fp32 in a fixed order, so results are
+ * deterministic; they differ from a library GEMM's only by summation order.
+ * x: row stride ldx (elements), unit column stride; w: row-major with row stride ldw (a multiple
+ * of 4, 16-byte aligned); out: row stride ldo; D a multiple of 4. partial: caller-provided
+ * fp32 workspace of bdh_decoder_f32_slices(K) * M * D elements, 16-byte aligned.
+ */
+int64_t bdh_decoder_f32_slices(int64_t K);
+int bdh_decoder_f32(const float* x, int64_t ldx, const float* w, int64_t ldw, float* out,
+                    int64_t ldo, float* partial, int64_t M, int64_t K, int64_t D, void* stream);
+
+/*
  * Launch timing for benchmarks (no counterpart in the reference, which timed whole calls with
  * perf_counter, benchmarks/bench_gpu_attn.py:263-280). Between begin and end, every kernel of
  * this library is bracketed by CUDA events on its own stream; end synchronises them and
  * returns the summed device milliseconds and launch counts per kernel kind:
  *   0 score pass, 1 value pass, 2 RoPE, 3 decode, 4 grad-Q pass, 5 grad-V pass, 6 split/transpose,
  *   7 gated product (bdh_relu_mul), 8 state pass of the chunked forward,
- *   9 latent encode (bdh_latent_encode), 10 latent gate (bdh_latent_gate), 11 LayerNorms.
+ *   9 latent encode (bdh_latent_encode), 10 latent gate (bdh_latent_gate), 11 LayerNorms,
+ *   12 fp32 decoder product of a decode step (bdh_decoder_f32).
  */
-#define BDH_PROF_KINDS 12
+#define BDH_PROF_KINDS 13
 int bdh_profile_begin(void);
 int bdh_profile_end(double ms[BDH_PROF_KINDS], int launches[BDH_PROF_KINDS]);
 
