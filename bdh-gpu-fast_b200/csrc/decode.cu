@@ -639,6 +639,9 @@ DecodePlan plan_decode(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N, i
   }
   if (max_splits > 0)
     while (rows < kDecRowsMax && (S + rows - 1) / rows > max_splits) rows *= 2;
+  // a forced row count that is not a power of two can double past the kernels' score stages
+  // (sc[kDecRowsMax], the N + kDecRowsMax shared-memory stage): never plan more rows than they hold
+  rows = std::min(rows, kDecRowsMax);
   pl.rows = static_cast<int>(std::min<int64_t>(rows, S));
   pl.splits = static_cast<int>((S + rows - 1) / rows);
   return pl;
@@ -881,8 +884,27 @@ static __device__ __align__(256) float g_decode_noalloc_scratch[kNoAllocScratchB
 
 // Device address of the array on the current device. In host code the array's name only
 // stands for it; the real address must be looked up once per device, with that device current.
+// The cached address belongs to the CUDA context it was looked up in: after cudaDeviceReset, or
+// under another context on the same device, the module is loaded again and the array can move,
+// so each cache entry records its context and a different current context repeats the lookup.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
 std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[64] = {nullptr};
+CUcontext g_noalloc_ctx[64] = {nullptr};
 
 float* noalloc_scratch(int* rc) {
   int dev = 0;
@@ -891,8 +913,17 @@ float* noalloc_scratch(int* rc) {
     *rc = BDH_ERR_CUDA;
     return nullptr;
   }
+  const CtxGetCurrentFn get_ctx = ctx_get_current_fn();
+  if (get_ctx == nullptr) {
+    set_error("tril_decode_noalloc: the driver has no cuCtxGetCurrent");
+    *rc = BDH_ERR_CUDA;
+    return nullptr;
+  }
+  // null before the runtime has bound a context on this thread; the lookup below binds one
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (g_noalloc_ptr[dev] == nullptr || ctx == nullptr || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -900,7 +931,13 @@ float* noalloc_scratch(int* rc) {
       *rc = BDH_ERR_CUDA;
       return nullptr;
     }
+    if (get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+      set_error("tril_decode_noalloc: no current CUDA context after the address lookup");
+      *rc = BDH_ERR_CUDA;
+      return nullptr;
+    }
     g_noalloc_ptr[dev] = static_cast<float*>(p);
+    g_noalloc_ctx[dev] = ctx;
   }
   *rc = BDH_OK;
   return g_noalloc_ptr[dev];

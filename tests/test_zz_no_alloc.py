@@ -118,3 +118,26 @@ def test_noalloc_rejects_problems_beyond_the_fixed_scratch():
     assert rc == 1
     msg = lib.bdh_last_error().decode()
     assert "scratch" in msg and str(8 << 20) in msg
+
+
+def test_noalloc_decode_at_the_split_cap_and_multi_query():
+    """Sizes that push the plan to its limits, both checked against bdh_tril_decode.
+
+    B*H = 256, D = 256, S = 4000: the fixed scratch holds 32 split partials, so the plan must
+    lengthen each split to 128 cached rows (the most a CTA takes) to stay within it. Then a
+    block of three queries (Tq = 3), whose partials take three times the room per split.
+    """
+    from kernels import sm100_attn
+
+    lib = _lib()
+    for call, (B, H, Tq, S, N, D, kvdt) in enumerate(((64, 4, 1, 4000, 512, 256, torch.bfloat16),
+                                                     (2, 4, 3, 300, 1024, 128, torch.float32))):
+        g = torch.Generator(device=DEV).manual_seed(300 + call)
+        kp = torch.randn(B, H, S, N, device=DEV, generator=g).to(kvdt)
+        vp = torch.randn(B, 1, S, D, device=DEV, generator=g).to(kvdt)
+        q = torch.randn(B, H, Tq, N, device=DEV, generator=g)
+        ref = sm100_attn.tril_decode(q, kp, vp)
+        out = _noalloc(lib, q, kp, vp)
+        torch.cuda.synchronize()
+        assert _rel(out, ref) <= 1e-5, f"case {call}"
+    assert sm100_attn.device_error() == 0
