@@ -3,7 +3,8 @@
 Plain nvcc, no torch extension machinery: every .cu / .cpp under csrc/ is compiled for
 sm_100a (-gencode arch=compute_100a,code=sm_100a) with -lineinfo, linked with a static CUDA
 runtime into one shared object next to this file. Rebuilds only when a source or header is
-newer than the library. Run as a script or call build().
+newer than the library, and then only the objects whose source (or any header) changed; the
+sources compile in parallel. Run as a script or call build().
 """
 
 from __future__ import annotations
@@ -59,17 +60,32 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         return LIB
     BUILD.mkdir(exist_ok=True)
     nvcc = _nvcc()
-    objs = []
-    logs = []
-    for src in _sources():
+    headers = [p for p in _deps() if p.suffix in (".h", ".cuh")]
+    newest_header = max((p.stat().st_mtime for p in headers), default=0.0)
+
+    def compile_one(src: Path):
         obj = BUILD / (src.name + ".o")
+        log = BUILD / (src.name + ".log")
+        if (not force and obj.exists() and log.exists()
+                and obj.stat().st_mtime >= max(src.stat().st_mtime, newest_header)):
+            return str(obj), log.read_text(), 0
         cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-c", str(src), "-o", str(obj)]
         r = subprocess.run(cmd, capture_output=True, text=True)
-        logs.append(f"$ {' '.join(cmd)}\n{r.stdout}{r.stderr}")
-        if r.returncode != 0:
-            sys.stderr.write("\n".join(logs))
-            raise RuntimeError(f"nvcc failed on {src.name}")
-        objs.append(str(obj))
+        text = f"$ {' '.join(cmd)}\n{r.stdout}{r.stderr}"
+        if r.returncode == 0:
+            log.write_text(text)
+        return str(obj), text, r.returncode
+
+    from concurrent.futures import ThreadPoolExecutor
+
+    with ThreadPoolExecutor(max_workers=max(1, min(8, os.cpu_count() or 1))) as pool:
+        results = list(pool.map(compile_one, _sources()))
+    objs = [o for o, _, _ in results]
+    logs = [t for _, t, _ in results]
+    failed = [Path(o).name for o, _, rc in results if rc != 0]
+    if failed:
+        sys.stderr.write("\n".join(logs))
+        raise RuntimeError(f"nvcc failed on {', '.join(failed)}")
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc, *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *objs]
     r = subprocess.run(cmd, capture_output=True, text=True)

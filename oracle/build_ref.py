@@ -8,7 +8,8 @@ g++ through ``torch.utils.cpp_extension.load`` (the same compiler driver the ref
 the resulting ``bdh_ref_ext*.so`` go to ``oracle/_ref/`` (git-ignored; it travels to the GPU
 host with the working tree, where ``load()`` imports the prebuilt module without the sources).
 
-Usage: ``python oracle/build_ref.py [/path/to/reference]``.
+Usage: ``python oracle/build_ref.py [/path/to/reference]``; without an argument the checkout is
+``$BDH_REFERENCE`` or the ``reference_path`` of ``BASELINE.json``.
 """
 
 from __future__ import annotations
@@ -22,8 +23,26 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 REF_OUT = HERE / "_ref"
-DEFAULT_REFERENCE = Path(os.environ.get("BDH_REFERENCE", "/root/reference"))
 NAME = "bdh_ref_ext"
+
+
+def reference_root() -> Path | None:
+    """Where the reference checkout is: ``$BDH_REFERENCE``, else the ``reference_path`` recorded
+    in the repository's ``BASELINE.json``; None when neither names an existing directory."""
+    env = os.environ.get("BDH_REFERENCE")
+    cands = [Path(env)] if env else []
+    try:
+        import json
+
+        rec = json.loads((HERE.parent / "BASELINE.json").read_text())
+        if rec.get("reference_path"):
+            cands.append(Path(rec["reference_path"]))
+    except (OSError, ValueError):
+        pass
+    for c in cands:
+        if c.is_dir():
+            return c
+    return None
 
 
 def built_path() -> Path | None:
@@ -31,8 +50,12 @@ def built_path() -> Path | None:
     return Path(hits[0]) if hits else None
 
 
-def build(reference: Path = DEFAULT_REFERENCE, verbose: bool = False) -> Path:
+def build(reference: Path | None = None, verbose: bool = False) -> Path:
     """Compile the reference CPU extension (if the reference sources are present)."""
+    if reference is None:
+        reference = reference_root()
+    if reference is None:
+        raise FileNotFoundError("no reference checkout: set BDH_REFERENCE")
     src = [reference / "csrc" / "tril_attn_cpu.cpp", reference / "csrc" / "tril_attn_bind.cpp"]
     if not all(p.exists() for p in src):
         raise FileNotFoundError(f"reference sources not found under {reference}/csrc")
@@ -72,5 +95,5 @@ def load_module():
 
 
 if __name__ == "__main__":
-    ref = Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_REFERENCE
+    ref = Path(sys.argv[1]) if len(sys.argv) > 1 and sys.argv[1] != "-v" else None
     print(build(ref, verbose="-v" in sys.argv))
