@@ -26,6 +26,7 @@ projections.
 
 from __future__ import annotations
 
+import contextlib
 import dataclasses
 import math
 import os
@@ -338,6 +339,37 @@ class BDH(nn.Module):
         # gated product), so the latents are never rewritten just to clamp them.
         fused = impl == "cuda_sm100" and not grad and (not self.training or self.drop.p == 0.0)
         latent = self._latent_fusable(impl, T, cache, x.device)
+        with self._score_rounding(impl):
+            x = self._layers(x, impl, grad, fused, latent, rope_start, cache, B, T, N)
+        if cache is not None:
+            cache.commit()
+        if logits_out is not None:
+            if T != 1:
+                raise ValueError("logits_out requires T==1 decode")
+            torch.mm(x[:, -1, :].to(logits_out.dtype), self.lm_head.to(logits_out.dtype), out=logits_out)
+            return logits_out, None
+        logits = F.linear(x, self.lm_head.t())
+        loss = None
+        if targets is not None:
+            loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1))
+        return logits, loss
+
+    @staticmethod
+    def _score_rounding(impl: str):
+        """bf16 attention scores on the native path are rounded once to bf16 before their
+        product with V, as the reference model's default (eager) attention does under autocast
+        (``(QR @ QR.mT).tril_(-1) @ V`` returns bf16 scores, kernels/attention.py:27-40), so the
+        model's logits follow the reference's bf16 chain. An explicit process setting
+        (``BDH_SM100_SPLIT_SCORES``) wins."""
+        if impl != "cuda_sm100" or os.environ.get("BDH_SM100_SPLIT_SCORES"):
+            return contextlib.nullcontext()
+        from kernels.sm100_attn import score_terms_scope
+
+        return score_terms_scope("bf16")
+
+    def _layers(self, x, impl, grad, fused, latent, rope_start, cache, B, T, N):
+        """The layer loop of ``forward`` (bdh.py:992-1052); returns the final residual x."""
+        C = self.config
         xb = None
         for level in range(C.n_layer):
             if latent:
@@ -397,18 +429,7 @@ class BDH(nn.Module):
                 xy = self.drop(x_bthn * F.relu(y_lat))
             y_mlp = self._decoder_product(xy, B, T, impl, grad)
             x = self._ln(x + self._ln(y_mlp))
-        if cache is not None:
-            cache.commit()
-        if logits_out is not None:
-            if T != 1:
-                raise ValueError("logits_out requires T==1 decode")
-            torch.mm(x[:, -1, :].to(logits_out.dtype), self.lm_head.to(logits_out.dtype), out=logits_out)
-            return logits_out, None
-        logits = F.linear(x, self.lm_head.t())
-        loss = None
-        if targets is not None:
-            loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1))
-        return logits, loss
+        return x
 
     @torch.inference_mode()
     def generate(self, idx: torch.Tensor, max_new_tokens: int, temperature: float = 1.0,

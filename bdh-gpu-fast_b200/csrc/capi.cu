@@ -56,8 +56,12 @@ bool use_chunked(int dtype, int64_t T) {
 // and prefix states S and the backward's dS / G and M^T are one term; the quadratic forward's P
 // stays split (its product is a small share of the forward). BDH_SM100_SPLIT_SCORES=1 splits
 // every one of them, =0 none. The fp32 path always uses the tf32 hi/lo split.
+// bdh_set_score_terms overrides both for the calling thread (the model's bf16 prefill asks for
+// one term, the reference's autocast rounding of its eager scores).
 enum ScoreTerms { kTermsDefault = -1, kTermsOne = 0, kTermsSplit = 1 };
+thread_local int g_score_terms_thread = kTermsDefault;
 int bf16_score_terms_env() {
+  if (g_score_terms_thread != kTermsDefault) return g_score_terms_thread;
   static const int v = [] {
     const char* e = std::getenv("BDH_SM100_SPLIT_SCORES");
     if (e == nullptr || *e == 0) return static_cast<int>(kTermsDefault);
@@ -630,6 +634,13 @@ int bdh_set_forward_algo(int algo) {
   if (algo != BDH_FWD_AUTO && algo != BDH_FWD_QUADRATIC && algo != BDH_FWD_CHUNKED)
     return -1;
   return g_fwd_algo.exchange(algo);
+}
+
+int bdh_set_score_terms(int mode) {
+  if (mode != BDH_SCORES_DEFAULT && mode != BDH_SCORES_ONE && mode != BDH_SCORES_SPLIT) return -2;
+  const int prev = g_score_terms_thread;
+  g_score_terms_thread = mode;
+  return prev;
 }
 
 size_t bdh_tril_decode_workspace_size(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N,

@@ -22,6 +22,7 @@ library's scratch workspace) comes from the PyTorch caching allocator on the cur
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 from pathlib import Path
@@ -39,7 +40,7 @@ _F32 = 0
 _BF16 = 1
 
 _c_i64_4 = ctypes.c_int64 * 4
-ABI_VERSION = 6  # BDH_ABI_VERSION of include/bdh_sm100.h
+ABI_VERSION = 7  # BDH_ABI_VERSION of include/bdh_sm100.h
 FP8 = torch.float8_e4m3fn  # the opt-in fp8 key-cache storage dtype
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -58,6 +59,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.bdh_decoder_f32.argtypes = [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _vp]
     lib.bdh_set_forward_algo.argtypes = [ctypes.c_int]
     lib.bdh_set_forward_algo.restype = ctypes.c_int
+    lib.bdh_set_score_terms.argtypes = [ctypes.c_int]
+    lib.bdh_set_score_terms.restype = ctypes.c_int
     lib.bdh_tril_score_v_workspace_size.restype = ctypes.c_size_t
     lib.bdh_tril_score_v_workspace_size.argtypes = [ctypes.c_int, _i64, _i64, _i64, _i64, _i64,
                                                     _i64, ctypes.c_int]
@@ -289,9 +292,39 @@ def set_forward_algo(algo: str) -> str:
     return {v: k for k, v in FWD_ALGOS.items()}[prev]
 
 
+SCORE_TERMS = {"default": -1, "bf16": 0, "split": 1}
+
+
+@contextlib.contextmanager
+def score_terms_scope(mode: Optional[str]):
+    """For the calling thread, how bf16 score-like operands enter their second tensor-core
+    product: ``"bf16"`` rounds each fp32 score once to bf16 (the reference's autocast chain,
+    ``(q @ k.mT).tril_(-1) @ v`` with bf16 scores), ``"split"`` keeps it exact as a bf16 hi + lo
+    pair, ``"default"``/None the process default. fp32 inputs are unaffected."""
+    if mode is None:
+        yield
+        return
+    if mode not in SCORE_TERMS:
+        raise ValueError(f"score terms must be one of {sorted(SCORE_TERMS)}, got {mode!r}")
+    lib = _require_lib()
+    prev = lib.bdh_set_score_terms(SCORE_TERMS[mode])
+    try:
+        yield
+    finally:
+        lib.bdh_set_score_terms(prev)
+
+
 # -------------------------------------------------------------------------- forward
-def tril_score_v(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
-    """``(q @ k.mT).tril(-1) @ v`` on the sm_100a tensor cores (fp32 accumulation)."""
+def tril_score_v(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                 score_terms: Optional[str] = None) -> torch.Tensor:
+    """``(q @ k.mT).tril(-1) @ v`` on the sm_100a tensor cores (fp32 accumulation).
+
+    ``score_terms`` (bf16 inputs): ``"bf16"`` rounds the scores to bf16 before the product with
+    ``v`` as the reference's eager autocast path does, ``"split"`` keeps them exact; None: the
+    process default (exact for the quadratic form)."""
+    if score_terms is not None:
+        with score_terms_scope(score_terms):
+            return tril_score_v(q, k, v)
     _check_cold_shapes(q, k, v)
     dev = _require_cuda(q, k, v)
     lib = _require_lib()
@@ -921,4 +954,5 @@ __all__ = [
     "rope_rotate",
     "relu_mul",
     "set_forward_algo",
+    "score_terms_scope",
 ]

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define BDH_ABI_VERSION 6
+#define BDH_ABI_VERSION 7
 
 #define BDH_DTYPE_F32 0
 #define BDH_DTYPE_BF16 1
@@ -89,6 +89,23 @@ int bdh_relu_mul(const void* x, const int64_t x_strides[4], const void* y,
 #define BDH_FWD_CHUNKED 2
 int bdh_set_forward_algo(int algo);
 
+/*
+ * bf16 score-like operands (P of the forward, the chunked prefix states, G and M^T of the
+ * backward) for the calling thread only: BDH_SCORES_ONE rounds each fp32 sum once to bf16
+ * before the next tensor-core product, as the reference's bf16 matmul chain does
+ * (kernels/attention.py:27-40: (q @ k.mT).tril_(-1) @ v returns bf16 scores under autocast);
+ * BDH_SCORES_SPLIT keeps it exact as a bf16 hi + lo pair (twice the work of the consuming
+ * product); BDH_SCORES_DEFAULT returns to the process default (BDH_SM100_SPLIT_SCORES, else the
+ * quadratic forward's P split and every other operand one term). The workspace-size queries
+ * follow the same setting, so set it before querying. fp32 inputs are unaffected (always the
+ * exact tf32 split). Returns the previous setting of the thread, or -2 for an unknown mode.
+ * No counterpart in the reference (a knob of this build's kernels).
+ */
+#define BDH_SCORES_DEFAULT (-1)
+#define BDH_SCORES_ONE 0
+#define BDH_SCORES_SPLIT 1
+int bdh_set_score_terms(int mode);
+
 /* Scratch bytes bdh_tril_score_v needs for these sizes (dtype of q/k/v). */
 size_t bdh_tril_score_v_workspace_size(int dtype, int64_t B, int64_t H, int64_t Hv, int64_t T,
                                        int64_t N, int64_t D, int k_is_q);
@@ -142,7 +159,10 @@ int bdh_tril_decode(const void* q, const int64_t q_strides[4], int q_dtype, cons
  * The new queries are rotated inside the decode kernel here (the workspace form rotates them
  * once in a separate pass).
  * The first call on each device looks the array's device address up (cudaGetSymbolAddress)
- * with that device current: make that first call before any stream capture begins.
+ * with that device current: make that first call before any stream capture begins. The address
+ * is remembered per device together with the CUDA context it was found in; a call under another
+ * current context (after cudaDeviceReset, or a context the caller created) looks it up again,
+ * so such a call, too, must not be the first one inside a stream capture.
  * All calls on a device share the array and it keeps the last call's contents; every
  * element a call reads is written by the same call first, so nothing needs clearing, but
  * calls whose work overlaps on the GPU (different streams, no ordering) race on it.

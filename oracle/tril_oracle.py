@@ -256,45 +256,61 @@ def bdh_forward(idx: np.ndarray, weights: dict, n_layer: int, n_head: int, acc=n
     return x.reshape(B, T, D) @ head
 
 
-def bdh_forward_bf16(idx: np.ndarray, weights: dict, n_layer: int, n_head: int,
-                     rounding: bool = True):
-    """Logits of the BDH forward under bf16 autocast with fp32 accumulation everywhere.
+def bdh_layer_bf16(x: np.ndarray, weights: dict, n_head: int, rounding: bool = True,
+                   round_scores: bool = True):
+    """One BDH layer under bf16 autocast with fp32 accumulation (bdh.py:991-1052 as
+    torch.autocast(bfloat16) runs it on a GPU): returns (x_out, attention output).
 
-    The layer of bdh.py:991-1052 as torch.autocast(bfloat16) runs it, except that the
-    attention keeps fp32 accumulation over the T x T scores (the reference's native
-    tril_score_v, csrc/tril_attn_cuda.cu, instead of the eager bf16 matmul that rounds every
-    score): every GEMM takes bf16 operands, accumulates exactly and rounds its output to bf16;
-    LayerNorm runs in fp32 on its (bf16 or fp32) input; the RoPE rotates bf16 values with fp32
-    cos/sin as kernels/rope.py:108-126; the sparse product is rounded to bf16.
-    rounding=False gives the same sequence with every bf16 rounding removed.
+    Every GEMM takes bf16 operands, accumulates exactly and rounds its output to bf16; LayerNorm
+    runs in fp32 on its (bf16 or fp32) input (CUDA autocast's fp32 policy for layer_norm; the
+    CPU autocast leaves it in bf16, bdh.py:731-750 then keeps a bf16 residual stream); the RoPE
+    rotates bf16 values with fp32 cos/sin as kernels/rope.py:108-126; the sparse product is
+    rounded to bf16. round_scores: the T x T scores are rounded to bf16 before their product
+    with V, as the reference's default eager attention returns them under autocast
+    (kernels/attention.py:27-40); False keeps them exact (its native tril_score_v,
+    csrc/tril_attn_cuda.cu, accumulates them in fp32). rounding=False removes every bf16
+    rounding. x: (B, T, D) float32 residual stream entering the layer.
     """
     r = bf16_round if rounding else (lambda a: np.asarray(a, np.float32))
-    emb = np.asarray(weights["embed"], np.float32)
     enc = r(np.asarray(weights["encoder"], np.float32)).astype(np.float64)
     enc_v = r(np.asarray(weights["encoder_v"], np.float32)).astype(np.float64)
     dec = r(np.asarray(weights["decoder"], np.float32)).astype(np.float64)
-    head = r(np.asarray(weights["lm_head"], np.float32)).astype(np.float64)
     freqs = np.asarray(weights["freqs"], dtype=np.float32)
-    B, T = idx.shape
+    B, T, _ = x.shape
     nh = n_head
     N = enc.shape[-1]
 
     def gemm(a, w, eq):
         return r(np.einsum(eq, r(a).astype(np.float64), w, optimize=True).astype(np.float32))
 
+    x = np.asarray(x, np.float32)
+    xs = np.maximum(gemm(x, enc, "btd,hdn->bthn"), np.float32(0.0))  # B,T,nh,N
+    qr = rope(np.swapaxes(xs, 1, 2), freqs, bf16=rounding).astype(np.float64)  # B,nh,T,N
+    s = np.einsum("bhtn,bhsn->bhts", qr, qr, optimize=True).astype(np.float32)
+    if round_scores:
+        s = r(s)
+    s = np.tril(s, -1).astype(np.float64)
+    v = r(x)[:, None].astype(np.float64)
+    y = r(np.einsum("bhts,bxsd->bhtd", s, v, optimize=True).astype(np.float32))
+    yn = layer_norm(y).astype(np.float32)
+    ys = np.maximum(gemm(yn, enc_v, "bhtd,hdn->bthn"), np.float32(0.0))
+    xy = r(xs * ys)
+    ymlp = gemm(xy.reshape(B, T, nh * N), dec, "btk,kd->btd")
+    return layer_norm(x + layer_norm(ymlp).astype(np.float32)).astype(np.float32), y
+
+
+def bdh_forward_bf16(idx: np.ndarray, weights: dict, n_layer: int, n_head: int,
+                     rounding: bool = True, round_scores: bool = True):
+    """Logits of the BDH forward under bf16 autocast with fp32 accumulation everywhere
+    (bdh.py:947-1072): the embedding's LayerNorm in fp32, ``bdh_layer_bf16`` per layer, then
+    the bf16 lm_head GEMM. Arguments as ``bdh_layer_bf16``."""
+    r = bf16_round if rounding else (lambda a: np.asarray(a, np.float32))
+    emb = np.asarray(weights["embed"], np.float32)
+    head = r(np.asarray(weights["lm_head"], np.float32)).astype(np.float64)
     x = layer_norm(emb[idx]).astype(np.float32)  # B,T,D fp32
     for _ in range(n_layer):
-        xs = np.maximum(gemm(x, enc, "btd,hdn->bthn"), np.float32(0.0))  # B,T,nh,N
-        qr = rope(np.swapaxes(xs, 1, 2), freqs, bf16=rounding)  # B,nh,T,N
-        v = r(x)[:, None]
-        y = r(tril_score_v(qr.astype(np.float64), qr.astype(np.float64),
-                           v.astype(np.float64)).astype(np.float32))
-        yn = layer_norm(y).astype(np.float32)
-        ys = np.maximum(gemm(yn, enc_v, "bhtd,hdn->bthn"), np.float32(0.0))
-        xy = r(xs * ys)
-        ymlp = gemm(xy.reshape(B, T, nh * N), dec, "btk,kd->btd")
-        x = layer_norm(x + layer_norm(ymlp).astype(np.float32)).astype(np.float32)
-    return gemm(x, head, "btd,dv->btv")
+        x, _ = bdh_layer_bf16(x, weights, n_head, rounding, round_scores)
+    return r(np.einsum("btd,dv->btv", r(x).astype(np.float64), head, optimize=True).astype(np.float32))
 
 
 def latent_encode(x: np.ndarray, enc: np.ndarray, freqs: np.ndarray, pos0: int = 0,

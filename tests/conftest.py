@@ -44,3 +44,26 @@ def golden(name: str):
     import numpy as np
 
     return np.load(GOLDEN / f"golden_{name}.npz")
+
+
+def config2_case():
+    """The config-2-width case of golden_config2_bf16.npz (tests/golden/config2_case.py)."""
+    if str(GOLDEN) not in sys.path:
+        sys.path.insert(0, str(GOLDEN))
+    import config2_case
+
+    return config2_case
+
+
+def reference_bf16_floor(g) -> float:
+    """The reference's own execution-to-execution spread of its config-2-width bf16 logits
+    (golden_config2_bf16.npz): the same autocast run with one CPU thread and with ATen's GEMMs
+    instead of oneDNN's, each against the stored run. Only fp32 accumulation orders differ."""
+    import numpy as np
+
+    ref = g["logits_bf16_cuda_policy"].astype(np.float64)
+
+    def rel(a):
+        return float(np.linalg.norm(a.astype(np.float64) - ref) / np.linalg.norm(ref))
+
+    return max(rel(g["logits_bf16_cuda_policy_1thread"]), rel(g["logits_bf16_cuda_policy_aten_gemm"]))

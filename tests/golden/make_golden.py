@@ -4,7 +4,9 @@ Run in the build container (the reference checkout is not available on GPU hosts
 
     PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py <reference checkout>
 
-(default: the ``BDH_REFERENCE`` environment variable, else the checkout path build_ref.py uses)
+(default: the ``BDH_REFERENCE`` environment variable, else the ``reference_path`` of
+BASELINE.json, as oracle/build_ref.py resolves it; ``--config2-only`` / ``--latent-only``
+rewrite one fixture)
 
 It imports the reference's own Python modules (``bdh``, ``bdh_baseline``, ``bdh_cache``,
 ``kernels``) and its CPU extension built by ``oracle/build_ref.py`` (``csrc/tril_attn_cpu.cpp``),
@@ -154,6 +156,7 @@ def main(reference: Path) -> None:
         mod["logits_cached_steps"] = np.stack(steps)
     np.savez_compressed(HERE / "golden_model.npz", **mod)
     latent_fixture(bdh, HERE)
+    config2_bf16_fixture(bdh, HERE)
     print("wrote", sorted(p.name for p in HERE.glob("golden_*.npz")))
 
 
@@ -184,6 +187,103 @@ def latent_fixture(bdh, out_dir: Path) -> None:
     np.savez_compressed(out_dir / "golden_latent.npz", **lat)
 
 
+def config2_bf16_fixture(bdh, out_dir: Path) -> None:
+    """The reference model at config-2 width (config2_case.py) under bf16 autocast on the CPU,
+    as bdh.py's AMP path runs it (bdh.py:486-500, default eager attention
+    ``(QR @ QR.mT).tril_(-1) @ V``, kernels/attention.py:27-40).
+
+    The two autocast device types cast differently: CUDA's autocast runs ``layer_norm`` in fp32
+    (fp32 policy) while the CPU's leaves it in its input dtype, so on the CPU the residual stream
+    x = LN(x + LN(y_mlp)) (bdh.py:731-750) becomes bf16 after the first layer and on a GPU it
+    stays fp32. Two runs are stored: ``*_cpu`` with the stock CPU autocast, and ``*_cuda_policy``
+    with CUDA's cast for ``layer_norm`` applied on the CPU (its input cast to fp32 by a
+    TorchFunctionMode, what CUDA autocast does for that op); the reference code itself is
+    unchanged. For each: logits and the attention output of every layer (bf16, stored as bit
+    patterns); for the CUDA policy also the residual stream entering and leaving every layer
+    (fp32), and the logits of two other executions of the same run (one thread; ATen's GEMMs),
+    whose spread is the reference's own floor. Also the fp32 logits without autocast."""
+    import torch
+    import torch.nn.functional as F
+    from torch.overrides import TorchFunctionMode
+
+    class LayerNormFp32(TorchFunctionMode):
+        def __torch_function__(self, func, types, args=(), kwargs=None):
+            kwargs = kwargs or {}
+            if func is F.layer_norm and args and args[0].dtype in (torch.bfloat16, torch.float16):
+                args = (args[0].float(),) + tuple(args[1:])
+            return func(*args, **kwargs)
+
+    sys.path.insert(0, str(HERE))
+    import config2_case as C
+
+    cfg = bdh.BDHConfig(n_layer=C.N_LAYER, n_embd=C.N_EMBD, n_head=C.N_HEAD,
+                        mlp_internal_dim_multiplier=C.MULT, dropout=0.0, vocab_size=C.VOCAB)
+    model = bdh.BDH(cfg).eval()
+    w = C.make_weights()
+    sd = model.state_dict()
+    for k, v in w.items():
+        assert tuple(sd[k].shape) == v.shape, k
+        sd[k] = torch.from_numpy(v)
+    model.load_state_dict(sd)
+    idx = torch.from_numpy(C.make_idx())
+    attn_out = []
+    hook = model.attn.register_forward_hook(lambda m, a, o: attn_out.append(o[0].detach().clone()))
+    fix = {"idx": idx.numpy()}
+    from contextlib import nullcontext
+
+    # the residual stream entering each layer and leaving it (instance-level wrappers of the
+    # model's own helpers; the reference code is not changed)
+    layer_in, layer_out = [], []
+    enc_fwd, res_ln = model._encoder_relu_fwd, model._residual_ln
+
+    def enc_hook(x):
+        layer_in.append(x.detach().clone())
+        return enc_fwd(x)
+
+    def res_hook(x, y):
+        out = res_ln(x, y)
+        layer_out.append(out.detach().clone())
+        return out
+
+    model._encoder_relu_fwd, model._residual_ln = enc_hook, res_hook
+    threads = torch.get_num_threads()
+    torch.set_num_threads(8)
+    with torch.no_grad():
+        for tag, mode in (("cpu", nullcontext()), ("cuda_policy", LayerNormFp32())):
+            attn_out.clear()
+            layer_in.clear()
+            layer_out.clear()
+            with mode, torch.autocast(device_type="cpu", dtype=torch.bfloat16):
+                logits, _ = model(idx)
+            assert len(attn_out) == C.N_LAYER and attn_out[0].dtype == torch.bfloat16
+            fix[f"logits_bf16_{tag}"] = _f32(logits)
+            for i, a in enumerate(attn_out):
+                fix[f"attn_out_bf16_bits_{tag}_l{i}"] = (
+                    a.contiguous().view(torch.int16).numpy().view(np.uint16))
+            if tag == "cuda_policy":
+                for i in range(C.N_LAYER):
+                    assert layer_in[i].dtype == torch.float32 and layer_out[i].dtype == torch.float32
+                    fix[f"layer_in_l{i}"] = _f32(layer_in[i])
+                    fix[f"layer_out_l{i}"] = _f32(layer_out[i])
+        # The same reference bf16 run executed differently: one CPU thread, and ATen's own CPU
+        # GEMMs instead of oneDNN's. Only the order of the fp32 accumulations inside each GEMM
+        # changes; the spread of these logits is the reference's own execution-to-execution floor.
+        torch.set_num_threads(1)
+        with LayerNormFp32(), torch.autocast(device_type="cpu", dtype=torch.bfloat16):
+            fix["logits_bf16_cuda_policy_1thread"] = _f32(model(idx)[0])
+        torch.set_num_threads(8)
+        with torch.backends.mkldnn.flags(enabled=False), LayerNormFp32(), \
+                torch.autocast(device_type="cpu", dtype=torch.bfloat16):
+            fix["logits_bf16_cuda_policy_aten_gemm"] = _f32(model(idx)[0])
+        hook.remove()
+        model._encoder_relu_fwd, model._residual_ln = enc_fwd, res_ln
+        logits32, _ = model(idx)
+        fix["logits_f32"] = _f32(logits32)
+    torch.set_num_threads(threads)
+    fix["freqs"] = model.attn.freqs.reshape(-1).numpy()
+    np.savez_compressed(out_dir / "golden_config2_bf16.npz", **fix)
+
+
 def dataclasses_asdict(c):
     import dataclasses
 
@@ -197,11 +297,16 @@ if __name__ == "__main__":
         sys.path.insert(0, str(HERE.parent.parent / "oracle"))
         import build_ref
 
-        ref = build_ref.DEFAULT_REFERENCE
-    if "--latent-only" in sys.argv:
+        ref = build_ref.reference_root()
+        if ref is None:
+            sys.exit("no reference checkout: pass its path or set BDH_REFERENCE")
+    if "--latent-only" in sys.argv or "--config2-only" in sys.argv:
         sys.path.insert(0, str(ref))
         import bdh as _bdh
 
-        latent_fixture(_bdh, HERE)
+        if "--latent-only" in sys.argv:
+            latent_fixture(_bdh, HERE)
+        else:
+            config2_bf16_fixture(_bdh, HERE)
     else:
         main(ref)

@@ -104,12 +104,11 @@ def test_gate_dec_rejects_unsupported_layouts():
 def test_model_gate_dec_matches_gate_then_cublas(monkeypatch):
     """The model's layer with the fused gate + decoder (default) and with the gate followed by
     cuBLAS's decoder GEMM (BDH_SM100_GATE_DEC=0): one fused launch per layer, logits within the
-    end-to-end bound of the other model tests (1e-2: two layers of LayerNorm amplify the last-bit
-    differences of a different decoder summation order; the kernel itself is held to 3e-3
-    above)."""
+    bf16 bar (one layer; the two decoder summation orders flip a few bf16 outputs, which
+    further layers would amplify)."""
     import bdh_model
 
-    cfg = bdh_model.BDHConfig(n_layer=2, n_embd=256, n_head=4, mlp_internal_dim_multiplier=128,
+    cfg = bdh_model.BDHConfig(n_layer=1, n_embd=256, n_head=4, mlp_internal_dim_multiplier=128,
                               vocab_size=256, dropout=0.0)
     torch.manual_seed(3)
     m = bdh_model.BDH(cfg).to(DEV).eval()
@@ -123,5 +122,5 @@ def test_model_gate_dec_matches_gate_then_cublas(monkeypatch):
             sa().profile_begin()
             out[flag] = m(idx)[0].float()
             cnt = {k: v["launches"] for k, v in sa().profile_end().items()}
-        assert cnt["gate"] == 2, cnt
-    assert ((out["1"] - out["0"]).norm() / out["0"].norm()).item() < 1e-2
+        assert cnt["gate"] == 1, cnt
+    assert ((out["1"] - out["0"]).norm() / out["0"].norm()).item() < 3e-3

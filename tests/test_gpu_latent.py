@@ -217,40 +217,37 @@ def _launch_counts(fn):
 
 
 def test_model_latent_layer_matches_unfused_and_oracle(monkeypatch):
-    """Fused latent layers vs the unfused sm100 layers (the same arithmetic: bf16 GEMM outputs,
-    bf16 RoPE and product), and vs the float64 oracle of the bf16-autocast forward.
-
-    End to end, bf16 activations put a noise floor under any comparison of two independent
-    implementations of this randomly initialised model: the oracle against itself with the
-    attention accumulated in float32 instead of float64 already moves the logits by 2.5e-3
-    (LayerNorm of the attention output amplifies its last-bit rounding). The end-to-end bound
-    is therefore 1e-2, and the 3e-3 bound is applied stage by stage below."""
-    m = _model(n_layer=2)
+    """Fused latent layer vs the unfused sm100 layer (the same arithmetic: bf16 GEMM outputs,
+    bf16 RoPE and product, scores rounded to bf16 before the value product), and vs the float64
+    oracle of the bf16-autocast forward, all within the bf16 bar. One layer: through more
+    layers every bf16 rounding point that flips with the accumulation order grows (two faithful
+    executions of the reference's own bf16 model differ by about 3e-3 at two layers); the
+    multi-layer end-to-end check is against the reference's logits in
+    test_gpu_config2_parity.py."""
+    m = _model(n_layer=1)
     idx = torch.randint(0, 256, (2, 128), generator=torch.Generator().manual_seed(9)).to(DEV)
     res = {}
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         monkeypatch.setenv("BDH_SM100_LATENT", "1")
         assert m._latent_fusable("cuda_sm100", 128, None, idx.device)
         cnt = _launch_counts(lambda: res.setdefault("fused", m(idx)[0].float()))
-        assert cnt["encode"] == 2 and cnt["gate"] == 2 and cnt["rope"] == 0, cnt
-        # the same arithmetic as the unfused layers: the gate followed by cuBLAS's decoder (the
-        # fused gate + decoder sums the decoder product in its own order, which at these small
-        # shapes cuBLAS may not share; its own model test is in test_gpu_gate_dec.py)
+        assert cnt["encode"] == 1 and cnt["gate"] == 1 and cnt["rope"] == 0, cnt
+        # the same arithmetic as the unfused layers: the gate followed by cuBLAS's decoder
         monkeypatch.setenv("BDH_SM100_GATE_DEC", "0")
         res["fused_cublas_dec"] = m(idx)[0].float()
         monkeypatch.setenv("BDH_SM100_LATENT", "0")
         cnt = _launch_counts(lambda: res.setdefault("plain", m(idx)[0].float()))
-        assert cnt["encode"] == 0 and cnt["rope"] == 2, cnt
+        assert cnt["encode"] == 0 and cnt["rope"] == 1, cnt
     fused, plain = res["fused"], res["plain"]
     fc = res["fused_cublas_dec"]
     assert ((fc - plain).norm() / plain.norm()).item() < 1e-3
-    assert ((fused - plain).norm() / plain.norm()).item() < 1e-2
+    assert ((fused - plain).norm() / plain.norm()).item() < 3e-3
     w = {k: getattr(m, k).detach().to(torch.bfloat16).float().cpu().numpy()
          for k in ("encoder", "encoder_v", "decoder", "lm_head")}
     w["embed"] = m.embed.weight.detach().float().cpu().numpy()
     w["freqs"] = m.attn.freqs.reshape(-1).cpu().numpy()
-    ref16 = O.bdh_forward_bf16(idx.cpu().numpy(), w, n_layer=2, n_head=4)
-    assert O.rel_fro(f32(fused), ref16) < 1e-2
+    ref16 = O.bdh_forward_bf16(idx.cpu().numpy(), w, n_layer=1, n_head=4)
+    assert O.rel_fro(f32(fused), ref16) < 3e-3
 
 
 def test_model_gate_x_matches_stored_xs(monkeypatch):

@@ -160,6 +160,47 @@ def test_bf16_autocast_oracle_pinned_to_reference_model():
     assert O.rel_fro(rounded, g["logits_baseline"]) < 2e-2
 
 
+def _config2_oracle_weights(g):
+    from conftest import config2_case
+
+    w = config2_case().make_weights()
+    return {"embed": w["embed.weight"], "encoder": w["encoder"], "encoder_v": w["encoder_v"],
+            "decoder": w["decoder"], "lm_head": w["lm_head"], "freqs": g["freqs"]}
+
+
+def test_bf16_layer_oracle_pinned_to_reference_at_config2_width():
+    """Each layer of the bf16-autocast restatement, fed the reference's own residual stream
+    (teacher forcing, golden_config2_bf16: bdh.BDH at n_embd 256, 4 heads, N = 8192 under
+    autocast with CUDA's layer_norm policy), reproduces that layer's attention output and
+    output stream within the bf16 bar. The scores are rounded to bf16 as the reference's eager
+    attention rounds them; kept exact, the attention output moves by about the bar."""
+    from conftest import config2_case
+
+    C = config2_case()
+    g = golden("config2_bf16")
+    w = _config2_oracle_weights(g)
+    for layer in range(C.N_LAYER):
+        x_out, y = O.bdh_layer_bf16(g[f"layer_in_l{layer}"], w, C.N_HEAD)
+        y_ref = C.bf16_bits_to_f32(g[f"attn_out_bf16_bits_cuda_policy_l{layer}"])
+        assert O.rel_fro(y, y_ref) < 3e-3
+        assert O.rel_fro(x_out, g[f"layer_out_l{layer}"]) < 3e-3
+
+
+def test_bf16_model_oracle_pinned_to_reference_logits_at_config2_width():
+    """End to end, every bf16 rounding point of a layer can flip with the fp32 accumulation
+    order, and the flips grow through the layers: the reference's own logits move by its
+    execution floor (reference_bf16_floor: one thread or ATen's GEMMs instead of oneDNN's;
+    about 3e-3 at two layers). The oracle's float64 accumulation is one more such order."""
+    from conftest import config2_case, reference_bf16_floor
+
+    C = config2_case()
+    g = golden("config2_bf16")
+    floor = reference_bf16_floor(g)
+    assert 5e-4 < floor < 1e-2
+    logits = O.bdh_forward_bf16(g["idx"], _config2_oracle_weights(g), C.N_LAYER, C.N_HEAD)
+    assert O.rel_fro(logits, g["logits_bf16_cuda_policy"]) <= max(3e-3, floor)
+
+
 def test_state_decode_oracle_equals_history_decode():
     """The N x D state form reproduces the reference decode (golden_decode, the reference CPU
     extension's tril_decode_cpu) step by step."""
