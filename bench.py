@@ -6,20 +6,31 @@ Default workload: full BDH prefill forward under bf16 autoca
 random N(0, 0.02) weights, synthetic token ids uniform in [0, 256), B=32 x T=512 per GPU
 (weak scaling: every rank runs its own batch; no collective on the data path).
 
-    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--config 1|2|3|4|5]
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--config 1|2|3|4|5] [--only]
 
 * ``value``      tokens/s over all ranks, inputs resident in HBM (device-timed, max over ranks)
 * ``e2e``        the same through the public model API with host buffers: pinned token ids
                  copied in and logits copied out inside every timed step
-* ``roofline``   the dominant kernel of this path (the tcgen05 score pass), timed live inside
-                 the timed region with CUDA events recorded by the library around each launch
-* ``cpu_baseline`` the reference's own CPU extension (``csrc/tril_attn_cpu.cpp``, built into
-                 oracle/_ref) inside the same model on the host cores, on a bounded sample
-* ``--impl reference`` runs only that CPU reference arm (rank 0) on this config's metric.
+* ``roofline``   the kernel with the most device time in the step (``rooflines``: the three
+                 largest), timed live inside the timed region with CUDA events recorded by the
+                 library around each launch on its own stream; the bf16 peak is the burst figure
+                 for sub-second timed regions, the sustained one for longer ones
+* ``cpu_baseline`` the reference's baseline model (bdh_baseline.BDH restated in torch by
+                 oracle/baseline_model.py) with the attention computed by the reference's own
+                 CPU extension (``csrc/tril_attn_cpu.cpp``, built into oracle/_ref), on the host
+                 cores, on a bounded sample
+* ``gpu_eager_baseline`` the reference's eval forward op for op on this GPU (eager attention,
+                 cuBLAS projections) for the config-2 step and the config-4 decode step
+* ``configs``    the metric's other numbers on the same lease, each with its own roofline,
+                 clocks and cpu_baseline: config 4 decode tokens/s over the whole span
+                 (S = 515 .. 1023), config 5 forward + backward TFLOP/s, config 3 TFLOP/s
+* ``strong_scaling`` (N > 1) config 2 at its global batch of 32 sequences and config 5's 64
+                 (b, h) units, sharded over the ranks
+* ``--impl reference`` runs only the CPU reference arm (rank 0) on this config's metric.
+* ``--only``     the config-2 line alone.
 
-Other ``--config`` values run the standalone-op workloads (1: fp32 op, 3: long-T bf16 op,
-4: cached decode, 5: forward+backward) with the same JSON schema; they are measurement aids,
-the driver's headline is config 2.
+Other ``--config`` values run one workload (1: fp32 op, 3: long-T bf16 op, 4: cached decode,
+5: forward+backward) with the same JSON schema.
 """
 
 from __future__ import annotations
@@ -52,6 +63,19 @@ def load_peaks():
         d = json.loads(p.read_text())
         return d, "measured"
     return PEAKS_FALLBACK, "fallback"
+
+
+SUSTAINED_REGION_S = 2.0  # timed regions at least this long are held to the sustained peak
+
+
+def tensor_peak(peaks: dict, src: str, region_ms: float):
+    """bf16 tensor peak for a kernel timed inside a region of `region_ms`: the burst figure
+    (cuBLAS timed alone) for sub-second regions, the sustained one (seconds-long loop under the
+    power cap) from SUSTAINED_REGION_S on. Returns (peak, source)."""
+    if region_ms / 1e3 >= SUSTAINED_REGION_S and "bf16_tflops_sustained" in peaks:
+        return peaks["bf16_tflops_sustained"], (
+            f"{src} bf16_tflops_sustained (timed region {region_ms / 1e3:.2f} s)")
+    return peaks["bf16_tflops"], f"{src} bf16_tflops burst (timed region {region_ms / 1e3:.2f} s)"
 
 
 # ------------------------------------------------------------------------ clocks
@@ -268,57 +292,38 @@ def load_traffic(name: str, batch: int | None = None):
 
 # ------------------------------------------------------------------ CPU reference
 def cpu_reference_model(B_cpu: int, T: int, steps: int):
-    """BDH prefill on the host: the reference CPU extension computes the attention inside the
-    model (everything else is PyTorch CPU ops in fp32). Returns (tokens/s, kind, cores, sample)."""
-    import bdh_model
-    from kernels import attention_dispatch as ad
+    """BDH prefill on the host cores: the reference's baseline model (bdh_baseline.BDH,
+    restated in torch CPU fp32 by oracle/baseline_model.py) with its strictly causal attention
+    computed by the reference's own C++ extension (``tril_score_v_cpu``, built into oracle/_ref;
+    the same arithmetic in torch when that is missing). Config-2 model, random N(0, 0.02)
+    weights. Returns (tokens/s, kind, cores, sample)."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import baseline_model
 
     torch.set_num_threads(os.cpu_count() or 1)
     cores = torch.get_num_threads()
-    kind = "reference"
-    try:
-        sys.path.insert(0, str(REPO / "oracle"))
-        import build_ref
+    attn = baseline_model.reference_tril_score_v()
+    how = "the reference CPU extension (oracle/_ref)" if attn is not None else "torch (extension not built)"
+    g = torch.Generator().manual_seed(1002)
+    N = N_LAT
+    w = {"embed": torch.randn(VOCAB, D_MODEL, generator=g) * 0.02,
+         "encoder": torch.randn(N_HEAD, D_MODEL, N, generator=g) * 0.02,
+         "encoder_v": torch.randn(N_HEAD, D_MODEL, N, generator=g) * 0.02,
+         "decoder": torch.randn(N_HEAD * N, D_MODEL, generator=g) * 0.02,
+         "lm_head": torch.randn(D_MODEL, VOCAB, generator=g) * 0.02}
+    import bdh_model
 
-        ext = build_ref.load_module()
-        attn = lambda q, k, v: ext.tril_score_v_cpu(q, k, v)  # noqa: E731
-    except Exception:  # noqa: BLE001 - reference not built here: time the numpy port instead
-        import numpy as np
-
-        import tril_oracle
-
-        kind = "port"
-        attn = lambda q, k, v: torch.from_numpy(  # noqa: E731
-            tril_oracle.tril_score_v(q.numpy(), k.numpy(), v.numpy(), acc=np.float32))
-    cfg = bdh_model.BDHConfig(n_layer=N_LAYER, n_embd=D_MODEL, n_head=N_HEAD,
-                              mlp_internal_dim_multiplier=128, vocab_size=VOCAB, dropout=0.0)
-    torch.manual_seed(1002)
-    model = bdh_model.BDH(cfg).eval()
-    model.attn._attn_impl_override = "eager"
-    g = torch.Generator().manual_seed(2002)
-    idx = torch.randint(0, VOCAB, (B_cpu, T), generator=g)
-    orig = ad.eager_tril_attn
-    ad.eager_tril_attn = attn
-    try:
-        with torch.inference_mode():
-            model(idx)  # warm-up
-            t0 = time.perf_counter()
-            for _ in range(steps):
-                model(idx)
-            dt = time.perf_counter() - t0
-    finally:
-        ad.eager_tril_attn = orig
-    cpu = ""
-    try:
-        for ln in Path("/proc/cpuinfo").read_text().splitlines():
-            if ln.startswith("model name"):
-                cpu = ln.split(":", 1)[1].strip()
-                break
-    except Exception:  # noqa: BLE001
-        pass
+    w["freqs"] = bdh_model.get_freqs(N, 2 ** 16, torch.float32)
+    idx = torch.randint(0, VOCAB, (B_cpu, T), generator=torch.Generator().manual_seed(2002))
+    baseline_model.baseline_forward(idx, w, N_LAYER, N_HEAD, attn)  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        baseline_model.baseline_forward(idx, w, N_LAYER, N_HEAD, attn)
+    dt = time.perf_counter() - t0
     sample = (f"BDH prefill B={B_cpu} x T={T}, {N_LAYER} layers, fp32, {steps} timed forward(s) "
-              f"after 1 warm-up; attention by the reference CPU extension; {cores} threads; {cpu}")
-    return B_cpu * T * steps / dt, kind, cores, sample
+              f"after 1 warm-up; bdh_baseline.BDH restated in torch (oracle/baseline_model.py), "
+              f"attention by {how}; {cores} threads; {_cpu_model_name()}")
+    return B_cpu * T * steps / dt, "port", cores, sample
 
 
 def _ref_ext():
@@ -432,75 +437,32 @@ def cpu_decode_baseline(steps: int = 4):
 
 
 # --------------------------------------------------------------------- config 2
-def bench_config2(args, world, rank, dev):
+def config2_model(dev, impl: str = "cuda_sm100"):
+    """The config-2 model (identical random N(0, 0.02) weights on every rank)."""
     import bdh_model
-    from kernels import sm100_attn
 
-    B, T = args.batch or 32, 512
     cfg = bdh_model.BDHConfig(n_layer=N_LAYER, n_embd=D_MODEL, n_head=N_HEAD,
                               mlp_internal_dim_multiplier=128, vocab_size=VOCAB, dropout=0.0)
-    torch.manual_seed(1002)  # identical weights on every rank
+    torch.manual_seed(1002)
     model = bdh_model.BDH(cfg).to(dev).eval()
-    model.attn._attn_impl_override = "cuda_sm100"
-    g = torch.Generator().manual_seed(rank_seed(2002, rank))
-    idx_host = torch.randint(0, VOCAB, (B, T), generator=g).pin_memory()
-    idx = idx_host.to(dev)
+    model.attn._attn_impl_override = impl
+    return model
 
-    def step():
-        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
-            return model(idx)[0]
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(dev)
-    assert sm100_attn.device_error(dev) == 0
-    clocks = ClockSampler(dev)
-    clocks.start()
-    profile_begin()
-    ms = timed(step, args.steps, world, dev)
-    prof = profile_end()
-    clk = clocks.stop()
-    value = world * B * T * args.steps / (ms / 1e3)
-
-    # end to end through the public API with host buffers
-    idx_dev = torch.empty_like(idx)
-    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
-        out_shape = model(idx)[0].shape
-    logits_host = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
-
-    def e2e_step():
-        idx_dev.copy_(idx_host, non_blocking=True)
-        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
-            logits = model(idx_dev)[0]
-        logits_host.copy_(logits, non_blocking=True)
-
-    def verify_logits():
-        gv = torch.Generator().manual_seed(4242)  # the same batch on every rank
-        iv = torch.randint(0, VOCAB, (2, 256), generator=gv).to(dev)
-        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
-            return model(iv)[0].float()
-
-    xcheck = cross_rank_check(verify_logits, world, dev)
-    for _ in range(max(1, args.warmup)):
-        e2e_step()
-    ms_e2e = timed(e2e_step, args.steps, world, dev)
-    torch.cuda.synchronize(dev)
-    e2e = world * B * T * args.steps / (ms_e2e / 1e3)
-
-    # rooflines of the three largest kernels of the step; "roofline" is the one with the most
-    # device time. Algorithmic work per launch (one layer, the whole batch):
-    #   score pass  B H T (T-1) N flops (causal Q K^T, T(T-1)/2 pairs x 2N)       tensor
-    # With xs recomputed in the gate (BDH_SM100_GATE_X=1):
-    #   encode      B T H N x 2 bytes written (QR) + x and weights read            HBM
-    #   gate        2 x 2 B T H N D flops (x enc and y encv), xy written           tensor
-    # With xs stored (default):
-    #   encode      2 B T H N x 2 bytes written (xs, QR) + x and weights read      HBM
-    #   gate + decoder in one kernel (default, BDH_SM100_GATE_DEC=0 splits them):
-    #               2 x 2 B T H N D flops (y encv, xy dec), xs read, xy never stored  tensor
-    #   gate alone  B T H N x 2 read (xs) + B T H N x 2 written (xy) + y, weights  HBM
+def config2_rooflines(prof: dict, B: int, T: int, steps: int, region_ms: float) -> dict:
+    """Rooflines of the three largest kernels of the config-2 step. Algorithmic work per launch
+    (one layer, the whole batch):
+      score pass  B H T (T-1) N flops (causal Q K^T, T(T-1)/2 pairs x 2N)       tensor
+    With xs stored (default):
+      encode      2 B T H N x 2 bytes written (xs, QR) + x and weights read      HBM
+      gate + decoder in one kernel (default, BDH_SM100_GATE_DEC=0 splits them):
+                  2 x 2 B T H N D flops (y encv, xy dec), xs read, xy never stored  tensor
+      gate alone  B T H N x 2 read (xs) + B T H N x 2 written (xy) + y, weights  HBM
+    With xs recomputed in the gate (BDH_SM100_GATE_X=1):
+      encode      B T H N x 2 bytes written (QR) + x and weights read            HBM
+      gate        2 x 2 B T H N D flops (x enc and y encv), xy written           tensor"""
     peaks, src = load_peaks()
-    tpeak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
-    tsrc = f"{src} bf16_tflops_sustained (kernel timed inside a long step)"
+    tpeak, tsrc = tensor_peak(peaks, src, region_ms)
     lat = B * T * N_HEAD * N_LAT * 2
     small = B * T * D_MODEL * 2 + N_HEAD * D_MODEL * N_LAT * 2
     gate_x = os.environ.get("BDH_SM100_GATE_X", "0") == "1"
@@ -544,7 +506,68 @@ def bench_config2(args, world, rank, dev):
         rooflines[k] = {"kernel": name, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
                         "frac": ach / peak, "peak_source": psrc, "traffic": load_traffic(tname, B),
                         "avg_launch_ms": per, "work_per_launch": work,
-                        "ms_per_step": kp["ms"] / args.steps}
+                        "ms_per_step": kp["ms"] / steps}
+    return rooflines
+
+
+def time_config2(model, idx, steps: int, warmup: int, world: int, dev, native: bool = True):
+    """Device-timed prefill steps of `model` on `idx` (max over ranks). Returns
+    (ms, library per-kernel profile or None, clocks)."""
+    def step():
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+            return model(idx)[0]
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(dev)
+    clocks.start()
+    if native:
+        profile_begin()
+    ms = timed(step, steps, world, dev)
+    prof = profile_end() if native else None
+    clk = clocks.stop()
+    return ms, prof, clk
+
+
+def bench_config2(args, world, rank, dev):
+    from kernels import sm100_attn
+
+    B, T = args.batch or 32, 512
+    model = config2_model(dev)
+    g = torch.Generator().manual_seed(rank_seed(2002, rank))
+    idx_host = torch.randint(0, VOCAB, (B, T), generator=g).pin_memory()
+    idx = idx_host.to(dev)
+    ms, prof, clk = time_config2(model, idx, args.steps, args.warmup, world, dev)
+    assert sm100_attn.device_error(dev) == 0
+    value = world * B * T * args.steps / (ms / 1e3)
+
+    # end to end through the public API with host buffers
+    idx_dev = torch.empty_like(idx)
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        out_shape = model(idx)[0].shape
+    logits_host = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        idx_dev.copy_(idx_host, non_blocking=True)
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+            logits = model(idx_dev)[0]
+        logits_host.copy_(logits, non_blocking=True)
+
+    def verify_logits():
+        gv = torch.Generator().manual_seed(4242)  # the same batch on every rank
+        iv = torch.randint(0, VOCAB, (2, 256), generator=gv).to(dev)
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+            return model(iv)[0].float()
+
+    xcheck = cross_rank_check(verify_logits, world, dev)
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    ms_e2e = timed(e2e_step, args.steps, world, dev)
+    torch.cuda.synchronize(dev)
+    e2e = world * B * T * args.steps / (ms_e2e / 1e3)
+
+    rooflines = config2_rooflines(prof, B, T, args.steps, ms)
     dominant = max(rooflines, key=lambda k: rooflines[k]["ms_per_step"]) if rooflines else None
     attn_ms = sum(prof[k]["ms"] for k in ("score", "value", "rope"))
     attn_flops = N_LAYER * args.steps * B * N_HEAD * T * (T - 1) * (N_LAT + D_MODEL)
@@ -574,7 +597,85 @@ def bench_config2(args, world, rank, dev):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, kind, cores, sample = cpu_reference_model(1, T, 1)
         line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
+    if args.only:
+        return line
+    del idx_dev, logits_host
+    # the reference's op sequence on this GPU: the same model with eager attention and torch
+    # (cuBLAS) projections, bit for bit the calls bdh.py's eval forward makes under autocast
+    model.attn._attn_impl_override = "eager"
+    os.environ["BDH_SM100_LATENT"] = "0"
+    try:
+        ms_eager, _, clk_e = time_config2(model, idx, 5, 3, world, dev, native=False)
+    finally:
+        os.environ.pop("BDH_SM100_LATENT", None)
+        model.attn._attn_impl_override = "cuda_sm100"
+    line["gpu_eager_baseline"] = {
+        "config2": {"value": world * B * T * 5 / (ms_eager / 1e3), "unit": "tokens/s",
+                    "ms_per_step": ms_eager / 5, "steps": 5, "warmup": 3, "clocks": clk_e,
+                    "what": "config-2 step with BDH_ATTN_IMPL=eager and torch/cuBLAS projections "
+                            "(the reference's eval forward op for op: kernels/attention.py:27-40, "
+                            "bdh.py:947-1072) on this GPU"}}
+    if world > 1:
+        line["strong_scaling"] = strong_scaling(model, args, world, rank, dev)
+    del model
+    torch.cuda.empty_cache()
+    line["configs"] = other_configs(args, world, rank, dev, line["gpu_eager_baseline"])
     return line
+
+
+def strong_scaling(model, args, world, rank, dev):
+    """Config 2 at its stated global batch (B = 32 sequences sharded over the ranks, 32 / N
+    each) and config 5's 64 (b, h) units sharded the same way (16 / N sequences of 4 heads):
+    the whole job's throughput at fixed total work, and the per-kernel device times of one rank,
+    to show which kernel stops shrinking."""
+    out = {}
+    Bg, T = 32, 512
+    if Bg % world == 0:
+        b = Bg // world
+        g = torch.Generator().manual_seed(rank_seed(2102, rank))
+        idx = torch.randint(0, VOCAB, (b, T), generator=g).to(dev)
+        ms, prof, clk = time_config2(model, idx, args.steps, args.warmup, world, dev)
+        out["config2"] = {"value": Bg * T * args.steps / (ms / 1e3), "unit": "tokens/s",
+                          "global_batch": Bg, "per_gpu_batch": b, "ms_per_step": ms / args.steps,
+                          "kernel_ms_rank0": {k: v["ms"] / args.steps for k, v in prof.items()
+                                              if v["launches"]},
+                          "clocks": clk, "scaling": "strong"}
+    if 16 % world == 0:
+        sub = argparse.Namespace(**vars(args))
+        sub.config, sub.batch, sub.no_cpu_baseline = 5, 16 // world, True
+        sub.steps = max(args.steps // 2, 5)
+        ln = bench_op(sub, world, rank, dev)
+        out["config5"] = {"value": ln["value"], "unit": ln["unit"], "global_units": 64,
+                          "per_gpu_units": 4 * (16 // world), "ms_per_step": ln["ms_per_step"],
+                          "kernel_ms_rank0": ln["kernel_ms"], "clocks": ln["clocks"],
+                          "scaling": "strong"}
+    return out
+
+
+def other_configs(args, world, rank, dev, eager):
+    """The metric's other numbers on the same lease (each a sub-object with its own roofline,
+    clocks and cpu_baseline): config 4 decode tokens/s over the whole span (B = 64, 512-token
+    prompt, S up to 1023), config 5 forward + backward TFLOP/s, config 3 long-context TFLOP/s;
+    and the eager decode step beside config 4."""
+    out = {}
+    sub = argparse.Namespace(**vars(args))
+    sub.batch = 0
+    sub.config, sub.warmup = 4, 3
+    sub.steps = 1024 - 512 - sub.warmup
+    out["config4_decode"] = bench_decode(sub, world, rank, dev)
+    torch.cuda.empty_cache()
+    sub.eager = True  # the same span
+    eager["config4"] = bench_decode(sub, world, rank, dev)
+    sub.eager = False
+    torch.cuda.empty_cache()
+    sub.steps = 10
+    sub.config = 5
+    out["config5_fwd_bwd"] = bench_op(sub, world, rank, dev)
+    torch.cuda.empty_cache()
+    sub.config = 3
+    out["config3_long_context"] = bench_op(sub, world, rank, dev)
+    torch.cuda.empty_cache()
+    return out
 
 
 # ----------------------------------------------------------- standalone op configs
@@ -640,14 +741,15 @@ def state_terms() -> int:
     return 2 if os.environ.get("BDH_SM100_SPLIT_SCORES", "") == "1" else 1
 
 
-def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev, steps):
+def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev, steps, region_ms):
     """Roofline of the dominant kernel of an op config (algorithmic work per launch / time).
 
     * config 1 (fp32): score pass, causal Q K^T flops B H T(T-1) N against a measured cuBLAS
       TF32 GEMM peak (the pass issues 3 TF32 products per algorithmic product for fp32 accuracy);
     * config 3 (chunked): prefix-state pass, HBM bytes = K and V read once + the bf16 prefix
       states written, (T/C - 1) N D 2 bytes per (b,h) (4 with the hi/lo split);
-    * config 5: grad-Q pass, dQ_total = dS Q + dS^T Q, causal flops 2 T(T-1) N per (b,h).
+    * config 5: grad-Q pass, dQ_total = dS Q + dS^T Q, causal flops 2 T(T-1) N per (b,h),
+      against the burst bf16 peak for sub-second timed regions (``tensor_peak``).
     """
     B, H, T, N, D = shape
     units = B * H
@@ -672,8 +774,7 @@ def op_roofline(cfg_id, prof, shape, chunked, peaks, src, dev, steps):
     else:
         k = prof["grad_q"] if cfg_id == 5 else prof["score"]
         work = units * T * (T - 1) * N * (2 if cfg_id == 5 else 1)
-        peak, unit, bound = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]), "TFLOP/s", "tensor"
-        psrc = f"{src} bf16_tflops_sustained"
+        (peak, psrc), unit, bound = tensor_peak(peaks, src, region_ms), "TFLOP/s", "tensor"
         kern = ("grad-Q pass (tc_pair_kernel<GradQPair>, cta_group::2)" if cfg_id == 5
                 else "score pass")
         tname = "grad_q_config5" if cfg_id == 5 else "score_pass_config3"
@@ -737,7 +838,7 @@ def bench_op(args, world, rank, dev):
     peaks, src = load_peaks()
     sc = prof["score"]
     per_launch = sc["ms"] / sc["launches"] if sc["launches"] else None
-    roof = op_roofline(cfg_id, prof, (B, H, T, N, D), chunked, peaks, src, dev, args.steps)
+    roof = op_roofline(cfg_id, prof, (B, H, T, N, D), chunked, peaks, src, dev, args.steps, ms)
     line = {
         "metric": f"tril-attn TFLOP/s (config {cfg_id}, executed-algorithm causal flops)",
         "value": flops / (ms / 1e3) / 1e12,
@@ -779,11 +880,12 @@ def bench_decode(args, world, rank, dev):
     from bdh_cache import CacheManager
 
     B, P = args.batch or 64, 512
+    eager = getattr(args, "eager", False)
     cfg = bdh_model.BDHConfig(n_layer=N_LAYER, n_embd=D_MODEL, n_head=N_HEAD,
                               mlp_internal_dim_multiplier=128, vocab_size=VOCAB, dropout=0.0)
     torch.manual_seed(1004)
     model = bdh_model.BDH(cfg).to(dev).eval()
-    model.attn._attn_impl_override = "cuda_sm100"
+    model.attn._attn_impl_override = "eager" if eager else "cuda_sm100"
     steps_total = args.warmup + args.steps
     g = torch.Generator().manual_seed(rank_seed(2004, rank))
     toks = torch.randint(0, VOCAB, (B, P + steps_total), generator=g).to(dev)
@@ -813,6 +915,14 @@ def bench_decode(args, world, rank, dev):
         prof = profile_end()
         clk = clocks.stop()
     S_mean = S0 + (args.steps - 1) / 2
+    del cache
+    if eager:
+        return {"value": world * B * args.steps / (ms / 1e3), "unit": "tokens/s",
+                "ms_per_step": ms / args.steps, "steps": args.steps, "warmup": args.warmup,
+                "S_mean": S_mean, "clocks": clk,
+                "what": "config-4 decode step (B=64, fp32 cache) with BDH_ATTN_IMPL=eager: the "
+                        "reference's two-GEMM decode (kernels/attention.py:193-219) and torch "
+                        "projections on this GPU"}
     if storage == torch.float8_e4m3fn:  # e4m3 keys + one fp32 scale per row, bf16 values
         bytes_step = N_LAYER * (B * N_HEAD * S_mean * (N_LAT + 4) + B * S_mean * D_MODEL * 2)
     else:
@@ -834,6 +944,7 @@ def bench_decode(args, world, rank, dev):
         "cache_dtype": ("fp8 e4m3 keys (row scales) + bf16 values" if storage == torch.float8_e4m3fn
                         else "bf16" if storage is not None else "f32"), "cache_kind": kind,
         "data": "synthetic", "config": {"workload": "config 4 decode", "B": B, "prompt": P,
+                                        "S_first": S0, "S_last": S0 + args.steps - 1,
                                         "S_mean": S_mean},
         "roofline": {"kernel": ("state decode (state_decode_kernel + state_reduce_kernel)" if kind == "state"
                                 else "decode over e4m3 keys (decode_slice_kernel<..., uint8, ..., fp8> "
@@ -895,6 +1006,9 @@ def main():
                     help="config 4 with the N x D recurrent-state cache instead of the history")
     ap.add_argument("--batch", type=int, default=0,
                     help="per-GPU batch override (profiling aid; defaults: the config's own)")
+    ap.add_argument("--only", action="store_true",
+                    help="config 2: the headline line alone (no other configs, eager baseline "
+                         "or strong-scaling objects)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl != "reference":
         args.warmup = 3

@@ -215,3 +215,25 @@ def test_state_decode_oracle_equals_history_decode():
     for s in range(1, 25):
         _, S = O.state_decode(kbuf[:, :, s:s + 1], S, vbuf[:, :, s:s + 1])
     assert O.rel_fro(S, S25) < 1e-12
+
+
+def test_baseline_model_port_pinned_to_reference_logits():
+    """The CPU restatement of bdh_baseline.BDH that the timed reference arm runs
+    (oracle/baseline_model.py) reproduces the reference's own fp32 logits: the small golden
+    model (bdh_baseline.BDH) and the config-2-width model (bdh.BDH without autocast), with the
+    attention from the reference's C++ extension where it is built, else in torch."""
+    import torch
+
+    import baseline_model as BM
+    from conftest import config2_case
+
+    attn = BM.reference_tril_score_v()
+    g = golden("model")
+    w = {k: torch.from_numpy(np.asarray(v, np.float32)) for k, v in _model_weights(g).items()}
+    got = BM.baseline_forward(torch.from_numpy(g["idx"]), w, n_layer=2, n_head=2, attn=attn)
+    assert O.rel_fro(got.numpy(), g["logits_baseline"]) < 1e-5
+    C = config2_case()
+    g2 = golden("config2_bf16")
+    w2 = {k: torch.from_numpy(np.asarray(v, np.float32)) for k, v in _config2_oracle_weights(g2).items()}
+    got2 = BM.baseline_forward(torch.from_numpy(g2["idx"]), w2, C.N_LAYER, C.N_HEAD, attn=attn)
+    assert O.rel_fro(got2.numpy(), g2["logits_f32"]) < 1e-5
