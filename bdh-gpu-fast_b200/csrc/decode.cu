@@ -393,9 +393,10 @@ __device__ __forceinline__ void load_q4(const uint16_t* p, bool vec, float (&x)[
   }
 }
 
-// F8: TK = uint8_t e4m3 keys with one fp32 scale per row (ksc); the fused RoPE / slot write
-// (freqs) is only used with F8 = false.
-template <typename TQ, typename TK, typename TV, int QC, bool F8>
+// F8: TK = uint8_t e4m3 keys with one fp32 scale per row (ksc). ROT: the query is rotated
+// here (freqs) and split 0 writes the cache slot; a separate instantiation, so that the kernels
+// without it keep their registers for the load ring (F8 never rotates here).
+template <typename TQ, typename TK, typename TV, int QC, bool F8, bool ROT>
 __global__ void __launch_bounds__(kSliceWarps * 32, 2) decode_slice_kernel(
     const TQ* __restrict__ q, const TK* __restrict__ kp, const float* __restrict__ ksc,
     const TV* __restrict__ vp, float* __restrict__ partial, TK* __restrict__ slot,
@@ -405,7 +406,11 @@ __global__ void __launch_bounds__(kSliceWarps * 32, 2) decode_slice_kernel(
     int64_t pos, int rows_per_cta, bool qvec) {
   constexpr int E = 16 / sizeof(TK);
   constexpr int CS = kSliceWarps * 32 * E;  // elements of one chunk row across the CTA
-  constexpr int L = 8 * QC;                 // loads of a group of eight rows
+  // rows per group: fewer when the lane holds many query elements (32 at N = 8192) or rotates
+  // them here, so that the query slice, the load ring and the group's sums fit the 128
+  // registers of two CTAs per SM (fp32 keys at N = 8192: two rows per group)
+  constexpr int GR = (QC * E >= 32 && sizeof(TK) == 4) ? 2 : (QC * E >= 32 || (ROT && QC * E >= 16)) ? 4 : 8;
+  constexpr int L = GR * QC;                // loads of a group of GR rows
   constexpr int DP = kSliceAhead;
   static_assert(DP % QC == 0 && L % DP == 0, "the prefetch distance covers whole rows");
   __shared__ float red[kSliceWarps][kDecRowsMax];
@@ -448,8 +453,8 @@ __global__ void __launch_bounds__(kSliceWarps * 32, 2) decode_slice_kernel(
       float x[4] = {0.f, 0.f, 0.f, 0.f};
       if (i < nval) {
         load_q4(qr + n, qvec, x);
-        if constexpr (!F8) {
-          if (freqs != nullptr) {
+        if constexpr (ROT && !F8) {
+          {
 #pragma unroll
             for (int j = 0; j < 4; j += 2) {
               float c0, s0, c1, s1;
@@ -479,12 +484,12 @@ __global__ void __launch_bounds__(kSliceWarps * 32, 2) decode_slice_kernel(
     }
   }
 
-  // 3. the rows, eight at a time; loads run kSliceAhead ahead across group boundaries
-  const int groups = (rows + 7) >> 3;
+  // 3. the rows, GR at a time; loads run kSliceAhead ahead across group boundaries
+  const int groups = (rows + GR - 1) / GR;
   for (int g = 0; g < groups; ++g) {
-    float acc[8];
+    float acc[GR];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+    for (int k = 0; k < GR; ++k) acc[k] = 0.f;
 #pragma unroll
     for (int t = 0; t < L; ++t) {
       const uint4 u = ring[t % DP];
@@ -501,23 +506,49 @@ __global__ void __launch_bounds__(kSliceWarps * 32, 2) decode_slice_kernel(
       else
         acc[t / QC] += dot16<TK>(qv[i], u);
     }
-    // eight values per lane -> lane (b4 b3 b2) holds the warp's sum for row 4 b4 + 2 b3 + b2
     const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
-    float u4[4], u2[2];
+    if constexpr (GR == 2) {
+      // two values per lane -> lane (b4) holds the warp's sum for row b4
+      float u1 = (b4 ? acc[1] : acc[0]) + __shfl_xor_sync(0xffffffffu, b4 ? acc[0] : acc[1], 16);
+      u1 += __shfl_xor_sync(0xffffffffu, u1, 8);
+      u1 += __shfl_xor_sync(0xffffffffu, u1, 4);
+      u1 += __shfl_xor_sync(0xffffffffu, u1, 2);
+      u1 += __shfl_xor_sync(0xffffffffu, u1, 1);
+      (void)b3;
+      (void)b2;
+      if ((lane & 15) == 0) red[warp][g * 2 + b4] = u1;
+    } else if constexpr (GR == 8) {
+      // eight values per lane -> lane (b4 b3 b2) holds the warp's sum for row 4 b4 + 2 b3 + b2
+      float u4[4], u2[2];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float keep = b4 ? acc[k + 4] : acc[k], send = b4 ? acc[k] : acc[k + 4];
-      u4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
+      for (int k = 0; k < 4; ++k) {
+        const float keep = b4 ? acc[k + 4] : acc[k], send = b4 ? acc[k] : acc[k + 4];
+        u4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const float keep = b3 ? u4[k + 2] : u4[k], send = b3 ? u4[k] : u4[k + 2];
-      u2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      for (int k = 0; k < 2; ++k) {
+        const float keep = b3 ? u4[k + 2] : u4[k], send = b3 ? u4[k] : u4[k + 2];
+        u2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      float u1 = (b2 ? u2[1] : u2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? u2[0] : u2[1], 4);
+      u1 += __shfl_xor_sync(0xffffffffu, u1, 2);
+      u1 += __shfl_xor_sync(0xffffffffu, u1, 1);
+      if ((lane & 3) == 0) red[warp][g * 8 + 4 * b4 + 2 * b3 + b2] = u1;
+    } else {
+      // four values per lane -> lane (b4 b3) holds the warp's sum for row 2 b4 + b3
+      float u2[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const float keep = b4 ? acc[k + 2] : acc[k], send = b4 ? acc[k] : acc[k + 2];
+        u2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+      float u1 = (b3 ? u2[1] : u2[0]) + __shfl_xor_sync(0xffffffffu, b3 ? u2[0] : u2[1], 8);
+      u1 += __shfl_xor_sync(0xffffffffu, u1, 4);
+      u1 += __shfl_xor_sync(0xffffffffu, u1, 2);
+      u1 += __shfl_xor_sync(0xffffffffu, u1, 1);
+      (void)b2;
+      if ((lane & 7) == 0) red[warp][g * 4 + 2 * b4 + b3] = u1;
     }
-    float u1 = (b2 ? u2[1] : u2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? u2[0] : u2[1], 4);
-    u1 += __shfl_xor_sync(0xffffffffu, u1, 2);
-    u1 += __shfl_xor_sync(0xffffffffu, u1, 1);
-    if ((lane & 3) == 0) red[warp][g * 8 + 4 * b4 + 2 * b3 + b2] = u1;
   }
   __syncthreads();
 
@@ -540,32 +571,36 @@ __global__ void __launch_bounds__(kSliceWarps * 32, 2) decode_slice_kernel(
   }
 }
 
-// Chunks per warp for the column-slice kernel: the smallest of 1, 2, 4, 8 (fp8: 1, 2, 4) with
-// QC * 8 warps * 32 lanes * E >= N, or 0 when N is wider (the row-per-warp kernel then runs).
+// Chunks per warp for the column-slice kernel: the smallest of 1, 2, 4, 8 (fp8: 1, 2; bf16:
+// up to 4) with QC * 8 warps * 32 lanes * E >= N, or 0 when N is wider (the row-per-warp kernel
+// then runs). The caps keep the lane's query slice (QC * E floats) at 32 registers, N <= 8192.
 int slice_qc(int64_t N, int key_bytes) {
   const int64_t per = static_cast<int64_t>(kSliceWarps) * 32 * (16 / key_bytes);
-  const int qmax = key_bytes == 1 ? 4 : 8;
+  const int qmax = key_bytes == 1 ? 2 : key_bytes == 2 ? 4 : 8;
   for (int qc = 1; qc <= qmax; qc *= 2)
     if (qc * per >= N) return qc;
   return 0;
 }
 
-template <typename TQ, typename TK, typename TV, bool F8>
+template <typename TQ, typename TK, typename TV, bool F8, bool ROT>
 void launch_slice(int qc, dim3 grid, cudaStream_t stream, const TQ* q, const TK* k,
                   const float* ksc, const TV* v, float* partial, TK* slot, const float* freqs,
                   int H, int Hv, int S, int N, int D, const int64_t qs[4], const int64_t ks[4],
                   const int64_t cs[3], const int64_t vs[4], const int64_t ss[4], int64_t pos,
                   int rows, bool qvec) {
 #define BDH_SLICE(QC)                                                                             \
-  decode_slice_kernel<TQ, TK, TV, QC, F8><<<grid, kSliceWarps * 32, 0, stream>>>(                \
+  decode_slice_kernel<TQ, TK, TV, QC, F8, ROT><<<grid, kSliceWarps * 32, 0, stream>>>(           \
       q, k, ksc, v, partial, slot, freqs, H, Hv, S, N, D, qs[0], qs[1], qs[2], ks[0], ks[1],      \
       ks[2], cs[0], cs[1], cs[2], vs[0], vs[1], vs[2], ss[0], ss[1], ss[2], pos, rows, qvec)
+  constexpr int kB = sizeof(TK);  // key bytes: the widest QC instantiated follows slice_qc
   switch (qc) {
     case 1: BDH_SLICE(1); break;
     case 2: BDH_SLICE(2); break;
-    case 4: BDH_SLICE(4); break;
+    case 4:
+      if constexpr (kB >= 2) BDH_SLICE(4);
+      break;
     default:
-      if constexpr (!F8) BDH_SLICE(8);
+      if constexpr (kB == 4) BDH_SLICE(8);
       break;
   }
 #undef BDH_SLICE
@@ -619,7 +654,7 @@ DecodePlan plan_decode(int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t N, i
   cudaGetDevice(&dev);
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-          &occ, decode_slice_kernel<float, float, float, 8, false>, kSliceWarps * 32, 0) !=
+          &occ, decode_slice_kernel<float, float, float, 8, false, false>, kSliceWarps * 32, 0) !=
           cudaSuccess ||
       occ <= 0) {
     cudaGetLastError();
@@ -725,11 +760,18 @@ int launch_decode(const DecodeArgs& a_in, float* partial, float* qrot, int64_t m
     const bool qv = q_vec_ok(a.q, a.q_dtype, a.q_strides);
     const int64_t cs[3] = {0, 0, 0};
 #define BDH_SLICE_GO(TQ, TK)                                                                      \
-  launch_slice<TQ, TK, TK, false>(qc, grid, stream, static_cast<const TQ*>(a.q),                 \
-                                  static_cast<const TK*>(a.k), nullptr,                          \
-                                  static_cast<const TK*>(a.v), partial, static_cast<TK*>(a.slot), \
-                                  a.freqs, Hi, Hvi, Si, Ni, Di, a.q_strides, a.k_strides, cs,     \
-                                  a.v_strides, a.slot_strides, a.pos, pl.rows, qv)
+  do {                                                                                            \
+    if (a.freqs != nullptr)                                                                       \
+      launch_slice<TQ, TK, TK, false, true>(                                                      \
+          qc, grid, stream, static_cast<const TQ*>(a.q), static_cast<const TK*>(a.k), nullptr,    \
+          static_cast<const TK*>(a.v), partial, static_cast<TK*>(a.slot), a.freqs, Hi, Hvi, Si,   \
+          Ni, Di, a.q_strides, a.k_strides, cs, a.v_strides, a.slot_strides, a.pos, pl.rows, qv); \
+    else                                                                                          \
+      launch_slice<TQ, TK, TK, false, false>(                                                     \
+          qc, grid, stream, static_cast<const TQ*>(a.q), static_cast<const TK*>(a.k), nullptr,    \
+          static_cast<const TK*>(a.v), partial, nullptr, nullptr, Hi, Hvi, Si, Ni, Di,            \
+          a.q_strides, a.k_strides, cs, a.v_strides, a.slot_strides, a.pos, pl.rows, qv);         \
+  } while (0)
     if (qf && kf) BDH_SLICE_GO(float, float);
     else if (qf) BDH_SLICE_GO(float, uint16_t);
     else if (kf) BDH_SLICE_GO(uint16_t, float);
@@ -826,7 +868,7 @@ int launch_decode_fp8(const DecodeFp8Args& a_in, float* partial, float* qrot, cu
     const bool qv = q_vec_ok(a.q, a.q_dtype, a.q_strides);
     const int64_t ss[4] = {0, 0, 0, 1};
 #define BDH_SLICE8_GO(TQ, TV)                                                                    \
-  launch_slice<TQ, uint8_t, TV, true>(qc, grid, stream, static_cast<const TQ*>(a.q), a.k,       \
+  launch_slice<TQ, uint8_t, TV, true, false>(qc, grid, stream, static_cast<const TQ*>(a.q), a.k,       \
                                       a.k_scale, static_cast<const TV*>(a.v), partial, nullptr,  \
                                       nullptr, Hi, Hvi, Si, Ni, Di, a.q_strides, a.k_strides,    \
                                       a.ks_strides, a.v_strides, ss, 0, pl.rows, qv)
