@@ -138,6 +138,7 @@ struct ScorePair {
   using S = PairShape<false, false, 1, 1, 6>;
   struct Tile {
     int unit, m, n;  // 256-row query block, 256-key block
+    int sub;         // -1: all 256 keys; else keys [sub * w, (sub + 1) * w), w = 256 / tail_sub
   };
   __device__ static int key0(const Params& p, int m) {
     return p.chunk > 0 ? (m * 256 / p.chunk) * p.chunk : 0;
@@ -145,9 +146,19 @@ struct ScorePair {
   __device__ static int nt_for(const Params& p, int m) {
     return ceil_div_d(min(p.T, (m + 1) * 256), 256) - key0(p, m) / 256;
   }
-  __device__ static int num_tiles(const Params& p) { return p.units * p.tiles_per_unit; }
+  __device__ static int num_tiles(const Params& p) {
+    const int n = p.units * p.tiles_per_unit;
+    return p.tail_sub > 1 ? p.tail_from + (n - p.tail_from) * p.tail_sub : n;
+  }
   __device__ static Tile tile(const Params& p, int t) {
     Tile tl;
+    tl.sub = -1;
+    if (p.tail_sub > 1 && t >= p.tail_from) {  // the narrow tiles of a tail tile are consecutive
+      const int e = t - p.tail_from;
+      const int q = e / p.tail_sub;
+      tl.sub = e - q * p.tail_sub;
+      t = p.tail_from + q;
+    }
     tl.unit = t / p.tiles_per_unit;
     int r = t - tl.unit * p.tiles_per_unit;
     int m = 0;
@@ -160,12 +171,23 @@ struct ScorePair {
     tl.n = r + key0(p, m) / 256;
     return tl;
   }
+  // narrow tail tiles: an M = 256, N = 256 / tail_sub MMA over all of K (pair-engine kVarN)
+  static constexpr bool kVarN = true;
+  __device__ static uint32_t tile_idesc(const Params& p, const Tile& tl) {
+    return tl.sub < 0 ? S::IDESC : make_idesc(1u, 0u, 0u, 256u, static_cast<uint32_t>(256 / p.tail_sub));
+  }
+  __device__ static int tile_cols(const Params& p, const Tile& tl) {
+    return tl.sub < 0 ? 256 : 256 / p.tail_sub;
+  }
   __device__ static int k_blocks(const Params& p, const Tile&) { return ceil_div_d(p.K, 64); }
   __device__ static uint32_t pair_mask(const Params&, const Tile&, int) { return 0x1u; }
-  __device__ static uint32_t stage_tx(const Params&, const Tile&, int) { return 2 * S::STAGE_BYTES; }
+  __device__ static uint32_t stage_tx(const Params& p, const Tile& tl, int) {
+    return tl.sub < 0 ? 2 * S::STAGE_BYTES : 2 * (S::A_TILE + S::B_TILE / p.tail_sub);
+  }
   __device__ static void prefetch(const Params& p) {
     tma_prefetch_desc(&p.a_map[0]);
     tma_prefetch_desc(&p.b_map[0]);
+    if (p.tail_sub > 1) tma_prefetch_desc(&p.b_nar);
   }
   __device__ static void load_stage(const Params& p, const Tile& tl, int kb, uint32_t rank,
                                     uint32_t bar, uint8_t* a_dst, uint8_t* b_dst) {
@@ -173,7 +195,13 @@ struct ScorePair {
     const int hb = p.b_shared ? 0 : h;
     const int r128 = static_cast<int>(rank) * 128;
     tma_load_4d_pair(&p.a_map[0], bar, a_dst, kb * 64, tl.m * 256 + r128, h, b);
-    tma_load_4d_pair(&p.b_map[0], bar, b_dst, kb * 64, tl.n * 256 + r128, hb, b);
+    if (tl.sub < 0) {
+      tma_load_4d_pair(&p.b_map[0], bar, b_dst, kb * 64, tl.n * 256 + r128, hb, b);
+    } else {  // this CTA's half of the narrow tile's keys
+      const int w = 256 / p.tail_sub;
+      tma_load_4d_pair(&p.b_nar, bar, b_dst, kb * 64,
+                       tl.n * 256 + tl.sub * w + static_cast<int>(rank) * (w / 2), hb, b);
+    }
   }
   // 4 KB per epilogue warp: the transposed stores of the backward's G and M^T go through
   // shared memory (whole 64-byte column segments instead of two-byte element stores)
@@ -184,7 +212,8 @@ struct ScorePair {
     t.unit = tl.unit;
     t.mi = 2 * tl.m + rank;
     t.ni = tl.n;
-    Base::epilogue(p, t, row, c0, r, scratch);
+    // a narrow tile's accumulator columns are its keys: column c0 of the 256-key block below
+    Base::epilogue(p, t, row, tl.sub < 0 ? c0 : tl.sub * (256 / p.tail_sub) + c0, r, scratch);
   }
 };
 
@@ -287,7 +316,29 @@ int launch_score_pass(const ScoreArgs& a, cudaStream_t stream, int* err) {
       tpu += static_cast<int>((lim + 255) / 256 - k0 / 256);
     }
     prm.tiles_per_unit = tpu;
-    return launch_pair<ScorePair::S, ScorePair>(prm, prm.units * tpu, stream, kProfScore);
+    const int ntiles = prm.units * tpu;
+    // The last, partial wave of the persistent grid (ntiles mod pairs tiles) runs as narrower
+    // tiles (64 or 128 keys) on the pairs the full waves leave idle: the same MMAs over all of
+    // K for each output element, so the same bits, in about half the time of the wide tiles.
+    static const bool tail_on = [] {  // BDH_SM100_SCORE_TAIL=0: keep the last wave wide
+      const char* e = std::getenv("BDH_SM100_SCORE_TAIL");
+      return !(e != nullptr && std::atoi(e) == 0);
+    }();
+    const int cap = resident_pairs<ScorePair::S, ScorePair>();
+    if (cap < 0) return -cap;
+    const int tail = ntiles % cap;
+    int sub = 0;
+    if (tail_on && tail > 0 && a.mode == kStoreDirect) sub = tail * 4 <= cap ? 4 : tail * 2 <= cap ? 2 : 0;
+    if (sub > 1) {
+      int64_t bd[4] = {a.K, a.T, a.Hb, a.B};
+      int64_t bs[3] = {a.b_strides[2] * elem, a.b_strides[1] * elem, a.b_strides[0] * elem};
+      if (!make_map_4d(&prm.b_nar, a.b[0], elem, bd, bs, 64, 128 / sub, "score pass: B (tail)"))
+        return BDH_ERR_INVALID;
+      prm.tail_sub = sub;
+      prm.tail_from = ntiles - tail;
+      return launch_pair<ScorePair::S, ScorePair>(prm, prm.tail_from + tail * sub, stream, kProfScore);
+    }
+    return launch_pair<ScorePair::S, ScorePair>(prm, ntiles, stream, kProfScore);
   }
   if (elem == 2 && score_tile_n() == 256) {
     ScoreBf16Wide::Params prm{};

@@ -5,9 +5,12 @@
 //
 // Slice kernel: CTA (s, mb, db) multiplies X rows [64 mb, 64 mb + 64) by W rows
 // [kDecKS s, kDecKS (s + 1)) and columns [128 db, 128 db + 128) and writes the fp32 partial to
-// part[s]. X's slice is staged transposed in shared memory; each thread keeps a 16-row x
-// 4-column register tile, so every k step costs one 16-byte W load, four 16-byte shared loads
-// and 64 FMAs. Reduce kernel: out = sum over s of part[s], in a fixed order (deterministic).
+// part[s]. X's slice is staged transposed in shared memory; W's slice streams through a
+// double-buffered shared-memory stage in chunks of kDecWK rows (16-byte asynchronous copies,
+// the next chunk in flight while this one is multiplied). Each of the 256 threads keeps an
+// 8-row x 4-column register tile: per k, two 16-byte shared loads of X (4 distinct addresses per
+// warp), one of W (8 distinct per warp) and 32 FMAs. Reduce kernel: out = sum over s of part[s],
+// in a fixed order (deterministic).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -22,78 +25,97 @@ namespace {
 constexpr int kDecKS = 256;    // K rows per slice
 constexpr int kDecRows = 64;   // X rows per CTA
 constexpr int kDecCols = 128;  // output columns per CTA
-constexpr int kDecPad = 68;    // floats per staged k row (16-byte aligned, fewer bank conflicts)
-constexpr int kDecThreads = 128;
-constexpr int kDecWB = 8;     // W rows per register block
+constexpr int kDecPad = 68;    // floats per staged X k row (16-byte aligned, fewer bank conflicts)
+constexpr int kDecThreads = 256;
+constexpr int kDecWK = 32;     // W rows per shared-memory chunk
 constexpr int kRedGroups = 4;  // slice groups summed side by side by the reduce kernel
+constexpr int kDecSmem = (kDecKS * kDecPad + 2 * kDecWK * kDecCols) * static_cast<int>(sizeof(float));
 
-__global__ void __launch_bounds__(kDecThreads) dec_f32_slice_kernel(
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__global__ void __launch_bounds__(kDecThreads, 2) dec_f32_slice_kernel(
     const float* __restrict__ x, int64_t ldx, const float* __restrict__ w, int64_t ldw,
     float* __restrict__ part, int M, int K, int D) {
-  extern __shared__ __align__(16) float xs[];  // [kDecKS][kDecPad]
+  extern __shared__ __align__(16) float smem[];
+  float* xs = smem;                          // [kDecKS][kDecPad]
+  float* wsm = smem + kDecKS * kDecPad;      // [2][kDecWK][kDecCols]
   const int k0 = blockIdx.x * kDecKS;
   const int m0 = blockIdx.y * kDecRows;
   const int d0 = blockIdx.z * kDecCols;
   const int ks = min(kDecKS, K - k0);
+  const int nchunk = (ks + kDecWK - 1) / kDecWK;
+
+  // W chunk c -> buffer c & 1: 32 rows x 128 columns, four 16-byte copies per thread (rows at or
+  // beyond ks and columns at or beyond D are zero-filled)
+  auto load_w = [&](int c) {
+    float* dst = wsm + (c & 1) * (kDecWK * kDecCols);
+#pragma unroll
+    for (int i = 0; i < (kDecWK * kDecCols / 4) / kDecThreads; ++i) {
+      const int e = i * kDecThreads + threadIdx.x;  // float4 index in the chunk
+      const int r = e / (kDecCols / 4), c4 = e - r * (kDecCols / 4);
+      const int k = c * kDecWK + r, d = d0 + 4 * c4;
+      const bool ok = k < ks && d < D;
+      const float* src = ok ? w + static_cast<int64_t>(k0 + k) * ldw + d : w;
+      cp_async16(dst + r * kDecCols + 4 * c4, src, ok);
+    }
+    cp_async_commit();
+  };
+  load_w(0);
+  if (nchunk > 1) load_w(1);
   for (int i = threadIdx.x; i < kDecKS * kDecRows; i += kDecThreads) {
     const int m = i / kDecKS, k = i - m * kDecKS;  // consecutive threads read consecutive k
     float v = 0.f;
     if (m0 + m < M && k < ks) v = __ldg(x + static_cast<int64_t>(m0 + m) * ldx + k0 + k);
     xs[k * kDecPad + m] = v;
   }
-  __syncthreads();
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int cg = warp * 8 + (lane >> 2);  // 4-column group
-  const int mg = lane & 3;                // 16-row group
-  const int d = d0 + cg * 4;
-  const bool dok = d < D;                 // D is a multiple of 4
-  float acc[16][4];
+  const int cg = (warp & 3) * 8 + (lane >> 2);  // 4-column group, 0..31
+  const int mg = (warp >> 2) * 4 + (lane & 3);  // 8-row group, 0..7
+  float acc[8][4];
 #pragma unroll
-  for (int r = 0; r < 16; ++r)
+  for (int r = 0; r < 8; ++r)
 #pragma unroll
     for (int c = 0; c < 4; ++c) acc[r][c] = 0.f;
-  const float* wp = w + static_cast<int64_t>(k0) * ldw + d;
-  const float* xr = xs + mg * 16;
-  // W rows in blocks of kDecWB, the next block's loads in flight while this block is multiplied
-  // (staged X rows at k >= ks are zero and their W loads are skipped, so blocks need no tail)
-  float4 wcur[kDecWB], wnxt[kDecWB];
+  const float* xr = xs + mg * 8;
+  for (int c = 0; c < nchunk; ++c) {
+    if (c + 1 < nchunk) cp_async_wait<1>(); else cp_async_wait<0>();
+    __syncthreads();  // chunk c (and, at c = 0, the staged X) visible to every thread
+    const float* wc = wsm + (c & 1) * (kDecWK * kDecCols) + cg * 4;
+#pragma unroll 8
+    for (int q = 0; q < kDecWK; ++q) {
+      const int k = c * kDecWK + q;
+      const float4 wv = *reinterpret_cast<const float4*>(wc + q * kDecCols);
+      const float4 xa = *reinterpret_cast<const float4*>(xr + k * kDecPad);
+      const float4 xb = *reinterpret_cast<const float4*>(xr + k * kDecPad + 4);
+      const float xe[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
-  for (int j = 0; j < kDecWB; ++j)
-    wcur[j] = (dok && j < ks) ? __ldg(reinterpret_cast<const float4*>(wp + static_cast<int64_t>(j) * ldw))
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int kb = 0; kb < ks; kb += kDecWB) {
-#pragma unroll
-    for (int j = 0; j < kDecWB; ++j) {
-      const int k = kb + kDecWB + j;
-      wnxt[j] = (dok && k < ks) ? __ldg(reinterpret_cast<const float4*>(wp + static_cast<int64_t>(k) * ldw))
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int q = 0; q < kDecWB; ++q) {
-      const float4 wv = wcur[q];
-      const float4* xv4 = reinterpret_cast<const float4*>(xr + (kb + q) * kDecPad);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float4 xv = xv4[j];
-        const float xe[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          acc[4 * j + e][0] = fmaf(xe[e], wv.x, acc[4 * j + e][0]);
-          acc[4 * j + e][1] = fmaf(xe[e], wv.y, acc[4 * j + e][1]);
-          acc[4 * j + e][2] = fmaf(xe[e], wv.z, acc[4 * j + e][2]);
-          acc[4 * j + e][3] = fmaf(xe[e], wv.w, acc[4 * j + e][3]);
-        }
+      for (int e = 0; e < 8; ++e) {
+        acc[e][0] = fmaf(xe[e], wv.x, acc[e][0]);
+        acc[e][1] = fmaf(xe[e], wv.y, acc[e][1]);
+        acc[e][2] = fmaf(xe[e], wv.z, acc[e][2]);
+        acc[e][3] = fmaf(xe[e], wv.w, acc[e][3]);
       }
     }
-#pragma unroll
-    for (int j = 0; j < kDecWB; ++j) wcur[j] = wnxt[j];
+    __syncthreads();  // every thread is done with buffer c & 1 before it is refilled
+    if (c + 2 < nchunk) load_w(c + 2);
   }
-  if (!dok) return;
+  const int d = d0 + cg * 4;
+  if (d >= D) return;  // D is a multiple of 4
   float* pp = part + static_cast<int64_t>(blockIdx.x) * M * D + d;
 #pragma unroll
-  for (int r = 0; r < 16; ++r) {
-    const int m = m0 + mg * 16 + r;
+  for (int r = 0; r < 8; ++r) {
+    const int m = m0 + mg * 8 + r;
     if (m < M)
       *reinterpret_cast<float4*>(pp + static_cast<int64_t>(m) * D) =
           make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
@@ -154,7 +176,7 @@ int launch_decoder_f32(const float* x, int64_t ldx, const float* w, int64_t ldw,
     }
     return BDH_OK;
   }
-  const int smem = kDecKS * kDecPad * static_cast<int>(sizeof(float));
+  const int smem = kDecSmem;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);

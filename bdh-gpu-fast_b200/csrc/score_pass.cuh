@@ -39,6 +39,11 @@ struct ScoreProb {
   struct Params {
     CUtensorMap a_map[2];  // rows i of A (hi, lo), box BK x 128
     CUtensorMap b_map[2];  // rows j of B (hi, lo), box BK x BN
+    // CTA-pair pass: the tiles from tail_from on (the last, partial wave of the persistent
+    // grid) run as tail_sub narrower tiles of 256 / tail_sub keys each (tail_sub > 1), their
+    // B rows loaded through b_nar (box BK x 128 / tail_sub)
+    CUtensorMap b_nar;
+    int tail_from, tail_sub;
     int H, T, K;           // heads, sequence length, contraction width
     int b_shared;          // B has a single head shared by all H heads of A
     int mode;              // ScoreStore

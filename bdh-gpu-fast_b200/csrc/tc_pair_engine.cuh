@@ -46,6 +46,14 @@ constexpr int pair_smem_bytes() {
   return S::SMEM_BYTES + EpiWarps<P>::value * EpiScratch<P>::value;
 }
 
+// P::kVarN: a tile may use fewer accumulator columns than S::BN (a narrower MMA):
+// P::tile_idesc(prm, tile) is its instruction descriptor, P::tile_cols(prm, tile) the columns
+// the epilogue drains (a multiple of 32, of 64 with eight epilogue warps).
+template <class P, class = void>
+struct HasVarN : std::false_type {};
+template <class P>
+struct HasVarN<P, std::void_t<decltype(P::kVarN)>> : std::true_type {};
+
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -247,6 +255,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<P>(), 1
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * S::BN);
+        uint32_t idesc = S::IDESC;
+        if constexpr (HasVarN<P>::value) idesc = P::tile_idesc(prm, tile);
         for (int kb = 0; kb < nkb; ++kb) {
           if (!wait_bounded(full + stage, ph, abort_flag, prm.err, kErrTimeoutMma)) {
             ok = false;
@@ -263,7 +273,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<P>(), 1
               const int tb = (pr == 2 || (pr == 1 && S::A_TERMS == 1)) ? 1 : 0;
               const uint64_t ad = a0 + (soff16 + ((ta * S::A_TILE + S::a_koff(kk)) >> 4));
               const uint64_t bd = b0 + (soff16 + ((tb * S::B_TILE + S::b_koff(kk)) >> 4));
-              umma_f16_pair(d_tmem, ad, bd, S::IDESC, (kb > 0 || kk > 0 || pr > 0) ? 1u : 0u);
+              umma_f16_pair(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0 || pr > 0) ? 1u : 0u);
             }
           }
           umma_commit_pair(empty_own + stage * 8u);
@@ -288,8 +298,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<P>(), 1
     const int quad = warp & 3;
     const int row = quad * 32 + static_cast<int>(lane_id());
     const int part = (warp - 2) >> 2;  // column half (eight epilogue warps) or 0
-    const int c_begin = EW == 8 ? part * (S::BN / 2) : 0;
-    const int c_end = EW == 8 ? c_begin + S::BN / 2 : S::BN;
     const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
     int lt = 0;
     for (int t = pair; t < ntiles; t += npairs, ++lt) {
@@ -301,6 +309,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<P>(), 1
       tc_fence_after();
       const uint32_t tbase =
           tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * S::BN);
+      int cols = S::BN;
+      if constexpr (HasVarN<P>::value) cols = P::tile_cols(prm, tile);
+      const int c_begin = EW == 8 ? part * (cols / 2) : 0;
+      const int c_end = EW == 8 ? c_begin + cols / 2 : cols;
 #pragma unroll 1
       for (int c0 = c_begin; c0 < c_end; c0 += 32) {
         uint32_t r[32];
@@ -327,9 +339,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<P>(), 1
   }
 }
 
+// CTA pairs of this kernel that fit on the current device at once (the persistent grid), or a
+// negative BDH error code. Looked up once per device.
 template <class S, class P>
-static int launch_pair(const typename P::Params& prm, int ntiles, cudaStream_t stream, int kind) {
-  if (ntiles <= 0) return 0;
+static int resident_pairs() {
   int dev = 0;
   cudaGetDevice(&dev);
   static int max_pairs[64] = {0};
@@ -339,7 +352,7 @@ static int launch_pair(const typename P::Params& prm, int ntiles, cudaStream_t s
                                          pair_smem_bytes<S, P>());
     if (e != cudaSuccess) {
       set_error(std::string("cudaFuncSetAttribute (pair): ") + cudaGetErrorString(e));
-      return BDH_ERR_CUDA;
+      return -BDH_ERR_CUDA;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 74);
@@ -354,10 +367,21 @@ static int launch_pair(const typename P::Params& prm, int ntiles, cudaStream_t s
     cfg.numAttrs = 1;
     int n = 0;
     e = cudaOccupancyMaxActiveClusters(&n, tc_pair_kernel<S, P>, &cfg);
-    if (e != cudaSuccess || n <= 0) n = sm_count(dev) / 2;
+    if (e != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count(dev) / 2;
+    }
     max_pairs[dev] = n;
   }
-  const int pairs = std::min(ntiles, max_pairs[(dev >= 0 && dev < 64) ? dev : 0]);
+  return max_pairs[(dev >= 0 && dev < 64) ? dev : 0];
+}
+
+template <class S, class P>
+static int launch_pair(const typename P::Params& prm, int ntiles, cudaStream_t stream, int kind) {
+  if (ntiles <= 0) return 0;
+  const int cap = resident_pairs<S, P>();
+  if (cap < 0) return -cap;
+  const int pairs = std::min(ntiles, cap);
   prof_start(kind, stream);
   tc_pair_kernel<S, P><<<2 * pairs, pair_threads<P>(), pair_smem_bytes<S, P>(), stream>>>(prm);
   prof_stop(kind, stream);

@@ -175,6 +175,31 @@ def test_forward_linear_in_v_full_size_bf16():
     assert ((o1 - ref).norm() / ref.norm()).item() <= 3e-3
 
 
+@pytest.mark.parametrize("B,N", [(32, 8192), (1, 2048)])
+def test_forward_bf16_narrow_last_wave(B, N):
+    """bf16 forward whose pair score pass runs its last, partial wave as narrower tiles (64 keys
+    each): config 2's attention (B = 32, 4 heads, T = 512, N = 8192: 384 pair tiles on 74 pairs,
+    the last 14 as 56 narrow tiles) and a problem smaller than one wave (12 tiles, 48 narrow
+    ones). The narrow tiles' units against float64 at the bf16 bar, strictly causal, the same
+    bits on a second call."""
+    H, T, D = 4, 512, 256
+    g = torch.Generator(device=DEV).manual_seed(17)
+    q = torch.relu(torch.randn(B, H, T, N, device=DEV, generator=g)).to(torch.bfloat16)
+    v = torch.randn(B, 1, T, D, device=DEV, generator=g).to(torch.bfloat16)
+    out = sa().tril_score_v(q, q, v)
+    again = sa().tril_score_v(q, q, v)
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)
+    assert torch.all(out[:, :, 0] == 0)
+    # the narrow tiles are the last ones of the tile list: the highest units
+    for u in sorted({B * H - 1, B * H - 2, B * H - 5, 0}):
+        b, h = divmod(u, H)
+        qd = q[b, h].double()
+        ref = (qd @ qd.T).tril(-1) @ v[b, 0].double()
+        err = ((out[b, h].double() - ref).norm() / ref.norm()).item()
+        assert err <= 3e-3, (u, err)
+
+
 def test_forward_full_size_fp32_config1():
     B, H, T, N, D = 4, 4, 512, 8192, 256
     q = torch.relu(torch.randn(B, H, T, N, device=DEV))
