@@ -317,12 +317,14 @@ int launch_score_pass(const ScoreArgs& a, cudaStream_t stream, int* err) {
     }
     prm.tiles_per_unit = tpu;
     const int ntiles = prm.units * tpu;
-    // The last, partial wave of the persistent grid (ntiles mod pairs tiles) runs as narrower
-    // tiles (64 or 128 keys) on the pairs the full waves leave idle: the same MMAs over all of
-    // K for each output element, so the same bits, in about half the time of the wide tiles.
-    static const bool tail_on = [] {  // BDH_SM100_SCORE_TAIL=0: keep the last wave wide
+    // BDH_SM100_SCORE_TAIL=1: the last, partial wave of the persistent grid (ntiles mod pairs
+    // tiles) runs as narrower tiles (64 or 128 keys) on the pairs the full waves leave idle, the
+    // same MMAs over all of K for each output element (the same bits). Measured on B200 at
+    // config 2's attention (384 tiles on 74 pairs, the last 14 as 56 narrow tiles): 0.306 ms per
+    // launch against 0.289 ms with the wide last wave, so it is off by default.
+    static const bool tail_on = [] {
       const char* e = std::getenv("BDH_SM100_SCORE_TAIL");
-      return !(e != nullptr && std::atoi(e) == 0);
+      return e != nullptr && std::atoi(e) == 1;
     }();
     const int cap = resident_pairs<ScorePair::S, ScorePair>();
     if (cap < 0) return -cap;

@@ -176,12 +176,11 @@ def test_forward_linear_in_v_full_size_bf16():
 
 
 @pytest.mark.parametrize("B,N", [(32, 8192), (1, 2048)])
-def test_forward_bf16_narrow_last_wave(B, N):
-    """bf16 forward whose pair score pass runs its last, partial wave as narrower tiles (64 keys
-    each): config 2's attention (B = 32, 4 heads, T = 512, N = 8192: 384 pair tiles on 74 pairs,
-    the last 14 as 56 narrow tiles) and a problem smaller than one wave (12 tiles, 48 narrow
-    ones). The narrow tiles' units against float64 at the bf16 bar, strictly causal, the same
-    bits on a second call."""
+def test_forward_bf16_last_wave(B, N):
+    """bf16 forward at config 2's attention (B = 32, 4 heads, T = 512, N = 8192: 384 pair tiles
+    on 74 pairs, a partial last wave of 14) and a problem smaller than one wave (12 tiles): the
+    last wave's units against float64 at the bf16 bar, strictly causal, the same bits on a second
+    call. With BDH_SM100_SCORE_TAIL=1 the last wave runs as narrow tiles (the same bits)."""
     H, T, D = 4, 512, 256
     g = torch.Generator(device=DEV).manual_seed(17)
     q = torch.relu(torch.randn(B, H, T, N, device=DEV, generator=g)).to(torch.bfloat16)
@@ -191,7 +190,7 @@ def test_forward_bf16_narrow_last_wave(B, N):
     torch.cuda.synchronize()
     assert torch.equal(out, again)
     assert torch.all(out[:, :, 0] == 0)
-    # the narrow tiles are the last ones of the tile list: the highest units
+    # the last wave's tiles are the last ones of the tile list: the highest units
     for u in sorted({B * H - 1, B * H - 2, B * H - 5, 0}):
         b, h = divmod(u, H)
         qd = q[b, h].double()
