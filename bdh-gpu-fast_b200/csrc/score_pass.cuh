@@ -44,6 +44,7 @@ struct ScoreProb {
     // B rows loaded through b_nar (box BK x 128 / tail_sub)
     CUtensorMap b_nar;
     int tail_from, tail_sub;
+    int self_ab;           // CTA-pair pass: B is A (one tensor, one set of strides, per head)
     int H, T, K;           // heads, sequence length, contraction width
     int b_shared;          // B has a single head shared by all H heads of A
     int mode;              // ScoreStore

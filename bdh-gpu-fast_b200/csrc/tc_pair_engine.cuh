@@ -54,6 +54,14 @@ struct HasVarN : std::false_type {};
 template <class P>
 struct HasVarN<P, std::void_t<decltype(P::kVarN)>> : std::true_type {};
 
+// P::kBFromA: when P::b_is_a(prm, tile) holds, the tile's B operand is its A operand (a
+// diagonal tile of a self product Q Q^T: each CTA's 128 rows of A are also its 128 rows of B),
+// so the stages carry A only (P::load_stage loads no B) and the MMAs read B from A's buffer.
+template <class P, class = void>
+struct HasBFromA : std::false_type {};
+template <class P>
+struct HasBFromA<P, std::void_t<decltype(P::kBFromA)>> : std::true_type {};
+
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -234,7 +242,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<P>(), 1
     if (leader && elect_one()) {
       const uint32_t base = smem_u32(smem);
       const uint64_t a0 = S::a_desc(base);
-      const uint64_t b0 = S::b_desc(base + S::A_TERMS * S::A_TILE);
+      const uint64_t b0_own = S::b_desc(base + S::A_TERMS * S::A_TILE);
+      const uint64_t b0_a = S::b_desc(base);  // B read from A's buffer (kBFromA)
       const uint32_t empty_peer = mapa_shared(smem_u32(empty), 1);
       const uint32_t tfull_peer = mapa_shared(smem_u32(tfull), 1);
       const uint32_t empty_own = mapa_shared(smem_u32(empty), 0);
@@ -257,6 +266,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<P>(), 1
         const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * S::BN);
         uint32_t idesc = S::IDESC;
         if constexpr (HasVarN<P>::value) idesc = P::tile_idesc(prm, tile);
+        uint64_t b0 = b0_own;
+        if constexpr (HasBFromA<P>::value) {
+          if (P::b_is_a(prm, tile)) b0 = b0_a;
+        }
         for (int kb = 0; kb < nkb; ++kb) {
           if (!wait_bounded(full + stage, ph, abort_flag, prm.err, kErrTimeoutMma)) {
             ok = false;
