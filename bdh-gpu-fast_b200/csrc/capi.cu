@@ -400,11 +400,16 @@ int bdh_latent_gate_x(const void* y, const int64_t y_strides[4], const void* enc
   return launch_latent_gate_x(a, static_cast<cudaStream_t>(stream), device_error_ptr());
 }
 
-int bdh_latent_gate_dec(const void* y, const int64_t y_strides[4], const void* encv,
-                        const int64_t encv_strides[3], const void* xs, const int64_t xs_strides[4],
-                        const void* dec, const int64_t dec_strides[2], void* out,
-                        const int64_t out_strides[3], int64_t B, int64_t T, int64_t H, int64_t D,
-                        int64_t N, void* stream) {
+size_t bdh_latent_gate_dec_workspace_size(int64_t B, int64_t T, int64_t H, int64_t D, int64_t N) {
+  if (B < 0 || T < 0 || H < 0 || D < 0 || N < 0) return 0;
+  return latent_gate_dec_workspace_bytes(B, T, H, D, N);
+}
+
+int bdh_latent_gate_dec_ws(const void* y, const int64_t y_strides[4], const void* encv,
+                           const int64_t encv_strides[3], const void* xs, const int64_t xs_strides[4],
+                           const void* dec, const int64_t dec_strides[2], void* out,
+                           const int64_t out_strides[3], int64_t B, int64_t T, int64_t H, int64_t D,
+                           int64_t N, void* workspace, size_t workspace_bytes, void* stream) {
   std::string msg;
   if (!latent_sizes_ok(B, T, H, D, N, &msg)) return fail(BDH_ERR_INVALID, "latent_gate_dec: " + msg);
   if (D != 256 || N % 128 != 0)
@@ -436,7 +441,20 @@ int bdh_latent_gate_dec(const void* y, const int64_t y_strides[4], const void* e
   a.out = out;
   std::memcpy(a.out_strides, out_strides, sizeof(a.out_strides));
   a.B = B; a.T = T; a.H = H; a.D = D; a.N = N;
+  if (workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0)
+    return fail(BDH_ERR_INVALID, "latent_gate_dec: the workspace must be 16-byte aligned");
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
   return launch_latent_gate_dec(a, static_cast<cudaStream_t>(stream), device_error_ptr());
+}
+
+int bdh_latent_gate_dec(const void* y, const int64_t y_strides[4], const void* encv,
+                        const int64_t encv_strides[3], const void* xs, const int64_t xs_strides[4],
+                        const void* dec, const int64_t dec_strides[2], void* out,
+                        const int64_t out_strides[3], int64_t B, int64_t T, int64_t H, int64_t D,
+                        int64_t N, void* stream) {
+  return bdh_latent_gate_dec_ws(y, y_strides, encv, encv_strides, xs, xs_strides, dec, dec_strides,
+                                out, out_strides, B, T, H, D, N, nullptr, 0, stream);
 }
 
 int bdh_quantize_rows_fp8(const void* x, const int64_t x_strides[4], int x_dtype, int64_t B,

@@ -26,6 +26,11 @@
 //   warps 2..9 : epilogue in both CTAs, two warps per TMEM lane quadrant (64 gate columns and
 //                128 output columns each); releases go to the leader with cluster-scope arrives.
 // Every wait is bounded (an abort flag and the device error word as in the other engines).
+//
+// Few rows (B T / 256 row pairs well below the number of CTA pairs, e.g. a small batch, or one
+// rank's share of a strongly scaled batch): with a workspace, each row pair's latent walk is cut
+// into `split` equal ranges run by different pairs; each writes its fp32 decoder sums, and a
+// second kernel adds the ranges in order and rounds once to bf16 (deterministic).
 #include <algorithm>
 #include <string>
 
@@ -59,6 +64,8 @@ struct GateDecParams {
   int64_t out_sb, out_st;
   int B, T, H, N;
   int tb_n, tbp_n, nb_n;  // 128-row blocks, row-block pairs per batch; 128-column blocks per head
+  int split, jper;        // latent ranges per row pair and blocks per range (split divides H nb_n)
+  float* part;            // split > 1: fp32 sums [split][B][tbp_n * 256][256]
   int* err;
 };
 
@@ -145,8 +152,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGdThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
-  const int nitems = prm.B * prm.tbp_n;
-  const int J = prm.H * prm.nb_n;  // latent blocks per item
+  const int nitems = prm.B * prm.tbp_n * prm.split;  // (row pair, latent range) items
+  const int J = prm.H * prm.nb_n;  // latent blocks per row pair
 
   if (threadIdx.x == 0) {
     mbar_init(br.y_full, 1);
@@ -211,11 +218,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGdThreads, 1)
         return true;
       };
       for (int item = pair; item < nitems && ok; item += npairs) {
-        const GdItem it = gd_item(prm, item, rank);
-        for (int j = 0; j < J && ok; ++j) {
+        const int ri = item / prm.split;
+        const int jlo = (item - ri * prm.split) * prm.jper, jhi = jlo + prm.jper;
+        const GdItem it = gd_item(prm, ri, rank);
+        for (int j = jlo; j < jhi && ok; ++j) {
           const int jj = gd_walk(prm, item, j, J);
           const int h = jj / prm.nb_n, nb = jj - (jj / prm.nb_n) * prm.nb_n;
-          if (j == 0 || nb == 0) {  // a new head: its y rows (resident for its latent blocks)
+          if (j == jlo || nb == 0) {  // a new head: its y rows (resident for its latent blocks)
             if (*br.abort_flag || !wait_bounded(br.y_empty, static_cast<uint32_t>(hc & 1) ^ 1u,
                                                 br.abort_flag, prm.err, kErrTimeoutProducer)) {
               ok = false;
@@ -241,9 +250,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGdThreads, 1)
               eph ^= 1u;
             }
           }
-          if (ok && j > 0) ok = load_dt(item, j - 1);
+          if (ok && j > jlo) ok = load_dt(item, j - 1);
         }
-        if (ok) ok = load_dt(item, J - 1);
+        if (ok) ok = load_dt(item, jhi - 1);
       }
     }
   } else if (warp == 1) {
@@ -288,10 +297,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGdThreads, 1)
         return true;
       };
       for (int item = pair; item < nitems && ok; item += npairs) {
-        for (int j = 0; j < J && ok; ++j) {
+        const int jlo = (item - (item / prm.split) * prm.split) * prm.jper, jhi = jlo + prm.jper;
+        for (int j = jlo; j < jhi && ok; ++j) {
           const int jj = gd_walk(prm, item, j, J);
           const int nb = jj - (jj / prm.nb_n) * prm.nb_n;
-          if (j == 0 || nb == 0) {
+          if (j == jlo || nb == 0) {
             if (!wait_bounded(br.y_full, static_cast<uint32_t>(hc & 1), br.abort_flag, prm.err,
                               kErrTimeoutMma)) {
               ok = false;
@@ -328,15 +338,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGdThreads, 1)
           }
           if (!ok) break;
           both(br.gfull + s);
-          if (nb == prm.nb_n - 1 || j == J - 1) both(br.y_empty);  // the head's gate MMAs issued
-          if (j > 0 && !dec(g - 1, j == 1)) {
+          if (nb == prm.nb_n - 1 || j == jhi - 1) both(br.y_empty);  // the head's gate MMAs issued
+          if (j > jlo && !dec(g - 1, j == jlo + 1)) {
             ok = false;
             break;
           }
           ++g;
         }
         if (!ok) break;
-        if (!dec(g - 1, J == 1)) break;
+        if (!dec(g - 1, prm.jper == 1)) break;
         both(br.dfull);
         ++ic;
       }
@@ -355,7 +365,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGdThreads, 1)
     const uint32_t ready_l = mapa_shared(smem_u32(br.xy_ready), 0);
     const uint32_t dempty_l = mapa_shared(smem_u32(br.dempty), 0);
     const int my_items = pair < nitems ? (nitems - 1 - pair) / npairs + 1 : 0;
-    const int total = my_items * J;
+    const int total = my_items * prm.jper;
     // xs slice of latent block gg (this CTA's walk) into slot gg % 3 (lane 0 issues)
     auto issue_xs = [&](int gg) -> bool {
       bool ok = true;
@@ -366,9 +376,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGdThreads, 1)
                             (static_cast<uint32_t>(gg / kGdXySlots) & 1u) ^ 1u, br.abort_flag,
                             prm.err, kErrTimeoutEpilogue);
         if (ok) {
-          const int item = pair + (gg / J) * npairs;
-          const GdItem it = gd_item(prm, item, rank);
-          const int jj = gd_walk(prm, item, gg - (gg / J) * J, J);
+          const int item = pair + (gg / prm.jper) * npairs;
+          const int ri = item / prm.split;
+          const GdItem it = gd_item(prm, ri, rank);
+          const int jj = gd_walk(prm, item,
+                                 (item - ri * prm.split) * prm.jper + gg - (gg / prm.jper) * prm.jper, J);
           const int h = jj / prm.nb_n, nb = jj - (jj / prm.nb_n) * prm.nb_n;
           uint64_t* bar = br.xs_full + s * kGdEpiWarps + w;
           mbar_arrive_expect_tx(bar, 32 * 128);
@@ -384,8 +396,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGdThreads, 1)
     for (int gg = 0; gg < 2 && gg < total && ok; ++gg) ok = issue_xs(gg);
     int g = 0;
     for (int k = 0; k < my_items && ok; ++k) {
-      const GdItem it = gd_item(prm, pair + k * npairs, rank);
-      for (int j = 0; j < J; ++j, ++g) {
+      const int item = pair + k * npairs;
+      const int ri = item / prm.split;
+      const int rs = item - ri * prm.split;  // latent range of a split row pair
+      const GdItem it = gd_item(prm, ri, rank);
+      for (int j = 0; j < prm.jper; ++j, ++g) {
         const int s = g % kGdXySlots;  // xs / xy slot
         const int a = g & 1;           // gate accumulator
         const bool okw = wait_bounded(br.xs_full + s * kGdEpiWarps + w,
@@ -445,12 +460,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGdThreads, 1)
       tc_fence_after();
       const int t = it.t0 + row;
       uint16_t* orow = prm.out + it.b * prm.out_sb + static_cast<int64_t>(t) * prm.out_st + part * 128;
+      float* prow = prm.split > 1
+                        ? prm.part + ((static_cast<int64_t>(rs) * prm.B + it.b) * (prm.tbp_n * 256) + t) * kGdD +
+                              part * 128
+                        : nullptr;
 #pragma unroll 1
       for (int c = 0; c < 128; c += 32) {
         uint32_t r[32];
         tmem_ld32(lane_base + static_cast<uint32_t>(256 + part * 128 + c), r);
         tmem_ld_wait();
-        if (t < prm.T) {
+        if (prow != nullptr) {  // this range's fp32 sums (the reduce kernel adds the ranges)
+          if (t < prm.T) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              *reinterpret_cast<uint4*>(prow + c + 4 * q) =
+                  make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          }
+        } else if (t < prm.T) {
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             *reinterpret_cast<uint4*>(orow + c + 8 * q) =
@@ -475,10 +501,92 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGdThreads, 1)
   }
 }
 
+// out[b, t, :] = bf16(sum over the ranges s = 0 .. split-1 of part[s][b][t][:]), in that order:
+// 32 threads per row, eight columns each.
+__global__ void __launch_bounds__(256) gate_dec_reduce_kernel(const float* __restrict__ part,
+                                                              uint16_t* __restrict__ out,
+                                                              int64_t out_sb, int64_t out_st, int B,
+                                                              int T, int tpad, int split) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= static_cast<int64_t>(B) * T) return;
+  const int b = static_cast<int>(row / T), t = static_cast<int>(row - static_cast<int64_t>(b) * T);
+  const int c = (threadIdx.x & 31) * 8;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < split; ++s) {
+    const float4* p = reinterpret_cast<const float4*>(
+        part + ((static_cast<int64_t>(s) * B + b) * tpad + t) * kGdD + c);
+    const float4 u = __ldcs(p), v = __ldcs(p + 1);
+    acc[0] += u.x; acc[1] += u.y; acc[2] += u.z; acc[3] += u.w;
+    acc[4] += v.x; acc[5] += v.y; acc[6] += v.z; acc[7] += v.w;
+  }
+  *reinterpret_cast<uint4*>(out + b * out_sb + static_cast<int64_t>(t) * out_st + c) =
+      make_uint4(cvt_bf16x2(acc[0], acc[1]), cvt_bf16x2(acc[2], acc[3]), cvt_bf16x2(acc[4], acc[5]),
+                 cvt_bf16x2(acc[6], acc[7]));
+}
+
 constexpr int kGdES = 4;
 constexpr int kGdDS = 2;
+constexpr int kGdSplitMax = 16;
+
+// CTA pairs of the gate + decoder kernel that fit on the current device at once.
+int gate_dec_pairs() {
+  using L = GdLayout<kGdES, kGdDS>;
+  auto kern = gate_dec_kernel<kGdES, kGdDS>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static int max_pairs[64] = {0};
+  if (dev >= 0 && dev < 64 && max_pairs[dev] == 0) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    if (e != cudaSuccess) {
+      set_error(std::string("cudaFuncSetAttribute (gate_dec): ") + cudaGetErrorString(e));
+      return -BDH_ERR_CUDA;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 74);
+    cfg.blockDim = dim3(kGdThreads);
+    cfg.dynamicSmemBytes = L::SMEM;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count(dev) / 2;
+    }
+    max_pairs[dev] = n;
+  }
+  return max_pairs[(dev >= 0 && dev < 64) ? dev : 0];
+}
+
+// Latent ranges per row pair: 1, or the largest power of two (at most kGdSplitMax, dividing
+// the H * N / 128 latent blocks) that keeps the split row pairs within one wave of CTA pairs,
+// when the row pairs fill at most half of them.
+int gate_dec_split(int64_t B, int64_t T, int64_t H, int64_t N, int pairs) {
+  const int64_t rows = B * ((T + 255) / 256);
+  const int64_t J = H * (N / 128);
+  if (rows <= 0 || pairs <= 0 || 2 * rows > pairs) return 1;
+  int split = 1;
+  while (split * 2 <= kGdSplitMax && rows * split * 2 <= pairs && J % (split * 2) == 0) split *= 2;
+  return split;
+}
+
+size_t gate_dec_part_bytes(int64_t B, int64_t T, int split) {
+  return split > 1 ? static_cast<size_t>(split) * B * ((T + 255) / 256) * 256 * kGdD * sizeof(float) : 0;
+}
 
 }  // namespace
+
+size_t latent_gate_dec_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t D, int64_t N) {
+  if (D != kGdD || N % 128 != 0 || B * T == 0 || H * N == 0) return 0;
+  const int pairs = gate_dec_pairs();
+  if (pairs <= 0) return 0;
+  return gate_dec_part_bytes(B, T, gate_dec_split(B, T, H, N, pairs));
+}
 
 int launch_latent_gate_dec(const GateDecArgs& a, cudaStream_t stream, int* err) {
   if (a.D != kGdD || a.N % 128 != 0) {
@@ -518,38 +626,27 @@ int launch_latent_gate_dec(const GateDecArgs& a, cudaStream_t stream, int* err) 
   prm.tbp_n = (prm.tb_n + 1) / 2;
   prm.nb_n = static_cast<int>(a.N / 128);
   prm.err = err;
-  const int nitems = prm.B * prm.tbp_n;
-  if (nitems == 0) return BDH_OK;
+  const int rows = prm.B * prm.tbp_n;
+  if (rows == 0) return BDH_OK;
   using L = GdLayout<kGdES, kGdDS>;
   auto kern = gate_dec_kernel<kGdES, kGdDS>;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  static int max_pairs[64] = {0};
-  if (dev >= 0 && dev < 64 && max_pairs[dev] == 0) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
-    if (e != cudaSuccess) {
-      set_error(std::string("cudaFuncSetAttribute (gate_dec): ") + cudaGetErrorString(e));
-      return BDH_ERR_CUDA;
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * 74);
-    cfg.blockDim = dim3(kGdThreads);
-    cfg.dynamicSmemBytes = L::SMEM;
-    cudaLaunchAttribute attr;
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 2;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-    if (e != cudaSuccess || n <= 0) n = sm_count(dev) / 2;
-    max_pairs[dev] = n;
-  }
-  const int pairs = std::min(nitems, max_pairs[(dev >= 0 && dev < 64) ? dev : 0]);
+  const int cap = gate_dec_pairs();
+  if (cap < 0) return -cap;
+  int split = gate_dec_split(a.B, a.T, a.H, a.N, cap);
+  if (split > 1 && (a.workspace == nullptr || a.workspace_bytes < gate_dec_part_bytes(a.B, a.T, split)))
+    split = 1;  // no room for the range sums: one range per row pair
+  prm.split = split;
+  prm.jper = static_cast<int>(a.H) * prm.nb_n / split;
+  prm.part = split > 1 ? static_cast<float*>(a.workspace) : nullptr;
+  const int nitems = rows * split;
+  const int pairs = std::min(nitems, cap);
   prof_start(kProfGate, stream);
   kern<<<2 * pairs, kGdThreads, L::SMEM, stream>>>(prm);
+  if (split > 1) {
+    const int64_t nrow = a.B * a.T;
+    gate_dec_reduce_kernel<<<static_cast<unsigned>((nrow + 7) / 8), 256, 0, stream>>>(
+        prm.part, prm.out, prm.out_sb, prm.out_st, prm.B, prm.T, prm.tbp_n * 256, split);
+  }
   prof_stop(kProfGate, stream);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

@@ -168,8 +168,13 @@ struct GateDecArgs {
   void* out = nullptr;           // (B,T,D) {b,t,d}
   int64_t out_strides[3] = {0, 0, 1};
   int64_t B = 0, T = 0, H = 0, D = 0, N = 0;
+  void* workspace = nullptr;     // optional: the latent-range sums of few-row problems
+  size_t workspace_bytes = 0;
 };
 int launch_latent_gate_dec(const GateDecArgs& a, cudaStream_t stream, int* err);
+// Workspace bytes with which launch_latent_gate_dec splits the latent walk of these sizes on
+// the current device (0: no split).
+size_t latent_gate_dec_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t D, int64_t N);
 int launch_latent_encode(const LatentArgs& a, cudaStream_t stream, int* err);
 int launch_latent_gate_x(const LatentArgs& a, cudaStream_t stream, int* err);
 int launch_latent_gate(const LatentArgs& a, cudaStream_t stream, int* err);

@@ -40,7 +40,7 @@ _F32 = 0
 _BF16 = 1
 
 _c_i64_4 = ctypes.c_int64 * 4
-ABI_VERSION = 7  # BDH_ABI_VERSION of include/bdh_sm100.h
+ABI_VERSION = 8  # BDH_ABI_VERSION of include/bdh_sm100.h
 FP8 = torch.float8_e4m3fn  # the opt-in fp8 key-cache storage dtype
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -87,6 +87,11 @@ def _declare(lib: ctypes.CDLL) -> None:
     _c_i64_2p = ctypes.POINTER(ctypes.c_int64)
     lib.bdh_latent_gate_dec.argtypes = [_vp, P, _vp, _c_i64_3p, _vp, P, _vp, _c_i64_2p, _vp,
                                         _c_i64_3p, _i64, _i64, _i64, _i64, _i64, _vp]
+    lib.bdh_latent_gate_dec_ws.argtypes = [_vp, P, _vp, _c_i64_3p, _vp, P, _vp, _c_i64_2p, _vp,
+                                           _c_i64_3p, _i64, _i64, _i64, _i64, _i64, _vp,
+                                           ctypes.c_size_t, _vp]
+    lib.bdh_latent_gate_dec_workspace_size.restype = ctypes.c_size_t
+    lib.bdh_latent_gate_dec_workspace_size.argtypes = [_i64, _i64, _i64, _i64, _i64]
     lib.bdh_quantize_rows_fp8.argtypes = [_vp, P, ctypes.c_int, _i64, _i64, _i64, _i64, _vp, P,
                                           _vp, P, _vp]
     lib.bdh_tril_decode_fp8.argtypes = [_vp, P, ctypes.c_int, _vp, P, _vp, P, _vp, P, ctypes.c_int,
@@ -103,7 +108,7 @@ def _declare(lib: ctypes.CDLL) -> None:
                                      ctypes.c_size_t, _vp]
     for name in ("bdh_rope_rotate", "bdh_tril_score_v", "bdh_tril_decode", "bdh_tril_score_v_bwd",
                  "bdh_relu_mul", "bdh_latent_encode", "bdh_latent_gate", "bdh_latent_gate_x",
-                 "bdh_latent_gate_dec",
+                 "bdh_latent_gate_dec", "bdh_latent_gate_dec_ws",
                  "bdh_layernorm", "bdh_quantize_rows_fp8", "bdh_tril_decode_fp8",
                  "bdh_residual_layernorm", "bdh_state_decode"):
         getattr(lib, name).restype = ctypes.c_int
@@ -636,9 +641,15 @@ def latent_gate_dec(y: torch.Tensor, encv: torch.Tensor, xs: torch.Tensor, dec: 
         raise ValueError("latent_gate_dec: out must be (B,T,D)")
     _check_latent("latent_gate_dec", y, xs, out, weight=encv)
     with torch.cuda.device(dev):
-        rc = lib.bdh_latent_gate_dec(y.data_ptr(), _st(y, 4), encv.data_ptr(), _st(encv, 3),
-                                     xs.data_ptr(), _st(xs, 4), dec.data_ptr(), _st(dec, 2),
-                                     out.data_ptr(), _st(out, 3), B, T, H, D, N, _stream(dev))
+        # few rows (a small batch): the latent walk is split across the GPU, its range sums in
+        # a workspace from the caching allocator
+        wsz = int(lib.bdh_latent_gate_dec_workspace_size(B, T, H, D, N))
+        ws = torch.empty(max(wsz, 1), dtype=torch.uint8, device=dev) if wsz else None
+        rc = lib.bdh_latent_gate_dec_ws(y.data_ptr(), _st(y, 4), encv.data_ptr(), _st(encv, 3),
+                                        xs.data_ptr(), _st(xs, 4), dec.data_ptr(), _st(dec, 2),
+                                        out.data_ptr(), _st(out, 3), B, T, H, D, N,
+                                        ws.data_ptr() if ws is not None else None, wsz,
+                                        _stream(dev))
     _check(rc, "latent_gate_dec")
     return out
 

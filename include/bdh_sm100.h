@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define BDH_ABI_VERSION 7
+#define BDH_ABI_VERSION 8
 
 #define BDH_DTYPE_F32 0
 #define BDH_DTYPE_BF16 1
@@ -275,6 +275,21 @@ int bdh_latent_gate_dec(const void* y, const int64_t y_strides[4], const void* e
                         const void* dec, const int64_t dec_strides[2], void* out,
                         const int64_t out_strides[3], int64_t B, int64_t T, int64_t H, int64_t D,
                         int64_t N, void* stream);
+/*
+ * bdh_latent_gate_dec with a workspace (same computation, same reference lines). When the
+ * problem has few rows (B * ceil(T / 256) row pairs filling at most half the GPU's CTA pairs: a
+ * small batch, or one rank's share of a strongly scaled batch), each row pair's walk over the
+ * H * N latent columns is cut into up to 16 ranges run side by side, and the ranges' fp32 sums
+ * are added in range order before the single rounding to bf16 (deterministic). The workspace
+ * holds those sums: bdh_latent_gate_dec_workspace_size bytes (0 when no split is made; a smaller
+ * workspace than asked for runs unsplit), 16-byte aligned. No counterpart in the reference.
+ */
+size_t bdh_latent_gate_dec_workspace_size(int64_t B, int64_t T, int64_t H, int64_t D, int64_t N);
+int bdh_latent_gate_dec_ws(const void* y, const int64_t y_strides[4], const void* encv,
+                           const int64_t encv_strides[3], const void* xs, const int64_t xs_strides[4],
+                           const void* dec, const int64_t dec_strides[2], void* out,
+                           const int64_t out_strides[3], int64_t B, int64_t T, int64_t H, int64_t D,
+                           int64_t N, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * fp8 wire format of the cached rotated keys (opt-in cache storage; the reference keeps its

@@ -72,6 +72,24 @@ def test_gate_dec_matches_unfused_library_path():
     assert ((fused.double() - unfused.double()).norm() / unfused.double().norm()).item() < 3e-3
 
 
+@pytest.mark.parametrize("B,T", [(1, 512), (4, 512), (2, 130)])
+def test_gate_dec_split_latent_walk_for_few_rows(B, T):
+    """Few row pairs (a small batch; one rank's share of a strongly scaled config-2 batch): the
+    latent walk runs split across the GPU with a workspace, the ranges' fp32 sums added in a
+    fixed order. Config-2 layer widths (4 heads, N = 8192) against float64 sums of the same xy,
+    the same bits on a second call."""
+    H, N = 4, 8192
+    s = sa()
+    assert s.load_library().bdh_latent_gate_dec_workspace_size(B, T, H, 256, N) > 0
+    y, encv, xs, dec = (t.to(DEV) for t in _operands(B, T, H, N, seed=B * 7 + T))
+    w, d = s.weight_k_major(encv), s.decoder_k_major(dec)
+    out = s.latent_gate_dec(y, w, xs, d)
+    assert torch.equal(out, s.latent_gate_dec(y, w, xs, d))
+    xy = s.latent_gate(y, w, xs)
+    ref = xy.view(B, T, H * N).double() @ dec.double()
+    assert ((out.double() - ref).norm() / ref.norm()).item() < 3e-3
+
+
 def test_gate_dec_into_strided_output():
     B, T, H, N = 2, 256, 2, 256
     y, encv, xs, dec = _operands(B, T, H, N, seed=9)
