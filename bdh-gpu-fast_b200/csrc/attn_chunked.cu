@@ -53,12 +53,17 @@ int forced_chunk() {
 // store tensor map and writes them with four TMA bulk stores (whole 128-byte lines), then
 // reuses the staging once the previous chunk's stores have read it.
 // ST = 2: S as bf16 hi + lo; ST = 1: S as one bf16 term.
-template <int STAGES, int CKB, int ST = 2>  // CKB = k-blocks (64 keys) per chunk
+// BNS = 256 (D = 256 in one tile, eight epilogue warps, each 32 rows x 128 columns): every key
+// row is staged once per latent block instead of once per 128-column value half, a quarter less
+// operand traffic out of L2 (the latents once, V once per latent block) at three stages of
+// 48 KB instead of four of 32 KB.
+template <int STAGES, int CKB, int ST = 2, int BNS = 128>  // CKB = k-blocks (64 keys) per chunk
 struct StateProb {
-  using S = TcShape<2, 128, true, true, 1, 1, STAGES, CKB>;
+  using S = TcShape<2, BNS, true, true, 1, 1, STAGES, CKB>;
   static constexpr int kEmitEveryChunk = 1;
+  static constexpr int kEpiWarps = BNS == 256 ? 8 : 4;
   static constexpr int kWarpStage = 2 * ST * 32 * 128;  // terms x two 64-column boxes x 32 rows
-  static constexpr int kEpiSmemBytes = 4 * kWarpStage;
+  static constexpr int kEpiSmemBytes = kEpiWarps * kWarpStage;
   struct Params {
     CUtensorMap a_map[1];  // K (B,H,T,N) read MN-major: box 64 (n) x 64 (t)
     CUtensorMap b_map[1];  // V (B,Hv,T,D) read MN-major: box 64 (d) x 64 (t)
@@ -93,18 +98,21 @@ struct StateProb {
     const int hv = p.Hv == 1 ? 0 : h;
     const int t0 = kb * 64;
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
+    for (int c = 0; c < 2; ++c)
       tma_load_4d(&p.a_map[0], bar, a_dst + c * 64 * 128, tl.ni * 128 + c * 64, t0, h, b);
-      tma_load_4d(&p.b_map[0], bar, b_dst + c * 64 * 128, tl.di * 128 + c * 64, t0, hv, b);
-    }
+#pragma unroll
+    for (int c = 0; c < BNS / 64; ++c)
+      tma_load_4d(&p.b_map[0], bar, b_dst + c * 64 * 128, tl.di * BNS + c * 64, t0, hv, b);
   }
   __device__ static void epilogue(const Params&, const Tile&, int, int, const uint32_t (&)[32]) {}
   // After chunk ch the running sum is S_ch, the prefix state of chunk ch + 1.
   __device__ static void epilogue_chunk(const Params& p, const Tile& tl, int row, int ch, int,
-                                        int c0, const uint32_t (&r)[32], uint8_t* epi) {
+                                        int c_tile, const uint32_t (&r)[32], uint8_t* epi) {
     const int quad = row >> 5, lr = row & 31;
     const bool leader = lr == 0;
-    uint8_t* st = epi + quad * kWarpStage;
+    const int part = c_tile >> 7;  // this warp's 128 of the tile's columns
+    const int c0 = c_tile & 127;
+    uint8_t* st = epi + (part * 4 + quad) * kWarpStage;
     if (c0 == 0) {
       // the previous chunk's stores must have read the staging before it is overwritten
       if (leader) bulk_wait_read_all();
@@ -127,14 +135,14 @@ struct StateProb {
       *reinterpret_cast<uint4*>(hi_row + sw) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
       if (ST == 2) *reinterpret_cast<uint4*>(lo_row + sw) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
     }
-    if (c0 + 32 == S::BN) {
+    if (c0 + 32 == 128) {
       fence_async_smem();
       __syncwarp();
       const int n0 = tl.ni * 128 + quad * 32;
       if (leader && n0 < p.N) {
 #pragma unroll
         for (int hb = 0; hb < 2; ++hb) {
-          const int x = tl.di * 128 + hb * 64;
+          const int x = tl.di * BNS + part * 128 + hb * 64;
           if (x < p.D) {
             tma_store_4d(&p.s_map[0], st + hb * 4096, x, n0, ch + 1, tl.unit);
             if (ST == 2) tma_store_4d(&p.s_map[1], st + (2 + hb) * 4096, x, n0, ch + 1, tl.unit);
@@ -352,8 +360,8 @@ bool use_pairs_chunked() {
 
 using StateBf16C256 = StateProb<4, 4>;
 using StateBf16C512 = StateProb<4, 8>;
-using StateBf16C256One = StateProb<4, 4, 1>;
-using StateBf16C512One = StateProb<4, 8, 1>;
+using StateBf16C256One = StateProb<3, 4, 1, 256>;
+using StateBf16C512One = StateProb<3, 8, 1, 256>;
 
 }  // namespace
 
@@ -389,7 +397,7 @@ int launch_state_pass(const FwdArgs& a, void* s_hi, void* s_lo, int nchunks, cud
   prm.N = static_cast<int>(a.N);
   prm.D = static_cast<int>(a.D);
   prm.nn = static_cast<int>((a.N + 127) / 128);
-  prm.nd = static_cast<int>((a.D + 127) / 128);
+  prm.nd = static_cast<int>((a.D + SP::S::BN - 1) / SP::S::BN);
   prm.units = static_cast<int>(a.B * a.H);
   prm.nchunks = nchunks;
   const int64_t sd[4] = {a.D, a.N, nchunks, a.B * a.H};

@@ -164,9 +164,10 @@ struct EpiSmem<P, std::void_t<decltype(P::kEpiSmemBytes)>> {
 constexpr int kTcThreads = 192;
 constexpr int kEpiThreads = 128;
 
-//   P::kEpiWarps = 8 (custom epilogues only) -> two epilogue warps per TMEM lane quadrant, each
-//       draining half of the tile's columns (`part` 0 / 1 in the custom hooks); the CTA then
-//       has 64 + 256 threads.
+//   P::kEpiWarps = 8 (custom epilogues, or chunked accumulation) -> two epilogue warps per TMEM
+//       lane quadrant, each draining half of the tile's columns (`part` 0 / 1 in the custom
+//       hooks; with KCHUNK each keeps BN / 2 running sums and passes its columns' c0 offsets,
+//       part * BN / 2 + ..., to P::epilogue_chunk); the CTA then has 64 + 256 threads.
 template <class P, class = void>
 struct EpiWarps {
   static constexpr int value = 4;
@@ -210,7 +211,7 @@ struct TcShape {
   static constexpr int NPAIRS = (A_TERMS == 1 && B_TERMS == 1) ? 1 : (A_TERMS == 2 && B_TERMS == 2 ? 3 : 2);
 
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
-  static_assert(KCHUNK == 0 || BN <= 128, "chunked accumulation keeps BN fp32 sums per thread");
+  static_assert(KCHUNK == 0 || BN <= 256, "chunked accumulation keeps the tile's fp32 sums in registers");
 
   __host__ __device__ static int chunks(int nkb) {
     return KCHUNK == 0 ? 1 : (nkb + KCHUNK - 1) / KCHUNK;
@@ -265,8 +266,11 @@ __device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity, int* 
 template <class S, class P>
 __global__ void __launch_bounds__(tc_threads<P>(), 1)
     tc_gemm_kernel(const __grid_constant__ typename P::Params prm) {
-  static_assert(EpiWarps<P>::value == 4 || (EpiWarps<P>::value == 8 && HasCustomEpi<P>::value),
-                "eight epilogue warps need a custom epilogue");
+  static_assert(EpiWarps<P>::value == 4 ||
+                    (EpiWarps<P>::value == 8 && (HasCustomEpi<P>::value || S::KCHUNK > 0)),
+                "eight epilogue warps need a custom epilogue or chunked accumulation");
+  static_assert(S::KCHUNK == 0 || S::BN / (EpiWarps<P>::value / 4) <= 128,
+                "at most 128 running sums per epilogue thread");
   static_assert(tc_smem_bytes<S, P>() <= 232448, "shared memory budget");
   static_assert(ResidentB<P>::value == 0 || S::B_TERMS == 1, "resident B holds one term");
   static_assert(S::STAGES <= 8, "barrier block layout (2 x 8 stages + 2 x 4 accumulators + 5)");
@@ -539,7 +543,9 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
         mbar_arrive(tempty + acc);
         ++lc;
       } else {
-        constexpr int BNC = S::KCHUNK == 0 ? 32 : S::BN;
+        // this thread's columns: all BN (four epilogue warps) or one half (eight)
+        constexpr int BNC = S::KCHUNK == 0 ? 32 : S::BN / (EpiWarps<P>::value / 4);
+        const int col0 = part * BNC;
         float sum[BNC];
 #pragma unroll
         for (int i = 0; i < BNC; ++i) sum[i] = 0.0f;
@@ -555,13 +561,18 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
           tc_fence_after();
           const uint32_t tbase =
               tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * ACC_COLS);
+          // 16 columns at a time when a thread keeps 128 running sums (register budget)
+          constexpr int LDC = BNC > 64 ? 16 : 32;
 #pragma unroll
-          for (int c0 = 0; c0 < BNC; c0 += 32) {
-            uint32_t r[32];
-            tmem_ld32(tbase + static_cast<uint32_t>(c0), r);
+          for (int c0 = 0; c0 < BNC; c0 += LDC) {
+            uint32_t r[LDC];
+            if constexpr (LDC == 16)
+              tmem_ld16(tbase + static_cast<uint32_t>(col0 + c0), r);
+            else
+              tmem_ld32(tbase + static_cast<uint32_t>(col0 + c0), r);
             tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) sum[c0 + e] = __fadd_rn(sum[c0 + e], __uint_as_float(r[e]));
+            for (int e = 0; e < LDC; ++e) sum[c0 + e] = __fadd_rn(sum[c0 + e], __uint_as_float(r[e]));
           }
           tc_fence_before();
           mbar_arrive(tempty + acc);
@@ -571,7 +582,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
               uint32_t r[32];
 #pragma unroll
               for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(sum[c0 + e]);
-              P::epilogue_chunk(prm, tile, row, ch, nch, c0, r, epi);
+              P::epilogue_chunk(prm, tile, row, ch, nch, col0 + c0, r, epi);
             }
           }
         }
@@ -582,7 +593,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
             uint32_t r[32];
 #pragma unroll
             for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(sum[c0 + e]);
-            P::epilogue(prm, tile, row, c0, r);
+            P::epilogue(prm, tile, row, col0 + c0, r);
           }
         }
       }
