@@ -116,6 +116,12 @@ def test_config2_bf16_logits_match_reference(monkeypatch):
     assert gpu_floor < 1e-2  # the reference's own chain on this GPU (sanity)
     assert err <= max(3e-3, cpu_floor, 1.1 * gpu_floor)
     assert _sa().device_error() == 0
+    # this build's eager model path issues the same calls: the same bits
+    m.attn._attn_impl_override = "eager"
+    monkeypatch.setenv("BDH_SM100_LATENT", "0")
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        eager = m(idx)[0]
+    assert torch.equal(eager, ref_gpu)
 
 
 def test_config2_bf16_layers_teacher_forced_match_reference(monkeypatch):
