@@ -592,9 +592,17 @@ using GateX = GateXProb<6>;
 using GateXK = GateXProb<6, true>;
 
 // Row blocks per chunk of the chunked walk: the largest divisor of the row-block count <= 32.
-int walk_chunk_for(int64_t row_blocks) {
+// Row blocks per chunk of the chunked walk: the largest divisor of row_blocks up to 32 that
+// still leaves at least six chunks per SM (chunks = row_blocks / c x column blocks), so that the
+// last round of chunks is a small share of a CTA's work; long chunks keep the resident weights
+// of a column block for more tiles. Config 2 (128 row blocks, 256 column blocks): 32; B = 4:
+// 4 instead of 16 (1024 chunks on 148 SMs instead of 256).
+int walk_chunk_for(int64_t row_blocks, int64_t col_blocks) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int64_t want = 6 * static_cast<int64_t>(sm_count(dev));
   for (int c = 32; c > 1; --c)
-    if (row_blocks % c == 0) return c;
+    if (row_blocks % c == 0 && (row_blocks / c) * col_blocks >= want) return c;
   return 1;
 }
 
@@ -668,7 +676,7 @@ int launch_latent_encode(const LatentArgs& a, cudaStream_t stream, int* err) {
   prm.pos0 = static_cast<int>(a.pos0);
   prm.tb_n = static_cast<int>((a.T + 127) / 128);
   prm.nb_n = static_cast<int>((a.N + 127) / 128);
-  prm.walk_chunk = walk_chunk_for(a.B * int64_t(prm.tb_n));
+  prm.walk_chunk = walk_chunk_for(a.B * int64_t(prm.tb_n), int64_t(prm.H) * prm.nb_n);
   prm.fd_chunk = FastDiv(static_cast<uint32_t>(prm.walk_chunk));
   prm.fd_ncb = FastDiv(static_cast<uint32_t>(prm.H * prm.nb_n));
   prm.fd_b = FastDiv(static_cast<uint32_t>(prm.B));
@@ -721,7 +729,7 @@ int launch_latent_gate_x(const LatentArgs& a, cudaStream_t stream, int* err) {
   prm.tb_n = static_cast<int>((a.T + 127) / 128);
   prm.nb_n = static_cast<int>((a.N + 127) / 128);
   prm.kbs = static_cast<int>((a.D + 63) / 64);
-  prm.walk_chunk = walk_chunk_for(a.B * int64_t(prm.tb_n));
+  prm.walk_chunk = walk_chunk_for(a.B * int64_t(prm.tb_n), int64_t(prm.H) * prm.nb_n);
   prm.fd_chunk = FastDiv(static_cast<uint32_t>(prm.walk_chunk));
   prm.fd_ncb = FastDiv(static_cast<uint32_t>(prm.H * prm.nb_n));
   prm.fd_b = FastDiv(static_cast<uint32_t>(prm.B));
@@ -747,7 +755,7 @@ int launch_latent_gate(const LatentArgs& a, cudaStream_t stream, int* err) {
   prm.N = static_cast<int>(a.N);
   prm.tb_n = static_cast<int>((a.T + 127) / 128);
   prm.nb_n = static_cast<int>((a.N + 127) / 128);
-  prm.walk_chunk = walk_chunk_for(a.B * int64_t(prm.tb_n));
+  prm.walk_chunk = walk_chunk_for(a.B * int64_t(prm.tb_n), int64_t(prm.H) * prm.nb_n);
   prm.fd_chunk = FastDiv(static_cast<uint32_t>(prm.walk_chunk));
   prm.fd_ncb = FastDiv(static_cast<uint32_t>(prm.H * prm.nb_n));
   prm.fd_b = FastDiv(static_cast<uint32_t>(prm.B));
