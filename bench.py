@@ -546,25 +546,41 @@ def bench_config2(args, world, rank, dev):
     assert sm100_attn.device_error(dev) == 0
     value = world * B * T * args.steps / (ms / 1e3)
 
+    # the same step replayed from CUDA graphs (the public bdh_model.GraphedForward: launches
+    # and their host work paid once, at capture); two captures so that one step's logits can be
+    # copied out while the other graph runs the next step
+    graphs = [model.graphed_forward(B, T) for _ in range(2)]
+
+    def graph_step_n():
+        graphs[0](idx)
+
+    ms_graph = timed(graph_step_n, args.steps, world, dev)
+    value_graphed = world * B * T * args.steps / (ms_graph / 1e3)
+
     # end to end through the public API with host buffers: every step copies its token ids in
-    # from pinned memory and its bf16 logits out to pinned memory; the copy-out of step i runs on
-    # a side stream beside step i + 1's kernels (two host buffers in turn), and the timed region
-    # ends after the last copy has landed
-    idx_dev = torch.empty_like(idx)
-    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
-        out_shape = model(idx)[0].shape
-    logits_host = [torch.empty(out_shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    # from pinned memory (into the graph's input buffer) and its bf16 logits out to pinned
+    # memory; the copy-out of step i runs on a side stream beside step i + 1 (the other graph,
+    # two host buffers in turn), and the timed region ends after the last copy has landed
+    logits_host = [torch.empty(tuple(graphs[0].logits.shape), dtype=torch.bfloat16).pin_memory()
+                   for _ in range(2)]
     copy_stream = torch.cuda.Stream(dev)
+    copied = [None, None]  # event after the copy-out of each graph's last logits
     n_e2e = [0]
 
     def e2e_step():
-        idx_dev.copy_(idx_host, non_blocking=True)
-        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
-            logits = model(idx_dev)[0]
-        copy_stream.wait_stream(torch.cuda.current_stream(dev))
+        k = n_e2e[0] % 2
+        run = graphs[k]
+        cur = torch.cuda.current_stream(dev)
+        if copied[k] is not None:
+            cur.wait_event(copied[k])  # that graph's previous logits have been copied out
+        run.idx.copy_(idx_host, non_blocking=True)
+        run.graph.replay()
+        copy_stream.wait_stream(cur)
         with torch.cuda.stream(copy_stream):
-            logits_host[n_e2e[0] % 2].copy_(logits, non_blocking=True)
-        logits.record_stream(copy_stream)
+            logits_host[k].copy_(run.logits, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(copy_stream)
+        copied[k] = ev
         n_e2e[0] += 1
 
     def e2e_join():
@@ -601,8 +617,14 @@ def bench_config2(args, world, rank, dev):
                    "cache": "inputs larger than L2 (1 GB latent per layer per GPU); no flush"},
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": idx_host.numel() * 8,
                 "d2h_bytes_per_step": logits_host[0].numel() * 2,
+                "api": "bdh_model.BDH.graphed_forward (the step captured as a CUDA graph)",
                 "copies": "token ids in on the compute stream; logits out on a side stream, "
                           "overlapping the next step; the timed region ends after the last"},
+        "value_graphed": {"value": value_graphed, "unit": "tokens/s",
+                          "ms_per_step": ms_graph / args.steps,
+                          "what": "the same step replayed from a CUDA graph, inputs resident "
+                                  "(value: eager calls with per-launch CUDA events, which the "
+                                  "rooflines use)"},
         "roofline": rooflines.get(dominant),
         "rooflines": rooflines,
         "attn_tflops": attn_flops / (attn_ms / 1e3) / 1e12 if attn_ms else None,
@@ -617,7 +639,7 @@ def bench_config2(args, world, rank, dev):
         line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
     if args.only:
         return line
-    del idx_dev, logits_host, copy_stream
+    del graphs, logits_host, copy_stream
     # the reference's op sequence on this GPU: the same model with eager attention and torch
     # (cuBLAS) projections, bit for bit the calls bdh.py's eval forward makes under autocast
     model.attn._attn_impl_override = "eager"
