@@ -675,8 +675,13 @@ def strong_scaling(model, args, world, rank, dev):
         g = torch.Generator().manual_seed(rank_seed(2102, rank))
         idx = torch.randint(0, VOCAB, (b, T), generator=g).to(dev)
         ms, prof, clk = time_config2(model, idx, args.steps, args.warmup, world, dev)
+        graph = model.graphed_forward(b, T)
+        ms_g = timed(lambda: graph(idx), args.steps, world, dev)
+        del graph
         out["config2"] = {"value": Bg * T * args.steps / (ms / 1e3), "unit": "tokens/s",
+                          "value_graphed": Bg * T * args.steps / (ms_g / 1e3),
                           "global_batch": Bg, "per_gpu_batch": b, "ms_per_step": ms / args.steps,
+                          "ms_per_step_graphed": ms_g / args.steps,
                           "kernel_ms_rank0": {k: v["ms"] / args.steps for k, v in prof.items()
                                               if v["launches"]},
                           "clocks": clk, "scaling": "strong"}
