@@ -7,6 +7,7 @@ random N(0, 0.02) weights, synthetic token ids uniform in [0, 256), B=32 x T=512
 (weak scaling: every rank runs its own batch; no collective on the data path).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--config 1|2|3|4|5] [--only]
+                    [--global-batch G]
 
 * ``value``      tokens/s over all ranks, inputs resident in HBM (device-timed, max over ranks)
 * ``e2e``        the same through the public model API with host buffers: pinned token ids
@@ -537,7 +538,14 @@ def time_config2(model, idx, steps: int, warmup: int, world: int, dev, native: b
 def bench_config2(args, world, rank, dev):
     from kernels import sm100_attn
 
-    B, T = args.batch or 32, 512
+    T = 512
+    strong = args.global_batch > 0
+    if strong:
+        if args.global_batch % world:
+            raise SystemExit(f"--global-batch {args.global_batch} is not a multiple of {world} GPUs")
+        B = args.global_batch // world
+    else:
+        B = args.batch or 32
     model = config2_model(dev)
     g = torch.Generator().manual_seed(rank_seed(2002, rank))
     idx_host = torch.randint(0, VOCAB, (B, T), generator=g).pin_memory()
@@ -608,12 +616,14 @@ def bench_config2(args, world, rank, dev):
         "metric": "BDH prefill tokens/s (config 2: 6L, D=256, nh=4, N=8192, B=32, T=512)",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
         "config": {"workload": "BDH prefill forward, bf16 autocast, random-init weights, "
                                "token ids uniform [0,256)",
                    "global_batch": B * world, "per_gpu_batch": B, "seq_len": T,
                    "n_layer": N_LAYER, "n_head": N_HEAD, "n_latent_per_head": N_LAT, "n_embd": D_MODEL,
-                   "parallelism": f"batch-sharded x{world} (weak), no collective on the data path",
+                   "parallelism": f"batch-sharded x{world} ({'strong' if strong else 'weak'}), "
+                                  "no collective on the data path",
                    "cache": "inputs larger than L2 (1 GB latent per layer per GPU); no flush"},
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": idx_host.numel() * 8,
                 "d2h_bytes_per_step": logits_host[0].numel() * 2,
@@ -1051,6 +1061,9 @@ def main():
                     help="config 4 with the N x D recurrent-state cache instead of the history")
     ap.add_argument("--batch", type=int, default=0,
                     help="per-GPU batch override (profiling aid; defaults: the config's own)")
+    ap.add_argument("--global-batch", type=int, default=0,
+                    help="config 2: shard this many sequences over the GPUs (strong scaling) "
+                         "instead of 32 per GPU (weak scaling, the default)")
     ap.add_argument("--only", action="store_true",
                     help="config 2: the headline line alone (no other configs, eager baseline "
                          "or strong-scaling objects)")
