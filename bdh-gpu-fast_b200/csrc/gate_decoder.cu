@@ -32,7 +32,6 @@
 // into `split` equal ranges run by different pairs; each writes its fp32 decoder sums, and a
 // second kernel adds the ranges in order and rounds once to bf16 (deterministic).
 #include <algorithm>
-#include <cstdlib>
 #include <string>
 
 #include "bdh_sm100.h"
@@ -66,7 +65,6 @@ struct GateDecParams {
   int B, T, H, N;
   int tb_n, tbp_n, nb_n;  // 128-row blocks, row-block pairs per batch; 128-column blocks per head
   int split, jper;        // latent ranges per row pair and blocks per range (split divides H nb_n)
-  int walk_step;          // unsplit: row pair r starts its latent walk at block r * walk_step
   float* part;            // split > 1: fp32 sums [split][B][tbp_n * 256][256]
   int* err;
 };
@@ -134,17 +132,13 @@ __device__ __forceinline__ void epi_bar_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(32 * kGdEpiWarps) : "memory");
 }
 
-// Latent block (h * nb_n + nb) visited at step j of an item's walk. Unsplit row pairs start
-// their walks at different blocks (row pair r at block r * J / rows, then around), so that the
-// pairs running at one time read different encoder_v / decoder weight blocks instead of all
-// requesting the same L2 lines together; each row's decoder sum is then taken in that rotated
-// order (fixed per row pair, so the result is deterministic). A split walk (few rows) keeps the
-// ascending order inside each range.
-__device__ __forceinline__ int gd_walk(const GateDecParams& p, int item, int j, int J) {
-  if (p.split > 1 || p.walk_step == 0) return j;
-  int jj = j + (item * p.walk_step) % J;
-  return jj >= J ? jj - J : jj;
-}
+// Latent block (h * nb_n + nb) visited at step j of an item's walk: every item walks the blocks
+// in order, so the decoder sums run over the latent index in ascending order, as a single-pass
+// GEMM over K = H N does (measured: bit-identical to cuBLAS's bf16 GEMM on the config-2
+// shapes). Starting the walks of different items at different blocks, so that concurrent pairs
+// read different weight blocks, changes the summation order and was measured no faster inside
+// the config-2 step (2.71-2.75 ms of gate + decoder per 6-layer step, against 2.68-2.70).
+__device__ __forceinline__ int gd_walk(const GateDecParams&, int, int j, int) { return j; }
 
 template <int ES, int DS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGdThreads, 1)
@@ -644,15 +638,6 @@ int launch_latent_gate_dec(const GateDecArgs& a, cudaStream_t stream, int* err) 
     split = 1;  // no room for the range sums: one range per row pair
   prm.split = split;
   prm.jper = static_cast<int>(a.H) * prm.nb_n / split;
-  {
-    const int J = static_cast<int>(a.H) * prm.nb_n;
-    const int conc = std::max(1, std::min(rows, cap));  // row pairs running at one time
-    static const bool rotate = [] {  // BDH_SM100_GATE_WALK=0: every row pair walks in order
-      const char* e = std::getenv("BDH_SM100_GATE_WALK");
-      return !(e != nullptr && std::atoi(e) == 0);
-    }();
-    prm.walk_step = (split == 1 && rotate) ? std::max(1, J / conc) : 0;
-  }
   prm.part = split > 1 ? static_cast<float*>(a.workspace) : nullptr;
   const int nitems = rows * split;
   const int pairs = std::min(nitems, cap);
