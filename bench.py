@@ -550,20 +550,29 @@ def bench_config2(args, world, rank, dev):
     g = torch.Generator().manual_seed(rank_seed(2002, rank))
     idx_host = torch.randint(0, VOCAB, (B, T), generator=g).pin_memory()
     idx = idx_host.to(dev)
-    ms, prof, clk = time_config2(model, idx, args.steps, args.warmup, world, dev)
+    # eager calls with a CUDA event pair around every library launch: the per-kernel device
+    # times the rooflines use (the events and the per-launch host work slow the step itself)
+    ms_ev, prof, clk_ev = time_config2(model, idx, args.steps, args.warmup, world, dev)
     assert sm100_attn.device_error(dev) == 0
-    value = world * B * T * args.steps / (ms / 1e3)
+    value_eager = world * B * T * args.steps / (ms_ev / 1e3)
 
-    # the same step replayed from CUDA graphs (the public bdh_model.GraphedForward: launches
-    # and their host work paid once, at capture); two captures so that one step's logits can be
-    # copied out while the other graph runs the next step
+    # `value`: the same step replayed from CUDA graphs (the public bdh_model.GraphedForward:
+    # launches and their host work paid once, at capture), inputs resident; two captures so that
+    # one step's logits can be copied out while the other graph runs the next step (e2e below)
     graphs = [model.graphed_forward(B, T) for _ in range(2)]
 
     def graph_step_n():
         graphs[0](idx)
 
-    ms_graph = timed(graph_step_n, args.steps, world, dev)
-    value_graphed = world * B * T * args.steps / (ms_graph / 1e3)
+    for _ in range(args.warmup):
+        graph_step_n()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(dev)
+    clocks.start()
+    ms = timed(graph_step_n, args.steps, world, dev)
+    clk = clocks.stop()
+    assert sm100_attn.device_error(dev) == 0
+    value = world * B * T * args.steps / (ms / 1e3)
 
     # end to end through the public API with host buffers: every step copies its token ids in
     # from pinned memory (into the graph's input buffer) and its bf16 logits out to pinned
@@ -607,7 +616,7 @@ def bench_config2(args, world, rank, dev):
     torch.cuda.synchronize(dev)
     e2e = world * B * T * args.steps / (ms_e2e / 1e3)
 
-    rooflines = config2_rooflines(prof, B, T, args.steps, ms)
+    rooflines = config2_rooflines(prof, B, T, args.steps, ms_ev)
     dominant = max(rooflines, key=lambda k: rooflines[k]["ms_per_step"]) if rooflines else None
     attn_ms = sum(prof[k]["ms"] for k in ("score", "value", "rope"))
     attn_flops = N_LAYER * args.steps * B * N_HEAD * T * (T - 1) * (N_LAT + D_MODEL)
@@ -630,15 +639,16 @@ def bench_config2(args, world, rank, dev):
                 "api": "bdh_model.BDH.graphed_forward (the step captured as a CUDA graph)",
                 "copies": "token ids in on the compute stream; logits out on a side stream, "
                           "overlapping the next step; the timed region ends after the last"},
-        "value_graphed": {"value": value_graphed, "unit": "tokens/s",
-                          "ms_per_step": ms_graph / args.steps,
-                          "what": "the same step replayed from a CUDA graph, inputs resident "
-                                  "(value: eager calls with per-launch CUDA events, which the "
-                                  "rooflines use)"},
+        "timing": "value: the step replayed from a CUDA graph (BDH.graphed_forward), inputs "
+                  "resident, CUDA events over the K steps; value_eager: the same step as eager "
+                  "calls with an event pair around every library launch, the per-kernel times "
+                  "that roofline, rooflines and kernel_ms come from",
+        "value_eager": {"value": value_eager, "unit": "tokens/s",
+                        "ms_per_step": ms_ev / args.steps, "clocks": clk_ev},
         "roofline": rooflines.get(dominant),
         "rooflines": rooflines,
         "attn_tflops": attn_flops / (attn_ms / 1e3) / 1e12 if attn_ms else None,
-        "attn_share_of_step": attn_ms / ms if ms else None,
+        "attn_share_of_step": attn_ms / ms_ev if ms_ev else None,
         "kernel_ms": {k: v["ms"] / args.steps for k, v in prof.items() if v["launches"]},
         "gpu_launches": launches,
         "clocks": clk,
@@ -684,17 +694,26 @@ def strong_scaling(model, args, world, rank, dev):
         b = Bg // world
         g = torch.Generator().manual_seed(rank_seed(2102, rank))
         idx = torch.randint(0, VOCAB, (b, T), generator=g).to(dev)
-        ms, prof, clk = time_config2(model, idx, args.steps, args.warmup, world, dev)
+        ms_ev, prof, clk_ev = time_config2(model, idx, args.steps, args.warmup, world, dev)
         graph = model.graphed_forward(b, T)
+        for _ in range(args.warmup):
+            graph(idx)
+        torch.cuda.synchronize(dev)
+        clocks = ClockSampler(dev)
+        clocks.start()
         ms_g = timed(lambda: graph(idx), args.steps, world, dev)
+        clk = clocks.stop()
         del graph
-        out["config2"] = {"value": Bg * T * args.steps / (ms / 1e3), "unit": "tokens/s",
-                          "value_graphed": Bg * T * args.steps / (ms_g / 1e3),
-                          "global_batch": Bg, "per_gpu_batch": b, "ms_per_step": ms / args.steps,
-                          "ms_per_step_graphed": ms_g / args.steps,
+        out["config2"] = {"value": Bg * T * args.steps / (ms_g / 1e3), "unit": "tokens/s",
+                          "global_batch": Bg, "per_gpu_batch": b,
+                          "ms_per_step": ms_g / args.steps, "clocks": clk,
+                          "value_eager": Bg * T * args.steps / (ms_ev / 1e3),
+                          "ms_per_step_eager": ms_ev / args.steps, "clocks_eager": clk_ev,
                           "kernel_ms_rank0": {k: v["ms"] / args.steps for k, v in prof.items()
                                               if v["launches"]},
-                          "clocks": clk, "scaling": "strong"}
+                          "timing": "value: CUDA-graph replay of the step; value_eager and "
+                                    "kernel_ms_rank0: eager calls with per-launch events",
+                          "scaling": "strong"}
     if 16 % world == 0:
         sub = argparse.Namespace(**vars(args))
         sub.config, sub.batch, sub.no_cpu_baseline = 5, 16 // world, True
