@@ -1,4 +1,5 @@
-"""Build recipe for libbdh_sm100.so (the C-ABI library of the sm_100a kernels).
+"""Build recipe for libbdh_sm100.so (the C-ABI library of the sm_100a kernels) and for
+bdh_sm100_ext.so (the PyTorch extension that binds it under the reference module's names).
 
 Plain nvcc, no torch extension machinery: every .cu / .cpp under csrc/ is compiled for
 sm_100a (-gencode arch=compute_100a,code=sm_100a) with -lineinfo, linked with a static CUDA
@@ -87,7 +88,8 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         sys.stderr.write("\n".join(logs))
         raise RuntimeError(f"nvcc failed on {', '.join(failed)}")
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc, *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *objs]
+    cmd = [nvcc, *ARCH, "-shared", "-cudart", "static", "-Xlinker", f"-soname={LIB.name}", "-o",
+           str(tmp), *objs]
     r = subprocess.run(cmd, capture_output=True, text=True)
     logs.append(f"$ {' '.join(cmd)}\n{r.stdout}{r.stderr}")
     if r.returncode != 0:
@@ -100,6 +102,43 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
+EXT_SRC = HERE / "ext" / "bdh_sm100_ext.cpp"
+EXT_BUILD = BUILD / "ext"
+EXT = HERE / "bdh_sm100_ext.so"
+
+
+def ext_up_to_date() -> bool:
+    if not EXT.exists():
+        return False
+    t = EXT.stat().st_mtime
+    return all(p.stat().st_mtime <= t for p in (EXT_SRC, *sorted(INCLUDE.glob("*.h"))))
+
+
+def build_ext(force: bool = False, verbose: bool = False) -> Path:
+    """Compile ext/bdh_sm100_ext.cpp (the PyTorch extension over the C-ABI, linked against
+    libbdh_sm100.so through an $ORIGIN run path) into bdh_sm100_ext.so next to this file."""
+    if not force and ext_up_to_date():
+        return EXT
+    if not LIB.exists():
+        build()
+    from torch.utils import cpp_extension
+
+    EXT_BUILD.mkdir(parents=True, exist_ok=True)
+    cpp_extension.load(
+        name="bdh_sm100_ext", sources=[str(EXT_SRC)], extra_include_paths=[str(INCLUDE)],
+        extra_cflags=["-O2"],
+        # "$ORIGIN" escaped for ninja ($$) and the shell (\\$): the run path stays literal
+        extra_ldflags=[f"-L{HERE}", "-lbdh_sm100", "-Wl,-rpath,\\$$ORIGIN:\\$$ORIGIN/../.."],
+        build_directory=str(EXT_BUILD), with_cuda=True, verbose=verbose, is_python_module=True)
+    built = EXT_BUILD / "bdh_sm100_ext.so"
+    tmp = EXT.with_suffix(".so.tmp")
+    shutil.copy2(built, tmp)
+    os.replace(tmp, EXT)
+    return EXT
+
+
 if __name__ == "__main__":
     build(force="--force" in sys.argv, verbose="-v" in sys.argv)
     print(LIB)
+    if "--ext" in sys.argv:
+        print(build_ext(force="--force" in sys.argv, verbose="-v" in sys.argv))

@@ -5,9 +5,13 @@ Same public names as the reference module (``kernels/cuda_attn.py``: ``tril_scor
 ``has_cuda_kernel`` / ``ext_status`` :91-100, :505-513, the tile pickers :134-290), so callers
 written against it import this module unchanged. Differences on purpose:
 
-* ``tril_score_v`` / ``tril_decode`` run the B200 kernels (``kernels.sm100_attn``) and never
-  fall back: CPU tensors or a missing library raise instead of silently returning the
-  reference's CPU result (``cuda_attn.py:401-409``);
+* ``tril_score_v`` / ``tril_decode`` run the B200 kernels through ``bdh_sm100_ext`` (the
+  PyTorch extension with the reference module's names, ``kernels.sm100_ext``) as the reference
+  calls ``bdh_cuda_ext`` (``import bdh_cuda_ext as _ext``, :85), or through the ctypes binding
+  of the same library (``kernels.sm100_attn``) when the extension is not built. They never fall
+  back: CPU tensors or a missing library raise instead of silently returning the reference's
+  CPU result (``cuda_attn.py:401-409``). Shapes are checked first, with the reference's
+  ValueError messages (:103-131);
 * the ``*_tiled_ref`` CPU mirrors of the reference's CUDA tiling compute the same values as the
   plain references and are kept as aliases;
 * the tile pickers describe this library's fixed tcgen05 tiles (128-row query blocks, 128/256-key
@@ -19,6 +23,7 @@ from __future__ import annotations
 import torch
 
 from . import sm100_attn as _sm
+from . import sm100_ext as _sx
 
 CUDA_TILE_M = 128
 CUDA_TILE_N = 128
@@ -30,15 +35,18 @@ CUDA_DECODE_TILE_N_MAX = 128
 
 
 def has_cuda_ext() -> bool:
-    return _sm.has_cuda_ext()
+    """True if the native path imports (the extension, else the library through ctypes)."""
+    return _sx.try_load_ext() is not None or _sm.has_cuda_ext()
 
 
 def has_cuda_kernel() -> bool:
-    return _sm.has_cuda_kernel()
+    return has_cuda_ext() and torch.cuda.is_available()
 
 
 def ext_status() -> str:
-    return _sm.ext_status()
+    ext = _sx.try_load_ext()
+    binding = "bdh_sm100_ext" if ext is not None else f"ctypes (bdh_sm100_ext: {_sx.ext_error()!r})"
+    return f"{_sm.ext_status()} binding={binding}"
 
 
 def pick_cuda_cold_tiles(T: int, Dk: int, *args, **kwargs):
@@ -65,6 +73,10 @@ def tril_score_v_tiled_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
 
 def tril_score_v(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     """``(q @ k.mT).tril(-1) @ v`` on the sm_100a tensor cores (CUDA tensors only)."""
+    _sm._check_cold_shapes(q, k, v)
+    ext = _sx.try_load_ext()
+    if ext is not None:
+        return ext.tril_score_v(q, k, v)
     return _sm.tril_score_v(q, k, v)
 
 
@@ -84,4 +96,8 @@ def tril_decode_tiled_ref(q: torch.Tensor, k_past: torch.Tensor, v_past: torch.T
 
 def tril_decode(q: torch.Tensor, k_past: torch.Tensor, v_past: torch.Tensor) -> torch.Tensor:
     """``(q @ k_past.mT) @ v_past`` streaming the cache on the GPU (CUDA tensors only)."""
+    _sm._check_decode_shapes(q, k_past, v_past)
+    ext = _sx.try_load_ext()
+    if ext is not None:
+        return ext.tril_decode(q, k_past, v_past)
     return _sm.tril_decode(q, k_past, v_past)
