@@ -275,9 +275,12 @@ class BDH(nn.Module):
         per config-2 step for a second K = 256 GEMM in the gate and measures slower on one
         B200 (1.68M vs 1.74M tokens/s: the gate becomes tensor-bound under the power cap), so
         the default stores xs."""
-        from kernels.sm100_attn import (latent_encode, latent_gate, latent_gate_dec,
-                                        latent_gate_x, layer_norm, residual_layer_norm,
-                                        tril_score_v)
+        from kernels.sm100_attn import latent_gate, latent_gate_x
+        from kernels.sm100_ext import model_ops
+
+        ops = model_ops()  # the torch extension when built, else the ctypes binding
+        latent_encode, latent_gate_dec, layer_norm = ops.latent_encode, ops.latent_gate_dec, ops.layer_norm
+        residual_layer_norm, tril_score_v = ops.residual_layer_norm, ops.tril_score_v
 
         B, T, _ = x.shape
         nh = self.config.n_head

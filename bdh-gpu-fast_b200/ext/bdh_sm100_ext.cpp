@@ -21,8 +21,11 @@
 #include <torch/extension.h>
 
 #include <cstdint>
+#include <mutex>
 #include <optional>
 #include <string>
+#include <tuple>
+#include <vector>
 
 #include "bdh_sm100.h"
 
@@ -302,6 +305,193 @@ std::tuple<at::Tensor, std::optional<at::Tensor>, at::Tensor> tril_score_v_bwd(
   return {dq, dk, dv};
 }
 
+// ------------------------------------------------------------ fused layer (model path)
+// The same checks and C-ABI calls as kernels/sm100_attn.py's latent_encode, latent_gate_dec,
+// layer_norm and residual_layer_norm (bf16 latents with a contiguous last dimension, 16-byte
+// aligned bases, strides in multiples of 8 elements; weights d-contiguous or n-contiguous).
+void check_latent(const char* name, std::initializer_list<const at::Tensor*> ts) {
+  for (const at::Tensor* t : ts) {
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16,
+                std::string(name) + ": bf16 tensors required, got " + c10::toString(t->scalar_type()));
+    bool ok = t->stride(-1) == 1 && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0;
+    for (int64_t d = 0; ok && d + 1 < t->dim(); ++d)
+      if (t->size(d) > 1 && t->stride(d) % 8 != 0) ok = false;
+    TORCH_CHECK(ok, std::string(name) +
+                        ": tensors need a contiguous last dim, 16-byte aligned base and strides "
+                        "that are multiples of 8 elements");
+  }
+}
+
+void check_weight(const char* name, const at::Tensor& w) {
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16,
+              std::string(name) + ": bf16 weights required, got " + c10::toString(w.scalar_type()));
+  const bool k_major = w.stride(1) == 1 && w.stride(2) != 1 && w.stride(0) % 8 == 0 && w.stride(2) % 8 == 0;
+  if (!k_major) {
+    check_latent(name, {&w});
+  } else {
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
+                std::string(name) + ": weights need a 16-byte aligned base");
+  }
+}
+
+// Element strides for the C-ABI: a size-1 dimension is never stepped, so an odd stride there
+// becomes a legal 8.
+template <int R>
+struct StridesN {
+  int64_t s[R];
+  explicit StridesN(const at::Tensor& t) {
+    for (int i = 0; i < R; ++i) {
+      const int64_t st = t.stride(i);
+      s[i] = (t.size(i) > 1 || st % 8 == 0 || st == 1) ? st : 8;
+    }
+    s[R - 1] = t.stride(R - 1);
+  }
+};
+
+// freqs[2p] == freqs[2p + 1] (BDH's get_freqs): the fused encode shares one (cos, sin) per
+// pair. Checked once per freqs tensor version (the check reads the tensor back).
+bool paired_freqs(const at::Tensor& f) {
+  static std::mutex mu;
+  static std::vector<std::tuple<const void*, int64_t, int64_t, bool>> seen;
+  const auto key = std::make_tuple(f.data_ptr(), static_cast<int64_t>(f._version()), f.numel());
+  {
+    std::lock_guard<std::mutex> g(mu);
+    for (const auto& e : seen)
+      if (std::get<0>(e) == std::get<0>(key) && std::get<1>(e) == std::get<1>(key) &&
+          std::get<2>(e) == std::get<2>(key))
+        return std::get<3>(e);
+  }
+  const bool ok = at::equal(f.slice(0, 0, f.numel(), 2), f.slice(0, 1, f.numel(), 2));
+  std::lock_guard<std::mutex> g(mu);
+  if (seen.size() > 64) seen.clear();
+  seen.emplace_back(std::get<0>(key), std::get<1>(key), std::get<2>(key), ok);
+  return ok;
+}
+
+// xs = relu(x enc) (B,T,H,N) and qr = RoPE(xs) (B,H,T,N) at positions pos0.., bf16.
+std::tuple<std::optional<at::Tensor>, at::Tensor> latent_encode(
+    const at::Tensor& x, const at::Tensor& enc, const at::Tensor& freqs, int64_t pos0,
+    std::optional<at::Tensor> xs_out, std::optional<at::Tensor> qr_out, bool want_xs) {
+  TORCH_CHECK(x.dim() == 3 && enc.dim() == 3 && x.size(2) == enc.size(1),
+              "latent_encode expects x (B,T,D) and enc (H,D,N)");
+  require_cuda({&x, &enc, &freqs});
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t B = x.size(0), T = x.size(1), D = x.size(2), H = enc.size(0), N = enc.size(2);
+  const at::Tensor f = freqs_vector(freqs, N);
+  TORCH_CHECK(paired_freqs(f), "latent_encode requires paired frequencies (freqs[2p] == freqs[2p+1])");
+  std::optional<at::Tensor> xs = xs_out;
+  if (!xs.has_value() && want_xs) xs = at::empty({B, T, H, N}, x.options().dtype(at::kBFloat16));
+  at::Tensor qr = qr_out.has_value() ? *qr_out : at::empty({B, H, T, N}, x.options().dtype(at::kBFloat16));
+  TORCH_CHECK((!xs.has_value() || xs->sizes() == at::IntArrayRef({B, T, H, N})) &&
+                  qr.sizes() == at::IntArrayRef({B, H, T, N}),
+              "latent_encode: xs_out must be (B,T,H,N) and qr_out (B,H,T,N)");
+  if (xs.has_value())
+    check_latent("latent_encode", {&x, &*xs, &qr});
+  else
+    check_latent("latent_encode", {&x, &qr});
+  check_weight("latent_encode", enc);
+  const StridesN<3> sx(x), se(enc);
+  const StridesN<4> sq(qr);
+  std::optional<StridesN<4>> sxs;
+  if (xs.has_value()) sxs.emplace(*xs);
+  check_rc(bdh_latent_encode(x.data_ptr(), sx.s, enc.data_ptr(), se.s,
+                             xs.has_value() ? xs->data_ptr() : nullptr, sxs ? sxs->s : nullptr,
+                             qr.data_ptr(), sq.s, f.data_ptr<float>(), B, T, H, D, N, pos0,
+                             stream_of(x)),
+           "latent_encode");
+  return {xs, qr};
+}
+
+// (xs * relu(y encv)) dec in one kernel: y (B,H,T,D), encv (H,D,N) d-contiguous, xs (B,T,H,N),
+// dec (H*N, D) latent-contiguous; D = 256, N a multiple of 128. Returns (B,T,D) bf16.
+at::Tensor latent_gate_dec(const at::Tensor& y, const at::Tensor& encv, const at::Tensor& xs,
+                           const at::Tensor& dec, std::optional<at::Tensor> out_opt) {
+  TORCH_CHECK(y.dim() == 4 && encv.dim() == 3 && xs.dim() == 4 && dec.dim() == 2,
+              "latent_gate_dec expects y (B,H,T,D), encv (H,D,N), xs (B,T,H,N), dec (H*N,D)");
+  require_cuda({&y, &encv, &xs, &dec});
+  const c10::cuda::CUDAGuard guard(y.device());
+  const int64_t B = y.size(0), H = y.size(1), T = y.size(2), D = y.size(3), N = encv.size(2);
+  TORCH_CHECK(xs.sizes() == at::IntArrayRef({B, T, H, N}) && encv.sizes() == at::IntArrayRef({H, D, N}) &&
+                  dec.sizes() == at::IntArrayRef({H * N, D}),
+              "latent_gate_dec: shapes of y, encv, xs and dec disagree");
+  TORCH_CHECK(D == 256 && N % 128 == 0, "latent_gate_dec: needs D = 256 and N a multiple of 128");
+  TORCH_CHECK(dec.scalar_type() == at::kBFloat16 && encv.scalar_type() == at::kBFloat16,
+              "latent_gate_dec: bf16 weights required");
+  at::Tensor out = out_opt.has_value() ? *out_opt : at::empty({B, T, D}, y.options().dtype(at::kBFloat16));
+  TORCH_CHECK(out.sizes() == at::IntArrayRef({B, T, D}), "latent_gate_dec: out must be (B,T,D)");
+  check_latent("latent_gate_dec", {&y, &xs, &out});
+  check_weight("latent_gate_dec", encv);
+  const size_t wsz = bdh_latent_gate_dec_workspace_size(B, T, H, D, N);
+  at::Tensor ws;
+  if (wsz > 0) ws = at::empty({static_cast<int64_t>(wsz)}, y.options().dtype(at::kByte));
+  const StridesN<4> sy(y), sxs(xs);
+  const StridesN<3> sev(encv), so(out);
+  const StridesN<2> sd(dec);
+  check_rc(bdh_latent_gate_dec_ws(y.data_ptr(), sy.s, encv.data_ptr(), sev.s, xs.data_ptr(), sxs.s,
+                                  dec.data_ptr(), sd.s, out.data_ptr(), so.s, B, T, H, D, N,
+                                  wsz > 0 ? ws.data_ptr() : nullptr, wsz, stream_of(y)),
+           "latent_gate_dec");
+  return out;
+}
+
+// (rows, D) with one row stride for the LayerNorm entries: a view when the leading dimensions
+// flatten to one, else nullopt.
+std::optional<at::Tensor> rows_view(const at::Tensor& t) {
+  if (t.stride(-1) != 1) return std::nullopt;
+  try {
+    return t.view({-1, t.size(-1)});
+  } catch (const c10::Error&) {
+    return std::nullopt;
+  }
+}
+
+int64_t row_stride(const at::Tensor& v) { return v.size(0) > 1 ? v.stride(0) : v.size(1); }
+
+// Affine-free LayerNorm over the last dim, fp32 math, stored in out_dtype (default x's dtype).
+at::Tensor layer_norm(const at::Tensor& x, double eps, std::optional<at::ScalarType> out_dtype,
+                      std::optional<at::Tensor> out_opt) {
+  require_cuda({&x});
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t D = x.size(-1);
+  std::optional<at::Tensor> xv = rows_view(x);
+  if (!xv.has_value()) xv = x.contiguous().view({-1, D});
+  at::Tensor out = out_opt.has_value() ? *out_opt
+                                       : at::empty(x.sizes(), x.options().dtype(out_dtype.value_or(x.scalar_type())));
+  std::optional<at::Tensor> ov = rows_view(out);
+  TORCH_CHECK(ov.has_value() && ov->size(0) == xv->size(0),
+              "layer_norm: out must be row-contiguous with x's shape");
+  check_rc(bdh_layernorm(xv->data_ptr(), dtype_code(*xv), row_stride(*xv), ov->data_ptr(),
+                         dtype_code(*ov), row_stride(*ov), xv->size(0), D, static_cast<float>(eps),
+                         stream_of(x)),
+           "layer_norm");
+  return out;
+}
+
+// LN(x + LN(y)) over the last dim (BDH._residual_ln): x fp32, y fp32 or bf16. Returns the
+// fp32 result and, with want_bf16, its bf16 copy.
+std::tuple<at::Tensor, std::optional<at::Tensor>> residual_layer_norm(const at::Tensor& x,
+                                                                      const at::Tensor& y,
+                                                                      double eps, bool want_bf16) {
+  TORCH_CHECK(x.scalar_type() == at::kFloat && x.sizes() == y.sizes(),
+              "residual_layer_norm: x must be fp32 and y of x's shape");
+  require_cuda({&x, &y});
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t D = x.size(-1);
+  std::optional<at::Tensor> xv = rows_view(x);
+  if (!xv.has_value()) xv = x.contiguous().view({-1, D});
+  std::optional<at::Tensor> yv = rows_view(y);
+  if (!yv.has_value()) yv = y.contiguous().view({-1, D});
+  at::Tensor out = at::empty(x.sizes(), x.options());
+  std::optional<at::Tensor> out16;
+  if (want_bf16) out16 = at::empty(x.sizes(), x.options().dtype(at::kBFloat16));
+  check_rc(bdh_residual_layernorm(xv->data_ptr<float>(), row_stride(*xv), yv->data_ptr(),
+                                  dtype_code(*yv), row_stride(*yv), out.data_ptr<float>(), D,
+                                  out16.has_value() ? out16->data_ptr() : nullptr, D, xv->size(0), D,
+                                  static_cast<float>(eps), stream_of(x)),
+           "residual_layer_norm");
+  return {out, out16};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -327,6 +517,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "decode step with the new query RoPE-rotated to positions pos.. (and written to kr_slot)",
         py::arg("q_new"), py::arg("freqs"), py::arg("pos"), py::arg("kr_past"), py::arg("v_past"),
         py::arg("kr_slot") = py::none());
+  m.def("latent_encode", &latent_encode,
+        "(xs, qr): xs = relu(x @ enc) (B,T,H,N), qr = RoPE(xs) (B,H,T,N) at positions pos0.., bf16",
+        py::arg("x"), py::arg("enc"), py::arg("freqs"), py::arg("pos0") = 0,
+        py::arg("xs_out") = py::none(), py::arg("qr_out") = py::none(), py::arg("want_xs") = true);
+  m.def("latent_gate_dec", &latent_gate_dec, "(xs * relu(y @ encv)) @ dec in one kernel, (B,T,D) bf16",
+        py::arg("y"), py::arg("encv"), py::arg("xs"), py::arg("dec"), py::arg("out") = py::none());
+  m.def("layer_norm", &layer_norm, "affine-free LayerNorm over the last dim (fp32 math)",
+        py::arg("x"), py::arg("eps") = 1e-5, py::arg("out_dtype") = py::none(),
+        py::arg("out") = py::none());
+  m.def("residual_layer_norm", &residual_layer_norm,
+        "(LN(x + LN(y)), its bf16 copy or None): the BDH layer's residual double LayerNorm",
+        py::arg("x"), py::arg("y"), py::arg("eps") = 1e-5, py::arg("want_bf16") = false);
   m.def("abi_version", &bdh_abi_version, "ABI version of the loaded libbdh_sm100.so");
   m.attr("has_cuda") = true;
 }

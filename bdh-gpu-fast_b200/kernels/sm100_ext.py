@@ -1,7 +1,8 @@
 """Loader of ``bdh_sm100_ext``: the PyTorch extension that binds libbdh_sm100.so under the names
 of the reference's native module ``bdh_cuda_ext`` (csrc/tril_attn_bind.cpp:25-40:
 ``tril_score_v``, ``tril_decode``, ``has_cuda``), plus ``tril_score_v_bwd``, ``rope_rotate``,
-``rope_tril_score_v`` and ``rope_tril_decode``.
+``rope_tril_score_v``, ``rope_tril_decode`` and the fused layer's ``latent_encode``,
+``latent_gate_dec``, ``layer_norm`` and ``residual_layer_norm``.
 
 The extension is a C++ module built in-tree next to the library
 (``python bdh-gpu-fast_b200/build_lib.py --ext``; ``__graft_entry__.build()`` does it). It calls
@@ -53,6 +54,9 @@ def load_ext() -> ModuleType:
 
 
 def try_load_ext() -> Optional[ModuleType]:
+    """The extension, or None when it is not built or failed to load (remembered: not retried)."""
+    if _ext is None and _ext_error is not None:
+        return None
     try:
         return load_ext()
     except BaseException:  # noqa: BLE001
@@ -61,3 +65,18 @@ def try_load_ext() -> Optional[ModuleType]:
 
 def ext_error() -> Optional[BaseException]:
     return _ext_error
+
+
+def model_ops() -> ModuleType:
+    """The fused layer's library entries (``latent_encode``, ``tril_score_v``, ``layer_norm``,
+    ``latent_gate_dec``, ``residual_layer_norm``, same signatures): from the extension when it is
+    built and ``BDH_SM100_EXT`` is not ``0``, else the ctypes binding. Both call the same C-ABI
+    entries with the same arguments (the same bits); the extension costs less host time per
+    call, which is what an eager step of the model spends between its kernels."""
+    import os
+
+    if os.environ.get("BDH_SM100_EXT", "1") != "0":
+        ext = try_load_ext()
+        if ext is not None:
+            return ext
+    return sm100_attn

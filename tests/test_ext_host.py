@@ -66,3 +66,18 @@ def test_cuda_attn_keeps_the_reference_value_errors(ext):
     with pytest.raises(ValueError, match="v_past heads must equal q heads or 1"):
         cuda_attn.tril_decode(z(1, 2, 1, 8), z(1, 2, 3, 8), z(1, 3, 3, 4))
     assert "binding=bdh_sm100_ext" in cuda_attn.ext_status()
+
+
+def test_fused_layer_ops_exported_and_checked(ext):
+    for name in ("latent_encode", "latent_gate_dec", "layer_norm", "residual_layer_norm"):
+        assert callable(getattr(ext, name)), name
+    z = torch.zeros
+    with pytest.raises(RuntimeError, match="latent_encode expects x"):
+        ext.latent_encode(z(2, 8, 16), z(4, 32, 64), z(64))
+    with pytest.raises(RuntimeError, match="requires CUDA tensors"):
+        ext.latent_gate_dec(z(1, 4, 8, 256), z(4, 256, 128), z(1, 8, 4, 128), z(512, 256))
+    with pytest.raises(RuntimeError, match="x must be fp32"):
+        ext.residual_layer_norm(z(4, 8).bfloat16(), z(4, 8))
+    from kernels import sm100_ext
+
+    assert sm100_ext.model_ops() is ext

@@ -168,3 +168,52 @@ def test_extension_calls_capture_in_a_cuda_graph(ext):
     torch.cuda.synchronize()
     assert torch.equal(out, eager)
     assert sa().device_error() == 0
+
+
+def test_fused_layer_ops_same_bits_as_ctypes(ext):
+    """latent_encode, latent_gate_dec, layer_norm and residual_layer_norm through the extension
+    against the ctypes binding on config-2 layer shapes (B = 2, T = 256)."""
+    B, T, D, H, N = 2, 256, 256, 4, 8192
+    g = torch.Generator(device=DEV).manual_seed(21)
+    x = torch.randn(B, T, D, device=DEV, generator=g)
+    xb = x.bfloat16()
+    enc = sa().weight_k_major((0.02 * torch.randn(H, D, N, device=DEV, generator=g)).bfloat16())
+    encv = sa().weight_k_major((0.02 * torch.randn(H, D, N, device=DEV, generator=g)).bfloat16())
+    dec = sa().decoder_k_major((0.02 * torch.randn(H * N, D, device=DEV, generator=g)).bfloat16())
+    freqs = torch.tensor(O.get_freqs(N), device=DEV)
+    xs_a, qr_a = ext.latent_encode(xb, enc, freqs, 3)
+    xs_b, qr_b = sa().latent_encode(xb, enc, freqs, 3)
+    assert torch.equal(xs_a, xs_b) and torch.equal(qr_a, qr_b)
+    none, qr_c = ext.latent_encode(xb, enc, freqs, 3, want_xs=False)
+    assert none is None and torch.equal(qr_c, qr_b)
+    y = sa().tril_score_v(qr_a, qr_a, xb.unsqueeze(1), score_terms="bf16")
+    yn_a = ext.layer_norm(y, 1e-5, torch.bfloat16)
+    yn_b = sa().layer_norm(y, 1e-5, out_dtype=torch.bfloat16)
+    assert yn_a.dtype == torch.bfloat16 and torch.equal(yn_a, yn_b)
+    m_a = ext.latent_gate_dec(yn_a, encv, xs_a, dec)
+    m_b = sa().latent_gate_dec(yn_b, encv, xs_b, dec)
+    assert torch.equal(m_a, m_b)
+    r_a = ext.residual_layer_norm(x, m_a, 1e-5, True)
+    r_b = sa().residual_layer_norm(x, m_b, 1e-5, want_bf16=True)
+    assert torch.equal(r_a[0], r_b[0]) and torch.equal(r_a[1], r_b[1])
+    assert ext.residual_layer_norm(x, m_a, 1e-5, False)[1] is None
+    with pytest.raises(RuntimeError, match="paired frequencies"):
+        ext.latent_encode(xb, enc, torch.arange(N, device=DEV, dtype=torch.float32), 0)
+
+
+def test_model_logits_same_bits_through_either_binding(ext, monkeypatch):
+    """The fused model's bf16 forward with the layer ops through the extension (the default when
+    built) and through the ctypes binding (BDH_SM100_EXT=0): the same logits."""
+    import bdh_model
+
+    cfg = bdh_model.BDHConfig(n_layer=2, n_embd=256, n_head=4, mlp_internal_dim_multiplier=128,
+                              vocab_size=256, dropout=0.0)
+    torch.manual_seed(5)
+    m = bdh_model.BDH(cfg).to(DEV).eval()
+    m.attn._attn_impl_override = "cuda_sm100"
+    idx = torch.randint(0, 256, (4, 256), device=DEV)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        a = m(idx)[0]
+        monkeypatch.setenv("BDH_SM100_EXT", "0")
+        b = m(idx)[0]
+    assert torch.equal(a, b)
