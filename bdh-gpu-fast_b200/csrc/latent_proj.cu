@@ -579,9 +579,9 @@ struct GateXProb : ChunkedResidentWalkT<8> {
 
 // Pipeline forms. Default: weights resident per column block, chunked walk, six 16 KB
 // activation stages (Encode / Gate; EncodeK / GateK read d-contiguous weights K-major).
-// BDH_SM100_LATENT_VARIANT=1 selects the streamed-operand forms (both operands through the
-// stage ring; contiguous walk for encode, column-fastest strided walk for gate), kept for
-// measurement and used for D > 256.
+// The streamed-operand forms (both operands through the stage ring; contiguous walk for
+// encode, column-fastest strided walk for gate) serve D > 256, the encode of small batches
+// (encode_streamed) and BDH_SM100_LATENT_VARIANT=1.
 using Encode = EncodeProb<6, 1, 3>;
 using EncodeK = EncodeProb<6, 1, 3, true>;
 using EncodeS = EncodeProb<5, 1, 0>;
@@ -624,12 +624,26 @@ bool walk_rotate() {
   return on;
 }
 
+// BDH_SM100_LATENT_VARIANT: 1 forces the streamed-operand forms, 0 the resident-weight forms;
+// unset (-1): the encode picks by shape (encode_streamed).
 int latent_variant() {
   static int v = [] {
     const char* e = std::getenv("BDH_SM100_LATENT_VARIANT");
-    return e ? std::atoi(e) : 0;
+    return e ? std::atoi(e) : -1;
   }();
   return v;
+}
+
+// The encode streams both operands when the chunked walk would reload the resident weights
+// every few tiles: with fewer than 16 row blocks per chunk (a small batch, e.g. one rank's share
+// of a strongly scaled batch). Measured on B200 at config-2 layer shapes, per 6-layer step:
+// B = 4 0.46 against 0.56 ms, B = 8 0.78 against 0.84 ms; at B = 32 (32-row-block chunks) the
+// resident weights are faster.
+bool encode_streamed(int walk_chunk) {
+  const int v = latent_variant();
+  if (v == 1) return true;
+  if (v == 0) return false;
+  return walk_chunk < 16;
 }
 
 bool map_x_btd(CUtensorMap* m, const void* x, const int64_t s[3], int64_t B, int64_t T, int64_t D,
@@ -704,7 +718,7 @@ int launch_latent_encode(const LatentArgs& a, cudaStream_t stream, int* err) {
   const int64_t ntiles = a.B * a.H * int64_t(prm.tb_n) * prm.nb_n;
   const bool kw = weight_k_major(a.w_strides);
   const int nt = static_cast<int>(ntiles);
-  if (a.D > 256 || latent_variant() == 1) {  // resident weights hold D <= 256
+  if (a.D > 256 || encode_streamed(prm.walk_chunk)) {  // resident weights hold D <= 256
     if (!wx)
       return kw ? launch_tc<EncodeSQK::S, EncodeSQK>(prm, nt, stream, kProfEncode)
                 : launch_tc<EncodeSQ::S, EncodeSQ>(prm, nt, stream, kProfEncode);
