@@ -262,8 +262,9 @@ class BDH(nn.Module):
 
     def _layer_latent(self, x: torch.Tensor, xb: Optional[torch.Tensor], level: int,
                       rope_start: int, cache):
-        """One layer on the fused kernels: encode (+ReLU +RoPE) -> tril attention -> LN ->
-        encoder_v gate (xs * relu(.)) -> decoder -> residual double LN. Same arithmetic as the
+        """One layer on the fused kernels: encode (+ReLU +RoPE) -> tril attention with its LN in
+        the value pass's epilogue -> encoder_v gate (xs * relu(.)) -> decoder -> residual double
+        LN. Same arithmetic as the
         bf16-autocast layer of bdh.py:991-1052. With D = 256 and N a multiple of 128 the gate and
         the decoder product run as one kernel (``latent_gate_dec``, ``BDH_SM100_GATE_DEC=0``
         keeps the gate + cuBLAS decoder), so the (B, T, nh, N) xy latent is never stored. ``xb`` is the bf16 copy of ``x`` (made
@@ -279,7 +280,7 @@ class BDH(nn.Module):
         from kernels.sm100_ext import model_ops
 
         ops = model_ops()  # the torch extension when built, else the ctypes binding
-        latent_encode, latent_gate_dec, layer_norm = ops.latent_encode, ops.latent_gate_dec, ops.layer_norm
+        latent_encode, latent_gate_dec = ops.latent_encode, ops.latent_gate_dec
         residual_layer_norm, tril_score_v = ops.residual_layer_norm, ops.tril_score_v
 
         B, T, _ = x.shape
@@ -307,8 +308,8 @@ class BDH(nn.Module):
                 quantize_rows_fp8(qr, out=dst_kr, scale=cache.reserve_scale(level, T))
             else:
                 dst_kr.copy_(qr)
-        y_kv = tril_score_v(qr, qr, xb.unsqueeze(1))
-        yn = layer_norm(y_kv, eps, out_dtype=torch.bfloat16)
+        # the attention output's LayerNorm runs in the value pass's epilogue
+        yn = tril_score_v(qr, qr, xb.unsqueeze(1), ln_eps=eps)
         encv = self._bf16_param("encoder_v", kmaj)
         N = enc.size(-1)
         gate_dec = (not gate_x and kmaj and x.size(-1) == 256 and N % 128 == 0

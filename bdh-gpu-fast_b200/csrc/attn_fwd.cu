@@ -45,6 +45,7 @@ struct ValueProb {
     int64_t os_b, os_h, os_t;
     int out_f32;
     int vec_ok;
+    float ln_eps;          // ValueLnProb: the LayerNorm's eps
     int* err;
   };
   struct Tile {
@@ -123,6 +124,91 @@ struct ValueProb {
       }
     }
   }
+};
+
+// Value pass with the row LayerNorm of the attention output folded into the epilogue: the
+// reference's y = LN(bf16(P V)) of a BDH layer (bdh.py:1044 after kernels/attention.py:27-40,
+// the LayerNorm in fp32 under autocast, its result cast to bf16 by the next op). One thread owns
+// one output row (all D <= 256 columns in its TMEM lane), so the un-normalised output
+// never reaches HBM and no separate LayerNorm kernel runs. The row is read from TMEM three times
+// (a compact loop each; keeping it in registers, fully unrolled, measured slower). Statistics as
+// csrc/layernorm.cu computes them (fp32; mean, then the biased variance of the deviations;
+// rstd = 1 / sqrt(var + eps)), each summed in four interleaved partial sums.
+template <int STAGES, int AT>
+struct ValueLnProb : ValueProb<2, STAGES, AT> {
+  using Base = ValueProb<2, STAGES, AT>;
+  using S = typename Base::S;
+  using Params = typename Base::Params;
+  using Tile = typename Base::Tile;
+  static constexpr int kCustomEpilogue = 1;
+  struct EpiState {};
+  __device__ static void epilogue_begin(const Params&, int, int, uint8_t*, EpiState&, bool,
+                                        const Tile&) {}
+  __device__ static void epilogue_prefetch(const Params&, const Tile&, bool, const Tile&, int, int,
+                                           uint8_t*, EpiState&) {}
+  __device__ static bool epilogue_tile(const Params& p, const Tile& tl, int row, int,
+                                       uint32_t taddr, uint8_t*, EpiState&, volatile int*) {
+    const int D = p.D;  // <= S::BN (one D tile)
+    // pass 1: mean; pass 2: variance of the deviations; pass 3: normalise and store. Each pass
+    // reads the row from TMEM again (a compact loop); sums in four interleaved partial sums
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < D; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld32(taddr + static_cast<uint32_t>(c0), r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        const uint32_t p0 = cvt_bf16x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+        const uint32_t p1 = cvt_bf16x2(__uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
+        if (c0 + e < D) a0 += bf16x2_lo(p0);
+        if (c0 + e + 1 < D) a1 += bf16x2_hi(p0);
+        if (c0 + e + 2 < D) a2 += bf16x2_lo(p1);
+        if (c0 + e + 3 < D) a3 += bf16x2_hi(p1);
+      }
+    }
+    const float mean = ((a0 + a1) + (a2 + a3)) / static_cast<float>(D);
+    a0 = a1 = a2 = a3 = 0.0f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < D; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld32(taddr + static_cast<uint32_t>(c0), r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        const uint32_t p0 = cvt_bf16x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+        const uint32_t p1 = cvt_bf16x2(__uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
+        const float d0 = bf16x2_lo(p0) - mean, d1 = bf16x2_hi(p0) - mean;
+        const float d2 = bf16x2_lo(p1) - mean, d3 = bf16x2_hi(p1) - mean;
+        if (c0 + e < D) a0 = fmaf(d0, d0, a0);
+        if (c0 + e + 1 < D) a1 = fmaf(d1, d1, a1);
+        if (c0 + e + 2 < D) a2 = fmaf(d2, d2, a2);
+        if (c0 + e + 3 < D) a3 = fmaf(d3, d3, a3);
+      }
+    }
+    const float rstd = 1.0f / sqrtf(((a0 + a1) + (a2 + a3)) / static_cast<float>(D) + p.ln_eps);
+    // every lane of the warp takes part in each TMEM load (tcgen05.ld is warp-aligned); rows at
+    // or beyond T only skip the store
+    const bool row_ok = tl.mi * S::BM + row < p.T;
+    Tile t1 = tl;
+    t1.ni = 0;
+#pragma unroll 1
+    for (int c0 = 0; c0 < D; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld32(taddr + static_cast<uint32_t>(c0), r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        const uint32_t pr = cvt_bf16x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+        r[e] = __float_as_uint((bf16x2_lo(pr) - mean) * rstd);
+        r[e + 1] = __float_as_uint((bf16x2_hi(pr) - mean) * rstd);
+      }
+      if (row_ok) Base::epilogue(p, t1, row, c0, r);  // the output store of the plain value pass
+    }
+    return true;
+  }
+  __device__ static void epilogue_after(const Params&, const Tile&, int, int, uint8_t*, EpiState&) {}
+  __device__ static void epilogue_end(const Params&, int, int, uint8_t*, EpiState&) {}
 };
 
 // ----------------------------------------------------------------- launchers ----
@@ -247,6 +333,8 @@ int score_tile_n() {
 using ScoreTf32 = ScoreProb<4, 128, 3>;
 using ValueBf16 = ValueProb<2, 3>;
 using ValueBf16One = ValueProb<2, 4, 1>;
+using ValueLnBf16 = ValueLnProb<3, 2>;
+using ValueLnBf16One = ValueLnProb<4, 1>;
 using ValueTf32 = ValueProb<4, 3>;
 
 // One row of the fp32 score pair from its K-split partials: columns of the row's stored tiles
@@ -487,6 +575,20 @@ int launch_value(const FwdArgs& a, const void* p_hi, const void* p_lo, cudaStrea
   if (elem != 2 && p_lo == nullptr) {
     set_error("value pass: the fp32 path needs the tf32 hi/lo score pair");
     return BDH_ERR_INVALID;
+  }
+  if (elem == 2 && a.ln && a.D <= ValueLnBf16One::S::BN) {  // LayerNorm in the epilogue
+    if (p_lo == nullptr) {
+      ValueLnBf16One::Params prm{};
+      if (!fill(prm, ValueLnBf16One::S::BK, ValueLnBf16One::BN)) return BDH_ERR_INVALID;
+      prm.ln_eps = a.ln_eps;
+      return launch_tc<ValueLnBf16One::S, ValueLnBf16One>(prm, prm.units * prm.mt * prm.nd,
+                                                          stream, kProfValue);
+    }
+    ValueLnBf16::Params prm{};
+    if (!fill(prm, ValueLnBf16::S::BK, ValueLnBf16::BN)) return BDH_ERR_INVALID;
+    prm.ln_eps = a.ln_eps;
+    return launch_tc<ValueLnBf16::S, ValueLnBf16>(prm, prm.units * prm.mt * prm.nd, stream,
+                                                  kProfValue);
   }
   if (elem == 2 && p_lo == nullptr) {
     ValueBf16One::Params prm{};

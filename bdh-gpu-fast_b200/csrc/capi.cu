@@ -571,11 +571,13 @@ size_t bdh_tril_score_v_workspace_size(int dtype, int64_t B, int64_t H, int64_t 
   return fwd_layout(dtype, B, H, Hv, T, N, D, k_is_q != 0).total;
 }
 
-int bdh_tril_score_v(const void* q, const int64_t q_strides[4], const void* k,
-                     const int64_t k_strides[4], const void* v, const int64_t v_strides[4],
-                     int dtype, void* out, const int64_t out_strides[4], int out_dtype,
-                     int64_t B, int64_t H, int64_t Hv, int64_t T, int64_t N, int64_t D,
-                     void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+// The forward; ln: each output row LayerNormed (eps) before the store (bdh_tril_score_v_layernorm).
+int score_v_impl(const void* q, const int64_t q_strides[4], const void* k,
+                 const int64_t k_strides[4], const void* v, const int64_t v_strides[4],
+                 int dtype, void* out, const int64_t out_strides[4], int out_dtype,
+                 int64_t B, int64_t H, int64_t Hv, int64_t T, int64_t N, int64_t D,
+                 void* workspace, size_t workspace_bytes, void* stream, bool ln, float eps) {
   if (!dtype_ok(dtype) || !dtype_ok(out_dtype))
     return fail(BDH_ERR_INVALID, "tril_score_v: dtype must be f32 or bf16");
   if (B < 0 || H < 0 || T < 0 || N < 0 || D < 0)
@@ -639,13 +641,55 @@ int bdh_tril_score_v(const void* q, const int64_t q_strides[4], const void* k,
     std::memcpy(a.v_strides, v_strides, sizeof(a.v_strides));
   }
   void* p_lo = L.one ? nullptr : ws + L.p_lo;
-  if (L.chunked)
-    return launch_chunked_forward(a, ws + L.p_hi, p_lo, ws + L.s_hi,
-                                  L.one ? nullptr : ws + L.s_lo, st, err);
-  int rc = launch_score(a, ws + L.p_hi, p_lo,
-                        L.part ? reinterpret_cast<float*>(ws + L.part) : nullptr, st, err);
-  if (rc) return rc;
-  return launch_value(a, ws + L.p_hi, p_lo, st, err);
+  // the LayerNorm folds into the quadratic bf16 value pass; other forms normalise the output
+  // rows in place afterwards (rows of one stride)
+  const bool ln_fused = ln && !L.chunked && dtype == BDH_DTYPE_BF16 && D <= 256;
+  const bool ln_after = ln && !ln_fused;
+  if (ln_after) {
+    const bool rows_flat = (H <= 1 || out_strides[1] == T * out_strides[2]) &&
+                           (B <= 1 || out_strides[0] == H * T * out_strides[2]);
+    if (!rows_flat || D > 1024 || D % 8 != 0 || (out_strides[2] % 8) != 0 ||
+        (reinterpret_cast<uintptr_t>(out) & 15u) != 0)
+      return fail(BDH_ERR_INVALID,
+                  "tril_score_v_layernorm: this form needs output rows of one stride (a multiple "
+                  "of 8), D a multiple of 8 up to 1024 and a 16-byte aligned output");
+  }
+  a.ln = ln_fused ? 1 : 0;
+  a.ln_eps = eps;
+  int rc;
+  if (L.chunked) {
+    rc = launch_chunked_forward(a, ws + L.p_hi, p_lo, ws + L.s_hi,
+                                L.one ? nullptr : ws + L.s_lo, st, err);
+  } else {
+    rc = launch_score(a, ws + L.p_hi, p_lo,
+                      L.part ? reinterpret_cast<float*>(ws + L.part) : nullptr, st, err);
+    if (!rc) rc = launch_value(a, ws + L.p_hi, p_lo, st, err);
+  }
+  if (rc || !ln_after) return rc;
+  return launch_layernorm(out, out_dtype, out_strides[2], out, out_dtype, out_strides[2],
+                          B * H * T, static_cast<int>(D), eps, st);
+}
+}  // namespace
+
+int bdh_tril_score_v(const void* q, const int64_t q_strides[4], const void* k,
+                     const int64_t k_strides[4], const void* v, const int64_t v_strides[4],
+                     int dtype, void* out, const int64_t out_strides[4], int out_dtype,
+                     int64_t B, int64_t H, int64_t Hv, int64_t T, int64_t N, int64_t D,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  return score_v_impl(q, q_strides, k, k_strides, v, v_strides, dtype, out, out_strides,
+                      out_dtype, B, H, Hv, T, N, D, workspace, workspace_bytes, stream, false,
+                      0.0f);
+}
+
+int bdh_tril_score_v_layernorm(const void* q, const int64_t q_strides[4], const void* k,
+                               const int64_t k_strides[4], const void* v,
+                               const int64_t v_strides[4], int dtype, void* out,
+                               const int64_t out_strides[4], int out_dtype, int64_t B, int64_t H,
+                               int64_t Hv, int64_t T, int64_t N, int64_t D, float eps,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (!(eps >= 0.0f)) return fail(BDH_ERR_INVALID, "tril_score_v_layernorm: eps must be >= 0");
+  return score_v_impl(q, q_strides, k, k_strides, v, v_strides, dtype, out, out_strides,
+                      out_dtype, B, H, Hv, T, N, D, workspace, workspace_bytes, stream, true, eps);
 }
 
 int bdh_set_forward_algo(int algo) {

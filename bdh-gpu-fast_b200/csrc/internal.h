@@ -34,6 +34,9 @@ struct FwdArgs {
   int64_t out_strides[4] = {0, 0, 0, 1};
   int out_dtype = BDH_DTYPE_BF16;
   int64_t B = 0, H = 0, Hv = 0, T = 0, N = 0, D = 0;
+  // > 0: each output row (over D) is LayerNormed (affine-free, eps = ln_eps) before the store
+  int ln = 0;
+  float ln_eps = 1e-5f;
 };
 
 // Layouts of the masked score pass output (see score_pass.cuh).

@@ -436,8 +436,9 @@ struct GateProb : LatentWalk<ORDER> {
     const int slot = st.iter % kSlots;
     uint8_t* box = epi + w * kWarpStage + slot * kBox;
     const uint32_t parity = static_cast<uint32_t>(st.iter / kSlots) & 1u;
-    if (!wait_bounded(bar(epi, w, slot), parity, abort_flag, p.err, kErrTimeoutEpilogue))
-      return false;
+    // the whole warp leaves together on a timeout (the TMEM loads below are warp-aligned)
+    const bool ok = wait_bounded(bar(epi, w, slot), parity, abort_flag, p.err, kErrTimeoutEpilogue);
+    if (!__all_sync(0xffffffffu, ok)) return false;
     uint32_t rr[2][32];
     tmem_ld32(taddr + static_cast<uint32_t>(part * 64), rr[0]);
     tmem_ld32(taddr + static_cast<uint32_t>(part * 64 + 32), rr[1]);

@@ -113,7 +113,8 @@ at::Tensor freqs_vector(const at::Tensor& freqs, int64_t n) {
 }
 
 // ------------------------------------------------------------------------ forward
-at::Tensor tril_score_v(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v) {
+// ln_eps >= 0: each output row LayerNormed over D (bdh_tril_score_v_layernorm).
+at::Tensor score_v(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double ln_eps) {
   check_cold_shapes(q, k, v);
   require_cuda({&q, &k, &v});
   const c10::cuda::CUDAGuard guard(q.device());
@@ -132,12 +133,27 @@ at::Tensor tril_score_v(const at::Tensor& q, const at::Tensor& k, const at::Tens
   at::Tensor ws = at::empty({static_cast<int64_t>(std::max<size_t>(wsz, 1))},
                             q.options().dtype(at::kByte));
   const Strides4 sq(qq), sk(kk), sv(vv), so(out_full);
-  check_rc(bdh_tril_score_v(qq.data_ptr(), sq.s, kk.data_ptr(), sk.s, vv.data_ptr(), sv.s, dt,
-                            out_full.data_ptr(), so.s, dt, B, H, Hv, T, Np, Dp, ws.data_ptr(), wsz,
-                            stream_of(q)),
-           "tril_score_v");
+  if (ln_eps < 0) {
+    check_rc(bdh_tril_score_v(qq.data_ptr(), sq.s, kk.data_ptr(), sk.s, vv.data_ptr(), sv.s, dt,
+                              out_full.data_ptr(), so.s, dt, B, H, Hv, T, Np, Dp, ws.data_ptr(),
+                              wsz, stream_of(q)),
+             "tril_score_v");
+  } else {
+    TORCH_CHECK(Dp == D, "tril_score_v: the fused LayerNorm needs D a multiple of 16 bytes");
+    check_rc(bdh_tril_score_v_layernorm(qq.data_ptr(), sq.s, kk.data_ptr(), sk.s, vv.data_ptr(),
+                                        sv.s, dt, out_full.data_ptr(), so.s, dt, B, H, Hv, T, Np,
+                                        Dp, static_cast<float>(ln_eps), ws.data_ptr(), wsz,
+                                        stream_of(q)),
+             "tril_score_v_layernorm");
+  }
   if (Dp != D) out.copy_(out_full.narrow(3, 0, D));
   return out;
+}
+
+at::Tensor tril_score_v(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                        std::optional<double> ln_eps) {
+  if (ln_eps.has_value()) TORCH_CHECK(*ln_eps >= 0.0, "ln_eps must be >= 0");
+  return score_v(q, k, v, ln_eps.has_value() ? *ln_eps : -1.0);
 }
 
 // RoPE of x (B,H,T,N) at positions pos0 .. pos0 + T - 1 (phases from freqs in registers);
@@ -179,7 +195,7 @@ std::tuple<at::Tensor, at::Tensor> rope_tril_score_v(const at::Tensor& q, const 
                                                      std::optional<at::Tensor> qr_out) {
   at::Tensor qr = rope_rotate(q, freqs, rope_start, qr_out, false);
   at::Tensor qq = qr.scalar_type() == q.scalar_type() ? qr : qr.to(q.scalar_type());
-  return {tril_score_v(qq, qq, v), qr};
+  return {score_v(qq, qq, v, -1.0), qr};
 }
 
 // ------------------------------------------------------------------------- decode
@@ -496,8 +512,10 @@ std::tuple<at::Tensor, std::optional<at::Tensor>> residual_layer_norm(const at::
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "BDH strict lower-triangular score x V, decode and backward on sm_100a (no softmax)";
-  m.def("tril_score_v", &tril_score_v, "out = tril(Q@K.T, diagonal=-1) @ V  (no softmax, no scale)",
-        py::arg("q"), py::arg("k"), py::arg("v"));
+  m.def("tril_score_v", &tril_score_v,
+        "out = tril(Q@K.T, diagonal=-1) @ V  (no softmax, no scale); with ln_eps each output row "
+        "is LayerNormed over D before the store",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("ln_eps") = py::none());
   m.def("tril_decode", &tril_decode,
         "out = (Q @ K_past.T) @ V_past  (packed past; no self-attend)", py::arg("q"),
         py::arg("k_past"), py::arg("v_past"));

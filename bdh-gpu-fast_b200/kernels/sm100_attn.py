@@ -40,7 +40,7 @@ _F32 = 0
 _BF16 = 1
 
 _c_i64_4 = ctypes.c_int64 * 4
-ABI_VERSION = 8  # BDH_ABI_VERSION of include/bdh_sm100.h
+ABI_VERSION = 9  # BDH_ABI_VERSION of include/bdh_sm100.h
 FP8 = torch.float8_e4m3fn  # the opt-in fp8 key-cache storage dtype
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -66,6 +66,9 @@ def _declare(lib: ctypes.CDLL) -> None:
                                                     _i64, ctypes.c_int]
     lib.bdh_tril_score_v.argtypes = [_vp, P, _vp, P, _vp, P, ctypes.c_int, _vp, P, ctypes.c_int,
                                      _i64, _i64, _i64, _i64, _i64, _i64, _vp, ctypes.c_size_t, _vp]
+    lib.bdh_tril_score_v_layernorm.argtypes = [_vp, P, _vp, P, _vp, P, ctypes.c_int, _vp, P,
+                                               ctypes.c_int, _i64, _i64, _i64, _i64, _i64, _i64,
+                                               ctypes.c_float, _vp, ctypes.c_size_t, _vp]
     lib.bdh_tril_decode_workspace_size.restype = ctypes.c_size_t
     lib.bdh_tril_decode_workspace_size.argtypes = [_i64, _i64, _i64, _i64, _i64, _i64]
     lib.bdh_tril_decode.argtypes = [_vp, P, ctypes.c_int, _vp, P, _vp, P, ctypes.c_int, _vp, P,
@@ -106,7 +109,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.bdh_state_decode.argtypes = [_vp, P, ctypes.c_int, _vp, P, _vp, P, ctypes.c_int, _vp, P,
                                      _i64, _i64, _i64, _i64, _i64, _vp, _i64, ctypes.c_int, _vp,
                                      ctypes.c_size_t, _vp]
-    for name in ("bdh_rope_rotate", "bdh_tril_score_v", "bdh_tril_decode", "bdh_tril_score_v_bwd",
+    for name in ("bdh_rope_rotate", "bdh_tril_score_v", "bdh_tril_score_v_layernorm",
+                 "bdh_tril_decode", "bdh_tril_score_v_bwd",
                  "bdh_relu_mul", "bdh_latent_encode", "bdh_latent_gate", "bdh_latent_gate_x",
                  "bdh_latent_gate_dec", "bdh_latent_gate_dec_ws",
                  "bdh_layernorm", "bdh_quantize_rows_fp8", "bdh_tril_decode_fp8",
@@ -321,15 +325,17 @@ def score_terms_scope(mode: Optional[str]):
 
 # -------------------------------------------------------------------------- forward
 def tril_score_v(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
-                 score_terms: Optional[str] = None) -> torch.Tensor:
+                 score_terms: Optional[str] = None, ln_eps: Optional[float] = None) -> torch.Tensor:
     """``(q @ k.mT).tril(-1) @ v`` on the sm_100a tensor cores (fp32 accumulation).
 
     ``score_terms`` (bf16 inputs): ``"bf16"`` rounds the scores to bf16 before the product with
     ``v`` as the reference's eager autocast path does, ``"split"`` keeps them exact; None: the
-    process default (exact for the quadratic form)."""
+    process default (exact for the quadratic form). ``ln_eps``: each output row is LayerNormed
+    (affine-free, over D, that eps) before the store (``bdh_tril_score_v_layernorm``: in the value
+    pass's epilogue for the quadratic bf16 form)."""
     if score_terms is not None:
         with score_terms_scope(score_terms):
-            return tril_score_v(q, k, v)
+            return tril_score_v(q, k, v, ln_eps=ln_eps)
     _check_cold_shapes(q, k, v)
     dev = _require_cuda(q, k, v)
     lib = _require_lib()
@@ -352,13 +358,21 @@ def tril_score_v(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     else:
         out_full = out
     k_is_q = 1 if kk is qq else 0
+    if ln_eps is not None and Dp != D:
+        raise ValueError("tril_score_v: the fused LayerNorm needs D a multiple of 16 bytes")
     wsz = lib.bdh_tril_score_v_workspace_size(dt, B, H, Hv, T, Np, Dp, k_is_q)
     ws = torch.empty(max(int(wsz), 1), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
-        rc = lib.bdh_tril_score_v(
-            qq.data_ptr(), _strides(qq), kk.data_ptr(), _strides(kk), vv.data_ptr(), _strides(vv),
-            dt, out_full.data_ptr(), _strides(out_full), dt, B, H, Hv, T, Np, Dp,
-            ws.data_ptr(), int(wsz), _stream(dev))
+        if ln_eps is None:
+            rc = lib.bdh_tril_score_v(
+                qq.data_ptr(), _strides(qq), kk.data_ptr(), _strides(kk), vv.data_ptr(),
+                _strides(vv), dt, out_full.data_ptr(), _strides(out_full), dt, B, H, Hv, T, Np,
+                Dp, ws.data_ptr(), int(wsz), _stream(dev))
+        else:
+            rc = lib.bdh_tril_score_v_layernorm(
+                qq.data_ptr(), _strides(qq), kk.data_ptr(), _strides(kk), vv.data_ptr(),
+                _strides(vv), dt, out_full.data_ptr(), _strides(out_full), dt, B, H, Hv, T, Np,
+                Dp, float(ln_eps), ws.data_ptr(), int(wsz), _stream(dev))
     _check(rc, "tril_score_v")
     if out_full is not out:
         out.copy_(out_full[..., :D])

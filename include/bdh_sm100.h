@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define BDH_ABI_VERSION 8
+#define BDH_ABI_VERSION 9
 
 #define BDH_DTYPE_F32 0
 #define BDH_DTYPE_BF16 1
@@ -122,6 +122,24 @@ int bdh_tril_score_v(const void* q, const int64_t q_strides[4], const void* k,
                      int dtype, void* out, const int64_t out_strides[4], int out_dtype,
                      int64_t B, int64_t H, int64_t Hv, int64_t T, int64_t N, int64_t D,
                      void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * The forward followed by the affine-free LayerNorm of every output row over D (eps as
+ * F.layer_norm): out = LN(tril(q k^T, -1) v), the attention output of a BDH layer as its
+ * encoder_v projection reads it (bdh.py:1044; under bf16 autocast the LayerNorm runs in fp32 on
+ * the bf16 attention output and its consumer casts the result to bf16). For the quadratic bf16
+ * forward with D <= 256 the normalisation is done in the value pass's epilogue (the
+ * un-normalised output never reaches HBM); other forms normalise the output rows in place
+ * afterwards and then need rows of one stride. Arguments and workspace (the
+ * bdh_tril_score_v_workspace_size figure) as bdh_tril_score_v. No counterpart in the
+ * reference (a model-level fusion).
+ */
+int bdh_tril_score_v_layernorm(const void* q, const int64_t q_strides[4], const void* k,
+                               const int64_t k_strides[4], const void* v,
+                               const int64_t v_strides[4], int dtype, void* out,
+                               const int64_t out_strides[4], int out_dtype, int64_t B, int64_t H,
+                               int64_t Hv, int64_t T, int64_t N, int64_t D, float eps,
+                               void* workspace, size_t workspace_bytes, void* stream);
 
 /* Scratch bytes bdh_tril_decode needs: the split partial sums, plus B*H*Tq*N*4 for the rotated
  * queries (used when freqs is given). */

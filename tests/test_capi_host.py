@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
     lib = sa.load_library()
     for name in _declared():
         assert hasattr(lib, name), f"{name} missing from {sa._LIB_PATH}"
-    assert lib.bdh_abi_version() == sa.ABI_VERSION == 8
+    assert lib.bdh_abi_version() == sa.ABI_VERSION == 9
 
 
 def test_workspace_queries_are_host_only():
