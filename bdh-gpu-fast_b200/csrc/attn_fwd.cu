@@ -218,10 +218,13 @@ using ScoreBf16Wide = ScoreProb<2, 256, 4>;  // 128 x 256 tiles: 25% fewer opera
 // CTA-pair score pass: 256 x 256 tiles (each CTA 128 query rows x all 256 keys of the tile in
 // TMEM, staging 128 query rows and 128 key rows per stage). Epilogue and parameters are those of
 // the single-CTA 128 x 256 score pass, applied to each CTA's 128-row half.
-struct ScorePair {
+// STAGES operand stages of 32 KB; SCRATCH bytes of shared memory per epilogue warp for the
+// transposed stores of the backward's G and M^T (0: direct stores only, room for a seventh stage).
+template <int STAGES, int SCRATCH>
+struct ScorePairT {
   using Base = ScoreBf16Wide;
   using Params = Base::Params;  // b_map box is 64 x 128 (one CTA's key rows)
-  using S = PairShape<false, false, 1, 1, 6>;
+  using S = PairShape<false, false, 1, 1, STAGES>;
   struct Tile {
     int unit, m, n;  // 256-row query block, 256-key block
     int sub;         // -1: all 256 keys; else keys [sub * w, (sub + 1) * w), w = 256 / tail_sub
@@ -299,11 +302,11 @@ struct ScorePair {
                        tl.n * 256 + tl.sub * w + static_cast<int>(rank) * (w / 2), hb, b);
     }
   }
-  // 4 KB per epilogue warp: the transposed stores of the backward's G and M^T go through
-  // shared memory (whole 64-byte column segments instead of two-byte element stores)
-  static constexpr int kEpiScratch = 2 * 32 * 32 * 2;
+  // 4 KB per epilogue warp (SCRATCH): the transposed stores of the backward's G and M^T go
+  // through shared memory (whole 64-byte column segments instead of two-byte element stores)
+  static constexpr int kEpiScratch = SCRATCH;
   __device__ static void epilogue(const Params& p, const Tile& tl, int rank, int row, int c0,
-                                  const uint32_t (&r)[32], uint8_t* scratch) {
+                                  const uint32_t (&r)[32], uint8_t* scratch = nullptr) {
     Base::Tile t;
     t.unit = tl.unit;
     t.mi = 2 * tl.m + rank;
@@ -312,6 +315,10 @@ struct ScorePair {
     Base::epilogue(p, t, row, tl.sub < 0 ? c0 : tl.sub * (256 / p.tail_sub) + c0, r, scratch);
   }
 };
+
+using ScorePair = ScorePairT<6, 2 * 32 * 32 * 2>;
+// Direct stores only (the forward's P): seven 32 KB stages, 224 KB of operands in flight.
+using ScorePairDirect = ScorePairT<7, 0>;
 
 // CTA pairs for the bf16 tensor passes (BDH_SM100_PAIR=0 selects single-CTA tiles instead).
 bool use_pairs() {
@@ -443,6 +450,14 @@ int launch_score_pass(const ScoreArgs& a, cudaStream_t stream, int* err) {
       prm.tail_from = ntiles - tail;
       return launch_pair<ScorePair::S, ScorePair>(prm, prm.tail_from + tail * sub, stream, kProfScore);
     }
+    // direct stores (the forward's P): the form with seven operand stages
+    // (BDH_SM100_SCORE_STAGES=6 keeps six)
+    static const bool seven = [] {
+      const char* e = std::getenv("BDH_SM100_SCORE_STAGES");
+      return !(e != nullptr && std::atoi(e) == 6);
+    }();
+    if (a.mode == kStoreDirect && seven)
+      return launch_pair<ScorePairDirect::S, ScorePairDirect>(prm, ntiles, stream, kProfScore);
     return launch_pair<ScorePair::S, ScorePair>(prm, ntiles, stream, kProfScore);
   }
   if (elem == 2 && score_tile_n() == 256) {
