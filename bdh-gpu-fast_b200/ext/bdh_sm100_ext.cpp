@@ -170,7 +170,8 @@ at::Tensor rope_rotate(const at::Tensor& x_in, const at::Tensor& freqs, int64_t 
     out = *out_opt;
     TORCH_CHECK(out.sizes() == x_in.sizes() && out.device() == x_in.device(),
                 "rope out= must match x shape/device");
-    TORCH_CHECK(at::get_overlap_status(out, x_in) == at::MemOverlapStatus::No,
+    const at::MemOverlapStatus ov = at::get_overlap_status(out, x_in);
+    TORCH_CHECK(ov != at::MemOverlapStatus::Full && ov != at::MemOverlapStatus::Partial,
                 "rope out= must not alias x");
     TORCH_CHECK(out.stride(3) == 1, "rope out= must have a contiguous last dimension");
   } else {
