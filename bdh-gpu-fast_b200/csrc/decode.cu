@@ -707,17 +707,27 @@ int launch_decode(const DecodeArgs& a_in, float* partial, float* qrot, int64_t m
     // (the elementwise RoPE kernel), instead of once per split CTA: an fp32 copy for the dot
     // products and the storage-dtype copy in this step's cache slot.
     const int64_t qs[4] = {a.H * a.Tq * a.N, a.Tq * a.N, a.N, 1};
-    int rc = launch_rope(a.q, a.q_dtype, a.q_strides, qrot, BDH_DTYPE_F32, qs, nullptr, a.freqs, a.B,
-                         a.H, a.Tq, a.N, a.pos, 0, stream);
-    if (rc) return rc;
-    if (a.slot != nullptr) {
-      rc = launch_rope(a.q, a.q_dtype, a.q_strides, a.slot, a.kv_dtype, a.slot_strides, nullptr,
-                       a.freqs, a.B, a.H, a.Tq, a.N, a.pos, 0, stream);
+    if (a.slot != nullptr && a.kv_dtype == BDH_DTYPE_F32) {
+      // an fp32 slot holds exactly the fp32 rotated queries: one pass, and the kernel reads them
+      // from the slot (the position after the past it streams)
+      int rc = launch_rope(a.q, a.q_dtype, a.q_strides, a.slot, BDH_DTYPE_F32, a.slot_strides,
+                           nullptr, a.freqs, a.B, a.H, a.Tq, a.N, a.pos, 0, stream);
       if (rc) return rc;
+      a.q = a.slot;
+      for (int i = 0; i < 4; ++i) a.q_strides[i] = a.slot_strides[i];
+    } else {
+      int rc = launch_rope(a.q, a.q_dtype, a.q_strides, qrot, BDH_DTYPE_F32, qs, nullptr, a.freqs,
+                           a.B, a.H, a.Tq, a.N, a.pos, 0, stream);
+      if (rc) return rc;
+      if (a.slot != nullptr) {
+        rc = launch_rope(a.q, a.q_dtype, a.q_strides, a.slot, a.kv_dtype, a.slot_strides, nullptr,
+                         a.freqs, a.B, a.H, a.Tq, a.N, a.pos, 0, stream);
+        if (rc) return rc;
+      }
+      a.q = qrot;
+      for (int i = 0; i < 4; ++i) a.q_strides[i] = qs[i];
     }
-    a.q = qrot;
     a.q_dtype = BDH_DTYPE_F32;
-    for (int i = 0; i < 4; ++i) a.q_strides[i] = qs[i];
     a.freqs = nullptr;
     a.slot = nullptr;
   }

@@ -217,3 +217,19 @@ def test_model_logits_same_bits_through_either_binding(ext, monkeypatch):
         monkeypatch.setenv("BDH_SM100_EXT", "0")
         b = m(idx)[0]
     assert torch.equal(a, b)
+
+
+def test_rope_into_a_strided_cache_slot(ext):
+    """RoPE written straight into a capacity-strided cache slot (a view that the overlap check
+    cannot classify), as the prefill of a cached model does."""
+    B, H, T, cap, N = 2, 4, 48, 128, 1024
+    g = torch.Generator(device=DEV).manual_seed(13)
+    x = torch.relu(torch.randn(B, H, T, N, device=DEV, generator=g)).bfloat16()
+    freqs = torch.tensor(O.get_freqs(N), device=DEV)
+    a = torch.zeros(B, H, cap, N, device=DEV, dtype=torch.bfloat16)
+    b = torch.zeros_like(a)
+    ext.rope_rotate(x, freqs, 7, a[:, :, 10:10 + T])
+    sa().rope_rotate(x, freqs, 7, out=b[:, :, 10:10 + T])
+    assert torch.equal(a, b) and bool(a[:, :, 10:10 + T].abs().sum() > 0)
+    with pytest.raises(RuntimeError, match="must not alias"):
+        ext.rope_rotate(x, freqs, 0, x)
