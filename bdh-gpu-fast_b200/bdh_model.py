@@ -198,6 +198,24 @@ class BDH(nn.Module):
             cache[(name, k_major)] = hit
         return hit[1]
 
+    def _encoder_lin(self) -> torch.Tensor:
+        """The encoder as the (nh * N, D) matrix F.linear reads (the reference's _encoder_relu
+        layout, bdh.py:861-889): x_lat[b, t, h, n] = x[b, t] . encoder[h, :, n]. Kept between
+        calls while no gradient is needed (an einsum over the (nh, D, N) parameter copies it
+        into a GEMM layout on every call); built per call otherwise, so gradients reach the
+        parameter."""
+        p = self.encoder
+        nh, D, N = p.shape
+        if torch.is_grad_enabled() and p.requires_grad:
+            return p.transpose(1, 2).reshape(nh * N, D)
+        cache = self.__dict__.setdefault("_lin_cache", {})
+        key = (p.data_ptr(), p._version, p.device, p.dtype)
+        hit = cache.get("encoder")
+        if hit is None or hit[0] != key:
+            hit = (key, p.detach().transpose(1, 2).reshape(nh * N, D).contiguous())
+            cache["encoder"] = hit
+        return hit[1]
+
     def _attn_state(self, Q: torch.Tensor, V: torch.Tensor, level: int, rope_start: int, cache,
                     impl: str, relu_input: bool) -> torch.Tensor:
         """Attention of a block against a StateCache, folding the block into the state.
@@ -379,7 +397,7 @@ class BDH(nn.Module):
             if latent:
                 x, xb = self._layer_latent(x, xb, level, rope_start, cache)
                 continue
-            x_lat = torch.einsum("btd,hdn->bthn", x, self.encoder)  # (B, T, nh, N)
+            x_lat = F.linear(x, self._encoder_lin()).view(B, T, C.n_head, N)  # (B, T, nh, N)
             x_bthn = x_lat if fused else F.relu(x_lat)
             x_sparse = x_bthn.permute(0, 2, 1, 3)  # (B, nh, T, N) view
             v_tok = x.unsqueeze(1)
