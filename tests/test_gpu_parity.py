@@ -321,6 +321,14 @@ BWD_SHAPES = [  # B, H, Hv, T, N, D
     (1, 2, 2, 130, 64, 32),
     (2, 3, 1, 257, 256, 256),
     (1, 4, 1, 512, 1024, 256),
+    # T on and just below the 128- and 256-row tile edges, latent and value widths that are not
+    # multiples of the 64-element k-block (zero-filled tails), the value rows of D = 300 not
+    # 16-byte aligned in bf16, and a long odd T: the strict past must hold at every tile edge
+    # (tests/test_attn_bwd.py of the reference checks it at its default tile boundary)
+    (1, 2, 1, 128, 72, 40),
+    (2, 2, 2, 255, 136, 96),
+    (1, 1, 1, 256, 200, 300),
+    (1, 1, 1, 1537, 72, 40),
 ]
 
 
@@ -343,6 +351,83 @@ def test_backward_vs_oracle(shape, dt, self_form):
     assert rel(dv.float().cpu().numpy(), rv) <= TOL[dt]
     if not self_form:
         assert rel(dk.float().cpu().numpy(), rk) <= TOL[dt]
+
+
+@pytest.mark.parametrize("dt,T,j0,N,D", [(torch.float32, 65, 63, 16, 8),
+                                          (torch.float32, 129, 127, 16, 8),
+                                          (torch.float32, 257, 128, 16, 8),
+                                          (torch.bfloat16, 256, 255, 16, 8),
+                                          (torch.bfloat16, 1537, 255, 128, 64),
+                                          (torch.bfloat16, 1537, 256, 128, 64),
+                                          (torch.bfloat16, 1600, 1535, 128, 64)])
+def test_forward_strict_past_at_tile_edges(dt, T, j0, N, D):
+    """V nonzero on one key row j0 only: every output row t <= j0 is exactly zero (no diagonal,
+    no future), across the 128- and 256-row tile edges and, for bf16 at T >= 1536, the chunked
+    form's 256-key chunk edges (intra-chunk scores and carried prefix state); the rest matches
+    fp64 (Q K^T).tril(-1) V."""
+    g = torch.Generator().manual_seed(4099 + T + j0)
+    q64 = torch.randn(1, 2, T, N, generator=g, dtype=torch.float64)
+    k64 = torch.randn(1, 2, T, N, generator=g, dtype=torch.float64)
+    v64 = torch.zeros(1, 1, T, D, dtype=torch.float64)
+    v64[:, :, j0, :] = torch.randn(1, 1, D, generator=g, dtype=torch.float64)
+    q, k, v = (x.to(dt).to(DEV) for x in (q64, k64, v64))
+    out = sa().tril_score_v(q, k, v)
+    assert torch.count_nonzero(out[:, :, : j0 + 1, :]).item() == 0
+    if j0 == T - 1:  # no row after the key: the whole output is zero
+        return
+    qr, kr, vr = (x.to(dt).double() for x in (q64, k64, v64))
+    ref = (qr @ kr.mT).tril(-1) @ vr
+    tol = 1e-5 if dt == torch.float32 else 3e-3
+    assert ((out.double().cpu() - ref).norm() / ref.norm()).item() <= tol
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("T,queries", [(65, (63,)), (65, (64,)), (128, (127,)), (129, (128,)),
+                                       (257, (255,)), (257, (256,)), (257, (127, 128, 255))])
+def test_backward_strict_past_at_tile_edges(T, queries, dt):
+    """Upstream gradient on a few rows only, next to the 64-, 128- and 256-row tile edges: dK and
+    dV of every key at or after the last such row are exactly zero (strict past, no diagonal, no
+    future), and all three gradients match fp64 autograd of (Q K^T).tril(-1) V (the reference's
+    tests/test_attn_bwd_v4_contract.py:611-667 strict-past and multi-tile accumulation cases,
+    with N = 3 and D = 4 padded by the wrapper)."""
+    g = torch.Generator().manual_seed(2031 + T + sum(queries))
+    q64 = torch.randn(1, 2, T, 3, generator=g, dtype=torch.float64)
+    k64 = torch.randn(1, 2, T, 3, generator=g, dtype=torch.float64)
+    v64 = torch.randn(1, 1, T, 4, generator=g, dtype=torch.float64)
+    do64 = torch.zeros(1, 2, T, 4, dtype=torch.float64)
+    for i in queries:
+        do64[:, :, i, :] = torch.randn(1, 2, 4, generator=g, dtype=torch.float64)
+    q, k, v, do = (x.to(dt).to(DEV) for x in (q64, k64, v64, do64))
+    dq, dk, dv = sa().tril_score_v_bwd(q, k, v, do)
+    last = max(queries)
+    assert torch.count_nonzero(dk[:, :, last:, :]).item() == 0
+    assert torch.count_nonzero(dv[:, :, last:, :]).item() == 0
+    quiet = [i for i in range(T) if i not in queries]  # rows without upstream gradient
+    assert torch.count_nonzero(dq[:, :, quiet, :]).item() == 0
+    # the reference math on the operands as the kernel saw them (rounded to dt), in fp64
+    qr, kr, vr = (x.to(dt).double().requires_grad_(True) for x in (q64, k64, v64))
+    dod = do.double().cpu()
+    ((qr @ kr.mT).tril(-1) @ vr).backward(dod)
+    got = {"dq": dq, "dk": dk, "dv": dv}
+    ref = {"dq": qr.grad, "dk": kr.grad, "dv": vr.grad}
+    if dt == torch.float32:
+        for n in got:
+            assert ((got[n].double().cpu() - ref[n]).norm() / ref[n].norm()).item() <= 1e-5
+        return
+    # bf16: with one upstream row and N = 3 a handful of values carry the whole norm, so the
+    # relative-Frobenius bar (held on full tensors by test_backward_vs_oracle) is replaced by an
+    # elementwise bound: one bf16 rounding of every score the products read (P = Q K^T and
+    # dS = dO V^T, both masked) and of every output, at 2^-8 (twice bf16's unit roundoff)
+    qd, kd, vd = qr.detach(), kr.detach(), vr.detach()
+    P = (qd @ kd.mT).tril(-1).abs()
+    dS = (dod @ vd.mT).tril(-1).abs()
+    eps = 2.0 ** -8
+    bound = {"dq": eps * (dS @ kd.abs() + ref["dq"].abs()),
+             "dk": eps * (dS.mT @ qd.abs() + ref["dk"].abs()),
+             "dv": eps * ((P.mT @ dod.abs()).sum(dim=1, keepdim=True) + ref["dv"].abs())}
+    for n in got:
+        err = (got[n].double().cpu() - ref[n]).abs()
+        assert torch.all(err <= bound[n]), (n, (err - bound[n]).max().item())
 
 
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
