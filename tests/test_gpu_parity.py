@@ -242,6 +242,21 @@ def test_decode_storage_dtypes(qdt, kvdt):
     assert ((out.double() - ref).norm() / ref.norm()).item() <= TOL[qdt] * (1 if qdt == torch.float32 else 1)
 
 
+@pytest.mark.parametrize("qdt,kvdt,S", [(torch.float32, torch.float32, 700),
+                                        (torch.float32, torch.bfloat16, 1023),
+                                        (torch.bfloat16, torch.bfloat16, 129)])
+def test_decode_exact_small_integers(qdt, kvdt, S):
+    """Integer query and cache (scores <= 32, sums below 2^24): the decode step, with its split
+    plan and fixed-order reduction, returns (q K^T) V exactly, rounded once to the query dtype."""
+    B, H, N, D = 3, 4, 8, 64
+    g = torch.Generator().manual_seed(S)
+    q64 = torch.randint(0, 3, (B, H, 1, N), generator=g).double()
+    k64 = torch.randint(0, 3, (B, H, S, N), generator=g).double()
+    v64 = torch.randint(-2, 3, (B, 1, S, D), generator=g).double()
+    out = sa().tril_decode(q64.to(qdt).to(DEV), k64.to(kvdt).to(DEV), v64.to(kvdt).to(DEV))
+    assert torch.equal(out.cpu(), ((q64 @ k64.mT) @ v64).to(qdt))
+
+
 def test_decode_equals_last_row_of_forward():
     B, H, T, N, D = 2, 4, 300, 1024, 256
     q = torch.relu(torch.randn(B, H, T, N, device=DEV))
@@ -428,6 +443,51 @@ def test_backward_strict_past_at_tile_edges(T, queries, dt):
     for n in got:
         err = (got[n].double().cpu() - ref[n]).abs()
         assert torch.all(err <= bound[n]), (n, (err - bound[n]).max().item())
+
+
+def test_raw_score_contract_exact_small_integers():
+    """The reference's raw-score contract (tests/test_prefill_blocked.py:47-87): integer Q, K, V
+    give an exactly representable tril(Q K^T, -1) V, so the fp32 path must return it bit for bit;
+    the backward of out.sum() has no gradient on Q's first row and on K's and V's last rows, and
+    is exact as well."""
+    Q = torch.tensor([2.0, 3.0, 5.0, 7.0, 11.0], dtype=torch.float64).view(1, 1, 5, 1)
+    K = torch.tensor([13.0, 17.0, 19.0, 23.0, 29.0], dtype=torch.float64).view(1, 1, 5, 1)
+    V = torch.tensor([[[[1.0, -1.0], [2.0, -2.0], [4.0, -4.0], [8.0, -8.0], [16.0, -16.0]]]],
+                     dtype=torch.float64)
+    exact = (Q @ K.mT).tril(-1) @ V
+    got = sa().tril_score_v(Q.float().to(DEV), K.float().to(DEV), V.float().to(DEV))
+    assert torch.equal(got.double().cpu(), exact)
+    v1 = V[..., :1]
+    qd, kd, vd = (x.clone().requires_grad_(True) for x in (Q, K, v1))
+    ((qd @ kd.mT).tril(-1) @ vd).sum().backward()
+    dq, dk, dv = sa().tril_score_v_bwd(Q.float().to(DEV), K.float().to(DEV), v1.float().to(DEV),
+                                       torch.ones(1, 1, 5, 1, device=DEV))
+    assert torch.count_nonzero(dq[:, :, 0]).item() == 0
+    assert torch.count_nonzero(dk[:, :, -1]).item() == 0 and torch.count_nonzero(dv[:, :, -1]).item() == 0
+    for got_g, ref_g in ((dq, qd.grad), (dk, kd.grad), (dv, vd.grad)):
+        assert torch.equal(got_g.double().cpu(), ref_g)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_exact_small_integers_across_tiles(dt):
+    """Integer operands small enough that every score (<= 32) and dS is exact in bf16 and every
+    sum exact in fp32: across the 128- and 256-row tile edges (T = 300) the forward and all three
+    gradients equal the exact result, rounded once to the output dtype (bit for bit)."""
+    B, H, T, N, D = 1, 2, 300, 8, 8
+    g = torch.Generator().manual_seed(77)
+    q64 = torch.randint(0, 3, (B, H, T, N), generator=g).double()
+    k64 = torch.randint(0, 3, (B, H, T, N), generator=g).double()
+    v64 = torch.randint(-2, 3, (B, 1, T, D), generator=g).double()
+    do64 = torch.randint(-2, 3, (B, H, T, D), generator=g).double()
+    q, k, v, do = (x.to(dt).to(DEV) for x in (q64, k64, v64, do64))
+    out = sa().tril_score_v(q, k, v)
+    exact = (q64 @ k64.mT).tril(-1) @ v64
+    assert torch.equal(out.cpu(), exact.to(dt))
+    qd, kd, vd = (x.clone().requires_grad_(True) for x in (q64, k64, v64))
+    ((qd @ kd.mT).tril(-1) @ vd).backward(do64)
+    dq, dk, dv = sa().tril_score_v_bwd(q, k, v, do)
+    for got_g, ref_g in ((dq, qd.grad), (dk, kd.grad), (dv, vd.grad)):
+        assert torch.equal(got_g.cpu(), ref_g.to(dt))
 
 
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
