@@ -490,6 +490,66 @@ def test_exact_small_integers_across_tiles(dt):
         assert torch.equal(got_g.cpu(), ref_g.to(dt))
 
 
+@pytest.mark.parametrize("value_heads", [1, 2])
+@pytest.mark.parametrize("padding", ["feature", "sequence"])
+def test_autograd_through_padded_storage(padding, value_heads):
+    """The reference's padded-storage autograd contracts (tests/test_prefill_blocked.py:262-300
+    and the capacity-padded sequence variant): Q and K are views of larger buffers (one spare
+    latent column, or spare capacity rows, as a cache keeps them); the gradients land in the
+    right elements of the buffers, none in the padding, and match fp64 eager attention."""
+    import kernels
+
+    T, B, H, N, D = 257, 2, 2, 5, 4
+    g = torch.Generator().manual_seed(327 + value_heads)
+    shape = (B, H, T, N + 1) if padding == "feature" else (B, H, T + 7, N)
+    qs0 = torch.randn(*shape, dtype=torch.float64, generator=g)
+    ks0 = torch.randn(*shape, dtype=torch.float64, generator=g)
+    v0 = torch.randn(B, value_heads, T, D, dtype=torch.float64, generator=g)
+    w = torch.randn(B, H, T, D, dtype=torch.float64, generator=g)
+
+    def run(fn, dev, dt):
+        qs = qs0.to(dev, dt).requires_grad_(True)
+        ks = ks0.to(dev, dt).requires_grad_(True)
+        v = v0.to(dev, dt).requires_grad_(True)
+        q, k = ((x[..., :N] if padding == "feature" else x[:, :, :T]) for x in (qs, ks))
+        assert not q.is_contiguous() and not k.is_contiguous()
+        out = fn(q, k, v)
+        grads = torch.autograd.grad((out * w.to(dev, dt)).sum(), (qs, ks, v))
+        return out, grads
+
+    ref, ref_g = run(lambda q, k, v: (q @ k.mT).tril(-1) @ v, "cpu", torch.float64)
+    got, got_g = run(lambda q, k, v: kernels.bdh_attn(q, k, v, impl="cuda_sm100", use_autograd_fn=True),
+                     DEV, torch.float32)
+    assert ((got.double().cpu() - ref).norm() / ref.norm()).item() < 1e-5
+    for a, b in zip(got_g, ref_g):
+        assert ((a.double().cpu() - b).norm() / b.norm()).item() < 1e-5
+    assert torch.count_nonzero(got[:, :, 0]).item() == 0
+    for gs in got_g[:2]:
+        pad = gs[..., N] if padding == "feature" else gs[:, :, T:]
+        assert torch.count_nonzero(pad).item() == 0
+
+
+@pytest.mark.parametrize("T", [1600, 4100])
+def test_chunked_forward_exact_sparse_binary(T):
+    """The chunked form (bf16, T >= 1536; 256-key chunks at T = 1600, 512 at 4100, ragged last
+    chunks) on sparse binary latents (5% ones) and V in {-1, 0, 1}: every intra-chunk score and
+    every prefix-state entry stays an integer below 256, exact in its bf16 storage, and every sum
+    below 2^24, so the output equals tril(Q Q^T, -1) V rounded once to bf16."""
+    B, H, N, D = 1, 2, 128, 64
+    g = torch.Generator().manual_seed(T)
+    q64 = (torch.rand(B, H, T, N, generator=g) < 0.05).double()
+    v64 = torch.randint(-1, 2, (B, 1, T, D), generator=g).double()
+    q = q64.to(torch.bfloat16).to(DEV)
+    sa().profile_begin()
+    out = sa().tril_score_v(q, q, v64.to(torch.bfloat16).to(DEV))
+    torch.cuda.synchronize()
+    assert sa().profile_end()["state"]["launches"] == 1  # the prefix-state pass ran: chunked form
+    exact = (q64 @ q64.mT).tril(-1) @ v64
+    states = torch.einsum("bhtn,bhtd->bhnd", q64, v64.abs().expand(B, H, T, D))
+    assert states.max().item() < 256  # the largest possible prefix-state entry
+    assert torch.equal(out.cpu(), exact.to(torch.bfloat16))
+
+
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
 def test_backward_fused_rope_adjoint(dt):
     B, H, T, N, D, pos0 = 1, 2, 200, 512, 64, 7
