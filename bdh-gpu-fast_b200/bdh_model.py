@@ -417,7 +417,12 @@ class BDH(nn.Module):
             past_kr = past_v = out_kr = past_scale = out_scale = None
             raw = False
             if cache is not None:
-                native = impl == "cuda_sm100" and not grad
+                # the native decode reads fp32, bf16 and fp8 caches in place; another storage
+                # dtype (fp16) is upcast per step by get_past, as the reference's cache does
+                # (bdh_cache.py:240-243), and the native kernels run on the fp32 copy
+                native = (impl == "cuda_sm100" and not grad
+                          and cache.storage_dtype in (torch.float32, torch.bfloat16,
+                                                      torch.float8_e4m3fn))
                 eager_inplace = (not grad and cache.storage_matches_compute
                                  and v_tok.dtype == cache.storage_dtype)
                 if native or eager_inplace:
