@@ -142,11 +142,26 @@ class Attention(nn.Module):
         if QR is None:
             from kernels.sm100_attn import rope_rotate
 
-            QR = rope_rotate(Q, self.freqs, rope_start, out=qr_out)
+            if qr_out is not None and qr_out.dtype != Q.dtype:
+                # the block attends in the compute dtype (its own keys unrounded, as the
+                # reference's past || block in compute dtype); the cache slot gets the rounded copy
+                QR = rope_rotate(Q, self.freqs, rope_start)
+                qr_out.copy_(QR)
+            else:
+                QR = rope_rotate(Q, self.freqs, rope_start, out=qr_out)
         if fp8_slot:
             from bdh_cache import _quantize_into
 
             _quantize_into(QR, out_kr, out_kr_scale)
+        if impl == "cuda_sm100" and 1 < T <= 16:
+            # a short block after a past (multi-token decode): the block's own strict past by the
+            # tril pass plus the whole cached past by the decode kernel, which reads it in its
+            # storage dtype; only the block's rows are computed (the reference recomputes
+            # past || block with the cold path and keeps the last T rows, bdh.py:439-461)
+            from kernels.sm100_attn import tril_decode, tril_score_v
+
+            Vb = V.to(QR.dtype)
+            return tril_score_v(QR, QR, Vb) + tril_decode(QR, past_kr, past_v), QR, V
         if past_is_raw and past_kr.dtype != QR.dtype:
             past_kr, past_v = past_kr.to(QR.dtype), past_v.to(QR.dtype)
         if T == 1:
@@ -437,7 +452,8 @@ class BDH(nn.Module):
                         past_kr, past_v = cache.get_past(level)
                     dst_v.copy_(v_tok)
                     out_kr = dst_kr
-                    v_tok = dst_v
+                    if dst_v.dtype == v_tok.dtype:  # the slot view (past || block without a copy)
+                        v_tok = dst_v
                 else:
                     past_kr, past_v = cache.get_past(level)
             y_kv, new_kr, new_v = self.attn(x_sparse, x_sparse, v_tok, rope_start=rope_start,

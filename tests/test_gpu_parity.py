@@ -757,6 +757,36 @@ def test_state_decode_equals_history_decode(qdt, vdt):
     assert torch.equal(state[zero_rows], s0[zero_rows])
 
 
+@pytest.mark.parametrize("storage", [None, torch.bfloat16])
+def test_model_multi_token_blocks_after_a_past(storage):
+    """Prefill, then blocks of 4 and 16 tokens (the block's tril pass plus the decode kernel over
+    the cached past, read in its storage dtype), a block of 20 (past || block through the cold
+    path, as the reference does) and single tokens: the logits of every position match one full
+    forward of the whole sequence."""
+    import bdh_model
+    from bdh_cache import CacheManager
+
+    cfg = bdh_model.BDHConfig(n_layer=2, n_embd=128, n_head=4, mlp_internal_dim_multiplier=16,
+                              vocab_size=256, dropout=0.0)
+    torch.manual_seed(31)
+    m = bdh_model.BDH(cfg).to(DEV).eval()
+    m.attn._attn_impl_override = "cuda_sm100"
+    B, blocks = 2, [40, 4, 16, 20, 1, 1]
+    total = sum(blocks)
+    idx = torch.randint(0, 256, (B, total), generator=torch.Generator().manual_seed(32)).to(DEV)
+    cache = CacheManager.from_config(m.config, B, total, DEV, storage_dtype=storage)
+    parts, t = [], 0
+    with torch.no_grad():
+        full, _ = m(idx)
+        for n in blocks:
+            parts.append(m(idx[:, t:t + n], cache=cache)[0])
+            t += n
+    assert cache.seq_len == total
+    got = torch.cat(parts, 1)
+    r = ((got.double() - full.double()).norm() / full.double().norm()).item()
+    assert r < (1e-5 if storage is None else 3e-3), r
+
+
 @pytest.mark.parametrize("amp", [False, True])
 def test_model_state_cache_matches_history(amp):
     """Prefill + decode on the sm100 path with the N x D state cache vs the history cache."""
