@@ -144,8 +144,8 @@ def _run_cached(m, idx, P, storage, impl="cuda_sm100"):
 def test_model_fp8_cache_matches_eager_and_fp32_cache(monkeypatch):
     """Cached prefill + decode on an fp8 key cache: the native decode (fp8 stream, fused RoPE and
     slot quantization) matches the eager path over the dequantized cache within the bf16 bound
-    (the native prefill attends over the bf16 value slots, as with a bf16 cache, the eager one
-    over fp32 values), and stays within 3e-2 of the fp32 cache (the e4m3 rounding of the keys)."""
+    (the decode steps read the bf16 value slots; both prefills attend over the fp32 values), and
+    stays within 3e-2 of the fp32 cache (the e4m3 rounding of the keys)."""
     m = _model()
     B, P, steps = 2, 160, 6
     idx = torch.randint(0, 256, (B, P + steps), generator=torch.Generator().manual_seed(8)).to(DEV)

@@ -757,12 +757,13 @@ def test_state_decode_equals_history_decode(qdt, vdt):
     assert torch.equal(state[zero_rows], s0[zero_rows])
 
 
-@pytest.mark.parametrize("storage", [None, torch.bfloat16])
-def test_model_multi_token_blocks_after_a_past(storage):
+@pytest.mark.parametrize("storage,bar", [(None, 1e-5), (torch.bfloat16, 3e-3),
+                                         (torch.float8_e4m3fn, 3e-2)])
+def test_model_multi_token_blocks_after_a_past(storage, bar):
     """Prefill, then blocks of 4 and 16 tokens (the block's tril pass plus the decode kernel over
     the cached past, read in its storage dtype), a block of 20 (past || block through the cold
     path, as the reference does) and single tokens: the logits of every position match one full
-    forward of the whole sequence."""
+    forward of the whole sequence, for fp32, bf16 and fp8-key caches."""
     import bdh_model
     from bdh_cache import CacheManager
 
@@ -784,7 +785,7 @@ def test_model_multi_token_blocks_after_a_past(storage):
     assert cache.seq_len == total
     got = torch.cat(parts, 1)
     r = ((got.double() - full.double()).norm() / full.double().norm()).item()
-    assert r < (1e-5 if storage is None else 3e-3), r
+    assert r < bar, r  # fp8: the e4m3 keys of the past (the fp8 cache's own bar)
 
 
 @pytest.mark.parametrize("amp", [False, True])
