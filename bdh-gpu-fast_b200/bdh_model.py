@@ -480,36 +480,55 @@ class BDH(nn.Module):
         ``GraphedForward``)."""
         return GraphedForward(self, batch, seq_len, amp_dtype)
 
-    @torch.inference_mode()
+    @staticmethod
+    def _sample(logits: torch.Tensor, temperature: float, top_k: Optional[int]) -> torch.Tensor:
+        """One token per row of fp32 (B, V) logits, drawing from the RNG exactly as the
+        reference's sampler does (bdh.py:680-728), so a seed gives the same tokens: temperature
+        as a multiplication by its reciprocal; with top_k < V a softmax over the k largest
+        logits, one multinomial draw among them and a gather of its index; with top_k >= V the
+        logits below the k-th largest masked to -inf; then a softmax over the vocabulary and
+        one multinomial draw."""
+        if float(temperature) != 1.0:
+            logits = logits * (1.0 / float(temperature))
+        if top_k is not None:
+            V = logits.size(-1)
+            k = min(int(top_k), V)
+            values, indices = torch.topk(logits, k, dim=-1)
+            if k < V:
+                return indices.gather(1, torch.multinomial(F.softmax(values, dim=-1), 1))
+            logits = logits.masked_fill(logits < values[:, -1:], float("-inf"))
+        return torch.multinomial(torch.softmax(logits, dim=-1), 1)
+
     def generate(self, idx: torch.Tensor, max_new_tokens: int, temperature: float = 1.0,
                  top_k: Optional[int] = None, *, cache_dtype: Optional[torch.dtype] = None,
-                 amp_dtype: Optional[torch.dtype] = None, cache_kind: str = "kv") -> torch.Tensor:
-        """Autoregressive sampling with the packed cache (prefill, then T=1 steps);
-        ``cache_kind="state"`` keeps the N x D recurrent state instead of the history."""
+                 amp_dtype: Optional[torch.dtype] = None, cache_page_size: Optional[int] = None,
+                 cache_kind: str = "kv") -> torch.Tensor:
+        """Autoregressive sampling with the packed cache (prefill, then T = 1 steps), the
+        reference's ``BDH.generate`` (bdh.py:1076-1190): the same keywords (``cache_dtype`` the
+        cache storage dtype, ``cache_page_size`` its paging, ``amp_dtype`` autocast over the
+        forward) and the same tokens for a seed. ``cache_kind="state"`` keeps the N x D
+        recurrent state instead of the history."""
         was_training = self.training
         self.eval()
         B, T0 = idx.shape
         cache = CacheManager.from_config(self.config, B, T0 + max_new_tokens, idx.device,
-                                         storage_dtype=cache_dtype, storage_kind=cache_kind)
+                                         storage_dtype=cache_dtype, page_size=cache_page_size,
+                                         storage_kind=cache_kind)
         out = torch.empty(B, T0 + max_new_tokens, dtype=idx.dtype, device=idx.device)
         out[:, :T0] = idx
         ctx = (torch.autocast(idx.device.type, dtype=amp_dtype) if amp_dtype is not None
                else torch.autocast(idx.device.type, enabled=False))
-        with ctx:
-            logits, _ = self(idx, cache=cache)
-            step = logits[:, -1, :].float()
-            for t in range(max_new_tokens):
-                step = step / temperature
-                if top_k is not None:
-                    vals, _ = torch.topk(step, min(top_k, step.size(-1)))
-                    step = step.masked_fill(step < vals[:, [-1]], float("-inf"))
-                nxt = torch.multinomial(F.softmax(step, dim=-1), 1)
-                out[:, T0 + t] = nxt[:, 0]
-                if t + 1 < max_new_tokens:
-                    logits, _ = self(nxt, cache=cache)
-                    step = logits[:, -1, :].float()
-        if was_training:
-            self.train()
+        try:
+            with torch.inference_mode(), ctx:
+                logits, _ = self(idx, cache=cache)
+                for t in range(max_new_tokens):
+                    nxt = self._sample(logits[:, -1, :].float(), temperature, top_k)
+                    out[:, T0 + t] = nxt[:, 0]
+                    if t + 1 < max_new_tokens:
+                        logits, _ = self(nxt, cache=cache)
+        finally:
+            if was_training:
+                self.train()
         return out
 
 

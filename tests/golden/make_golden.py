@@ -5,8 +5,8 @@ Run in the build container (the reference checkout is not available on GPU hosts
     PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py <reference checkout>
 
 (default: the ``BDH_REFERENCE`` environment variable, else the ``reference_path`` of
-BASELINE.json, as oracle/build_ref.py resolves it; ``--config2-only`` / ``--latent-only``
-rewrite one fixture)
+BASELINE.json, as oracle/build_ref.py resolves it; ``--config2-only`` / ``--latent-only`` /
+``--generate-only`` rewrite one fixture)
 
 It imports the reference's own Python modules (``bdh``, ``bdh_baseline``, ``bdh_cache``,
 ``kernels``) and its CPU extension built by ``oracle/build_ref.py`` (``csrc/tril_attn_cpu.cpp``),
@@ -157,6 +157,7 @@ def main(reference: Path) -> None:
     np.savez_compressed(HERE / "golden_model.npz", **mod)
     latent_fixture(bdh, HERE)
     config2_bf16_fixture(bdh, HERE)
+    generate_fixture(bdh, HERE)
     print("wrote", sorted(p.name for p in HERE.glob("golden_*.npz")))
 
 
@@ -284,6 +285,36 @@ def config2_bf16_fixture(bdh, out_dir: Path) -> None:
     np.savez_compressed(out_dir / "golden_config2_bf16.npz", **fix)
 
 
+GENERATE_CASES = (  # (name, seed, temperature, top_k, cache_dtype, cache_page_size)
+    ("plain", 101, 1.0, None, None, None),
+    ("temp07", 102, 0.7, None, None, None),
+    ("topk5_temp13", 103, 1.3, 5, None, None),
+    ("topk300", 104, 1.0, 300, None, None),
+    ("fp16_cache", 105, 1.0, None, "float16", None),
+    ("paged", 106, 0.9, 20, None, 4),
+)
+
+
+def generate_fixture(bdh, out_dir: Path) -> None:
+    """The reference's BDH.generate (bdh.py:1076-1190, sampler :680-728) on a small seeded model:
+    for each case torch.manual_seed(seed) and then generate(prompt, 10, ...) on the CPU."""
+    import torch
+
+    cfg = bdh.BDHConfig(n_layer=2, n_embd=64, n_head=4, mlp_internal_dim_multiplier=8,
+                        dropout=0.0, vocab_size=256)
+    torch.manual_seed(41)
+    m = bdh.BDH(cfg).eval()
+    fix = {f"w_{k}": v.numpy() for k, v in m.state_dict().items()}
+    prompt = torch.randint(0, 256, (2, 6), generator=torch.Generator().manual_seed(42))
+    fix["prompt"] = prompt.numpy()
+    for name, seed, temp, top_k, cdt, page in GENERATE_CASES:
+        torch.manual_seed(seed)
+        out = m.generate(prompt.clone(), 10, temperature=temp, top_k=top_k,
+                         cache_dtype=getattr(torch, cdt) if cdt else None, cache_page_size=page)
+        fix[f"tokens_{name}"] = out.numpy()
+    np.savez_compressed(out_dir / "golden_generate.npz", **fix)
+
+
 def dataclasses_asdict(c):
     import dataclasses
 
@@ -300,12 +331,14 @@ if __name__ == "__main__":
         ref = build_ref.reference_root()
         if ref is None:
             sys.exit("no reference checkout: pass its path or set BDH_REFERENCE")
-    if "--latent-only" in sys.argv or "--config2-only" in sys.argv:
+    if "--latent-only" in sys.argv or "--config2-only" in sys.argv or "--generate-only" in sys.argv:
         sys.path.insert(0, str(ref))
         import bdh as _bdh
 
         if "--latent-only" in sys.argv:
             latent_fixture(_bdh, HERE)
+        elif "--generate-only" in sys.argv:
+            generate_fixture(_bdh, HERE)
         else:
             config2_bf16_fixture(_bdh, HERE)
     else:
