@@ -788,6 +788,29 @@ def test_model_multi_token_blocks_after_a_past(storage, bar):
     assert r < bar, r  # fp8: the e4m3 keys of the past (the fp8 cache's own bar)
 
 
+@pytest.mark.parametrize("kw", [{}, {"top_k": 8, "temperature": 0.8},
+                                {"cache_dtype": torch.float16}, {"cache_page_size": 4},
+                                {"cache_kind": "state"}])
+def test_generate_native_matches_eager_tokens(kw, monkeypatch):
+    """BDH.generate on the native path (prefill kernels, decode kernel with the fused RoPE and
+    cache-slot write, or the state decode) against the eager path on the same GPU: one seed,
+    the same sampled tokens (the sampler draws identically; the logits agree to ~1e-6)."""
+    import bdh_model
+
+    cfg = bdh_model.BDHConfig(n_layer=2, n_embd=128, n_head=4, mlp_internal_dim_multiplier=16,
+                              vocab_size=256, dropout=0.0)
+    torch.manual_seed(51)
+    m = bdh_model.BDH(cfg).to(DEV).eval()
+    prompt = torch.randint(0, 256, (3, 20), generator=torch.Generator().manual_seed(52)).to(DEV)
+    toks = {}
+    for impl in ("eager", "cuda_sm100"):
+        monkeypatch.setenv("BDH_ATTN_IMPL", impl)
+        torch.manual_seed(53)
+        toks[impl] = m.generate(prompt, 12, **kw)
+    assert torch.equal(toks["eager"], toks["cuda_sm100"])
+    assert torch.equal(toks["eager"][:, :20], prompt)
+
+
 @pytest.mark.parametrize("amp", [False, True])
 def test_model_state_cache_matches_history(amp):
     """Prefill + decode on the sm100 path with the N x D state cache vs the history cache."""
