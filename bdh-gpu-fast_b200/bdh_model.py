@@ -86,9 +86,61 @@ class Attention(nn.Module):
         N = config.mlp_internal_dim_multiplier * D // nh
         self.freqs = nn.Buffer(get_freqs(N, theta=2 ** 16, dtype=torch.float32).view(1, 1, 1, N))
         self._attn_impl_override: Optional[str] = None
+        self._rope_table = None       # (cos, sin) of positions [0, max_T), ensure_rope_table
+        self._rope_table_key = None   # (max_T, device type, device index)
+
+    @staticmethod
+    def phases_cos_sin(phases: torch.Tensor):
+        """(cos, sin) of phases given in turns: ((phases mod 1) * 2 pi) (bdh.py:119-122)."""
+        phases = (phases % 1) * (2 * math.pi)
+        return torch.cos(phases), torch.sin(phases)
+
+    @staticmethod
+    def rope(phases, v: torch.Tensor, out: Optional[torch.Tensor] = None, cos_sin=None):
+        """Rotate the adjacent pairs of ``v`` by ``phases`` (or by precomputed ``cos_sin``) into
+        ``out`` or a fresh tensor, through the ``BDH_ROPE_IMPL`` dispatch (bdh.py:124-140)."""
+        from kernels.rope_dispatch import bdh_rope_rotate
+
+        cos, sin = cos_sin if cos_sin is not None else Attention.phases_cos_sin(phases)
+        return bdh_rope_rotate(v, cos, sin, out=out)
+
+    def ensure_rope_table(self, max_T: int, device) -> None:
+        """Precompute (cos, sin) for positions [0, max_T) once (bdh.py:157-191); rope_cos_sin
+        and t1_cis_pairs then narrow into it instead of computing the phases again. Only the
+        eager path reads tables: the native kernels compute the phases in registers."""
+        if max_T < 1:
+            raise ValueError("max_T must be >= 1")
+        device = torch.device(device)
+        key = (int(max_T), device.type, device.index)
+        if self._rope_table is not None and self._rope_table_key == key:
+            return
+        cos, sin = rope_tables(self.freqs, int(max_T), 0, device)
+        self._rope_table, self._rope_table_key = (cos, sin), key
+
+    def _table_covers(self, rope_start: int, T: int, device) -> bool:
+        if self._rope_table is None:
+            return False
+        max_T, dev_type, dev_index = self._rope_table_key
+        device = torch.device(device)
+        return (0 <= rope_start and rope_start + T <= max_T and device.type == dev_type
+                and device.index == dev_index)
 
     def rope_cos_sin(self, T: int, rope_start: int, device):
+        """(cos, sin) of positions [rope_start, rope_start + T), (1, 1, T, N) fp32: a narrow of
+        the ensure_rope_table table when it covers them, else computed (bdh.py:193-262)."""
+        if self._table_covers(rope_start, T, device):
+            cos, sin = self._rope_table
+            return cos.narrow(-2, rope_start, T), sin.narrow(-2, rope_start, T)
         return rope_tables(self.freqs, T, rope_start, device)
+
+    def t1_cis_pairs(self, rope_start: int, device):
+        """(cos, sin) of one position in the paired layout (1, 1, 1, N / 2, 2) from the
+        ensure_rope_table table, or None without a covering table (bdh.py:301-347)."""
+        if not self._table_covers(rope_start, 1, device):
+            return None
+        cos, sin = self._rope_table
+        pair = lambda t: t.reshape(*t.shape[:-1], -1, 2).narrow(-3, rope_start, 1)
+        return pair(cos), pair(sin)
 
     def forward(self, Q, K, V, rope_start: int = 0, past_kr=None, past_v=None, out_kr=None,
                 past_is_raw: bool = False, relu_input: bool = False, past_kr_scale=None,
@@ -136,9 +188,10 @@ class Attention(nn.Module):
             QR = rope_rotate(Q, self.freqs, rope_start)
             return tril_decode(QR, past_kr, past_v), QR, V
         # eager T=1 decode, or a multi-token block continuing a past
-        cos, sin = rope_tables(self.freqs, T, rope_start, Q.device)
         qr_out = None if fp8_slot else out_kr
-        QR = eager_rope_rotate(Q, cos, sin, out=qr_out) if impl == "eager" else None
+        QR = None
+        if impl == "eager":
+            QR = eager_rope_rotate(Q, *self.rope_cos_sin(T, rope_start, Q.device), out=qr_out)
         if QR is None:
             from kernels.sm100_attn import rope_rotate
 
@@ -247,13 +300,12 @@ class BDH(nn.Module):
             return out
         if relu_input:
             Q = F.relu(Q)
-        cos, sin = rope_tables(self.attn.freqs, T, rope_start, Q.device)
         if impl == "cuda_sm100":
             from kernels.sm100_attn import rope_rotate
 
             QR = rope_rotate(Q, self.attn.freqs, rope_start)
         else:
-            QR = eager_rope_rotate(Q, cos, sin)
+            QR = eager_rope_rotate(Q, *self.attn.rope_cos_sin(T, rope_start, Q.device))
         Vq = V.to(QR.dtype)
         out = bdh_attn(QR, QR, Vq, impl=impl)
         chunk = max(1, (1 << 28) // max(1, nh * T * N))  # bound the fp32 copies of QR
@@ -514,6 +566,8 @@ class BDH(nn.Module):
         cache = CacheManager.from_config(self.config, B, T0 + max_new_tokens, idx.device,
                                          storage_dtype=cache_dtype, page_size=cache_page_size,
                                          storage_kind=cache_kind)
+        if (self.attn._attn_impl_override or resolve_attn_impl()) == "eager":
+            self.attn.ensure_rope_table(T0 + max_new_tokens, idx.device)  # the span's phases once
         out = torch.empty(B, T0 + max_new_tokens, dtype=idx.dtype, device=idx.device)
         out[:, :T0] = idx
         ctx = (torch.autocast(idx.device.type, dtype=amp_dtype) if amp_dtype is not None

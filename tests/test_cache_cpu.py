@@ -199,3 +199,29 @@ def test_reserve_and_stage_across_page_grow():  # test_cache_pack.py:540-590
     assert torch.all(all_kr[:, :, :4] == 1.0) and torch.all(all_v[:, :, 5:] == 6.0)
     cm.commit()
     assert cm.seq_len == 8
+
+
+def test_attention_rope_api_matches_reference_golden():
+    """Attention's RoPE members of the reference (bdh.py:119-347): phases_cos_sin / rope (static),
+    ensure_rope_table, rope_cos_sin narrowing into the table (the same bits as computing them),
+    t1_cis_pairs (paired layout, None without a covering table); the rotation reproduces the
+    reference's Attention.rope outputs (tests/golden/golden_rope.npz)."""
+    from conftest import golden
+
+    g = golden("rope")
+    att = bdh_model.Attention(_cfg(n_layer=1, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4))
+    x = torch.from_numpy(g["x"])  # (2, 3, 17, 64)
+    for pos0 in (0, 37, 4000):
+        fresh = att.rope_cos_sin(17, pos0, torch.device("cpu"))
+        y = bdh_model.Attention.rope(None, x, cos_sin=fresh)
+        assert torch.allclose(y, torch.from_numpy(g[f"y_f32_pos{pos0}"]), rtol=0, atol=2e-6)
+        phases = torch.arange(pos0, pos0 + 17, dtype=torch.float32).view(1, 1, -1, 1) * att.freqs
+        assert torch.equal(bdh_model.Attention.rope(phases, x), y)
+    assert att.t1_cis_pairs(3, "cpu") is None
+    att.ensure_rope_table(64, "cpu")
+    cached = att.rope_cos_sin(17, 37, torch.device("cpu"))
+    fresh = bdh_model.rope_tables(att.freqs, 17, 37, torch.device("cpu"))
+    assert torch.equal(cached[0], fresh[0]) and torch.equal(cached[1], fresh[1])
+    cp, sp = att.t1_cis_pairs(37, "cpu")
+    assert cp.shape == (1, 1, 1, 32, 2) and torch.equal(cp.reshape(1, 1, 1, 64), fresh[0][:, :, :1])
+    assert att.t1_cis_pairs(64, "cpu") is None  # past the table
