@@ -195,3 +195,21 @@ def test_cuda_attn_module_mirrors_reference_names():
     assert float(cuda_attn.tril_decode_ref(qd, kb[:, :, :0], vb[:, :, :0]).abs().sum()) == 0.0
     with pytest.raises(RuntimeError):
         cuda_attn.tril_score_v(q, q, v)
+
+
+def test_package_reexports_reference_names():
+    """The kernels package re-exports what the reference's kernels/__init__.py does from its
+    cuda_attn module (tile constants, tile pickers, CPU references), besides the dispatch, the
+    autograd functions and the RoPE dispatch; the blocked and Triton backends stay removed."""
+    import kernels
+
+    for name in ("cuda_attn", "CUDA_TILE_M", "CUDA_TILE_N", "CUDA_TILE_M_MAX", "CUDA_TILE_N_MAX",
+                 "CUDA_DECODE_TILE_N", "CUDA_DECODE_TILE_N_MAX", "pick_cuda_cold_tiles",
+                 "pick_cuda_decode_tile_n", "tril_score_v_ref", "tril_score_v_tiled_ref",
+                 "tril_decode_ref", "tril_decode_tiled_ref", "bdh_attn", "bdh_attn_decode",
+                 "StrictTrilAttnFn", "StrictTrilSelfAttnFn", "analytic_tril_attn_backward",
+                 "bdh_rope_rotate", "bdh_rope_rotate_paired", "resolve_rope_impl"):
+        assert hasattr(kernels, name), name
+        assert name in kernels.__all__, name
+    for removed in ("blocked_tril_attn", "triton_tril_attn", "triton_decode_attn"):
+        assert not hasattr(kernels, removed), removed
