@@ -6,7 +6,7 @@ Run in the build container (the reference checkout is not available on GPU hosts
 
 (default: the ``BDH_REFERENCE`` environment variable, else the ``reference_path`` of
 BASELINE.json, as oracle/build_ref.py resolves it; ``--config2-only`` / ``--latent-only`` /
-``--generate-only`` rewrite one fixture)
+``--generate-only`` / ``--train-only`` rewrite one fixture)
 
 It imports the reference's own Python modules (``bdh``, ``bdh_baseline``, ``bdh_cache``,
 ``kernels``) and its CPU extension built by ``oracle/build_ref.py`` (``csrc/tril_attn_cpu.cpp``),
@@ -158,6 +158,7 @@ def main(reference: Path) -> None:
     latent_fixture(bdh, HERE)
     config2_bf16_fixture(bdh, HERE)
     generate_fixture(bdh, HERE)
+    train_fixture(bdh_baseline, HERE)
     print("wrote", sorted(p.name for p in HERE.glob("golden_*.npz")))
 
 
@@ -315,6 +316,28 @@ def generate_fixture(bdh, out_dir: Path) -> None:
     np.savez_compressed(out_dir / "golden_generate.npz", **fix)
 
 
+def train_fixture(bdh_baseline, out_dir: Path) -> None:
+    """One training step's numbers from the reference's upstream model (bdh_baseline.BDH,
+    bdh_baseline.py:97-139, dropout 0): logits, the cross-entropy loss and the gradient of every
+    parameter, on a small seeded model and batch (fp32, CPU)."""
+    import torch
+
+    cfg = bdh_baseline.BDHConfig(n_layer=2, n_embd=64, n_head=4, mlp_internal_dim_multiplier=8,
+                                 dropout=0.0, vocab_size=256)
+    torch.manual_seed(61)
+    m = bdh_baseline.BDH(cfg)
+    fix = {f"w_{k}": v.detach().numpy().copy() for k, v in m.state_dict().items()}
+    g = torch.Generator().manual_seed(62)
+    idx = torch.randint(0, 256, (3, 40), generator=g)
+    tgt = torch.randint(0, 256, (3, 40), generator=g)
+    logits, loss = m(idx, tgt)
+    loss.backward()
+    fix.update(idx=idx.numpy(), targets=tgt.numpy(), logits=_f32(logits), loss=np.float64(loss.item()))
+    for k, p in m.named_parameters():
+        fix[f"grad_{k}"] = _f32(p.grad)
+    np.savez_compressed(out_dir / "golden_train.npz", **fix)
+
+
 def dataclasses_asdict(c):
     import dataclasses
 
@@ -331,15 +354,16 @@ if __name__ == "__main__":
         ref = build_ref.reference_root()
         if ref is None:
             sys.exit("no reference checkout: pass its path or set BDH_REFERENCE")
-    if "--latent-only" in sys.argv or "--config2-only" in sys.argv or "--generate-only" in sys.argv:
+    only = [a for a in sys.argv[1:] if a in ("--latent-only", "--config2-only", "--generate-only",
+                                             "--train-only")]
+    if only:
         sys.path.insert(0, str(ref))
         import bdh as _bdh
+        import bdh_baseline as _bdh_baseline
 
-        if "--latent-only" in sys.argv:
-            latent_fixture(_bdh, HERE)
-        elif "--generate-only" in sys.argv:
-            generate_fixture(_bdh, HERE)
-        else:
-            config2_bf16_fixture(_bdh, HERE)
+        {"--latent-only": lambda: latent_fixture(_bdh, HERE),
+         "--config2-only": lambda: config2_bf16_fixture(_bdh, HERE),
+         "--generate-only": lambda: generate_fixture(_bdh, HERE),
+         "--train-only": lambda: train_fixture(_bdh_baseline, HERE)}[only[0]]()
     else:
         main(ref)
