@@ -493,7 +493,7 @@ def config2_rooflines(prof: dict, B: int, T: int, steps: int, region_ms: float) 
                          "hbm", 2 * lat + small + B * N_HEAD * T * D_MODEL * 2, 1e9, "GB/s",
                          peaks["hbm_gbs"], f"{src} hbm_gbs", "latent_gate_config2")
     specs = {
-        "score": ("score pass tril(QR QR^T,-1) (tc_pair_kernel<ScorePair>, cta_group::2 256x256 tiles)"
+        "score": ("score pass tril(QR QR^T,-1) (tc_pair_kernel<ScorePairT<7, 0>>, cta_group::2 256x256 tiles, seven operand stages)"
                   if os.environ.get("BDH_SM100_PAIR", "1") != "0"
                   else "score pass tril(QR QR^T,-1) (tc_gemm_kernel<ScoreProb<bf16>>)",
                   "tensor", B * N_HEAD * T * (T - 1) * N_LAT, 1e12, "TFLOP/s", tpeak, tsrc,
