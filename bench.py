@@ -21,7 +21,8 @@ random N(0, 0.02) weights, synthetic token ids uniform in [0, 256), B=32 x T=512
                  CPU extension (``csrc/tril_attn_cpu.cpp``, built into oracle/_ref), on the host
                  cores, on a bounded sample
 * ``gpu_eager_baseline`` the reference's eval forward op for op on this GPU (eager attention,
-                 cuBLAS projections) for the config-2 step and the config-4 decode step
+                 cuBLAS projections) for the config-2 step and the config-4 decode step, and its
+                 eager op (torch matmuls, torch autograd) beside configs 5 and 3
 * ``configs``    the metric's other numbers on the same lease, each with its own roofline,
                  clocks and cpu_baseline: config 4 decode tokens/s over the whole span
                  (S = 515 .. 1023), config 5 forward + backward TFLOP/s, config 3 TFLOP/s
@@ -730,7 +731,8 @@ def other_configs(args, world, rank, dev, eager):
     """The metric's other numbers on the same lease (each a sub-object with its own roofline,
     clocks and cpu_baseline): config 4 decode tokens/s over the whole span (B = 64, 512-token
     prompt, S up to 1023), config 5 forward + backward TFLOP/s, config 3 long-context TFLOP/s;
-    and the eager decode step beside config 4."""
+    and, into ``eager`` (the line's gpu_eager_baseline), the reference's eager path for each:
+    the decode step beside config 4 and the op beside configs 5 and 3."""
     out = {}
     sub = argparse.Namespace(**vars(args))
     sub.batch = 0
@@ -746,8 +748,15 @@ def other_configs(args, world, rank, dev, eager):
     sub.config = 5
     out["config5_fwd_bwd"] = bench_op(sub, world, rank, dev)
     torch.cuda.empty_cache()
+    sub.steps = 5
+    eager["config5"] = bench_op_eager(sub, world, rank, dev, out["config5_fwd_bwd"])
+    torch.cuda.empty_cache()
+    sub.steps = 10
     sub.config = 3
     out["config3_long_context"] = bench_op(sub, world, rank, dev)
+    torch.cuda.empty_cache()
+    sub.steps = 5
+    eager["config3"] = bench_op_eager(sub, world, rank, dev, out["config3_long_context"])
     torch.cuda.empty_cache()
     return out
 
@@ -933,6 +942,50 @@ def bench_op(args, world, rank, dev):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_op_baseline(cfg_id)
     return line
+
+
+def bench_op_eager(args, world, rank, dev, native_line):
+    """The reference's path for an op config on this GPU, beside ``bench_op``'s line: RoPE
+    tables and (QR QR^T).tril(-1) V as torch matmuls (cuBLAS), the reference's eager attention
+    (kernels/attention.py:27-40 behind BDH_ATTN_IMPL=eager); for config 5 the backward is torch
+    autograd through those ops (its default training path, BDH_ATTN_AUTOGRAD=0). ``value`` uses
+    the native line's flop count, so the two values compare as times do."""
+    import bdh_model
+    from kernels.attention_dispatch import bdh_rope_attn
+
+    cfg_id = args.config
+    q, v, (B, H, T, N, D, dt) = _op_inputs(cfg_id, dev, rank, args.batch)
+    freqs = bdh_model.get_freqs(N, 2 ** 16, torch.float32).to(dev)
+    if cfg_id == 5:
+        dO = torch.randn(B, H, T, D, device=dev).to(dt)
+        qg = q.clone().requires_grad_(True)
+        vg = v.clone().requires_grad_(True)
+
+        def step():
+            qg.grad = None
+            vg.grad = None
+            out, _ = bdh_rope_attn(qg, vg, freqs, 0, impl="eager", use_autograd_fn=False)
+            out.backward(dO)
+    else:
+        def step():
+            with torch.no_grad():
+                return bdh_rope_attn(q, v, freqs, 0, impl="eager")[0]
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(dev)
+    clocks.start()
+    ms = timed(step, args.steps, world, dev)
+    clk = clocks.stop()
+    ms_native = native_line["ms_per_step"] * args.steps
+    return {"value": native_line["value"] * ms_native / ms, "unit": native_line["unit"],
+            "ms_per_step": ms / args.steps, "steps": args.steps, "warmup": args.warmup,
+            "clocks": clk,
+            "what": f"config-{cfg_id} op with BDH_ATTN_IMPL=eager: RoPE tables and "
+                    "(QR QR^T).tril(-1) V as torch/cuBLAS matmuls (kernels/attention.py:27-40)"
+                    + ("; backward by torch autograd (BDH_ATTN_AUTOGRAD=0)" if cfg_id == 5 else "")
+                    + "; value: the native line's flops over this time"}
 
 
 # ------------------------------------------------------------------ config 4 decode
