@@ -40,15 +40,19 @@ extern "C" {
 #define BDH_ERR_CUDA 2      /* CUDA runtime error at launch */
 #define BDH_ERR_WORKSPACE 3 /* workspace missing or too small */
 
-/* ABI version of the loaded library (BDH_ABI_VERSION). */
+/* ABI version of the loaded library (BDH_ABI_VERSION); bindings refuse a library of another
+ * version. No counterpart in the reference (its module is built together with its callers). */
 int bdh_abi_version(void);
 
-/* Message of the calling thread's last failing call ("" if none). */
+/* Message of the calling thread's last failing call ("" if none). The reference reports the
+ * same failures as C++ exceptions through pybind (TORCH_CHECK, csrc/tril_attn_cuda.cu:252,
+ * csrc/tril_attn_bind.cpp:8); a C-ABI returns a code and keeps the message here. */
 const char* bdh_last_error(void);
 
 /* Read (and optionally clear) the device error word of `device`: 0 = no kernel has
  * reported a failure; otherwise one of the codes of csrc/common.cuh (pipeline timeouts).
- * Synchronises the device. */
+ * Synchronises the device. No counterpart in the reference (its kernels have no waits that
+ * can time out). */
 int bdh_device_error(int device, int* code, int reset);
 
 /*
