@@ -250,6 +250,34 @@ def test_model_latent_layer_matches_unfused_and_oracle(monkeypatch):
     assert O.rel_fro(f32(fused), ref16) < 3e-3
 
 
+@pytest.mark.parametrize("n_embd,n_head,mult", [(128, 4, 12), (384, 6, 8), (256, 4, 3)])
+def test_model_latent_layer_other_widths(monkeypatch, n_embd, n_head, mult):
+    """The fused layer's other branches: D = 128 (N = 384) and D = 384 (six heads, N = 512: the
+    attention LayerNorm runs after the value pass, D > 256), where the gate runs with cuBLAS's
+    decoder GEMM (the fused gate + decoder needs D = 256); and D = 256 with N = 192, a latent
+    width that is not a multiple of 128 (gate with ragged latent blocks). Against the unfused
+    sm100 layer and the float64 oracle of the bf16-autocast forward, one layer, bf16 bar."""
+    m = _model(n_layer=1, n_embd=n_embd, n_head=n_head, mult=mult)
+    idx = torch.randint(0, 256, (2, 128), generator=torch.Generator().manual_seed(19)).to(DEV)
+    res = {}
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        monkeypatch.setenv("BDH_SM100_LATENT", "1")
+        assert m._latent_fusable("cuda_sm100", 128, None, idx.device)
+        cnt = _launch_counts(lambda: res.setdefault("fused", m(idx)[0].float()))
+        assert cnt["encode"] == 1 and cnt["gate"] == 1 and cnt["rope"] == 0, cnt
+        monkeypatch.setenv("BDH_SM100_LATENT", "0")
+        res["plain"] = m(idx)[0].float()
+    fused, plain = res["fused"], res["plain"]
+    assert ((fused - plain).norm() / plain.norm()).item() < 3e-3
+    w = {k: getattr(m, k).detach().to(torch.bfloat16).float().cpu().numpy()
+         for k in ("encoder", "encoder_v", "decoder", "lm_head")}
+    w["embed"] = m.embed.weight.detach().float().cpu().numpy()
+    w["freqs"] = m.attn.freqs.reshape(-1).cpu().numpy()
+    ref16 = O.bdh_forward_bf16(idx.cpu().numpy(), w, n_layer=1, n_head=n_head)
+    assert O.rel_fro(f32(fused), ref16) < 3e-3
+    assert sa().device_error() == 0
+
+
 def test_model_gate_x_matches_stored_xs(monkeypatch):
     """The model's fused layer with xs recomputed in the gate (BDH_SM100_GATE_X=1) and with xs
     stored and re-read (default) give identical logits."""
