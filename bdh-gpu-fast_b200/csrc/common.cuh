@@ -230,6 +230,17 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream serialization may
+// begin while the previous kernel of its stream still runs; pdl_wait() returns once that kernel
+// has completed and its writes are visible (immediately for a kernel launched without the
+// attribute), so every thread calls it before its first global-memory access, read or write.
+// pdl_trigger() lets the stream's next such kernel begin launching its CTAs; that kernel still
+// waits for this one's completion before touching memory.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (bf16/fp16 operands, fp32 accumulate).
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {

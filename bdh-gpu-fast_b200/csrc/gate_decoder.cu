@@ -188,6 +188,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGdThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised and TMEM allocated before any use
   tc_fence_after();
   const uint32_t tmem = *br.tmem_slot;
+  // the set-up above touches shared memory and TMEM only: with a programmatic launch it overlaps
+  // the previous kernel's tail
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
@@ -642,7 +646,12 @@ int launch_latent_gate_dec(const GateDecArgs& a, cudaStream_t stream, int* err) 
   const int nitems = rows * split;
   const int pairs = std::min(nitems, cap);
   prof_start(kProfGate, stream);
-  kern<<<2 * pairs, kGdThreads, L::SMEM, stream>>>(prm);
+  cudaError_t le = launch_pdl(kern, dim3(2 * pairs), dim3(kGdThreads), L::SMEM, stream, prm);
+  if (le != cudaSuccess) {
+    prof_stop(kProfGate, stream);
+    set_error(std::string("gate_dec_kernel launch: ") + cudaGetErrorString(le));
+    return BDH_ERR_CUDA;
+  }
   if (split > 1) {
     const int64_t nrow = a.B * a.T;
     gate_dec_reduce_kernel<<<static_cast<unsigned>((nrow + 7) / 8), 256, 0, stream>>>(

@@ -4,10 +4,42 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
+#include <utility>
 
 #include "bdh_sm100.h"
 
 namespace bdh {
+
+// Programmatic dependent launch of the persistent tensor-core kernels (BDH_SM100_PDL=0 turns it
+// off; read once). Such a launch lets the kernel's CTAs start, set up their barriers and TMEM and
+// wait on the device (griddepcontrol.wait, before their first global-memory access) on the SMs
+// that the previous kernel of the stream has already left, instead of starting only after it
+// completes. Results are the same either way. The row LayerNorms launch plainly: launched early,
+// their small CTAs fit beside the running gate + decoder's and waited there for its whole run,
+// and the config-2 step measured slower.
+inline bool pdl_on() {
+  static const bool on = [] {
+    const char* e = std::getenv("BDH_SM100_PDL");
+    return !(e != nullptr && std::atoi(e) == 0);
+  }();
+  return on;
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_on() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Launch timing hooks (prof.cpp); kinds as documented at bdh_profile_end.
 enum ProfKind : int { kProfScore = 0, kProfValue = 1, kProfRope = 2, kProfDecode = 3,

@@ -89,6 +89,8 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_rows_kernel(const TI* __rest
                                                                 int64_t xs, TO* __restrict__ y,
                                                                 int64_t ys, int64_t rows, int D,
                                                                 float eps) {
+  pdl_wait();     // returns at once: these kernels launch plainly (internal.h, pdl_on)
+  pdl_trigger();  // the next kernel's CTAs (the encode) may start setting up
   const int lane = threadIdx.x & 31;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * kLnWarps + (threadIdx.x >> 5);
   if (r >= rows) return;
@@ -113,6 +115,8 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_residual_kernel(
     const float* __restrict__ x, int64_t xs, const TY* __restrict__ y, int64_t ys,
     float* __restrict__ out, int64_t os, uint16_t* __restrict__ out16, int64_t os16, int64_t rows,
     int D, float eps) {
+  pdl_wait();     // returns at once: these kernels launch plainly (internal.h, pdl_on)
+  pdl_trigger();  // the next kernel's CTAs (the encode) may start setting up
   const int lane = threadIdx.x & 31;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * kLnWarps + (threadIdx.x >> 5);
   if (r >= rows) return;

@@ -311,9 +311,10 @@ static int launch_tc(const typename P::Params& prm, int ntiles, cudaStream_t str
   int grid = std::min(ntiles, sm_count(dev));
   if constexpr (HasMaxCtas<P>::value) grid = std::max(1, std::min(grid, P::max_ctas(prm, sm_count(dev))));
   prof_start(kind, stream);
-  tc_gemm_kernel<S, P><<<grid, tc_threads<P>(), tc_smem_bytes<S, P>(), stream>>>(prm);
+  cudaError_t e = launch_pdl(tc_gemm_kernel<S, P>, dim3(grid), dim3(tc_threads<P>()),
+                             tc_smem_bytes<S, P>(), stream, prm);
   prof_stop(kind, stream);
-  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("tc_gemm_kernel launch: ") + cudaGetErrorString(e));
     return BDH_ERR_CUDA;

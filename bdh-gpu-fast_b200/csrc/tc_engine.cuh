@@ -321,6 +321,10 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the set-up above touches shared memory and TMEM only: with a programmatic launch it overlaps
+  // the previous kernel's tail
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer

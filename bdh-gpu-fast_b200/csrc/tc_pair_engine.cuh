@@ -208,6 +208,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<P>(), 1
   cluster_sync();  // barriers of both CTAs initialised and TMEM allocated before any use
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the set-up above touches shared memory and TMEM only: with a programmatic launch it overlaps
+  // the previous kernel's tail
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
@@ -396,9 +400,10 @@ static int launch_pair(const typename P::Params& prm, int ntiles, cudaStream_t s
   if (cap < 0) return -cap;
   const int pairs = std::min(ntiles, cap);
   prof_start(kind, stream);
-  tc_pair_kernel<S, P><<<2 * pairs, pair_threads<P>(), pair_smem_bytes<S, P>(), stream>>>(prm);
+  cudaError_t e = launch_pdl(tc_pair_kernel<S, P>, dim3(2 * pairs), dim3(pair_threads<P>()),
+                             pair_smem_bytes<S, P>(), stream, prm);
   prof_stop(kind, stream);
-  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("tc_pair_kernel launch: ") + cudaGetErrorString(e));
     return BDH_ERR_CUDA;
