@@ -35,3 +35,56 @@ def test_graphed_forward_matches_eager_calls(amp):
     from kernels import sm100_attn
 
     assert sm100_attn.device_error() == 0
+
+
+_PLAIN_LAUNCH_SCRIPT = r"""
+import os, sys
+import torch
+sys.path.insert(0, {pkg!r})
+import bdh_model
+cfg = bdh_model.BDHConfig(n_layer=2, n_embd=256, n_head=4, mlp_internal_dim_multiplier=128,
+                          vocab_size=256, dropout=0.0)
+torch.manual_seed(7)
+m = bdh_model.BDH(cfg).to("cuda").eval()
+m.attn._attn_impl_override = "cuda_sm100"
+idx = torch.randint(0, 256, (4, 256), generator=torch.Generator().manual_seed(9)).to("cuda")
+run = m.graphed_forward(4, 256)
+with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+    eager = m(idx)[0]
+graphed = run(idx).clone()
+torch.save({{"eager": eager.cpu(), "graphed": graphed.cpu()}}, {out!r})
+"""
+
+
+def test_programmatic_launch_gives_the_plain_launch_bits(tmp_path):
+    """The tensor-core kernels launch as programmatic dependent launches by default
+    (BDH_SM100_PDL): each waits on the device for the previous kernel before touching memory.
+    The same model step in a child process with BDH_SM100_PDL=0 (plain launches; the setting is
+    read once per process) gives the same logits bit for bit, eager and graphed."""
+    import os
+    import subprocess
+    import sys
+
+    import bdh_model
+
+    pkg = os.path.dirname(bdh_model.__file__)
+    out = str(tmp_path / "plain.pt")
+    env = dict(os.environ, BDH_SM100_PDL="0")
+    subprocess.run([sys.executable, "-c", _PLAIN_LAUNCH_SCRIPT.format(pkg=pkg, out=out)],
+                   env=env, check=True, timeout=600)
+    plain = torch.load(out)
+
+    cfg = bdh_model.BDHConfig(n_layer=2, n_embd=256, n_head=4, mlp_internal_dim_multiplier=128,
+                              vocab_size=256, dropout=0.0)
+    torch.manual_seed(7)
+    m = bdh_model.BDH(cfg).to(DEV).eval()
+    m.attn._attn_impl_override = "cuda_sm100"
+    idx = torch.randint(0, 256, (4, 256), generator=torch.Generator().manual_seed(9)).to(DEV)
+    run = m.graphed_forward(4, 256)
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        eager = m(idx)[0]
+    graphed = run(idx).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(eager.cpu(), plain["eager"])
+    assert torch.equal(graphed.cpu(), plain["graphed"])
+    assert torch.equal(eager, graphed)
