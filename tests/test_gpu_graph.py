@@ -88,3 +88,26 @@ def test_programmatic_launch_gives_the_plain_launch_bits(tmp_path):
     assert torch.equal(eager.cpu(), plain["eager"])
     assert torch.equal(graphed.cpu(), plain["graphed"])
     assert torch.equal(eager, graphed)
+
+
+def test_side_stream_gives_the_default_stream_bits():
+    """The native kernels run on the caller's current stream, programmatic launches included:
+    the model step issued on a created stream, with the input copied on that stream just before
+    it, gives the default stream's logits bit for bit."""
+    import bdh_model
+
+    cfg = bdh_model.BDHConfig(n_layer=2, n_embd=256, n_head=4, mlp_internal_dim_multiplier=128,
+                              vocab_size=256, dropout=0.0)
+    torch.manual_seed(7)
+    m = bdh_model.BDH(cfg).to(DEV).eval()
+    m.attn._attn_impl_override = "cuda_sm100"
+    idx_host = torch.randint(0, 256, (4, 256), generator=torch.Generator().manual_seed(11)).pin_memory()
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        want = m(idx_host.to(DEV))[0]
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s), torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        idx = idx_host.to(DEV, non_blocking=True)
+        got = [m(idx)[0] for _ in range(2)]
+    s.synchronize()
+    assert torch.equal(got[0], want) and torch.equal(got[1], want)
